@@ -1,0 +1,74 @@
+// Shared helpers for the DIAL B200 kernels: status plumbing, launch counting,
+// activation dtype traits and small PTX wrappers.  sm_100a only.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "dial_cuda.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "this library targets sm_100a (B200) only"
+#endif
+
+namespace dial {
+
+// ---------------------------------------------------------------- host side
+// Records a formatted message in the calling thread's error slot and returns s.
+dial_status fail(dial_status s, const char* fmt, ...);
+// Maps a CUDA error (from the call named `what`) to DIAL_ERR_CUDA.
+dial_status cuda_fail(cudaError_t e, const char* what);
+// Checks the launch that was just made; counts it on success.
+dial_status check_launch(const char* kernel_name);
+void clear_error();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline cudaStream_t as_stream(dial_stream s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Number of SMs of the current device (cached per device ordinal).
+int sm_count();
+
+// ---------------------------------------------------------------- device side
+template <typename T>
+struct Act;
+template <>
+struct Act<float> {
+  static __device__ __forceinline__ float to_f32(float v) { return v; }
+  static __device__ __forceinline__ float from_f32(float v) { return v; }
+};
+template <>
+struct Act<__half> {
+  static __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f32(float v) { return __float2half_rn(v); }
+};
+template <>
+struct Act<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f32(float v) { return __float2bfloat16_rn(v); }
+};
+
+// Streaming 128-bit load: read-only path, do not keep the line in L1.
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Read-only 128-bit load that may stay in L1 (activations reused across warps).
+__device__ __forceinline__ uint4 ld_ro16(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+}  // namespace dial

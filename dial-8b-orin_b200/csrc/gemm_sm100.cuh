@@ -1,0 +1,18 @@
+// Prefill dequant-GEMM on the sm_100a tensor cores (tcgen05 + TMEM), gemm_sm100.cu.
+#pragma once
+
+#include "common.cuh"
+
+namespace dial {
+
+// True when the tcgen05 GEMM takes this shape (else the caller uses the skinny kernel).
+bool gemm_sm100_supported(int64_t M, int64_t K, int64_t N);
+size_t gemm_sm100_gguf_workspace_bytes(int64_t M, int64_t K);
+dial_status launch_w8a16_gemm_sm100(const void* x, dial_dtype xdt, const int8_t* q,
+                                    const void* scale, dial_dtype sdt, void* y, int64_t M,
+                                    int64_t K, int64_t N, cudaStream_t st);
+dial_status launch_gguf_gemm_sm100(const void* x, dial_dtype xdt, const void* qs,
+                                   const uint16_t* d, int type, void* y, int64_t M, int64_t K,
+                                   int64_t N, void* ws, cudaStream_t st);
+
+}  // namespace dial

@@ -1,0 +1,32 @@
+// Launchers implemented in quant.cu, skinny.cu and gemm_sm100.cu.
+#pragma once
+
+#include "common.cuh"
+
+namespace dial {
+
+dial_status launch_w8a16_quantize(const void* w, dial_dtype wdt, int64_t N, int64_t K, int8_t* q,
+                                  void* scale, dial_dtype sdt, cudaStream_t st);
+dial_status launch_w8a16_dequantize(const int8_t* q, const void* scale, dial_dtype sdt, int64_t N,
+                                    int64_t K, void* w, dial_dtype wdt, cudaStream_t st);
+dial_status launch_gguf_repack(const void* blocks, int type, int64_t N, int64_t K, void* qs,
+                               uint16_t* d, cudaStream_t st);
+dial_status launch_gguf_unpack(const void* qs, const uint16_t* d, int type, int64_t N, int64_t K,
+                               void* blocks, cudaStream_t st);
+dial_status launch_gguf_quantize(const float* w, int type, int64_t N, int64_t K, void* qs,
+                                 uint16_t* d, cudaStream_t st);
+dial_status launch_gguf_dequantize(const void* qs, const uint16_t* d, int type, int64_t N,
+                                   int64_t K, void* w, dial_dtype wdt, cudaStream_t st);
+
+// Skinny (small-M) register-dequant tensor-core kernels, skinny.cu.
+constexpr int kSkinnyMaxM = 32;
+dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
+                                dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
+                                cudaStream_t st);
+// GGUF integer path: activations quantised to Q8_0 in `ws` first.
+size_t gguf_skinny_workspace_bytes(int64_t M, int64_t K);
+dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,
+                               int type, void* y, int64_t M, int64_t K, int64_t N, void* ws,
+                               cudaStream_t st);
+
+}  // namespace dial

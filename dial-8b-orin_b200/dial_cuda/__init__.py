@@ -1,0 +1,286 @@
+"""Python front-end of libdial_cuda.so (the C ABI in include/dial_cuda.h).
+
+This mirrors the reference's linear-module interface so a caller that used
+DIAL's `TextLinear` finds the same shape of API:
+
+  reference (lisa301/DIAL-8B-orin)                          here
+  TextLinear::from_dense        worker_w8a16.rs:78-101      TextLinear.from_dense
+  TextLinear::forward           worker_w8a16.rs:103-121     TextLinear.forward
+  CudaW8A16Linear::from_linear  worker_w8a16.rs:301-366     W8A16Linear.from_linear
+  CudaW8A16Linear::forward      worker_w8a16.rs:368-386     W8A16Linear.forward
+  load_worker_gguf_linear       worker_gguf.rs:462-522      GgufLinear.from_blocks
+  forward_worker_gguf           worker_gguf.rs:574-611      GgufLinear.forward
+  QTensor::dequantize(_f16)     worker_gguf.rs:56-63        GgufLinear.dequantize
+
+torch is used only for device memory and the current CUDA stream; all
+arithmetic runs in the library's sm_100a kernels.  There is no CPU fallback:
+if the library or a GPU is missing, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.dirname(_HERE)
+LIB_PATH = os.path.join(PKG_ROOT, "_build", "libdial_cuda.so")
+
+F32, F16, BF16 = 0, 1, 2
+Q4_0, Q8_0 = 2, 8
+
+STATUS = {
+    0: "ok", 1: "invalid argument", 2: "unsupported dtype", 3: "misaligned", 4: "shape",
+    5: "CUDA error", 6: "NCCL error", 7: "timeout", 8: "no device",
+}
+
+
+class DialError(RuntimeError):
+    def __init__(self, status: int, where: str, message: str):
+        super().__init__(f"{where}: {STATUS.get(status, status)} ({status}): {message}")
+        self.status = status
+
+
+_lib: Optional[ctypes.CDLL] = None
+
+# name -> (argtypes, restype); kept in the order of include/dial_cuda.h
+_vp, _i64, _i32, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+SIGNATURES = {
+    "dial_status_string": ([_i32], ctypes.c_char_p),
+    "dial_last_error": ([], ctypes.c_char_p),
+    "dial_abi_version": ([], _i32),
+    "dial_launch_count": ([], ctypes.c_uint64),
+    "dial_w8a16_quantize": ([_vp, _i32, _i64, _i64, _vp, _vp, _i32, _vp], _i32),
+    "dial_w8a16_dequantize": ([_vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp], _i32),
+    "dial_w8a16_linear": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp], _i32),
+    "dial_gguf_qs_bytes": ([_i32, _i64, _i64], _sz),
+    "dial_gguf_d_bytes": ([_i64, _i64], _sz),
+    "dial_gguf_repack": ([_vp, _i32, _i64, _i64, _vp, _vp, _vp], _i32),
+    "dial_gguf_unpack": ([_vp, _vp, _i32, _i64, _i64, _vp, _vp], _i32),
+    "dial_gguf_quantize": ([_vp, _i32, _i64, _i64, _vp, _vp, _vp], _i32),
+    "dial_gguf_dequantize": ([_vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp], _i32),
+    "dial_gguf_linear_workspace_bytes": ([_i64, _i64], _sz),
+    "dial_gguf_linear": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp, _sz, _vp], _i32),
+}
+
+
+def lib() -> ctypes.CDLL:
+    """Load libdial_cuda.so; raises (never falls back) if it is missing."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C {PKG_ROOT}` "
+                               "(or __graft_entry__.build()); there is no fallback path")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (argtypes, restype) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = L
+    return _lib
+
+
+def check(status: int, where: str) -> None:
+    if status != 0:
+        raise DialError(status, where, lib().dial_last_error().decode(errors="replace"))
+
+
+def launch_count() -> int:
+    return int(lib().dial_launch_count())
+
+
+# ------------------------------------------------------------------ torch plumbing
+def _torch():
+    import torch  # noqa: PLC0415  (torch is plumbing: device memory and streams)
+    return torch
+
+
+def _require_cuda(t) -> None:
+    if not t.is_cuda:
+        raise RuntimeError("dial_cuda ops take CUDA tensors; there is no CPU path")
+    if not t.is_contiguous():
+        raise RuntimeError("dial_cuda ops take contiguous tensors")
+
+
+def dtype_code(dt) -> int:
+    torch = _torch()
+    if dt == torch.float32:
+        return F32
+    if dt == torch.float16:
+        return F16
+    if dt == torch.bfloat16:
+        return BF16
+    raise TypeError(f"unsupported dtype {dt}")
+
+
+def stream_ptr(stream=None) -> int:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+# ------------------------------------------------------------------ W8A16
+class W8A16Linear:
+    """Per-output-row int8 weight + scale, f16/bf16 activations (CudaW8A16Linear)."""
+
+    def __init__(self, qweight, scales, in_dim: int, out_dim: int, name: str = ""):
+        self.qweight, self.scales = qweight, scales
+        self.in_dim, self.out_dim, self.name = in_dim, out_dim, name
+
+    @classmethod
+    def from_linear(cls, name: str, weight, scale_dtype=None) -> "W8A16Linear":
+        """Quantise a dense [out, in] f32/f16 CUDA weight on the GPU (bit-exact with
+        worker_w8a16.rs:322-341).  The reference stores f32 scales; f16 is allowed."""
+        torch = _torch()
+        _require_cuda(weight)
+        if weight.dim() != 2:
+            raise ValueError("weight must be [out_dim, in_dim]")
+        if weight.dtype not in (torch.float32, torch.float16):
+            raise TypeError(f"expected f32/f16 weight, got {weight.dtype}")
+        scale_dtype = scale_dtype or torch.float32
+        N, K = weight.shape
+        q = torch.empty((N, K), dtype=torch.int8, device=weight.device)
+        s = torch.empty((N,), dtype=scale_dtype, device=weight.device)
+        check(lib().dial_w8a16_quantize(weight.data_ptr(), dtype_code(weight.dtype), N, K,
+                                        q.data_ptr(), s.data_ptr(), dtype_code(scale_dtype),
+                                        stream_ptr()), "dial_w8a16_quantize")
+        return cls(q, s, K, N, name)
+
+    def forward(self, x, out=None):
+        """x [..., in_dim] f16/bf16 -> [..., out_dim] same dtype (worker_w8a16.rs:368-386)."""
+        torch = _torch()
+        _require_cuda(x)
+        if x.dtype not in (torch.float16, torch.bfloat16):
+            raise TypeError(f"W8A16 expects F16/BF16 activation, got {x.dtype}")
+        if x.shape[-1] != self.in_dim:
+            raise ValueError(f"W8A16 input mismatch: expected last dim {self.in_dim}, got {tuple(x.shape)}")
+        rows = x.numel() // self.in_dim
+        if out is None:
+            out = torch.empty((*x.shape[:-1], self.out_dim), dtype=x.dtype, device=x.device)
+        check(lib().dial_w8a16_linear(x.data_ptr(), dtype_code(x.dtype), self.qweight.data_ptr(),
+                                      self.scales.data_ptr(), dtype_code(self.scales.dtype),
+                                      out.data_ptr(), rows, self.in_dim, self.out_dim,
+                                      stream_ptr()), "dial_w8a16_linear")
+        return out
+
+    __call__ = forward
+
+    def dequantize(self, dtype=None):
+        torch = _torch()
+        dtype = dtype or torch.float32
+        w = torch.empty((self.out_dim, self.in_dim), dtype=dtype, device=self.qweight.device)
+        check(lib().dial_w8a16_dequantize(self.qweight.data_ptr(), self.scales.data_ptr(),
+                                          dtype_code(self.scales.dtype), self.out_dim, self.in_dim,
+                                          w.data_ptr(), dtype_code(dtype), stream_ptr()),
+              "dial_w8a16_dequantize")
+        return w
+
+    @property
+    def weight_bytes(self) -> int:
+        return self.qweight.numel() + self.scales.numel() * self.scales.element_size()
+
+
+# ------------------------------------------------------------------ GGUF
+class GgufLinear:
+    """Q4_0 / Q8_0 weight in the split device layout (candle QMatMul equivalent)."""
+
+    def __init__(self, qs, d, qtype: int, in_dim: int, out_dim: int, name: str = ""):
+        self.qs, self.d, self.qtype = qs, d, qtype
+        self.in_dim, self.out_dim, self.name = in_dim, out_dim, name
+        self._ws = None
+
+    @staticmethod
+    def _alloc(qtype: int, N: int, K: int, device):
+        torch = _torch()
+        qs = torch.empty(lib().dial_gguf_qs_bytes(qtype, N, K), dtype=torch.uint8, device=device)
+        d = torch.empty(lib().dial_gguf_d_bytes(N, K) // 2, dtype=torch.int16, device=device)
+        return qs, d
+
+    @classmethod
+    def from_blocks(cls, blocks, qtype: int, in_dim: int, out_dim: int, name: str = "") -> "GgufLinear":
+        """blocks: CUDA uint8 tensor holding the native GGUF blocks of an [out_dim, in_dim]
+        tensor (what load_worker_gguf_linear reads from the file)."""
+        _require_cuda(blocks)
+        qs, d = cls._alloc(qtype, out_dim, in_dim, blocks.device)
+        check(lib().dial_gguf_repack(blocks.data_ptr(), qtype, out_dim, in_dim, qs.data_ptr(),
+                                     d.data_ptr(), stream_ptr()), "dial_gguf_repack")
+        return cls(qs, d, qtype, in_dim, out_dim, name)
+
+    @classmethod
+    def quantize(cls, weight, qtype: int, name: str = "") -> "GgufLinear":
+        """GGML reference quantiser on the GPU from a dense f32 [out, in] weight."""
+        torch = _torch()
+        _require_cuda(weight)
+        if weight.dtype != torch.float32:
+            raise TypeError("GGUF quantiser takes f32 weights")
+        N, K = weight.shape
+        qs, d = cls._alloc(qtype, N, K, weight.device)
+        check(lib().dial_gguf_quantize(weight.data_ptr(), qtype, N, K, qs.data_ptr(), d.data_ptr(),
+                                       stream_ptr()), "dial_gguf_quantize")
+        return cls(qs, d, qtype, K, N, name)
+
+    def to_blocks(self):
+        torch = _torch()
+        bb = 18 if self.qtype == Q4_0 else 34
+        out = torch.empty(self.out_dim * (self.in_dim // 32) * bb, dtype=torch.uint8, device=self.qs.device)
+        check(lib().dial_gguf_unpack(self.qs.data_ptr(), self.d.data_ptr(), self.qtype, self.out_dim,
+                                     self.in_dim, out.data_ptr(), stream_ptr()), "dial_gguf_unpack")
+        return out
+
+    def dequantize(self, dtype=None):
+        torch = _torch()
+        dtype = dtype or torch.float32
+        w = torch.empty((self.out_dim, self.in_dim), dtype=dtype, device=self.qs.device)
+        check(lib().dial_gguf_dequantize(self.qs.data_ptr(), self.d.data_ptr(), self.qtype,
+                                         self.out_dim, self.in_dim, w.data_ptr(), dtype_code(dtype),
+                                         stream_ptr()), "dial_gguf_dequantize")
+        return w
+
+    def workspace(self, rows: int):
+        torch = _torch()
+        need = lib().dial_gguf_linear_workspace_bytes(rows, self.in_dim)
+        if need and (self._ws is None or self._ws.numel() < need):
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.qs.device)
+        return self._ws, need
+
+    def forward(self, x, out=None):
+        """x [..., in_dim] f32/f16/bf16 -> [..., out_dim] in x's dtype (worker_gguf.rs:574-611)."""
+        torch = _torch()
+        _require_cuda(x)
+        if x.shape[-1] != self.in_dim:
+            raise ValueError(f"GGUF input mismatch: expected last dim {self.in_dim}, got {tuple(x.shape)}")
+        rows = x.numel() // self.in_dim
+        if out is None:
+            out = torch.empty((*x.shape[:-1], self.out_dim), dtype=x.dtype, device=x.device)
+        ws, need = self.workspace(rows)
+        check(lib().dial_gguf_linear(x.data_ptr(), dtype_code(x.dtype), self.qs.data_ptr(),
+                                     self.d.data_ptr(), self.qtype, out.data_ptr(), rows, self.in_dim,
+                                     self.out_dim, ws.data_ptr() if need else None, need,
+                                     stream_ptr()), "dial_gguf_linear")
+        return out
+
+    __call__ = forward
+
+    @property
+    def weight_bytes(self) -> int:
+        return self.qs.numel() + self.d.numel() * 2
+
+
+class TextLinear:
+    """Dispatch wrapper with the reference's constructor names (worker_w8a16.rs:65-121)."""
+
+    def __init__(self, inner):
+        self.inner = inner
+
+    @classmethod
+    def from_dense(cls, name: str, weight, scale_dtype=None) -> "TextLinear":
+        return cls(W8A16Linear.from_linear(name, weight, scale_dtype))
+
+    @classmethod
+    def from_gguf(cls, name: str, blocks, qtype: int, in_dim: int, out_dim: int) -> "TextLinear":
+        return cls(GgufLinear.from_blocks(blocks, qtype, in_dim, out_dim, name))
+
+    def forward(self, x, out=None):
+        return self.inner.forward(x, out)
+
+    __call__ = forward

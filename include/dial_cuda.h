@@ -1,0 +1,149 @@
+/*
+ * dial_cuda.h -- C ABI of the B200 (sm_100a) quantized-linear hot path of DIAL.
+ *
+ * Plain pointers and sizes only.  All tensor pointers are DEVICE pointers
+ * unless a comment says otherwise; `stream` is a cudaStream_t (NULL = legacy
+ * default stream).  No entry point allocates device memory: outputs and
+ * workspaces come from the caller, which matches the reference's ownership
+ * (the linear owns its device weights, activations are borrowed and
+ * contiguous, the output is allocated by the caller side).
+ *
+ * Every entry point returns a dial_status and never throws or aborts across
+ * the boundary; `dial_last_error()` gives a thread-local message for the last
+ * failure on the calling thread.  Launch errors are checked right after each
+ * launch.
+ *
+ * Reference interfaces replaced (paths inside lisa301/DIAL-8B-orin):
+ *   TextLinear::{from_dense, forward}          dial-core/src/models/qwen3_vl/worker_w8a16.rs:65-121
+ *   CudaW8A16Linear::{from_linear, forward}     worker_w8a16.rs:301-386
+ *   CustomOp1::cuda_fwd (NVRTC kernels)         worker_w8a16.rs:402-475 (kernels :146-224)
+ *   load_worker_gguf_linear / forward_worker_gguf
+ *                                               dial-core/src/models/qwen3_vl/worker_gguf.rs:462-522, :574-611
+ *   QTensor::dequantize / dequantize_f16        worker_gguf.rs:56-63, worker_w8a16.rs:123-128
+ */
+#ifndef DIAL_CUDA_H_
+#define DIAL_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DIAL_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define DIAL_API __attribute__((visibility("default")))
+#else
+#define DIAL_API
+#endif
+
+typedef int dial_status;
+enum {
+  DIAL_OK = 0,
+  DIAL_ERR_INVALID_ARG = 1,       /* null pointer, non-positive size, bad enum */
+  DIAL_ERR_UNSUPPORTED_DTYPE = 2, /* dtype combination the op does not support */
+  DIAL_ERR_MISALIGNED = 3,        /* pointer or row stride breaks the 16-byte rule */
+  DIAL_ERR_SHAPE = 4,             /* K not a multiple of the block / vector width */
+  DIAL_ERR_CUDA = 5,              /* CUDA runtime error (message in dial_last_error) */
+  DIAL_ERR_NCCL = 6,              /* NCCL error in the stage pipe */
+  DIAL_ERR_TIMEOUT = 7,           /* bounded wait ran out (device flag or host deadline) */
+  DIAL_ERR_NO_DEVICE = 8          /* no sm_100 device visible */
+};
+
+typedef enum { DIAL_F32 = 0, DIAL_F16 = 1, DIAL_BF16 = 2 } dial_dtype;
+
+/* GGML type codes, as in the GGUF file format. */
+typedef enum { DIAL_GGML_Q4_0 = 2, DIAL_GGML_Q8_0 = 8 } dial_ggml_type;
+
+typedef void* dial_stream; /* cudaStream_t */
+
+/* ------------------------------------------------------------------ misc */
+DIAL_API const char* dial_status_string(dial_status s);
+/* Thread-local description of the last failure on this thread ("" if none). */
+DIAL_API const char* dial_last_error(void);
+DIAL_API int dial_abi_version(void);
+/* Number of kernels launched by this library in this process (all threads). */
+DIAL_API uint64_t dial_launch_count(void);
+
+/* ------------------------------------------------------------------ W8A16
+ * Layout: q int8 [N, K] row-major (K contiguous), scale [N] (f32 as in the
+ * reference, or f16).  K must be a multiple of 16 and q 16-byte aligned.
+ */
+
+/* Per-output-row symmetric quantiser, bit-exact with worker_w8a16.rs:322-341:
+ * scale = absmax/127 (1.0 for an all-zero row), q = clamp(round(w * (1/scale)),
+ * -127, 127) with round-half-away-from-zero.  w is [N, K] f32 or f16 (f16 is
+ * widened to f32 first, as the reference does).  With sdt == DIAL_F16 the int8
+ * values are those of the f32 scale and the stored scale is its f16 rounding. */
+DIAL_API dial_status dial_w8a16_quantize(const void* w, dial_dtype wdt, int64_t N, int64_t K, int8_t* q,
+                                void* scale, dial_dtype sdt, dial_stream stream);
+
+/* w[n, k] = q[n, k] * scale[n], one f32 rounding, then converted to wdt. */
+DIAL_API dial_status dial_w8a16_dequantize(const int8_t* q, const void* scale, dial_dtype sdt, int64_t N,
+                                  int64_t K, void* w, dial_dtype wdt, dial_stream stream);
+
+/* y[m, n] = round_ydt( (sum_k f32(q[n,k]) * f32(x[m,k])) * scale[n] ), f32
+ * accumulation (worker_w8a16.rs:158-181).  x is [M, K] f16 or bf16, y is
+ * [M, N] in the same dtype (the reference is f16 in / f16 out).  Any M >= 1;
+ * the kernel is picked by M (decode GEMV, small-M tensor-core tile, or the
+ * tcgen05 dequant-GEMM). */
+DIAL_API dial_status dial_w8a16_linear(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
+                              dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
+                              dial_stream stream);
+
+/* ------------------------------------------------------------------ GGUF
+ * Native block layout (what a GGUF file holds and candle uploads):
+ *   Q4_0: 18-byte blocks {f16 d; u8 qs[16]} per 32 weights, element j in the
+ *         low nibble of qs[j], element j+16 in the high nibble;
+ *   Q8_0: 34-byte blocks {f16 d; i8 qs[32]}.
+ * Blocks are row-major over [N, K/32].  On the device the linear keeps a
+ * split layout made once at load by dial_gguf_repack, in groups of 4 blocks
+ * (G = ceil(K/128) groups per row, missing blocks zero-padded):
+ *   d  : f16 [N, 4*G]                      (dial_gguf_d_bytes)
+ *   qs : u8  [N, G*64] (Q4_0) or [N, G*128] (Q8_0)   (dial_gguf_qs_bytes)
+ * with the bytes of a group interleaved so that each 16-byte load is one
+ * lane's slice of an int8 tensor-core fragment (dial-8b-orin_b200/csrc/layout.cuh
+ * gives the byte map).  Values and scales are unchanged, so dequantised
+ * weights stay bit-exact.  K must be a multiple of 32.
+ */
+DIAL_API size_t dial_gguf_qs_bytes(dial_ggml_type type, int64_t N, int64_t K);
+DIAL_API size_t dial_gguf_d_bytes(int64_t N, int64_t K);
+
+/* Native blocks -> split (qs, d) device layout.  `blocks` is a device pointer. */
+DIAL_API dial_status dial_gguf_repack(const void* blocks, dial_ggml_type type, int64_t N, int64_t K,
+                             void* qs, uint16_t* d, dial_stream stream);
+
+/* Split layout -> native blocks (inverse of dial_gguf_repack). */
+DIAL_API dial_status dial_gguf_unpack(const void* qs, const uint16_t* d, dial_ggml_type type, int64_t N,
+                             int64_t K, void* blocks, dial_stream stream);
+
+/* GGML reference quantiser (quantize_row_q4_0_ref / quantize_row_q8_0_ref,
+ * which candle's QTensor::quantize restates), w [N, K] f32 -> split layout. */
+DIAL_API dial_status dial_gguf_quantize(const float* w, dial_ggml_type type, int64_t N, int64_t K,
+                               void* qs, uint16_t* d, dial_stream stream);
+
+/* w[n, k] = f32(d) * q, bit-exact with GGML dequantize_row_*, then to wdt. */
+DIAL_API dial_status dial_gguf_dequantize(const void* qs, const uint16_t* d, dial_ggml_type type,
+                                 int64_t N, int64_t K, void* w, dial_dtype wdt,
+                                 dial_stream stream);
+
+/* y = x . deq(W)^T.  x [M, K] f32/f16/bf16, y [M, N] in the same dtype
+ * (forward_worker_gguf keeps the activation dtype, worker_gguf.rs:589-605).
+ * Small M (<= 32 rows per pass): activations are quantised to Q8_0 blocks and
+ * every block is an exact integer dot scaled in f32 (candle's CPU QMatMul
+ * arithmetic).  Larger M: weights are dequantised to f16/bf16 tiles feeding
+ * tensor-core MMAs with f32 accumulation.  K % 32 == 0.  `workspace` must hold
+ * dial_gguf_linear_workspace_bytes(M, K) bytes (16-byte aligned; may be NULL
+ * when that is 0). */
+DIAL_API size_t dial_gguf_linear_workspace_bytes(int64_t M, int64_t K);
+DIAL_API dial_status dial_gguf_linear(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,
+                             dial_ggml_type type, void* y, int64_t M, int64_t K, int64_t N,
+                             void* workspace, size_t workspace_bytes, dial_stream stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* DIAL_CUDA_H_ */

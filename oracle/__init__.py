@@ -1,0 +1,206 @@
+"""ctypes front-end for the CPU oracle (oracle/dial_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU-baseline leg of bench.py as the checker.  The product library in
+dial-8b-orin_b200/ never imports this module and never falls back to it.
+
+Every function here follows the reference file:line cited in dial_oracle.c.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libdial_oracle.so")
+
+F32, F16, BF16 = 0, 1, 2
+Q4_0, Q8_0 = 2, 8
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34}
+
+_lib = None
+
+
+def build() -> str:
+    """Compile the oracle with oracle/Makefile (no-op when up to date)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(
+            os.path.join(_HERE, "dial_oracle.c")
+        ):
+            build()
+        _lib = ctypes.CDLL(_LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+def _declare(L: ctypes.CDLL) -> None:
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    sig = {
+        "orc_f32_to_f16": ([vp, vp, i64], None),
+        "orc_f16_to_f32": ([vp, vp, i64], None),
+        "orc_f32_to_bf16": ([vp, vp, i64], None),
+        "orc_bf16_to_f32": ([vp, vp, i64], None),
+        "orc_num_threads": ([], i32),
+        "orc_w8a16_quantize": ([vp, i32, i64, i64, vp, vp, vp], None),
+        "orc_w8a16_dequantize": ([vp, vp, i32, i64, i64, vp], None),
+        "orc_w8a16_linear": ([vp, i32, vp, vp, i32, i64, i64, i64, vp, vp], None),
+        "orc_w8a16_linear_f32": ([vp, vp, vp, i64, i64, i64, vp], None),
+        "orc_gguf_block_bytes": ([i32], i64),
+        "orc_gguf_quantize": ([vp, i32, i64, i64, vp], i32),
+        "orc_gguf_dequantize": ([vp, i32, i64, i64, vp], i32),
+        "orc_gguf_linear_exact": ([vp, i32, vp, i32, i64, i64, i64, vp], i32),
+        "orc_gguf_linear_candle": ([vp, i32, vp, i32, i64, i64, i64, vp], i32),
+        "orc_q8_0_quantize_rows": ([vp, i32, i64, i64, vp, vp], i32),
+    }
+    for name, (argtypes, restype) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _dt(a: np.ndarray, bf16: bool = False) -> int:
+    if a.dtype == np.float32:
+        return F32
+    if a.dtype == np.float16:
+        return F16
+    if a.dtype == np.uint16 and bf16:
+        return BF16
+    raise TypeError(f"unsupported activation dtype {a.dtype}")
+
+
+# ---------------------------------------------------------------- conversions
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib().orc_f32_to_bf16(_p(x), _p(out), x.size)
+    return out
+
+
+def bf16_to_f32(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    out = np.empty(x.shape, np.float32)
+    lib().orc_bf16_to_f32(_p(x), _p(out), x.size)
+    return out
+
+
+def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib().orc_f32_to_f16(_p(x), _p(out), x.size)
+    return out
+
+
+# ---------------------------------------------------------------- W8A16
+def w8a16_quantize(w: np.ndarray):
+    """w [N,K] f32 or f16 -> (q int8 [N,K], scale f32 [N], scale f16 [N])."""
+    w = np.ascontiguousarray(w)
+    N, K = w.shape
+    q = np.empty((N, K), np.int8)
+    s32 = np.empty(N, np.float32)
+    s16 = np.empty(N, np.uint16)
+    lib().orc_w8a16_quantize(_p(w), _dt(w), N, K, _p(q), _p(s32), _p(s16))
+    return q, s32, s16.view(np.float16)
+
+
+def w8a16_dequantize(q: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    scale = np.ascontiguousarray(scale)
+    N, K = q.shape
+    out = np.empty((N, K), np.float32)
+    lib().orc_w8a16_dequantize(_p(q), _p(scale), _dt(scale), N, K, _p(out))
+    return out
+
+
+def w8a16_linear(x: np.ndarray, q: np.ndarray, scale: np.ndarray, x_is_bf16: bool = False):
+    """x [M,K] (f16, or uint16 bf16 bits) -> (y_f32 [M,N] pre-rounding, y_half [M,N] bits)."""
+    x = np.ascontiguousarray(x)
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    scale = np.ascontiguousarray(scale)
+    M, K = x.shape
+    N = q.shape[0]
+    y = np.empty((M, N), np.float32)
+    yh = np.empty((M, N), np.uint16)
+    lib().orc_w8a16_linear(_p(x), _dt(x, x_is_bf16), _p(q), _p(scale), _dt(scale), M, K, N,
+                           _p(y), _p(yh))
+    return y, yh
+
+
+def w8a16_linear_f32(x_f16: np.ndarray, q: np.ndarray, scale_f32: np.ndarray) -> np.ndarray:
+    x_f16 = np.ascontiguousarray(x_f16, dtype=np.float16)
+    M, K = x_f16.shape
+    N = q.shape[0]
+    y = np.empty((M, N), np.float16)
+    lib().orc_w8a16_linear_f32(_p(x_f16), _p(q), _p(np.ascontiguousarray(scale_f32, np.float32)),
+                               M, K, N, _p(y))
+    return y
+
+
+# ---------------------------------------------------------------- GGUF
+def gguf_quantize(w: np.ndarray, qtype: int) -> np.ndarray:
+    """w [N,K] f32 -> native GGML blocks, uint8 [N, K/32*block_bytes]."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    out = np.empty((N, K // 32 * BLOCK_BYTES[qtype]), np.uint8)
+    rc = lib().orc_gguf_quantize(_p(w), qtype, N, K, _p(out))
+    assert rc == 0
+    return out
+
+
+def gguf_dequantize(blocks: np.ndarray, qtype: int, N: int, K: int) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty((N, K), np.float32)
+    rc = lib().orc_gguf_dequantize(_p(blocks), qtype, N, K, _p(out))
+    assert rc == 0
+    return out
+
+
+def gguf_linear_exact(x: np.ndarray, blocks: np.ndarray, qtype: int, N: int,
+                      x_is_bf16: bool = False) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    M, K = x.shape
+    y = np.empty((M, N), np.float64)
+    rc = lib().orc_gguf_linear_exact(_p(x), _dt(x, x_is_bf16), _p(np.ascontiguousarray(blocks)),
+                                     qtype, M, K, N, _p(y))
+    assert rc == 0
+    return y
+
+
+def gguf_linear_candle(x: np.ndarray, blocks: np.ndarray, qtype: int, N: int,
+                       x_is_bf16: bool = False) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    M, K = x.shape
+    y = np.empty((M, N), np.float32)
+    rc = lib().orc_gguf_linear_candle(_p(x), _dt(x, x_is_bf16), _p(np.ascontiguousarray(blocks)),
+                                      qtype, M, K, N, _p(y))
+    assert rc == 0
+    return y
+
+
+def q8_0_quantize_rows(x: np.ndarray, x_is_bf16: bool = False):
+    x = np.ascontiguousarray(x)
+    M, K = x.shape
+    qs = np.empty((M, K), np.int8)
+    d = np.empty((M, K // 32), np.uint16)
+    rc = lib().orc_q8_0_quantize_rows(_p(x), _dt(x, x_is_bf16), M, K, _p(qs), _p(d))
+    assert rc == 0
+    return qs, d.view(np.float16)
+
+
+def num_threads() -> int:
+    return int(lib().orc_num_threads())

@@ -1,0 +1,394 @@
+/*
+ * dial_oracle.c -- CPU restatement of DIAL's quantized-linear hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA kernels in
+ * dial-8b-orin_b200/csrc: only tests/, __graft_entry__.smoke() and the CPU
+ * baseline leg of bench.py load it.  No product code path calls it, and the
+ * product library fails loudly instead of falling back to it.
+ *
+ * Parity anchors (paths are inside the reference project lisa301/DIAL-8B-orin):
+ *  - W8A16 quantiser: dial-core/src/models/qwen3_vl/worker_w8a16.rs:322-341
+ *    (CPU twin dial-core/src/models/qwen3_vl/text.rs:265-278).  Pinned by the
+ *    reference's own known-answer test worker_w8a16.rs:483-516, restated in
+ *    tests/test_oracle_golden.py.
+ *  - W8A16 linear: worker_w8a16.rs:158-181 and :202-222 -- f32 accumulation of
+ *    f32(int8) * f32(f16 x), scale applied after the sum, f16 round-to-nearest.
+ *  - GGUF Q4_0 / Q8_0: the arithmetic lives in candle-core 0.11.0
+ *    (Cargo.lock:509-512, not vendored).  Call sites: worker_gguf.rs:500-505
+ *    (QMatMul::from_arc), :593 and :609-610 (forward), :60-61 (dequantize).
+ *    Restated from the published GGML block format (ggml-quants reference
+ *    quantisers quantize_row_q4_0_ref / quantize_row_q8_0_ref and candle's
+ *    k_quants vec_dot_q4_0_q8_0 / vec_dot_q8_0_q8_0).  Pinned against the
+ *    independent `gguf` 0.19.0 Python implementation through the fixtures in
+ *    tests/golden/ (script: tests/golden/make_golden.py).  candle equality
+ *    itself cannot be checked here (no Rust toolchain, candle not vendored).
+ *  - Decoder glue: text.rs:1478-1596 (attention order), text.rs:1636-1688
+ *    (residuals), text.rs:816-820 (SwiGLU), llama3/cache.rs:24-64 (RoPE
+ *    tables), cache.rs:149-217 (KV append), qwen3_vl.rs:130-143 (argmax).
+ *
+ * Build: oracle/Makefile (gcc -O3 -fopenmp -ffp-contract=off).  Contraction
+ * must stay off: the GGML quantisers compute `x*id + 8.5f` as two roundings.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define ORC_API __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------------ */
+/* half / bfloat16 conversions (IEEE round-to-nearest-even)                  */
+/* ------------------------------------------------------------------------ */
+
+static inline uint32_t f32_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float bits_f32(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+static inline float h2f(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1fu;
+  uint32_t man = h & 0x3ffu;
+  if (exp == 0) {
+    if (man == 0) return bits_f32(sign);
+    /* subnormal: value = man * 2^-24 (exact in f32) */
+    float v = (float)man * 5.9604644775390625e-8f;
+    return sign ? -v : v;
+  }
+  if (exp == 31) return bits_f32(sign | 0x7f800000u | (man << 13));
+  return bits_f32(sign | ((exp + 112u) << 23) | (man << 13));
+}
+
+static inline uint16_t f2h(float f) {
+  uint32_t x = f32_bits(f);
+  uint32_t sign = (x >> 16) & 0x8000u;
+  uint32_t ax = x & 0x7fffffffu;
+  if (ax >= 0x7f800000u) return (uint16_t)(sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0));
+  if (ax >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u); /* rounds to inf */
+  if (ax < 0x38800000u) {
+    /* result is subnormal or zero: round ax * 2^24 to an integer (RNE) */
+    float a = bits_f32(ax);
+    float scaled = a * 16777216.0f; /* exact: power of two */
+    /* nearbyintf uses the current rounding mode (nearest-even by default) */
+    uint32_t m = (uint32_t)nearbyintf(scaled);
+    return (uint16_t)(sign | m);
+  }
+  uint32_t exp = (ax >> 23) - 112u;
+  uint32_t man = ax & 0x7fffffu;
+  uint32_t h = (exp << 10) | (man >> 13);
+  uint32_t rem = man & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h += 1u;
+  return (uint16_t)(sign | h);
+}
+
+static inline float bf2f(uint16_t b) { return bits_f32((uint32_t)b << 16); }
+
+static inline uint16_t f2bf(float f) {
+  uint32_t x = f32_bits(f);
+  if ((x & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((x >> 16) | 0x40u);
+  uint32_t lsb = (x >> 16) & 1u;
+  x += 0x7fffu + lsb;
+  return (uint16_t)(x >> 16);
+}
+
+/* dtype codes shared with include/dial_cuda.h */
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_BF16 = 2 };
+
+static inline float load_act(const void* p, int dt, int64_t i) {
+  switch (dt) {
+    case ORC_F16: return h2f(((const uint16_t*)p)[i]);
+    case ORC_BF16: return bf2f(((const uint16_t*)p)[i]);
+    default: return ((const float*)p)[i];
+  }
+}
+
+static inline void store_act(void* p, int dt, int64_t i, float v) {
+  switch (dt) {
+    case ORC_F16: ((uint16_t*)p)[i] = f2h(v); break;
+    case ORC_BF16: ((uint16_t*)p)[i] = f2bf(v); break;
+    default: ((float*)p)[i] = v; break;
+  }
+}
+
+ORC_API void orc_f32_to_f16(const float* in, uint16_t* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = f2h(in[i]);
+}
+ORC_API void orc_f16_to_f32(const uint16_t* in, float* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = h2f(in[i]);
+}
+ORC_API void orc_f32_to_bf16(const float* in, uint16_t* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = f2bf(in[i]);
+}
+ORC_API void orc_bf16_to_f32(const uint16_t* in, float* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = bf2f(in[i]);
+}
+
+ORC_API int orc_num_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+/* ------------------------------------------------------------------------ */
+/* W8A16: per-output-row symmetric int8 (worker_w8a16.rs:322-341)           */
+/* ------------------------------------------------------------------------ */
+
+/* Rust's f32::round: half away from zero == C roundf. */
+static inline int8_t w8a16_q(float v, float inv_scale) {
+  float r = roundf(v * inv_scale);
+  if (r > 127.0f) r = 127.0f;
+  if (r < -127.0f) r = -127.0f;
+  return (int8_t)r;
+}
+
+/*
+ * w: [N, K] row-major, dtype wdt (F32, or F16 which the reference widens to
+ * f32 first, worker_w8a16.rs:323-327).  q: [N, K] int8.  scale_f32: [N].
+ * scale_f16 (optional): [N], the f32 scale rounded to f16 -- the int8 values
+ * are always those of the f32 scale, so they are identical for either scale
+ * dtype.
+ */
+ORC_API void orc_w8a16_quantize(const void* w, int wdt, int64_t N, int64_t K, int8_t* q,
+                                float* scale_f32, uint16_t* scale_f16) {
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n) {
+    float max_abs = 0.0f;
+    for (int64_t k = 0; k < K; ++k) {
+      float v = fabsf(load_act(w, wdt, n * K + k));
+      max_abs = max_abs > v ? max_abs : v; /* fold(0, max) */
+    }
+    float scale = max_abs > 0.0f ? max_abs / 127.0f : 1.0f;
+    float inv = 1.0f / scale;
+    for (int64_t k = 0; k < K; ++k) q[n * K + k] = w8a16_q(load_act(w, wdt, n * K + k), inv);
+    scale_f32[n] = scale;
+    if (scale_f16) scale_f16[n] = f2h(scale);
+  }
+}
+
+/* Dequantised weight value q * scale, in f32 (one rounding, bit-exact target). */
+ORC_API void orc_w8a16_dequantize(const int8_t* q, const void* scale, int sdt, int64_t N,
+                                  int64_t K, float* w) {
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n) {
+    float s = load_act(scale, sdt, n);
+    for (int64_t k = 0; k < K; ++k) w[n * K + k] = (float)q[n * K + k] * s;
+  }
+}
+
+/*
+ * y[m, n] = (sum_k f32(q[n,k]) * f32(x[m,k])) * scale[n]   (worker_w8a16.rs:158-181)
+ * The sum is accumulated in double here (the order-independent reference the
+ * GPU result is compared with); y_out gets the pre-rounding f32 value and,
+ * if y_half is given, its f16 (xdt F16) / bf16 (xdt BF16) rounding.
+ */
+ORC_API void orc_w8a16_linear(const void* x, int xdt, const int8_t* q, const void* scale,
+                              int sdt, int64_t M, int64_t K, int64_t N, float* y_out,
+                              uint16_t* y_half) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      double acc = 0.0;
+      const int8_t* row = q + n * K;
+      for (int64_t k = 0; k < K; ++k) acc += (double)row[k] * (double)load_act(x, xdt, m * K + k);
+      float v = (float)acc * load_act(scale, sdt, n);
+      y_out[m * N + n] = v;
+      if (y_half) y_half[m * N + n] = (xdt == ORC_BF16) ? f2bf(v) : f2h(v);
+    }
+  }
+}
+
+/* Same linear with the f32 sequential accumulation the reference kernel's
+ * single-thread order would give (used by the CPU baseline timing, which wants
+ * the reference's arithmetic cost, not double precision). */
+ORC_API void orc_w8a16_linear_f32(const uint16_t* x_f16, const int8_t* q, const float* scale,
+                                  int64_t M, int64_t K, int64_t N, uint16_t* y_f16) {
+  float* xf = (float*)malloc(sizeof(float) * (size_t)(M * K));
+  for (int64_t i = 0; i < M * K; ++i) xf[i] = h2f(x_f16[i]);
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      const int8_t* row = q + n * K;
+      const float* xr = xf + m * K;
+      float acc = 0.0f;
+      for (int64_t k = 0; k < K; ++k) acc += (float)row[k] * xr[k];
+      y_f16[m * N + n] = f2h(acc * scale[n]);
+    }
+  }
+  free(xf);
+}
+
+/* ------------------------------------------------------------------------ */
+/* GGUF Q4_0 / Q8_0 (published GGML block format)                            */
+/*   Q4_0 block: { f16 d; u8 qs[16]; }  18 bytes / 32 weights                 */
+/*     element j     = (qs[j] & 0xF) - 8,  element j+16 = (qs[j] >> 4) - 8     */
+/*   Q8_0 block: { f16 d; i8 qs[32]; }  34 bytes / 32 weights                 */
+/* ------------------------------------------------------------------------ */
+
+enum { ORC_Q4_0 = 2, ORC_Q8_0 = 8 };
+#define QK 32
+
+static void q4_0_block(const float* x, uint8_t* out) {
+  float amax = 0.0f, maxv = 0.0f;
+  for (int j = 0; j < QK; ++j) {
+    float v = x[j];
+    if (amax < fabsf(v)) { amax = fabsf(v); maxv = v; }
+  }
+  float d = maxv / -8.0f;
+  float id = d != 0.0f ? 1.0f / d : 0.0f;
+  uint16_t dh = f2h(d);
+  out[0] = (uint8_t)(dh & 0xff);
+  out[1] = (uint8_t)(dh >> 8);
+  for (int j = 0; j < QK / 2; ++j) {
+    float x0 = x[j] * id;
+    float x1 = x[QK / 2 + j] * id;
+    x0 = x0 + 8.5f;
+    x1 = x1 + 8.5f;
+    int i0 = (int)x0; /* C truncation == np.trunc for these finite values */
+    int i1 = (int)x1;
+    if (i0 > 15) i0 = 15;
+    if (i1 > 15) i1 = 15;
+    if (i0 < 0) i0 = 0; /* only reachable for NaN-free but id==0 inputs */
+    if (i1 < 0) i1 = 0;
+    out[2 + j] = (uint8_t)(i0 | (i1 << 4));
+  }
+}
+
+/* GGML quantize_row_q8_0_ref: d = amax/127, q = roundf(x / d) (via x * (1/d)). */
+static void q8_0_block(const float* x, uint8_t* out) {
+  float amax = 0.0f;
+  for (int j = 0; j < QK; ++j) {
+    float v = fabsf(x[j]);
+    amax = amax > v ? amax : v;
+  }
+  float d = amax / 127.0f;
+  float id = d != 0.0f ? 1.0f / d : 0.0f;
+  uint16_t dh = f2h(d);
+  out[0] = (uint8_t)(dh & 0xff);
+  out[1] = (uint8_t)(dh >> 8);
+  for (int j = 0; j < QK; ++j) out[2 + j] = (uint8_t)(int8_t)roundf(x[j] * id);
+}
+
+ORC_API int64_t orc_gguf_block_bytes(int type) {
+  return type == ORC_Q4_0 ? 18 : type == ORC_Q8_0 ? 34 : -1;
+}
+
+/* w: [N, K] f32, K % 32 == 0.  blocks: [N, K/32] blocks in native layout. */
+ORC_API int orc_gguf_quantize(const float* w, int type, int64_t N, int64_t K, uint8_t* blocks) {
+  int64_t bb = orc_gguf_block_bytes(type);
+  if (bb < 0 || K % QK) return -1;
+  int64_t nb = K / QK;
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t b = 0; b < nb; ++b) {
+      const float* src = w + n * K + b * QK;
+      uint8_t* dst = blocks + (n * nb + b) * bb;
+      if (type == ORC_Q4_0) q4_0_block(src, dst); else q8_0_block(src, dst);
+    }
+  }
+  return 0;
+}
+
+static inline float block_d(const uint8_t* blk) { return h2f((uint16_t)(blk[0] | (blk[1] << 8))); }
+
+static inline int block_q(const uint8_t* blk, int type, int j) {
+  if (type == ORC_Q8_0) return (int)(int8_t)blk[2 + j];
+  return j < QK / 2 ? (int)(blk[2 + j] & 0xf) - 8 : (int)(blk[2 + j - QK / 2] >> 4) - 8;
+}
+
+/* Dequantised value d * q in f32 (GGML dequantize_row_*; bit-exact target). */
+ORC_API int orc_gguf_dequantize(const uint8_t* blocks, int type, int64_t N, int64_t K, float* w) {
+  int64_t bb = orc_gguf_block_bytes(type);
+  if (bb < 0 || K % QK) return -1;
+  int64_t nb = K / QK;
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t b = 0; b < nb; ++b) {
+      const uint8_t* blk = blocks + (n * nb + b) * bb;
+      float d = block_d(blk);
+      for (int j = 0; j < QK; ++j) w[n * K + b * QK + j] = d * (float)block_q(blk, type, j);
+    }
+  }
+  return 0;
+}
+
+/* Exact linear on dequantised weights, double accumulation: y = x . deq(W)^T */
+ORC_API int orc_gguf_linear_exact(const void* x, int xdt, const uint8_t* blocks, int type,
+                                  int64_t M, int64_t K, int64_t N, double* y) {
+  int64_t bb = orc_gguf_block_bytes(type);
+  if (bb < 0 || K % QK) return -1;
+  int64_t nb = K / QK;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      double acc = 0.0;
+      for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = blocks + (n * nb + b) * bb;
+        double d = (double)block_d(blk);
+        double s = 0.0;
+        for (int j = 0; j < QK; ++j)
+          s += (double)block_q(blk, type, j) * (double)load_act(x, xdt, m * K + b * QK + j);
+        acc += d * s;
+      }
+      y[m * N + n] = acc;
+    }
+  }
+  return 0;
+}
+
+/*
+ * candle's CPU QMatMul semantics (k_quants.rs matmul + vec_dot): each
+ * activation row is quantised to Q8_0 blocks (same quantiser as weights,
+ * f16 d), then per block an exact integer dot, scaled in f32:
+ *     sumf += (f32)sumi * d_w * d_x          (sequential over blocks)
+ * y is f32 (the QMatMul output dtype for f32 input).
+ */
+ORC_API int orc_gguf_linear_candle(const void* x, int xdt, const uint8_t* blocks, int type,
+                                   int64_t M, int64_t K, int64_t N, float* y) {
+  int64_t bb = orc_gguf_block_bytes(type);
+  if (bb < 0 || K % QK) return -1;
+  int64_t nb = K / QK;
+  uint8_t* xq = (uint8_t*)malloc((size_t)(M * nb * 34));
+  float* xrow = (float*)malloc(sizeof(float) * (size_t)(M * K));
+  for (int64_t i = 0; i < M * K; ++i) xrow[i] = load_act(x, xdt, i);
+  for (int64_t m = 0; m < M; ++m)
+    for (int64_t b = 0; b < nb; ++b) q8_0_block(xrow + m * K + b * QK, xq + (m * nb + b) * 34);
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      float sumf = 0.0f;
+      for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* wb = blocks + (n * nb + b) * bb;
+        const uint8_t* xb = xq + (m * nb + b) * 34;
+        int sumi = 0;
+        for (int j = 0; j < QK; ++j) sumi += block_q(wb, type, j) * (int)(int8_t)xb[2 + j];
+        sumf += (float)sumi * block_d(wb) * block_d(xb);
+      }
+      y[m * N + n] = sumf;
+    }
+  }
+  free(xrow);
+  free(xq);
+  return 0;
+}
+
+/* Activation Q8_0 quantisation exposed on its own (the GPU kernels quantise
+ * activations the same way before the integer block dots). */
+ORC_API int orc_q8_0_quantize_rows(const void* x, int xdt, int64_t M, int64_t K,
+                                   int8_t* qs, uint16_t* d) {
+  if (K % QK) return -1;
+  int64_t nb = K / QK;
+  float buf[QK];
+  uint8_t blk[34];
+  for (int64_t m = 0; m < M; ++m)
+    for (int64_t b = 0; b < nb; ++b) {
+      for (int j = 0; j < QK; ++j) buf[j] = load_act(x, xdt, m * K + b * QK + j);
+      q8_0_block(buf, blk);
+      d[m * nb + b] = (uint16_t)(blk[0] | (blk[1] << 8));
+      memcpy(qs + m * K + b * QK, blk + 2, QK);
+    }
+  return 0;
+}

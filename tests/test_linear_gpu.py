@@ -1,0 +1,181 @@
+"""GPU parity of the quantised linears against the CPU oracle, through the C ABI.
+
+Bars (from the north star): dequantised weights and quantised bytes
+bit-exact; linear outputs within max relative error 1e-2 (max |y - y_ref| /
+max |y_ref|) with f32 accumulation.  The W8A16 kernels compute the same f32
+sums as the reference kernel (worker_w8a16.rs:158-181) in another order, and
+are checked far tighter (rel 2e-3, i.e. f16 output rounding); the GGUF
+integer path reproduces candle's Q8_0-activation arithmetic and is checked
+against the candle-style oracle at 1e-4 and against the exact product at 1e-2.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "gguf_q4_0_q8_0.npz")
+
+
+def rel_err(y, ref):
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(np.asarray(y, np.float64) - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def D():
+    import dial_cuda
+    return dial_cuda
+
+
+@pytest.fixture(scope="module")
+def torch(cuda):
+    import torch as _t
+    return _t
+
+
+def _to_dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+# ---------------------------------------------------------------- W8A16
+@pytest.mark.parametrize("N,K", [(37, 64), (300, 4096), (1024, 12288)])
+@pytest.mark.parametrize("wdt", ["f32", "f16"])
+def test_w8a16_quantize_bit_exact(D, torch, N, K, wdt):
+    rng = np.random.default_rng(N * 7 + K)
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    w[0, :] = 0.0  # all-zero row -> scale 1
+    if wdt == "f16":
+        w = w.astype(np.float16)
+    q_ref, s32_ref, s16_ref = O.w8a16_quantize(w)
+    lin = D.W8A16Linear.from_linear("t", _to_dev(torch, w))
+    assert np.array_equal(lin.qweight.cpu().numpy(), q_ref)
+    assert np.array_equal(lin.scales.cpu().numpy().view(np.uint32), s32_ref.view(np.uint32))
+    lin16 = D.W8A16Linear.from_linear("t", _to_dev(torch, w), scale_dtype=torch.float16)
+    assert np.array_equal(lin16.qweight.cpu().numpy(), q_ref)
+    assert np.array_equal(lin16.scales.cpu().numpy().view(np.uint16), s16_ref.view(np.uint16))
+    deq = lin.dequantize().cpu().numpy()
+    assert np.array_equal(deq.view(np.uint32), O.w8a16_dequantize(q_ref, s32_ref).view(np.uint32))
+
+
+def test_w8a16_reference_kat(D, torch):
+    """worker_w8a16.rs:483-516 on the GPU path: max_abs < 0.04 vs dense f16."""
+    idx = np.arange(37 * 64, dtype=np.float32)
+    w = (np.sin(idx * np.float32(0.037)) * np.float32(0.25)
+         + ((np.arange(37 * 64) % 11).astype(np.float32) - np.float32(5.0)) * np.float32(0.002))
+    w16 = w.reshape(37, 64).astype(np.float16)
+    lin = D.W8A16Linear.from_linear("test.linear", _to_dev(torch, w16))
+    for rows in (1, 9):
+        x = (np.cos(np.arange(rows * 64, dtype=np.float32) * np.float32(0.071)) * np.float32(0.5))
+        x = x.astype(np.float16).reshape(1, rows, 64)
+        dense = (x.astype(np.float32) @ w16.astype(np.float32).T).astype(np.float16)
+        y = lin.forward(_to_dev(torch, x)).cpu().numpy()
+        assert y.shape == (1, rows, 37)
+        assert np.abs(dense.astype(np.float32) - y.astype(np.float32)).max() < 0.04
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 9, 16, 17, 32, 33, 64, 130])
+@pytest.mark.parametrize("xdt", ["f16", "bf16"])
+@pytest.mark.parametrize("sdt", ["f32", "f16"])
+def test_w8a16_linear_parity(D, torch, M, xdt, sdt):
+    N, K = 1000, 2048 + 16  # odd N tail; K tail past the last 128-wide group
+    rng = np.random.default_rng(M * 131 + N)
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    x = rng.normal(0, 1, (M, K)).astype(np.float32)
+    lin = D.W8A16Linear.from_linear("t", _to_dev(torch, w),
+                                    scale_dtype=torch.float32 if sdt == "f32" else torch.float16)
+    scale_np = lin.scales.cpu().numpy()
+    if xdt == "f16":
+        xh = x.astype(np.float16)
+        y_ref, _ = O.w8a16_linear(xh, lin.qweight.cpu().numpy(), scale_np)
+        xt = _to_dev(torch, xh)
+    else:
+        xb = O.f32_to_bf16(x)
+        y_ref, _ = O.w8a16_linear(xb, lin.qweight.cpu().numpy(), scale_np, x_is_bf16=True)
+        xt = _to_dev(torch, xb.view(np.int16)).view(torch.bfloat16)
+    y = lin.forward(xt).float().cpu().numpy()
+    tol = 2e-3 if xdt == "f16" else 8e-3  # output rounding of f16 / bf16
+    assert rel_err(y, y_ref) <= tol
+
+
+def test_w8a16_decode_config1_shape(D, torch):
+    """BASELINE config 1 shape: x f16 [1,4096] ~N(0,1), W [12288,4096] ~N(0,0.02), f16 scale."""
+    rng = np.random.default_rng(299792458)
+    w = rng.normal(0, 0.02, (12288, 4096)).astype(np.float32)
+    x = rng.normal(0, 1, (1, 4096)).astype(np.float16)
+    lin = D.W8A16Linear.from_linear("up", _to_dev(torch, w), scale_dtype=torch.float16)
+    y = lin.forward(_to_dev(torch, x)).float().cpu().numpy()
+    y_ref, _ = O.w8a16_linear(x, lin.qweight.cpu().numpy(), lin.scales.cpu().numpy())
+    assert rel_err(y, y_ref) <= 2e-3
+
+
+# ---------------------------------------------------------------- GGUF
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN)
+
+
+@pytest.mark.parametrize("name,qt", [("q4_0", O.Q4_0), ("q8_0", O.Q8_0)])
+def test_gguf_golden_roundtrip_and_dequant(D, torch, golden, name, qt):
+    w = golden["w"]
+    N, K = w.shape
+    blocks = golden[f"{name}_blocks"]
+    lin = D.GgufLinear.from_blocks(_to_dev(torch, blocks), qt, K, N)
+    assert np.array_equal(lin.to_blocks().cpu().numpy(), blocks.reshape(-1))
+    deq = lin.dequantize().cpu().numpy()
+    assert np.array_equal(deq.view(np.uint32), golden[f"{name}_dequant"].view(np.uint32))
+    # GPU quantiser from the f32 weights gives the gguf package's bytes
+    lq = D.GgufLinear.quantize(_to_dev(torch, w), qt)
+    assert np.array_equal(lq.to_blocks().cpu().numpy(), blocks.reshape(-1))
+
+
+@pytest.mark.parametrize("qt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("K", [96, 4096, 12288])
+def test_gguf_quantize_dequant_random(D, torch, qt, K):
+    rng = np.random.default_rng(K + qt)
+    w = rng.normal(0, 0.02, (70, K)).astype(np.float32)
+    blocks = O.gguf_quantize(w, qt)
+    lq = D.GgufLinear.quantize(_to_dev(torch, w), qt)
+    assert np.array_equal(lq.to_blocks().cpu().numpy(), blocks.reshape(-1))
+    deq = lq.dequantize().cpu().numpy()
+    assert np.array_equal(deq.view(np.uint32), O.gguf_dequantize(blocks, qt, 70, K).view(np.uint32))
+
+
+@pytest.mark.parametrize("qt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 32, 33, 512])
+@pytest.mark.parametrize("xdt", ["f32", "f16", "bf16"])
+def test_gguf_linear_parity(D, torch, qt, M, xdt):
+    N, K = 1030, 4096 + 96  # row tail, and a K that ends in a partial group
+    rng = np.random.default_rng(M * 17 + qt)
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    x = rng.normal(0, 1, (M, K)).astype(np.float32)
+    blocks = O.gguf_quantize(w, qt)
+    lin = D.GgufLinear.from_blocks(_to_dev(torch, blocks), qt, K, N)
+    if xdt == "f32":
+        xin, xt, bf = x, _to_dev(torch, x), False
+    elif xdt == "f16":
+        xin = x.astype(np.float16)
+        xt, bf = _to_dev(torch, xin), False
+    else:
+        xin = O.f32_to_bf16(x)
+        xt, bf = _to_dev(torch, xin.view(np.int16)).view(torch.bfloat16), True
+    y = lin.forward(xt).float().cpu().numpy()
+    exact = O.gguf_linear_exact(xin, blocks, qt, N, x_is_bf16=bf)
+    out_tol = {"f32": 0.0, "f16": 1e-3, "bf16": 8e-3}[xdt]
+    assert rel_err(y, exact) <= 1e-2 + out_tol
+    if M <= 32:  # the integer (candle-arithmetic) path
+        cand = O.gguf_linear_candle(xin, blocks, qt, N, x_is_bf16=bf)
+        assert rel_err(y, cand) <= 1e-4 + out_tol
+
+
+def test_gguf_rejects_missing_workspace(D, torch):
+    w = torch.zeros((64, 64), dtype=torch.float32, device="cuda")
+    lin = D.GgufLinear.quantize(w, O.Q4_0)
+    x = torch.zeros((1, 64), dtype=torch.float32, device="cuda")
+    y = torch.empty((1, 64), dtype=torch.float32, device="cuda")
+    st = D.lib().dial_gguf_linear(x.data_ptr(), D.F32, lin.qs.data_ptr(), lin.d.data_ptr(), D.Q4_0,
+                                  y.data_ptr(), 1, 64, 64, None, 0, D.stream_ptr())
+    assert st == 1

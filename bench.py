@@ -2,24 +2,27 @@
 """Benchmark of the DIAL quantized-linear hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload w8a16_gemv|gguf_sweep]
+                    [--workload NAME]
 
 Prints ONE JSON line on rank 0.
 
 Workloads (seeded synthetic inputs with the shapes and distributions of the
 benchmark configurations; no dataset is involved):
-  w8a16_gemv  W8A16 decode linear: x f16 [1,4096] ~N(0,1), W [12288,4096]
-              ~N(0,0.02) quantised per row to int8 with an f16 scale (Qwen3-8B
-              MLP up-proj).  Metric: dequant-GEMV HBM GB/s.
-  gguf_sweep  GGUF QMatMul over the 7 linears of an 8B decoder layer (q, k, v,
-              o, gate, up, down) for Q4_0 and Q8_0 at M in {1, 8}, f32
-              activations.  Metric: dequant-GEMV HBM GB/s over the sweep.
-A step is one pass of the workload.  Inputs: rotating copies of the weights
-whose total exceeds the 126 MB L2, so every step reads its weights from HBM.
+  w8a16_gemv    W8A16 decode linear: x f16 [1,4096] ~N(0,1), W [12288,4096]
+                ~N(0,0.02) quantised per row to int8 with an f16 scale
+                (Qwen3-8B MLP up-proj).  Metric: dequant-GEMV HBM GB/s.
+  gguf_sweep    GGUF QMatMul over the 7 linears of an 8B decoder layer (q, k,
+                v, o, gate, up, down) for Q4_0 and Q8_0 at M in {1, 8}, f32
+                activations.  Metric: dequant-GEMV HBM GB/s over the sweep.
+  gguf_prefill  The same sweep at M = 512 (the prefill point of the GGUF
+                sweep).  Metric: dequant-GEMM TFLOP/s (tensor roofline).
+A step is one pass of the workload.  Multi-linear steps are captured once in
+a CUDA graph and replayed.  Inputs: rotating copies of the weights whose total
+exceeds the 126 MB L2, so every step reads its weights from HBM.
 
 Multi-GPU: a single linear does not shard (replicas only): under torchrun
 every rank runs the same workload on its own GPU, the timed region is the max
-over ranks, and `value` is the sum of all ranks' bytes over that time.
+over ranks, and `value` is the sum of all ranks' work over that time.
 
 --impl reference times the CPU restatement of the reference's path (the C
 oracle, OpenMP over all host threads) on the same workload and prints the
@@ -31,98 +34,105 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "dial-8b-orin_b200")
-for p in (ROOT, PKG):
-    if p not in sys.path:
-        sys.path.insert(0, p)
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
 
 SEED = 299792458
 L2_BYTES = 126 * 2**20
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
-FALLBACK_HBM_GBS = 6650.0
-FALLBACK_BF16_TFLOPS = 1590.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 LAYER_SHAPES = [  # (name, out N, in K) of one 8B decoder layer (Qwen3-8B / config 2)
     ("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
     ("gate", 12288, 4096), ("up", 12288, 4096), ("down", 4096, 12288),
 ]
+GGUF_BLOCK_BYTES = {"Q4_0": 18, "Q8_0": 34}
 
 
 def peaks():
     try:
         with open(PEAKS_PATH) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), float(p.get("bf16_tflops", FALLBACK_BF16_TFLOPS)), "measured"
+        return {k: float(p[k]) for k in FALLBACK}, "measured"
     except Exception:
-        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+        return dict(FALLBACK), "fallback"
 
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and throttle reasons, sampled with NVML every ~2 ms in a thread."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
+    def __init__(self, torch, device_index: int):
+        self.samples = []
+        self.stop = threading.Event()
+        self.handle = None
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            props = torch.cuda.get_device_properties(device_index)
+            bus = getattr(props, "pci_bus_id", None)
+            if bus is not None:
+                dom = getattr(props, "pci_domain_id", 0)
+                dev = getattr(props, "pci_device_id", 0)
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dev:02x}.0")
+            else:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.handle = None
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((time.perf_counter(), mhz, rs))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._t = threading.Thread(target=self._read, daemon=True)
-            self._t.start()
-        except Exception:
-            self.proc = None
+        if self.handle is not None:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop.set()
+        if self.handle is not None:
+            self.thread.join(timeout=2)
 
-    def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+    def summary(self, t0=None, t1=None):
+        sel = [s for s in self.samples if t0 is None or (t0 <= s[0] <= t1)]
+        window = "timed region"
+        if not sel:
+            sel, window = self.samples, "warm-up + timed region"
+        if not sel:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        reasons = set()
+        for _, _, rs in sel:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[1] for s in sel), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sel), "window": window}
 
 
 # ------------------------------------------------------------------ distributed
-def dist_setup(n_gpus: int):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -153,14 +163,16 @@ def max_over_ranks(v: float, world: int) -> float:
     return float(t.item())
 
 
-# ------------------------------------------------------------------ workloads
+# ------------------------------------------------------------------ workloads (GPU)
 class W8A16Gemv:
-    name = "w8a16_gemv"
-    desc = "W8A16 decode GEMV x f16 [1,4096] . W int8 [12288,4096]^T (f16 row scale)"
+    """one W8A16 decode linear per step."""
+    metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "int8 x f16"
+    kernel = "w8a16_skinny_kernel<NT=1>"
+    M, N, K = 1, 12288, 4096
+    graph = False
 
     def __init__(self, torch, D):
-        self.torch, self.D = torch, D
-        self.M, self.N, self.K = 1, 12288, 4096
+        self.torch = torch
         g = torch.Generator(device="cuda").manual_seed(SEED)
         per = self.N * self.K + 2 * self.N
         self.copies = max(2, -(-3 * L2_BYTES // per))  # rotate past the L2
@@ -169,20 +181,21 @@ class W8A16Gemv:
             w = torch.randn((self.N, self.K), generator=g, device="cuda", dtype=torch.float32) * 0.02
             self.lins.append(D.W8A16Linear.from_linear("up", w, scale_dtype=torch.float16))
             del w
-        self.x = (torch.randn((self.M, self.K), generator=g, device="cuda")).half()
+        self.x = torch.randn((self.M, self.K), generator=g, device="cuda").half()
         self.y = torch.empty((self.M, self.N), dtype=torch.float16, device="cuda")
         self.i = 0
-        self.bytes_per_step = self.N * self.K + 2 * self.N + 2 * self.M * self.K + 2 * self.M * self.N
-        self.flops_per_step = 2 * self.M * self.N * self.K
-        self.kernel_bytes = self.bytes_per_step  # one launch per step
-        self.launches_per_step = 1
-        self.h_x = torch.empty_like(self.x, device="cpu").pin_memory()
-        self.h_x.copy_(self.x.cpu())
-        self.h_y = torch.empty_like(self.y, device="cpu").pin_memory()
-        self.config = {"workload": self.name, "M": 1, "N": self.N, "K": self.K,
+        self.work_per_step = self.bytes()  # GB/s metric: bytes
+        self.kernel_work = self.work_per_step
+        self.h_x = self.x.cpu().pin_memory()
+        self.h_y = torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
+        self.config = {"workload": "w8a16_gemv", "M": 1, "N": self.N, "K": self.K,
                        "weight": "int8 per-row, f16 scale", "activation": "f16",
                        "l2": f"{self.copies} rotating weight copies "
                              f"({self.copies * per / 1e6:.0f} MB > 126 MB L2)"}
+
+    @classmethod
+    def bytes(cls):
+        return cls.N * cls.K + 2 * cls.N + 2 * cls.M * cls.K + 2 * cls.M * cls.N
 
     def step(self):
         lin = self.lins[self.i % self.copies]
@@ -190,31 +203,24 @@ class W8A16Gemv:
         lin.forward(self.x, out=self.y)
 
     def step_e2e(self):
+        """Through the public API with host buffers: H2D x, linear, D2H y."""
         self.x.copy_(self.h_x, non_blocking=True)
         self.step()
         self.h_y.copy_(self.y, non_blocking=True)
         return self.h_x.numel() * 2, self.h_y.numel() * 2
 
-    # CPU baseline: the oracle on the same shape
-    def cpu_setup(self, np, O):
-        rng = np.random.default_rng(SEED)
-        w = rng.normal(0, 0.02, (self.N, self.K)).astype(np.float32)
-        self.c_q, self.c_s32, _ = O.w8a16_quantize(w)
-        self.c_x = rng.normal(0, 1, (1, self.K)).astype(np.float16)
-
-    def cpu_step(self, O):
-        O.w8a16_linear_f32(self.c_x, self.c_q, self.c_s32)
-
 
 class GgufSweep:
-    name = "gguf_sweep"
-    desc = "GGUF QMatMul over the 7 linears of an 8B layer, Q4_0 and Q8_0, M in {1, 8}, f32 x"
+    """BASELINE config 2 (decode points): 7 shapes x {Q4_0, Q8_0} x M in {1, 8}."""
+    metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "q4_0/q8_0 x f32"
+    kernel = "gguf_skinny_kernel + q8_0_act_quantize_kernel (whole sweep)"
+    ms = (1, 8)
+    graph = True
 
-    def __init__(self, torch, D, ms=(1, 8)):
-        self.torch, self.D, self.ms = torch, D, tuple(ms)
+    def __init__(self, torch, D):
+        self.torch, self.D = torch, D
         g = torch.Generator(device="cuda").manual_seed(SEED)
-        layer = []
-        per_layer = 0
+        layer, per_layer = [], 0
         for qt in (D.Q4_0, D.Q8_0):
             for name, N, K in LAYER_SHAPES:
                 w = torch.randn((N, K), generator=g, device="cuda", dtype=torch.float32) * 0.02
@@ -223,125 +229,163 @@ class GgufSweep:
                 layer.append(lin)
                 per_layer += lin.weight_bytes
         self.copies = max(2, -(-3 * L2_BYTES // per_layer))
-        self.layers = [layer]
-        for _ in range(self.copies - 1):
-            cp = []
-            for lin in layer:
-                cp.append(D.GgufLinear(lin.qs.clone(), lin.d.clone(), lin.qtype, lin.in_dim,
-                                       lin.out_dim, lin.name))
-            self.layers.append(cp)
-        maxk = max(k for _, _, k in LAYER_SHAPES)
-        maxn = max(n for _, n, _ in LAYER_SHAPES)
-        self.xs = {m: torch.randn((m, maxk), generator=g, device="cuda") for m in self.ms}
-        self.ys = {m: torch.empty((m, maxn), device="cuda") for m in self.ms}
+        self.layers = [layer] + [[D.GgufLinear(l.qs.clone(), l.d.clone(), l.qtype, l.in_dim,
+                                               l.out_dim, l.name) for l in layer]
+                                 for _ in range(self.copies - 1)]
+        self.calls = []
+        for li, lay in enumerate(self.layers):
+            for m in self.ms:
+                for lin in lay:
+                    x = torch.randn((m, lin.in_dim), generator=g, device="cuda")
+                    y = torch.empty((m, lin.out_dim), device="cuda")
+                    lin.workspace(m)
+                    self.calls.append((li, lin, x, y))
         self.i = 0
-        b = 0
-        for m in self.ms:
-            for lin in layer:
-                b += lin.weight_bytes + 4 * m * lin.in_dim + 4 * m * lin.out_dim
-        self.bytes_per_step = b
-        self.kernel_bytes = None
-        self.launches_per_step = 2 * len(layer) * len(self.ms)
-        self.flops_per_step = sum(2 * m * lin.in_dim * lin.out_dim for m in self.ms for lin in layer)
-        self.config = {"workload": self.name, "M": list(self.ms), "types": ["Q4_0", "Q8_0"],
+        self.work_per_step = self.bytes()
+        self.kernel_work = None
+        self.config = {"workload": "gguf_sweep", "M": list(self.ms), "types": ["Q4_0", "Q8_0"],
                        "shapes": [f"{n}:{k}->{N}" for n, N, k in LAYER_SHAPES], "activation": "f32",
                        "l2": f"{self.copies} rotating layer copies "
-                             f"({self.copies * per_layer / 1e6:.0f} MB > 126 MB L2)"}
+                             f"({self.copies * per_layer / 1e6:.0f} MB > 126 MB L2)",
+                       "launch": "CUDA graph per layer copy"}
+
+    @classmethod
+    def bytes(cls):
+        b = 0
+        for m in cls.ms:
+            for bb in GGUF_BLOCK_BYTES.values():
+                for _, N, K in LAYER_SHAPES:
+                    b += N * (K // 32) * bb + 4 * m * K + 4 * m * N
+        return b
+
+    def run_copy(self, li):
+        for lj, lin, x, y in self.calls:
+            if lj == li:
+                lin.forward(x, out=y)
+
+    def build_graphs(self):
+        torch = self.torch
+        self.graphs = []
+        for li in range(self.copies):
+            self.run_copy(li)  # warm (attributes, tensor-map entry point)
+        torch.cuda.synchronize()
+        for li in range(self.copies):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                self.run_copy(li)
+            self.graphs.append(gr)
+        torch.cuda.synchronize()
 
     def step(self):
-        layer = self.layers[self.i % self.copies]
+        self.graphs[self.i % self.copies].replay()
         self.i += 1
-        for m in self.ms:
-            for lin in layer:
-                x = self.xs[m][:, : lin.in_dim]
-                if not x.is_contiguous():
-                    x = x.contiguous()
-                lin.forward(x, out=self.ys[m][:, : lin.out_dim].contiguous())
 
-    def step_e2e(self):
-        raise NotImplementedError
 
-    def cpu_setup(self, np, O):
+class GgufPrefill(GgufSweep):
+    """BASELINE config 2 (prefill point): the same sweep at M = 512 (tensor-bound)."""
+    metric, unit, bound, dtype = "dequant-GEMM TFLOP/s", "TFLOP/s", "tensor", "q4_0/q8_0 x f32 -> f16 MMA"
+    kernel = "dequant_gemm_kernel (whole sweep)"
+    ms = (512,)
+
+    def __init__(self, torch, D):
+        super().__init__(torch, D)
+        self.work_per_step = self.flops()
+        self.config["workload"] = "gguf_prefill"
+        self.config["M"] = list(self.ms)
+
+    @classmethod
+    def flops(cls):
+        return sum(2 * m * N * K for m in cls.ms for _ in GGUF_BLOCK_BYTES for _, N, K in LAYER_SHAPES)
+
+
+WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep, "gguf_prefill": GgufPrefill}
+
+
+# ------------------------------------------------------------------ workloads (CPU oracle)
+class CpuWorkload:
+    """The same workload on the C oracle (the CPU restatement of the reference's path)."""
+
+    def __init__(self, name):
+        import numpy as np
+
+        import oracle as O
+        self.O, self.name = O, name
         rng = np.random.default_rng(SEED)
-        self.c = []
-        for qt in (O.Q4_0, O.Q8_0):
-            for _, N, K in LAYER_SHAPES:
-                w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
-                self.c.append((O.gguf_quantize(w, qt), qt, N, K))
-        self.c_x = {m: rng.normal(0, 1, (m, 12288)).astype(np.float32) for m in self.ms}
+        wl = WORKLOADS[name]
+        if name == "w8a16_gemv":
+            w = rng.normal(0, 0.02, (wl.N, wl.K)).astype(np.float32)
+            self.q, self.s32, _ = O.w8a16_quantize(w)
+            self.x = rng.normal(0, 1, (1, wl.K)).astype(np.float16)
+            self.work = wl.bytes()
+        else:
+            self.lins = []
+            for qt in (O.Q4_0, O.Q8_0):
+                for _, N, K in LAYER_SHAPES:
+                    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+                    self.lins.append((O.gguf_quantize(w, qt), qt, N, K))
+            self.xs = {m: rng.normal(0, 1, (m, 12288)).astype(np.float32) for m in wl.ms}
+            self.work = wl.flops() if name == "gguf_prefill" else wl.bytes()
+            self.ms = wl.ms
 
-    def cpu_step(self, O):
+    def step(self, frac=1.0):
+        """One pass (or, for the big prefill sweep, `frac` of it: a bounded sample)."""
+        O = self.O
+        if self.name == "w8a16_gemv":
+            O.w8a16_linear_f32(self.x, self.q, self.s32)
+            return 1.0
+        done = 0.0
         for m in self.ms:
-            for blocks, qt, N, K in self.c:
-                O.gguf_linear_candle(self.c_x[m][:, :K], blocks, qt, N)
+            mm = max(1, int(round(m * frac)))
+            for blocks, qt, N, K in self.lins:
+                O.gguf_linear_candle(self.xs[m][:mm, :K], blocks, qt, N)
+            done = mm / m
+        return done
 
 
-WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep}
-
-
-# ------------------------------------------------------------------ CPU legs
-def cpu_measure(wl_cls, budget_s: float):
-    import numpy as np
-
-    import oracle as O
-    wl = wl_cls.__new__(wl_cls)
-    wl_cls_init_cpu(wl)
-    wl.cpu_setup(np, O)
-    wl.cpu_step(O)  # warm-up
+def cpu_measure(name, budget_s):
+    cw = CpuWorkload(name)
+    frac = 1.0 if name != "gguf_prefill" else 16 / 512  # 16 of the 512 rows per sample
+    cw.step(frac)  # warm-up
     t0 = time.perf_counter()
-    n = 0
+    n, work = 0, 0.0
     while True:
-        wl.cpu_step(O)
+        work += cw.step(frac) * cw.work
         n += 1
         if time.perf_counter() - t0 >= budget_s:
             break
-    dt = (time.perf_counter() - t0) / n
-    return dt, n, O.num_threads()
+    dt = time.perf_counter() - t0
+    sample = (f"{n} passes of the C oracle in {dt:.1f}s" if frac == 1.0 else
+              f"{n} passes over 16 of the 512 rows ({frac:.3f} of a step) in {dt:.1f}s, scaled")
+    return work / dt, dt / n, cw.O.num_threads(), sample
 
 
-def wl_cls_init_cpu(wl):
-    if isinstance(wl, W8A16Gemv):
-        wl.M, wl.N, wl.K = 1, 12288, 4096
-        wl.bytes_per_step = wl.N * wl.K + 2 * wl.N + 2 * wl.M * wl.K + 2 * wl.M * wl.N
-    elif isinstance(wl, GgufSweep):
-        wl.ms = (1, 8)
-        b = 0
-        for m in wl.ms:
-            for qt_bytes in (18, 34):
-                for _, N, K in LAYER_SHAPES:
-                    b += N * K // 32 * qt_bytes + 4 * m * K + 4 * m * N
-        wl.bytes_per_step = b
+def unit_scale(unit):
+    return 1e9 if unit == "GB/s" else 1e12
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    wl_cls = WORKLOADS[args.workload]
-    dts = []
-    n_total = 0
+    wl = WORKLOADS[args.workload]
     for _ in range(args.warmup):
-        cpu_measure(wl_cls, 0.0)
-    per_step_budget = max(1.0, min(20.0, 60.0 / max(args.steps, 1)))
-    threads = 1
+        cpu_measure(args.workload, 0.0)
+    per_step = max(1.0, min(20.0, 60.0 / max(args.steps, 1)))
+    rates, threads, sample = [], 1, ""
     for _ in range(args.steps):
-        dt, n, threads = cpu_measure(wl_cls, per_step_budget)
-        dts.append(dt)
-        n_total += n
-    wl = wl_cls.__new__(wl_cls)
-    wl_cls_init_cpu(wl)
-    dt = statistics.median(dts)
-    value = wl.bytes_per_step / dt / 1e9
+        rate, _, threads, sample = cpu_measure(args.workload, per_step)
+        rates.append(rate)
+    value = statistics.median(rates) / unit_scale(wl.unit)
+    work = wl.bytes() if wl.unit == "GB/s" else wl.flops()
     line = {
-        "impl": "reference", "metric": "dequant-GEMV HBM GB/s", "value": round(value, 3),
-        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8xf16" if args.workload == "w8a16_gemv" else "q4_0/q8_0 x f32",
+        "impl": "reference", "metric": wl.metric, "value": round(value, 4), "unit": wl.unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(work / (value * unit_scale(wl.unit)) * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
         "config": {"workload": args.workload},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{n_total} calls of the oracle over {args.steps} steps of "
-                                   f"~{per_step_budget:.0f}s"},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+        "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads, "kind": "port",
+                         "sample": f"per step: {sample}"},
+        "e2e": {"value": round(value, 4), "unit": wl.unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -355,19 +399,29 @@ def run_ours(args, rank, local, world):
     torch.cuda.set_device(local)
     wl = WORKLOADS[args.workload](torch, D)
     stream = torch.cuda.current_stream()
+
+    # launches per step, counted on an eager pass
+    c0 = D.launch_count()
+    if wl.graph:
+        wl.run_copy(0)
+    else:
+        wl.step()
+    torch.cuda.synchronize()
+    launches_per_step = D.launch_count() - c0
+    if wl.graph:
+        wl.build_graphs()
     for _ in range(max(args.warmup, 3)):
         wl.step()
     torch.cuda.synchronize()
+    assert D.lib().dial_device_error(1) == 0
 
-    # ---- device-timed region: K steps, events around every step on the launching stream
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    t_begin = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    launches0 = D.launch_count()
-    with ClockSampler(local) as clocks:
+    t_begin, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch, local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
         t_begin.record(stream)
         for i in range(args.steps):
             starts[i].record(stream)
@@ -375,20 +429,19 @@ def run_ours(args, rank, local, world):
             ends[i].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize()
-    barrier(world)
-    launches = D.launch_count() - launches0
+        w1 = time.perf_counter()
+        barrier(world)
     total_ms = max_over_ranks(t_begin.elapsed_time(t_end), world)
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    assert D.lib().dial_device_error(1) == 0
 
-    # ---- end-to-end: host buffers, H2D + call + D2H inside the timed region
     e2e = None
-    if hasattr(wl, "h_x"):
+    if hasattr(wl, "step_e2e"):
         for _ in range(3):
             wl.step_e2e()
         torch.cuda.synchronize()
         barrier(world)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         h2d = d2h = 0
         for _ in range(args.steps):
@@ -396,35 +449,37 @@ def run_ours(args, rank, local, world):
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
-        e2e = {"value": round(wl.bytes_per_step * world * args.steps / (e2e_ms / 1e3) / 1e9, 3),
-               "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+        e2e = {"value": round(wl.work_per_step * world * args.steps / (e2e_ms / 1e3)
+                              / unit_scale(wl.unit), 3),
+               "unit": wl.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(e2e_ms / args.steps, 5)}
 
-    hbm_peak, tf_peak, peak_src = peaks()
-    value = wl.bytes_per_step * world * args.steps / (total_ms / 1e3) / 1e9
-    avg_step_ms = statistics.mean(step_ms)
-    kernel_bytes = wl.kernel_bytes if wl.kernel_bytes else wl.bytes_per_step / wl.launches_per_step
-    kernel_ms = avg_step_ms / (1 if wl.kernel_bytes else wl.launches_per_step)
-    achieved = kernel_bytes / (kernel_ms / 1e3) / 1e9
+    pk, peak_src = peaks()
+    value = wl.work_per_step * world * args.steps / (total_ms / 1e3) / unit_scale(wl.unit)
+    # roofline of the dominant kernel: algorithmic work per step / mean step time
+    achieved = wl.work_per_step / (statistics.mean(step_ms) / 1e3) / unit_scale(wl.unit)
+    if wl.bound == "hbm":
+        peak = pk["hbm_gbs"]
+    else:
+        peak = pk["bf16_tflops"]
     line = {
-        "metric": "dequant-GEMV HBM GB/s", "value": round(value, 3), "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8xf16" if args.workload == "w8a16_gemv" else "q4_0/q8_0 x f32",
+        "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
         "config": dict(wl.config, parallelism=f"replicas x{world}"),
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
-                     "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": None,
-                     "peak_source": peak_src, "kernel": "w8a16_skinny_kernel<1>"
-                     if args.workload == "w8a16_gemv" else "gguf_skinny_kernel (mean per linear)"},
-        "e2e": e2e, "gpu_launches": launches, "clocks": clocks.summary(),
+        "roofline": {"bound": wl.bound, "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "GB/s" if wl.bound == "hbm" else "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": f"{peak_src} ({'hbm_gbs' if wl.bound == 'hbm' else 'bf16_tflops'} burst)",
+                     "kernel": wl.kernel},
+        "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(w0, w1),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        dt, n, threads = cpu_measure(WORKLOADS[args.workload], args.cpu_budget)
-        line["cpu_baseline"] = {"value": round(wl.bytes_per_step / dt / 1e9, 3), "unit": "GB/s",
-                                "cores": threads, "kind": "port",
-                                "sample": f"{n} calls of the C oracle in ~{args.cpu_budget:.0f}s"}
+        rate, _, threads, sample = cpu_measure(args.workload, args.cpu_budget)
+        line["cpu_baseline"] = {"value": round(rate / unit_scale(wl.unit), 4), "unit": wl.unit,
+                                "cores": threads, "kind": "port", "sample": sample}
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -439,7 +494,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    rank, local, world = dist_setup(args.gpus)
+    rank, local, world = dist_setup()
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)

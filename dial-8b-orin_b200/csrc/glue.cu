@@ -1,0 +1,475 @@
+// Decoder glue around the quantised linears (f16/bf16 activations, f32 math).
+//
+// Reference semantics (lisa301/DIAL-8B-orin):
+//   RMSNorm       candle_nn::RmsNorm used at text.rs:1620-1626 (rms_1 / rms_2),
+//                 :1466-1467 (q_norm / k_norm), ln_f qwen3_vl.rs:2425-2429:
+//                 y = x * rsqrt(mean(x^2) + eps) * w, computed in f32.
+//   residual      text.rs:1650-1674: (attn + residual), (mlp + residual) in the
+//                 activation dtype -- fused here into the following RMSNorm.
+//   RoPE          text.rs:1143-1153 (candle rotary_emb::rope, non-interleaved
+//                 halves), tables llama3/cache.rs:24-64: inv_freq_i =
+//                 1/theta^(2i/D) in f32, angle = pos * inv_freq, cos/sin stored
+//                 in the activation dtype.
+//   KV append     llama3/cache.rs:149-217: preallocated [b, kv_h, max_seq, D]
+//                 storage, the new token written at its position.
+//   attention     text.rs:1258-1327: GQA, softmax(q.K^T / sqrt(D)) V, causal.
+//   SwiGLU        text.rs:816-820: silu(gate) * up over the halves of gate_up.
+//   argmax        qwen3_vl.rs:130-143 (greedy sampling on the device).
+#include <algorithm>
+#include <cfloat>
+
+#include "common.cuh"
+#include "glue.cuh"
+
+namespace dial {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld(const T* p, int64_t i) {
+  return Act<T>::to_f32(p[i]);
+}
+template <typename T>
+__device__ __forceinline__ T rnd(float v) {
+  return Act<T>::from_f32(v);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = threadIdx.x < THREADS / 32 ? red[threadIdx.x] : 0.f;
+  if (w == 0) v = warp_sum(v);
+  if (threadIdx.x == 0) red[0] = v;
+  __syncthreads();
+  return red[0];
+}
+
+// ------------------------------------------------------------------ RMSNorm (+ residual)
+// One CTA per row.  h = x (+ residual, rounded to T); y = h * rsqrt(mean(h^2)+eps) * w.
+template <typename T, int THREADS>
+__global__ void __launch_bounds__(THREADS) rmsnorm_kernel(const T* __restrict__ x,
+                                                          const T* __restrict__ res,
+                                                          T* __restrict__ h_out,
+                                                          const T* __restrict__ w,
+                                                          T* __restrict__ y, int dim, float eps) {
+  extern __shared__ float hbuf[];  // dim floats
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * dim;
+  const T* rr = res ? res + row * dim : nullptr;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += THREADS) {
+    float v = ld(xr, i);
+    if (rr) v = Act<T>::to_f32(rnd<T>(v + ld(rr, i)));  // residual add in the activation dtype
+    hbuf[i] = v;
+    ss += v * v;
+  }
+  ss = block_sum<THREADS>(ss, red);
+  const float inv = rsqrtf(ss / (float)dim + eps);
+  for (int i = threadIdx.x; i < dim; i += THREADS) {
+    const float v = hbuf[i];
+    if (h_out) h_out[row * dim + i] = rnd<T>(v);
+    y[row * dim + i] = rnd<T>(v * inv * ld(w, i));
+  }
+}
+
+// ------------------------------------------------------------------ QK-norm + RoPE + KV append
+// One warp per (token, head) over Hq + 2*Hkv heads; lane l owns elements
+// {l, l+32, l+64, l+96} of the 128-wide head, so both RoPE pairs (i, i+64)
+// stay in the lane.  head_dim is fixed to 128 (Qwen3-8B / Llama-3-8B).
+template <typename T>
+__global__ void qk_rope_kv_kernel(const T* __restrict__ qkv, const T* __restrict__ qn,
+                                  const T* __restrict__ kn, const T* __restrict__ cos_t,
+                                  const T* __restrict__ sin_t, const int32_t* __restrict__ pos,
+                                  const int32_t* __restrict__ slot, T* __restrict__ q_out,
+                                  T* __restrict__ kc, T* __restrict__ vc, int64_t tokens, int hq,
+                                  int hkv, int64_t max_seq, float eps, int qk_norm) {
+  constexpr int D = 128;
+  const int heads = hq + 2 * hkv;
+  const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= tokens * heads) return;
+  const int64_t t = gw / heads;
+  const int h = (int)(gw % heads);
+  const T* src = qkv + t * (int64_t)heads * D + (int64_t)h * D;
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = ld(src, lane + 32 * i);
+  const int p = pos[t];
+  const int64_t s = slot[t];
+  if (h >= hq + hkv) {  // value head: straight into the cache
+    T* dst = vc + ((s * hkv + (h - hq - hkv)) * max_seq + p) * D;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = rnd<T>(v[i]);
+    return;
+  }
+  const bool is_q = h < hq;
+  if (qk_norm) {
+    const T* nw = is_q ? qn : kn;
+    const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+    const float inv = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      v[i] = Act<T>::to_f32(rnd<T>(v[i] * inv * ld(nw, lane + 32 * i)));  // normed tensor in T
+  }
+  // rotate_half: out[i] = x[i] c_i - x[i+64] s_i ; out[i+64] = x[i+64] c_i + x[i] s_i
+  const T* cr = cos_t + (int64_t)p * (D / 2);
+  const T* sr = sin_t + (int64_t)p * (D / 2);
+  float o[4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int e = lane + 32 * i;  // 0..63
+    const float c = ld(cr, e), sn = ld(sr, e);
+    o[i] = v[i] * c - v[i + 2] * sn;
+    o[i + 2] = v[i + 2] * c + v[i] * sn;
+  }
+  T* dst = is_q ? q_out + (t * hq + h) * D : kc + ((s * hkv + (h - hq)) * max_seq + p) * D;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = rnd<T>(o[i]);
+}
+
+// ------------------------------------------------------------------ attention
+// Query token t attends cache rows 0..pos[t] of slot[t] (decode: one token per
+// sequence; prefill: a run of tokens of one sequence, causal through pos).
+// CTA = (token, kv head, key chunk); the n_rep query heads of the group share
+// every K/V row read.  f32 scores / softmax / accumulation.
+constexpr int kAttnThreads = 128;
+constexpr int kAttnChunk = 512;
+constexpr int kMaxRep = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(kAttnThreads)
+    attention_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
+                     const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
+                     T* __restrict__ out, float* __restrict__ part, int hq, int hkv,
+                     int64_t max_seq, int nchunks, float scale) {
+  constexpr int D = 128;
+  __shared__ float qs[kMaxRep][D];
+  __shared__ float sc[kMaxRep][kAttnChunk];
+  __shared__ float red[32];
+  const int64_t t = blockIdx.x;
+  const int g = blockIdx.y;
+  const int chunk = blockIdx.z;
+  const int rep = hq / hkv;
+  const int len = pos[t] + 1;
+  const int k0 = chunk * kAttnChunk;
+  if (k0 >= len) {  // empty chunk: mark so the combine step skips it
+    if (nchunks > 1 && threadIdx.x < rep) {
+      float* pp = part + ((t * hq + g * rep + threadIdx.x) * nchunks + chunk) * (D + 2);
+      pp[0] = -FLT_MAX;
+      pp[1] = 0.f;
+    }
+    return;
+  }
+  const int k1 = min(len, k0 + kAttnChunk);
+  const int64_t s = slot[t];
+  for (int i = threadIdx.x; i < rep * D; i += kAttnThreads)
+    qs[i / D][i % D] = ld(q, (t * hq + g * rep) * D + i) * scale;
+  __syncthreads();
+  const T* kbase = kc + (s * hkv + g) * max_seq * D;
+  const T* vbase = vc + (s * hkv + g) * max_seq * D;
+  // scores: one key row per thread and pass
+  for (int j = k0 + threadIdx.x; j < k1; j += kAttnThreads) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kbase + (int64_t)j * D);
+    float acc[kMaxRep];
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) acc[r] = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < D / 8; ++c) {
+      const uint4 u = __ldg(kr + c);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float kv = Act<T>::to_f32(e[i]);
+#pragma unroll
+        for (int r = 0; r < kMaxRep; ++r)
+          if (r < rep) acc[r] = fmaf(qs[r][c * 8 + i], kv, acc[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r)
+      if (r < rep) sc[r][j - k0] = acc[r];
+  }
+  __syncthreads();
+  // per-head max and exp-sum over the chunk
+  float mx[kMaxRep], sm[kMaxRep];
+  for (int r = 0; r < rep; ++r) {
+    float m = -FLT_MAX;
+    for (int j = threadIdx.x; j < k1 - k0; j += kAttnThreads) m = fmaxf(m, sc[r][j]);
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float sum = 0.f;
+    for (int j = threadIdx.x; j < k1 - k0; j += kAttnThreads) {
+      const float e = __expf(sc[r][j] - m);
+      sc[r][j] = e;
+      sum += e;
+    }
+    sum = block_sum<kAttnThreads>(sum, red);
+    mx[r] = m;
+    sm[r] = sum;
+  }
+  __syncthreads();
+  // output: thread d accumulates sum_j p[r][j] * V[j][d]
+  const int d = threadIdx.x;  // kAttnThreads == D
+  float o[kMaxRep];
+#pragma unroll
+  for (int r = 0; r < kMaxRep; ++r) o[r] = 0.f;
+  for (int j = k0; j < k1; ++j) {
+    const float vv = ld(vbase, (int64_t)j * D + d);
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r)
+      if (r < rep) o[r] = fmaf(sc[r][j - k0], vv, o[r]);
+  }
+  for (int r = 0; r < rep; ++r) {
+    const int64_t head = t * hq + g * rep + r;
+    if (nchunks == 1) {
+      out[head * D + d] = rnd<T>(o[r] / sm[r]);
+    } else {
+      float* pp = part + (head * nchunks + chunk) * (D + 2);
+      if (d == 0) {
+        pp[0] = mx[r];
+        pp[1] = sm[r];
+      }
+      pp[2 + d] = o[r];
+    }
+  }
+}
+
+template <typename T>
+__global__ void attention_combine_kernel(const float* __restrict__ part, T* __restrict__ out,
+                                         int nchunks) {
+  constexpr int D = 128;
+  const int64_t head = blockIdx.x;
+  const int d = threadIdx.x;
+  const float* pp = part + head * nchunks * (D + 2);
+  float m = -FLT_MAX;
+  for (int c = 0; c < nchunks; ++c) m = fmaxf(m, pp[c * (D + 2)]);
+  float sum = 0.f, acc = 0.f;
+  for (int c = 0; c < nchunks; ++c) {
+    const float cm = pp[c * (D + 2)];
+    if (cm == -FLT_MAX) continue;
+    const float f = __expf(cm - m);
+    sum += pp[c * (D + 2) + 1] * f;
+    acc += pp[c * (D + 2) + 2 + d] * f;
+  }
+  out[head * D + d] = rnd<T>(acc / sum);
+}
+
+// ------------------------------------------------------------------ SwiGLU
+// out[t, i] = round(round(silu(g)) * u), g = gate_up[t, i], u = gate_up[t, I + i]
+template <typename T>
+__global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t tokens,
+                              int64_t inter) {
+  const int64_t n = tokens * inter;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / inter, c = i % inter;
+    const float g = ld(gu, t * 2 * inter + c);
+    const float u = ld(gu, t * 2 * inter + inter + c);
+    const float s = Act<T>::to_f32(rnd<T>(g / (1.0f + expf(-g))));
+    out[i] = rnd<T>(s * u);
+  }
+}
+
+// ------------------------------------------------------------------ embedding / argmax
+template <typename T>
+__global__ void embedding_kernel(const T* __restrict__ table, const int32_t* __restrict__ ids,
+                                 T* __restrict__ out, int64_t tokens, int64_t vocab, int64_t dim,
+                                 int* __restrict__ err) {
+  const int64_t t = blockIdx.x;
+  const int32_t id = ids[t];
+  const bool ok = id >= 0 && id < vocab;
+  if (!ok && threadIdx.x == 0) atomicCAS(err, 0, (int)DIAL_ERR_INVALID_ARG);
+  for (int64_t i = threadIdx.x; i < dim; i += blockDim.x)
+    out[t * dim + i] = ok ? table[(int64_t)id * dim + i] : rnd<T>(0.f);
+}
+
+// First index of the maximum (NaN never wins), one CTA per row.
+template <typename T>
+__global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x,
+                                                      int32_t* __restrict__ out, int64_t n) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * n;
+  float best = -FLT_MAX;
+  int64_t bidx = n;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = ld(xr, i);
+    if (v > best) { best = v; bidx = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+    if (ov > best || (ov == best && oi < bidx)) { best = ov; bidx = oi; }
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) { bv[w] = best; bi[w] = (int)bidx; }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    best = threadIdx.x < nw ? bv[threadIdx.x] : -FLT_MAX;
+    bidx = threadIdx.x < nw ? bi[threadIdx.x] : n;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+      if (ov > best || (ov == best && oi < bidx)) { best = ov; bidx = oi; }
+    }
+    if (threadIdx.x == 0) out[row] = (int32_t)(bidx < n ? bidx : 0);
+  }
+}
+
+// cos/sin tables: angle = pos * (1 / theta^(i/ (D/2) ... )) computed in f32 as
+// llama3/cache.rs:31-50 (inv_freq from powf in f32, the product in f32).
+template <typename T>
+__global__ void rope_table_kernel(T* __restrict__ cos_t, T* __restrict__ sin_t, int64_t max_pos,
+                                  int half, float theta) {
+  const int64_t n = max_pos * half;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = i / half;
+    const int j = (int)(i % half);
+    const float inv = 1.0f / powf(theta, (float)(2 * j) / (float)(2 * half));
+    const float a = (float)p * inv;
+    cos_t[i] = rnd<T>(cosf(a));
+    sin_t[i] = rnd<T>(sinf(a));
+  }
+}
+
+unsigned grid_cap(int64_t work, int threads, int per_sm = 16) {
+  int64_t b = (work + threads - 1) / threads;
+  const int64_t cap = (int64_t)sm_count() * per_sm;
+  return (unsigned)std::max<int64_t>(1, std::min(b, cap));
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ launchers
+#define DISPATCH_T(dt, ...)                          \
+  do {                                               \
+    if ((dt) == DIAL_F16) {                          \
+      using T = __half;                              \
+      __VA_ARGS__;                                   \
+    } else if ((dt) == DIAL_BF16) {                  \
+      using T = __nv_bfloat16;                       \
+      __VA_ARGS__;                                   \
+    } else {                                         \
+      using T = float;                               \
+      __VA_ARGS__;                                   \
+    }                                                \
+  } while (0)
+
+dial_status launch_rmsnorm(const void* x, const void* res, void* h_out, const void* w, void* y,
+                           dial_dtype dt, int64_t rows, int64_t dim, float eps, cudaStream_t st) {
+  const size_t smem = (size_t)dim * sizeof(float);
+  if (smem > 96 * 1024) return fail(DIAL_ERR_SHAPE, "rmsnorm dim too large (%lld)", (long long)dim);
+  DISPATCH_T(dt, {
+    auto k = rmsnorm_kernel<T, 512>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<(unsigned)rows, 512, smem, st>>>(static_cast<const T*>(x), static_cast<const T*>(res),
+                                         static_cast<T*>(h_out), static_cast<const T*>(w),
+                                         static_cast<T*>(y), (int)dim, eps);
+  });
+  return check_launch("rmsnorm_kernel");
+}
+
+dial_status launch_qk_rope_kv(const void* qkv, const void* qn, const void* kn, const void* cos_t,
+                              const void* sin_t, const int32_t* pos, const int32_t* slot,
+                              void* q_out, void* kc, void* vc, dial_dtype dt, int64_t tokens,
+                              int hq, int hkv, int64_t max_seq, float eps, int qk_norm,
+                              cudaStream_t st) {
+  const int64_t warps = tokens * (hq + 2 * hkv);
+  const unsigned grid = (unsigned)((warps * 32 + 255) / 256);
+  DISPATCH_T(dt, {
+    qk_rope_kv_kernel<T><<<grid, 256, 0, st>>>(
+        static_cast<const T*>(qkv), static_cast<const T*>(qn), static_cast<const T*>(kn),
+        static_cast<const T*>(cos_t), static_cast<const T*>(sin_t), pos, slot,
+        static_cast<T*>(q_out), static_cast<T*>(kc), static_cast<T*>(vc), tokens, hq, hkv,
+        max_seq, eps, qk_norm);
+  });
+  return check_launch("qk_rope_kv_kernel");
+}
+
+size_t attention_workspace_bytes(int64_t tokens, int hq, int64_t max_len) {
+  const int64_t nch = (max_len + kAttnChunk - 1) / kAttnChunk;
+  return nch > 1 ? (size_t)(tokens * hq * nch * (128 + 2)) * sizeof(float) : 0;
+}
+
+dial_status launch_attention(const void* q, const void* kc, const void* vc, const int32_t* pos,
+                             const int32_t* slot, void* out, void* ws, dial_dtype dt,
+                             int64_t tokens, int hq, int hkv, int64_t max_seq, int64_t max_len,
+                             cudaStream_t st) {
+  const int nch = (int)((max_len + kAttnChunk - 1) / kAttnChunk);
+  const float scale = 1.0f / sqrtf(128.0f);
+  dim3 grid((unsigned)tokens, (unsigned)hkv, (unsigned)nch);
+  DISPATCH_T(dt, {
+    attention_kernel<T><<<grid, kAttnThreads, 0, st>>>(
+        static_cast<const T*>(q), static_cast<const T*>(kc), static_cast<const T*>(vc), pos, slot,
+        static_cast<T*>(out), static_cast<float*>(ws), hq, hkv, max_seq, nch, scale);
+  });
+  dial_status s = check_launch("attention_kernel");
+  if (s != DIAL_OK || nch == 1) return s;
+  DISPATCH_T(dt, {
+    attention_combine_kernel<T><<<(unsigned)(tokens * hq), 128, 0, st>>>(
+        static_cast<const float*>(ws), static_cast<T*>(out), nch);
+  });
+  return check_launch("attention_combine_kernel");
+}
+
+dial_status launch_swiglu(const void* gu, void* out, dial_dtype dt, int64_t tokens, int64_t inter,
+                          cudaStream_t st) {
+  DISPATCH_T(dt, {
+    swiglu_kernel<T><<<grid_cap(tokens * inter, 256), 256, 0, st>>>(
+        static_cast<const T*>(gu), static_cast<T*>(out), tokens, inter);
+  });
+  return check_launch("swiglu_kernel");
+}
+
+dial_status launch_embedding(const void* table, const int32_t* ids, void* out, dial_dtype dt,
+                             int64_t tokens, int64_t vocab, int64_t dim, cudaStream_t st) {
+  int* err = device_error_ptr();
+  if (!err) return fail(DIAL_ERR_CUDA, "device error flag unavailable");
+  DISPATCH_T(dt, {
+    embedding_kernel<T><<<(unsigned)tokens, 256, 0, st>>>(
+        static_cast<const T*>(table), ids, static_cast<T*>(out), tokens, vocab, dim, err);
+  });
+  return check_launch("embedding_kernel");
+}
+
+dial_status launch_argmax(const void* x, int32_t* out, dial_dtype dt, int64_t rows, int64_t n,
+                          cudaStream_t st) {
+  DISPATCH_T(dt, { argmax_kernel<T><<<(unsigned)rows, 1024, 0, st>>>(static_cast<const T*>(x), out, n); });
+  return check_launch("argmax_kernel");
+}
+
+dial_status launch_rope_tables(void* cos_t, void* sin_t, dial_dtype dt, int64_t max_pos,
+                               int head_dim, float theta, cudaStream_t st) {
+  DISPATCH_T(dt, {
+    rope_table_kernel<T><<<grid_cap(max_pos * head_dim / 2, 256), 256, 0, st>>>(
+        static_cast<T*>(cos_t), static_cast<T*>(sin_t), max_pos, head_dim / 2, theta);
+  });
+  return check_launch("rope_table_kernel");
+}
+
+}  // namespace dial

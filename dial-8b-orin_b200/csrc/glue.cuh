@@ -1,0 +1,33 @@
+// Launchers of the decoder glue kernels (glue.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace dial {
+
+// Device flag that kernels set on a detected error (bounded wait expired,
+// out-of-range token id); defined in gemm_sm100.cu.
+int* device_error_ptr();
+
+dial_status launch_rmsnorm(const void* x, const void* res, void* h_out, const void* w, void* y,
+                           dial_dtype dt, int64_t rows, int64_t dim, float eps, cudaStream_t st);
+dial_status launch_qk_rope_kv(const void* qkv, const void* qn, const void* kn, const void* cos_t,
+                              const void* sin_t, const int32_t* pos, const int32_t* slot,
+                              void* q_out, void* kc, void* vc, dial_dtype dt, int64_t tokens,
+                              int hq, int hkv, int64_t max_seq, float eps, int qk_norm,
+                              cudaStream_t st);
+size_t attention_workspace_bytes(int64_t tokens, int hq, int64_t max_len);
+dial_status launch_attention(const void* q, const void* kc, const void* vc, const int32_t* pos,
+                             const int32_t* slot, void* out, void* ws, dial_dtype dt,
+                             int64_t tokens, int hq, int hkv, int64_t max_seq, int64_t max_len,
+                             cudaStream_t st);
+dial_status launch_swiglu(const void* gu, void* out, dial_dtype dt, int64_t tokens, int64_t inter,
+                          cudaStream_t st);
+dial_status launch_embedding(const void* table, const int32_t* ids, void* out, dial_dtype dt,
+                             int64_t tokens, int64_t vocab, int64_t dim, cudaStream_t st);
+dial_status launch_argmax(const void* x, int32_t* out, dial_dtype dt, int64_t rows, int64_t n,
+                          cudaStream_t st);
+dial_status launch_rope_tables(void* cos_t, void* sin_t, dial_dtype dt, int64_t max_pos,
+                               int head_dim, float theta, cudaStream_t st);
+
+}  // namespace dial

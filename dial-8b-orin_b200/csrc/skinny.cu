@@ -86,10 +86,6 @@ __device__ __forceinline__ void i8x4_to_bf16x2(uint32_t w, uint32_t& lo, uint32_
   hi = *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ uint32_t word(const uint4& v, int i) {
-  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
-
 constexpr int kWarps = 8;
 
 // ------------------------------------------------------------------ W8A16
@@ -98,6 +94,7 @@ __global__ void __launch_bounds__(256, 2)
     w8a16_skinny_kernel(const int8_t* __restrict__ q, const ST* __restrict__ scale,
                         const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int N,
                         int K, int S) {
+  constexpr int U = NT == 1 ? 3 : (NT == 2 ? 2 : 1);
   __shared__ float red[kWarps][NT][4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int tiles_per_cta = kWarps / S;
@@ -119,43 +116,53 @@ __global__ void __launch_bounds__(256, 2)
   const uint4 z = make_uint4(0, 0, 0, 0);
 
   if (tile * 16 < N) {
-    for (int gi = gbeg; gi < gend; ++gi) {
-      const int k0 = gi * 128 + 16 * t, k1 = k0 + 64;
-      const bool v0 = k0 < K, v1 = k1 < K;
-      const uint4 al0 = v0 ? ld_stream16(wlo + k0) : z;
-      const uint4 al1 = v1 ? ld_stream16(wlo + k1) : z;
-      const uint4 ah0 = v0 ? ld_stream16(whi + k0) : z;
-      const uint4 ah1 = v1 ? ld_stream16(whi + k1) : z;
-      uint4 xv[NT][4];
+    // U groups per iteration: all their loads are issued before any MMA so
+    // that every lane keeps U * 64 bytes of weights in flight.
+    for (int gi0 = gbeg; gi0 < gend; gi0 += U) {
+      uint4 al[U][2], ah[U][2];
+      uint4 xv[U][NT][4];
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        const int tok = j * 8 + g;
-        const uint16_t* xr = x + (size_t)min(tok, M - 1) * K;
-        const bool tv = tok < M;
-        xv[j][0] = (tv && v0) ? ld_ro16(xr + k0) : z;
-        xv[j][1] = (tv && v0) ? ld_ro16(xr + k0 + 8) : z;
-        xv[j][2] = (tv && v1) ? ld_ro16(xr + k1) : z;
-        xv[j][3] = (tv && v1) ? ld_ro16(xr + k1 + 8) : z;
+      for (int u = 0; u < U; ++u) {
+        const int gi = gi0 + u;
+        const int k0 = gi * 128 + 16 * t, k1 = k0 + 64;
+        const bool v0 = gi < gend && k0 < K, v1 = gi < gend && k1 < K;
+        al[u][0] = v0 ? ld_stream16(wlo + k0) : z;
+        al[u][1] = v1 ? ld_stream16(wlo + k1) : z;
+        ah[u][0] = v0 ? ld_stream16(whi + k0) : z;
+        ah[u][1] = v1 ? ld_stream16(whi + k1) : z;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const int tok = j * 8 + g;
+          const uint16_t* xr = x + (size_t)min(tok, M - 1) * K;
+          const bool tv = tok < M;
+          xv[u][j][0] = (tv && v0) ? ld_ro16(xr + k0) : z;
+          xv[u][j][1] = (tv && v0) ? ld_ro16(xr + k0 + 8) : z;
+          xv[u][j][2] = (tv && v1) ? ld_ro16(xr + k1) : z;
+          xv[u][j][3] = (tv && v1) ? ld_ro16(xr + k1 + 8) : z;
+        }
       }
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int u = 0; u < U; ++u) {
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          const uint32_t wl = word(h ? al1 : al0, s), wh = word(h ? ah1 : ah0, s);
-          uint32_t a0, a1, a2, a3;
-          if (BF16) {
-            i8x4_to_bf16x2(wl, a0, a2);
-            i8x4_to_bf16x2(wh, a1, a3);
-          } else {
-            i8x4_to_f16x2(wl, a0, a2);
-            i8x4_to_f16x2(wh, a1, a3);
-          }
+        for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            const uint4& xs = xv[j][2 * h + (s >> 1)];
-            const uint32_t b0 = word(xs, 2 * (s & 1)), b1 = word(xs, 2 * (s & 1) + 1);
-            if (BF16) mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
-            else mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
+          for (int s = 0; s < 4; ++s) {
+            const uint32_t wl = word(al[u][h], s), wh = word(ah[u][h], s);
+            uint32_t a0, a1, a2, a3;
+            if (BF16) {
+              i8x4_to_bf16x2(wl, a0, a2);
+              i8x4_to_bf16x2(wh, a1, a3);
+            } else {
+              i8x4_to_f16x2(wl, a0, a2);
+              i8x4_to_f16x2(wh, a1, a3);
+            }
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+              const uint4& xs = xv[u][j][2 * h + (s >> 1)];
+              const uint32_t b0 = word(xs, 2 * (s & 1)), b1 = word(xs, 2 * (s & 1) + 1);
+              if (BF16) mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
+              else mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
+            }
           }
         }
       }
@@ -244,6 +251,8 @@ __global__ void __launch_bounds__(256, 2)
                        const int8_t* __restrict__ xq, const float2* __restrict__ xs,
                        YT* __restrict__ y, int M, int Mp, int N, int G, int S) {
   constexpr int GB = TYPE == DIAL_GGML_Q4_0 ? 64 : 128;
+  // groups per iteration, so every lane keeps ~8 loads of 16 bytes in flight
+  constexpr int U = TYPE == DIAL_GGML_Q4_0 ? (NT <= 2 ? 4 : 2) : (NT == 1 ? 2 : 1);
   __shared__ float red[kWarps][NT][4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int tiles_per_cta = kWarps / S;
@@ -265,69 +274,76 @@ __global__ void __launch_bounds__(256, 2)
   const __half* dhi = dw + (size_t)rhi * G * 4;
 
   if (row0 < N) {
-    for (int gi = gbeg; gi < gend; ++gi) {
-      uint4 wl[TYPE == DIAL_GGML_Q4_0 ? 1 : 2], wh[TYPE == DIAL_GGML_Q4_0 ? 1 : 2];
-      if (TYPE == DIAL_GGML_Q4_0) {
-        wl[0] = ld_stream16(qlo + (size_t)gi * GB + 16 * t);
-        wh[0] = ld_stream16(qhi + (size_t)gi * GB + 16 * t);
-      } else {
-        wl[0] = ld_stream16(qlo + (size_t)gi * GB + 32 * t);
-        wl[TYPE == DIAL_GGML_Q4_0 ? 0 : 1] = ld_stream16(qlo + (size_t)gi * GB + 32 * t + 16);
-        wh[0] = ld_stream16(qhi + (size_t)gi * GB + 32 * t);
-        wh[TYPE == DIAL_GGML_Q4_0 ? 0 : 1] = ld_stream16(qhi + (size_t)gi * GB + 32 * t + 16);
-      }
-      const uint2 dl = __ldg(reinterpret_cast<const uint2*>(dlo + (size_t)gi * 4));
-      const uint2 dh = __ldg(reinterpret_cast<const uint2*>(dhi + (size_t)gi * 4));
-      const float dlv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dl.x)),
-                            __high2float(*reinterpret_cast<const __half2*>(&dl.x)),
-                            __low2float(*reinterpret_cast<const __half2*>(&dl.y)),
-                            __high2float(*reinterpret_cast<const __half2*>(&dl.y))};
-      const float dhv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dh.x)),
-                            __high2float(*reinterpret_cast<const __half2*>(&dh.x)),
-                            __low2float(*reinterpret_cast<const __half2*>(&dh.y)),
-                            __high2float(*reinterpret_cast<const __half2*>(&dh.y))};
-      uint4 xv[NT][2];
+    for (int gi0 = gbeg; gi0 < gend; gi0 += U) {
+      constexpr int NW = TYPE == DIAL_GGML_Q4_0 ? 1 : 2;  // 16-byte loads per row and group
+      uint4 wl[U][NW], wh[U][NW];
+      uint2 dl[U], dh[U];
+      uint4 xv[U][NT][2];
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        const int8_t* xr = xq + (size_t)(j * 8 + g) * G * 128 + (size_t)gi * 128 + 32 * t;
-        xv[j][0] = ld_ro16(xr);
-        xv[j][1] = ld_ro16(xr + 16);
-      }
+      for (int u = 0; u < U; ++u) {
+        const int gi = min(gi0 + u, gend - 1);  // clamped: a repeated group is never used
 #pragma unroll
-      for (int jb = 0; jb < 4; ++jb) {
-        uint32_t a0, a1, a2, a3;
-        if (TYPE == DIAL_GGML_Q4_0) {
-          const uint32_t l = word(wl[0], jb), h = word(wh[0], jb);
-          a0 = l & 0x0F0F0F0Fu;
-          a2 = (l >> 4) & 0x0F0F0F0Fu;
-          a1 = h & 0x0F0F0F0Fu;
-          a3 = (h >> 4) & 0x0F0F0F0Fu;
-        } else {
-          const uint4& l = wl[TYPE == DIAL_GGML_Q4_0 ? 0 : (jb >> 1)];
-          const uint4& h = wh[TYPE == DIAL_GGML_Q4_0 ? 0 : (jb >> 1)];
-          a0 = word(l, 2 * (jb & 1));
-          a2 = word(l, 2 * (jb & 1) + 1);
-          a1 = word(h, 2 * (jb & 1));
-          a3 = word(h, 2 * (jb & 1) + 1);
+        for (int c = 0; c < NW; ++c) {
+          wl[u][c] = ld_stream16(qlo + (size_t)gi * GB + (16 * NW) * t + 16 * c);
+          wh[u][c] = ld_stream16(qhi + (size_t)gi * GB + (16 * NW) * t + 16 * c);
         }
+        dl[u] = __ldg(reinterpret_cast<const uint2*>(dlo + (size_t)gi * 4));
+        dh[u] = __ldg(reinterpret_cast<const uint2*>(dhi + (size_t)gi * 4));
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
-          const uint4& xw = xv[j][jb >> 1];
-          int c[4] = {0, 0, 0, 0};
-          mma_s8(c, a0, a1, a2, a3, word(xw, 2 * (jb & 1)), word(xw, 2 * (jb & 1) + 1));
-          const float4 sc =
-              __ldg(reinterpret_cast<const float4*>(xs + (size_t)(gi * 4 + jb) * Mp + j * 8 + 2 * t));
-          float v0 = (float)c[0], v1 = (float)c[1], v2 = (float)c[2], v3 = (float)c[3];
+          const int8_t* xr = xq + (size_t)(j * 8 + g) * G * 128 + (size_t)gi * 128 + 32 * t;
+          xv[u][j][0] = ld_ro16(xr);
+          xv[u][j][1] = ld_ro16(xr + 16);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int gi = gi0 + u;
+        if (gi >= gend) break;
+        const float dlv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dl[u].x)),
+                              __high2float(*reinterpret_cast<const __half2*>(&dl[u].x)),
+                              __low2float(*reinterpret_cast<const __half2*>(&dl[u].y)),
+                              __high2float(*reinterpret_cast<const __half2*>(&dl[u].y))};
+        const float dhv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dh[u].x)),
+                              __high2float(*reinterpret_cast<const __half2*>(&dh[u].x)),
+                              __low2float(*reinterpret_cast<const __half2*>(&dh[u].y)),
+                              __high2float(*reinterpret_cast<const __half2*>(&dh[u].y))};
+#pragma unroll
+        for (int jb = 0; jb < 4; ++jb) {
+          uint32_t a0, a1, a2, a3;
           if (TYPE == DIAL_GGML_Q4_0) {
-            v0 = fmaf(-8.0f, sc.y, v0);
-            v1 = fmaf(-8.0f, sc.w, v1);
-            v2 = fmaf(-8.0f, sc.y, v2);
-            v3 = fmaf(-8.0f, sc.w, v3);
+            const uint32_t l = word(wl[u][0], jb), h = word(wh[u][0], jb);
+            a0 = l & 0x0F0F0F0Fu;
+            a2 = (l >> 4) & 0x0F0F0F0Fu;
+            a1 = h & 0x0F0F0F0Fu;
+            a3 = (h >> 4) & 0x0F0F0F0Fu;
+          } else {
+            const uint4& l = wl[u][(jb >> 1) % NW];
+            const uint4& h = wh[u][(jb >> 1) % NW];
+            a0 = word(l, 2 * (jb & 1));
+            a2 = word(l, 2 * (jb & 1) + 1);
+            a1 = word(h, 2 * (jb & 1));
+            a3 = word(h, 2 * (jb & 1) + 1);
           }
-          acc[j][0] = fmaf(dlv[jb] * sc.x, v0, acc[j][0]);
-          acc[j][1] = fmaf(dlv[jb] * sc.z, v1, acc[j][1]);
-          acc[j][2] = fmaf(dhv[jb] * sc.x, v2, acc[j][2]);
-          acc[j][3] = fmaf(dhv[jb] * sc.z, v3, acc[j][3]);
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const uint4& xw = xv[u][j][jb >> 1];
+            int c[4] = {0, 0, 0, 0};
+            mma_s8(c, a0, a1, a2, a3, word(xw, 2 * (jb & 1)), word(xw, 2 * (jb & 1) + 1));
+            const float4 sc = __ldg(
+                reinterpret_cast<const float4*>(xs + (size_t)(gi * 4 + jb) * Mp + j * 8 + 2 * t));
+            float v0 = (float)c[0], v1 = (float)c[1], v2 = (float)c[2], v3 = (float)c[3];
+            if (TYPE == DIAL_GGML_Q4_0) {
+              v0 = fmaf(-8.0f, sc.y, v0);
+              v1 = fmaf(-8.0f, sc.w, v1);
+              v2 = fmaf(-8.0f, sc.y, v2);
+              v3 = fmaf(-8.0f, sc.w, v3);
+            }
+            acc[j][0] = fmaf(dlv[jb] * sc.x, v0, acc[j][0]);
+            acc[j][1] = fmaf(dlv[jb] * sc.z, v1, acc[j][1]);
+            acc[j][2] = fmaf(dhv[jb] * sc.x, v2, acc[j][2]);
+            acc[j][3] = fmaf(dhv[jb] * sc.z, v3, acc[j][3]);
+          }
         }
       }
     }

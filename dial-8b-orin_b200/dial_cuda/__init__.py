@@ -50,6 +50,7 @@ SIGNATURES = {
     "dial_last_error": ([], ctypes.c_char_p),
     "dial_abi_version": ([], _i32),
     "dial_launch_count": ([], ctypes.c_uint64),
+    "dial_device_error": ([_i32], _i32),
     "dial_w8a16_quantize": ([_vp, _i32, _i64, _i64, _vp, _vp, _i32, _vp], _i32),
     "dial_w8a16_dequantize": ([_vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp], _i32),
     "dial_w8a16_linear": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp], _i32),
@@ -61,6 +62,16 @@ SIGNATURES = {
     "dial_gguf_dequantize": ([_vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp], _i32),
     "dial_gguf_linear_workspace_bytes": ([_i64, _i64], _sz),
     "dial_gguf_linear": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp, _sz, _vp], _i32),
+    "dial_rmsnorm": ([_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, ctypes.c_float, _vp], _i32),
+    "dial_rope_tables": ([_vp, _vp, _i32, _i64, _i32, ctypes.c_float, _vp], _i32),
+    "dial_qk_norm_rope_kv_append": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64,
+                                     _i32, _i32, _i32, _i64, ctypes.c_float, _i32, _vp], _i32),
+    "dial_attention_workspace_bytes": ([_i64, _i32, _i64], _sz),
+    "dial_attention": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i32, _i64, _i32, _i32, _i32, _i64,
+                        _i64, _vp], _i32),
+    "dial_swiglu": ([_vp, _vp, _i32, _i64, _i64, _vp], _i32),
+    "dial_embedding": ([_vp, _vp, _vp, _i32, _i64, _i64, _i64, _vp], _i32),
+    "dial_argmax": ([_vp, _vp, _i32, _i64, _i64, _vp], _i32),
 }
 
 

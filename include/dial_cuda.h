@@ -66,6 +66,9 @@ DIAL_API const char* dial_last_error(void);
 DIAL_API int dial_abi_version(void);
 /* Number of kernels launched by this library in this process (all threads). */
 DIAL_API uint64_t dial_launch_count(void);
+/* Synchronising check of the device error flag that kernels with bounded
+ * waits set when a wait expires (DIAL_ERR_TIMEOUT); `clear` resets it. */
+DIAL_API dial_status dial_device_error(int clear);
 
 /* ------------------------------------------------------------------ W8A16
  * Layout: q int8 [N, K] row-major (K contiguous), scale [N] (f32 as in the
@@ -141,6 +144,64 @@ DIAL_API size_t dial_gguf_linear_workspace_bytes(int64_t M, int64_t K);
 DIAL_API dial_status dial_gguf_linear(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,
                              dial_ggml_type type, void* y, int64_t M, int64_t K, int64_t N,
                              void* workspace, size_t workspace_bytes, dial_stream stream);
+
+/* ------------------------------------------------------------------ decoder glue
+ * Activations are row-major [tokens, ...] in `dt` (f16 as the reference's
+ * --dtype f16, or bf16); all arithmetic is f32.  head_dim must be 128.
+ * KV caches are [slots, n_kv_heads, max_seq, head_dim]: one slot per sequence,
+ * the preallocated decode storage of llama3/cache.rs:149-217.
+ */
+
+/* RMSNorm with an optional fused residual add (candle_nn::RmsNorm at
+ * text.rs:1620-1626, 1649-1674; ln_f qwen3_vl.rs:2425-2429):
+ *   h = residual ? round_dt(x + residual) : x;   if h_out: h_out = h
+ *   y = round_dt(h * rsqrt(mean(h^2) + eps) * w)          w: [dim]
+ * h_out may alias x or residual. */
+DIAL_API dial_status dial_rmsnorm(const void* x, const void* residual, void* h_out, const void* w,
+                                  void* y, dial_dtype dt, int64_t rows, int64_t dim, float eps,
+                                  dial_stream stream);
+
+/* RoPE tables of llama3/cache.rs:24-64: angle[p, i] = p * (1 / theta^(2i/D)),
+ * cos/sin [max_pos, D/2] in dt. */
+DIAL_API dial_status dial_rope_tables(void* cos_t, void* sin_t, dial_dtype dt, int64_t max_pos,
+                                      int head_dim, float theta, dial_stream stream);
+
+/* Post-QKV step of QwenAttention::forward (text.rs:1485-1531): split the fused
+ * qkv [T, (Hq + 2*Hkv) * D]; per-head RMSNorm of q and k with q_norm_w / k_norm_w
+ * [D] when qk_norm != 0 (Qwen3; Llama has none); RoPE at positions[t]; q goes to
+ * q_out [T, Hq, D], k and v to row positions[t] of cache slot slots[t]. */
+DIAL_API dial_status dial_qk_norm_rope_kv_append(
+    const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos_t,
+    const void* sin_t, const int32_t* positions, const int32_t* slots, void* q_out,
+    void* k_cache, void* v_cache, dial_dtype dt, int64_t tokens, int n_heads, int n_kv_heads,
+    int head_dim, int64_t max_seq, float eps, int qk_norm, dial_stream stream);
+
+/* GQA attention over the cache (text.rs:1258-1327): query t (q [T, Hq, D]) attends
+ * rows 0..positions[t] of slot slots[t]; out [T, Hq*D] = softmax(q.K^T/sqrt(D)) V.
+ * Decode passes one token per sequence, prefill a run of tokens (causal through
+ * positions).  max_len >= max(positions)+1 sizes the key split; `workspace` holds
+ * dial_attention_workspace_bytes(T, Hq, max_len) bytes (NULL when 0). */
+DIAL_API size_t dial_attention_workspace_bytes(int64_t tokens, int n_heads, int64_t max_len);
+DIAL_API dial_status dial_attention(const void* q, const void* k_cache, const void* v_cache,
+                                    const int32_t* positions, const int32_t* slots, void* out,
+                                    void* workspace, size_t workspace_bytes, dial_dtype dt,
+                                    int64_t tokens, int n_heads, int n_kv_heads, int head_dim,
+                                    int64_t max_seq, int64_t max_len, dial_stream stream);
+
+/* SwiGLU of Mlp (text.rs:816-820): out[t, i] = silu(g) * u over the halves of
+ * gate_up [T, 2I] (silu result rounded to dt first, as two tensor ops). */
+DIAL_API dial_status dial_swiglu(const void* gate_up, void* out, dial_dtype dt, int64_t tokens,
+                                 int64_t intermediate, dial_stream stream);
+
+/* Embedding rows: out[t] = table[ids[t]] (table [vocab, dim]).  An id outside
+ * [0, vocab) writes zeros and sets the device error flag (DIAL_ERR_INVALID_ARG). */
+DIAL_API dial_status dial_embedding(const void* table, const int32_t* ids, void* out,
+                                    dial_dtype dt, int64_t tokens, int64_t vocab, int64_t dim,
+                                    dial_stream stream);
+
+/* Greedy sampling (qwen3_vl.rs:130-143): out[r] = first index of max(x[r, :]). */
+DIAL_API dial_status dial_argmax(const void* x, int32_t* out, dial_dtype dt, int64_t rows,
+                                 int64_t n, dial_stream stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

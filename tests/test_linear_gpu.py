@@ -179,3 +179,50 @@ def test_gguf_rejects_missing_workspace(D, torch):
     st = D.lib().dial_gguf_linear(x.data_ptr(), D.F32, lin.qs.data_ptr(), lin.d.data_ptr(), D.Q4_0,
                                   y.data_ptr(), 1, 64, 64, None, 0, D.stream_ptr())
     assert st == 1
+
+
+# ---------------------------------------------------------------- tcgen05 GEMM path (M > 32)
+@pytest.mark.parametrize("M,N,K", [(33, 256, 64), (128, 512, 4096), (200, 1000, 1024),
+                                   (512, 4096, 4096), (300, 12288, 192)])
+@pytest.mark.parametrize("xdt", ["f16", "bf16"])
+def test_w8a16_gemm_parity(D, torch, M, N, K, xdt):
+    rng = np.random.default_rng(M + N + K)
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    x = rng.normal(0, 1, (M, K)).astype(np.float32)
+    lin = D.W8A16Linear.from_linear("t", _to_dev(torch, w))
+    if xdt == "f16":
+        xin = x.astype(np.float16)
+        xt = _to_dev(torch, xin)
+    else:
+        xin = O.f32_to_bf16(x)
+        xt = _to_dev(torch, xin.view(np.int16)).view(torch.bfloat16)
+    y = lin.forward(xt).float().cpu().numpy()
+    assert D.lib().dial_device_error(1) == 0
+    y_ref, _ = O.w8a16_linear(xin, lin.qweight.cpu().numpy(), lin.scales.cpu().numpy(),
+                              x_is_bf16=(xdt == "bf16"))
+    assert rel_err(y, y_ref) <= (2e-3 if xdt == "f16" else 8e-3)
+
+
+@pytest.mark.parametrize("qt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("M,N,K", [(64, 512, 4096), (512, 1024, 4096), (130, 300, 12288 + 64)])
+@pytest.mark.parametrize("xdt", ["f32", "f16", "bf16"])
+def test_gguf_gemm_parity(D, torch, qt, M, N, K, xdt):
+    rng = np.random.default_rng(M * 3 + N + qt)
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    x = rng.normal(0, 1, (M, K)).astype(np.float32)
+    blocks = O.gguf_quantize(w, qt)
+    lin = D.GgufLinear.from_blocks(_to_dev(torch, blocks), qt, K, N)
+    if xdt == "f32":
+        xin, xt, bf = x, _to_dev(torch, x), False
+    elif xdt == "f16":
+        xin = x.astype(np.float16)
+        xt, bf = _to_dev(torch, xin), False
+    else:
+        xin = O.f32_to_bf16(x)
+        xt, bf = _to_dev(torch, xin.view(np.int16)).view(torch.bfloat16), True
+    y = lin.forward(xt).float().cpu().numpy()
+    assert D.lib().dial_device_error(1) == 0
+    exact = O.gguf_linear_exact(xin, blocks, qt, N, x_is_bf16=bf)
+    # f16 operands (weights d*q and f32 activations rounded once) or bf16 operands
+    tol = {"f32": 2e-3, "f16": 2e-3, "bf16": 1e-2}[xdt]
+    assert rel_err(y, exact) <= tol

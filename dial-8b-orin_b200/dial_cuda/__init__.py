@@ -62,6 +62,7 @@ SIGNATURES = {
     "dial_gguf_dequantize": ([_vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp], _i32),
     "dial_gguf_linear_workspace_bytes": ([_i64, _i64], _sz),
     "dial_gguf_linear": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp, _sz, _vp], _i32),
+    "dial_gguf_linear_noalloc": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp], _i32),
     "dial_rmsnorm": ([_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, ctypes.c_float, _vp], _i32),
     "dial_rope_tables": ([_vp, _vp, _i32, _i64, _i32, ctypes.c_float, _vp], _i32),
     "dial_qk_norm_rope_kv_append": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64,

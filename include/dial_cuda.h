@@ -145,6 +145,20 @@ DIAL_API dial_status dial_gguf_linear(const void* x, dial_dtype xdt, const void*
                              dial_ggml_type type, void* y, int64_t M, int64_t K, int64_t N,
                              void* workspace, size_t workspace_bytes, dial_stream stream);
 
+/* The same GGUF linear (integer path: activations quantised to Q8_0, exact
+ * block dots) for callers that cannot allocate device memory when they run it
+ * -- e.g. a worker loop whose allocator is not re-entrant, or an FFI caller
+ * with no device allocator.  No counterpart in the reference: its scratch
+ * lives in a fixed 640 KiB __device__ array inside this library instead of a
+ * caller workspace, so the call allocates nothing.  K <= 16384 (larger K
+ * returns DIAL_ERR_SHAPE); any M, 32 rows per pass.  The first call on a
+ * device looks up the array's address (make it before any stream capture).
+ * All calls share the array: calls that overlap on the GPU race on it, so
+ * order them on one stream. */
+DIAL_API dial_status dial_gguf_linear_noalloc(const void* x, dial_dtype xdt, const void* qs,
+                                              const uint16_t* d, dial_ggml_type type, void* y,
+                                              int64_t M, int64_t K, int64_t N, dial_stream stream);
+
 /* ------------------------------------------------------------------ decoder glue
  * Activations are row-major [tokens, ...] in `dt` (f16 as the reference's
  * --dtype f16, or bf16); all arithmetic is f32.  head_dim must be 128.

@@ -63,9 +63,9 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // ------------------------------------------------------------------ RMSNorm (+ residual)
 // One CTA per row.  h = x (+ residual, rounded to T); y = h * rsqrt(mean(h^2)+eps) * w.
 template <typename T, int THREADS>
-__global__ void __launch_bounds__(THREADS) rmsnorm_kernel(const T* __restrict__ x,
-                                                          const T* __restrict__ res,
-                                                          T* __restrict__ h_out,
+__global__ void __launch_bounds__(THREADS) rmsnorm_kernel(const T* x,  // x/res may alias h_out
+                                                          const T* res,
+                                                          T* h_out,
                                                           const T* __restrict__ w,
                                                           T* __restrict__ y, int dim, float eps) {
   extern __shared__ float hbuf[];  // dim floats
@@ -290,6 +290,22 @@ __global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int
   }
 }
 
+// h = round(h + d), the residual add after the last layer of a stage (text.rs:1672-1674)
+template <typename T>
+__global__ void add_kernel(T* __restrict__ h, const T* __restrict__ d, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    h[i] = rnd<T>(ld(h, i) + ld(d, i));
+}
+
+template <typename T>
+__global__ void gather_rows_kernel(const T* __restrict__ src, const int32_t* __restrict__ idx,
+                                   T* __restrict__ dst, int64_t dim) {
+  const int64_t r = blockIdx.x;
+  const int64_t s = idx[r];
+  for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) dst[r * dim + i] = src[s * dim + i];
+}
+
 // ------------------------------------------------------------------ embedding / argmax
 template <typename T>
 __global__ void embedding_kernel(const T* __restrict__ table, const int32_t* __restrict__ ids,
@@ -444,6 +460,22 @@ dial_status launch_swiglu(const void* gu, void* out, dial_dtype dt, int64_t toke
         static_cast<const T*>(gu), static_cast<T*>(out), tokens, inter);
   });
   return check_launch("swiglu_kernel");
+}
+
+dial_status launch_gather_rows(const void* src, const int32_t* idx, void* dst, dial_dtype dt,
+                               int64_t rows, int64_t dim, cudaStream_t st) {
+  DISPATCH_T(dt, {
+    gather_rows_kernel<T><<<(unsigned)rows, 256, 0, st>>>(static_cast<const T*>(src), idx,
+                                                          static_cast<T*>(dst), dim);
+  });
+  return check_launch("gather_rows_kernel");
+}
+
+dial_status launch_add(void* h, const void* d, dial_dtype dt, int64_t n, cudaStream_t st) {
+  DISPATCH_T(dt, {
+    add_kernel<T><<<grid_cap(n, 256), 256, 0, st>>>(static_cast<T*>(h), static_cast<const T*>(d), n);
+  });
+  return check_launch("add_kernel");
 }
 
 dial_status launch_embedding(const void* table, const int32_t* ids, void* out, dial_dtype dt,

@@ -217,6 +217,80 @@ DIAL_API dial_status dial_embedding(const void* table, const int32_t* ids, void*
 DIAL_API dial_status dial_argmax(const void* x, int32_t* out, dial_dtype dt, int64_t rows,
                                  int64_t n, dial_stream stream);
 
+/* ------------------------------------------------------------------ decoder stage
+ * A pipeline stage = a contiguous range of decoder layers (spm::Forwarder /
+ * Transformer::forward, text.rs:1636-1688), with the embedding on the first
+ * stage and final norm + output head + greedy argmax on the last
+ * (qwen3_vl.rs:2420-2451, :130-143).  Weights stay in the quantised formats
+ * above; activations are `act_dtype` (f16 as the reference's --dtype f16).
+ */
+typedef enum {
+  DIAL_WFMT_W8A16 = 0,     /* int8 [N,K] + f32 scale [N] (reference layout) */
+  DIAL_WFMT_W8A16_F16S = 1, /* int8 [N,K] + f16 scale [N] */
+  DIAL_WFMT_Q4_0 = 2,      /* dial_gguf_repack layout: qs + d */
+  DIAL_WFMT_Q8_0 = 8
+} dial_weight_format;
+
+typedef struct dial_decoder_dims {
+  int32_t hidden;         /* 4096 */
+  int32_t intermediate;   /* 12288 (Qwen3-8B), 14336 (Llama-3-8B) */
+  int32_t n_heads;        /* 32 */
+  int32_t n_kv_heads;     /* 8 */
+  int32_t head_dim;       /* 128 */
+  int32_t vocab;          /* 151936 (Qwen3), 128256 (Llama-3) */
+  int32_t qk_norm;        /* 1: per-head q_norm/k_norm (Qwen3); 0: none (Llama) */
+  int32_t weight_format;  /* dial_weight_format of the layer linears */
+  int32_t head_format;    /* dial_weight_format of the output head */
+  int32_t act_dtype;      /* DIAL_F16 or DIAL_BF16 */
+  float rms_eps;          /* 1e-6 */
+  int64_t max_seq;        /* KV rows per slot */
+  int32_t n_slots;        /* KV slots (sequences) */
+} dial_decoder_dims;
+
+/* A quantised linear: W8A16 {int8 q, scale}; GGUF {qs, d}. */
+typedef struct dial_linear_ref {
+  const void* w;
+  const void* s;
+} dial_linear_ref;
+
+typedef struct dial_layer_weights {
+  dial_linear_ref qkv;     /* [(Hq + 2*Hkv)*D, H] -- fused q,k,v (text.rs:1428-1432) */
+  dial_linear_ref o;       /* [H, Hq*D] */
+  dial_linear_ref gate_up; /* [2*I, H] -- fused gate,up (text.rs:634-637) */
+  dial_linear_ref down;    /* [H, I] */
+  const void* input_norm;  /* [H] */
+  const void* post_norm;   /* [H] */
+  const void* q_norm;      /* [D], qk_norm only */
+  const void* k_norm;      /* [D] */
+  void* k_cache;           /* [n_slots, Hkv, max_seq, D] */
+  void* v_cache;
+} dial_layer_weights;
+
+/* Workspace for dial_decoder_layers / dial_decoder_head on `tokens` rows whose
+ * positions are < max_len. */
+DIAL_API size_t dial_decoder_workspace_bytes(const dial_decoder_dims* dims, int64_t tokens,
+                                             int64_t max_len);
+
+/* Runs n_layers consecutive decoder layers on hidden [T, H] in place (the
+ * residual stream).  Token t is at positions[t] of KV slot slots[t]; decode
+ * passes one token per sequence, prefill a run of one sequence's tokens.
+ * cos_t/sin_t come from dial_rope_tables (max_pos >= max_len). */
+DIAL_API dial_status dial_decoder_layers(const dial_decoder_dims* dims,
+                                         const dial_layer_weights* layers, int n_layers,
+                                         void* hidden, const int32_t* positions,
+                                         const int32_t* slots, int64_t tokens, int64_t max_len,
+                                         const void* cos_t, const void* sin_t, void* workspace,
+                                         size_t workspace_bytes, dial_stream stream);
+
+/* Last stage: y = head(rmsnorm(hidden[rows], final_norm)); out_ids[r] = argmax.
+ * `rows` selects which hidden rows to sample (row_index[r], NULL = 0..rows-1);
+ * logits (optional, [rows, vocab] act_dtype) receives the head output. */
+DIAL_API dial_status dial_decoder_head(const dial_decoder_dims* dims, const void* final_norm,
+                                       dial_linear_ref head, const void* hidden,
+                                       const int32_t* row_index, int64_t rows, int32_t* out_ids,
+                                       void* logits, void* workspace, size_t workspace_bytes,
+                                       dial_stream stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

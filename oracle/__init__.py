@@ -61,10 +61,73 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_gguf_linear_candle": ([vp, i32, vp, i32, i64, i64, i64, vp], i32),
         "orc_q8_0_quantize_rows": ([vp, i32, i64, i64, vp, vp], i32),
     }
+    f32 = ctypes.c_float
+    sig.update({
+        "orc_rmsnorm": ([vp, vp, vp, vp, vp, i64, i64, f32], None),
+        "orc_rope_tables": ([vp, vp, i64, i32, f32], None),
+        "orc_decoder_generate": ([ctypes.POINTER(OrcDecoder), ctypes.POINTER(ctypes.c_void_p), vp, vp,
+                                  vp, vp, vp, i32, i32, vp, vp], i32),
+    })
     for name, (argtypes, restype) in sig.items():
         fn = getattr(L, name)
         fn.argtypes = argtypes
         fn.restype = restype
+
+
+class OrcDecoder(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int32), ("hidden", ctypes.c_int32), ("inter", ctypes.c_int32),
+                ("n_heads", ctypes.c_int32), ("n_kv", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("vocab", ctypes.c_int32), ("qk_norm", ctypes.c_int32), ("eps", ctypes.c_float),
+                ("theta", ctypes.c_float)]
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float, res: np.ndarray | None = None):
+    """f16 in/out: (h, y) with h = f16(x + res) (or x), y = f16(h*rsqrt(mean(h^2)+eps)*w)."""
+    x = np.ascontiguousarray(x, np.float16)
+    rows, dim = x.shape
+    y = np.empty_like(x)
+    h = np.empty_like(x)
+    r = None if res is None else np.ascontiguousarray(res, np.float16)
+    lib().orc_rmsnorm(_p(x), _p(r), _p(h), _p(np.ascontiguousarray(w, np.float16)), _p(y), rows, dim,
+                      eps)
+    return h, y
+
+
+def rope_tables(max_pos: int, head_dim: int, theta: float):
+    c = np.empty((max_pos, head_dim // 2), np.float16)
+    s = np.empty_like(c)
+    lib().orc_rope_tables(_p(c), _p(s), max_pos, head_dim, theta)
+    return c, s
+
+
+def decoder_generate(cfg: dict, layers: list, embed: np.ndarray, final_norm: np.ndarray,
+                     head_q: np.ndarray, head_s: np.ndarray, prompt, n_new: int):
+    """Greedy generation on the oracle decoder (W8A16 weights, f16 activations).
+
+    layers: list of dicts with int8 `qkv_q, o_q, gu_q, down_q`, f32 `*_s` and f16
+    `input_norm, post_norm, q_norm, k_norm`.  Returns (tokens, top1-top2 margins)."""
+    keys = ["qkv_q", "qkv_s", "o_q", "o_s", "gu_q", "gu_s", "down_q", "down_s", "input_norm",
+            "post_norm", "q_norm", "k_norm"]
+    keep = []
+    ptrs = (ctypes.c_void_p * (len(layers) * len(keys)))()
+    for i, L in enumerate(layers):
+        for j, k in enumerate(keys):
+            a = np.ascontiguousarray(L[k])
+            keep.append(a)
+            ptrs[i * len(keys) + j] = a.ctypes.data
+    d = OrcDecoder(cfg["n_layers"], cfg["hidden"], cfg["inter"], cfg["n_heads"], cfg["n_kv"],
+                   cfg["head_dim"], cfg["vocab"], int(cfg["qk_norm"]), cfg["eps"], cfg["theta"])
+    prompt = np.ascontiguousarray(prompt, np.int32)
+    toks = np.empty(n_new, np.int32)
+    margins = np.empty(n_new, np.float32)
+    embed = np.ascontiguousarray(embed, np.float16)
+    rc = lib().orc_decoder_generate(ctypes.byref(d), ptrs, _p(embed),
+                                    _p(np.ascontiguousarray(final_norm, np.float16)),
+                                    _p(np.ascontiguousarray(head_q, np.int8)),
+                                    _p(np.ascontiguousarray(head_s, np.float32)), _p(prompt),
+                                    len(prompt), n_new, _p(toks), _p(margins))
+    assert rc == 0
+    return toks, margins
 
 
 def _p(a: np.ndarray | None):

@@ -392,3 +392,198 @@ ORC_API int orc_q8_0_quantize_rows(const void* x, int xdt, int64_t M, int64_t K,
     }
   return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Decoder glue and a whole decoder (greedy), W8A16 weights, f16 activations */
+/* Order and rounding points follow the reference's f16 tensors:            */
+/*   text.rs:1636-1688 (Transformer::forward: rms_1, attn + residual, rms_2, */
+/*   mlp + residual), text.rs:1478-1596 (QKV -> QK RMSNorm -> RoPE -> KV ->   */
+/*   GQA attention -> O), text.rs:816-820 (silu(gate) * up),                  */
+/*   llama3/cache.rs:24-64 (RoPE tables in f32, stored as f16),              */
+/*   qwen3_vl.rs:2420-2451 (ln_f -> last position -> lm_head), :130-143       */
+/*   (argmax).  Accumulations are done in double.                            */
+/* ------------------------------------------------------------------------ */
+
+static inline float hr(float v) { return h2f(f2h(v)); } /* round through f16 */
+
+/* y = f16(h * (1/sqrt(mean(h^2)+eps)) * w), h = f16(x + res) when res != NULL */
+ORC_API void orc_rmsnorm(const uint16_t* x, const uint16_t* res, uint16_t* h_out,
+                         const uint16_t* w, uint16_t* y, int64_t rows, int64_t dim, float eps) {
+  float* h = (float*)malloc(sizeof(float) * (size_t)dim);
+  for (int64_t r = 0; r < rows; ++r) {
+    double ss = 0.0;
+    for (int64_t i = 0; i < dim; ++i) {
+      float v = h2f(x[r * dim + i]);
+      if (res) v = hr(v + h2f(res[r * dim + i]));
+      h[i] = v;
+      ss += (double)v * v;
+    }
+    const float inv = (float)(1.0 / sqrt(ss / (double)dim + (double)eps));
+    for (int64_t i = 0; i < dim; ++i) {
+      if (h_out) h_out[r * dim + i] = f2h(h[i]);
+      y[r * dim + i] = f2h(h[i] * inv * h2f(w[i]));
+    }
+  }
+  free(h);
+}
+
+/* cos/sin [max_pos, D/2] as f16: inv_freq = 1/theta^(2i/D) (f32), angle = p*inv_freq */
+ORC_API void orc_rope_tables(uint16_t* cos_t, uint16_t* sin_t, int64_t max_pos, int D,
+                             float theta) {
+  for (int64_t p = 0; p < max_pos; ++p)
+    for (int i = 0; i < D / 2; ++i) {
+      const float inv = 1.0f / powf(theta, (float)(2 * i) / (float)D);
+      const float a = (float)p * inv;
+      cos_t[p * (D / 2) + i] = f2h(cosf(a));
+      sin_t[p * (D / 2) + i] = f2h(sinf(a));
+    }
+}
+
+/* one head (D values, f16 bits in/out): optional RMSNorm then RoPE at position p */
+static void head_norm_rope(const uint16_t* src, const uint16_t* nw, int qk_norm, float eps,
+                           const uint16_t* cos_t, const uint16_t* sin_t, int p, int D,
+                           uint16_t* dst) {
+  float v[256];
+  double ss = 0.0;
+  for (int i = 0; i < D; ++i) { v[i] = h2f(src[i]); ss += (double)v[i] * v[i]; }
+  if (qk_norm) {
+    const float inv = (float)(1.0 / sqrt(ss / (double)D + (double)eps));
+    for (int i = 0; i < D; ++i) v[i] = hr(v[i] * inv * h2f(nw[i]));
+  }
+  const int half = D / 2;
+  for (int i = 0; i < half; ++i) {
+    const float c = h2f(cos_t[(int64_t)p * half + i]), s = h2f(sin_t[(int64_t)p * half + i]);
+    dst[i] = f2h(v[i] * c - v[i + half] * s);
+    dst[i + half] = f2h(v[i + half] * c + v[i] * s);
+  }
+}
+
+/* attention of one query head over cache rows 0..len-1 (f16 K/V [max_seq][D]) */
+static void attend(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int len, int D,
+                   uint16_t* out) {
+  double* sc = (double*)malloc(sizeof(double) * (size_t)len);
+  const double scale = 1.0 / sqrt((double)D);
+  double mx = -1e300;
+  for (int j = 0; j < len; ++j) {
+    double s = 0.0;
+    for (int d = 0; d < D; ++d) s += (double)h2f(q[d]) * h2f(kc[(int64_t)j * D + d]);
+    sc[j] = s * scale;
+    if (sc[j] > mx) mx = sc[j];
+  }
+  double sum = 0.0;
+  for (int j = 0; j < len; ++j) { sc[j] = exp(sc[j] - mx); sum += sc[j]; }
+  for (int d = 0; d < D; ++d) {
+    double acc = 0.0;
+    for (int j = 0; j < len; ++j) acc += sc[j] * h2f(vc[(int64_t)j * D + d]);
+    out[d] = f2h((float)(acc / sum));
+  }
+  free(sc);
+}
+
+/* y[t, n] = f16((sum_k q[n,k] x[t,k]) * s[n]) */
+static void lin16(const uint16_t* x, const int8_t* q, const float* s, int64_t T, int64_t K,
+                  int64_t N, uint16_t* y) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t n = 0; n < N; ++n) {
+      double acc = 0.0;
+      const int8_t* row = q + n * K;
+      for (int64_t k = 0; k < K; ++k) acc += (double)row[k] * h2f(x[t * K + k]);
+      y[t * N + n] = f2h((float)acc * s[n]);
+    }
+}
+
+typedef struct orc_decoder {
+  int32_t n_layers, hidden, inter, n_heads, n_kv, head_dim, vocab, qk_norm;
+  float eps, theta;
+} orc_decoder;
+
+/* Per-layer pointer table (12 entries): qkv_q, qkv_s, o_q, o_s, gu_q, gu_s,
+ * down_q, down_s, input_norm, post_norm, q_norm, k_norm.  Norms are f16 bits. */
+enum { L_QKV_Q, L_QKV_S, L_O_Q, L_O_S, L_GU_Q, L_GU_S, L_DN_Q, L_DN_S, L_IN, L_POST, L_QN, L_KN, L_N };
+
+/* Greedy generation for one sequence: prefill `prompt`, then n_new tokens.
+ * out_tokens[n_new]; margins[n_new] = top1 - top2 logit of each step. */
+ORC_API int orc_decoder_generate(const orc_decoder* c, const void* const* layer_ptrs,
+                                 const uint16_t* embed, const uint16_t* final_norm,
+                                 const int8_t* head_q, const float* head_s, const int32_t* prompt,
+                                 int n_prompt, int n_new, int32_t* out_tokens, float* margins) {
+  const int64_t H = c->hidden, I = c->inter, D = c->head_dim, Hq = c->n_heads, Hkv = c->n_kv;
+  const int64_t QKV = (Hq + 2 * Hkv) * D, QD = Hq * D, V = c->vocab;
+  const int64_t max_seq = n_prompt + n_new + 1;
+  const int rep = (int)(Hq / Hkv);
+  uint16_t* kc = (uint16_t*)calloc((size_t)(c->n_layers * Hkv * max_seq * D), 2);
+  uint16_t* vc = (uint16_t*)calloc((size_t)(c->n_layers * Hkv * max_seq * D), 2);
+  uint16_t* cos_t = (uint16_t*)malloc((size_t)(max_seq * D / 2) * 2);
+  uint16_t* sin_t = (uint16_t*)malloc((size_t)(max_seq * D / 2) * 2);
+  orc_rope_tables(cos_t, sin_t, max_seq, (int)D, c->theta);
+  const int64_t Tmax = n_prompt;
+  uint16_t* h = (uint16_t*)malloc((size_t)(Tmax * H) * 2);
+  uint16_t* x1 = (uint16_t*)malloc((size_t)(Tmax * H) * 2);
+  uint16_t* qkv = (uint16_t*)malloc((size_t)(Tmax * QKV) * 2);
+  uint16_t* qr = (uint16_t*)malloc((size_t)(Tmax * QD) * 2);
+  uint16_t* att = (uint16_t*)malloc((size_t)(Tmax * QD) * 2);
+  uint16_t* dl = (uint16_t*)malloc((size_t)(Tmax * H) * 2);
+  uint16_t* gu = (uint16_t*)malloc((size_t)(Tmax * 2 * I) * 2);
+  uint16_t* mid = (uint16_t*)malloc((size_t)(Tmax * I) * 2);
+  uint16_t* logits = (uint16_t*)malloc((size_t)V * 2);
+  int32_t* toks = (int32_t*)malloc(sizeof(int32_t) * (size_t)(n_prompt + n_new));
+  memcpy(toks, prompt, sizeof(int32_t) * (size_t)n_prompt);
+  int64_t p0 = 0, T = n_prompt;
+  for (int step = 0; step < n_new; ++step) {
+    for (int64_t t = 0; t < T; ++t) memcpy(h + t * H, embed + (int64_t)toks[p0 + t] * H, (size_t)H * 2);
+    for (int l = 0; l < c->n_layers; ++l) {
+      const void* const* P = layer_ptrs + (int64_t)l * L_N;
+      orc_rmsnorm(h, NULL, NULL, (const uint16_t*)P[L_IN], x1, T, H, c->eps);
+      lin16(x1, (const int8_t*)P[L_QKV_Q], (const float*)P[L_QKV_S], T, H, QKV, qkv);
+      uint16_t* kl = kc + (int64_t)l * Hkv * max_seq * D;
+      uint16_t* vl = vc + (int64_t)l * Hkv * max_seq * D;
+      for (int64_t t = 0; t < T; ++t) {
+        const int pos = (int)(p0 + t);
+        for (int64_t hh = 0; hh < Hq; ++hh)
+          head_norm_rope(qkv + t * QKV + hh * D, (const uint16_t*)P[L_QN], c->qk_norm, c->eps,
+                         cos_t, sin_t, pos, (int)D, qr + t * QD + hh * D);
+        for (int64_t g = 0; g < Hkv; ++g) {
+          head_norm_rope(qkv + t * QKV + (Hq + g) * D, (const uint16_t*)P[L_KN], c->qk_norm, c->eps,
+                         cos_t, sin_t, pos, (int)D, kl + (g * max_seq + pos) * D);
+          memcpy(vl + (g * max_seq + pos) * D, qkv + t * QKV + (Hq + Hkv + g) * D, (size_t)D * 2);
+        }
+      }
+      for (int64_t t = 0; t < T; ++t)
+        for (int64_t hh = 0; hh < Hq; ++hh) {
+          const int64_t g = hh / rep;
+          attend(qr + t * QD + hh * D, kl + g * max_seq * D, vl + g * max_seq * D,
+                 (int)(p0 + t + 1), (int)D, att + t * QD + hh * D);
+        }
+      lin16(att, (const int8_t*)P[L_O_Q], (const float*)P[L_O_S], T, QD, H, dl);
+      orc_rmsnorm(dl, h, h, (const uint16_t*)P[L_POST], x1, T, H, c->eps);
+      lin16(x1, (const int8_t*)P[L_GU_Q], (const float*)P[L_GU_S], T, H, 2 * I, gu);
+      for (int64_t t = 0; t < T; ++t)
+        for (int64_t i = 0; i < I; ++i) {
+          const float g = h2f(gu[t * 2 * I + i]), u = h2f(gu[t * 2 * I + I + i]);
+          const float s = hr(g / (1.0f + expf(-g)));
+          mid[t * I + i] = f2h(s * u);
+        }
+      lin16(mid, (const int8_t*)P[L_DN_Q], (const float*)P[L_DN_S], T, I, H, dl);
+      for (int64_t i = 0; i < T * H; ++i) h[i] = f2h(h2f(h[i]) + h2f(dl[i]));
+    }
+    /* head on the last position */
+    orc_rmsnorm(h + (T - 1) * H, NULL, NULL, final_norm, x1, 1, H, c->eps);
+    lin16(x1, head_q, head_s, 1, H, V, logits);
+    float best = -INFINITY, second = -INFINITY;
+    int32_t bi = 0;
+    for (int64_t v = 0; v < V; ++v) {
+      const float lv = h2f(logits[v]);
+      if (lv > best) { second = best; best = lv; bi = (int32_t)v; }
+      else if (lv > second) second = lv;
+    }
+    out_tokens[step] = bi;
+    if (margins) margins[step] = best - second;
+    toks[p0 + T] = bi;
+    p0 += T;
+    T = 1;
+  }
+  free(kc); free(vc); free(cos_t); free(sin_t); free(h); free(x1); free(qkv); free(qr);
+  free(att); free(dl); free(gu); free(mid); free(logits); free(toks);
+  return 0;
+}

@@ -164,12 +164,32 @@ def max_over_ranks(v: float, world: int) -> float:
 
 
 # ------------------------------------------------------------------ workloads (GPU)
+def build_copy_graphs(wl):
+    """One CUDA graph per weight copy, captured on a side stream that was warmed
+    first (kernel attributes, the tensor-map entry point, that stream's linear
+    workspace), so the graphs hold the kernels only."""
+    torch = wl.torch
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for li in range(wl.copies):
+            wl.run_copy(li)
+    torch.cuda.synchronize()
+    wl.graphs = []
+    for li in range(wl.copies):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            wl.run_copy(li)
+        wl.graphs.append(gr)
+    torch.cuda.synchronize()
+
+
 class W8A16Gemv:
     """one W8A16 decode linear per step."""
     metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "int8 x f16"
-    kernel = "w8a16_skinny_kernel<NT=1>"
+    kernel = "w8a16_tma_kernel<NT=1>"
     M, N, K = 1, 12288, 4096
-    graph = False
+    graph = True
 
     def __init__(self, torch, D):
         self.torch = torch
@@ -197,15 +217,21 @@ class W8A16Gemv:
     def bytes(cls):
         return cls.N * cls.K + 2 * cls.N + 2 * cls.M * cls.K + 2 * cls.M * cls.N
 
+    def run_copy(self, li):
+        self.lins[li].forward(self.x, out=self.y)
+
+    def build_graphs(self):
+        build_copy_graphs(self)
+
     def step(self):
-        lin = self.lins[self.i % self.copies]
+        self.graphs[self.i % self.copies].replay()
         self.i += 1
-        lin.forward(self.x, out=self.y)
 
     def step_e2e(self):
         """Through the public API with host buffers: H2D x, linear, D2H y."""
         self.x.copy_(self.h_x, non_blocking=True)
-        self.step()
+        self.lins[self.i % self.copies].forward(self.x, out=self.y)
+        self.i += 1
         self.h_y.copy_(self.y, non_blocking=True)
         return self.h_x.numel() * 2, self.h_y.numel() * 2
 
@@ -213,7 +239,7 @@ class W8A16Gemv:
 class GgufSweep:
     """BASELINE config 2 (decode points): 7 shapes x {Q4_0, Q8_0} x M in {1, 8}."""
     metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "q4_0/q8_0 x f32"
-    kernel = "gguf_skinny_kernel + q8_0_act_quantize_kernel (whole sweep)"
+    kernel = "gguf_tma_kernel + q8_0_act_quantize_kernel (whole sweep)"
     ms = (1, 8)
     graph = True
 
@@ -264,17 +290,7 @@ class GgufSweep:
                 lin.forward(x, out=y)
 
     def build_graphs(self):
-        torch = self.torch
-        self.graphs = []
-        for li in range(self.copies):
-            self.run_copy(li)  # warm (attributes, tensor-map entry point)
-        torch.cuda.synchronize()
-        for li in range(self.copies):
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr):
-                self.run_copy(li)
-            self.graphs.append(gr)
-        torch.cuda.synchronize()
+        build_copy_graphs(self)
 
     def step(self):
         self.graphs[self.i % self.copies].replay()
@@ -298,7 +314,146 @@ class GgufPrefill(GgufSweep):
         return sum(2 * m * N * K for m in cls.ms for _ in GGUF_BLOCK_BYTES for _, N, K in LAYER_SHAPES)
 
 
-WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep, "gguf_prefill": GgufPrefill}
+class QwenDecode:
+    """BASELINE configs 3/4: Qwen3-8B-shaped W8A16 decoder (36 layers, hidden 4096,
+    MLP 12288, 32/8 heads, vocab 151936, random init N(0, 0.02)), 8 sequences,
+    1024-token prompts (prefilled before timing), decode as micro-batches of 1.
+    A step advances every sequence by one greedy token.  Metric: decode tok/s."""
+    metric, unit, bound, dtype = "8B W8A16 decode tok/s", "tok/s", "hbm", "int8 x bf16"
+    kernel = "w8a16_tma_kernel<NT=1> (the token's 145 linears from one graph, events)"
+    graph = True
+    n_seqs, prompt_len, decode_cap = 8, 1024, 256
+    copies_per_step = 8  # one graph per sequence
+
+    def __init__(self, torch, D):
+        from dial_cuda.model import ModelConfig, Stage
+        self.torch, self.D = torch, D
+        self.cfg = ModelConfig(act_dtype="bf16")
+        self.max_seq = self.prompt_len + self.decode_cap + 16
+        self.stage = Stage(self.cfg, 0, self.cfg.n_layers, n_slots=self.n_seqs, max_seq=self.max_seq)
+        st = self.stage
+        dev = st.device
+        g = torch.Generator(device="cuda").manual_seed(SEED)
+        self.ids = torch.zeros(self.n_seqs, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(self.n_seqs, dtype=torch.int32, device=dev)
+        self.slots = torch.arange(self.n_seqs, dtype=torch.int32, device=dev)
+        self.hidden = [torch.empty((1, self.cfg.hidden), device=dev, dtype=st.dt) for _ in range(self.n_seqs)]
+        # prefill every sequence (untimed: the metric is decode throughput)
+        t0 = time.perf_counter()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for b in range(self.n_seqs):
+            prompt = torch.randint(0, self.cfg.vocab, (self.prompt_len,), generator=g, device=dev,
+                                   dtype=torch.int32)
+            h = torch.empty((self.prompt_len, self.cfg.hidden), device=dev, dtype=st.dt)
+            st.embed_tokens(prompt, h)
+            st.layers_forward(h, torch.arange(self.prompt_len, dtype=torch.int32, device=dev),
+                              torch.full((self.prompt_len,), b, dtype=torch.int32, device=dev),
+                              self.prompt_len)
+            st.head_forward(h, self.ids[b:b + 1],
+                            row_index=torch.tensor([self.prompt_len - 1], dtype=torch.int32, device=dev))
+        ev1.record()
+        torch.cuda.synchronize()
+        self.prefill_ms = ev0.elapsed_time(ev1) / self.n_seqs
+        self.pos.fill_(self.prompt_len)
+        self.work_per_step = self.n_seqs  # tokens
+        self.weight_bytes = st.weight_bytes
+        self.h_ids = torch.empty(self.n_seqs, dtype=torch.int32).pin_memory()
+        self.h_out = torch.empty(self.n_seqs, dtype=torch.int32).pin_memory()
+        self.steps_done = 0
+        self.config = {"workload": "qwen3_8b_w8a16_decode", "model": "Qwen3-8B-shaped, random init",
+                       "layers": 36, "hidden": 4096, "intermediate": 12288, "heads": "32/8",
+                       "vocab": 151936, "sequences": self.n_seqs, "micro_batch": 1,
+                       "prompt_len": self.prompt_len, "activation": "bf16", "kv_cache": "bf16",
+                       "weights_GB": round(self.weight_bytes / 1e9, 3),
+                       "prefill_ms_per_seq": round(self.prefill_ms, 2),
+                       "l2": "7.6 GB of weights per token >> 126 MB L2",
+                       "launch": "one CUDA graph per sequence slot"}
+
+    def one_token(self, b: int):
+        st = self.stage
+        st.embed_tokens(self.ids[b:b + 1], self.hidden[b])
+        st.layers_forward(self.hidden[b], self.pos[b:b + 1], self.slots[b:b + 1], self.max_seq)
+        st.head_forward(self.hidden[b], self.ids[b:b + 1])
+        self.pos[b:b + 1].add_(1)
+
+    def run_copy(self, _):
+        self.one_token(0)
+        self.pos[0:1].sub_(1)  # the counting pass must not advance the sequence
+
+    def build_graphs(self):
+        torch = self.torch
+        self.graphs = []
+        for b in range(self.n_seqs):
+            self.one_token(b)  # warm (workspace, attributes) outside capture
+        torch.cuda.synchronize()
+        self.pos.sub_(1)
+        for b in range(self.n_seqs):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):  # capture records the work without running it
+                self.one_token(b)
+            self.graphs.append(gr)
+        torch.cuda.synchronize()
+
+    def step(self):
+        if self.steps_done >= self.decode_cap - 1:
+            self.pos.fill_(self.prompt_len)  # wrap: keep the KV window inside its capacity
+            self.steps_done = 0
+        for gr in self.graphs:
+            gr.replay()
+        self.steps_done += 1
+
+    def step_e2e(self):
+        """Public-API loop: the host sends each sequence's token, receives the next."""
+        self.ids.copy_(self.h_ids, non_blocking=True)
+        self.step()
+        self.h_out.copy_(self.ids, non_blocking=True)
+        return self.h_ids.numel() * 4, self.h_out.numel() * 4
+
+    def kernel_roofline(self, reps: int = 5):
+        """HBM GB/s of the dominant kernel: the token's linears (36 x {qkv, o,
+        gate_up, down} + lm_head, M = 1) launched back to back in model order
+        from one CUDA graph, algorithmic bytes over the replay's event time."""
+        torch, st = self.torch, self.stage
+        from dial_cuda.model import WFMT_W8A16
+        lins = st.linears + ([st.head] if st.head is not None else [])
+        assert lins[0].fmt == WFMT_W8A16
+        xs, ys = {}, []
+        for lin in lins:
+            wl = lin.lin
+            if wl.in_dim not in xs:
+                xs[wl.in_dim] = torch.randn((1, wl.in_dim), device="cuda").to(st.dt)
+            ys.append(torch.empty((1, wl.out_dim), device="cuda", dtype=st.dt))
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+
+        def run():
+            for lin, y in zip(lins, ys):
+                lin.lin.forward(xs[lin.lin.in_dim], out=y)
+
+        with torch.cuda.stream(side):
+            run()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            run()
+        gr.replay()
+        torch.cuda.synchronize()
+        total_b = sum(l.lin.weight_bytes + 2 * l.lin.in_dim + 2 * l.lin.out_dim for l in lins)
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            gr.replay()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        del gr
+        return total_b / (statistics.median(ts) / 1e3) / 1e9
+
+
+WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep, "gguf_prefill": GgufPrefill,
+             "qwen3_decode": QwenDecode}
 
 
 # ------------------------------------------------------------------ workloads (CPU oracle)
@@ -342,7 +497,63 @@ class CpuWorkload:
         return done
 
 
+def cpu_decode_measure(budget_s):
+    """Qwen3-8B decode on the C oracle (the CPU restatement of the reference's
+    layer + head path): 1- and 2-layer models with the full dims time the cost of
+    a layer and of embed + head; a 36-layer token is extrapolated from them."""
+    import numpy as np
+
+    import oracle as O
+    rng = np.random.default_rng(SEED)
+    H, I, V, Dh, Hq, Hkv = 4096, 12288, 151936, 128, 32, 8
+    QKV = (Hq + 2 * Hkv) * Dh
+
+    # the cost depends on the shapes only: int8 weights and scales are drawn directly
+    def q8(shape):
+        return (rng.integers(-127, 128, shape, dtype=np.int8),
+                np.full(shape[0], 0.02 * 3.5 / 127, np.float32))
+
+    def layer():
+        L = {}
+        for key, shape in (("qkv", (QKV, H)), ("o", (H, Hq * Dh)), ("gu", (2 * I, H)),
+                           ("down", (H, I))):
+            L[f"{key}_q"], L[f"{key}_s"] = q8(shape)
+        for n, dim in (("input_norm", H), ("post_norm", H), ("q_norm", Dh), ("k_norm", Dh)):
+            L[n] = np.ones(dim, np.float16)
+        return L
+
+    layers = [layer(), layer()]
+    embed = (rng.random((V, H), dtype=np.float32) * 0.04 - 0.02).astype(np.float16)
+    hq, hs = q8((V, H))
+    norm = np.ones(H, np.float16)
+    cfg = dict(n_layers=1, hidden=H, inter=I, n_heads=Hq, n_kv=Hkv, head_dim=Dh, vocab=V,
+               qk_norm=True, eps=1e-6, theta=1e6)
+    prompt = np.array([1], np.int32)
+
+    def per_token(nl, n_new):
+        c = dict(cfg, n_layers=nl)
+        t0 = time.perf_counter()
+        O.decoder_generate(c, layers[:nl], embed, norm, hq, hs, prompt, n_new)
+        return (time.perf_counter() - t0) / n_new
+
+    per_token(1, 1)  # warm-up
+    n_new, t1, t2 = 2, [], []
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or not t1:
+        t1.append(per_token(1, n_new))
+        t2.append(per_token(2, n_new))
+    a, b = statistics.median(t1), statistics.median(t2)
+    t_layer = max(b - a, 1e-9)
+    t_tok = (a - t_layer) + 36 * t_layer
+    sample = (f"{len(t1)} x ({n_new} tokens on 1-layer and 2-layer Qwen3-8B-dim oracle models, "
+              f"f16 activations); token = embed/head {1e3 * (a - t_layer):.1f} ms + 36 x layer "
+              f"{1e3 * t_layer:.1f} ms")
+    return 1.0 / t_tok, t_tok, O.num_threads(), sample
+
+
 def cpu_measure(name, budget_s):
+    if name == "qwen3_decode":
+        return cpu_decode_measure(budget_s)
     cw = CpuWorkload(name)
     frac = 1.0 if name != "gguf_prefill" else 16 / 512  # 16 of the 512 rows per sample
     cw.step(frac)  # warm-up
@@ -360,7 +571,7 @@ def cpu_measure(name, budget_s):
 
 
 def unit_scale(unit):
-    return 1e9 if unit == "GB/s" else 1e12
+    return {"GB/s": 1e9, "TFLOP/s": 1e12}.get(unit, 1.0)
 
 
 def run_reference(args, rank, world):
@@ -375,7 +586,10 @@ def run_reference(args, rank, world):
         rate, _, threads, sample = cpu_measure(args.workload, per_step)
         rates.append(rate)
     value = statistics.median(rates) / unit_scale(wl.unit)
-    work = wl.bytes() if wl.unit == "GB/s" else wl.flops()
+    if wl.unit == "tok/s":
+        work = wl.n_seqs  # tokens per step
+    else:
+        work = wl.bytes() if wl.unit == "GB/s" else wl.flops()
     line = {
         "impl": "reference", "metric": wl.metric, "value": round(value, 4), "unit": wl.unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -407,7 +621,7 @@ def run_ours(args, rank, local, world):
     else:
         wl.step()
     torch.cuda.synchronize()
-    launches_per_step = D.launch_count() - c0
+    launches_per_step = (D.launch_count() - c0) * getattr(wl, "copies_per_step", 1)
     if wl.graph:
         wl.build_graphs()
     for _ in range(max(args.warmup, 3)):
@@ -457,7 +671,13 @@ def run_ours(args, rank, local, world):
     pk, peak_src = peaks()
     value = wl.work_per_step * world * args.steps / (total_ms / 1e3) / unit_scale(wl.unit)
     # roofline of the dominant kernel: algorithmic work per step / mean step time
-    achieved = wl.work_per_step / (statistics.mean(step_ms) / 1e3) / unit_scale(wl.unit)
+    # (for the whole-model decode: the linears' bytes over their per-launch times)
+    if hasattr(wl, "kernel_roofline"):
+        achieved = wl.kernel_roofline()
+        wl.config["step_weight_GBps"] = round(
+            wl.weight_bytes * wl.work_per_step / (statistics.mean(step_ms) / 1e3) / 1e9, 1)
+    else:
+        achieved = wl.work_per_step / (statistics.mean(step_ms) / 1e3) / unit_scale(wl.unit)
     if wl.bound == "hbm":
         peak = pk["hbm_gbs"]
     else:

@@ -61,9 +61,14 @@ dial_status dial_w8a16_dequantize(const int8_t* q, const void* scale, dial_dtype
   return launch_w8a16_dequantize(q, scale, sdt, N, K, w, wdt, as_stream(stream));
 }
 
+size_t dial_w8a16_linear_workspace_bytes(int64_t N) {
+  if (N <= 0) return 0;
+  return gemv_workspace_bytes(N);
+}
+
 dial_status dial_w8a16_linear(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
                               dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
-                              dial_stream stream) {
+                              void* workspace, size_t workspace_bytes, dial_stream stream) {
   clear_error();
   if (!x || !q || !scale || !y) return fail(DIAL_ERR_INVALID_ARG, "null pointer");
   dial_status s = check_dims(M, K, N);
@@ -76,6 +81,11 @@ dial_status dial_w8a16_linear(const void* x, dial_dtype xdt, const int8_t* q, co
   if (K % 16) return fail(DIAL_ERR_SHAPE, "W8A16 needs K %% 16 == 0 (K=%lld)", (long long)K);
   if (!aligned16(x) || !aligned16(q))
     return fail(DIAL_ERR_MISALIGNED, "x and q must be 16-byte aligned");
+  if (workspace) {
+    const size_t need = dial_w8a16_linear_workspace_bytes(N);
+    if (workspace_bytes < need || !aligned16(workspace))
+      return fail(DIAL_ERR_INVALID_ARG, "workspace must be 16-byte aligned and hold %zu bytes", need);
+  }
   cudaStream_t st = as_stream(stream);
   if (M > kSkinnyMaxM && gemm_sm100_supported(M, K, N))
     return launch_w8a16_gemm_sm100(x, xdt, q, scale, sdt, y, M, K, N, st);
@@ -84,7 +94,7 @@ dial_status dial_w8a16_linear(const void* x, dial_dtype xdt, const int8_t* q, co
   for (int64_t m0 = 0; m0 < M; m0 += kSkinnyMaxM) {
     const int64_t mc = std::min<int64_t>(kSkinnyMaxM, M - m0);
     s = launch_w8a16_skinny(static_cast<const uint16_t*>(x) + m0 * K, xdt, q, scale, sdt,
-                            static_cast<uint16_t*>(y) + m0 * N, mc, K, N, st);
+                            static_cast<uint16_t*>(y) + m0 * N, mc, K, N, st, workspace);
     if (s != DIAL_OK) return s;
   }
   return DIAL_OK;
@@ -136,14 +146,14 @@ dial_status dial_gguf_dequantize(const void* qs, const uint16_t* d, dial_ggml_ty
   return launch_gguf_dequantize(qs, d, type, N, K, w, wdt, as_stream(stream));
 }
 
-size_t dial_gguf_linear_workspace_bytes(int64_t M, int64_t K) {
-  if (M <= 0 || K <= 0) return 0;
-  size_t b = 0;
-  for (int64_t m0 = 0; m0 < M; m0 += kSkinnyMaxM) {
-    b = std::max(b, gguf_skinny_workspace_bytes(std::min<int64_t>(kSkinnyMaxM, M - m0), K));
-    if (M > kSkinnyMaxM) break;
-  }
-  return std::max(b, gemm_sm100_gguf_workspace_bytes(M, K));
+// [stream-K scratch (fixed size for N)][Q8_0 activations of one <=32-row pass,
+// or the tcgen05 path's f16 copy of f32 activations].  The stream-K counters
+// sit at a fixed place, so one workspace serves calls with any M.
+size_t dial_gguf_linear_workspace_bytes(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t act = std::max(gguf_skinny_workspace_bytes(std::min<int64_t>(kSkinnyMaxM, M), K),
+                              gemm_sm100_gguf_workspace_bytes(M, K));
+  return gemv_workspace_bytes(N) + act;
 }
 
 dial_status dial_gguf_linear(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,
@@ -159,17 +169,19 @@ dial_status dial_gguf_linear(const void* x, dial_dtype xdt, const void* qs, cons
   if (K % kQK) return fail(DIAL_ERR_SHAPE, "GGUF needs K %% 32 == 0 (K=%lld)", (long long)K);
   if (!aligned16(qs) || !aligned16(d) || !aligned16(x))
     return fail(DIAL_ERR_MISALIGNED, "x, qs and d must be 16-byte aligned");
-  const size_t need = dial_gguf_linear_workspace_bytes(M, K);
+  const size_t need = dial_gguf_linear_workspace_bytes(M, K, N);
   if (need && (!workspace || workspace_bytes < need || !aligned16(workspace)))
     return fail(DIAL_ERR_INVALID_ARG, "workspace must be 16-byte aligned and hold %zu bytes", need);
   cudaStream_t st = as_stream(stream);
+  void* sk = workspace;
+  void* act = static_cast<uint8_t*>(workspace) + gemv_workspace_bytes(N);
   if (M > kSkinnyMaxM && gemm_sm100_supported(M, K, N))
-    return launch_gguf_gemm_sm100(x, xdt, qs, d, type, y, M, K, N, workspace, st);
+    return launch_gguf_gemm_sm100(x, xdt, qs, d, type, y, M, K, N, act, st);
   const size_t xsz = xdt == DIAL_F32 ? 4 : 2;
   for (int64_t m0 = 0; m0 < M; m0 += kSkinnyMaxM) {
     const int64_t mc = std::min<int64_t>(kSkinnyMaxM, M - m0);
     s = launch_gguf_skinny(static_cast<const uint8_t*>(x) + m0 * K * xsz, xdt, qs, d, type,
-                           static_cast<uint8_t*>(y) + m0 * N * xsz, mc, K, N, workspace, st);
+                           static_cast<uint8_t*>(y) + m0 * N * xsz, mc, K, N, act, st, sk);
     if (s != DIAL_OK) return s;
   }
   return DIAL_OK;
@@ -186,7 +198,7 @@ size_t dial_gguf_qs_bytes(dial_ggml_type type, int64_t N, int64_t K) {
 
 size_t dial_gguf_d_bytes(int64_t N, int64_t K) {
   if (N <= 0 || K <= 0) return 0;
-  return (size_t)N * (size_t)gguf_groups(K) * kBlocksPerGroup * sizeof(uint16_t);
+  return (size_t)gguf_d_elems(N, K) * sizeof(uint16_t);  // rows padded to a multiple of 16
 }
 
 }  // extern "C"

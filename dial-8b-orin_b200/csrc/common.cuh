@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "dial_cuda.h"
@@ -31,6 +32,64 @@ inline cudaStream_t as_stream(dial_stream s) { return reinterpret_cast<cudaStrea
 
 // Number of SMs of the current device (cached per device ordinal).
 int sm_count();
+
+// Raises KERN's dynamic shared-memory limit to `bytes` once per device (the
+// attribute belongs to the device's context, so every device needs its own call).
+template <auto KERN>
+cudaError_t ensure_smem(int bytes) {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(KERN, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
+
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: the decode-chain kernels are launched with
+// programmatic stream serialization, so a kernel's CTAs may be scheduled while
+// its predecessor in the stream is still running.  Every such kernel calls
+// pdl_trigger() (let the next kernel be scheduled) and pdl_wait() (block until
+// the predecessor grid has completed and its memory is visible) before it
+// touches any global data another kernel writes, and before any early return,
+// so completion stays transitive along the stream.  Work that reads only
+// constant data (weights) may run between the two.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_begin() {
+  pdl_trigger();
+  pdl_wait();
+}
+
+// DIAL_PDL=0 in the environment turns the attribute off (kernels then start
+// only after their predecessor ends; pdl_wait() returns at once).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+dial_status launch_pdl(const char* name, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return cuda_fail(e, name);
+  }
+  return check_launch(name);
+}
 
 // ---------------------------------------------------------------- device side
 template <typename T>

@@ -25,6 +25,7 @@ namespace {
 size_t al256(size_t b) { return (b + 255) / 256 * 256; }
 
 struct Ws {
+  uint8_t* sk;      // stream-K scratch shared by every linear (zero counters between calls)
   uint8_t* x1;      // [T, H]
   uint8_t* qkv;     // [T, (Hq+2Hkv)D]
   uint8_t* q;       // [T, Hq D]
@@ -49,6 +50,8 @@ Ws layout(const dial_decoder_dims& d, int64_t T, int64_t max_len, uint8_t* base)
     off += al256(bytes);
     return p;
   };
+  const int64_t nmax = std::max<int64_t>(std::max<int64_t>(QKV, 2 * I), std::max<int64_t>(H, d.vocab));
+  w.sk = take(gemv_workspace_bytes(nmax));  // first, so its place does not depend on T
   w.x1 = take(T * H * e);
   w.qkv = take(T * QKV * e);
   w.q = take(T * QD * e);
@@ -67,7 +70,7 @@ Ws layout(const dial_decoder_dims& d, int64_t T, int64_t max_len, uint8_t* base)
 
 // One quantised linear y[T, N] = x[T, K] W^T in the stage's weight format.
 dial_status linear(const dial_decoder_dims& d, int fmt, dial_linear_ref W, const void* x, void* y,
-                   int64_t T, int64_t K, int64_t N, void* lin_ws, cudaStream_t st) {
+                   int64_t T, int64_t K, int64_t N, void* lin_ws, void* sk_ws, cudaStream_t st) {
   const dial_dtype xdt = (dial_dtype)d.act_dtype;
   if (fmt == DIAL_WFMT_W8A16 || fmt == DIAL_WFMT_W8A16_F16S) {
     const dial_dtype sdt = fmt == DIAL_WFMT_W8A16 ? DIAL_F32 : DIAL_F16;
@@ -78,7 +81,7 @@ dial_status linear(const dial_decoder_dims& d, int fmt, dial_linear_ref W, const
       const int64_t mc = std::min<int64_t>(kSkinnyMaxM, T - m0);
       dial_status s = launch_w8a16_skinny(static_cast<const uint16_t*>(x) + m0 * K, xdt,
                                           static_cast<const int8_t*>(W.w), W.s, sdt,
-                                          static_cast<uint16_t*>(y) + m0 * N, mc, K, N, st);
+                                          static_cast<uint16_t*>(y) + m0 * N, mc, K, N, st, sk_ws);
       if (s != DIAL_OK) return s;
     }
     return DIAL_OK;
@@ -91,7 +94,7 @@ dial_status linear(const dial_decoder_dims& d, int fmt, dial_linear_ref W, const
     const int64_t mc = std::min<int64_t>(kSkinnyMaxM, T - m0);
     dial_status s = launch_gguf_skinny(static_cast<const uint8_t*>(x) + m0 * K * e, xdt, W.w, dd,
                                        fmt, static_cast<uint8_t*>(y) + m0 * N * e, mc, K, N,
-                                       lin_ws, st);
+                                       lin_ws, st, sk_ws);
     if (s != DIAL_OK) return s;
   }
   return DIAL_OK;
@@ -158,7 +161,7 @@ dial_status dial_decoder_layers(const dial_decoder_dims* dims, const dial_layer_
     if (li == 0) s = launch_rmsnorm(hidden, nullptr, nullptr, L.input_norm, w.x1, dt, T, H, d.rms_eps, st);
     else s = launch_rmsnorm(w.delta, hidden, hidden, L.input_norm, w.x1, dt, T, H, d.rms_eps, st);
     if (s != DIAL_OK) return s;
-    if ((s = linear(d, d.weight_format, L.qkv, w.x1, w.qkv, T, H, QKV, w.lin_ws, st)) != DIAL_OK) return s;
+    if ((s = linear(d, d.weight_format, L.qkv, w.x1, w.qkv, T, H, QKV, w.lin_ws, w.sk, st)) != DIAL_OK) return s;
     if ((s = launch_qk_rope_kv(w.qkv, L.q_norm, L.k_norm, cos_t, sin_t, positions, slots, w.q,
                                L.k_cache, L.v_cache, dt, T, d.n_heads, d.n_kv_heads, d.max_seq,
                                d.rms_eps, d.qk_norm, st)) != DIAL_OK)
@@ -166,13 +169,13 @@ dial_status dial_decoder_layers(const dial_decoder_dims* dims, const dial_layer_
     if ((s = launch_attention(w.q, L.k_cache, L.v_cache, positions, slots, w.attn, w.attn_ws, dt, T,
                               d.n_heads, d.n_kv_heads, d.max_seq, max_len, st)) != DIAL_OK)
       return s;
-    if ((s = linear(d, d.weight_format, L.o, w.attn, w.delta, T, QD, H, w.lin_ws, st)) != DIAL_OK) return s;
+    if ((s = linear(d, d.weight_format, L.o, w.attn, w.delta, T, QD, H, w.lin_ws, w.sk, st)) != DIAL_OK) return s;
     // h = h + o ; x2 = rms_2(h)
     if ((s = launch_rmsnorm(w.delta, hidden, hidden, L.post_norm, w.x1, dt, T, H, d.rms_eps, st)) != DIAL_OK)
       return s;
-    if ((s = linear(d, d.weight_format, L.gate_up, w.x1, w.gu, T, H, 2 * I, w.lin_ws, st)) != DIAL_OK) return s;
+    if ((s = linear(d, d.weight_format, L.gate_up, w.x1, w.gu, T, H, 2 * I, w.lin_ws, w.sk, st)) != DIAL_OK) return s;
     if ((s = launch_swiglu(w.gu, w.mid, dt, T, I, st)) != DIAL_OK) return s;
-    if ((s = linear(d, d.weight_format, L.down, w.mid, w.delta, T, I, H, w.lin_ws, st)) != DIAL_OK) return s;
+    if ((s = linear(d, d.weight_format, L.down, w.mid, w.delta, T, I, H, w.lin_ws, w.sk, st)) != DIAL_OK) return s;
   }
   return launch_add(hidden, w.delta, dt, T * H, st);  // h = h + d of the last layer
 }
@@ -202,7 +205,7 @@ dial_status dial_decoder_head(const dial_decoder_dims* dims, const void* final_n
   if ((s = launch_rmsnorm(src, nullptr, nullptr, final_norm, w.x1, dt, rows, H, d.rms_eps, st)) != DIAL_OK)
     return s;
   void* lg = logits ? logits : w.logits;
-  if ((s = linear(d, d.head_format, head, w.x1, lg, rows, H, V, w.lin_ws, st)) != DIAL_OK) return s;
+  if ((s = linear(d, d.head_format, head, w.x1, lg, rows, H, V, w.lin_ws, w.sk, st)) != DIAL_OK) return s;
   return launch_argmax(lg, out_ids, dt, rows, V, st);
 }
 

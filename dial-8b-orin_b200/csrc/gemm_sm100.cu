@@ -32,6 +32,7 @@
 #include "gemm_sm100.cuh"
 #include "glue.cuh"
 #include "layout.cuh"
+#include "tma.cuh"
 
 namespace dial {
 
@@ -381,7 +382,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int c = 0; c < GB / 16; ++c) raw[c] = __ldg(reinterpret_cast<const uint4*>(src) + c);
         const uint2 dd =
-            __ldg(reinterpret_cast<const uint2*>(p.gd + (size_t)n * p.G * 4 + (size_t)gi * 4));
+            __ldg(reinterpret_cast<const uint2*>(p.gd + gguf_d_index(n, 4 * gi, p.G)));
         dv[0] = __low2float(bits_h2(dd.x));
         dv[1] = __high2float(bits_h2(dd.x));
         dv[2] = __low2float(bits_h2(dd.y));
@@ -525,6 +526,26 @@ dial_status launch_one(const CUtensorMap& map, const Params& p, cudaStream_t st)
 }
 
 }  // namespace
+
+namespace tma {
+dial_status make_byte_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
+                          int box_bytes, int box_rows, bool swizzle128) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(DIAL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (!aligned16(base) || row_bytes % 16 != 0 || (swizzle128 && box_bytes != 128))
+    return fail(DIAL_ERR_MISALIGNED, "tensor map: base and row pitch must be 16-byte aligned");
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DIAL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DIAL_OK;
+}
+}  // namespace tma
 
 bool gemm_sm100_supported(int64_t M, int64_t K, int64_t N) {
   (void)N;

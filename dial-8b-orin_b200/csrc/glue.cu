@@ -40,12 +40,6 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
 template <int THREADS>
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
@@ -68,6 +62,7 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_kernel(const T* x,  // x/res 
                                                           T* h_out,
                                                           const T* __restrict__ w,
                                                           T* __restrict__ y, int dim, float eps) {
+  pdl_begin();
   extern __shared__ float hbuf[];  // dim floats
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
@@ -100,6 +95,7 @@ __global__ void qk_rope_kv_kernel(const T* __restrict__ qkv, const T* __restrict
                                   const int32_t* __restrict__ slot, T* __restrict__ q_out,
                                   T* __restrict__ kc, T* __restrict__ vc, int64_t tokens, int hq,
                                   int hkv, int64_t max_seq, float eps, int qk_norm) {
+  pdl_begin();
   constexpr int D = 128;
   const int heads = hq + 2 * hkv;
   const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
@@ -147,109 +143,119 @@ __global__ void qk_rope_kv_kernel(const T* __restrict__ qkv, const T* __restrict
 // ------------------------------------------------------------------ attention
 // Query token t attends cache rows 0..pos[t] of slot[t] (decode: one token per
 // sequence; prefill: a run of tokens of one sequence, causal through pos).
-// CTA = (token, kv head, key chunk); the n_rep query heads of the group share
-// every K/V row read.  f32 scores / softmax / accumulation.
-constexpr int kAttnThreads = 128;
-constexpr int kAttnChunk = 512;
-constexpr int kMaxRep = 8;
+// CTA = (token, kv head, key split); 8 warps stream the split's keys (warp w
+// takes keys k0+w, k0+w+8, ...), lanes own 4 of the 128 dims, so every K/V row
+// is one coalesced 256-byte warp load shared by the n_rep query heads of the
+// group.  Each warp keeps an online softmax (running max / sum / output); the
+// 8 warps are merged in shared memory; splits are merged by the combine step.
+// Scores are in the log2 domain (q pre-scaled by log2(e)/sqrt(D)), f32 math.
+constexpr int kAttnWarps = 8;
 
 template <typename T>
-__global__ void __launch_bounds__(kAttnThreads)
+__device__ __forceinline__ void ld4(const T* p, float (&v)[4]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 u = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = u.x, v[1] = u.y, v[2] = u.z, v[3] = u.w;
+  } else {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = Act<T>::to_f32(e[i]);
+  }
+}
+
+template <typename T, int REP>
+__global__ void __launch_bounds__(kAttnWarps * 32)
     attention_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
                      const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
                      T* __restrict__ out, float* __restrict__ part, int hq, int hkv,
-                     int64_t max_seq, int nchunks, float scale) {
+                     int64_t max_seq, int nsplit, float qscale) {
+  pdl_begin();
   constexpr int D = 128;
-  __shared__ float qs[kMaxRep][D];
-  __shared__ float sc[kMaxRep][kAttnChunk];
-  __shared__ float red[32];
+  __shared__ float sm_m[kAttnWarps][REP], sm_l[kAttnWarps][REP];
+  __shared__ float sm_o[kAttnWarps][REP][D];
   const int64_t t = blockIdx.x;
-  const int g = blockIdx.y;
-  const int chunk = blockIdx.z;
-  const int rep = hq / hkv;
+  const int g = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int len = pos[t] + 1;
-  const int k0 = chunk * kAttnChunk;
-  if (k0 >= len) {  // empty chunk: mark so the combine step skips it
-    if (nchunks > 1 && threadIdx.x < rep) {
-      float* pp = part + ((t * hq + g * rep + threadIdx.x) * nchunks + chunk) * (D + 2);
-      pp[0] = -FLT_MAX;
-      pp[1] = 0.f;
-    }
-    return;
-  }
-  const int k1 = min(len, k0 + kAttnChunk);
+  const int per = (len + nsplit - 1) / nsplit;
+  const int k0 = split * per, k1 = min(len, k0 + per);
   const int64_t s = slot[t];
-  for (int i = threadIdx.x; i < rep * D; i += kAttnThreads)
-    qs[i / D][i % D] = ld(q, (t * hq + g * rep) * D + i) * scale;
-  __syncthreads();
-  const T* kbase = kc + (s * hkv + g) * max_seq * D;
-  const T* vbase = vc + (s * hkv + g) * max_seq * D;
-  // scores: one key row per thread and pass
-  for (int j = k0 + threadIdx.x; j < k1; j += kAttnThreads) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kbase + (int64_t)j * D);
-    float acc[kMaxRep];
+  const T* kbase = kc + ((s * hkv + g) * max_seq) * D + 4 * lane;
+  const T* vbase = vc + ((s * hkv + g) * max_seq) * D + 4 * lane;
+  float qv[REP][4];
 #pragma unroll
-    for (int r = 0; r < kMaxRep; ++r) acc[r] = 0.f;
-#pragma unroll 4
-    for (int c = 0; c < D / 8; ++c) {
-      const uint4 u = __ldg(kr + c);
-      const T* e = reinterpret_cast<const T*>(&u);
+  for (int r = 0; r < REP; ++r) {
+    ld4(q + (t * hq + g * REP + r) * D + 4 * lane, qv[r]);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float kv = Act<T>::to_f32(e[i]);
+    for (int i = 0; i < 4; ++i) qv[r][i] *= qscale;
+  }
+  float m[REP], l[REP], o[REP][4];
 #pragma unroll
-        for (int r = 0; r < kMaxRep; ++r)
-          if (r < rep) acc[r] = fmaf(qs[r][c * 8 + i], kv, acc[r]);
+  for (int r = 0; r < REP; ++r) {
+    m[r] = -FLT_MAX;
+    l[r] = 0.f;
+    o[r][0] = o[r][1] = o[r][2] = o[r][3] = 0.f;
+  }
+  constexpr int U = 4;  // keys per iteration (loads issued together)
+  for (int j0 = k0 + warp; j0 < k1; j0 += kAttnWarps * U) {
+    float kv[U][4], vv[U][4];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = min(j0 + u * kAttnWarps, k1 - 1);
+      ld4(kbase + (int64_t)j * D, kv[u]);
+      ld4(vbase + (int64_t)j * D, vv[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (j0 + u * kAttnWarps >= k1) break;
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        const float sc = warp_sum(qv[r][0] * kv[u][0] + qv[r][1] * kv[u][1] + qv[r][2] * kv[u][2] +
+                                  qv[r][3] * kv[u][3]);
+        const float nm = fmaxf(m[r], sc);
+        const float corr = exp2f(m[r] - nm), p = exp2f(sc - nm);
+        l[r] = l[r] * corr + p;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[r][i] = fmaf(p, vv[u][i], o[r][i] * corr);
+        m[r] = nm;
       }
     }
-#pragma unroll
-    for (int r = 0; r < kMaxRep; ++r)
-      if (r < rep) sc[r][j - k0] = acc[r];
   }
-  __syncthreads();
-  // per-head max and exp-sum over the chunk
-  float mx[kMaxRep], sm[kMaxRep];
-  for (int r = 0; r < rep; ++r) {
-    float m = -FLT_MAX;
-    for (int j = threadIdx.x; j < k1 - k0; j += kAttnThreads) m = fmaxf(m, sc[r][j]);
-    m = warp_max(m);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-    __syncthreads();
-    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    __syncthreads();
-    float sum = 0.f;
-    for (int j = threadIdx.x; j < k1 - k0; j += kAttnThreads) {
-      const float e = __expf(sc[r][j] - m);
-      sc[r][j] = e;
-      sum += e;
+  // merge the warps
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    if (lane == 0) {
+      sm_m[warp][r] = m[r];
+      sm_l[warp][r] = l[r];
     }
-    sum = block_sum<kAttnThreads>(sum, red);
-    mx[r] = m;
-    sm[r] = sum;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sm_o[warp][r][4 * lane + i] = o[r][i];
   }
   __syncthreads();
-  // output: thread d accumulates sum_j p[r][j] * V[j][d]
-  const int d = threadIdx.x;  // kAttnThreads == D
-  float o[kMaxRep];
+  for (int idx = threadIdx.x; idx < REP * D; idx += kAttnWarps * 32) {
+    const int r = idx / D, d = idx % D;
+    float M = -FLT_MAX;
 #pragma unroll
-  for (int r = 0; r < kMaxRep; ++r) o[r] = 0.f;
-  for (int j = k0; j < k1; ++j) {
-    const float vv = ld(vbase, (int64_t)j * D + d);
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][r]);
+    float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxRep; ++r)
-      if (r < rep) o[r] = fmaf(sc[r][j - k0], vv, o[r]);
-  }
-  for (int r = 0; r < rep; ++r) {
-    const int64_t head = t * hq + g * rep + r;
-    if (nchunks == 1) {
-      out[head * D + d] = rnd<T>(o[r] / sm[r]);
+    for (int w = 0; w < kAttnWarps; ++w) {
+      if (sm_m[w][r] == -FLT_MAX) continue;  // warp saw no key
+      const float f = exp2f(sm_m[w][r] - M);
+      L += sm_l[w][r] * f;
+      O += sm_o[w][r][d] * f;
+    }
+    const int64_t head = t * hq + g * REP + r;
+    if (nsplit == 1) {
+      out[head * D + d] = rnd<T>(O / L);
     } else {
-      float* pp = part + (head * nchunks + chunk) * (D + 2);
+      float* pp = part + (head * nsplit + split) * (D + 2);
       if (d == 0) {
-        pp[0] = mx[r];
-        pp[1] = sm[r];
+        pp[0] = M;  // -FLT_MAX for an empty split
+        pp[1] = L;
       }
-      pp[2 + d] = o[r];
+      pp[2 + d] = O;
     }
   }
 }
@@ -257,6 +263,7 @@ __global__ void __launch_bounds__(kAttnThreads)
 template <typename T>
 __global__ void attention_combine_kernel(const float* __restrict__ part, T* __restrict__ out,
                                          int nchunks) {
+  pdl_begin();
   constexpr int D = 128;
   const int64_t head = blockIdx.x;
   const int d = threadIdx.x;
@@ -267,7 +274,7 @@ __global__ void attention_combine_kernel(const float* __restrict__ part, T* __re
   for (int c = 0; c < nchunks; ++c) {
     const float cm = pp[c * (D + 2)];
     if (cm == -FLT_MAX) continue;
-    const float f = __expf(cm - m);
+    const float f = exp2f(cm - m);  // partial maxima are in the log2 domain
     sum += pp[c * (D + 2) + 1] * f;
     acc += pp[c * (D + 2) + 2 + d] * f;
   }
@@ -279,6 +286,7 @@ __global__ void attention_combine_kernel(const float* __restrict__ part, T* __re
 template <typename T>
 __global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t tokens,
                               int64_t inter) {
+  pdl_begin();
   const int64_t n = tokens * inter;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -293,6 +301,7 @@ __global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int
 // h = round(h + d), the residual add after the last layer of a stage (text.rs:1672-1674)
 template <typename T>
 __global__ void add_kernel(T* __restrict__ h, const T* __restrict__ d, int64_t n) {
+  pdl_begin();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     h[i] = rnd<T>(ld(h, i) + ld(d, i));
@@ -301,6 +310,7 @@ __global__ void add_kernel(T* __restrict__ h, const T* __restrict__ d, int64_t n
 template <typename T>
 __global__ void gather_rows_kernel(const T* __restrict__ src, const int32_t* __restrict__ idx,
                                    T* __restrict__ dst, int64_t dim) {
+  pdl_begin();
   const int64_t r = blockIdx.x;
   const int64_t s = idx[r];
   for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) dst[r * dim + i] = src[s * dim + i];
@@ -311,6 +321,7 @@ template <typename T>
 __global__ void embedding_kernel(const T* __restrict__ table, const int32_t* __restrict__ ids,
                                  T* __restrict__ out, int64_t tokens, int64_t vocab, int64_t dim,
                                  int* __restrict__ err) {
+  pdl_begin();
   const int64_t t = blockIdx.x;
   const int32_t id = ids[t];
   const bool ok = id >= 0 && id < vocab;
@@ -323,6 +334,7 @@ __global__ void embedding_kernel(const T* __restrict__ table, const int32_t* __r
 template <typename T>
 __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x,
                                                       int32_t* __restrict__ out, int64_t n) {
+  pdl_begin();
   __shared__ float bv[32];
   __shared__ int bi[32];
   const int64_t row = blockIdx.x;
@@ -400,14 +412,15 @@ dial_status launch_rmsnorm(const void* x, const void* res, void* h_out, const vo
                            dial_dtype dt, int64_t rows, int64_t dim, float eps, cudaStream_t st) {
   const size_t smem = (size_t)dim * sizeof(float);
   if (smem > 96 * 1024) return fail(DIAL_ERR_SHAPE, "rmsnorm dim too large (%lld)", (long long)dim);
+  dial_status s = DIAL_OK;
   DISPATCH_T(dt, {
     auto k = rmsnorm_kernel<T, 512>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<(unsigned)rows, 512, smem, st>>>(static_cast<const T*>(x), static_cast<const T*>(res),
-                                         static_cast<T*>(h_out), static_cast<const T*>(w),
-                                         static_cast<T*>(y), (int)dim, eps);
+    s = launch_pdl("rmsnorm_kernel", k, dim3((unsigned)rows), dim3(512), smem, st,
+                   static_cast<const T*>(x), static_cast<const T*>(res), static_cast<T*>(h_out),
+                   static_cast<const T*>(w), static_cast<T*>(y), (int)dim, eps);
   });
-  return check_launch("rmsnorm_kernel");
+  return s;
 }
 
 dial_status launch_qk_rope_kv(const void* qkv, const void* qn, const void* kn, const void* cos_t,
@@ -417,18 +430,27 @@ dial_status launch_qk_rope_kv(const void* qkv, const void* qn, const void* kn, c
                               cudaStream_t st) {
   const int64_t warps = tokens * (hq + 2 * hkv);
   const unsigned grid = (unsigned)((warps * 32 + 255) / 256);
+  dial_status s = DIAL_OK;
   DISPATCH_T(dt, {
-    qk_rope_kv_kernel<T><<<grid, 256, 0, st>>>(
-        static_cast<const T*>(qkv), static_cast<const T*>(qn), static_cast<const T*>(kn),
-        static_cast<const T*>(cos_t), static_cast<const T*>(sin_t), pos, slot,
-        static_cast<T*>(q_out), static_cast<T*>(kc), static_cast<T*>(vc), tokens, hq, hkv,
-        max_seq, eps, qk_norm);
+    s = launch_pdl("qk_rope_kv_kernel", qk_rope_kv_kernel<T>, dim3(grid), dim3(256), 0, st,
+                   static_cast<const T*>(qkv), static_cast<const T*>(qn), static_cast<const T*>(kn),
+                   static_cast<const T*>(cos_t), static_cast<const T*>(sin_t), pos, slot,
+                   static_cast<T*>(q_out), static_cast<T*>(kc), static_cast<T*>(vc), tokens, hq, hkv,
+                   max_seq, eps, qk_norm);
   });
-  return check_launch("qk_rope_kv_kernel");
+  return s;
+}
+
+// Key splits per (token, kv head): enough CTAs for ~2 per SM, at least 64 keys each.
+static int attention_splits(int64_t tokens, int hkv, int64_t max_len) {
+  const int64_t want = (2 * (int64_t)sm_count() + tokens * hkv - 1) / (tokens * hkv);
+  const int64_t cap = (max_len + 63) / 64;
+  return (int)std::max<int64_t>(1, std::min(want, cap));
 }
 
 size_t attention_workspace_bytes(int64_t tokens, int hq, int64_t max_len) {
-  const int64_t nch = (max_len + kAttnChunk - 1) / kAttnChunk;
+  // hkv is not known here: size for the largest split count any hkv >= 1 gives
+  const int64_t nch = attention_splits(tokens, 1, max_len);
   return nch > 1 ? (size_t)(tokens * hq * nch * (128 + 2)) * sizeof(float) : 0;
 }
 
@@ -436,63 +458,84 @@ dial_status launch_attention(const void* q, const void* kc, const void* vc, cons
                              const int32_t* slot, void* out, void* ws, dial_dtype dt,
                              int64_t tokens, int hq, int hkv, int64_t max_seq, int64_t max_len,
                              cudaStream_t st) {
-  const int nch = (int)((max_len + kAttnChunk - 1) / kAttnChunk);
-  const float scale = 1.0f / sqrtf(128.0f);
+  const int nch = attention_splits(tokens, hkv, max_len);
+  const float qscale = 1.4426950408889634f / sqrtf(128.0f);  // log2(e) / sqrt(D)
   dim3 grid((unsigned)tokens, (unsigned)hkv, (unsigned)nch);
+  const int rep = hq / hkv;
+  dial_status s = DIAL_OK;
+#define ATT(REP_)                                                                                \
+  s = launch_pdl("attention_kernel", attention_kernel<T, REP_>, grid, dim3(kAttnWarps * 32), 0, st, \
+                 static_cast<const T*>(q), static_cast<const T*>(kc), static_cast<const T*>(vc),  \
+                 pos, slot, static_cast<T*>(out), static_cast<float*>(ws), hq, hkv, max_seq, nch, \
+                 qscale)
   DISPATCH_T(dt, {
-    attention_kernel<T><<<grid, kAttnThreads, 0, st>>>(
-        static_cast<const T*>(q), static_cast<const T*>(kc), static_cast<const T*>(vc), pos, slot,
-        static_cast<T*>(out), static_cast<float*>(ws), hq, hkv, max_seq, nch, scale);
+    switch (rep) {
+      case 1: ATT(1); break;
+      case 2: ATT(2); break;
+      case 4: ATT(4); break;
+      case 8: ATT(8); break;
+      default: return fail(DIAL_ERR_SHAPE, "attention supports Hq/Hkv in {1,2,4,8}");
+    }
   });
-  dial_status s = check_launch("attention_kernel");
+#undef ATT
   if (s != DIAL_OK || nch == 1) return s;
   DISPATCH_T(dt, {
-    attention_combine_kernel<T><<<(unsigned)(tokens * hq), 128, 0, st>>>(
-        static_cast<const float*>(ws), static_cast<T*>(out), nch);
+    s = launch_pdl("attention_combine_kernel", attention_combine_kernel<T>,
+                   dim3((unsigned)(tokens * hq)), dim3(128), 0, st, static_cast<const float*>(ws),
+                   static_cast<T*>(out), nch);
   });
-  return check_launch("attention_combine_kernel");
+  return s;
 }
 
 dial_status launch_swiglu(const void* gu, void* out, dial_dtype dt, int64_t tokens, int64_t inter,
                           cudaStream_t st) {
+  dial_status s = DIAL_OK;
   DISPATCH_T(dt, {
-    swiglu_kernel<T><<<grid_cap(tokens * inter, 256), 256, 0, st>>>(
-        static_cast<const T*>(gu), static_cast<T*>(out), tokens, inter);
+    s = launch_pdl("swiglu_kernel", swiglu_kernel<T>, dim3(grid_cap(tokens * inter, 256)), dim3(256),
+                   0, st, static_cast<const T*>(gu), static_cast<T*>(out), tokens, inter);
   });
-  return check_launch("swiglu_kernel");
+  return s;
 }
 
 dial_status launch_gather_rows(const void* src, const int32_t* idx, void* dst, dial_dtype dt,
                                int64_t rows, int64_t dim, cudaStream_t st) {
+  dial_status s = DIAL_OK;
   DISPATCH_T(dt, {
-    gather_rows_kernel<T><<<(unsigned)rows, 256, 0, st>>>(static_cast<const T*>(src), idx,
-                                                          static_cast<T*>(dst), dim);
+    s = launch_pdl("gather_rows_kernel", gather_rows_kernel<T>, dim3((unsigned)rows), dim3(256), 0,
+                   st, static_cast<const T*>(src), idx, static_cast<T*>(dst), dim);
   });
-  return check_launch("gather_rows_kernel");
+  return s;
 }
 
 dial_status launch_add(void* h, const void* d, dial_dtype dt, int64_t n, cudaStream_t st) {
+  dial_status s = DIAL_OK;
   DISPATCH_T(dt, {
-    add_kernel<T><<<grid_cap(n, 256), 256, 0, st>>>(static_cast<T*>(h), static_cast<const T*>(d), n);
+    s = launch_pdl("add_kernel", add_kernel<T>, dim3(grid_cap(n, 256)), dim3(256), 0, st,
+                   static_cast<T*>(h), static_cast<const T*>(d), n);
   });
-  return check_launch("add_kernel");
+  return s;
 }
 
 dial_status launch_embedding(const void* table, const int32_t* ids, void* out, dial_dtype dt,
                              int64_t tokens, int64_t vocab, int64_t dim, cudaStream_t st) {
   int* err = device_error_ptr();
   if (!err) return fail(DIAL_ERR_CUDA, "device error flag unavailable");
+  dial_status s = DIAL_OK;
   DISPATCH_T(dt, {
-    embedding_kernel<T><<<(unsigned)tokens, 256, 0, st>>>(
-        static_cast<const T*>(table), ids, static_cast<T*>(out), tokens, vocab, dim, err);
+    s = launch_pdl("embedding_kernel", embedding_kernel<T>, dim3((unsigned)tokens), dim3(256), 0, st,
+                   static_cast<const T*>(table), ids, static_cast<T*>(out), tokens, vocab, dim, err);
   });
-  return check_launch("embedding_kernel");
+  return s;
 }
 
 dial_status launch_argmax(const void* x, int32_t* out, dial_dtype dt, int64_t rows, int64_t n,
                           cudaStream_t st) {
-  DISPATCH_T(dt, { argmax_kernel<T><<<(unsigned)rows, 1024, 0, st>>>(static_cast<const T*>(x), out, n); });
-  return check_launch("argmax_kernel");
+  dial_status s = DIAL_OK;
+  DISPATCH_T(dt, {
+    s = launch_pdl("argmax_kernel", argmax_kernel<T>, dim3((unsigned)rows), dim3(1024), 0, st,
+                   static_cast<const T*>(x), out, n);
+  });
+  return s;
 }
 
 dial_status launch_rope_tables(void* cos_t, void* sin_t, dial_dtype dt, int64_t max_pos,

@@ -5,8 +5,10 @@
 // (element j in the low nibble of qs[j], element j+16 in the high nibble),
 // Q8_0 {f16 d; i8 qs[32]}.  dial_gguf_repack splits a row of blocks into
 //
-//   d  : f16 [N, 4*G]        G = ceil(K/128) groups of 4 blocks, padding d = 0
-//   qs : u8  [N, G*GB]       GB = 64 (Q4_0) or 128 (Q8_0) bytes per group
+//   qs : u8  [N, G*GB]       G = ceil(K/128) groups of 4 blocks (padding zero),
+//                            GB = 64 (Q4_0) or 128 (Q8_0) bytes per group
+//   d  : f16 [ceil(N/16), G, 16, 4]  the scales of a 16-row tile and one group
+//                            are 128 contiguous bytes (one bulk copy); padding 0
 //
 // and interleaves the bytes of the 4 blocks of a group so that the 16 (Q4_0)
 // or 32 (Q8_0) contiguous bytes a lane loads with 128-bit loads are exactly
@@ -34,6 +36,15 @@ __host__ __device__ constexpr int group_bytes(int ggml_type) { return ggml_type 
 __host__ __device__ constexpr int native_block_bytes(int ggml_type) { return ggml_type == 2 ? 18 : 34; }
 
 __host__ __device__ inline int64_t gguf_groups(int64_t K) { return (K / kQK + 3) / 4; }
+
+// Element index of the scale of block b (0 .. 4G-1) of row n in the d array.
+__host__ __device__ inline int64_t gguf_d_index(int64_t n, int64_t b, int64_t G) {
+  return (((n >> 4) * G + (b >> 2)) * 16 + (n & 15)) * 4 + (b & 3);
+}
+// Size of the d array in f16 elements.
+__host__ __device__ inline int64_t gguf_d_elems(int64_t N, int64_t K) {
+  return ((N + 15) / 16) * 16 * gguf_groups(K) * 4;
+}
 
 // Byte offset inside a group of qs byte `p` of block `j` (p indexes the
 // native qs array: 0..15 for Q4_0, 0..31 for Q8_0).

@@ -98,7 +98,8 @@ extern "C" dial_status dial_gguf_linear_noalloc(const void* x, dial_dtype xdt, c
   for (int64_t m0 = 0; m0 < M; m0 += kNoAllocRows) {
     const int64_t mc = M - m0 < kNoAllocRows ? M - m0 : kNoAllocRows;
     s = launch_gguf_skinny(static_cast<const uint8_t*>(x) + m0 * K * xsz, xdt, qs, d, type,
-                           static_cast<uint8_t*>(y) + m0 * N * xsz, mc, K, N, scratch, st);
+                           static_cast<uint8_t*>(y) + m0 * N * xsz, mc, K, N, scratch, st,
+                           /*sk_ws=*/nullptr);
     if (s != DIAL_OK) return s;
   }
   return DIAL_OK;

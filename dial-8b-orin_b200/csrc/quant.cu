@@ -78,11 +78,11 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ blocks, int type,
     uint8_t* dst = qs + n * G * gb + g * gb;
     if (b < nb) {
       const uint8_t* src = blocks + (n * nb + b) * bb;
-      d[n * nbp + b] = __ushort_as_half((unsigned short)(src[0] | (src[1] << 8)));
+      d[gguf_d_index(n, b, G)] = __ushort_as_half((unsigned short)(src[0] | (src[1] << 8)));
       for (int p = 0; p < nq; ++p)
         dst[type == DIAL_GGML_Q4_0 ? q4_0_offset(j, p) : q8_0_offset(j, p)] = src[2 + p];
     } else {
-      d[n * nbp + b] = __ushort_as_half(0);
+      d[gguf_d_index(n, b, G)] = __ushort_as_half(0);
       for (int p = 0; p < nq; ++p) dst[type == DIAL_GGML_Q4_0 ? q4_0_offset(j, p) : q8_0_offset(j, p)] = 0;
     }
   }
@@ -91,7 +91,6 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ blocks, int type,
 __global__ void gguf_unpack_kernel(const uint8_t* __restrict__ qs, const __half* __restrict__ d,
                                    int type, int64_t N, int64_t nb, int64_t G,
                                    uint8_t* __restrict__ blocks) {
-  const int64_t nbp = G * kBlocksPerGroup;
   const int64_t total = N * nb;
   const int gb = group_bytes(type), bb = native_block_bytes(type), nq = bb - 2;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -101,7 +100,7 @@ __global__ void gguf_unpack_kernel(const uint8_t* __restrict__ qs, const __half*
     const int j = (int)(b % kBlocksPerGroup);
     const uint8_t* src = qs + n * G * gb + g * gb;
     uint8_t* dst = blocks + i * bb;
-    const unsigned short h = __half_as_ushort(d[n * nbp + b]);
+    const unsigned short h = __half_as_ushort(d[gguf_d_index(n, b, G)]);
     dst[0] = (uint8_t)(h & 0xff);
     dst[1] = (uint8_t)(h >> 8);
     for (int p = 0; p < nq; ++p)
@@ -122,7 +121,7 @@ __global__ void gguf_quantize_kernel(const float* __restrict__ w, int type, int6
     const int j = (int)(b % kBlocksPerGroup);
     uint8_t* dst = qs + n * G * gb + g * gb;
     if (b >= nb) {
-      d[i] = __ushort_as_half(0);
+      d[gguf_d_index(n, b, G)] = __ushort_as_half(0);
       const int nq = type == DIAL_GGML_Q4_0 ? 16 : 32;
       for (int p = 0; p < nq; ++p) dst[type == DIAL_GGML_Q4_0 ? q4_0_offset(j, p) : q8_0_offset(j, p)] = 0;
       continue;
@@ -136,7 +135,7 @@ __global__ void gguf_quantize_kernel(const float* __restrict__ w, int type, int6
       }
       const float dd = __fdiv_rn(maxv, -8.0f);
       const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-      d[i] = __float2half_rn(dd);
+      d[gguf_d_index(n, b, G)] = __float2half_rn(dd);
       for (int p = 0; p < 16; ++p) {
         const float x0 = __fadd_rn(__fmul_rn(x[p], id), 8.5f);
         const float x1 = __fadd_rn(__fmul_rn(x[16 + p], id), 8.5f);
@@ -150,7 +149,7 @@ __global__ void gguf_quantize_kernel(const float* __restrict__ w, int type, int6
       for (int e = 0; e < kQK; ++e) amax = fmaxf(amax, fabsf(x[e]));
       const float dd = __fdiv_rn(amax, 127.0f);
       const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-      d[i] = __float2half_rn(dd);
+      d[gguf_d_index(n, b, G)] = __float2half_rn(dd);
       for (int p = 0; p < 32; ++p) dst[q8_0_offset(j, p)] = (uint8_t)(int8_t)(int)roundf(__fmul_rn(x[p], id));
     }
   }
@@ -160,7 +159,7 @@ template <typename OT>
 __global__ void gguf_dequantize_kernel(const uint8_t* __restrict__ qs, const __half* __restrict__ d,
                                        int type, int64_t N, int64_t K, int64_t G,
                                        OT* __restrict__ out) {
-  const int64_t total = N * K, nbp = G * kBlocksPerGroup;
+  const int64_t total = N * K;
   const int gb = group_bytes(type);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -177,7 +176,7 @@ __global__ void gguf_dequantize_kernel(const uint8_t* __restrict__ qs, const __h
     } else {
       qv = (int8_t)src[q8_0_offset(j, e)];
     }
-    out[i] = Act<OT>::from_f32(__fmul_rn(__half2float(d[n * nbp + b]), (float)qv));
+    out[i] = Act<OT>::from_f32(__fmul_rn(__half2float(d[gguf_d_index(n, b, G)]), (float)qv));
   }
 }
 

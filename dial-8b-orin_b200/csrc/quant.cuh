@@ -18,15 +18,20 @@ dial_status launch_gguf_quantize(const float* w, int type, int64_t N, int64_t K,
 dial_status launch_gguf_dequantize(const void* qs, const uint16_t* d, int type, int64_t N,
                                    int64_t K, void* w, dial_dtype wdt, cudaStream_t st);
 
-// Skinny (small-M) register-dequant tensor-core kernels, skinny.cu.
+// Skinny (small-M) dequant tensor-core kernels, skinny.cu.
 constexpr int kSkinnyMaxM = 32;
+// GEMV scratch (partial-chunk slots, chunk and per-tile counters) for M-row
+// (M <= 32) passes over N output rows, any K.  The counter part must be zero
+// before the first call; every call leaves it zero.  sk_ws == NULL selects the
+// in-CTA K split instead (no scratch).
+size_t gemv_workspace_bytes(int64_t N);
 dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
                                 dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
-                                cudaStream_t st);
+                                cudaStream_t st, void* sk_ws);
 // GGUF integer path: activations quantised to Q8_0 in `ws` first.
 size_t gguf_skinny_workspace_bytes(int64_t M, int64_t K);
 dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,
                                int type, void* y, int64_t M, int64_t K, int64_t N, void* ws,
-                               cudaStream_t st);
+                               cudaStream_t st, void* sk_ws);
 
 }  // namespace dial

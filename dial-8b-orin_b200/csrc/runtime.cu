@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -39,6 +40,14 @@ dial_status check_launch(const char* kernel_name) {
   if (e != cudaSuccess) return cuda_fail(e, kernel_name);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return DIAL_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("DIAL_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 int sm_count() {

@@ -1,12 +1,22 @@
 // Decode / small-M linears (M <= 32): stream the packed weights once with
 // 128-bit loads, dequantise in registers and let the tensor cores do the dot
-// products (mma.sync, f32 or s32 accumulate).  One warp owns a 16-row tile and
-// a slice of K; the K-slices of a tile are reduced through shared memory.
+// products (mma.sync, f32 or s32 accumulate).
 //
 // Reference kernels this replaces:
 //   dial_w8a16_decode_f16   worker_w8a16.rs:146-184 (one block per output and
 //                           per activation row: weights re-read M times)
 //   candle QMatMul forward  worker_gguf.rs:584-605 (rows <= 8, MMVQ)
+//
+// Work unit: a 16-row weight tile x one 128-wide K group.  Two drivers:
+//   stream-K (default, needs a small workspace): every warp of a grid sized to
+//     the SMs takes an equal contiguous range of units, so all warps finish
+//     together whatever N and K are.  A tile split across warps is combined
+//     deterministically: each warp stores its partial tile in its own slot,
+//     bumps the tile's arrival counter, and the warp that completes the count
+//     sums the slots in warp order, writes the output and resets the counter
+//     (no float atomics, no waiting on other warps).
+//   split (no workspace): the K groups of a tile are split over the warps of
+//     one CTA and reduced through shared memory.
 //
 // W8A16 (f16 or bf16 activations): m16n8k16 MMAs.  Each lane loads 16
 // contiguous int8 of weight rows g and g+8 (g = lane/4) per 64-wide K span;
@@ -22,9 +32,13 @@
 // then every 32-wide block is one m16n8k32 s8 MMA (exact integer dot) scaled in
 // f32 by d_w * d_x.  Q4_0 nibbles enter the MMA as 0..15 and the -8 offset is
 // folded in as -8 * sum(x_q) per block.
+#include <algorithm>
+
 #include "common.cuh"
+#include "glue.cuh"
 #include "layout.cuh"
 #include "quant.cuh"
+#include "tma.cuh"
 
 namespace dial {
 
@@ -71,118 +85,101 @@ __device__ __forceinline__ void i8x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t
   hi = *reinterpret_cast<uint32_t*>(&hf);
 }
 
-// Four int8 -> two packed bf16x2, exact: 2^23 + u as f32 bits, minus 2^23 + 128,
-// then packed (integers up to 127 are exact in bf16).
+// Four int8 -> two packed bf16x2, exact.  Each byte b goes into a 16-bit lane
+// under the bf16 exponent of 128: v1 = 128 + (b & 127) (bit 7 cleared), and
+// v2 = -128 when b >= 0 or -256 when b < 0 (bit 7 of b moved into the exponent
+// of -128); v1 + v2 = b, an integer that bf16 holds exactly.
 __device__ __forceinline__ void i8x4_to_bf16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const float m = 8388736.0f;  // 2^23 + 128
-  const float f0 = __uint_as_float(prmt(u, 0x4B000000u, 0x7440u)) - m;
-  const float f1 = __uint_as_float(prmt(u, 0x4B000000u, 0x7441u)) - m;
-  const float f2 = __uint_as_float(prmt(u, 0x4B000000u, 0x7442u)) - m;
-  const float f3 = __uint_as_float(prmt(u, 0x4B000000u, 0x7443u)) - m;
-  __nv_bfloat162 l = __floats2bfloat162_rn(f0, f1);
-  __nv_bfloat162 h = __floats2bfloat162_rn(f2, f3);
+  const uint32_t tl = prmt(w, 0x43434343u, 0x4140u), th = prmt(w, 0x43434343u, 0x4342u);
+  const uint32_t l1 = tl & 0xFF7FFF7Fu, l2 = (tl & 0x00800080u) | 0xC300C300u;
+  const uint32_t h1 = th & 0xFF7FFF7Fu, h2 = (th & 0x00800080u) | 0xC300C300u;
+  __nv_bfloat162 l = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&l1),
+                             *reinterpret_cast<const __nv_bfloat162*>(&l2));
+  __nv_bfloat162 h = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&h1),
+                             *reinterpret_cast<const __nv_bfloat162*>(&h2));
   lo = *reinterpret_cast<uint32_t*>(&l);
   hi = *reinterpret_cast<uint32_t*>(&h);
 }
 
 constexpr int kWarps = 8;
+constexpr int kWarpsPerSM = 16;  // 2 CTAs of 8 warps at <= 128 registers
 
-// ------------------------------------------------------------------ W8A16
-template <int NT, bool BF16, typename ST>
-__global__ void __launch_bounds__(256, 2)
-    w8a16_skinny_kernel(const int8_t* __restrict__ q, const ST* __restrict__ scale,
-                        const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int N,
-                        int K, int S) {
-  constexpr int U = NT == 1 ? 3 : (NT == 2 ? 2 : 1);
-  __shared__ float red[kWarps][NT][4][32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int tiles_per_cta = kWarps / S;
-  const int tile = blockIdx.x * tiles_per_cta + warp / S;
-  const int seg = warp % S;
-  const int row0 = tile * 16;
-  const int ng = (K + 127) / 128;
-  const int gps = (ng + S - 1) / S;
-  const int gbeg = seg * gps;
-  const int gend = min(ng, gbeg + gps);
-
-  float acc[NT][4];
+template <int NT>
+__device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
 #pragma unroll
   for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+}
 
+// ------------------------------------------------------------------ W8A16 pieces
+// acc += W[row0:row0+16, groups g0..g1) . x^T (this lane's fragment)
+template <int NT, bool BF16>
+__device__ __forceinline__ void w8a16_segment(const int8_t* __restrict__ q,
+                                              const uint16_t* __restrict__ x, int M, int N, int K,
+                                              int row0, int g0, int g1, float (&acc)[NT][4]) {
+  constexpr int U = NT == 1 ? 3 : (NT == 2 ? 2 : 1);
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int rlo = min(row0 + g, N - 1), rhi = min(row0 + g + 8, N - 1);
   const int8_t* wlo = q + (size_t)rlo * K;
   const int8_t* whi = q + (size_t)rhi * K;
   const uint4 z = make_uint4(0, 0, 0, 0);
-
-  if (tile * 16 < N) {
-    // U groups per iteration: all their loads are issued before any MMA so
-    // that every lane keeps U * 64 bytes of weights in flight.
-    for (int gi0 = gbeg; gi0 < gend; gi0 += U) {
-      uint4 al[U][2], ah[U][2];
-      uint4 xv[U][NT][4];
+  // U groups per iteration: all their loads are issued before any MMA so that
+  // every lane keeps U * 64 bytes of weights in flight.
+  for (int gi0 = g0; gi0 < g1; gi0 += U) {
+    uint4 al[U][2], ah[U][2];
+    uint4 xv[U][NT][4];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int gi = gi0 + u;
-        const int k0 = gi * 128 + 16 * t, k1 = k0 + 64;
-        const bool v0 = gi < gend && k0 < K, v1 = gi < gend && k1 < K;
-        al[u][0] = v0 ? ld_stream16(wlo + k0) : z;
-        al[u][1] = v1 ? ld_stream16(wlo + k1) : z;
-        ah[u][0] = v0 ? ld_stream16(whi + k0) : z;
-        ah[u][1] = v1 ? ld_stream16(whi + k1) : z;
+    for (int u = 0; u < U; ++u) {
+      const int gi = gi0 + u;
+      const int k0 = gi * 128 + 16 * t, k1 = k0 + 64;
+      const bool v0 = gi < g1 && k0 < K, v1 = gi < g1 && k1 < K;
+      al[u][0] = v0 ? ld_stream16(wlo + k0) : z;
+      al[u][1] = v1 ? ld_stream16(wlo + k1) : z;
+      ah[u][0] = v0 ? ld_stream16(whi + k0) : z;
+      ah[u][1] = v1 ? ld_stream16(whi + k1) : z;
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          const int tok = j * 8 + g;
-          const uint16_t* xr = x + (size_t)min(tok, M - 1) * K;
-          const bool tv = tok < M;
-          xv[u][j][0] = (tv && v0) ? ld_ro16(xr + k0) : z;
-          xv[u][j][1] = (tv && v0) ? ld_ro16(xr + k0 + 8) : z;
-          xv[u][j][2] = (tv && v1) ? ld_ro16(xr + k1) : z;
-          xv[u][j][3] = (tv && v1) ? ld_ro16(xr + k1 + 8) : z;
-        }
+      for (int j = 0; j < NT; ++j) {
+        const int tok = j * 8 + g;
+        const uint16_t* xr = x + (size_t)min(tok, M - 1) * K;
+        const bool tv = tok < M;
+        xv[u][j][0] = (tv && v0) ? ld_ro16(xr + k0) : z;
+        xv[u][j][1] = (tv && v0) ? ld_ro16(xr + k0 + 8) : z;
+        xv[u][j][2] = (tv && v1) ? ld_ro16(xr + k1) : z;
+        xv[u][j][3] = (tv && v1) ? ld_ro16(xr + k1 + 8) : z;
       }
+    }
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
+    for (int u = 0; u < U; ++u) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int s = 0; s < 4; ++s) {
-            const uint32_t wl = word(al[u][h], s), wh = word(ah[u][h], s);
-            uint32_t a0, a1, a2, a3;
-            if (BF16) {
-              i8x4_to_bf16x2(wl, a0, a2);
-              i8x4_to_bf16x2(wh, a1, a3);
-            } else {
-              i8x4_to_f16x2(wl, a0, a2);
-              i8x4_to_f16x2(wh, a1, a3);
-            }
+        for (int s = 0; s < 4; ++s) {
+          const uint32_t wl = word(al[u][h], s), wh = word(ah[u][h], s);
+          uint32_t a0, a1, a2, a3;
+          if (BF16) {
+            i8x4_to_bf16x2(wl, a0, a2);
+            i8x4_to_bf16x2(wh, a1, a3);
+          } else {
+            i8x4_to_f16x2(wl, a0, a2);
+            i8x4_to_f16x2(wh, a1, a3);
+          }
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
-              const uint4& xs = xv[u][j][2 * h + (s >> 1)];
-              const uint32_t b0 = word(xs, 2 * (s & 1)), b1 = word(xs, 2 * (s & 1) + 1);
-              if (BF16) mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
-              else mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
-            }
+          for (int j = 0; j < NT; ++j) {
+            const uint4& xs = xv[u][j][2 * h + (s >> 1)];
+            const uint32_t b0 = word(xs, 2 * (s & 1)), b1 = word(xs, 2 * (s & 1) + 1);
+            if (BF16) mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
+            else mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
           }
         }
       }
     }
   }
+}
 
-  if (S > 1) {
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) red[warp][j][e][lane] = acc[j][e];
-    __syncthreads();
-    if (seg != 0) return;
-    for (int w = 1; w < S; ++w)
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][e] += red[warp + w][j][e][lane];
-  }
-  if (row0 >= N) return;
+// y[tok, row] = round((sum) * scale[row]) for this lane's fragment
+template <int NT, bool BF16, typename ST>
+__device__ __forceinline__ void w8a16_store(const float (&acc)[NT][4], const ST* __restrict__ scale,
+                                            uint16_t* __restrict__ y, int M, int N, int row0) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int r[2] = {row0 + g, row0 + g + 8};
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
@@ -204,7 +201,672 @@ __global__ void __launch_bounds__(256, 2)
   }
 }
 
-// ------------------------------------------------------------------ GGUF
+// ------------------------------------------------------------------ GGUF pieces
+template <int NT, int TYPE>
+__device__ __forceinline__ void gguf_segment(const uint8_t* __restrict__ qs,
+                                             const __half* __restrict__ dw,
+                                             const int8_t* __restrict__ xq,
+                                             const float2* __restrict__ xs, int Mp, int N, int G,
+                                             int row0, int g0, int g1, float (&acc)[NT][4]) {
+  constexpr int GB = TYPE == DIAL_GGML_Q4_0 ? 64 : 128;
+  // groups per iteration, so every lane keeps ~8 loads of 16 bytes in flight
+  constexpr int U = TYPE == DIAL_GGML_Q4_0 ? (NT <= 2 ? 4 : 2) : (NT == 1 ? 2 : 1);
+  constexpr int NW = TYPE == DIAL_GGML_Q4_0 ? 1 : 2;  // 16-byte loads per row and group
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int rlo = min(row0 + g, N - 1), rhi = min(row0 + g + 8, N - 1);
+  const uint8_t* qlo = qs + (size_t)rlo * G * GB;
+  const uint8_t* qhi = qs + (size_t)rhi * G * GB;
+  for (int gi0 = g0; gi0 < g1; gi0 += U) {
+    uint4 wl[U][NW], wh[U][NW];
+    uint2 dl[U], dh[U];
+    uint4 xv[U][NT][2];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int gi = min(gi0 + u, g1 - 1);  // clamped: a repeated group is never used
+#pragma unroll
+      for (int c = 0; c < NW; ++c) {
+        wl[u][c] = ld_stream16(qlo + (size_t)gi * GB + (16 * NW) * t + 16 * c);
+        wh[u][c] = ld_stream16(qhi + (size_t)gi * GB + (16 * NW) * t + 16 * c);
+      }
+      dl[u] = __ldg(reinterpret_cast<const uint2*>(dw + gguf_d_index(rlo, 4 * gi, G)));
+      dh[u] = __ldg(reinterpret_cast<const uint2*>(dw + gguf_d_index(rhi, 4 * gi, G)));
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const int8_t* xr = xq + (size_t)(j * 8 + g) * G * 128 + (size_t)gi * 128 + 32 * t;
+        xv[u][j][0] = ld_ro16(xr);
+        xv[u][j][1] = ld_ro16(xr + 16);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int gi = gi0 + u;
+      if (gi >= g1) break;
+      const float dlv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dl[u].x)),
+                            __high2float(*reinterpret_cast<const __half2*>(&dl[u].x)),
+                            __low2float(*reinterpret_cast<const __half2*>(&dl[u].y)),
+                            __high2float(*reinterpret_cast<const __half2*>(&dl[u].y))};
+      const float dhv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dh[u].x)),
+                            __high2float(*reinterpret_cast<const __half2*>(&dh[u].x)),
+                            __low2float(*reinterpret_cast<const __half2*>(&dh[u].y)),
+                            __high2float(*reinterpret_cast<const __half2*>(&dh[u].y))};
+#pragma unroll
+      for (int jb = 0; jb < 4; ++jb) {
+        uint32_t a0, a1, a2, a3;
+        if (TYPE == DIAL_GGML_Q4_0) {
+          const uint32_t l = word(wl[u][0], jb), h = word(wh[u][0], jb);
+          a0 = l & 0x0F0F0F0Fu;
+          a2 = (l >> 4) & 0x0F0F0F0Fu;
+          a1 = h & 0x0F0F0F0Fu;
+          a3 = (h >> 4) & 0x0F0F0F0Fu;
+        } else {
+          const uint4& l = wl[u][(jb >> 1) % NW];
+          const uint4& h = wh[u][(jb >> 1) % NW];
+          a0 = word(l, 2 * (jb & 1));
+          a2 = word(l, 2 * (jb & 1) + 1);
+          a1 = word(h, 2 * (jb & 1));
+          a3 = word(h, 2 * (jb & 1) + 1);
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const uint4& xw = xv[u][j][jb >> 1];
+          int c[4] = {0, 0, 0, 0};
+          mma_s8(c, a0, a1, a2, a3, word(xw, 2 * (jb & 1)), word(xw, 2 * (jb & 1) + 1));
+          const float4 sc = __ldg(
+              reinterpret_cast<const float4*>(xs + (size_t)(gi * 4 + jb) * Mp + j * 8 + 2 * t));
+          float v0 = (float)c[0], v1 = (float)c[1], v2 = (float)c[2], v3 = (float)c[3];
+          if (TYPE == DIAL_GGML_Q4_0) {
+            v0 = fmaf(-8.0f, sc.y, v0);
+            v1 = fmaf(-8.0f, sc.w, v1);
+            v2 = fmaf(-8.0f, sc.y, v2);
+            v3 = fmaf(-8.0f, sc.w, v3);
+          }
+          acc[j][0] = fmaf(dlv[jb] * sc.x, v0, acc[j][0]);
+          acc[j][1] = fmaf(dlv[jb] * sc.z, v1, acc[j][1]);
+          acc[j][2] = fmaf(dhv[jb] * sc.x, v2, acc[j][2]);
+          acc[j][3] = fmaf(dhv[jb] * sc.z, v3, acc[j][3]);
+        }
+      }
+    }
+  }
+}
+
+template <int NT, typename YT>
+__device__ __forceinline__ void gguf_store(const float (&acc)[NT][4], YT* __restrict__ y, int M,
+                                           int N, int row0) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int r[2] = {row0 + g, row0 + g + 8};
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    if (r[hr] >= N) continue;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int tok = j * 8 + 2 * t + c;
+        if (tok >= M) continue;
+        y[(size_t)tok * N + r[hr]] = Act<YT>::from_f32(acc[j][2 * hr + c]);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ drivers
+// In-CTA split: tile = blockIdx.x * (8/S) + warp/S, K groups split S ways, smem reduce.
+struct SplitPlan {
+  __device__ __forceinline__ static bool begin(int S, int ng, int& tile, int& g0, int& g1) {
+    const int warp = threadIdx.x >> 5;
+    const int tiles_per_cta = kWarps / S;
+    tile = blockIdx.x * tiles_per_cta + warp / S;
+    const int seg = warp % S;
+    const int gps = (ng + S - 1) / S;
+    g0 = seg * gps;
+    g1 = min(ng, g0 + gps);
+    return true;
+  }
+};
+
+template <int NT>
+__device__ __forceinline__ bool split_reduce(float (&acc)[NT][4], int S,
+                                             float (*red)[NT][4][32]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (S == 1) return true;
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) red[warp][j][e][lane] = acc[j][e];
+  __syncthreads();
+  if (warp % S != 0) return false;
+  for (int w = 1; w < S; ++w)
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][e] += red[warp + w][j][e][lane];
+  return true;
+}
+
+// Stream-K bookkeeping: warp w owns units [u_begin(w), u_begin(w+1)),
+// u_begin(w) = floor(W * w / NW), W = tiles * ng; NW <= W so no range is empty.
+// ------------------------------------------------------------------ TMA-fed stream-K GEMV
+// The weight matrix is cut into units of 16 rows x one 128-wide K group (2 KB
+// of W8A16 / Q8_0 bytes, 1 KB of Q4_0 plus 128 B of block scales), numbered
+// tile-major (unit = tile * ng + group; a tile is 16 output rows).  Warp w owns
+// the contiguous range [W*w/NW, W*(w+1)/NW) of the W units (stream-K), so every
+// warp streams the same number of bytes whatever the shape.  A tile done by one
+// warp alone is stored directly; otherwise each contributing warp leaves its
+// partial sum in a slot, and the warp whose arrival completes the tile adds
+// the slots in warp order (deterministic) and stores it.
+//
+// CTA = up to kTmaWarps independent warps, kCtasPerSM CTAs per SM.  Each warp
+// owns a ring of kStages unit buffers in shared memory; its lane 0 keeps up to
+// kStages unit loads in flight (TMA boxes, no multicast) while the warp
+// computes, and writes each stage's (tile, group) next to it.  Weight bytes in
+// flight cost no registers: 16 warps x 4 stages x 2 KB = 128 KB per SM.
+constexpr int kTmaWarps = 8;
+constexpr int kCtasPerSM = 2;
+constexpr int kStages = 4;        // power of two
+constexpr int kUnitBytes = 2048;  // W8A16 / Q8_0 box: 128 B x 16 rows (Q4_0 uses 64 B x 16)
+constexpr int kDBytes = 128;      // GGUF d of one unit: 16 rows x 4 blocks x f16
+constexpr int kMinUnits = 4;      // units per warp at least
+constexpr int kSlotBytes = (kSkinnyMaxM / 8) * 4 * 32 * 4;  // one partial tile at NT = 4
+
+__host__ __device__ constexpr int ring_bytes(int nwarps) {
+  return nwarps * kStages * (kUnitBytes + kDBytes + 8 + 8);
+}
+constexpr int kTmaSmem = ring_bytes(kTmaWarps) + 1024;  // + alignment slack
+
+struct GemvPlan {
+  int tiles;  // 16-row tiles
+  int ng;     // 128-wide K groups
+  int NW;     // warps
+  int64_t W;  // units, tiles * ng
+};
+
+// a / b with a 32-bit division whenever both fit (a 64-bit one is a long routine)
+__device__ __forceinline__ int64_t div_u(uint64_t a, uint64_t b) {
+  return (a >> 32) == 0 && (b >> 32) == 0 ? (int64_t)((uint32_t)a / (uint32_t)b) : (int64_t)(a / b);
+}
+__device__ __forceinline__ int64_t ubegin(const GemvPlan& p, int64_t w) {
+  return div_u((uint64_t)p.W * w, (uint64_t)p.NW);
+}
+// warp whose range holds unit u
+__device__ __forceinline__ int64_t owner(const GemvPlan& p, int64_t u) {
+  return div_u((uint64_t)(u + 1) * p.NW - 1, (uint64_t)p.W);
+}
+
+struct Ring {
+  uint32_t w;     // unit buffers (1024-aligned, kUnitBytes each)
+  uint32_t d;     // GGUF d buffers (kDBytes each)
+  uint32_t bar;   // kStages mbarriers
+  uint32_t info;  // kStages x {chunk, group} (chunk -1: no more work)
+};
+
+// Layout for the launch's warp count: [unit buffers][d][barriers][info][x staging].
+__device__ __forceinline__ Ring warp_ring(uint8_t* smem_raw) {
+  const uint32_t base = (tma::smem_u32(smem_raw) + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  Ring r;
+  r.w = base + (uint32_t)(warp * kStages * kUnitBytes);
+  r.d = base + (uint32_t)(nw * kStages * kUnitBytes + warp * kStages * kDBytes);
+  r.bar = base + (uint32_t)(nw * kStages * (kUnitBytes + kDBytes) + warp * kStages * 8);
+  r.info = base + (uint32_t)(nw * kStages * (kUnitBytes + kDBytes + 8) + warp * kStages * 8);
+  return r;
+}
+
+// First byte after the rings (the W8A16 activation staging area).
+__device__ __forceinline__ uint32_t ring_end(uint8_t* smem_raw) {
+  const uint32_t base = (tma::smem_u32(smem_raw) + 1023u) & ~1023u;
+  return base + (uint32_t)ring_bytes(blockDim.x >> 5);
+}
+
+__device__ __forceinline__ uint4 lds16(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds8(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts8(uint32_t a, int x, int y) {
+  asm volatile("st.shared.v2.s32 [%0], {%1,%2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void sts16(uint32_t a, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// 16-byte chunk c of row r of a 128-byte-row box loaded with SWIZZLE_128B
+__device__ __forceinline__ uint32_t sw128(uint32_t base, int r, int c) {
+  return base + (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Error path: waits (1 s in all) for every stage this warp still has in flight.
+__device__ __forceinline__ void drain_ring(const Ring& ring, int first, int issued) {
+  const unsigned long long deadline = tma::global_ns() + tma::kWaitNs;
+  for (int i = first; i < issued; ++i)
+    if (!tma::mbar_drain(ring.bar + 8u * (uint32_t)(i & (kStages - 1)), (uint32_t)((i / kStages) & 1),
+                         deadline))
+      return;
+}
+
+// Warp-uniform bounded wait for stage i of the ring.
+__device__ __forceinline__ bool ring_wait(const Ring& ring, int i, int* err) {
+  return __all_sync(0xffffffffu, tma::mbar_wait(ring.bar + 8u * (uint32_t)(i & (kStages - 1)),
+                                                (uint32_t)((i / kStages) & 1), err));
+}
+
+__device__ __forceinline__ void ring_init(const Ring& ring) {
+  if ((threadIdx.x & 31) == 0) {
+    for (int s = 0; s < kStages; ++s) tma::mbar_init(ring.bar + 8u * s, 1);
+    tma::fence_barrier_init();
+    tma::fence_proxy_async();
+  }
+  __syncwarp();
+}
+
+// Orders lane 0's next TMA write into a stage after every lane's shared-memory
+// reads of it: each lane first consumes `dep`, a value computed from its own
+// loaded registers (so its loads have returned), then the warp synchronises.
+// Lane 0's registers alone would not do: the warp's lanes need not execute the
+// loads together.
+__device__ __forceinline__ void stage_reads_done(uint32_t dep) {
+  asm volatile("" ::"r"(dep) : "memory");
+  __syncwarp();
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Lane 0's side of a warp: which unit goes into the next stage -- the next
+// unit of its static range, then the end marker.
+struct Producer {
+  GemvPlan pl;
+  int64_t su, su1;  // next unit, end
+  int st, sg;       // tile and group of su
+  int issued;
+  bool ended;
+
+  __device__ Producer(const GemvPlan& p, int w) : pl(p), issued(0), ended(false) {
+    su = ubegin(pl, w);
+    su1 = ubegin(pl, w + 1);
+    st = (int)div_u((uint64_t)su, (uint64_t)pl.ng);
+    sg = (int)(su - (int64_t)st * pl.ng);
+  }
+  // One more stage: the next unit, or the end marker (a stage completed with no bytes).
+  template <typename Load>
+  __device__ __forceinline__ void refill(const Ring& ring, Load& load) {
+    if (ended) return;
+    const int s = issued & (kStages - 1);
+    ++issued;
+    if (su >= su1) {
+      sts8(ring.info + 8u * (uint32_t)s, -1, 0);
+      mbar_arrive(ring.bar + 8u * (uint32_t)s);
+      ended = true;
+      return;
+    }
+    sts8(ring.info + 8u * (uint32_t)s, st, sg);
+    load(s, ring.bar + 8u * (uint32_t)s, st, sg);
+    if (++sg == pl.ng) {
+      sg = 0;
+      ++st;
+    }
+    ++su;
+  }
+};
+
+// Tile arrival: adds `v` to the tile's count with acquire-release semantics at
+// GPU scope (releases this warp's slot stores, which the preceding __syncwarp
+// orders before it; acquires the other contributors').
+__device__ __forceinline__ int arrive_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Adds n slots (stride NT*128 floats, addresses from slot_of(i), i = 0..n-1) in
+// order; the loads of a batch are all issued before its adds.
+template <int NT, typename SlotOf>
+__device__ __forceinline__ void sum_slots(int n, SlotOf slot_of, float (&sum)[NT][4]) {
+  const int lane = threadIdx.x & 31;
+  constexpr int B = NT == 1 ? 8 : (NT == 2 ? 4 : 2);
+  zero_acc(sum);
+  for (int v0 = 0; v0 < n; v0 += B) {
+    float part[B][NT][4];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (v0 + b < n) {
+        const float* sp = slot_of(v0 + b);
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) part[b][j][e] = __ldcg(sp + (j * 4 + e) * 32 + lane);
+      } else {
+        zero_acc(part[b]);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sum[j][e] += part[b][j][e];
+  }
+}
+
+// Ends warp w's segment of `tile` (`units` units of it).
+template <int NT, typename StoreFn>
+__device__ __forceinline__ void tile_finish(const GemvPlan& pl, float* __restrict__ slots,
+                                            int* __restrict__ cnt, int w, int first_tile, int tile,
+                                            int units, float (&acc)[NT][4], StoreFn& store) {
+  const int lane = threadIdx.x & 31;
+  if (units == pl.ng) {  // the whole tile in this warp
+    store(tile, acc);
+    return;
+  }
+  float* mine = slots + ((size_t)w * 2 + (tile == first_tile ? 0 : 1)) * (NT * 128);
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) __stcg(mine + (j * 4 + e) * 32 + lane, acc[j][e]);
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) old = arrive_acq_rel(cnt + tile, units);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old + units != pl.ng) return;  // another warp completes this tile
+  __syncwarp();
+  const int64_t u0 = (int64_t)tile * pl.ng;
+  const int64_t wa = owner(pl, u0), wb = owner(pl, u0 + pl.ng - 1);
+  float sum[NT][4];
+  sum_slots<NT>((int)(wb - wa + 1), [&](int i) {
+    const int64_t v = wa + i;
+    return slots + ((size_t)v * 2 + (ubegin(pl, v) >= u0 ? 0 : 1)) * (NT * 128);  // v starts in this tile
+  }, sum);
+  if (lane == 0) cnt[tile] = 0;  // ready for the next call
+  store(tile, sum);
+}
+
+// Activation staging for W8A16: with XS the CTA's active warps copy x [M, K]
+// (kXsBytes at most) into shared memory once, with plain loads -- a bulk copy
+// would queue behind the weight prefetch in the SM's TMA unit -- and every
+// lane then reads its fragments from there instead of from L1/L2 on each unit.
+constexpr int kXsBytes = 32 * 1024;
+constexpr int kXsSmem = kTmaSmem + kXsBytes;
+
+// Barrier 1 over the first `threads` threads of the CTA (the warps with work).
+__device__ __forceinline__ void active_warps_sync(int threads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+
+// W8A16 unit: 16 rows x 128 K of int8 weights.  Lane (g, t) takes 16-byte
+// chunks 2t and 2t+1 of rows g and g+8, i.e. K offsets [32t, 32t+32) of the
+// group; word s of chunk 2t+h feeds MMA k-step (h, s) as K positions
+// 32t + 16h + 4s + {0,1 | 2,3} <-> logical fragment columns {2t, 2t+1 | 2t+8, 2t+9},
+// and the activation fragments follow the same permutation.
+template <int NT, bool BF16, typename ST, bool XS>
+__global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
+    w8a16_tma_kernel(const __grid_constant__ CUtensorMap wmap, const ST* __restrict__ scale,
+                     const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int N, int K,
+                     GemvPlan pl, float* __restrict__ slots, int* __restrict__ cnt, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const Ring ring = warp_ring(smem_raw);
+  const uint32_t xsm = ring_end(smem_raw);
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int wpc = blockDim.x >> 5;
+  const int w = blockIdx.x * wpc + (threadIdx.x >> 5);
+  pdl_trigger();
+  if (w >= pl.NW) {  // only the last CTA's highest warps: no CTA-wide barrier below
+    pdl_wait();
+    return;
+  }
+  if (lane == 0) tma::prefetch_map(&wmap);
+  ring_init(ring);
+  Producer pr(pl, w);
+  auto load = [&](int s, uint32_t bar, int tile, int gi) {
+    tma::mbar_expect_tx(bar, kUnitBytes);
+    tma::load_2d(ring.w + (uint32_t)(s * kUnitBytes), &wmap, bar, gi * 128, tile * 16);
+  };
+  if (lane == 0)  // the weights are constant: prefetch before the previous kernel ends
+    while (pr.issued < kStages && !pr.ended) pr.refill(ring, load);
+  pdl_wait();  // x, y and the workspace belong to the stream's earlier kernels
+  if (XS) {
+    const int active = min(wpc, pl.NW - (int)blockIdx.x * wpc) * 32;  // warps 0.. of this CTA
+    const uint4* src = reinterpret_cast<const uint4*>(x);
+    const int n16 = M * K / 8;
+    for (int c = threadIdx.x; c < n16; c += active) sts16(xsm + 16u * (uint32_t)c, ld_ro16(src + c));
+    active_warps_sync(active);
+  }
+  auto store = [&](int tile, const float (&a)[NT][4]) {
+    w8a16_store<NT, BF16, ST>(a, scale, y, M, N, tile * 16);
+  };
+  const uint16_t* xr[NT];
+  uint32_t xo[NT];  // XS: byte offset of this lane's token row in shared memory
+  bool tv[NT];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const int tok = j * 8 + g;
+    tv[j] = tok < M;
+    xr[j] = x + (size_t)(tv[j] ? tok : 0) * K + 32 * t;
+    xo[j] = xsm + (uint32_t)(((tv[j] ? tok : 0) * K + 32 * t) * 2);
+  }
+  float acc[NT][4];
+  zero_acc(acc);
+  const int first_tile = (int)div_u((uint64_t)ubegin(pl, w), (uint64_t)pl.ng);
+  int cur = -1, units = 0;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  for (int i = 0;; ++i) {
+    if (!ring_wait(ring, i, err)) {
+      if (lane == 0) drain_ring(ring, i, pr.issued);
+      return;
+    }
+    const int s = i & (kStages - 1);
+    const uint2 info = lds8(ring.info + 8u * (uint32_t)s);
+    const int tile = (int)info.x, gi = (int)info.y;
+    if (tile < 0) break;
+    if (tile != cur) {
+      if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+      zero_acc(acc);
+      cur = tile;
+      units = 0;
+    }
+    ++units;
+    const int kb = gi * 128;
+    const bool v0 = kb + 32 * t < K, v1 = kb + 32 * t + 16 < K;
+    uint4 xv[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      if (XS) {
+        const uint32_t a = xo[j] + (uint32_t)(kb * 2);
+        xv[j][0] = (tv[j] && v0) ? lds16(a) : z;
+        xv[j][1] = (tv[j] && v0) ? lds16(a + 16) : z;
+        xv[j][2] = (tv[j] && v1) ? lds16(a + 32) : z;
+        xv[j][3] = (tv[j] && v1) ? lds16(a + 48) : z;
+      } else {
+        xv[j][0] = (tv[j] && v0) ? ld_ro16(xr[j] + kb) : z;
+        xv[j][1] = (tv[j] && v0) ? ld_ro16(xr[j] + kb + 8) : z;
+        xv[j][2] = (tv[j] && v1) ? ld_ro16(xr[j] + kb + 16) : z;
+        xv[j][3] = (tv[j] && v1) ? ld_ro16(xr[j] + kb + 24) : z;
+      }
+    }
+    const uint32_t buf = ring.w + (uint32_t)(s * kUnitBytes);
+    const uint4 al0 = lds16(sw128(buf, g, 2 * t)), al1 = lds16(sw128(buf, g, 2 * t + 1));
+    const uint4 ah0 = lds16(sw128(buf, g + 8, 2 * t)), ah1 = lds16(sw128(buf, g + 8, 2 * t + 1));
+    stage_reads_done(al0.x ^ al1.x ^ ah0.x ^ ah1.x ^ info.x);
+    if (lane == 0) pr.refill(ring, load);  // the stage's bytes are in registers: refill it
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int st = 0; st < 4; ++st) {
+        const uint32_t wl = word(h ? al1 : al0, st), wh = word(h ? ah1 : ah0, st);
+        uint32_t a0, a1, a2, a3;
+        if (BF16) {
+          i8x4_to_bf16x2(wl, a0, a2);
+          i8x4_to_bf16x2(wh, a1, a3);
+        } else {
+          i8x4_to_f16x2(wl, a0, a2);
+          i8x4_to_f16x2(wh, a1, a3);
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const uint4& xs = xv[j][2 * h + (st >> 1)];
+          const uint32_t b0 = word(xs, 2 * (st & 1)), b1 = word(xs, 2 * (st & 1) + 1);
+          if (BF16) mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
+          else mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
+        }
+      }
+    }
+  }
+  if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+}
+
+template <int NT, int TYPE, typename YT>
+__global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
+    gguf_tma_kernel(const __grid_constant__ CUtensorMap qmap, const __half* __restrict__ dw,
+                    const int8_t* __restrict__ xq, const float2* __restrict__ xs,
+                    YT* __restrict__ y, int M, int Mp, int N, int G, GemvPlan pl,
+                    float* __restrict__ slots, int* __restrict__ cnt, int* err) {
+  constexpr int GB = TYPE == DIAL_GGML_Q4_0 ? 64 : 128;
+  constexpr uint32_t BOX = GB * 16;
+  extern __shared__ uint8_t smem_raw[];
+  const Ring ring = warp_ring(smem_raw);
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_trigger();
+  if (w >= pl.NW) {
+    pdl_wait();
+    return;
+  }
+  if (lane == 0) tma::prefetch_map(&qmap);
+  ring_init(ring);
+  Producer pr(pl, w);
+  auto load = [&](int s, uint32_t bar, int tile, int gi) {
+    tma::mbar_expect_tx(bar, BOX + kDBytes);
+    tma::load_2d(ring.w + (uint32_t)(s * kUnitBytes), &qmap, bar, gi * GB, tile * 16);
+    // d of rows [16 tile, 16 tile + 16) x blocks [4 gi, 4 gi + 4): 128 contiguous bytes
+    tma::load_1d(ring.d + (uint32_t)(s * kDBytes), dw + ((int64_t)tile * G + gi) * 64, kDBytes, bar);
+  };
+  if (lane == 0)  // the weights are constant: prefetch before the previous kernel ends
+    while (pr.issued < kStages && !pr.ended) pr.refill(ring, load);
+  pdl_wait();  // activations, y and the workspace belong to the stream's earlier kernels
+  auto store = [&](int tile, const float (&a)[NT][4]) { gguf_store<NT, YT>(a, y, M, N, tile * 16); };
+  float acc[NT][4];
+  zero_acc(acc);
+  const int first_tile = (int)div_u((uint64_t)ubegin(pl, w), (uint64_t)pl.ng);
+  int cur = -1, units = 0;
+  for (int i = 0;; ++i) {
+    if (!ring_wait(ring, i, err)) {
+      if (lane == 0) drain_ring(ring, i, pr.issued);
+      return;
+    }
+    const int s = i & (kStages - 1);
+    const uint2 info = lds8(ring.info + 8u * (uint32_t)s);
+    const int tile = (int)info.x, gi = (int)info.y;
+    if (tile < 0) break;
+    if (tile != cur) {
+      if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+      zero_acc(acc);
+      cur = tile;
+      units = 0;
+    }
+    ++units;
+    // activations (with more than 2 token tiles the scales are read per block: registers)
+    constexpr bool kEarlySc = NT <= 2;
+    uint4 xv[NT][2];
+    float4 sc[NT][kEarlySc ? 4 : 1];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int8_t* xr = xq + (size_t)(j * 8 + g) * G * 128 + (size_t)gi * 128 + 32 * t;
+      xv[j][0] = ld_ro16(xr);
+      xv[j][1] = ld_ro16(xr + 16);
+      if (kEarlySc)
+#pragma unroll
+        for (int jb = 0; jb < 4; ++jb)
+          sc[j][jb & (kEarlySc ? 3 : 0)] =
+              __ldg(reinterpret_cast<const float4*>(xs + (size_t)(gi * 4 + jb) * Mp + j * 8 + 2 * t));
+    }
+    const uint32_t buf = ring.w + (uint32_t)(s * kUnitBytes);
+    uint4 wl[2], wh[2];
+    if (TYPE == DIAL_GGML_Q4_0) {  // 64-byte rows, no swizzle
+      wl[0] = lds16(buf + (uint32_t)(g * 64 + 16 * t));
+      wh[0] = lds16(buf + (uint32_t)((g + 8) * 64 + 16 * t));
+      wl[1] = wh[1] = make_uint4(0, 0, 0, 0);
+    } else {  // 128-byte rows, SWIZZLE_128B; lane quad t owns chunks 2t, 2t+1
+      wl[0] = lds16(sw128(buf, g, 2 * t));
+      wl[1] = lds16(sw128(buf, g, 2 * t + 1));
+      wh[0] = lds16(sw128(buf, g + 8, 2 * t));
+      wh[1] = lds16(sw128(buf, g + 8, 2 * t + 1));
+    }
+    const uint32_t dbuf = ring.d + (uint32_t)(s * kDBytes);
+    const uint2 dl = lds8(dbuf + (uint32_t)(g * 8)), dh = lds8(dbuf + (uint32_t)((g + 8) * 8));
+    stage_reads_done(wl[0].x ^ wl[1].x ^ wh[0].x ^ wh[1].x ^ dl.x ^ dh.x ^ info.x);
+    if (lane == 0) pr.refill(ring, load);  // the stage's bytes are in registers: refill it
+    const float dlv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dl.x)),
+                          __high2float(*reinterpret_cast<const __half2*>(&dl.x)),
+                          __low2float(*reinterpret_cast<const __half2*>(&dl.y)),
+                          __high2float(*reinterpret_cast<const __half2*>(&dl.y))};
+    const float dhv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dh.x)),
+                          __high2float(*reinterpret_cast<const __half2*>(&dh.x)),
+                          __low2float(*reinterpret_cast<const __half2*>(&dh.y)),
+                          __high2float(*reinterpret_cast<const __half2*>(&dh.y))};
+#pragma unroll
+    for (int jb = 0; jb < 4; ++jb) {
+      uint32_t a0, a1, a2, a3;
+      if (TYPE == DIAL_GGML_Q4_0) {
+        const uint32_t l = word(wl[0], jb), h = word(wh[0], jb);
+        a0 = l & 0x0F0F0F0Fu;
+        a2 = (l >> 4) & 0x0F0F0F0Fu;
+        a1 = h & 0x0F0F0F0Fu;
+        a3 = (h >> 4) & 0x0F0F0F0Fu;
+      } else {
+        a0 = word(wl[jb >> 1], 2 * (jb & 1));
+        a2 = word(wl[jb >> 1], 2 * (jb & 1) + 1);
+        a1 = word(wh[jb >> 1], 2 * (jb & 1));
+        a3 = word(wh[jb >> 1], 2 * (jb & 1) + 1);
+      }
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const uint4& xw = xv[j][jb >> 1];
+        int cc[4] = {0, 0, 0, 0};
+        mma_s8(cc, a0, a1, a2, a3, word(xw, 2 * (jb & 1)), word(xw, 2 * (jb & 1) + 1));
+        const float4 scv =
+            kEarlySc ? sc[j][jb & (kEarlySc ? 3 : 0)]
+                     : __ldg(reinterpret_cast<const float4*>(xs + (size_t)(gi * 4 + jb) * Mp + j * 8 + 2 * t));
+        float v0 = (float)cc[0], v1 = (float)cc[1], v2 = (float)cc[2], v3 = (float)cc[3];
+        if (TYPE == DIAL_GGML_Q4_0) {
+          v0 = fmaf(-8.0f, scv.y, v0);
+          v1 = fmaf(-8.0f, scv.w, v1);
+          v2 = fmaf(-8.0f, scv.y, v2);
+          v3 = fmaf(-8.0f, scv.w, v3);
+        }
+        acc[j][0] = fmaf(dlv[jb] * scv.x, v0, acc[j][0]);
+        acc[j][1] = fmaf(dlv[jb] * scv.z, v1, acc[j][1]);
+        acc[j][2] = fmaf(dhv[jb] * scv.x, v2, acc[j][2]);
+        acc[j][3] = fmaf(dhv[jb] * scv.z, v3, acc[j][3]);
+      }
+    }
+  }
+  if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+}
+
+// ------------------------------------------------------------------ kernels
+template <int NT, bool BF16, typename ST>
+__global__ void __launch_bounds__(256, 2)
+    w8a16_skinny_kernel(const int8_t* __restrict__ q, const ST* __restrict__ scale,
+                        const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int N,
+                        int K, int S) {
+  pdl_begin();
+  __shared__ float red[kWarps][NT][4][32];
+  const int ng = (K + 127) / 128;
+  int tile, g0, g1;
+  SplitPlan::begin(S, ng, tile, g0, g1);
+  float acc[NT][4];
+  zero_acc(acc);
+  if (tile * 16 < N) w8a16_segment<NT, BF16>(q, x, M, N, K, tile * 16, g0, g1, acc);
+  if (!split_reduce<NT>(acc, S, red)) return;
+  if (tile * 16 < N) w8a16_store<NT, BF16, ST>(acc, scale, y, M, N, tile * 16);
+}
+
 // Activation Q8_0 quantiser (GGML quantize_row_q8_0_ref arithmetic), writing
 // the interleaved Q8_0 order and per-block (d_x, sum of q_x) pairs:
 //   xq : int8  [Mp, G*128]
@@ -213,6 +875,7 @@ __global__ void __launch_bounds__(256, 2)
 template <typename XT>
 __global__ void q8_0_act_quantize_kernel(const XT* __restrict__ x, int M, int Mp, int K, int G,
                                          int8_t* __restrict__ xq, float2* __restrict__ xs) {
+  pdl_begin();
   const int nbp = G * kBlocksPerGroup, nb = K / kQK;
   const int total = Mp * nbp;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -250,159 +913,129 @@ __global__ void __launch_bounds__(256, 2)
     gguf_skinny_kernel(const uint8_t* __restrict__ qs, const __half* __restrict__ dw,
                        const int8_t* __restrict__ xq, const float2* __restrict__ xs,
                        YT* __restrict__ y, int M, int Mp, int N, int G, int S) {
-  constexpr int GB = TYPE == DIAL_GGML_Q4_0 ? 64 : 128;
-  // groups per iteration, so every lane keeps ~8 loads of 16 bytes in flight
-  constexpr int U = TYPE == DIAL_GGML_Q4_0 ? (NT <= 2 ? 4 : 2) : (NT == 1 ? 2 : 1);
+  pdl_begin();
   __shared__ float red[kWarps][NT][4][32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int tiles_per_cta = kWarps / S;
-  const int tile = blockIdx.x * tiles_per_cta + warp / S;
-  const int seg = warp % S;
-  const int row0 = tile * 16;
-  const int gps = (G + S - 1) / S;
-  const int gbeg = seg * gps;
-  const int gend = min(G, gbeg + gps);
-
+  int tile, g0, g1;
+  SplitPlan::begin(S, G, tile, g0, g1);
   float acc[NT][4];
-#pragma unroll
-  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-
-  const int rlo = min(row0 + g, N - 1), rhi = min(row0 + g + 8, N - 1);
-  const uint8_t* qlo = qs + (size_t)rlo * G * GB;
-  const uint8_t* qhi = qs + (size_t)rhi * G * GB;
-  const __half* dlo = dw + (size_t)rlo * G * 4;
-  const __half* dhi = dw + (size_t)rhi * G * 4;
-
-  if (row0 < N) {
-    for (int gi0 = gbeg; gi0 < gend; gi0 += U) {
-      constexpr int NW = TYPE == DIAL_GGML_Q4_0 ? 1 : 2;  // 16-byte loads per row and group
-      uint4 wl[U][NW], wh[U][NW];
-      uint2 dl[U], dh[U];
-      uint4 xv[U][NT][2];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int gi = min(gi0 + u, gend - 1);  // clamped: a repeated group is never used
-#pragma unroll
-        for (int c = 0; c < NW; ++c) {
-          wl[u][c] = ld_stream16(qlo + (size_t)gi * GB + (16 * NW) * t + 16 * c);
-          wh[u][c] = ld_stream16(qhi + (size_t)gi * GB + (16 * NW) * t + 16 * c);
-        }
-        dl[u] = __ldg(reinterpret_cast<const uint2*>(dlo + (size_t)gi * 4));
-        dh[u] = __ldg(reinterpret_cast<const uint2*>(dhi + (size_t)gi * 4));
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          const int8_t* xr = xq + (size_t)(j * 8 + g) * G * 128 + (size_t)gi * 128 + 32 * t;
-          xv[u][j][0] = ld_ro16(xr);
-          xv[u][j][1] = ld_ro16(xr + 16);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int gi = gi0 + u;
-        if (gi >= gend) break;
-        const float dlv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dl[u].x)),
-                              __high2float(*reinterpret_cast<const __half2*>(&dl[u].x)),
-                              __low2float(*reinterpret_cast<const __half2*>(&dl[u].y)),
-                              __high2float(*reinterpret_cast<const __half2*>(&dl[u].y))};
-        const float dhv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dh[u].x)),
-                              __high2float(*reinterpret_cast<const __half2*>(&dh[u].x)),
-                              __low2float(*reinterpret_cast<const __half2*>(&dh[u].y)),
-                              __high2float(*reinterpret_cast<const __half2*>(&dh[u].y))};
-#pragma unroll
-        for (int jb = 0; jb < 4; ++jb) {
-          uint32_t a0, a1, a2, a3;
-          if (TYPE == DIAL_GGML_Q4_0) {
-            const uint32_t l = word(wl[u][0], jb), h = word(wh[u][0], jb);
-            a0 = l & 0x0F0F0F0Fu;
-            a2 = (l >> 4) & 0x0F0F0F0Fu;
-            a1 = h & 0x0F0F0F0Fu;
-            a3 = (h >> 4) & 0x0F0F0F0Fu;
-          } else {
-            const uint4& l = wl[u][(jb >> 1) % NW];
-            const uint4& h = wh[u][(jb >> 1) % NW];
-            a0 = word(l, 2 * (jb & 1));
-            a2 = word(l, 2 * (jb & 1) + 1);
-            a1 = word(h, 2 * (jb & 1));
-            a3 = word(h, 2 * (jb & 1) + 1);
-          }
-#pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            const uint4& xw = xv[u][j][jb >> 1];
-            int c[4] = {0, 0, 0, 0};
-            mma_s8(c, a0, a1, a2, a3, word(xw, 2 * (jb & 1)), word(xw, 2 * (jb & 1) + 1));
-            const float4 sc = __ldg(
-                reinterpret_cast<const float4*>(xs + (size_t)(gi * 4 + jb) * Mp + j * 8 + 2 * t));
-            float v0 = (float)c[0], v1 = (float)c[1], v2 = (float)c[2], v3 = (float)c[3];
-            if (TYPE == DIAL_GGML_Q4_0) {
-              v0 = fmaf(-8.0f, sc.y, v0);
-              v1 = fmaf(-8.0f, sc.w, v1);
-              v2 = fmaf(-8.0f, sc.y, v2);
-              v3 = fmaf(-8.0f, sc.w, v3);
-            }
-            acc[j][0] = fmaf(dlv[jb] * sc.x, v0, acc[j][0]);
-            acc[j][1] = fmaf(dlv[jb] * sc.z, v1, acc[j][1]);
-            acc[j][2] = fmaf(dhv[jb] * sc.x, v2, acc[j][2]);
-            acc[j][3] = fmaf(dhv[jb] * sc.z, v3, acc[j][3]);
-          }
-        }
-      }
-    }
-  }
-
-  if (S > 1) {
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) red[warp][j][e][lane] = acc[j][e];
-    __syncthreads();
-    if (seg != 0) return;
-    for (int w = 1; w < S; ++w)
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][e] += red[warp + w][j][e][lane];
-  }
-  if (row0 >= N) return;
-  const int r[2] = {row0 + g, row0 + g + 8};
-#pragma unroll
-  for (int hr = 0; hr < 2; ++hr) {
-    if (r[hr] >= N) continue;
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int tok = j * 8 + 2 * t + c;
-        if (tok >= M) continue;
-        y[(size_t)tok * N + r[hr]] = Act<YT>::from_f32(acc[j][2 * hr + c]);
-      }
-    }
-  }
+  zero_acc(acc);
+  if (tile * 16 < N) gguf_segment<NT, TYPE>(qs, dw, xq, xs, Mp, N, G, tile * 16, g0, g1, acc);
+  if (!split_reduce<NT>(acc, S, red)) return;
+  if (tile * 16 < N) gguf_store<NT, YT>(acc, y, M, N, tile * 16);
 }
 
-// K-split: the fewest warps per tile that put >= ~16 warps on every SM.
+// K-split of the in-CTA driver: the fewest warps per tile that put >= ~16 warps on every SM.
 int pick_split(int64_t tiles, int64_t groups) {
-  const int64_t target = (int64_t)sm_count() * 16;
+  const int64_t target = (int64_t)sm_count() * kWarpsPerSM;
   int S = 1;
   while (S < kWarps && tiles * S < target && groups >= 2 * S) S *= 2;
   return S;
 }
 
+// Stream-K grid: at most kCtasPerSM x kTmaWarps warps per SM, at least kMinUnits units per warp.
+GemvPlan plan_gemv(int64_t tiles, int64_t ng) {
+  const int64_t resident = (int64_t)sm_count() * kCtasPerSM * kTmaWarps;
+  GemvPlan p;
+  p.tiles = (int)tiles;
+  p.ng = (int)ng;
+  p.W = tiles * ng;
+  p.NW = (int)std::min<int64_t>(resident, std::max<int64_t>(1, p.W / kMinUnits));
+  return p;
+}
+
+int64_t slot_bytes() { return 2ll * sm_count() * kCtasPerSM * kTmaWarps * kSlotBytes; }
+
+// Warps per CTA: enough CTAs to reach every CTA slot before CTAs grow past one warp.
+int tma_warps_per_cta(int NW) {
+  const int slots = sm_count() * kCtasPerSM;
+  const int wpc = (NW + slots - 1) / slots;
+  return wpc < 1 ? 1 : (wpc > kTmaWarps ? kTmaWarps : wpc);
+}
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
 }  // namespace
 
+// ------------------------------------------------------------------ workspaces
+// GEMV workspace, independent of M and K so that one serves every linear of a
+// model: [partial-tile slots: 2 per resident warp][tile counters, zero between calls].
+size_t gemv_workspace_bytes(int64_t N) {
+  const size_t cnt = (size_t)((N + 15) / 16) * sizeof(int);
+  return (size_t)slot_bytes() + (size_t)round_up((int64_t)cnt, 256);
+}
+
+size_t gguf_skinny_workspace_bytes(int64_t M, int64_t K) {
+  const int64_t G = gguf_groups(K);
+  const int64_t Mp = round_up(M, 8);
+  const size_t xq = (size_t)round_up(Mp * G * 128, 256);
+  const size_t xs = (size_t)(G * 4 * Mp) * sizeof(float2);
+  return xq + (size_t)round_up((int64_t)xs, 256);
+}
+
 // ------------------------------------------------------------------ launchers
+// sk_ws (may be NULL): GEMV workspace of gemv_workspace_bytes(N) bytes whose
+// counter part is zero (every call leaves it zero).  Given sk_ws, the TMA-fed
+// dynamic-chunk kernel runs; NULL (or an unaligned weight) selects the in-CTA split.
 dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
                                 dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
-                                cudaStream_t st) {
+                                cudaStream_t st, void* sk_ws) {
   const int64_t tiles = (N + 15) / 16;
-  const int S = pick_split(tiles, (K + 127) / 128);
-  const int tiles_per_cta = kWarps / S;
-  const unsigned grid = (unsigned)((tiles + tiles_per_cta - 1) / tiles_per_cta);
+  const int64_t ng = (K + 127) / 128;
   const int nt = (int)((M + 7) / 8);
   const uint16_t* xp = static_cast<const uint16_t*>(x);
   uint16_t* yp = static_cast<uint16_t*>(y);
-#define W8(NT_, BF, ST)                                                                     \
-  w8a16_skinny_kernel<NT_, BF, ST><<<grid, 256, 0, st>>>(q, static_cast<const ST*>(scale), \
-                                                          xp, yp, (int)M, (int)N, (int)K, S)
+  const bool bf = xdt == DIAL_BF16;
+  dial_status s = DIAL_OK;
+  if (sk_ws && K >= 128 && aligned16(q)) {
+    CUtensorMap map;
+    s = tma::make_byte_map(&map, q, N, K, 128, 16, /*swizzle128=*/true);
+    if (s != DIAL_OK) return s;
+    const GemvPlan pl = plan_gemv(tiles, ng);
+    float* slots = static_cast<float*>(sk_ws);
+    int* cnt = reinterpret_cast<int*>(static_cast<uint8_t*>(sk_ws) + slot_bytes());
+    int* err = device_error_ptr();
+    if (!err) return fail(DIAL_ERR_CUDA, "device error flag is unavailable");
+    const int wpc = tma_warps_per_cta(pl.NW);
+    const dim3 grid((unsigned)((pl.NW + wpc - 1) / wpc)), block((unsigned)(wpc * 32));
+    const bool xs = M * K * 2 <= kXsBytes && aligned16(x);
+    const size_t smem = (size_t)ring_bytes(wpc) + 1024 + (xs ? kXsBytes : 0);
+    cudaError_t ae = cudaSuccess;
+#define SKX(NT_, BF, ST, XS)                                                                   \
+  ae = ensure_smem<w8a16_tma_kernel<NT_, BF, ST, XS>>(XS ? kXsSmem : kTmaSmem);                \
+  if (ae == cudaSuccess)                                                                       \
+    s = launch_pdl("w8a16_tma_kernel", w8a16_tma_kernel<NT_, BF, ST, XS>, grid, block, smem, st, \
+                   map, static_cast<const ST*>(scale), xp, yp, (int)M, (int)N, (int)K, pl,     \
+                   slots, cnt, err)
+#define SK(NT_, BF, ST)       \
+  if (xs) {                   \
+    SKX(NT_, BF, ST, true);   \
+  } else {                    \
+    SKX(NT_, BF, ST, false);  \
+  }
+#define SK_NT(BF, ST)             \
+  switch (nt) {                   \
+    case 1: SK(1, BF, ST); break; \
+    case 2: SK(2, BF, ST); break; \
+    case 3: SK(3, BF, ST); break; \
+    default: SK(4, BF, ST); break; \
+  }
+    if (sdt == DIAL_F32) {
+      if (bf) { SK_NT(true, float) } else { SK_NT(false, float) }
+    } else {
+      if (bf) { SK_NT(true, __half) } else { SK_NT(false, __half) }
+    }
+#undef SK_NT
+#undef SK
+#undef SKX
+    if (ae != cudaSuccess) return cuda_fail(ae, "cudaFuncSetAttribute(w8a16_tma_kernel)");
+    return s;
+  }
+  const int S = pick_split(tiles, ng);
+  const int tiles_per_cta = kWarps / S;
+  const dim3 grid((unsigned)((tiles + tiles_per_cta - 1) / tiles_per_cta));
+#define W8(NT_, BF, ST)                                                                         \
+  s = launch_pdl("w8a16_skinny_kernel", w8a16_skinny_kernel<NT_, BF, ST>, grid, dim3(256), 0, st, \
+                 q, static_cast<const ST*>(scale), xp, yp, (int)M, (int)N, (int)K, S)
 #define W8_NT(BF, ST)            \
   switch (nt) {                  \
     case 1: W8(1, BF, ST); break; \
@@ -410,7 +1043,6 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
     case 3: W8(3, BF, ST); break; \
     default: W8(4, BF, ST); break; \
   }
-  const bool bf = xdt == DIAL_BF16;
   if (sdt == DIAL_F32) {
     if (bf) { W8_NT(true, float) } else { W8_NT(false, float) }
   } else {
@@ -418,51 +1050,80 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
   }
 #undef W8_NT
 #undef W8
-  return check_launch("w8a16_skinny_kernel");
-}
-
-static int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
-
-size_t gguf_skinny_workspace_bytes(int64_t M, int64_t K) {
-  const int64_t G = gguf_groups(K);
-  const int64_t Mp = round_up(M, 8);
-  const size_t xq = (size_t)round_up(Mp * G * 128, 256);
-  const size_t xs = (size_t)(G * 4 * Mp) * sizeof(float2);
-  return xq + xs;
+  return s;
 }
 
 dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,
                                int type, void* y, int64_t M, int64_t K, int64_t N, void* ws,
-                               cudaStream_t st) {
+                               cudaStream_t st, void* sk_ws) {
   const int64_t G = gguf_groups(K);
   const int64_t Mp = round_up(M, 8);
   int8_t* xq = static_cast<int8_t*>(ws);
   float2* xs = reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + round_up(Mp * G * 128, 256));
+  dial_status s = DIAL_OK;
   {
     const int64_t total = Mp * G * 4;
-    const unsigned grid = (unsigned)std::min<int64_t>((total + 127) / 128, (int64_t)sm_count() * 8);
+    const dim3 qgrid((unsigned)std::min<int64_t>((total + 127) / 128, (int64_t)sm_count() * 8));
     if (xdt == DIAL_F32)
-      q8_0_act_quantize_kernel<float><<<grid, 128, 0, st>>>(static_cast<const float*>(x), (int)M,
-                                                            (int)Mp, (int)K, (int)G, xq, xs);
+      s = launch_pdl("q8_0_act_quantize_kernel", q8_0_act_quantize_kernel<float>, qgrid, dim3(128), 0,
+                     st, static_cast<const float*>(x), (int)M, (int)Mp, (int)K, (int)G, xq, xs);
     else if (xdt == DIAL_F16)
-      q8_0_act_quantize_kernel<__half><<<grid, 128, 0, st>>>(static_cast<const __half*>(x), (int)M,
-                                                             (int)Mp, (int)K, (int)G, xq, xs);
+      s = launch_pdl("q8_0_act_quantize_kernel", q8_0_act_quantize_kernel<__half>, qgrid, dim3(128),
+                     0, st, static_cast<const __half*>(x), (int)M, (int)Mp, (int)K, (int)G, xq, xs);
     else
-      q8_0_act_quantize_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(
-          static_cast<const __nv_bfloat16*>(x), (int)M, (int)Mp, (int)K, (int)G, xq, xs);
-    dial_status s = check_launch("q8_0_act_quantize_kernel");
+      s = launch_pdl("q8_0_act_quantize_kernel", q8_0_act_quantize_kernel<__nv_bfloat16>, qgrid,
+                     dim3(128), 0, st, static_cast<const __nv_bfloat16*>(x), (int)M, (int)Mp, (int)K,
+                     (int)G, xq, xs);
     if (s != DIAL_OK) return s;
   }
   const int64_t tiles = (N + 15) / 16;
-  const int S = pick_split(tiles, G);
-  const int tiles_per_cta = kWarps / S;
-  const unsigned grid = (unsigned)((tiles + tiles_per_cta - 1) / tiles_per_cta);
   const int nt = (int)(Mp / 8);
   const uint8_t* qp = static_cast<const uint8_t*>(qs);
   const __half* dp = reinterpret_cast<const __half*>(d);
-#define GG(NT_, TY, YT)                                                                       \
-  gguf_skinny_kernel<NT_, TY, YT><<<grid, 256, 0, st>>>(qp, dp, xq, xs, static_cast<YT*>(y), \
-                                                         (int)M, (int)Mp, (int)N, (int)G, S)
+  if (sk_ws && aligned16(qs) && aligned16(d)) {
+    const int GB = type == DIAL_GGML_Q4_0 ? 64 : 128;
+    CUtensorMap map;
+    s = tma::make_byte_map(&map, qs, N, G * GB, GB, 16, type != DIAL_GGML_Q4_0);
+    if (s != DIAL_OK) return s;
+    const GemvPlan pl = plan_gemv(tiles, G);
+    float* slots = static_cast<float*>(sk_ws);
+    int* cnt = reinterpret_cast<int*>(static_cast<uint8_t*>(sk_ws) + slot_bytes());
+    int* err = device_error_ptr();
+    if (!err) return fail(DIAL_ERR_CUDA, "device error flag is unavailable");
+    const int wpc = tma_warps_per_cta(pl.NW);
+    const dim3 grid((unsigned)((pl.NW + wpc - 1) / wpc)), block((unsigned)(wpc * 32));
+    const size_t smem = (size_t)ring_bytes(wpc) + 1024;
+    cudaError_t ae = cudaSuccess;
+#define GK(NT_, TY, YT)                                                                          \
+  ae = ensure_smem<gguf_tma_kernel<NT_, TY, YT>>(kTmaSmem);                                      \
+  if (ae == cudaSuccess)                                                                         \
+    s = launch_pdl("gguf_tma_kernel", gguf_tma_kernel<NT_, TY, YT>, grid, block, smem, st, map,  \
+                   dp, xq, xs, static_cast<YT*>(y), (int)M, (int)Mp, (int)N, (int)G, pl, slots, \
+                   cnt, err)
+#define GK_NT(TY, YT)             \
+  switch (nt) {                   \
+    case 1: GK(1, TY, YT); break; \
+    case 2: GK(2, TY, YT); break; \
+    case 3: GK(3, TY, YT); break; \
+    default: GK(4, TY, YT); break; \
+  }
+#define GK_Y(TY)                                  \
+  if (xdt == DIAL_F32) { GK_NT(TY, float) }       \
+  else if (xdt == DIAL_F16) { GK_NT(TY, __half) } \
+  else { GK_NT(TY, __nv_bfloat16) }
+    if (type == DIAL_GGML_Q4_0) { GK_Y(DIAL_GGML_Q4_0) } else { GK_Y(DIAL_GGML_Q8_0) }
+#undef GK_Y
+#undef GK_NT
+#undef GK
+    if (ae != cudaSuccess) return cuda_fail(ae, "cudaFuncSetAttribute(gguf_tma_kernel)");
+    return s;
+  }
+  const int S = pick_split(tiles, G);
+  const int tiles_per_cta = kWarps / S;
+  const dim3 grid((unsigned)((tiles + tiles_per_cta - 1) / tiles_per_cta));
+#define GG(NT_, TY, YT)                                                                          \
+  s = launch_pdl("gguf_skinny_kernel", gguf_skinny_kernel<NT_, TY, YT>, grid, dim3(256), 0, st, qp, \
+                 dp, xq, xs, static_cast<YT*>(y), (int)M, (int)Mp, (int)N, (int)G, S)
 #define GG_NT(TY, YT)             \
   switch (nt) {                   \
     case 1: GG(1, TY, YT); break; \
@@ -478,7 +1139,7 @@ dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, co
 #undef GG_Y
 #undef GG_NT
 #undef GG
-  return check_launch("gguf_skinny_kernel");
+  return s;
 }
 
 }  // namespace dial

@@ -24,7 +24,8 @@ from typing import Optional
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 PKG_ROOT = os.path.dirname(_HERE)
-LIB_PATH = os.path.join(PKG_ROOT, "_build", "libdial_cuda.so")
+# DIAL_CUDA_LIB names another build of the library (e.g. one with other tile constants)
+LIB_PATH = os.environ.get("DIAL_CUDA_LIB") or os.path.join(PKG_ROOT, "_build", "libdial_cuda.so")
 
 F32, F16, BF16 = 0, 1, 2
 Q4_0, Q8_0 = 2, 8
@@ -53,14 +54,15 @@ SIGNATURES = {
     "dial_device_error": ([_i32], _i32),
     "dial_w8a16_quantize": ([_vp, _i32, _i64, _i64, _vp, _vp, _i32, _vp], _i32),
     "dial_w8a16_dequantize": ([_vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp], _i32),
-    "dial_w8a16_linear": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp], _i32),
+    "dial_w8a16_linear_workspace_bytes": ([_i64], _sz),
+    "dial_w8a16_linear": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp, _sz, _vp], _i32),
     "dial_gguf_qs_bytes": ([_i32, _i64, _i64], _sz),
     "dial_gguf_d_bytes": ([_i64, _i64], _sz),
     "dial_gguf_repack": ([_vp, _i32, _i64, _i64, _vp, _vp, _vp], _i32),
     "dial_gguf_unpack": ([_vp, _vp, _i32, _i64, _i64, _vp, _vp], _i32),
     "dial_gguf_quantize": ([_vp, _i32, _i64, _i64, _vp, _vp, _vp], _i32),
     "dial_gguf_dequantize": ([_vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp], _i32),
-    "dial_gguf_linear_workspace_bytes": ([_i64, _i64], _sz),
+    "dial_gguf_linear_workspace_bytes": ([_i64, _i64, _i64], _sz),
     "dial_gguf_linear": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp, _sz, _vp], _i32),
     "dial_gguf_linear_noalloc": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp], _i32),
     "dial_rmsnorm": ([_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, ctypes.c_float, _vp], _i32),
@@ -131,6 +133,30 @@ def stream_ptr(stream=None) -> int:
     return int(s.cuda_stream)
 
 
+_stream_ws: dict = {}
+
+
+def stream_workspace(device, need: int):
+    """Zero-filled linear workspace shared by the calls issued on one stream.
+
+    Calls on one stream run one after another, and every call leaves the
+    workspace's counters zero, so they can share it; another stream gets its own.
+    A stream that is being captured into a CUDA graph must have its workspace
+    already (one eager call on that stream first): an allocation inside the
+    capture would come from the graph's private pool.
+    """
+    torch = _torch()
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_ptr())
+    ws = _stream_ws.get(key)
+    if ws is None or ws.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("dial_cuda: no linear workspace for the capturing stream; make one "
+                               "eager call on that stream before capturing")
+        ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
+        _stream_ws[key] = ws
+    return ws, need
+
+
 # ------------------------------------------------------------------ W8A16
 class W8A16Linear:
     """Per-output-row int8 weight + scale, f16/bf16 activations (CudaW8A16Linear)."""
@@ -169,10 +195,11 @@ class W8A16Linear:
         rows = x.numel() // self.in_dim
         if out is None:
             out = torch.empty((*x.shape[:-1], self.out_dim), dtype=x.dtype, device=x.device)
+        ws, need = stream_workspace(x.device, lib().dial_w8a16_linear_workspace_bytes(self.out_dim))
         check(lib().dial_w8a16_linear(x.data_ptr(), dtype_code(x.dtype), self.qweight.data_ptr(),
                                       self.scales.data_ptr(), dtype_code(self.scales.dtype),
                                       out.data_ptr(), rows, self.in_dim, self.out_dim,
-                                      stream_ptr()), "dial_w8a16_linear")
+                                      ws.data_ptr(), need, stream_ptr()), "dial_w8a16_linear")
         return out
 
     __call__ = forward
@@ -205,7 +232,7 @@ class GgufLinear:
     def _alloc(qtype: int, N: int, K: int, device):
         torch = _torch()
         qs = torch.empty(lib().dial_gguf_qs_bytes(qtype, N, K), dtype=torch.uint8, device=device)
-        d = torch.empty(lib().dial_gguf_d_bytes(N, K) // 2, dtype=torch.int16, device=device)
+        d = torch.zeros(lib().dial_gguf_d_bytes(N, K) // 2, dtype=torch.int16, device=device)
         return qs, d
 
     @classmethod
@@ -249,11 +276,9 @@ class GgufLinear:
         return w
 
     def workspace(self, rows: int):
-        torch = _torch()
-        need = lib().dial_gguf_linear_workspace_bytes(rows, self.in_dim)
-        if need and (self._ws is None or self._ws.numel() < need):
-            self._ws = torch.empty(need, dtype=torch.uint8, device=self.qs.device)
-        return self._ws, need
+        """Zero-filled workspace shared by the linears issued on the current stream."""
+        need = lib().dial_gguf_linear_workspace_bytes(rows, self.in_dim, self.out_dim)
+        return stream_workspace(self.qs.device, need)
 
     def forward(self, x, out=None):
         """x [..., in_dim] f32/f16/bf16 -> [..., out_dim] in x's dtype (worker_gguf.rs:574-611)."""

@@ -209,7 +209,8 @@ class Stage:
         torch = _torch()
         need = self.L.dial_decoder_workspace_bytes(ctypes.byref(self.dims), tokens, max_len)
         if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            # zero-filled: the stream-K counters at its start must begin at zero
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
         return self._ws, need
 
     # -------------------------------------------------------------- forward pieces

@@ -91,10 +91,18 @@ DIAL_API dial_status dial_w8a16_dequantize(const int8_t* q, const void* scale, d
  * accumulation (worker_w8a16.rs:158-181).  x is [M, K] f16 or bf16, y is
  * [M, N] in the same dtype (the reference is f16 in / f16 out).  Any M >= 1;
  * the kernel is picked by M (decode GEMV, small-M tensor-core tile, or the
- * tcgen05 dequant-GEMM). */
+ * tcgen05 dequant-GEMM).
+ * `workspace` (optional, dial_w8a16_linear_workspace_bytes(N) bytes, about
+ * 10 MiB on a 148-SM B200, 16-byte aligned) lets the small-M kernel give every
+ * warp of the GPU an equal share of the weight bytes (stream-K); it must be
+ * zero-filled before its first use and every call leaves it zero-filled (a
+ * call that reported a device error may not: zero it again).  Calls that share
+ * a workspace must not overlap on the GPU.  One workspace sized for the largest
+ * N serves every linear.  NULL: no workspace (same results, slower small M). */
+DIAL_API size_t dial_w8a16_linear_workspace_bytes(int64_t N);
 DIAL_API dial_status dial_w8a16_linear(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
                               dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
-                              dial_stream stream);
+                              void* workspace, size_t workspace_bytes, dial_stream stream);
 
 /* ------------------------------------------------------------------ GGUF
  * Native block layout (what a GGUF file holds and candle uploads):
@@ -104,7 +112,9 @@ DIAL_API dial_status dial_w8a16_linear(const void* x, dial_dtype xdt, const int8
  * Blocks are row-major over [N, K/32].  On the device the linear keeps a
  * split layout made once at load by dial_gguf_repack, in groups of 4 blocks
  * (G = ceil(K/128) groups per row, missing blocks zero-padded):
- *   d  : f16 [N, 4*G]                      (dial_gguf_d_bytes)
+ *   d  : f16 [ceil(N/16), G, 16, 4]        (dial_gguf_d_bytes): the scales of
+ *        one 16-row x 4-block unit are 128 contiguous bytes; rows past N are
+ *        padding (allocate the array zero-filled)
  *   qs : u8  [N, G*64] (Q4_0) or [N, G*128] (Q8_0)   (dial_gguf_qs_bytes)
  * with the bytes of a group interleaved so that each 16-byte load is one
  * lane's slice of an int8 tensor-core fragment (dial-8b-orin_b200/csrc/layout.cuh
@@ -138,9 +148,11 @@ DIAL_API dial_status dial_gguf_dequantize(const void* qs, const uint16_t* d, dia
  * every block is an exact integer dot scaled in f32 (candle's CPU QMatMul
  * arithmetic).  Larger M: weights are dequantised to f16/bf16 tiles feeding
  * tensor-core MMAs with f32 accumulation.  K % 32 == 0.  `workspace` must hold
- * dial_gguf_linear_workspace_bytes(M, K) bytes (16-byte aligned; may be NULL
- * when that is 0). */
-DIAL_API size_t dial_gguf_linear_workspace_bytes(int64_t M, int64_t K);
+ * dial_gguf_linear_workspace_bytes(M, K, N) bytes, 16-byte aligned, zero-filled
+ * before its first use (every call leaves its counters zero again, unless it
+ * reported a device error); calls that share a workspace must not overlap on
+ * the GPU. */
+DIAL_API size_t dial_gguf_linear_workspace_bytes(int64_t M, int64_t K, int64_t N);
 DIAL_API dial_status dial_gguf_linear(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,
                              dial_ggml_type type, void* y, int64_t M, int64_t K, int64_t N,
                              void* workspace, size_t workspace_bytes, dial_stream stream);

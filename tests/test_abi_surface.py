@@ -52,18 +52,18 @@ def test_abi_version_and_status_strings():
 def test_validation_without_gpu():
     L = D.lib()
     # null pointers
-    assert L.dial_w8a16_linear(None, D.F16, None, None, D.F32, None, 1, 64, 64, None) == 1
+    assert L.dial_w8a16_linear(None, D.F16, None, None, D.F32, None, 1, 64, 64, None, 0, None) == 1
     assert b"null" in L.dial_last_error()
     fake = ctypes.c_void_p(0x1000)  # never dereferenced: checks fail first
     # f32 activations are rejected by W8A16 (the reference requires F16)
-    assert L.dial_w8a16_linear(fake, D.F32, fake, fake, D.F32, fake, 1, 64, 64, None) == 2
+    assert L.dial_w8a16_linear(fake, D.F32, fake, fake, D.F32, fake, 1, 64, 64, None, 0, None) == 2
     # K not a multiple of 16
-    assert L.dial_w8a16_linear(fake, D.F16, fake, fake, D.F32, fake, 1, 60, 64, None) == 4
+    assert L.dial_w8a16_linear(fake, D.F16, fake, fake, D.F32, fake, 1, 60, 64, None, 0, None) == 4
     # misaligned activation pointer
     odd = ctypes.c_void_p(0x1002)
-    assert L.dial_w8a16_linear(odd, D.F16, fake, fake, D.F32, fake, 1, 64, 64, None) == 3
+    assert L.dial_w8a16_linear(odd, D.F16, fake, fake, D.F32, fake, 1, 64, 64, None, 0, None) == 3
     # non-positive sizes
-    assert L.dial_w8a16_linear(fake, D.F16, fake, fake, D.F32, fake, 0, 64, 64, None) == 1
+    assert L.dial_w8a16_linear(fake, D.F16, fake, fake, D.F32, fake, 0, 64, 64, None, 0, None) == 1
     # GGUF: bad type, K % 32, missing workspace
     assert L.dial_gguf_linear(fake, D.F32, fake, fake, 3, fake, 1, 64, 64, None, 0, None) == 2
     assert L.dial_gguf_linear(fake, D.F32, fake, fake, D.Q4_0, fake, 1, 48, 64, None, 0, None) == 4
@@ -76,10 +76,10 @@ def test_gguf_size_helpers():
     # K=4096 -> 32 groups of 4 blocks; Q4_0 64 B / group, Q8_0 128 B / group
     assert L.dial_gguf_qs_bytes(D.Q4_0, 10, 4096) == 10 * 32 * 64
     assert L.dial_gguf_qs_bytes(D.Q8_0, 10, 4096) == 10 * 32 * 128
-    assert L.dial_gguf_d_bytes(10, 4096) == 10 * 128 * 2
+    assert L.dial_gguf_d_bytes(10, 4096) == 16 * 128 * 2  # rows padded to 16
     # K=96 -> 3 blocks padded to one group of 4
     assert L.dial_gguf_qs_bytes(D.Q4_0, 1, 96) == 64
-    assert L.dial_gguf_linear_workspace_bytes(1, 4096) > 0
+    assert L.dial_gguf_linear_workspace_bytes(1, 4096, 64) > 0
 
 
 def test_no_cpu_fallback_when_library_missing(monkeypatch, tmp_path):

@@ -101,6 +101,23 @@ def test_w8a16_linear_parity(D, torch, M, xdt, sdt):
     assert rel_err(y, y_ref) <= tol
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 16, 16384), (4, 48, 8192), (3, 100, 64), (2, 1, 4096)])
+def test_w8a16_linear_streamk_shapes(D, torch, M, N, K):
+    """Few tiles over a long K: one tile's K range is split across up to 64 warps
+    (the arrival counter / ordered slot sum), plus K < 128 (the in-CTA split) and
+    a single output row.  Repeated calls must give bit-identical outputs."""
+    rng = np.random.default_rng(M * 7 + N + K)
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    x = rng.normal(0, 1, (M, K)).astype(np.float16)
+    lin = D.W8A16Linear.from_linear("t", _to_dev(torch, w))
+    xt = _to_dev(torch, x)
+    y1 = lin.forward(xt).float().cpu().numpy()
+    y2 = lin.forward(xt).float().cpu().numpy()
+    y_ref, _ = O.w8a16_linear(x, lin.qweight.cpu().numpy(), lin.scales.cpu().numpy())
+    assert rel_err(y1, y_ref) <= 2e-3
+    assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
+
+
 def test_w8a16_decode_config1_shape(D, torch):
     """BASELINE config 1 shape: x f16 [1,4096] ~N(0,1), W [12288,4096] ~N(0,0.02), f16 scale."""
     rng = np.random.default_rng(299792458)

@@ -40,8 +40,8 @@ def test_noalloc_matches_workspace_entry_point(cuda, qt):
         x = torch.from_numpy(rng.normal(0, 1, (M, K)).astype(np.float32)).cuda()
         ref = torch.empty((M, N), dtype=torch.float32, device="cuda")
         out = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
-        need = L.dial_gguf_linear_workspace_bytes(M, K)
-        ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+        need = L.dial_gguf_linear_workspace_bytes(M, K, N)
+        ws = torch.zeros(need, dtype=torch.uint8, device="cuda")  # zero-filled before first use
         # the workspace-taking entry point on the same integer path, one pass per 32 rows
         for m0 in range(0, M, 32):
             mc = min(32, M - m0)

@@ -153,6 +153,16 @@ def barrier(world):
         dist.barrier()
 
 
+def sum_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def max_over_ranks(v: float, world: int) -> float:
     if world == 1:
         return v
@@ -191,7 +201,7 @@ class W8A16Gemv:
     M, N, K = 1, 12288, 4096
     graph = True
 
-    def __init__(self, torch, D):
+    def __init__(self, torch, D, rank: int = 0, world: int = 1):
         self.torch = torch
         g = torch.Generator(device="cuda").manual_seed(SEED)
         per = self.N * self.K + 2 * self.N
@@ -243,7 +253,7 @@ class GgufSweep:
     ms = (1, 8)
     graph = True
 
-    def __init__(self, torch, D):
+    def __init__(self, torch, D, rank: int = 0, world: int = 1):
         self.torch, self.D = torch, D
         g = torch.Generator(device="cuda").manual_seed(SEED)
         layer, per_layer = [], 0
@@ -303,7 +313,7 @@ class GgufPrefill(GgufSweep):
     kernel = "dequant_gemm_kernel (whole sweep)"
     ms = (512,)
 
-    def __init__(self, torch, D):
+    def __init__(self, torch, D, rank: int = 0, world: int = 1):
         super().__init__(torch, D)
         self.work_per_step = self.flops()
         self.config["workload"] = "gguf_prefill"
@@ -317,103 +327,96 @@ class GgufPrefill(GgufSweep):
 class QwenDecode:
     """BASELINE configs 3/4: Qwen3-8B-shaped W8A16 decoder (36 layers, hidden 4096,
     MLP 12288, 32/8 heads, vocab 151936, random init N(0, 0.02)), 8 sequences,
-    1024-token prompts (prefilled before timing), decode as micro-batches of 1.
-    A step advances every sequence by one greedy token.  Metric: decode tok/s."""
+    1024-token prompts (prefilled before timing), decoded as micro-batches of 1
+    through a pipeline of one stage per rank (layers split by the stage
+    planner, the output head counted as 3.2 layers).  A step advances every
+    sequence by one greedy token.  Metric: decode tok/s of the whole job."""
     metric, unit, bound, dtype = "8B W8A16 decode tok/s", "tok/s", "hbm", "int8 x bf16"
-    kernel = "w8a16_tma_kernel<NT=1> (the token's 145 linears from one graph, events)"
+    kernel = "w8a16_tma_kernel<NT=1> (the stage's linears from one graph, events)"
     graph = True
-    n_seqs, prompt_len, decode_cap = 8, 1024, 256
-    copies_per_step = 8  # one graph per sequence
+    scaling = "strong"
+    n_seqs, prompt_len, decode_cap = 8, 1024, 448
+    copies_per_step = 8  # one graph per micro-batch
 
-    def __init__(self, torch, D):
+    def __init__(self, torch, D, rank: int = 0, world: int = 1):
         from dial_cuda.model import ModelConfig, Stage
-        self.torch, self.D = torch, D
+        from dial_cuda.pipeline import ModelStageCompute, Pipeline, TorchChannel, stage_layers
+        self.torch, self.D, self.rank, self.world = torch, D, rank, world
         self.cfg = ModelConfig(act_dtype="bf16")
+        self.ranges = stage_layers(self.cfg.n_layers, world)
+        rr = self.ranges[rank]
         self.max_seq = self.prompt_len + self.decode_cap + 16
-        self.stage = Stage(self.cfg, 0, self.cfg.n_layers, n_slots=self.n_seqs, max_seq=self.max_seq)
+        self.stage = Stage(self.cfg, rr.start, rr.stop, n_slots=self.n_seqs, max_seq=self.max_seq)
         st = self.stage
-        dev = st.device
-        g = torch.Generator(device="cuda").manual_seed(SEED)
-        self.ids = torch.zeros(self.n_seqs, dtype=torch.int32, device=dev)
-        self.pos = torch.zeros(self.n_seqs, dtype=torch.int32, device=dev)
-        self.slots = torch.arange(self.n_seqs, dtype=torch.int32, device=dev)
-        self.hidden = [torch.empty((1, self.cfg.hidden), device=dev, dtype=st.dt) for _ in range(self.n_seqs)]
+        self.comp = ModelStageCompute(st, self.n_seqs, self.prompt_len)
+        self.pipe = Pipeline(rank, world, self.comp, TorchChannel() if world > 1 else None, self.n_seqs)
+        prompts = None
+        if rank == 0:
+            g = torch.Generator(device="cuda").manual_seed(SEED)
+            prompts = [torch.randint(0, self.cfg.vocab, (self.prompt_len,), generator=g, device=st.device,
+                                     dtype=torch.int32) for _ in range(self.n_seqs)]
         # prefill every sequence (untimed: the metric is decode throughput)
-        t0 = time.perf_counter()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
         ev0.record()
-        for b in range(self.n_seqs):
-            prompt = torch.randint(0, self.cfg.vocab, (self.prompt_len,), generator=g, device=dev,
-                                   dtype=torch.int32)
-            h = torch.empty((self.prompt_len, self.cfg.hidden), device=dev, dtype=st.dt)
-            st.embed_tokens(prompt, h)
-            st.layers_forward(h, torch.arange(self.prompt_len, dtype=torch.int32, device=dev),
-                              torch.full((self.prompt_len,), b, dtype=torch.int32, device=dev),
-                              self.prompt_len)
-            st.head_forward(h, self.ids[b:b + 1],
-                            row_index=torch.tensor([self.prompt_len - 1], dtype=torch.int32, device=dev))
+        self.pipe.prefill(prompts, prompt_len=self.prompt_len)
         ev1.record()
         torch.cuda.synchronize()
-        self.prefill_ms = ev0.elapsed_time(ev1) / self.n_seqs
-        self.pos.fill_(self.prompt_len)
-        self.work_per_step = self.n_seqs  # tokens
+        self.prefill_ms = max_over_ranks(ev0.elapsed_time(ev1), world) / self.n_seqs
+        self.work_per_step = self.n_seqs  # tokens (whole job)
         self.weight_bytes = st.weight_bytes
-        self.h_ids = torch.empty(self.n_seqs, dtype=torch.int32).pin_memory()
-        self.h_out = torch.empty(self.n_seqs, dtype=torch.int32).pin_memory()
         self.steps_done = 0
         self.config = {"workload": "qwen3_8b_w8a16_decode", "model": "Qwen3-8B-shaped, random init",
                        "layers": 36, "hidden": 4096, "intermediate": 12288, "heads": "32/8",
                        "vocab": 151936, "sequences": self.n_seqs, "micro_batch": 1,
                        "prompt_len": self.prompt_len, "activation": "bf16", "kv_cache": "bf16",
-                       "weights_GB": round(self.weight_bytes / 1e9, 3),
+                       "stages": [[r.start, r.stop] for r in self.ranges],
+                       "stage_weights_GB": round(self.weight_bytes / 1e9, 3),
                        "prefill_ms_per_seq": round(self.prefill_ms, 2),
                        "l2": "7.6 GB of weights per token >> 126 MB L2",
-                       "launch": "one CUDA graph per sequence slot"}
-
-    def one_token(self, b: int):
-        st = self.stage
-        st.embed_tokens(self.ids[b:b + 1], self.hidden[b])
-        st.layers_forward(self.hidden[b], self.pos[b:b + 1], self.slots[b:b + 1], self.max_seq)
-        st.head_forward(self.hidden[b], self.ids[b:b + 1])
-        self.pos[b:b + 1].add_(1)
+                       "launch": "one CUDA graph per micro-batch and stage; NCCL p2p hand-off"}
 
     def run_copy(self, _):
-        self.one_token(0)
-        self.pos[0:1].sub_(1)  # the counting pass must not advance the sequence
+        """One eager micro-batch for the launch count (its state is restored)."""
+        c = self.comp
+        saved = [t.clone() for t in c.tokens]
+        c._eager(0)
+        for t, s in zip(c.tokens, saved):
+            t.copy_(s)
 
     def build_graphs(self):
-        torch = self.torch
-        self.graphs = []
-        for b in range(self.n_seqs):
-            self.one_token(b)  # warm (workspace, attributes) outside capture
-        torch.cuda.synchronize()
-        self.pos.sub_(1)
-        for b in range(self.n_seqs):
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr):  # capture records the work without running it
-                self.one_token(b)
-            self.graphs.append(gr)
-        torch.cuda.synchronize()
+        c = self.comp
+        saved = [t.clone() for t in c.tokens]  # the warm-up runs of the capture must not move tokens
+        c.capture()
+        for t, s in zip(c.tokens, saved):
+            t.copy_(s)
+        self.torch.cuda.synchronize()
+
+    def _wrap(self):
+        if self.steps_done >= self.decode_cap - 1:  # every rank wraps at the same step
+            self.pipe.finish()
+            self.comp.reset_positions(self.prompt_len)
+            self.steps_done = 0
 
     def step(self):
-        if self.steps_done >= self.decode_cap - 1:
-            self.pos.fill_(self.prompt_len)  # wrap: keep the KV window inside its capacity
-            self.steps_done = 0
-        for gr in self.graphs:
-            gr.replay()
+        self._wrap()
+        self.pipe.steps(1)
         self.steps_done += 1
 
     def step_e2e(self):
-        """Public-API loop: the host sends each sequence's token, receives the next."""
-        self.ids.copy_(self.h_ids, non_blocking=True)
-        self.step()
-        self.h_out.copy_(self.ids, non_blocking=True)
-        return self.h_ids.numel() * 4, self.h_out.numel() * 4
+        """Serving loop: each token passes through pinned host memory."""
+        self._wrap()
+        self.pipe.steps(1, host_io=True)
+        self.steps_done += 1
+        return 4 * self.n_seqs, 4 * self.n_seqs
+
+    def finish(self):
+        self.pipe.finish()
 
     def kernel_roofline(self, reps: int = 5):
-        """HBM GB/s of the dominant kernel: the token's linears (36 x {qkv, o,
-        gate_up, down} + lm_head, M = 1) launched back to back in model order
-        from one CUDA graph, algorithmic bytes over the replay's event time."""
+        """HBM GB/s of the dominant kernel: this stage's linears (M = 1) launched
+        back to back in model order from one CUDA graph, algorithmic bytes over
+        the replay's event time."""
         torch, st = self.torch, self.stage
         from dial_cuda.model import WFMT_W8A16
         lins = st.linears + ([st.head] if st.head is not None else [])
@@ -611,8 +614,11 @@ def run_ours(args, rank, local, world):
 
     import dial_cuda as D
     torch.cuda.set_device(local)
-    wl = WORKLOADS[args.workload](torch, D)
+    wl = WORKLOADS[args.workload](torch, D, rank=rank, world=world)
     stream = torch.cuda.current_stream()
+    pipelined = getattr(wl, "scaling", "weak") == "strong"  # one stage per rank
+    # whole-job work per step: replicas each do a step's work, a pipeline does it once
+    job_work = wl.work_per_step * (1 if pipelined else world)
 
     # launches per step, counted on an eager pass
     c0 = D.launch_count()
@@ -622,6 +628,7 @@ def run_ours(args, rank, local, world):
         wl.step()
     torch.cuda.synchronize()
     launches_per_step = (D.launch_count() - c0) * getattr(wl, "copies_per_step", 1)
+    launches_per_step = int(sum_over_ranks(launches_per_step, world))  # every rank's kernels
     if wl.graph:
         wl.build_graphs()
     for _ in range(max(args.warmup, 3)):
@@ -645,6 +652,8 @@ def run_ours(args, rank, local, world):
         torch.cuda.synchronize()
         w1 = time.perf_counter()
         barrier(world)
+    if hasattr(wl, "finish"):
+        wl.finish()
     total_ms = max_over_ranks(t_begin.elapsed_time(t_end), world)
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     assert D.lib().dial_device_error(1) == 0
@@ -662,14 +671,15 @@ def run_ours(args, rank, local, world):
             h2d, d2h = wl.step_e2e()
         e1.record(stream)
         torch.cuda.synchronize()
+        if hasattr(wl, "finish"):
+            wl.finish()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
-        e2e = {"value": round(wl.work_per_step * world * args.steps / (e2e_ms / 1e3)
-                              / unit_scale(wl.unit), 3),
+        e2e = {"value": round(job_work * args.steps / (e2e_ms / 1e3) / unit_scale(wl.unit), 3),
                "unit": wl.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(e2e_ms / args.steps, 5)}
 
     pk, peak_src = peaks()
-    value = wl.work_per_step * world * args.steps / (total_ms / 1e3) / unit_scale(wl.unit)
+    value = job_work * args.steps / (total_ms / 1e3) / unit_scale(wl.unit)
     # roofline of the dominant kernel: algorithmic work per step / mean step time
     # (for the whole-model decode: the linears' bytes over their per-launch times)
     if hasattr(wl, "kernel_roofline"):
@@ -685,9 +695,9 @@ def run_ours(args, rank, local, world):
     line = {
         "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
-        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": dict(wl.config, parallelism=f"replicas x{world}"),
+        "higher_is_better": True, "scaling": "strong" if pipelined else "weak", "vs_baseline": None,
+        "dtype": wl.dtype, "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+        "config": dict(wl.config, parallelism=(f"pipeline x{world}" if pipelined else f"replicas x{world}")),
         "roofline": {"bound": wl.bound, "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s" if wl.bound == "hbm" else "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": None,
@@ -710,7 +720,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="w8a16_gemv")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen3_decode")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

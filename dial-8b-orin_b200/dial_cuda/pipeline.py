@@ -1,0 +1,296 @@
+"""Pipeline over the local GPUs: one process per GPU, one stage per process.
+
+This replaces the reference's master/worker hand-off (the hidden state
+serialised to bytes and sent over TCP, spm/message.rs:147-165 and 366-408,
+worker loop spm/worker.rs:645-765, Client::forward_batch spm/client.rs:389-452)
+with device-to-device sends over NVLink: stage s sends the bf16/f16 hidden
+state [rows, hidden] of each micro-batch to stage s+1, and the last stage
+sends each sequence's next token id (int32) back to stage 0, which embeds it
+for the next step.  Layers are split by the stage planner (planner.py).
+
+Schedule (every stage, micro-batches b = 0..B-1 of step t, m = t*B + b):
+    stage 0:    input = token of m-B from the last stage (t > 0) or the prompt's
+                first token (t = 0)
+    stage s>0:  input = hidden of m from stage s-1
+    compute     (embedding on stage 0, layers, head + argmax on the last stage)
+    stage s<P-1: hidden of m -> stage s+1;  last stage: token of m -> stage 0
+With B >= P micro-batches every stage is busy in the steady state.  Sends are
+asynchronous (a send buffer is reused only after its previous send finished)
+and each stage pair has its own channel, so the token ring back to stage 0
+cannot block the forward chain.
+
+The communication is a `Channel` object: TorchChannel (torch.distributed
+point-to-point; NCCL over NVLink on GPUs, gloo for the CPU tests).  The compute
+of a stage is a `StageCompute` object; ModelStageCompute runs a model.Stage.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+from typing import List, Optional, Sequence
+
+
+def _torch():
+    import torch  # noqa: PLC0415
+    return torch
+
+
+# ------------------------------------------------------------------ channels
+class TorchChannel:
+    """Point-to-point sends over torch.distributed (the default process group)."""
+
+    def __init__(self):
+        import torch.distributed as dist  # noqa: PLC0415
+        self.dist = dist
+
+    def isend(self, t, dst: int):
+        return self.dist.isend(t, dst)
+
+    def irecv(self, t, src: int):
+        return self.dist.irecv(t, src)
+
+
+def init_distributed(backend: str = "nccl", timeout_s: float = 120.0):
+    """rank, local_rank, world from the torchrun environment; short timeout so
+    that ranks waiting on a dead peer end with an error."""
+    import torch.distributed as dist  # noqa: PLC0415
+    torch = _torch()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        kw = {}
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
+    return rank, local, world
+
+
+# ------------------------------------------------------------------ stage compute
+class StageCompute:
+    """What one stage does to micro-batch b.  Buffers are fixed per micro-batch.
+    For prefill: prefill_buffer(T) is the [T, hidden] hand-off buffer and
+    prefill_run(b, ids) runs stage 0's embedding of `ids`, the layers, and the
+    last stage's head on the last row (the first token, into token_buffer(b))."""
+
+    first: bool
+    last: bool
+
+    def hidden_buffer(self, b: int):  # [rows, hidden] in the activation dtype
+        raise NotImplementedError
+
+    def token_buffer(self, b: int):  # int32 [rows]
+        raise NotImplementedError
+
+    def run(self, b: int) -> None:
+        """Stage 0 embeds token_buffer(b); every stage runs its layers on
+        hidden_buffer(b); the last stage writes the next token to token_buffer(b)."""
+        raise NotImplementedError
+
+    def advance(self, b: int) -> None:
+        """Moves micro-batch b to its next position (after its step)."""
+
+
+class ModelStageCompute(StageCompute):
+    """A model.Stage driving one micro-batch per sequence slot (micro-batch b is
+    KV slot b), each step captured once as a CUDA graph per micro-batch."""
+
+    def __init__(self, stage, n_mb: int, prompt_len: int, use_graphs: bool = True):
+        torch = _torch()
+        self.st = stage
+        self.first, self.last = stage.first == 0, stage.last == stage.cfg.n_layers
+        self.n_mb = n_mb
+        dev, dt, H = stage.device, stage.dt, stage.cfg.hidden
+        self.hidden = [torch.zeros((1, H), device=dev, dtype=dt) for _ in range(n_mb)]
+        self.tokens = [torch.zeros(1, device=dev, dtype=torch.int32) for _ in range(n_mb)]
+        self.pos = [torch.full((1,), prompt_len, device=dev, dtype=torch.int32) for _ in range(n_mb)]
+        self.slot = [torch.full((1,), b, device=dev, dtype=torch.int32) for b in range(n_mb)]
+        self.use_graphs = use_graphs
+        self.graphs: List = [None] * n_mb
+
+    def hidden_buffer(self, b):
+        return self.hidden[b]
+
+    def token_buffer(self, b):
+        return self.tokens[b]
+
+    def _eager(self, b):
+        st = self.st
+        if self.first:
+            st.embed_tokens(self.tokens[b], self.hidden[b])
+        st.layers_forward(self.hidden[b], self.pos[b], self.slot[b], st.max_seq)
+        if self.last:
+            st.head_forward(self.hidden[b], self.tokens[b])
+
+    def capture(self) -> None:
+        """Captures one graph per micro-batch (its positions advance in place)."""
+        if not self.use_graphs:
+            return
+        torch = _torch()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for b in range(self.n_mb):
+                self._eager(b)  # warm: workspaces, kernel attributes
+        torch.cuda.synchronize()
+        for b in range(self.n_mb):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                self._eager(b)
+            self.graphs[b] = g
+        torch.cuda.synchronize()
+
+    def run(self, b):
+        if self.graphs[b] is not None:
+            self.graphs[b].replay()
+        else:
+            self._eager(b)
+
+    def advance(self, b):
+        self.pos[b].add_(1)
+
+    def reset_positions(self, prompt_len: int) -> None:
+        for p in self.pos:
+            p.fill_(prompt_len)
+
+    # prefill: one sequence (KV slot b) of T prompt tokens per micro-batch
+    def prefill_buffer(self, T: int):
+        torch = _torch()
+        if getattr(self, "_pbuf", None) is None or self._pbuf.shape[0] != T:
+            self._pbuf = torch.empty((T, self.st.cfg.hidden), device=self.st.device, dtype=self.st.dt)
+            self._ppos = torch.arange(T, device=self.st.device, dtype=torch.int32)
+            self._plast = torch.tensor([T - 1], device=self.st.device, dtype=torch.int32)
+        return self._pbuf
+
+    def prefill_run(self, b: int, ids=None) -> None:
+        torch = _torch()
+        st, h = self.st, self._pbuf
+        T = h.shape[0]
+        if self.first:
+            st.embed_tokens(ids, h)
+        st.layers_forward(h, self._ppos, torch.full((T,), b, device=st.device, dtype=torch.int32), T)
+        if self.last:
+            st.head_forward(h, self.tokens[b], row_index=self._plast)
+
+
+# ------------------------------------------------------------------ the schedule
+class Pipeline:
+    """Stage `rank` of a `world`-stage pipeline over n_mb micro-batches."""
+
+    def __init__(self, rank: int, world: int, compute: StageCompute, channel, n_mb: int):
+        if world > 1 and n_mb < world:
+            raise ValueError(f"{n_mb} micro-batches cannot keep {world} stages busy")
+        self.rank, self.world, self.c, self.ch, self.n_mb = rank, world, compute, channel, n_mb
+        self.pending = [None] * n_mb  # last send of each micro-batch's output buffer
+        self.t = 0  # decode steps since the last prefill
+        self.host_io = None  # (host_in, host_out): pinned int32 token copies for host_io steps
+
+    def _wait_send(self, b):
+        if self.pending[b] is not None:
+            self.pending[b].wait()
+            self.pending[b] = None
+
+    def steps(self, n_steps: int, host_io: bool = False) -> None:
+        """n_steps decode steps: every micro-batch advances one token per step.
+        The last stage sends every token back to stage 0 (which embeds it at the
+        next step); finish() takes in the last step's tokens.  With host_io the
+        tokens also pass through pinned host memory as in a serving loop: stage 0
+        reads each token it receives back to the host and embeds the host copy
+        (one host synchronisation per micro-batch), and the last stage copies the
+        step's tokens to the host and synchronises at the end of the step."""
+        torch = _torch() if host_io else None
+        r, P, B, c, ch = self.rank, self.world, self.n_mb, self.c, self.ch
+        if host_io and self.host_io is None:
+            self.host_io = ([torch.zeros(1, dtype=torch.int32).pin_memory() for _ in range(B)],
+                            [torch.zeros(1, dtype=torch.int32).pin_memory() for _ in range(B)])
+        for _ in range(n_steps):
+            for b in range(B):
+                tok = c.token_buffer(b)
+                if P > 1:
+                    self._wait_send(b)  # the buffer is an input of this micro-batch again
+                    if r == 0:
+                        if self.t > 0:
+                            ch.irecv(tok, P - 1).wait()
+                    else:
+                        ch.irecv(c.hidden_buffer(b), r - 1).wait()
+                if host_io and r == 0:
+                    hin = self.host_io[0][b]
+                    hin.copy_(tok, non_blocking=True)
+                    torch.cuda.current_stream().synchronize()
+                    tok.copy_(hin, non_blocking=True)
+                c.run(b)
+                c.advance(b)
+                if host_io and r == P - 1:
+                    self.host_io[1][b].copy_(tok, non_blocking=True)
+                if P > 1:
+                    if r < P - 1:
+                        self.pending[b] = ch.isend(c.hidden_buffer(b), r + 1)
+                    else:
+                        self.pending[b] = ch.isend(tok, 0)
+            if host_io and r == P - 1:
+                torch.cuda.current_stream().synchronize()
+            self.t += 1
+
+    def finish(self) -> None:
+        """Ends a decode run: stage 0 takes in the last step's tokens (its token
+        buffers then hold every sequence's latest token), every stage waits for
+        its sends."""
+        if self.world > 1 and self.rank == 0 and self.t > 0:
+            for b in range(self.n_mb):
+                self.ch.irecv(self.c.token_buffer(b), self.world - 1).wait()
+        self.drain()
+        self.t = 0
+
+    def host_tokens(self):
+        """The last host_io step's tokens (last stage)."""
+        return [int(x) for x in self.host_io[1]] if self.host_io else None
+
+    def drain(self) -> None:
+        for b in range(self.n_mb):
+            self._wait_send(b)
+
+    def prefill(self, prompts: Optional[Sequence] = None, prompt_len: int = 0) -> None:
+        """Prefills micro-batch b with prompts[b] (stage 0 holds the prompts); the
+        first generated tokens end up in stage 0's token buffers.  The [T, hidden]
+        hand-off reuses one buffer per stage, so each send completes before the
+        next micro-batch overwrites it."""
+        r, P, B, c, ch = self.rank, self.world, self.n_mb, self.c, self.ch
+        T = len(prompts[0]) if prompts is not None else prompt_len
+        buf = c.prefill_buffer(T)
+        for b in range(B):
+            if r > 0:
+                ch.irecv(buf, r - 1).wait()
+            c.prefill_run(b, prompts[b] if r == 0 else None)
+            if r < P - 1:
+                ch.isend(buf, r + 1).wait()
+            elif P > 1:
+                self.pending[b] = ch.isend(c.token_buffer(b), 0)
+        if P > 1 and r == 0:
+            for b in range(B):
+                ch.irecv(c.token_buffer(b), P - 1).wait()
+        self.drain()
+        self.t = 0
+
+
+def even_split(n_layers: int, n_stages: int) -> List[range]:
+    """Contiguous, as even as possible (the first stages get the extra layers)."""
+    q, rem = divmod(n_layers, n_stages)
+    out, a = [], 0
+    for s in range(n_stages):
+        n = q + (1 if s < rem else 0)
+        out.append(range(a, a + n))
+        a += n
+    return out
+
+
+def stage_layers(n_layers: int, world: int, head_layers: float = 3.2,
+                 method: str = "planner") -> List[range]:
+    """Layer ranges per stage: the planner's bottleneck-balanced split (the head
+    counted as `head_layers` layers on the last stage) or an even split."""
+    if world == 1:
+        return [range(0, n_layers)]
+    if method == "even":
+        return even_split(n_layers, world)
+    from .planner import local_gpu_plan  # noqa: PLC0415
+    return local_gpu_plan(n_layers, world, head_layers=head_layers, link_latency_ms=0.0)

@@ -303,6 +303,71 @@ DIAL_API dial_status dial_decoder_head(const dial_decoder_dims* dims, const void
                                        void* logits, void* workspace, size_t workspace_bytes,
                                        dial_stream stream);
 
+/* ------------------------------------------------------------------ stage planner
+ * Host-only (no GPU needed).  Restates AutoPlanner::plan_with_algorithm
+ * (dial-core/src/spm/planner.rs:378-522, segment_cost :743-836): contiguous
+ * layer segments, each on a different device, chosen by an exact DP over
+ * (end layer, set of devices used, last device) under per-device memory
+ * limits, for one of three objectives.  Devices here are the local GPUs of
+ * one node; a worker's rtt/bandwidth/protocol describe the hand-off of a
+ * segment's hidden state (NVLink instead of the reference's TCP).  Extension:
+ * the model's head_* / embed_* costs (zero = the reference's cost model) are
+ * charged to the segment that ends at the last layer / starts at layer 0, which
+ * is where this pipeline keeps the output head and the embedding. */
+enum { DIAL_PLAN_DIAL = 0, DIAL_PLAN_EDGESHARD_LATENCY = 1, DIAL_PLAN_EDGESHARD_THROUGHPUT = 2 };
+enum { DIAL_PLAN_MASTER = 0, DIAL_PLAN_WORKER = 1 };
+#define DIAL_PLAN_MAX_DEVICES 12
+
+/* LayerMetric: per_layer[n_layers] when non-NULL, else `uniform` for every layer. */
+typedef struct dial_layer_metric {
+  const double* per_layer;
+  double uniform;
+} dial_layer_metric;
+
+typedef struct dial_plan_device {
+  int role;    /* DIAL_PLAN_MASTER / DIAL_PLAN_WORKER; exactly one enabled master */
+  int enabled;
+  double usable_memory_mb, fixed_memory_mb;
+  dial_layer_metric layer_memory_mb, prefill_ms, decode_ms;
+  int has_prefill_p95, has_decode_p95; /* else the mean profile */
+  dial_layer_metric prefill_p95_ms, decode_p95_ms;
+  dial_layer_metric prefill_energy_mj, decode_energy_mj;
+  double rtt_ms, protocol_ms, bandwidth_mbps;          /* workers only */
+  double rtt_p95_ms, protocol_p95_ms, bandwidth_p05_mbps; /* < 0: the mean value */
+} dial_plan_device;
+
+typedef struct dial_plan_objective {
+  int prompt_tokens, output_tokens, dtype_bytes;
+  int kv_context_tokens; /* 0: max_seq_len */
+  double ttft_weight, tpot_weight, risk_weight, energy_weight, remote_device_penalty;
+  int min_devices, max_devices; /* max_devices <= 0: every enabled device */
+} dial_plan_objective;
+
+typedef struct dial_plan_model {
+  int num_layers, hidden_size, num_attention_heads, num_key_value_heads, max_seq_len;
+  double head_memory_mb, head_prefill_ms, head_decode_ms;    /* segment ending at the last layer */
+  double embed_memory_mb, embed_prefill_ms, embed_decode_ms; /* segment starting at layer 0 */
+} dial_plan_model;
+
+typedef struct dial_plan_segment {
+  int device; /* index into the devices array */
+  int start_layer, end_layer; /* inclusive, as PlannedSegment */
+  double memory_mb, ttft_ms, tpot_ms, tail_ttft_ms, tail_tpot_ms;
+} dial_plan_segment;
+
+typedef struct dial_plan_result {
+  int n_segments;
+  dial_plan_segment segments[DIAL_PLAN_MAX_DEVICES];
+  double ttft_ms, tpot_ms, tail_ttft_ms, tail_tpot_ms, request_energy_mj, score;
+  int64_t states_considered, feasible_transitions, rejected_for_memory;
+} dial_plan_result;
+
+/* DIAL_ERR_INVALID_ARG with the reference's validation messages (dial_last_error)
+ * on a bad profile; DIAL_ERR_SHAPE when no placement fits in memory. */
+DIAL_API dial_status dial_plan_stages(const dial_plan_model* model, const dial_plan_objective* objective,
+                                      const dial_plan_device* devices, int n_devices, int algorithm,
+                                      dial_plan_result* out);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

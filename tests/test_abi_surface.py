@@ -37,8 +37,8 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_python_signatures_cover_header():
-    from dial_cuda import model
-    bound = set(D.SIGNATURES) | set(model._SIGS)
+    from dial_cuda import model, planner
+    bound = set(D.SIGNATURES) | set(model._SIGS) | set(planner._SIGS)
     assert set(declared_symbols()) <= bound, set(declared_symbols()) - bound
 
 

@@ -1,0 +1,157 @@
+"""Pipeline schedule on the CPU: world-size 2 and 3 gloo ranks, a stand-in for
+the stage compute, checked against the same chain run in one process.  Also
+the failure path: a rank that never joins makes its peers fail within the
+process-group timeout instead of hanging."""
+import os
+import socket
+import sys
+
+import pytest
+
+import torch
+import torch.multiprocessing as mp
+
+H, V = 8, 97
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class FakeCompute:
+    """Stage r of `world`: embedding (stage 0), a per-stage affine map, and a
+    token from the hidden state (last stage) -- deterministic f32 arithmetic."""
+
+    def __init__(self, r, world, n_mb):
+        self.r, self.world = r, world
+        self.first, self.last = r == 0, r == world - 1
+        self.hidden = [torch.zeros(1, H) for _ in range(n_mb)]
+        self.tokens = [torch.zeros(1, dtype=torch.int32) for _ in range(n_mb)]
+        self.pos = [0] * n_mb
+
+    @staticmethod
+    def embed(tok):
+        return (tok.float() + 1.0) * torch.arange(1, H + 1, dtype=torch.float32) / H
+
+    def layers(self, h, pos):
+        return h * 0.75 + 0.125 * (self.r + 1) + 0.01 * pos
+
+    @staticmethod
+    def sample(h):
+        return torch.tensor([int(h.sum().item() * 1000) % V], dtype=torch.int32)
+
+    def hidden_buffer(self, b):
+        return self.hidden[b]
+
+    def token_buffer(self, b):
+        return self.tokens[b]
+
+    def run(self, b):
+        if self.first:
+            self.hidden[b].copy_(self.embed(self.tokens[b]).view(1, H))
+        self.hidden[b].copy_(self.layers(self.hidden[b], self.pos[b]))
+        if self.last:
+            self.tokens[b].copy_(self.sample(self.hidden[b]))
+
+    def advance(self, b):
+        self.pos[b] += 1
+
+    def prefill_buffer(self, T):
+        self.pbuf = torch.zeros(T, H)
+        return self.pbuf
+
+    def prefill_run(self, b, ids=None):
+        if self.first:
+            self.pbuf.copy_(torch.stack([self.embed(torch.tensor(i)) for i in ids]))
+        self.pbuf.copy_(self.layers(self.pbuf, -1))
+        if self.last:
+            self.tokens[b].copy_(self.sample(self.pbuf[-1]))
+
+
+def reference(world, n_mb, prompts, steps):
+    """The same chain, every stage in one process."""
+    stages = [FakeCompute(r, world, n_mb) for r in range(world)]
+    out = []
+    for b in range(n_mb):
+        h = torch.stack([FakeCompute.embed(torch.tensor(i)) for i in prompts[b]])
+        for s in stages:
+            h = s.layers(h, -1)
+        tok = FakeCompute.sample(h[-1])
+        seq = [int(tok)]
+        for t in range(steps):
+            h = FakeCompute.embed(tok).view(1, H)
+            for s in stages:
+                h = s.layers(h, t)
+            tok = FakeCompute.sample(h)
+            seq.append(int(tok))
+        out.append(seq)
+    return out
+
+
+def _worker(rank, world, port, n_mb, prompts, steps, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "dial-8b-orin_b200"))
+    from dial_cuda.pipeline import Pipeline, TorchChannel, init_distributed
+    init_distributed("gloo", timeout_s=30)
+    c = FakeCompute(rank, world, n_mb)
+    p = Pipeline(rank, world, c, TorchChannel(), n_mb)
+    p.prefill(prompts if rank == 0 else None, prompt_len=len(prompts[0]))
+    firsts = [int(t) for t in c.tokens]
+    # two calls of one run, as the benchmark does (warm-up, then timed steps)
+    p.steps(2)
+    p.steps(steps - 2)
+    last = [int(t) for t in c.tokens]
+    p.finish()
+    torch.save({"firsts": firsts, "last": last, "after_finish": [int(t) for t in c.tokens]},
+               os.path.join(result_dir, f"r{rank}.pt"))
+    import torch.distributed as dist
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_pipeline_matches_single_process_chain(world, tmp_path):
+    n_mb, steps = 3, 5
+    prompts = [[(7 * b + 3 * i) % V for i in range(4)] for b in range(n_mb)]
+    mp.start_processes(_worker, args=(world, _free_port(), n_mb, prompts, steps, str(tmp_path)),
+                       nprocs=world, join=True, start_method="spawn")
+    ref = reference(world, n_mb, prompts, steps)
+    r0 = torch.load(tmp_path / "r0.pt")
+    rl = torch.load(tmp_path / f"r{world - 1}.pt")
+    assert r0["firsts"] == [seq[0] for seq in ref]          # prefill tokens reached stage 0
+    assert rl["last"] == [seq[-1] for seq in ref]           # last step's tokens on the last stage
+    assert r0["after_finish"] == [seq[-1] for seq in ref]   # finish() hands them to stage 0
+
+
+def test_pipeline_rejects_too_few_micro_batches():
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "dial-8b-orin_b200"))
+    from dial_cuda.pipeline import Pipeline
+    with pytest.raises(ValueError):
+        Pipeline(0, 4, FakeCompute(0, 4, 2), None, 2)
+
+
+def _lonely(rank, world, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "dial-8b-orin_b200"))
+    from dial_cuda.pipeline import init_distributed
+    try:
+        init_distributed("gloo", timeout_s=3)
+        msg = "joined"
+    except Exception as e:  # the peer never joins: rendezvous times out
+        msg = type(e).__name__
+    with open(os.path.join(result_dir, f"lonely{rank}.txt"), "w") as f:
+        f.write(msg)
+
+
+def test_missing_peer_fails_within_the_timeout(tmp_path):
+    """Rank 0 of a 2-rank group whose rank 1 never starts: it must give up."""
+    mp.start_processes(_lonely, args=(2, _free_port(), str(tmp_path)), nprocs=1, join=True,
+                       start_method="spawn")
+    assert (tmp_path / "lonely0.txt").read_text() != "joined"

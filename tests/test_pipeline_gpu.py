@@ -1,0 +1,136 @@
+"""Pipelined decode on the GPU.
+
+- One stage (world 1): the pipeline's schedule and CUDA graphs give the same
+  greedy tokens as Decoder.prefill/decode_step.
+- Two stages over NCCL (needs 2 GPUs; skipped otherwise): each rank holds half
+  the layers, and the tokens equal the single-GPU ones (the weights of a layer
+  do not depend on the split, and the arithmetic of a layer is the same).
+"""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+SMALL = dict(n_layers=4, hidden=1024, intermediate=2048, n_heads=8, n_kv_heads=2, head_dim=128,
+             vocab=4096, act_dtype="bf16")
+N_MB, PROMPT, STEPS = 4, 24, 6
+
+
+def _cfg():
+    from dial_cuda.model import ModelConfig
+    return ModelConfig(**SMALL)
+
+
+def _prompts(torch):
+    rng = np.random.default_rng(7)
+    return [torch.tensor(rng.integers(0, SMALL["vocab"], PROMPT).astype(np.int32), device="cuda")
+            for _ in range(N_MB)]
+
+
+def reference_tokens(torch):
+    """Greedy tokens of every sequence from the single-stage Decoder."""
+    from dial_cuda.model import Decoder
+    dec = Decoder(_cfg(), n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
+    out = []
+    for b, p in enumerate(_prompts(torch)):
+        tok = dec.prefill(p, slot=b)
+        seq = [int(tok.item())]
+        for t in range(STEPS):
+            o = torch.empty(1, dtype=torch.int32, device="cuda")
+            dec.decode_step(tok, torch.tensor([PROMPT + t], dtype=torch.int32, device="cuda"),
+                            torch.tensor([b], dtype=torch.int32, device="cuda"), PROMPT + STEPS + 8, o)
+            tok = o
+            seq.append(int(o.item()))
+        out.append(seq)
+    return out
+
+
+def test_single_stage_pipeline_matches_decoder(cuda):
+    import torch
+
+    from dial_cuda.model import Stage
+    from dial_cuda.pipeline import ModelStageCompute, Pipeline
+    ref = reference_tokens(torch)
+    cfg = _cfg()
+    st = Stage(cfg, 0, cfg.n_layers, n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
+    comp = ModelStageCompute(st, N_MB, PROMPT)
+    pipe = Pipeline(0, 1, comp, None, N_MB)
+    pipe.prefill(_prompts(torch))
+    assert [int(t.item()) for t in comp.tokens] == [s[0] for s in ref]
+    saved = [t.clone() for t in comp.tokens]
+    comp.capture()
+    for t, s in zip(comp.tokens, saved):
+        t.copy_(s)
+    pipe.steps(STEPS - 1)
+    pipe.steps(1, host_io=True)
+    torch.cuda.synchronize()
+    assert [int(t.item()) for t in comp.tokens] == [s[-1] for s in ref]
+    assert pipe.host_tokens() == [s[-1] for s in ref]
+
+
+def _two_stage_worker():
+    """Body of one rank (run by torchrun): prints this rank's tokens as JSON."""
+    import torch
+
+    from dial_cuda.model import Stage
+    from dial_cuda.pipeline import ModelStageCompute, Pipeline, TorchChannel, init_distributed
+    rank, local, world = init_distributed("nccl", timeout_s=60)
+    cfg = _cfg()
+    half = cfg.n_layers // 2
+    a, b = (0, half) if rank == 0 else (half, cfg.n_layers)
+    st = Stage(cfg, a, b, n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
+    comp = ModelStageCompute(st, N_MB, PROMPT)
+    pipe = Pipeline(rank, world, comp, TorchChannel(), N_MB)
+    pipe.prefill(_prompts(torch) if rank == 0 else None, prompt_len=PROMPT)
+    firsts = [int(t.item()) for t in comp.tokens]
+    saved = [t.clone() for t in comp.tokens]
+    comp.capture()
+    for t, s in zip(comp.tokens, saved):
+        t.copy_(s)
+    pipe.steps(STEPS)
+    torch.cuda.synchronize()
+    last = [int(t.item()) for t in comp.tokens]
+    pipe.finish()
+    import torch.distributed as dist
+    dist.barrier()
+    print(json.dumps({"rank": rank, "firsts": firsts, "last": last}), flush=True)
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_two_stage_pipeline_matches_single_gpu(cuda):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ref = reference_tokens(torch)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           os.path.abspath(__file__)]
+    out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
+    assert out.returncode == 0, out.stderr[-3000:]
+    res = {}
+    for line in out.stdout.splitlines():
+        if line.startswith("{"):
+            d = json.loads(line)
+            res[d["rank"]] = d
+    assert res[0]["firsts"] == [s[0] for s in ref]   # prefill tokens came back to stage 0
+    assert res[1]["last"] == [s[-1] for s in ref]    # last step's tokens on the last stage
+
+
+if __name__ == "__main__":  # a rank of the two-stage test
+    sys.path.insert(0, os.path.join(ROOT, "dial-8b-orin_b200"))
+    _two_stage_worker()

@@ -37,17 +37,33 @@ def _torch():
 
 # ------------------------------------------------------------------ channels
 class TorchChannel:
-    """Point-to-point sends over torch.distributed (the default process group)."""
+    """Point-to-point sends over torch.distributed, one process group per link:
+    fwd[s] carries stage s -> s+1, `ring` carries the last stage -> stage 0.
+    Separate groups are separate NCCL communicators with their own streams, so
+    a blocked send on one link never holds up another link's operations.
+    Every rank creates every group, in the same order (a torch requirement)."""
 
-    def __init__(self):
+    def __init__(self, world: Optional[int] = None):
         import torch.distributed as dist  # noqa: PLC0415
         self.dist = dist
+        self.rank = dist.get_rank()
+        P = world if world is not None else dist.get_world_size()
+        self.P = P
+        self.fwd = [dist.new_group([s, s + 1]) for s in range(P - 1)]
+        self.ring = dist.new_group([P - 1, 0]) if P > 1 else None
+
+    def _group(self, a: int, b: int):  # link a -> b
+        if b == a + 1:
+            return self.fwd[a]
+        if a == self.P - 1 and b == 0:
+            return self.ring
+        raise ValueError(f"no pipeline link {a} -> {b}")
 
     def isend(self, t, dst: int):
-        return self.dist.isend(t, dst)
+        return self.dist.isend(t, dst, group=self._group(self.rank, dst))
 
     def irecv(self, t, src: int):
-        return self.dist.irecv(t, src)
+        return self.dist.irecv(t, src, group=self._group(src, self.rank))
 
 
 def init_distributed(backend: str = "nccl", timeout_s: float = 120.0):

@@ -77,7 +77,7 @@ def test_single_stage_pipeline_matches_decoder(cuda):
 
 
 def _two_stage_worker():
-    """Body of one rank (run by torchrun): prints this rank's tokens as JSON."""
+    """Body of one rank (run by torchrun): writes this rank's tokens to DIAL_TEST_OUT."""
     import torch
 
     from dial_cuda.model import Stage
@@ -101,7 +101,8 @@ def _two_stage_worker():
     pipe.finish()
     import torch.distributed as dist
     dist.barrier()
-    print(json.dumps({"rank": rank, "firsts": firsts, "last": last}), flush=True)
+    with open(os.path.join(os.environ["DIAL_TEST_OUT"], f"rank{rank}.json"), "w") as f:
+        json.dump({"rank": rank, "firsts": firsts, "last": last}, f)
     dist.destroy_process_group()
 
 
@@ -111,22 +112,18 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_two_stage_pipeline_matches_single_gpu(cuda):
+def test_two_stage_pipeline_matches_single_gpu(cuda, tmp_path):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ref = reference_tokens(torch)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", DIAL_TEST_OUT=str(tmp_path))
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.abspath(__file__)]
     out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert out.returncode == 0, out.stderr[-3000:]
-    res = {}
-    for line in out.stdout.splitlines():
-        if line.startswith("{"):
-            d = json.loads(line)
-            res[d["rank"]] = d
+    res = {r: json.loads((tmp_path / f"rank{r}.json").read_text()) for r in (0, 1)}
     assert res[0]["firsts"] == [s[0] for s in ref]   # prefill tokens came back to stage 0
     assert res[1]["last"] == [s[-1] for s in ref]    # last step's tokens on the last stage
 

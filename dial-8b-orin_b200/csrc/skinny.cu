@@ -591,12 +591,114 @@ __device__ __forceinline__ void tile_finish(const GemvPlan& pl, float* __restric
 // (kXsBytes at most) into shared memory once, with plain loads -- a bulk copy
 // would queue behind the weight prefetch in the SM's TMA unit -- and every
 // lane then reads its fragments from there instead of from L1/L2 on each unit.
+//
+// Staged activations are f16 whatever the input dtype, and the weights enter
+// the f16 MMA biased: 1152 + q, built from the byte by one byte permute under
+// the f16 exponent of 1024 (plus one xor per 4 bytes), without the subtraction
+// of the exact conversion.  Per row, sum_k (1152 + q_k) x_k - 1152 sum_k x_k is
+// the wanted sum_k q_k x_k; the sums of x per 128-wide group are staged next
+// to x (fixed order, so results stay deterministic) and subtracted per segment.
+// Every (1152 + q) x product is exact in f32, as the plain products are; the
+// sums are rounded at a larger magnitude, a relative change of about 1e-5 of
+// the result, below the f16/bf16 rounding of the output.  bf16 inputs are
+// scaled per token by a power of two that puts max|x| in [2^13, 2^14) and
+// rounded to f16 (exact for every value within 2^27 of the max); the output
+// is scaled back by the same power of two.
 constexpr int kXsBytes = 32 * 1024;
-constexpr int kXsSmem = kTmaSmem + kXsBytes;
+constexpr int kXsAux = 1024 + 128;  // group sums (<= 160 floats) + per-token scale (<= 32 floats)
+constexpr int kXsSmem = kTmaSmem + kXsBytes + kXsAux;
+constexpr float kQBias = 1152.0f;
 
 // Barrier 1 over the first `threads` threads of the CTA (the warps with work).
 __device__ __forceinline__ void active_warps_sync(int threads) {
   asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+__device__ __forceinline__ float lds32f(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts32f(uint32_t a, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+
+// Four int8 -> two f16x2 holding 1152 + q (exact).
+__device__ __forceinline__ void i8x4_to_f16x2_biased(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  lo = prmt(u, 0x64646464u, 0x4140u);
+  hi = prmt(u, 0x64646464u, 0x4342u);
+}
+
+// Power-of-two exponent e with 2^13 <= max|x| * 2^-e < 2^14 (0 for a zero or
+// non-finite max): every bf16 value within 2^27 of the row's max is then an f16
+// normal number, so the rounding to f16 is exact for all but negligible values.
+__device__ __forceinline__ int tok_exp(float mx) {
+  return (mx > 0.0f && isfinite(mx)) ? ilogbf(mx) - 13 : 0;
+}
+
+// Stages x [M, K] (f16 or bf16 bits) as f16 into xsm, per-group sums into gs
+// [ng][M] and per-token output multipliers into tm [M].  Run by the CTA's first
+// `active` threads; ends with the barrier.
+template <bool BF16>
+__device__ __forceinline__ void stage_x(const uint16_t* __restrict__ x, int M, int K, int ng,
+                                        uint32_t xsm, uint32_t gs, uint32_t tm, int active) {
+  const int tid = threadIdx.x, n16 = M * K / 8, per_tok = K / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  if (BF16) {
+    if (tid < M) sts32f(tm + 4u * tid, 0.0f);  // running max |x| per token (bits compare as ints)
+    active_warps_sync(active);
+    for (int c = tid; c < n16; c += active) {
+      const uint4 v = ld_ro16(src + c);
+      uint32_t m = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t wv = word(v, i);
+        m = max(m, max((wv << 16) & 0x7FFFFFFFu, wv & 0x7FFF0000u));  // |bf16| as f32 bits
+      }
+      atomicMax(reinterpret_cast<unsigned int*>(__cvta_shared_to_generic(tm + 4u * (c / per_tok))), m);
+    }
+    active_warps_sync(active);
+    for (int c = tid; c < n16; c += active) {
+      const float mx = __uint_as_float(reinterpret_cast<const unsigned int*>(__cvta_shared_to_generic(tm))[c / per_tok]);
+      const int e = tok_exp(mx);
+      const uint4 v = ld_ro16(src + c);
+      uint4 o;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t wv = word(v, i);
+        const float f0 = ldexpf(__uint_as_float(wv << 16), -e), f1 = ldexpf(__uint_as_float(wv & 0xFFFF0000u), -e);
+        const __half2 h = __floats2half2_rn(f0, f1);
+        reinterpret_cast<uint32_t*>(&o)[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      sts16(xsm + 16u * (uint32_t)c, o);
+    }
+    active_warps_sync(active);
+    if (tid < M) {
+      const float mx = lds32f(tm + 4u * tid);
+      sts32f(tm + 4u * tid, ldexpf(1.0f, tok_exp(mx)));
+    }
+  } else {
+    for (int c = tid; c < n16; c += active) sts16(xsm + 16u * (uint32_t)c, ld_ro16(src + c));
+    if (tid < M) sts32f(tm + 4u * tid, 1.0f);
+    active_warps_sync(active);
+  }
+  // group sums in a fixed order: thread (g, m) adds its group's values in k order
+  for (int idx = tid; idx < ng * M; idx += active) {
+    const int gi = idx / M, m = idx - gi * M;
+    const int k0 = gi * 128, k1 = min(K, k0 + 128);
+    float s = 0.0f;
+    for (int k = k0; k < k1; k += 8) {
+      const uint4 v = lds16(xsm + 2u * (uint32_t)(m * K + k));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 h = *reinterpret_cast<const __half2*>(&reinterpret_cast<const uint32_t*>(&v)[i]);
+        s += __low2float(h);
+        s += __high2float(h);
+      }
+    }
+    sts32f(gs + 4u * (uint32_t)idx, s);
+  }
+  active_warps_sync(active);
 }
 
 // W8A16 unit: 16 rows x 128 K of int8 weights.  Lane (g, t) takes 16-byte
@@ -609,9 +711,10 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     w8a16_tma_kernel(const __grid_constant__ CUtensorMap wmap, const ST* __restrict__ scale,
                      const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int N, int K,
                      GemvPlan pl, float* __restrict__ slots, int* __restrict__ cnt, int* err) {
+  constexpr bool kF16Mma = XS || !BF16;  // staged activations are f16
   extern __shared__ uint8_t smem_raw[];
   const Ring ring = warp_ring(smem_raw);
-  const uint32_t xsm = ring_end(smem_raw);
+  const uint32_t xsm = ring_end(smem_raw), gs = xsm + kXsBytes, tm = gs + 1024;
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int wpc = blockDim.x >> 5;
   const int w = blockIdx.x * wpc + (threadIdx.x >> 5);
@@ -630,18 +733,25 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
   if (lane == 0)  // the weights are constant: prefetch before the previous kernel ends
     while (pr.issued < kStages && !pr.ended) pr.refill(ring, load);
   pdl_wait();  // x, y and the workspace belong to the stream's earlier kernels
-  if (XS) {
-    const int active = min(wpc, pl.NW - (int)blockIdx.x * wpc) * 32;  // warps 0.. of this CTA
-    const uint4* src = reinterpret_cast<const uint4*>(x);
-    const int n16 = M * K / 8;
-    for (int c = threadIdx.x; c < n16; c += active) sts16(xsm + 16u * (uint32_t)c, ld_ro16(src + c));
-    active_warps_sync(active);
-  }
+  if (XS) stage_x<BF16>(x, M, K, pl.ng, xsm, gs, tm, min(wpc, pl.NW - (int)blockIdx.x * wpc) * 32);
   auto store = [&](int tile, const float (&a)[NT][4]) {
-    w8a16_store<NT, BF16, ST>(a, scale, y, M, N, tile * 16);
+    if (XS && BF16) {  // undo the per-token power-of-two scale of the staged activations
+      float b[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const int t0 = j * 8 + 2 * t;
+        const float m0 = t0 < M ? lds32f(tm + 4u * t0) : 1.0f, m1 = t0 + 1 < M ? lds32f(tm + 4u * (t0 + 1)) : 1.0f;
+        b[j][0] = a[j][0] * m0, b[j][1] = a[j][1] * m1, b[j][2] = a[j][2] * m0, b[j][3] = a[j][3] * m1;
+      }
+      w8a16_store<NT, BF16, ST>(b, scale, y, M, N, tile * 16);
+    } else {
+      w8a16_store<NT, BF16, ST>(a, scale, y, M, N, tile * 16);
+    }
   };
   const uint16_t* xr[NT];
-  uint32_t xo[NT];  // XS: byte offset of this lane's token row in shared memory
+  uint32_t xo[NT];     // XS: byte offset of this lane's token row in shared memory
+  uint32_t so[NT][2];  // XS: group-sum offsets of the lane's two output tokens
+  bool sv[NT][2];      //     and whether those tokens exist
   bool tv[NT];
 #pragma unroll
   for (int j = 0; j < NT; ++j) {
@@ -649,9 +759,29 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     tv[j] = tok < M;
     xr[j] = x + (size_t)(tv[j] ? tok : 0) * K + 32 * t;
     xo[j] = xsm + (uint32_t)(((tv[j] ? tok : 0) * K + 32 * t) * 2);
+    const int t0 = j * 8 + 2 * t;
+    sv[j][0] = t0 < M, sv[j][1] = t0 + 1 < M;
+    so[j][0] = gs + 4u * (uint32_t)t0, so[j][1] = so[j][0] + 4u;
   }
-  float acc[NT][4];
+  float acc[NT][4], corr[NT][2];
   zero_acc(acc);
+  auto zero_corr = [&]() {
+#pragma unroll
+    for (int j = 0; j < NT; ++j) corr[j][0] = corr[j][1] = 0.0f;
+  };
+  auto apply_corr = [&]() {  // subtract the weight bias times the segment's x sums
+    if (XS) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        acc[j][0] = fmaf(-kQBias, corr[j][0], acc[j][0]);
+        acc[j][1] = fmaf(-kQBias, corr[j][1], acc[j][1]);
+        acc[j][2] = fmaf(-kQBias, corr[j][0], acc[j][2]);
+        acc[j][3] = fmaf(-kQBias, corr[j][1], acc[j][3]);
+      }
+      zero_corr();
+    }
+  };
+  zero_corr();
   const int first_tile = (int)div_u((uint64_t)ubegin(pl, w), (uint64_t)pl.ng);
   int cur = -1, units = 0;
   const uint4 z = make_uint4(0, 0, 0, 0);
@@ -665,7 +795,10 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     const int tile = (int)info.x, gi = (int)info.y;
     if (tile < 0) break;
     if (tile != cur) {
-      if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+      if (cur >= 0) {
+        apply_corr();
+        tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+      }
       zero_acc(acc);
       cur = tile;
       units = 0;
@@ -682,6 +815,9 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
         xv[j][1] = (tv[j] && v0) ? lds16(a + 16) : z;
         xv[j][2] = (tv[j] && v1) ? lds16(a + 32) : z;
         xv[j][3] = (tv[j] && v1) ? lds16(a + 48) : z;
+        const uint32_t go = 4u * (uint32_t)(gi * M);
+        if (sv[j][0]) corr[j][0] += lds32f(so[j][0] + go);
+        if (sv[j][1]) corr[j][1] += lds32f(so[j][1] + go);
       } else {
         xv[j][0] = (tv[j] && v0) ? ld_ro16(xr[j] + kb) : z;
         xv[j][1] = (tv[j] && v0) ? ld_ro16(xr[j] + kb + 8) : z;
@@ -700,7 +836,10 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
       for (int st = 0; st < 4; ++st) {
         const uint32_t wl = word(h ? al1 : al0, st), wh = word(h ? ah1 : ah0, st);
         uint32_t a0, a1, a2, a3;
-        if (BF16) {
+        if (XS) {
+          i8x4_to_f16x2_biased(wl, a0, a2);
+          i8x4_to_f16x2_biased(wh, a1, a3);
+        } else if (BF16) {
           i8x4_to_bf16x2(wl, a0, a2);
           i8x4_to_bf16x2(wh, a1, a3);
         } else {
@@ -711,13 +850,16 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
         for (int j = 0; j < NT; ++j) {
           const uint4& xs = xv[j][2 * h + (st >> 1)];
           const uint32_t b0 = word(xs, 2 * (st & 1)), b1 = word(xs, 2 * (st & 1) + 1);
-          if (BF16) mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
-          else mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
+          if (kF16Mma) mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
+          else mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
         }
       }
     }
   }
-  if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+  if (cur >= 0) {
+    apply_corr();
+    tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+  }
 }
 
 template <int NT, int TYPE, typename YT>
@@ -998,7 +1140,7 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
     const int wpc = tma_warps_per_cta(pl.NW);
     const dim3 grid((unsigned)((pl.NW + wpc - 1) / wpc)), block((unsigned)(wpc * 32));
     const bool xs = M * K * 2 <= kXsBytes && aligned16(x);
-    const size_t smem = (size_t)ring_bytes(wpc) + 1024 + (xs ? kXsBytes : 0);
+    const size_t smem = (size_t)ring_bytes(wpc) + 1024 + (xs ? kXsBytes + kXsAux : 0);
     cudaError_t ae = cudaSuccess;
 #define SKX(NT_, BF, ST, XS)                                                                   \
   ae = ensure_smem<w8a16_tma_kernel<NT_, BF, ST, XS>>(XS ? kXsSmem : kTmaSmem);                \

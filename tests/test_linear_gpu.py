@@ -118,6 +118,23 @@ def test_w8a16_linear_streamk_shapes(D, torch, M, N, K):
     assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
 
 
+@pytest.mark.parametrize("amax", [3e4, 1e6, 2.0**-20])
+def test_w8a16_bf16_activation_range(D, torch, amax):
+    """bf16 activations far outside the f16 range (and tiny ones) on the decode
+    path, which stages them as f16 under a per-token power-of-two scale."""
+    rng = np.random.default_rng(int(amax) % 1000 + 5)
+    N, K = 512, 4096
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    x = rng.normal(0, 1, (2, K)).astype(np.float32)
+    x *= amax / np.abs(x).max(axis=1, keepdims=True)
+    lin = D.W8A16Linear.from_linear("t", _to_dev(torch, w))
+    xb = O.f32_to_bf16(x)
+    y_ref, _ = O.w8a16_linear(xb, lin.qweight.cpu().numpy(), lin.scales.cpu().numpy(), x_is_bf16=True)
+    y = lin.forward(_to_dev(torch, xb.view(np.int16)).view(torch.bfloat16)).float().cpu().numpy()
+    assert np.isfinite(y).all()
+    assert rel_err(y, y_ref) <= 8e-3
+
+
 def test_w8a16_decode_config1_shape(D, torch):
     """BASELINE config 1 shape: x f16 [1,4096] ~N(0,1), W [12288,4096] ~N(0,0.02), f16 scale."""
     rng = np.random.default_rng(299792458)

@@ -44,6 +44,10 @@ cudaError_t ensure_smem(int bytes) {
   const uint64_t bit = 1ull << (dev & 63);
   if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
   e = cudaFuncSetAttribute(KERN, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  // the largest shared-memory carveout, so that two such CTAs can share an SM
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(KERN, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
   return e;
 }

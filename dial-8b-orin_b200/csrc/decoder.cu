@@ -31,6 +31,7 @@ struct Ws {
   uint8_t* q;       // [T, Hq D]
   uint8_t* attn;    // [T, Hq D]
   uint8_t* delta;   // [T, H]  (o, then down output)
+  uint8_t* h2;      // [T, H]  second residual buffer of the fused decode path
   uint8_t* gu;      // [T, 2I]
   uint8_t* mid;     // [T, I]
   uint8_t* attn_ws; // attention partials
@@ -57,6 +58,7 @@ Ws layout(const dial_decoder_dims& d, int64_t T, int64_t max_len, uint8_t* base)
   w.q = take(T * QD * e);
   w.attn = take(T * QD * e);
   w.delta = take(T * H * e);
+  w.h2 = take(T * H * e);
   w.gu = take(T * 2 * I * e);
   w.mid = take(T * I * e);
   w.attn_ws = take(attention_workspace_bytes(T, d.n_heads, max_len));
@@ -69,11 +71,17 @@ Ws layout(const dial_decoder_dims& d, int64_t T, int64_t max_len, uint8_t* base)
 }
 
 // One quantised linear y[T, N] = x[T, K] W^T in the stage's weight format.
+// `pro` (W8A16 decode only, see fused_decode_ok) makes the GEMV compute its own
+// input from x (rmsnorm / swiglu prologue).
 dial_status linear(const dial_decoder_dims& d, int fmt, dial_linear_ref W, const void* x, void* y,
-                   int64_t T, int64_t K, int64_t N, void* lin_ws, void* sk_ws, cudaStream_t st) {
+                   int64_t T, int64_t K, int64_t N, void* lin_ws, void* sk_ws, cudaStream_t st,
+                   const ActPrologue* pro = nullptr) {
   const dial_dtype xdt = (dial_dtype)d.act_dtype;
   if (fmt == DIAL_WFMT_W8A16 || fmt == DIAL_WFMT_W8A16_F16S) {
     const dial_dtype sdt = fmt == DIAL_WFMT_W8A16 ? DIAL_F32 : DIAL_F16;
+    if (pro)
+      return launch_w8a16_skinny(x, xdt, static_cast<const int8_t*>(W.w), W.s, sdt, y, T, K, N, st,
+                                 sk_ws, pro);
     if (T > kSkinnyMaxM && gemm_sm100_supported(T, K, N))
       return launch_w8a16_gemm_sm100(x, xdt, static_cast<const int8_t*>(W.w), W.s, sdt, y, T, K, N,
                                      st);
@@ -98,6 +106,15 @@ dial_status linear(const dial_decoder_dims& d, int fmt, dial_linear_ref W, const
     if (s != DIAL_OK) return s;
   }
   return DIAL_OK;
+}
+
+// Decode fast path: W8A16 layers and T rows small enough for the GEMV's staged
+// prologue at every input width; rmsnorm and swiglu then run inside the GEMVs.
+bool fused_decode_ok(const dial_decoder_dims& d, int64_t T) {
+  const bool w8 = d.weight_format == DIAL_WFMT_W8A16 || d.weight_format == DIAL_WFMT_W8A16_F16S;
+  const int64_t QD = (int64_t)d.n_heads * d.head_dim;
+  return w8 && d.act_dtype != DIAL_F32 && T <= kSkinnyMaxM && w8a16_prologue_ok(T, d.hidden) &&
+         w8a16_prologue_ok(T, d.intermediate) && w8a16_prologue_ok(T, QD);
 }
 
 dial_status check_dims(const dial_decoder_dims* d) {
@@ -155,6 +172,43 @@ dial_status dial_decoder_layers(const dial_decoder_dims* dims, const dial_layer_
   const dial_dtype dt = (dial_dtype)d.act_dtype;
   const int64_t H = d.hidden, I = d.intermediate, D = d.head_dim, T = tokens;
   const int64_t QKV = (int64_t)(d.n_heads + 2 * d.n_kv_heads) * D, QD = (int64_t)d.n_heads * D;
+  if (fused_decode_ok(d, T)) {
+    // residual stream in two buffers: the rmsnorm prologue writes x + res to
+    // the buffer that is not an input, so no GEMV CTA reads what another writes
+    void* h_cur = hidden;
+    void* h_buf[2] = {hidden, w.h2};
+    for (int li = 0; li < n_layers; ++li) {
+      const dial_layer_weights& L = layers[li];
+      void* h_next = h_cur == h_buf[0] ? h_buf[1] : h_buf[0];
+      const ActPrologue rms1{kProRms, li ? static_cast<const uint16_t*>(h_cur) : nullptr,
+                             li ? static_cast<uint16_t*>(h_next) : nullptr,
+                             static_cast<const uint16_t*>(L.input_norm), d.rms_eps};
+      if ((s = linear(d, d.weight_format, L.qkv, li ? w.delta : h_cur, w.qkv, T, H, QKV, w.lin_ws, w.sk,
+                      st, &rms1)) != DIAL_OK)
+        return s;
+      if (li) h_cur = h_next, h_next = h_cur == h_buf[0] ? h_buf[1] : h_buf[0];
+      if ((s = launch_qk_rope_kv(w.qkv, L.q_norm, L.k_norm, cos_t, sin_t, positions, slots, w.q,
+                                 L.k_cache, L.v_cache, dt, T, d.n_heads, d.n_kv_heads, d.max_seq,
+                                 d.rms_eps, d.qk_norm, st)) != DIAL_OK)
+        return s;
+      if ((s = launch_attention(w.q, L.k_cache, L.v_cache, positions, slots, w.attn, w.attn_ws, dt, T,
+                                d.n_heads, d.n_kv_heads, d.max_seq, max_len, st)) != DIAL_OK)
+        return s;
+      if ((s = linear(d, d.weight_format, L.o, w.attn, w.delta, T, QD, H, w.lin_ws, w.sk, st)) != DIAL_OK)
+        return s;
+      const ActPrologue rms2{kProRms, static_cast<const uint16_t*>(h_cur), static_cast<uint16_t*>(h_next),
+                             static_cast<const uint16_t*>(L.post_norm), d.rms_eps};
+      if ((s = linear(d, d.weight_format, L.gate_up, w.delta, w.gu, T, H, 2 * I, w.lin_ws, w.sk, st,
+                      &rms2)) != DIAL_OK)
+        return s;
+      h_cur = h_next;
+      const ActPrologue glu{kProSwiglu, nullptr, nullptr, nullptr, 0.0f};
+      if ((s = linear(d, d.weight_format, L.down, w.gu, w.delta, T, I, H, w.lin_ws, w.sk, st, &glu)) !=
+          DIAL_OK)
+        return s;
+    }
+    return launch_add(hidden, h_cur, w.delta, dt, T * H, st);  // h = h + d of the last layer
+  }
   for (int li = 0; li < n_layers; ++li) {
     const dial_layer_weights& L = layers[li];
     // x1 = rms_1(h + pending delta of the previous layer)
@@ -177,7 +231,7 @@ dial_status dial_decoder_layers(const dial_decoder_dims* dims, const dial_layer_
     if ((s = launch_swiglu(w.gu, w.mid, dt, T, I, st)) != DIAL_OK) return s;
     if ((s = linear(d, d.weight_format, L.down, w.mid, w.delta, T, I, H, w.lin_ws, w.sk, st)) != DIAL_OK) return s;
   }
-  return launch_add(hidden, w.delta, dt, T * H, st);  // h = h + d of the last layer
+  return launch_add(hidden, hidden, w.delta, dt, T * H, st);  // h = h + d of the last layer
 }
 
 dial_status dial_decoder_head(const dial_decoder_dims* dims, const void* final_norm,
@@ -197,6 +251,14 @@ dial_status dial_decoder_head(const dial_decoder_dims* dims, const void* final_n
   cudaStream_t st = as_stream(stream);
   const dial_dtype dt = (dial_dtype)d.act_dtype;
   const int64_t H = d.hidden, V = d.vocab;
+  void* lg = logits ? logits : w.logits;
+  const bool w8head = d.head_format == DIAL_WFMT_W8A16 || d.head_format == DIAL_WFMT_W8A16_F16S;
+  if (!row_index && w8head && d.act_dtype != DIAL_F32 && rows <= kSkinnyMaxM && w8a16_prologue_ok(rows, H)) {
+    const ActPrologue fin{kProRms, nullptr, nullptr, static_cast<const uint16_t*>(final_norm), d.rms_eps};
+    if ((s = linear(d, d.head_format, head, hidden, lg, rows, H, V, w.lin_ws, w.sk, st, &fin)) != DIAL_OK)
+      return s;
+    return launch_argmax(lg, out_ids, dt, rows, V, st);
+  }
   const void* src = hidden;
   if (row_index) {
     if ((s = launch_gather_rows(hidden, row_index, w.delta, dt, rows, H, st)) != DIAL_OK) return s;
@@ -204,7 +266,6 @@ dial_status dial_decoder_head(const dial_decoder_dims* dims, const void* final_n
   }
   if ((s = launch_rmsnorm(src, nullptr, nullptr, final_norm, w.x1, dt, rows, H, d.rms_eps, st)) != DIAL_OK)
     return s;
-  void* lg = logits ? logits : w.logits;
   if ((s = linear(d, d.head_format, head, w.x1, lg, rows, H, V, w.lin_ws, w.sk, st)) != DIAL_OK) return s;
   return launch_argmax(lg, out_ids, dt, rows, V, st);
 }

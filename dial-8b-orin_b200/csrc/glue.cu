@@ -298,13 +298,14 @@ __global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int
   }
 }
 
-// h = round(h + d), the residual add after the last layer of a stage (text.rs:1672-1674)
+// out = round(a + b), the residual add after the last layer of a stage
+// (text.rs:1672-1674); out may be a.
 template <typename T>
-__global__ void add_kernel(T* __restrict__ h, const T* __restrict__ d, int64_t n) {
+__global__ void add_kernel(T* out, const T* a, const T* __restrict__ b, int64_t n) {
   pdl_begin();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
-    h[i] = rnd<T>(ld(h, i) + ld(d, i));
+    out[i] = rnd<T>(ld(a, i) + ld(b, i));
 }
 
 template <typename T>
@@ -507,11 +508,12 @@ dial_status launch_gather_rows(const void* src, const int32_t* idx, void* dst, d
   return s;
 }
 
-dial_status launch_add(void* h, const void* d, dial_dtype dt, int64_t n, cudaStream_t st) {
+dial_status launch_add(void* out, const void* a, const void* b, dial_dtype dt, int64_t n,
+                       cudaStream_t st) {
   dial_status s = DIAL_OK;
   DISPATCH_T(dt, {
     s = launch_pdl("add_kernel", add_kernel<T>, dim3(grid_cap(n, 256)), dim3(256), 0, st,
-                   static_cast<T*>(h), static_cast<const T*>(d), n);
+                   static_cast<T*>(out), static_cast<const T*>(a), static_cast<const T*>(b), n);
   });
   return s;
 }

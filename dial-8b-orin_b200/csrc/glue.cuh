@@ -25,7 +25,9 @@ dial_status launch_swiglu(const void* gu, void* out, dial_dtype dt, int64_t toke
                           cudaStream_t st);
 dial_status launch_gather_rows(const void* src, const int32_t* idx, void* dst, dial_dtype dt,
                                int64_t rows, int64_t dim, cudaStream_t st);
-dial_status launch_add(void* h, const void* d, dial_dtype dt, int64_t n, cudaStream_t st);
+// out = round(a + b) elementwise; out may alias a.
+dial_status launch_add(void* out, const void* a, const void* b, dial_dtype dt, int64_t n,
+                       cudaStream_t st);
 dial_status launch_embedding(const void* table, const int32_t* ids, void* out, dial_dtype dt,
                              int64_t tokens, int64_t vocab, int64_t dim, cudaStream_t st);
 dial_status launch_argmax(const void* x, int32_t* out, dial_dtype dt, int64_t rows, int64_t n,

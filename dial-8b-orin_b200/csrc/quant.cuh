@@ -25,9 +25,26 @@ constexpr int kSkinnyMaxM = 32;
 // before the first call; every call leaves it zero.  sk_ws == NULL selects the
 // in-CTA K split instead (no scratch).
 size_t gemv_workspace_bytes(int64_t N);
+
+// Decode-path prologue of the W8A16 GEMV: its activation staging computes the
+// linear's input instead of reading it (the separate rmsnorm / swiglu kernels
+// then need not run).  kProRms: input = rmsnorm(x + res) * w, and x + res
+// (rounded) is written to h_out, which must not alias x or res.  kProSwiglu:
+// x is gate_up [M, 2K] and input = swiglu(gate, up).  Needs the staged path
+// (M * K * 2 <= 32 KiB, a workspace, 16-byte aligned pointers).
+enum { kProX = 0, kProRms = 1, kProSwiglu = 2 };
+struct ActPrologue {
+  int mode;
+  const uint16_t* res;
+  uint16_t* h_out;
+  const uint16_t* w;
+  float eps;
+};
+bool w8a16_prologue_ok(int64_t M, int64_t K);
+
 dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
                                 dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
-                                cudaStream_t st, void* sk_ws);
+                                cudaStream_t st, void* sk_ws, const ActPrologue* pro = nullptr);
 // GGUF integer path: activations quantised to Q8_0 in `ws` first.
 size_t gguf_skinny_workspace_bytes(int64_t M, int64_t K);
 dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,

@@ -605,8 +605,6 @@ __device__ __forceinline__ void tile_finish(const GemvPlan& pl, float* __restric
 // rounded to f16 (exact for every value within 2^27 of the max); the output
 // is scaled back by the same power of two.
 constexpr int kXsBytes = 32 * 1024;
-constexpr int kXsAux = 1024 + 128;  // group sums (<= 160 floats) + per-token scale (<= 32 floats)
-constexpr int kXsSmem = kTmaSmem + kXsBytes + kXsAux;
 constexpr float kQBias = 1152.0f;
 
 // Barrier 1 over the first `threads` threads of the CTA (the warps with work).
@@ -636,68 +634,145 @@ __device__ __forceinline__ int tok_exp(float mx) {
   return (mx > 0.0f && isfinite(mx)) ? ilogbf(mx) - 13 : 0;
 }
 
-// Stages x [M, K] (f16 or bf16 bits) as f16 into xsm, per-group sums into gs
-// [ng][M] and per-token output multipliers into tm [M].  Run by the CTA's first
-// `active` threads; ends with the barrier.
 template <bool BF16>
-__device__ __forceinline__ void stage_x(const uint16_t* __restrict__ x, int M, int K, int ng,
-                                        uint32_t xsm, uint32_t gs, uint32_t tm, int active) {
-  const int tid = threadIdx.x, n16 = M * K / 8, per_tok = K / 8;
-  const uint4* src = reinterpret_cast<const uint4*>(x);
-  if (BF16) {
-    if (tid < M) sts32f(tm + 4u * tid, 0.0f);  // running max |x| per token (bits compare as ints)
-    active_warps_sync(active);
+__device__ __forceinline__ float act_f32(uint32_t bits16) {
+  return BF16 ? __uint_as_float(bits16 << 16) : __half2float(__ushort_as_half((unsigned short)bits16));
+}
+template <bool BF16>
+__device__ __forceinline__ uint32_t act_rnd(float v) {
+  return BF16 ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v))
+              : (uint32_t)__half_as_ushort(__float2half_rn(v));
+}
+__device__ __forceinline__ uint32_t h16(const uint4& v, int i) {  // 16-bit element i of 8
+  return (word(v, i >> 1) >> (16 * (i & 1))) & 0xFFFFu;
+}
+__device__ __forceinline__ uint4 pack8(const uint32_t (&o)[8]) {
+  return make_uint4(o[0] | (o[1] << 16), o[2] | (o[3] << 16), o[4] | (o[5] << 16), o[6] | (o[7] << 16));
+}
+
+// Shared-memory scratch of the staging, after x: group sums [ng][M] (<= 160
+// floats), per-token multipliers [M], per-token 1/rms [M], per-chunk sums
+// [M*K/8] (<= 2048 floats).
+constexpr int kAuxGs = 0, kAuxTm = 1024, kAuxInv = 1152, kAuxCs = 1280;
+constexpr int kXsAux = kAuxCs + 2048 * 4;
+constexpr int kXsSmem = kTmaSmem + kXsBytes + kXsAux;
+
+// Stages the linear's input for rows [0, M) as f16 into xsm (see the section
+// comment), with the per-group sums and per-token multipliers for the kernel.
+// The input is p.mode's function of x: x itself; rmsnorm(x + res) * w (the
+// sum h = x + res, rounded to the activation dtype, also written to h_out by
+// CTA 0); or swiglu of gate_up = x [M, 2K].  Rounding follows the standalone
+// kernels (rmsnorm_kernel, swiglu_kernel): every tensor those produce is
+// rounded to the activation dtype here too.  The sums of squares of a row are
+// added in a fixed order (per chunk, then per warp lane, then a shuffle tree),
+// so the staged values do not depend on timing.  Run by the CTA's first
+// `active` threads; ends with a barrier.
+template <bool BF16>
+__device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* __restrict__ x, int M,
+                                          int K, int ng, uint32_t xsm, uint32_t aux, int active) {
+  const uint32_t gs = aux + kAuxGs, tm = aux + kAuxTm, tinv = aux + kAuxInv, cs = aux + kAuxCs;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarp = active >> 5;
+  const int per_tok = K / 8, n16 = M * per_tok;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  if (tid < M) sts32f(tm + 4u * tid, 0.0f);  // running max |input| per token (bits compare as ints)
+  if (p.mode == kProRms) {
     for (int c = tid; c < n16; c += active) {
-      const uint4 v = ld_ro16(src + c);
-      uint32_t m = 0;
+      const int m = c / per_tok;
+      const size_t off = (size_t)m * K + (size_t)(c - m * per_tok) * 8;
+      const uint4 xv = ld_ro16(x + off), rv = p.res ? ld_ro16(p.res + off) : z;
+      uint32_t o[8];
+      float ss = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t wv = word(v, i);
-        m = max(m, max((wv << 16) & 0x7FFFFFFFu, wv & 0x7FFF0000u));  // |bf16| as f32 bits
+      for (int i = 0; i < 8; ++i) {
+        float h = act_f32<BF16>(h16(xv, i));
+        if (p.res) h = act_f32<BF16>(act_rnd<BF16>(h + act_f32<BF16>(h16(rv, i))));
+        o[i] = act_rnd<BF16>(h);
+        ss += h * h;
       }
-      atomicMax(reinterpret_cast<unsigned int*>(__cvta_shared_to_generic(tm + 4u * (c / per_tok))), m);
+      const uint4 hv = pack8(o);
+      if (blockIdx.x == 0 && p.h_out) *reinterpret_cast<uint4*>(p.h_out + off) = hv;
+      sts16(xsm + 16u * (uint32_t)c, hv);
+      sts32f(cs + 4u * (uint32_t)c, ss);
     }
     active_warps_sync(active);
+    for (int m = warp; m < M; m += nwarp) {
+      float s = 0.0f;
+      for (int c = lane; c < per_tok; c += 32) s += lds32f(cs + 4u * (uint32_t)(m * per_tok + c));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) sts32f(tinv + 4u * m, rsqrtf(s / (float)K + p.eps));
+    }
+  } else if (p.mode == kProSwiglu) {
     for (int c = tid; c < n16; c += active) {
-      const float mx = __uint_as_float(reinterpret_cast<const unsigned int*>(__cvta_shared_to_generic(tm))[c / per_tok]);
-      const int e = tok_exp(mx);
-      const uint4 v = ld_ro16(src + c);
-      uint4 o;
+      const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
+      const uint16_t* gu = x + (size_t)m * 2 * K;
+      const uint4 gv = ld_ro16(gu + k8), uv = ld_ro16(gu + K + k8);
+      uint32_t o[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t wv = word(v, i);
-        const float f0 = ldexpf(__uint_as_float(wv << 16), -e), f1 = ldexpf(__uint_as_float(wv & 0xFFFF0000u), -e);
-        const __half2 h = __floats2half2_rn(f0, f1);
-        reinterpret_cast<uint32_t*>(&o)[i] = *reinterpret_cast<const uint32_t*>(&h);
+      for (int i = 0; i < 8; ++i) {
+        const float gg = act_f32<BF16>(h16(gv, i));
+        const float s = act_f32<BF16>(act_rnd<BF16>(gg / (1.0f + expf(-gg))));
+        o[i] = act_rnd<BF16>(s * act_f32<BF16>(h16(uv, i)));
       }
-      sts16(xsm + 16u * (uint32_t)c, o);
+      sts16(xsm + 16u * (uint32_t)c, pack8(o));
     }
-    active_warps_sync(active);
-    if (tid < M) {
-      const float mx = lds32f(tm + 4u * tid);
-      sts32f(tm + 4u * tid, ldexpf(1.0f, tok_exp(mx)));
-    }
-  } else {
-    for (int c = tid; c < n16; c += active) sts16(xsm + 16u * (uint32_t)c, ld_ro16(src + c));
-    if (tid < M) sts32f(tm + 4u * tid, 1.0f);
-    active_warps_sync(active);
   }
-  // group sums in a fixed order: thread (g, m) adds its group's values in k order
+  active_warps_sync(active);
+  // the input values of chunk c, as floats (exact in the activation dtype)
+  auto input8 = [&](int c, float (&v)[8]) {
+    const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
+    if (p.mode == kProX) {
+      const uint4 xv = ld_ro16(x + (size_t)m * K + k8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(xv, i));
+    } else if (p.mode == kProRms) {
+      const uint4 hv = lds16(xsm + 16u * (uint32_t)c), wv = ld_ro16(p.w + k8);
+      const float inv = lds32f(tinv + 4u * m);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[i] = act_f32<BF16>(act_rnd<BF16>(act_f32<BF16>(h16(hv, i)) * inv * act_f32<BF16>(h16(wv, i))));
+    } else {
+      const uint4 yv = lds16(xsm + 16u * (uint32_t)c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(yv, i));
+    }
+  };
+  for (int c = tid; c < n16; c += active) {
+    float v[8];
+    input8(c, v);
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[i]));
+    atomicMax(reinterpret_cast<unsigned int*>(__cvta_shared_to_generic(tm + 4u * (c / per_tok))),
+              __float_as_uint(mx));
+  }
+  active_warps_sync(active);
+  for (int c = tid; c < n16; c += active) {
+    float v[8];
+    input8(c, v);
+    const int e = tok_exp(__uint_as_float(
+        reinterpret_cast<const unsigned int*>(__cvta_shared_to_generic(tm))[c / per_tok]));
+    uint32_t o[8];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const __half h = __float2half_rn(ldexpf(v[i], -e));
+      o[i] = __half_as_ushort(h);
+      s += __half2float(h);
+    }
+    sts16(xsm + 16u * (uint32_t)c, pack8(o));
+    sts32f(cs + 4u * (uint32_t)c, s);
+  }
+  active_warps_sync(active);
+  // group sums: thread (g, m) adds the chunk sums of its group in k order
   for (int idx = tid; idx < ng * M; idx += active) {
     const int gi = idx / M, m = idx - gi * M;
-    const int k0 = gi * 128, k1 = min(K, k0 + 128);
+    const int c0 = m * per_tok + gi * 16, c1 = m * per_tok + min(per_tok, gi * 16 + 16);
     float s = 0.0f;
-    for (int k = k0; k < k1; k += 8) {
-      const uint4 v = lds16(xsm + 2u * (uint32_t)(m * K + k));
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __half2 h = *reinterpret_cast<const __half2*>(&reinterpret_cast<const uint32_t*>(&v)[i]);
-        s += __low2float(h);
-        s += __high2float(h);
-      }
-    }
+    for (int c = c0; c < c1; ++c) s += lds32f(cs + 4u * (uint32_t)c);
     sts32f(gs + 4u * (uint32_t)idx, s);
   }
+  if (tid < M) sts32f(tm + 4u * tid, ldexpf(1.0f, tok_exp(lds32f(tm + 4u * tid))));
   active_warps_sync(active);
 }
 
@@ -710,11 +785,12 @@ template <int NT, bool BF16, typename ST, bool XS>
 __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     w8a16_tma_kernel(const __grid_constant__ CUtensorMap wmap, const ST* __restrict__ scale,
                      const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int N, int K,
-                     GemvPlan pl, float* __restrict__ slots, int* __restrict__ cnt, int* err) {
+                     GemvPlan pl, float* __restrict__ slots, int* __restrict__ cnt, int* err,
+                     ActPrologue pro) {
   constexpr bool kF16Mma = XS || !BF16;  // staged activations are f16
   extern __shared__ uint8_t smem_raw[];
   const Ring ring = warp_ring(smem_raw);
-  const uint32_t xsm = ring_end(smem_raw), gs = xsm + kXsBytes, tm = gs + 1024;
+  const uint32_t xsm = ring_end(smem_raw), gs = xsm + kXsBytes + kAuxGs, tm = xsm + kXsBytes + kAuxTm;
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int wpc = blockDim.x >> 5;
   const int w = blockIdx.x * wpc + (threadIdx.x >> 5);
@@ -733,9 +809,9 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
   if (lane == 0)  // the weights are constant: prefetch before the previous kernel ends
     while (pr.issued < kStages && !pr.ended) pr.refill(ring, load);
   pdl_wait();  // x, y and the workspace belong to the stream's earlier kernels
-  if (XS) stage_x<BF16>(x, M, K, pl.ng, xsm, gs, tm, min(wpc, pl.NW - (int)blockIdx.x * wpc) * 32);
+  if (XS) stage_act<BF16>(pro, x, M, K, pl.ng, xsm, xsm + kXsBytes, min(wpc, pl.NW - (int)blockIdx.x * wpc) * 32);
   auto store = [&](int tile, const float (&a)[NT][4]) {
-    if (XS && BF16) {  // undo the per-token power-of-two scale of the staged activations
+    if (XS) {  // undo the per-token power-of-two scale of the staged activations
       float b[NT][4];
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
@@ -1118,9 +1194,14 @@ size_t gguf_skinny_workspace_bytes(int64_t M, int64_t K) {
 // sk_ws (may be NULL): GEMV workspace of gemv_workspace_bytes(N) bytes whose
 // counter part is zero (every call leaves it zero).  Given sk_ws, the TMA-fed
 // dynamic-chunk kernel runs; NULL (or an unaligned weight) selects the in-CTA split.
+bool w8a16_prologue_ok(int64_t M, int64_t K) { return K >= 128 && K % 16 == 0 && M * K * 2 <= kXsBytes; }
+
 dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
                                 dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
-                                cudaStream_t st, void* sk_ws) {
+                                cudaStream_t st, void* sk_ws, const ActPrologue* pro_in) {
+  const ActPrologue pro = pro_in ? *pro_in : ActPrologue{kProX, nullptr, nullptr, nullptr, 0.0f};
+  if (pro.mode != kProX && !(sk_ws && aligned16(q) && aligned16(x) && w8a16_prologue_ok(M, K)))
+    return fail(DIAL_ERR_SHAPE, "the fused prologue needs the staged decode path");
   const int64_t tiles = (N + 15) / 16;
   const int64_t ng = (K + 127) / 128;
   const int nt = (int)((M + 7) / 8);
@@ -1147,7 +1228,7 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
   if (ae == cudaSuccess)                                                                       \
     s = launch_pdl("w8a16_tma_kernel", w8a16_tma_kernel<NT_, BF, ST, XS>, grid, block, smem, st, \
                    map, static_cast<const ST*>(scale), xp, yp, (int)M, (int)N, (int)K, pl,     \
-                   slots, cnt, err)
+                   slots, cnt, err, pro)
 #define SK(NT_, BF, ST)       \
   if (xs) {                   \
     SKX(NT_, BF, ST, true);   \

@@ -200,6 +200,9 @@ class W8A16Gemv:
     kernel = "w8a16_tma_kernel<NT=1>"
     M, N, K = 1, 12288, 4096
     graph = True
+    # ncu DRAM read + write bytes of one launch of this shape
+    # (profiles/w8a16_tma_kernel_gemv_12288x4096.md)
+    traffic = 50_435_328 + 15_104
 
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
         self.torch = torch
@@ -335,6 +338,9 @@ class QwenDecode:
     kernel = "w8a16_tma_kernel<NT=1> (the stage's linears from one graph, events)"
     graph = True
     scaling = "strong"
+    # ncu DRAM bytes of the 145 GEMV launches of one token on one GPU
+    # (profiles/qwen3_decode_step_launches.md); per token, like `achieved`
+    traffic = 7_655_829_760
     n_seqs, prompt_len, decode_cap = 8, 1024, 448
     copies_per_step = 8  # one graph per micro-batch
 
@@ -702,7 +708,8 @@ def run_ours(args, rank, local, world):
         "config": dict(wl.config, parallelism=(f"pipeline x{world}" if pipelined else f"replicas x{world}")),
         "roofline": {"bound": wl.bound, "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s" if wl.bound == "hbm" else "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "frac": round(achieved / peak, 4),
+                     "traffic": getattr(wl, "traffic", None) if world == 1 else None,
                      "peak_source": f"{peak_src} ({'hbm_gbs' if wl.bound == 'hbm' else 'bf16_tflops'} burst)",
                      "kernel": wl.kernel},
         "e2e": e2e, "gpu_launches": launches_per_step * args.steps,

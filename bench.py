@@ -195,7 +195,7 @@ def build_copy_graphs(wl):
 
 
 class W8A16Gemv:
-    """one W8A16 decode linear per step."""
+    """One W8A16 decode linear per step (the Qwen3-8B up-proj shape)."""
     metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "int8 x f16"
     kernel = "w8a16_tma_kernel<NT=1>"
     M, N, K = 1, 12288, 4096
@@ -250,7 +250,7 @@ class W8A16Gemv:
 
 
 class GgufSweep:
-    """BASELINE config 2 (decode points): 7 shapes x {Q4_0, Q8_0} x M in {1, 8}."""
+    """GGUF decode sweep: 7 shapes x {Q4_0, Q8_0} x M in {1, 8}."""
     metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "q4_0/q8_0 x f32"
     kernel = "gguf_tma_kernel + q8_0_act_quantize_kernel (whole sweep)"
     ms = (1, 8)
@@ -311,7 +311,7 @@ class GgufSweep:
 
 
 class GgufPrefill(GgufSweep):
-    """BASELINE config 2 (prefill point): the same sweep at M = 512 (tensor-bound)."""
+    """GGUF prefill sweep: the same sweep at M = 512 (tensor-bound)."""
     metric, unit, bound, dtype = "dequant-GEMM TFLOP/s", "TFLOP/s", "tensor", "q4_0/q8_0 x f32 -> f16 MMA"
     kernel = "dequant_gemm_kernel (whole sweep)"
     ms = (512,)
@@ -328,7 +328,7 @@ class GgufPrefill(GgufSweep):
 
 
 class QwenDecode:
-    """BASELINE configs 3/4: Qwen3-8B-shaped W8A16 decoder (36 layers, hidden 4096,
+    """Qwen3-8B-shaped W8A16 decoder (36 layers, hidden 4096,
     MLP 12288, 32/8 heads, vocab 151936, random init N(0, 0.02)), 8 sequences,
     1024-token prompts (prefilled before timing), decoded as micro-batches of 1
     through a pipeline of one stage per rank (layers split by the stage
@@ -341,21 +341,38 @@ class QwenDecode:
     # ncu DRAM bytes of the 145 GEMV launches of one token on one GPU
     # (profiles/qwen3_decode_step_launches.md); per token, like `achieved`
     traffic = 7_655_829_760
-    n_seqs, prompt_len, decode_cap = 8, 1024, 448
+    n_seqs, mb_size, prompt_len, decode_cap = 8, 1, 1024, 448
+    head_layers = 3.2  # the output head's cost in layers (weights read per token)
     copies_per_step = 8  # one graph per micro-batch
+    act = "bf16"
+
+    def model_config(self):
+        from dial_cuda.model import ModelConfig
+        return ModelConfig(act_dtype=self.act)
+
+    def micro_batch(self, world):
+        return self.mb_size
+
+    def describe(self):
+        return {"workload": "qwen3_8b_w8a16_decode", "model": "Qwen3-8B-shaped, random init",
+                "layers": 36, "hidden": 4096, "intermediate": 12288, "heads": "32/8",
+                "vocab": 151936, "weights": "int8 per row, f32 scale (layers and head)",
+                "l2": "7.6 GB of weights per token >> 126 MB L2"}
 
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
-        from dial_cuda.model import ModelConfig, Stage
+        from dial_cuda.model import Stage
         from dial_cuda.pipeline import ModelStageCompute, Pipeline, TorchChannel, stage_layers
         self.torch, self.D, self.rank, self.world = torch, D, rank, world
-        self.cfg = ModelConfig(act_dtype="bf16")
-        self.ranges = stage_layers(self.cfg.n_layers, world)
+        self.cfg = self.model_config()
+        self.mb_size = self.micro_batch(world)
+        n_mb = self.n_seqs // self.mb_size
+        self.ranges = stage_layers(self.cfg.n_layers, world, head_layers=self.head_layers)
         rr = self.ranges[rank]
         self.max_seq = self.prompt_len + self.decode_cap + 16
         self.stage = Stage(self.cfg, rr.start, rr.stop, n_slots=self.n_seqs, max_seq=self.max_seq)
         st = self.stage
-        self.comp = ModelStageCompute(st, self.n_seqs, self.prompt_len)
-        self.pipe = Pipeline(rank, world, self.comp, TorchChannel() if world > 1 else None, self.n_seqs)
+        self.comp = ModelStageCompute(st, n_mb, self.prompt_len, mb_size=self.mb_size)
+        self.pipe = Pipeline(rank, world, self.comp, TorchChannel() if world > 1 else None, n_mb)
         prompts = None
         if rank == 0:
             g = torch.Generator(device="cuda").manual_seed(SEED)
@@ -372,15 +389,13 @@ class QwenDecode:
         self.work_per_step = self.n_seqs  # tokens (whole job)
         self.weight_bytes = st.weight_bytes
         self.steps_done = 0
-        self.config = {"workload": "qwen3_8b_w8a16_decode", "model": "Qwen3-8B-shaped, random init",
-                       "layers": 36, "hidden": 4096, "intermediate": 12288, "heads": "32/8",
-                       "vocab": 151936, "sequences": self.n_seqs, "micro_batch": 1,
-                       "prompt_len": self.prompt_len, "activation": "bf16", "kv_cache": "bf16",
-                       "stages": [[r.start, r.stop] for r in self.ranges],
-                       "stage_weights_GB": round(self.weight_bytes / 1e9, 3),
-                       "prefill_ms_per_seq": round(self.prefill_ms, 2),
-                       "l2": "7.6 GB of weights per token >> 126 MB L2",
-                       "launch": "one CUDA graph per micro-batch and stage; NCCL p2p hand-off"}
+        self.copies_per_step = n_mb
+        self.config = dict(self.describe(), sequences=self.n_seqs, micro_batch=self.mb_size,
+                           prompt_len=self.prompt_len, activation=self.act, kv_cache=self.act,
+                           stages=[[r.start, r.stop] for r in self.ranges],
+                           stage_weights_GB=round(self.weight_bytes / 1e9, 3),
+                           prefill_ms_per_seq=round(self.prefill_ms, 2),
+                           launch="one CUDA graph per micro-batch and stage; NCCL p2p hand-off")
 
     def run_copy(self, _):
         """One eager micro-batch for the launch count (its state is restored)."""
@@ -420,19 +435,18 @@ class QwenDecode:
         self.pipe.finish()
 
     def kernel_roofline(self, reps: int = 5):
-        """HBM GB/s of the dominant kernel: this stage's linears (M = 1) launched
-        back to back in model order from one CUDA graph, algorithmic bytes over
-        the replay's event time."""
+        """HBM GB/s of the dominant kernel: this stage's linears (M = one
+        micro-batch) launched back to back in model order from one CUDA graph,
+        algorithmic bytes over the replay's event time."""
         torch, st = self.torch, self.stage
-        from dial_cuda.model import WFMT_W8A16
         lins = st.linears + ([st.head] if st.head is not None else [])
-        assert lins[0].fmt == WFMT_W8A16
+        R = self.mb_size
         xs, ys = {}, []
         for lin in lins:
             wl = lin.lin
             if wl.in_dim not in xs:
-                xs[wl.in_dim] = torch.randn((1, wl.in_dim), device="cuda").to(st.dt)
-            ys.append(torch.empty((1, wl.out_dim), device="cuda", dtype=st.dt))
+                xs[wl.in_dim] = torch.randn((R, wl.in_dim), device="cuda").to(st.dt)
+            ys.append(torch.empty((R, wl.out_dim), device="cuda", dtype=st.dt))
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
 
@@ -448,7 +462,7 @@ class QwenDecode:
             run()
         gr.replay()
         torch.cuda.synchronize()
-        total_b = sum(l.lin.weight_bytes + 2 * l.lin.in_dim + 2 * l.lin.out_dim for l in lins)
+        total_b = sum(l.lin.weight_bytes + 2 * R * (l.lin.in_dim + l.lin.out_dim) for l in lins)
         ts = []
         for _ in range(reps):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -461,8 +475,41 @@ class QwenDecode:
         return total_b / (statistics.median(ts) / 1e3) / 1e9
 
 
+class LlamaGgufDecode(QwenDecode):
+    """Llama-3-8B-shaped GGUF decoder (32 layers, hidden 4096,
+    MLP 14336, 32/8 heads, vocab 128256, theta 5e5, no QK-norm), layers Q4_0 and
+    head Q8_0 from N(0, 0.02) weights, 32 sequences with 2048-token prompts
+    (prefilled before timing), batched decode as 8 micro-batches of 4 sequences
+    through the pipeline.  A step advances every sequence by one token."""
+    metric, unit, bound, dtype = "8B GGUF Q4_0 batched decode tok/s", "tok/s", "hbm", "q4_0 x f16"
+    kernel = "gguf_tma_kernel<NT=1> (the stage's linears from one graph, events)"
+    traffic = None
+    n_seqs, mb_size, prompt_len, decode_cap = 32, None, 2048, 160
+    head_layers = 1.4  # Q8_0 head 558 MB vs a Q4_0 layer's 123 MB + 268 MB of KV per step
+    act = "f16"
+
+    def model_config(self):
+        from dial_cuda.model import ModelConfig
+        c = ModelConfig.llama3_8b_q4_0()
+        c.act_dtype = self.act
+        return c
+
+    def micro_batch(self, world):
+        """As many micro-batches as stages (one on a single GPU): each stage reads
+        its weights once per micro-batch, and with fewer micro-batches than
+        stages some stage would idle."""
+        assert self.n_seqs % world == 0, "sequences must split evenly over the stages"
+        return self.n_seqs // world
+
+    def describe(self):
+        return {"workload": "llama3_8b_gguf_q4_0_batched_decode", "model": "Llama-3-8B-shaped, random init",
+                "layers": 32, "hidden": 4096, "intermediate": 14336, "heads": "32/8", "vocab": 128256,
+                "weights": "Q4_0 layers, Q8_0 head",
+                "l2": "3.9 GB of weights + 9 GB of KV per step >> 126 MB L2"}
+
+
 WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep, "gguf_prefill": GgufPrefill,
-             "qwen3_decode": QwenDecode}
+             "qwen3_decode": QwenDecode, "llama_gguf_decode": LlamaGgufDecode}
 
 
 # ------------------------------------------------------------------ workloads (CPU oracle)
@@ -560,9 +607,54 @@ def cpu_decode_measure(budget_s):
     return 1.0 / t_tok, t_tok, O.num_threads(), sample
 
 
+def cpu_gguf_decode_measure(budget_s):
+    """Llama-3-8B GGUF batched decode on the C oracle: the candle-style GGUF
+    linears (Q8_0-quantised activations, integer block dots) of one Q4_0 layer
+    and of the Q8_0 head at M = 4 rows (one micro-batch); a token costs
+    32 layers + head over 4.  Attention, norms and RoPE are left out, so the
+    CPU rate is an upper bound."""
+    import numpy as np
+
+    import oracle as O
+    rng = np.random.default_rng(SEED)
+    H, I, V, Hq, Hkv, Dh, R = 4096, 14336, 128256, 32, 8, 128, 4
+
+    # the cost depends on the shapes only: random quants with a finite block scale
+    def blocks(qt, N, K):
+        bb = O.BLOCK_BYTES[qt]
+        b = rng.integers(0, 256, (N, K // 32, bb), dtype=np.uint8)
+        b[:, :, 0:2] = np.frombuffer(np.float16(0.001).tobytes(), np.uint8)
+        return b.reshape(N, -1)
+
+    layer = [(blocks(O.Q4_0, N, K), O.Q4_0, N, K) for N, K in
+             (((Hq + 2 * Hkv) * Dh, H), (H, Hq * Dh), (2 * I, H), (H, I))]
+    head = (blocks(O.Q8_0, V, H), O.Q8_0, V, H)
+    xs = {k: rng.normal(0, 1, (R, k)).astype(np.float32) for k in (H, I)}
+
+    def run(lins):
+        t0 = time.perf_counter()
+        for b, qt, N, K in lins:
+            O.gguf_linear_candle(xs[K], b, qt, N)
+        return time.perf_counter() - t0
+
+    run(layer)  # warm-up
+    tl, th = [], []
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or not tl:
+        tl.append(run(layer))
+        th.append(run([head]))
+    a, b = statistics.median(tl), statistics.median(th)
+    t_tok = (32 * a + b) / R
+    sample = (f"{len(tl)} x (one Q4_0 layer's 4 linears + the Q8_0 head at 4 rows on the oracle); "
+              f"token = (32 x {1e3 * a:.1f} ms + {1e3 * b:.1f} ms) / 4; attention not included")
+    return 1.0 / t_tok, t_tok, O.num_threads(), sample
+
+
 def cpu_measure(name, budget_s):
     if name == "qwen3_decode":
         return cpu_decode_measure(budget_s)
+    if name == "llama_gguf_decode":
+        return cpu_gguf_decode_measure(budget_s)
     cw = CpuWorkload(name)
     frac = 1.0 if name != "gguf_prefill" else 16 / 512  # 16 of the 512 rows per sample
     cw.step(frac)  # warm-up
@@ -693,7 +785,7 @@ def run_ours(args, rank, local, world):
     if hasattr(wl, "kernel_roofline"):
         achieved = wl.kernel_roofline()
         wl.config["step_weight_GBps"] = round(
-            wl.weight_bytes * wl.work_per_step / (statistics.mean(step_ms) / 1e3) / 1e9, 1)
+            wl.weight_bytes * wl.copies_per_step / (statistics.mean(step_ms) / 1e3) / 1e9, 1)
     else:
         achieved = wl.work_per_step / (statistics.mean(step_ms) / 1e3) / unit_scale(wl.unit)
     if wl.bound == "hbm":

@@ -69,7 +69,7 @@ def _bind():
 
 @dataclass
 class ModelConfig:
-    """Decoder shape.  Defaults: the Qwen3-8B text decoder of BASELINE config 3."""
+    """Decoder shape.  Defaults: the Qwen3-8B text decoder (W8A16, QK-norm)."""
     n_layers: int = 36
     hidden: int = 4096
     intermediate: int = 12288
@@ -87,7 +87,7 @@ class ModelConfig:
 
     @staticmethod
     def llama3_8b_q4_0() -> "ModelConfig":
-        """BASELINE config 5: Llama-3-8B shape, Q4_0 layers, Q8_0 head, no QK-norm."""
+        """Llama-3-8B shape, Q4_0 layers, Q8_0 head, no QK-norm."""
         return ModelConfig(n_layers=32, intermediate=14336, vocab=128256, rope_theta=5e5,
                            qk_norm=False, weight_format=WFMT_Q4_0, head_format=WFMT_Q8_0)
 

@@ -109,19 +109,20 @@ class StageCompute:
 
 
 class ModelStageCompute(StageCompute):
-    """A model.Stage driving one micro-batch per sequence slot (micro-batch b is
-    KV slot b), each step captured once as a CUDA graph per micro-batch."""
+    """A model.Stage driving n_mb micro-batches of `mb_size` sequences each
+    (micro-batch b holds KV slots b*mb_size .. b*mb_size + mb_size - 1), each
+    step captured once as a CUDA graph per micro-batch."""
 
-    def __init__(self, stage, n_mb: int, prompt_len: int, use_graphs: bool = True):
+    def __init__(self, stage, n_mb: int, prompt_len: int, use_graphs: bool = True, mb_size: int = 1):
         torch = _torch()
         self.st = stage
         self.first, self.last = stage.first == 0, stage.last == stage.cfg.n_layers
-        self.n_mb = n_mb
-        dev, dt, H = stage.device, stage.dt, stage.cfg.hidden
-        self.hidden = [torch.zeros((1, H), device=dev, dtype=dt) for _ in range(n_mb)]
-        self.tokens = [torch.zeros(1, device=dev, dtype=torch.int32) for _ in range(n_mb)]
-        self.pos = [torch.full((1,), prompt_len, device=dev, dtype=torch.int32) for _ in range(n_mb)]
-        self.slot = [torch.full((1,), b, device=dev, dtype=torch.int32) for b in range(n_mb)]
+        self.n_mb, self.mb_size = n_mb, mb_size
+        dev, dt, H, R = stage.device, stage.dt, stage.cfg.hidden, mb_size
+        self.hidden = [torch.zeros((R, H), device=dev, dtype=dt) for _ in range(n_mb)]
+        self.tokens = [torch.zeros(R, device=dev, dtype=torch.int32) for _ in range(n_mb)]
+        self.pos = [torch.full((R,), prompt_len, device=dev, dtype=torch.int32) for _ in range(n_mb)]
+        self.slot = [torch.arange(b * R, (b + 1) * R, device=dev, dtype=torch.int32) for b in range(n_mb)]
         self.use_graphs = use_graphs
         self.graphs: List = [None] * n_mb
 
@@ -179,15 +180,18 @@ class ModelStageCompute(StageCompute):
             self._plast = torch.tensor([T - 1], device=self.st.device, dtype=torch.int32)
         return self._pbuf
 
-    def prefill_run(self, b: int, ids=None) -> None:
+    def prefill_run(self, b: int, ids=None, i: int = 0) -> None:
+        """Prefills sequence i of micro-batch b (KV slot b*mb_size + i); stage 0
+        embeds its prompt `ids` [T]."""
         torch = _torch()
         st, h = self.st, self._pbuf
         T = h.shape[0]
+        seq = b * self.mb_size + i
         if self.first:
             st.embed_tokens(ids, h)
-        st.layers_forward(h, self._ppos, torch.full((T,), b, device=st.device, dtype=torch.int32), T)
+        st.layers_forward(h, self._ppos, torch.full((T,), seq, device=st.device, dtype=torch.int32), T)
         if self.last:
-            st.head_forward(h, self.tokens[b], row_index=self._plast)
+            st.head_forward(h, self.tokens[b][i:i + 1], row_index=self._plast)
 
 
 # ------------------------------------------------------------------ the schedule
@@ -218,8 +222,9 @@ class Pipeline:
         torch = _torch() if host_io else None
         r, P, B, c, ch = self.rank, self.world, self.n_mb, self.c, self.ch
         if host_io and self.host_io is None:
-            self.host_io = ([torch.zeros(1, dtype=torch.int32).pin_memory() for _ in range(B)],
-                            [torch.zeros(1, dtype=torch.int32).pin_memory() for _ in range(B)])
+            n = [c.token_buffer(b).numel() for b in range(B)]  # one token per row
+            self.host_io = ([torch.zeros(n[b], dtype=torch.int32).pin_memory() for b in range(B)],
+                            [torch.zeros(n[b], dtype=torch.int32).pin_memory() for b in range(B)])
         for _ in range(n_steps):
             for b in range(B):
                 tok = c.token_buffer(b)
@@ -260,27 +265,32 @@ class Pipeline:
 
     def host_tokens(self):
         """The last host_io step's tokens (last stage)."""
-        return [int(x) for x in self.host_io[1]] if self.host_io else None
+        return [int(x) for t in self.host_io[1] for x in t.tolist()] if self.host_io else None
 
     def drain(self) -> None:
         for b in range(self.n_mb):
             self._wait_send(b)
 
     def prefill(self, prompts: Optional[Sequence] = None, prompt_len: int = 0) -> None:
-        """Prefills micro-batch b with prompts[b] (stage 0 holds the prompts); the
-        first generated tokens end up in stage 0's token buffers.  The [T, hidden]
-        hand-off reuses one buffer per stage, so each send completes before the
-        next micro-batch overwrites it."""
+        """Prefills every sequence (stage 0 holds the prompts, one per sequence,
+        micro-batch-major); the first generated tokens end up in stage 0's token
+        buffers.  The [T, hidden] hand-off reuses one buffer per stage, so each
+        send completes before the next sequence overwrites it."""
         r, P, B, c, ch = self.rank, self.world, self.n_mb, self.c, self.ch
+        R = getattr(c, "mb_size", 1)
         T = len(prompts[0]) if prompts is not None else prompt_len
         buf = c.prefill_buffer(T)
         for b in range(B):
-            if r > 0:
-                ch.irecv(buf, r - 1).wait()
-            c.prefill_run(b, prompts[b] if r == 0 else None)
-            if r < P - 1:
-                ch.isend(buf, r + 1).wait()
-            elif P > 1:
+            for i in range(R):
+                if r > 0:
+                    ch.irecv(buf, r - 1).wait()
+                if R == 1:
+                    c.prefill_run(b, prompts[b] if r == 0 else None)
+                else:
+                    c.prefill_run(b, prompts[b * R + i] if r == 0 else None, i)
+                if r < P - 1:
+                    ch.isend(buf, r + 1).wait()
+            if r == P - 1 and P > 1:
                 self.pending[b] = ch.isend(c.token_buffer(b), 0)
         if P > 1 and r == 0:
             for b in range(B):

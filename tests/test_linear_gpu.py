@@ -136,7 +136,7 @@ def test_w8a16_bf16_activation_range(D, torch, amax):
 
 
 def test_w8a16_decode_config1_shape(D, torch):
-    """BASELINE config 1 shape: x f16 [1,4096] ~N(0,1), W [12288,4096] ~N(0,0.02), f16 scale."""
+    """The up-proj decode shape: x f16 [1,4096] ~N(0,1), W [12288,4096] ~N(0,0.02), f16 scale."""
     rng = np.random.default_rng(299792458)
     w = rng.normal(0, 0.02, (12288, 4096)).astype(np.float32)
     x = rng.normal(0, 1, (1, 4096)).astype(np.float16)

@@ -24,8 +24,11 @@ SMALL = dict(n_layers=4, hidden=1024, intermediate=2048, n_heads=8, n_kv_heads=2
 N_MB, PROMPT, STEPS = 4, 24, 6
 
 
-def _cfg():
-    from dial_cuda.model import ModelConfig
+def _cfg(gguf: bool = False):
+    from dial_cuda.model import WFMT_Q4_0, WFMT_Q8_0, ModelConfig
+    if gguf:  # the Llama-style GGUF decoder: Q4_0 layers, Q8_0 head, f16, no QK-norm
+        return ModelConfig(**dict(SMALL, act_dtype="f16", qk_norm=False, rope_theta=5e5,
+                                  weight_format=WFMT_Q4_0, head_format=WFMT_Q8_0))
     return ModelConfig(**SMALL)
 
 
@@ -35,10 +38,10 @@ def _prompts(torch):
             for _ in range(N_MB)]
 
 
-def reference_tokens(torch):
+def reference_tokens(torch, gguf: bool = False):
     """Greedy tokens of every sequence from the single-stage Decoder."""
     from dial_cuda.model import Decoder
-    dec = Decoder(_cfg(), n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
+    dec = Decoder(_cfg(gguf), n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
     out = []
     for b, p in enumerate(_prompts(torch)):
         tok = dec.prefill(p, slot=b)
@@ -73,6 +76,34 @@ def test_single_stage_pipeline_matches_decoder(cuda):
     pipe.steps(1, host_io=True)
     torch.cuda.synchronize()
     assert [int(t.item()) for t in comp.tokens] == [s[-1] for s in ref]
+    assert pipe.host_tokens() == [s[-1] for s in ref]
+
+
+@pytest.mark.parametrize("gguf", [False, True], ids=["w8a16", "gguf"])
+def test_single_stage_micro_batches_match_decoder(cuda, gguf):
+    """Batched decode: the 4 sequences as 2 micro-batches of 2 rows (each row its
+    own slot and position) give the per-sequence Decoder's tokens."""
+    import torch
+
+    from dial_cuda.model import Stage
+    from dial_cuda.pipeline import ModelStageCompute, Pipeline
+    ref = reference_tokens(torch, gguf)
+    cfg = _cfg(gguf)
+    R = 2
+    st = Stage(cfg, 0, cfg.n_layers, n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
+    comp = ModelStageCompute(st, N_MB // R, PROMPT, mb_size=R)
+    pipe = Pipeline(0, 1, comp, None, N_MB // R)
+    pipe.prefill(_prompts(torch))
+    firsts = [int(v) for t in comp.tokens for v in t.tolist()]
+    assert firsts == [s[0] for s in ref]
+    saved = [t.clone() for t in comp.tokens]
+    comp.capture()
+    for t, s in zip(comp.tokens, saved):
+        t.copy_(s)
+    pipe.steps(STEPS - 1)
+    pipe.steps(1, host_io=True)
+    torch.cuda.synchronize()
+    assert [int(v) for t in comp.tokens for v in t.tolist()] == [s[-1] for s in ref]
     assert pipe.host_tokens() == [s[-1] for s in ref]
 
 

@@ -49,7 +49,7 @@ L2_BYTES = 126 * 2**20
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-LAYER_SHAPES = [  # (name, out N, in K) of one 8B decoder layer (Qwen3-8B / config 2)
+LAYER_SHAPES = [  # (name, out N, in K) of one 8B decoder layer (Qwen3-8B shapes)
     ("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
     ("gate", 12288, 4096), ("up", 12288, 4096), ("down", 4096, 12288),
 ]
@@ -482,7 +482,7 @@ class LlamaGgufDecode(QwenDecode):
     (prefilled before timing), batched decode as 8 micro-batches of 4 sequences
     through the pipeline.  A step advances every sequence by one token."""
     metric, unit, bound, dtype = "8B GGUF Q4_0 batched decode tok/s", "tok/s", "hbm", "q4_0 x f16"
-    kernel = "gguf_tma_kernel<NT=1> (the stage's linears from one graph, events)"
+    kernel = "gguf_tma_kernel (M = one micro-batch; the stage's linears from one graph, events)"
     traffic = None
     n_seqs, mb_size, prompt_len, decode_cap = 32, None, 2048, 160
     head_layers = 1.4  # Q8_0 head 558 MB vs a Q4_0 layer's 123 MB + 268 MB of KV per step

@@ -8,13 +8,27 @@
 // (worker_gguf.rs:399-460, :607-610).  No resident f16 copy: the packed
 // weights are dequantised tile by tile into shared memory.
 //
-// CTA tile: 128 activation rows (UMMA M) x 256 weight rows (UMMA N), K in
-// steps of 64 (one 128-byte swizzle atom of f16/bf16), 4-stage ring.
-//   warp 0     : TMA producer of the activation tile (SWIZZLE_128B, no multicast)
+// CTA tile: 256 weight rows x 128 activation rows (tokens), K in 64-deep
+// stages.  The dequantised weights are the MMA's A operand and live in TMEM:
+// two tcgen05.mma (M = 128 weight rows each, N = 128 tokens, K = 16) per
+// 16-deep K step read A from TMEM and the token tile from shared memory.
+//   warp 0     : TMA producer of the token tile (SWIZZLE_128B, 8-stage ring, no multicast)
 //   warp 1     : TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..9 : dequantisers (one weight row each per 128-wide K group,
-//                writing the canonical K-major SWIZZLE_128B layout), then the
-//                epilogue (tcgen05.ld -> scale -> global)
+//   warps 2..17: dequantisers: warp w owns TMEM lane quarter w % 4 (one weight
+//                row per thread) of weight half ((w - 2) / 4) & 1 and K half
+//                (w - 2) / 8 of every stage; each thread reads its row's packed
+//                group from the weight ring, dequantises its 32 K values per
+//                stage to f16/bf16 pairs and writes them with tcgen05.st into
+//                the A ring (4 stages), one stage behind so the store's latency
+//                hides under the next stage's arithmetic; then the epilogue
+//                (tcgen05.ld -> scale -> global, y[token, n])
+//   warp 18    : TMA producer of the packed weight groups (and GGUF scales)
+// Small grids are split along K over a thread-block cluster of S CTAs
+// (1 x 1 x S): each CTA leaves its f32 partial tile in shared memory and CTA z
+// adds the S partials of its token slice in rank order through distributed
+// shared memory, so the result does not depend on timing.
+// TMEM: accumulators in columns [0, 256) (weight half h at 128 h), A stages in
+// [256, 512), 64 columns each (32 per weight half: K 64 as f16x2 words).
 // Operands: f16 (f16 or f32 activations) or bf16 (bf16 activations), f32
 // accumulation in TMEM.  W8A16 int8 values are exact in f16/bf16 and the row
 // scale is applied in the epilogue, as in the reference (sum first, then
@@ -40,21 +54,44 @@ __device__ int g_device_error = 0;
 
 namespace {
 
-constexpr int BM = 128;  // activation rows per CTA (UMMA M)
-constexpr int BN = 256;  // weight rows per CTA (UMMA N)
-constexpr int BK = 64;   // K per stage
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_BYTES = BN * BK * 2;  // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int DQ_WARPS = 8;
-constexpr int DQ_THREADS = DQ_WARPS * 32;  // == BN: one weight row per thread
-constexpr int THREADS = 64 + DQ_THREADS;
-constexpr int TMEM_COLS = 256;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int BW = 256;   // weight rows per CTA (two UMMA M = 128 halves)
+constexpr int BT = 128;   // activation rows (tokens) per CTA (UMMA N)
+constexpr int BK = 64;    // K per stage (one 128-byte swizzle atom of f16/bf16)
+constexpr int B_STAGES = 4;  // token tiles in shared memory
+constexpr int A_STAGES = 4;  // dequantised weight stages in TMEM
+constexpr int W_STAGES = 4;  // packed weight groups (128 K) in shared memory
+constexpr int B_BYTES = BT * BK * 2;  // 16 KB token tile per stage
+constexpr int ACC_COLS = 2 * BT;      // two f32 accumulators of BT columns
+constexpr int A_HALF_COLS = BK / 2;   // TMEM columns of one weight half per stage
+constexpr int A_COLS = 2 * A_HALF_COLS;
+constexpr int TMEM_COLS = 512;
+static_assert(ACC_COLS + A_STAGES * A_COLS <= TMEM_COLS, "TMEM budget");
+constexpr int DQ_WARPS = 16;  // 4 per TMEM lane quarter: weight half x K half of a stage
+constexpr int THREADS = 64 + DQ_WARPS * 32 + 32;  // + the weight producer warp
+// split-K receive buffer of the owning CTA: [S senders][BW rows][BT / S + 4] f32
+// (the +4 pad keeps the 8 rows of a quarter warp's float4 accesses in distinct banks)
+constexpr int RED_BYTES = BW * 4 * (BT + 4 * 8);
+constexpr int kMaxSplit = 8;
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
 
 enum Fmt { kW8F32 = 0, kW8F16 = 1, kQ4 = 2, kQ8 = 3 };
+
+// Shared memory of one CTA: [token ring | packed weight ring | GGUF d ring],
+// every stage 1024-byte aligned (the swizzle atoms); the split-K partial tile
+// reuses it after the main loop.
+template <int FMT>
+struct Smem {
+  static constexpr bool GGUF = FMT == kQ4 || FMT == kQ8;
+  static constexpr int GB = FMT == kQ4 ? 64 : 128;  // packed bytes of a row per 128-K group
+  static constexpr int W_BYTES = BW * GB;
+  static constexpr int D_BYTES = GGUF ? (BW / 16) * 128 : 0;  // 16-row tiles x 4 blocks x 16 rows
+  static constexpr int W_OFF = B_STAGES * B_BYTES;
+  static constexpr int D_OFF = W_OFF + W_STAGES * W_BYTES;
+  static constexpr int RING = D_OFF + W_STAGES * D_BYTES;
+  static constexpr int DATA = RING > RED_BYTES ? RING : RED_BYTES;
+  static constexpr int BYTES = DATA + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(BYTES <= 227 * 1024, "shared memory budget");
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -129,12 +166,14 @@ __host__ __device__ constexpr uint32_t make_idesc(bool bf16, int m, int n) {
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t idesc, uint32_t accumulate) {
+// D[tmem_d] (+)= A[tmem_a] * B[bdesc]^T: A (M = 128 rows, K = 16) in TMEM, one
+// row per lane, K packed two 16-bit values per 32-bit column (even K low).
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -181,37 +220,35 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// 8 int8 values (two words) -> one 16-byte chunk of 8 operands, times `d`
-// (unscaled for W8A16, whose scale is applied in the epilogue).
-template <bool BF16, bool SCALED>
-__device__ __forceinline__ uint4 chunk_from_i8(uint32_t w0, uint32_t w1, float d, __half2 dh) {
-  uint4 out;
+// int8x4 -> (bf16x2 of bytes 0,1 ; bf16x2 of bytes 2,3), exact: under the
+// exponent of 128, v1 = 128 + (b & 127) and v2 = -128 - 128 * (b < 0), and
+// v1 + v2 = b is an integer that bf16 holds exactly.
+__device__ __forceinline__ void i8x4_bf16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t tl = prmt(w, 0x43434343u, 0x4140u), th = prmt(w, 0x43434343u, 0x4342u);
+  const uint32_t l1 = tl & 0xFF7FFF7Fu, l2 = (tl & 0x00800080u) | 0xC300C300u;
+  const uint32_t h1 = th & 0xFF7FFF7Fu, h2 = (th & 0x00800080u) | 0xC300C300u;
+  __nv_bfloat162 l = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&l1),
+                             *reinterpret_cast<const __nv_bfloat162*>(&l2));
+  __nv_bfloat162 h = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&h1),
+                             *reinterpret_cast<const __nv_bfloat162*>(&h2));
+  lo = *reinterpret_cast<uint32_t*>(&l);
+  hi = *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 4 int8 values times the block scale d, rounded once to the operand type.
+template <bool BF16>
+__device__ __forceinline__ void i8x4_scaled(uint32_t w, float d, __half2 dh, uint32_t& lo,
+                                            uint32_t& hi) {
   if (!BF16) {
-    uint32_t a, b, c, e;
-    i8x4_f16(w0, a, b);
-    i8x4_f16(w1, c, e);
-    if (SCALED) {
-      a = h2_bits(__hmul2(bits_h2(a), dh));
-      b = h2_bits(__hmul2(bits_h2(b), dh));
-      c = h2_bits(__hmul2(bits_h2(c), dh));
-      e = h2_bits(__hmul2(bits_h2(e), dh));
-    }
-    out = make_uint4(a, b, c, e);
+    i8x4_f16(w, lo, hi);  // exact
+    lo = h2_bits(__hmul2(bits_h2(lo), dh));
+    hi = h2_bits(__hmul2(bits_h2(hi), dh));
   } else {
-    float f0[4], f1[4];
-    i8x4_f32(w0, f0);
-    i8x4_f32(w1, f1);
-    if (SCALED) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        f0[i] *= d;
-        f1[i] *= d;
-      }
-    }
-    out = make_uint4(pack_bf16(f0[0], f0[1]), pack_bf16(f0[2], f0[3]), pack_bf16(f1[0], f1[1]),
-                     pack_bf16(f1[2], f1[3]));
+    float f[4];
+    i8x4_f32(w, f);
+    lo = pack_bf16(f[0] * d, f[1] * d);
+    hi = pack_bf16(f[2] * d, f[3] * d);
   }
-  return out;
 }
 
 // 4 nibbles (low or high half of each byte of `w`) -> 4 operands d*(q-8) as 2 words.
@@ -233,15 +270,28 @@ __device__ __forceinline__ void nib4(uint32_t w, bool high, float d, __half2 dh,
   }
 }
 
-__device__ __forceinline__ void st_shared16(uint32_t addr, uint4 v) {
-  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
+// ---------------------------------------------------------------- cluster helpers
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
 }
 
-// Byte offset of 16-byte chunk `c` (0..7) of row `r` in a K-major SWIZZLE_128B tile.
-__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
-  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
 }
 
 struct Params {
@@ -252,66 +302,172 @@ struct Params {
   int M, N, K, G, nk; // nk = number of 64-wide K stages
 };
 
-template <int FMT, bool BF16, typename YT>
-__device__ __forceinline__ void epilogue_store(const Params& p, int row, int nb, float (&v)[16]) {
-  if (FMT == kW8F32) {
-    const float* sc = static_cast<const float*>(p.scale) + nb;
+__device__ __forceinline__ uint4 ld_shared16(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint2 ld_shared8(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+// Row r (0..255) of a packed weight group staged by TMA: 16-byte chunk c sits
+// at chunk c ^ (r & 7) of the row (SWIZZLE_128B, 128-byte rows) or
+// c ^ ((r >> 1) & 3) (SWIZZLE_64B, 64-byte Q4_0 rows), so the 8 rows a quarter
+// warp reads at once fall in distinct banks.  d: the 16-row tile r / 16 of
+// group g holds [16 rows][4 blocks] f16, row r's 4 scales at (r & 15) * 8.
+template <int FMT>
+__device__ __forceinline__ void read_group(uint32_t wbase, uint32_t dbase, int r, uint4 (&raw)[8],
+                                           float (&dv)[4]) {
+  if (FMT == kQ4) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] *= (nb + i < p.N) ? __ldg(sc + i) : 0.f;
-  } else if (FMT == kW8F16) {
-    const __half* sc = static_cast<const __half*>(p.scale) + nb;
+    for (int c = 0; c < 4; ++c) raw[c] = ld_shared16(wbase + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+  } else {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] *= (nb + i < p.N) ? __half2float(sc[i]) : 0.f;
+    for (int c = 0; c < 8; ++c) raw[c] = ld_shared16(wbase + r * 128 + ((c ^ (r & 7)) << 4));
   }
-  YT* out = static_cast<YT*>(p.y) + (size_t)row * p.N + nb;
-  if (nb + 16 <= p.N && (p.N % 8) == 0) {
-    if (sizeof(YT) == 4) {
+  if (FMT == kQ4 || FMT == kQ8) {
+    const uint2 dd = ld_shared8(dbase + (r >> 4) * 128 + (r & 15) * 8);
+    dv[0] = __low2float(bits_h2(dd.x));
+    dv[1] = __high2float(bits_h2(dd.x));
+    dv[2] = __low2float(bits_h2(dd.y));
+    dv[3] = __high2float(bits_h2(dd.y));
+  }
+}
+
+// K 64H + 32KH .. +31 of a group (K half KH of the group's stage H) as 16
+// operand pairs: word j holds K 2j (low) and 2j+1 (high) of that range.
+template <int FMT, bool BF16, int H, int KH>
+__device__ __forceinline__ void dequant_part(const uint4 (&raw)[8], const float (&dv)[4],
+                                             uint32_t (&wv)[16]) {
+  if (FMT == kW8F32 || FMT == kW8F16) {
+    // bytes 64H + 32KH + 16c + 4q .. +3 are word q of chunk 4H + 2KH + c
 #pragma unroll
-      for (int i = 0; i < 16; i += 4)
-        *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-    } else {
-      uint32_t pk[8];
+    for (int c = 0; c < 2; ++c)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        YT a = Act<YT>::from_f32(v[2 * i]), b = Act<YT>::from_f32(v[2 * i + 1]);
-        pk[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&a)) |
-                ((uint32_t)(*reinterpret_cast<uint16_t*>(&b)) << 16);
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t w = word(raw[4 * H + 2 * KH + c], q);
+        if (BF16) i8x4_bf16(w, wv[8 * c + 2 * q], wv[8 * c + 2 * q + 1]);
+        else i8x4_f16(w, wv[8 * c + 2 * q], wv[8 * c + 2 * q + 1]);
       }
-      *reinterpret_cast<uint4*>(out) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      *reinterpret_cast<uint4*>(out + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  } else if (FMT == kQ4) {
+    // block b = 2H + KH: qs bytes 4c..4c+3 are word b of chunk c; element e < 16
+    // is the low nibble of byte e, element e + 16 its high nibble
+    constexpr int b = 2 * H + KH;
+    const float d = dv[b];
+    const __half2 dh = __float2half2_rn(d);  // exact: d is an f16 value
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t w = word(raw[c], b);
+      nib4<BF16>(w, false, d, dh, wv[2 * c], wv[2 * c + 1]);
+      nib4<BF16>(w, true, d, dh, wv[8 + 2 * c], wv[8 + 2 * c + 1]);
     }
   } else {
-    for (int i = 0; i < 16 && nb + i < p.N; ++i) out[i] = Act<YT>::from_f32(v[i]);
+    // Q8_0 block b = 2H + KH: lane-chunk t (raw[2t], raw[2t+1]) word 2b + hi
+    // holds elements 16 hi + 4t .. +3
+    constexpr int b = 2 * H + KH;
+    const float d = dv[b];
+    const __half2 dh = __float2half2_rn(d);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int hi = u >> 2, t = u & 3, wi = 2 * b + hi;
+      const uint32_t w = word(raw[2 * t + (wi >> 2)], wi & 3);
+      i8x4_scaled<BF16>(w, d, dh, wv[2 * u], wv[2 * u + 1]);
+    }
   }
+}
+
+template <int FMT, bool BF16>
+__device__ __forceinline__ void dequant_part(int h, int kh, const uint4 (&raw)[8],
+                                             const float (&dv)[4], uint32_t (&wv)[16]) {
+  if (h == 0) {
+    if (kh == 0) dequant_part<FMT, BF16, 0, 0>(raw, dv, wv);
+    else dequant_part<FMT, BF16, 0, 1>(raw, dv, wv);
+  } else {
+    if (kh == 0) dequant_part<FMT, BF16, 1, 0>(raw, dv, wv);
+    else dequant_part<FMT, BF16, 1, 1>(raw, dv, wv);
+  }
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
+      : "memory");
+}
+
+template <int FMT>
+__device__ __forceinline__ float row_scale(const Params& p, int n) {
+  if (n >= p.N) return 0.f;
+  if (FMT == kW8F32) return __ldg(static_cast<const float*>(p.scale) + n);
+  if (FMT == kW8F16) return __half2float(static_cast<const __half*>(p.scale)[n]);
+  return 1.f;
+}
+
+// y[t, n] for 4 consecutive tokens t0 .. t0+3 of weight row n (n < N checked by the caller).
+template <typename YT>
+__device__ __forceinline__ void store4(const Params& p, int t0, int n, float sc, float4 v) {
+  YT* y = static_cast<YT*>(p.y);
+  const float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (t0 + i < p.M) y[(size_t)(t0 + i) * p.N + n] = Act<YT>::from_f32(a[i] * sc);
 }
 
 template <int FMT, bool BF16, typename YT>
 __global__ void __launch_bounds__(THREADS, 1)
-    dequant_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+    dequant_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                        const __grid_constant__ CUtensorMap tmap_w,
+                        const __grid_constant__ CUtensorMap tmap_d, const Params p) {
+  using L = Smem<FMT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  // bars: full_x[STAGES], full_w[STAGES], empty[STAGES], acc_full, then the TMEM slot
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 1);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::DATA);
+  // bars: full/empty of the token ring, of the TMEM A ring, of the weight ring, acc_full
+  constexpr int NBARS = 2 * B_STAGES + 2 * A_STAGES + 2 * W_STAGES + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
   const uint32_t smem_base = smem_u32(smem);
   const uint32_t bar_base = smem_u32(bars);
-  const uint32_t acc_full = bar_base + 8u * (3 * STAGES);
-#define FULL_X(s) (bar_base + 8u * (uint32_t)(s))
-#define FULL_W(s) (bar_base + 8u * (uint32_t)(STAGES + (s)))
-#define EMPTY(s) (bar_base + 8u * (uint32_t)(2 * STAGES + (s)))
-#define A_ADDR(s) (smem_base + (uint32_t)((s) * STAGE_BYTES))
-#define B_ADDR(s) (smem_base + (uint32_t)((s) * STAGE_BYTES + A_BYTES))
+#define FULL_B(s) (bar_base + 8u * (uint32_t)(s))
+#define EMPTY_B(s) (bar_base + 8u * (uint32_t)(B_STAGES + (s)))
+#define FULL_A(s) (bar_base + 8u * (uint32_t)(2 * B_STAGES + (s)))
+#define EMPTY_A(s) (bar_base + 8u * (uint32_t)(2 * B_STAGES + A_STAGES + (s)))
+#define FULL_W(s) (bar_base + 8u * (uint32_t)(2 * B_STAGES + 2 * A_STAGES + (s)))
+#define EMPTY_W(s) (bar_base + 8u * (uint32_t)(2 * B_STAGES + 2 * A_STAGES + W_STAGES + (s)))
+  const uint32_t acc_full = bar_base + 8u * (uint32_t)(NBARS - 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM;
-  const int n0 = blockIdx.y * BN;
+  const int n0 = blockIdx.x * BW;  // weight rows
+  const int t0 = blockIdx.y * BT;  // tokens
+  const int S = (int)gridDim.z;
+  const int split = S > 1 ? (int)cluster_rank() : 0;
+  // this CTA's K range, in whole 128-wide groups (2 stages)
+  const int ngr = (p.nk + 1) >> 1;
+  const int g0 = (int)((int64_t)ngr * split / S), g1 = (int)((int64_t)ngr * (split + 1) / S);
+  const int kt0 = 2 * g0, kt1 = min(2 * g1, p.nk);
+  const int nst = kt1 - kt0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(FULL_X(s), 1);
-      mbar_init(FULL_W(s), DQ_THREADS);
-      mbar_init(EMPTY(s), 1);
+    for (int s = 0; s < B_STAGES; ++s) {
+      mbar_init(FULL_B(s), 1);
+      mbar_init(EMPTY_B(s), 1);
+    }
+    for (int s = 0; s < A_STAGES; ++s) {
+      mbar_init(FULL_A(s), DQ_WARPS);  // every dequantising warp writes every stage
+      mbar_init(EMPTY_A(s), 1);
+    }
+    for (int s = 0; s < W_STAGES; ++s) {
+      mbar_init(FULL_W(s), 1);
+      mbar_init(EMPTY_W(s), DQ_WARPS);  // every dequantising warp reads every group
     }
     mbar_init(acc_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -330,135 +486,174 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------ TMA producer (activations)
+    // ------------------------------------------------ TMA producer (tokens)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x) : "memory");
-      for (int kt = 0; kt < p.nk; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
-        if (!mbar_wait(EMPTY(s), ph ^ 1u)) break;
-        mbar_expect_tx(FULL_X(s), A_BYTES);
-        tma_load_2d(A_ADDR(s), &tmap_x, FULL_X(s), kt * BK, m0);
+      for (int i = 0; i < nst; ++i) {
+        const int s = i % B_STAGES;
+        const uint32_t ph = (uint32_t)(i / B_STAGES) & 1u;
+        if (!mbar_wait(EMPTY_B(s), ph ^ 1u)) break;
+        mbar_expect_tx(FULL_B(s), B_BYTES);
+        tma_load_2d(smem_base + (uint32_t)(s * B_BYTES), &tmap_x, FULL_B(s), (kt0 + i) * BK, t0);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(BF16, BM, BN);
-      for (int kt = 0; kt < p.nk; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
-        if (!mbar_wait(FULL_X(s), ph) || !mbar_wait(FULL_W(s), ph)) break;
+      constexpr uint32_t idesc = make_idesc(BF16, 128, BT);
+      for (int i = 0; i < nst; ++i) {
+        const int sb = i % B_STAGES, sa = i % A_STAGES;
+        const uint32_t pb = (uint32_t)(i / B_STAGES) & 1u, pa = (uint32_t)(i / A_STAGES) & 1u;
+        if (!mbar_wait(FULL_A(sa), pa) || !mbar_wait(FULL_B(sb), pb)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint64_t ad = sw128_desc(A_ADDR(s)), bd = sw128_desc(B_ADDR(s));
+        const uint64_t bd = sw128_desc(smem_base + (uint32_t)(sb * B_BYTES));
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          umma_f16(tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kt | k) != 0);
-        umma_commit(EMPTY(s));
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_ts(tmem + (uint32_t)(h * BT),
+                    tmem + (uint32_t)(ACC_COLS + sa * A_COLS + h * A_HALF_COLS + 8 * k),
+                    bd + (uint64_t)(2 * k), idesc, (i | k) != 0);
+        umma_commit(EMPTY_A(sa));
+        umma_commit(EMPTY_B(sb));
       }
       umma_commit(acc_full);  // arrives once every issued MMA has completed
     }
-  } else {
-    // ------------------------------------------------ dequantisers
-    const int r = threadIdx.x - 64;  // weight row within the tile
-    const int n = min(n0 + r, p.N - 1);
-    const bool row_ok = n0 + r < p.N;
-    bool ok = true;
-    for (int kt = 0; kt < p.nk && ok; kt += 2) {
-      // one 128-wide K group = stages kt and kt+1
-      const int gi = kt >> 1;
-      uint4 raw[8];
-      float dv[4] = {1.f, 1.f, 1.f, 1.f};
-      if (FMT == kW8F32 || FMT == kW8F16) {
-        const uint8_t* src = p.w + (size_t)n * p.K + (size_t)gi * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          raw[c] = (row_ok && gi * 128 + 16 * c < p.K)
-                       ? __ldg(reinterpret_cast<const uint4*>(src) + c)
-                       : make_uint4(0, 0, 0, 0);
-      } else {
-        constexpr int GB = FMT == kQ4 ? 64 : 128;
-        const uint8_t* src = p.w + (size_t)n * p.G * GB + (size_t)gi * GB;
-#pragma unroll
-        for (int c = 0; c < GB / 16; ++c) raw[c] = __ldg(reinterpret_cast<const uint4*>(src) + c);
-        const uint2 dd =
-            __ldg(reinterpret_cast<const uint2*>(p.gd + gguf_d_index(n, 4 * gi, p.G)));
-        dv[0] = __low2float(bits_h2(dd.x));
-        dv[1] = __high2float(bits_h2(dd.x));
-        dv[2] = __low2float(bits_h2(dd.y));
-        dv[3] = __high2float(bits_h2(dd.y));
-        if (!row_ok) dv[0] = dv[1] = dv[2] = dv[3] = 0.f;
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int st = kt + h;
-        if (st >= p.nk) break;
-        const int s = st % STAGES;
-        const uint32_t ph = (uint32_t)(st / STAGES) & 1u;
-        if (!mbar_wait(EMPTY(s), ph ^ 1u)) {
-          ok = false;
-          break;
-        }
-        const uint32_t tile = B_ADDR(s);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          // chunk c of this stage = group-local K [64h + 8c, 64h + 8c + 8)
-          const int cg = 8 * h + c;  // 0..15 within the group
-          uint4 v;
-          if (FMT == kW8F32 || FMT == kW8F16) {
-            const uint4& q = raw[cg >> 1];
-            v = (cg & 1) ? chunk_from_i8<BF16, false>(q.z, q.w, 1.f, __half2())
-                         : chunk_from_i8<BF16, false>(q.x, q.y, 1.f, __half2());
-          } else {
-            const int j = cg >> 2, qq = cg & 3;  // block j, quarter qq of its 32 values
-            const float d = dv[j];
-            const __half2 dh = __float2half2_rn(d);  // exact: d is an f16 value
-            if (FMT == kQ4) {
-              // lane-chunks t = 2*(qq&1) and +1 hold the bytes; low nibbles for qq < 2
-              const uint32_t w0 = word(raw[2 * (qq & 1)], j), w1 = word(raw[2 * (qq & 1) + 1], j);
-              uint32_t o0, o1, o2, o3;
-              nib4<BF16>(w0, qq >= 2, d, dh, o0, o1);
-              nib4<BF16>(w1, qq >= 2, d, dh, o2, o3);
-              v = make_uint4(o0, o1, o2, o3);
-            } else {
-              // Q8_0: lane-chunk t occupies raw[2t], raw[2t+1]; block j's low-half word
-              // is word 2j of the 32-byte chunk, its high-half word is 2j+1
-              const int t0 = 2 * (qq & 1), wsel = 2 * j + (qq >> 1);
-              const uint32_t w0 = word(raw[2 * t0 + (wsel >> 2)], wsel & 3);
-              const uint32_t w1 = word(raw[2 * (t0 + 1) + (wsel >> 2)], wsel & 3);
-              v = chunk_from_i8<BF16, true>(w0, w1, d, dh);
-            }
-          }
-          st_shared16(tile + sw128_off(r, c), v);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(FULL_W(s));
-      }
-    }
-
-    // ------------------------------------------------ epilogue
-    const int ew = warp - 2;                // 0..7
-    const int quarter = warp & 3;           // TMEM lanes this warp may read
-    const int col0 = (ew >> 2) * (BN / 2);  // two warps per lane quarter split the columns
-    const bool acc_ok = ok && mbar_wait(acc_full, 0);
-    __syncwarp();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (__all_sync(0xffffffffu, acc_ok)) {
-      const int row = m0 + quarter * 32 + lane;  // activation row (token)
-      for (int c = 0; c < BN / 2; c += 16) {
-        float v[16];
-        __syncwarp();
-        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c), v);
-        const int nb = n0 + col0 + c;
-        if (row < p.M && nb < p.N) epilogue_store<FMT, BF16, YT>(p, row, nb, v);
+  } else if (warp == 2 + DQ_WARPS) {
+    // ------------------------------------------------ TMA producer (packed weights)
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w) : "memory");
+      constexpr uint32_t tx = L::W_BYTES + L::D_BYTES;
+      for (int g = g0; g < g1; ++g) {
+        const int i = g - g0, s = i % W_STAGES;
+        if (!mbar_wait(EMPTY_W(s), ((uint32_t)(i / W_STAGES) & 1u) ^ 1u)) break;
+        mbar_expect_tx(FULL_W(s), tx);
+        tma_load_2d(smem_base + (uint32_t)(L::W_OFF + s * L::W_BYTES), &tmap_w, FULL_W(s),
+                    g * L::GB, n0);
+        if (L::GGUF)
+          tma_load_2d(smem_base + (uint32_t)(L::D_OFF + s * L::D_BYTES), &tmap_d, FULL_W(s),
+                      g * 128, n0 / 16);
       }
     }
   }
-#undef FULL_X
+
+  // ------------------------------------------------ dequantisers, then the epilogue
+  const bool dq = warp >= 2 && warp < 2 + DQ_WARPS;
+  const int quarter = warp & 3;             // TMEM lanes this warp may access
+  const int half = ((warp - 2) >> 2) & 1;   // weight half
+  const int kh = (warp - 2) >> 3;           // K half of each stage (and token half of the epilogue)
+  const int row = half * 128 + quarter * 32 + lane;  // weight row within the tile
+  const int n = n0 + row;
+  const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+  bool ok = true;
+  if (dq) {
+    const uint32_t a_col = (uint32_t)(ACC_COLS + half * A_HALF_COLS + kh * (A_HALF_COLS / 2));
+    int pend = -1;  // A slot written whose FULL_A arrival is still due
+    auto publish = [&]() {
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(FULL_A(pend));
+      pend = -1;
+    };
+    for (int g = g0; g < g1 && ok; ++g) {
+      const int gi = g - g0, ws = gi % W_STAGES;
+      // warp-uniform outcomes: tcgen05.st below needs every lane
+      const bool have = mbar_wait(FULL_W(ws), (uint32_t)(gi / W_STAGES) & 1u);
+      if (!__all_sync(0xffffffffu, have)) {
+        ok = false;
+        break;
+      }
+      uint4 raw[8];
+      float dv[4];
+      read_group<FMT>(smem_base + (uint32_t)(L::W_OFF + ws * L::W_BYTES),
+                      smem_base + (uint32_t)(L::D_OFF + ws * L::D_BYTES), row, raw, dv);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int kt = 2 * g + h;
+        if (kt >= kt1) break;
+        const int i = kt - kt0, sa = i % A_STAGES;
+        uint32_t wv[16];
+        dequant_part<FMT, BF16>(h, kh, raw, dv, wv);
+        if (pend >= 0) publish();
+        const bool free = mbar_wait(EMPTY_A(sa), ((uint32_t)(i / A_STAGES) & 1u) ^ 1u);
+        if (!__all_sync(0xffffffffu, free)) {
+          ok = false;
+          break;
+        }
+        tmem_st16(tmem + lane_base + a_col + (uint32_t)(sa * A_COLS), wv);
+        pend = sa;
+      }
+      // The slot is released only after the tcgen05.st above consumed values
+      // computed from it: the shared-memory loads have then returned, so the
+      // producer's next TMA write cannot overtake them.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(EMPTY_W(ws));
+    }
+    if (ok && pend >= 0) publish();
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(acc_full, 0));
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  }
+
+  // epilogue: warp (quarter, half, kh) owns token columns [64 kh, 64 kh + 64) of its rows
+  const uint32_t acc = tmem + lane_base + (uint32_t)(half * BT);
+  if (S == 1) {
+    if (dq && ok) {
+      const float sc = row_scale<FMT>(p, n);
+      for (int c = kh * (BT / 2); c < (kh + 1) * (BT / 2); c += 16) {
+        float v[16];
+        tmem_ld16(acc + (uint32_t)c, v);
+        if (n < p.N && t0 + c < p.M) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            store4<YT>(p, t0 + c + i, n, sc, make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+        }
+      }
+    }
+  } else {
+    // split-K: CTA z of the cluster owns token columns [z W, z W + W).  Every
+    // CTA pushes each slice of its partial tile into the owner's receive
+    // buffer (remote stores, no round trip), and after one cluster barrier the
+    // owner adds the S partials in rank order from its own shared memory.
+    const int W = BT / S, RS = W + 4;
+    float* red = reinterpret_cast<float*>(smem);
+    __syncwarp();
+    cluster_sync_all();  // every CTA is past its main loop: the receive buffers (rings) are free
+    if (dq && ok) {
+      for (int c = kh * (BT / 2); c < (kh + 1) * (BT / 2); c += 16) {
+        float v[16];
+        tmem_ld16(acc + (uint32_t)c, v);
+        const int z = c / W, cc = c - z * W;  // W >= 16: the 16 columns have one owner
+        const uint32_t dst = cluster_map(
+            smem_base + (uint32_t)(((split * BW + row) * RS + cc) * 4), (uint32_t)z);
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) st_cluster_v4(dst + 4u * i, v[i], v[i + 1], v[i + 2], v[i + 3]);
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // every push has landed; no shared memory is touched remotely after this
+    if (dq && ok && n < p.N) {
+      const float sc = row_scale<FMT>(p, n);
+      const int tb = t0 + split * W;
+      for (int cc = kh * (W / 2); cc < (kh + 1) * (W / 2) && tb + cc < p.M; cc += 4) {
+        float4 a = *reinterpret_cast<const float4*>(red + (row * RS + cc));
+        for (int r = 1; r < S; ++r) {
+          const float4 v = *reinterpret_cast<const float4*>(red + ((r * BW + row) * RS + cc));
+          a.x += v.x;
+          a.y += v.y;
+          a.z += v.z;
+          a.w += v.w;
+        }
+        store4<YT>(p, tb + cc, n, sc, a);
+      }
+    }
+  }
+#undef FULL_B
+#undef EMPTY_B
+#undef FULL_A
+#undef EMPTY_A
 #undef FULL_W
-#undef EMPTY
-#undef A_ADDR
-#undef B_ADDR
+#undef EMPTY_W
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -501,7 +696,7 @@ dial_status make_x_map(CUtensorMap* map, const void* x, bool bf16, int64_t M, in
   if (!enc) return fail(DIAL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {BK, BM};
+  const cuuint32_t box[2] = {BK, BT};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                    2, const_cast<void*>(x), dims, strides, box, estr,
@@ -511,17 +706,89 @@ dial_status make_x_map(CUtensorMap* map, const void* x, bool bf16, int64_t M, in
   return DIAL_OK;
 }
 
+// K splits for a grid of `tiles` CTAs over `ngr` K groups: the fewest waves of
+// clusters times the K groups each CTA runs, plus a fixed cost per wave
+// (pipeline fill and epilogue, about 4 groups) and one group for the
+// cross-CTA reduction.  Cluster capacity comes from the occupancy API.
+template <auto KERN>
+int choose_split(int64_t tiles, int ngr, int smem_bytes) {
+  static int cap[64][kMaxSplit + 1];  // active CTAs per device and split (0: not queried)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  int best = 1;
+  double best_cost = 1e30;
+  for (int S = 1; S <= kMaxSplit && S <= ngr; S *= 2) {
+    if (S > 1 && ngr / S < 2) break;
+    if (cap[dev][S] == 0) {
+      int clusters = 0;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, 1, (unsigned)S);
+      cfg.blockDim = dim3(THREADS);
+      cfg.dynamicSmemBytes = smem_bytes;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 1;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = (unsigned)S;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&clusters, KERN, &cfg) != cudaSuccess || clusters <= 0) {
+        cudaGetLastError();
+        clusters = S == 1 ? sm_count() : 0;
+      }
+      cap[dev][S] = clusters > 0 ? clusters * S : -1;
+    }
+    if (cap[dev][S] < 0) continue;
+    const double waves = (double)((tiles * S + cap[dev][S] - 1) / cap[dev][S]);
+    const double cost = waves * ((ngr + S - 1) / S + 4 + (S > 1 ? 1 : 0));
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = S;
+    }
+  }
+  return best;
+}
+
+// Tensor maps of the packed weights: rows of 128-K groups (GB bytes each) and,
+// for GGUF, the tile-major d array as [N / 16 tiles, G * 128 bytes].
+template <int FMT>
+dial_status make_w_maps(const Params& p, CUtensorMap* wmap, CUtensorMap* dmap) {
+  using L = Smem<FMT>;
+  if (!L::GGUF) {
+    dial_status s = tma::make_byte_map(wmap, p.w, p.N, p.K, 128, BW, 128);
+    *dmap = *wmap;  // unused
+    return s;
+  }
+  dial_status s = tma::make_byte_map(wmap, p.w, p.N, (int64_t)p.G * L::GB, L::GB, BW, L::GB);
+  if (s != DIAL_OK) return s;
+  return tma::make_byte_map(dmap, p.gd, (p.N + 15) / 16, (int64_t)p.G * 128, 128, BW / 16, 0);
+}
+
 template <int FMT, bool BF16, typename YT>
 dial_status launch_one(const CUtensorMap& map, const Params& p, cudaStream_t st) {
-  auto kern = dequant_gemm_kernel<FMT, BF16, YT>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  });
-  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(dequant_gemm)");
-  dim3 grid((unsigned)((p.M + BM - 1) / BM), (unsigned)((p.N + BN - 1) / BN));
-  kern<<<grid, THREADS, SMEM_BYTES, st>>>(map, p);
+  constexpr auto kern = dequant_gemm_kernel<FMT, BF16, YT>;
+  constexpr int smem = Smem<FMT>::BYTES;
+  CUtensorMap wmap, dmap;
+  dial_status ds = make_w_maps<FMT>(p, &wmap, &dmap);
+  if (ds != DIAL_OK) return ds;
+  cudaError_t e = ensure_smem<kern>(smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dequant_gemm)");
+  const int64_t wt = (p.N + BW - 1) / BW, tt = (p.M + BT - 1) / BT;
+  const int S = choose_split<kern>(wt * tt, (p.nk + 1) / 2, smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)wt, (unsigned)tt, (unsigned)S);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = (unsigned)S;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, map, wmap, dmap, p);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(dequant_gemm_kernel)");
   return check_launch("dequant_gemm_kernel");
 }
 
@@ -529,18 +796,20 @@ dial_status launch_one(const CUtensorMap& map, const Params& p, cudaStream_t st)
 
 namespace tma {
 dial_status make_byte_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
-                          int box_bytes, int box_rows, bool swizzle128) {
+                          int box_bytes, int box_rows, int swizzle_bytes) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(DIAL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  if (!aligned16(base) || row_bytes % 16 != 0 || (swizzle128 && box_bytes != 128))
+  if (!aligned16(base) || row_bytes % 16 != 0 || (swizzle_bytes && box_bytes != swizzle_bytes))
     return fail(DIAL_ERR_MISALIGNED, "tensor map: base and row pitch must be 16-byte aligned");
+  const CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                      : CU_TENSOR_MAP_SWIZZLE_NONE;
   const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
   const cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(DIAL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return DIAL_OK;

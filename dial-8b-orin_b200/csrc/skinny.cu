@@ -1211,7 +1211,7 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
   dial_status s = DIAL_OK;
   if (sk_ws && K >= 128 && aligned16(q)) {
     CUtensorMap map;
-    s = tma::make_byte_map(&map, q, N, K, 128, 16, /*swizzle128=*/true);
+    s = tma::make_byte_map(&map, q, N, K, 128, 16, 128);
     if (s != DIAL_OK) return s;
     const GemvPlan pl = plan_gemv(tiles, ng);
     float* slots = static_cast<float*>(sk_ws);
@@ -1306,7 +1306,7 @@ dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, co
   if (sk_ws && aligned16(qs) && aligned16(d)) {
     const int GB = type == DIAL_GGML_Q4_0 ? 64 : 128;
     CUtensorMap map;
-    s = tma::make_byte_map(&map, qs, N, G * GB, GB, 16, type != DIAL_GGML_Q4_0);
+    s = tma::make_byte_map(&map, qs, N, G * GB, GB, 16, type != DIAL_GGML_Q4_0 ? 128 : 0);
     if (s != DIAL_OK) return s;
     const GemvPlan pl = plan_gemv(tiles, G);
     float* slots = static_cast<float*>(sk_ws);

@@ -102,9 +102,10 @@ __device__ __forceinline__ void fence_barrier_init() {
 
 // ---------------------------------------------------------------- host side
 // 2D tensor map over a row-major [rows, row_bytes] byte matrix with a
-// {box_bytes, box_rows} box (SWIZZLE_128B needs box_bytes == 128).
+// {box_bytes, box_rows} box; swizzle_bytes 0 (none), 64 or 128 (SWIZZLE_64B /
+// SWIZZLE_128B, which need box_bytes == swizzle_bytes).
 dial_status make_byte_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
-                          int box_bytes, int box_rows, bool swizzle128);
+                          int box_bytes, int box_rows, int swizzle_bytes);
 
 }  // namespace tma
 }  // namespace dial

@@ -445,6 +445,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #define EMPTY_W(s) (bar_base + 8u * (uint32_t)(2 * B_STAGES + 2 * A_STAGES + W_STAGES + (s)))
   const uint32_t acc_full = bar_base + 8u * (uint32_t)(NBARS - 1);
 
+  // Programmatic dependent launch: the next kernel may be scheduled now; only
+  // the activation producer waits for the previous kernel (weights and scales
+  // are constant, so their loads and dequantisation start at once).
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BW;  // weight rows
   const int t0 = blockIdx.y * BT;  // tokens
@@ -489,6 +493,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------ TMA producer (tokens)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x) : "memory");
+      pdl_wait();
       for (int i = 0; i < nst; ++i) {
         const int s = i % B_STAGES;
         const uint32_t ph = (uint32_t)(i / B_STAGES) & 1u;
@@ -664,11 +669,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-template <typename XT>
-__global__ void to_f16_kernel(const XT* __restrict__ x, __half* __restrict__ out, int64_t n) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = __float2half_rn(Act<XT>::to_f32(x[i]));
+// f32 activations -> f16 operands, 8 values per thread (n is a multiple of 64).
+__global__ void to_f16_kernel(const float* __restrict__ x, __half* __restrict__ out, int64_t n8) {
+  pdl_begin();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(x) + 2 * i);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(x) + 2 * i + 1);
+    const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+    const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(h2_bits(h0), h2_bits(h1), h2_bits(h2), h2_bits(h3));
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -780,13 +791,15 @@ dial_status launch_one(const CUtensorMap& map, const Params& p, cudaStream_t st)
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 1;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = (unsigned)S;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, map, wmap, dmap, p);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(dequant_gemm_kernel)");
   return check_launch("dequant_gemm_kernel");
@@ -848,10 +861,10 @@ dial_status launch_gguf_gemm_sm100(const void* x, dial_dtype xdt, const void* qs
   const bool bf = xdt == DIAL_BF16;
   if (xdt == DIAL_F32) {  // the tensor cores take f16 operands: convert once
     __half* xh = static_cast<__half*>(ws);
-    const int64_t n = M * K;
-    const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 16);
-    to_f16_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(x), xh, n);
-    dial_status s = check_launch("to_f16_kernel");
+    const int64_t n8 = M * K / 8;
+    const unsigned grid = (unsigned)std::min<int64_t>((n8 + 255) / 256, (int64_t)sm_count() * 8);
+    dial_status s = launch_pdl("to_f16_kernel", to_f16_kernel, dim3(grid), dim3(256), 0, st,
+                               static_cast<const float*>(x), xh, n8);
     if (s != DIAL_OK) return s;
     xin = xh;
   }

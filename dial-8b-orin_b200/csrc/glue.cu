@@ -17,6 +17,7 @@
 //   argmax        qwen3_vl.rs:130-143 (greedy sampling on the device).
 #include <algorithm>
 #include <cfloat>
+#include <type_traits>
 
 #include "common.cuh"
 #include "glue.cuh"
@@ -143,123 +144,10 @@ __global__ void qk_rope_kv_kernel(const T* __restrict__ qkv, const T* __restrict
 // ------------------------------------------------------------------ attention
 // Query token t attends cache rows 0..pos[t] of slot[t] (decode: one token per
 // sequence; prefill: a run of tokens of one sequence, causal through pos).
-// CTA = (token, kv head, key split); 8 warps stream the split's keys (warp w
-// takes keys k0+w, k0+w+8, ...), lanes own 4 of the 128 dims, so every K/V row
-// is one coalesced 256-byte warp load shared by the n_rep query heads of the
-// group.  Each warp keeps an online softmax (running max / sum / output); the
-// 8 warps are merged in shared memory; splits are merged by the combine step.
-// Scores are in the log2 domain (q pre-scaled by log2(e)/sqrt(D)), f32 math.
-constexpr int kAttnWarps = 8;
-
-template <typename T>
-__device__ __forceinline__ void ld4(const T* p, float (&v)[4]) {
-  if constexpr (sizeof(T) == 4) {
-    const float4 u = __ldg(reinterpret_cast<const float4*>(p));
-    v[0] = u.x, v[1] = u.y, v[2] = u.z, v[3] = u.w;
-  } else {
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-    const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = Act<T>::to_f32(e[i]);
-  }
-}
-
-template <typename T, int REP>
-__global__ void __launch_bounds__(kAttnWarps * 32)
-    attention_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
-                     const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
-                     T* __restrict__ out, float* __restrict__ part, int hq, int hkv,
-                     int64_t max_seq, int nsplit, float qscale) {
-  pdl_begin();
-  constexpr int D = 128;
-  __shared__ float sm_m[kAttnWarps][REP], sm_l[kAttnWarps][REP];
-  __shared__ float sm_o[kAttnWarps][REP][D];
-  const int64_t t = blockIdx.x;
-  const int g = blockIdx.y, split = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int len = pos[t] + 1;
-  const int per = (len + nsplit - 1) / nsplit;
-  const int k0 = split * per, k1 = min(len, k0 + per);
-  const int64_t s = slot[t];
-  const T* kbase = kc + ((s * hkv + g) * max_seq) * D + 4 * lane;
-  const T* vbase = vc + ((s * hkv + g) * max_seq) * D + 4 * lane;
-  float qv[REP][4];
-#pragma unroll
-  for (int r = 0; r < REP; ++r) {
-    ld4(q + (t * hq + g * REP + r) * D + 4 * lane, qv[r]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) qv[r][i] *= qscale;
-  }
-  float m[REP], l[REP], o[REP][4];
-#pragma unroll
-  for (int r = 0; r < REP; ++r) {
-    m[r] = -FLT_MAX;
-    l[r] = 0.f;
-    o[r][0] = o[r][1] = o[r][2] = o[r][3] = 0.f;
-  }
-  constexpr int U = 4;  // keys per iteration (loads issued together)
-  for (int j0 = k0 + warp; j0 < k1; j0 += kAttnWarps * U) {
-    float kv[U][4], vv[U][4];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int j = min(j0 + u * kAttnWarps, k1 - 1);
-      ld4(kbase + (int64_t)j * D, kv[u]);
-      ld4(vbase + (int64_t)j * D, vv[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (j0 + u * kAttnWarps >= k1) break;
-#pragma unroll
-      for (int r = 0; r < REP; ++r) {
-        const float sc = warp_sum(qv[r][0] * kv[u][0] + qv[r][1] * kv[u][1] + qv[r][2] * kv[u][2] +
-                                  qv[r][3] * kv[u][3]);
-        const float nm = fmaxf(m[r], sc);
-        const float corr = exp2f(m[r] - nm), p = exp2f(sc - nm);
-        l[r] = l[r] * corr + p;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[r][i] = fmaf(p, vv[u][i], o[r][i] * corr);
-        m[r] = nm;
-      }
-    }
-  }
-  // merge the warps
-#pragma unroll
-  for (int r = 0; r < REP; ++r) {
-    if (lane == 0) {
-      sm_m[warp][r] = m[r];
-      sm_l[warp][r] = l[r];
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sm_o[warp][r][4 * lane + i] = o[r][i];
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < REP * D; idx += kAttnWarps * 32) {
-    const int r = idx / D, d = idx % D;
-    float M = -FLT_MAX;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][r]);
-    float L = 0.f, O = 0.f;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
-      if (sm_m[w][r] == -FLT_MAX) continue;  // warp saw no key
-      const float f = exp2f(sm_m[w][r] - M);
-      L += sm_l[w][r] * f;
-      O += sm_o[w][r][d] * f;
-    }
-    const int64_t head = t * hq + g * REP + r;
-    if (nsplit == 1) {
-      out[head * D + d] = rnd<T>(O / L);
-    } else {
-      float* pp = part + (head * nsplit + split) * (D + 2);
-      if (d == 0) {
-        pp[0] = M;  // -FLT_MAX for an empty split
-        pp[1] = L;
-      }
-      pp[2 + d] = O;
-    }
-  }
-}
-
+// CTA = (token, kv head, key split); the n_rep query heads of the group share
+// every K/V row.  Scores are in the log2 domain (log2(e)/sqrt(D) applied to the
+// f32 dot products), softmax and accumulation in f32; splits are merged by the
+// combine step.
 template <typename T>
 __global__ void attention_combine_kernel(const float* __restrict__ part, T* __restrict__ out,
                                          int nchunks) {
@@ -279,6 +167,242 @@ __global__ void attention_combine_kernel(const float* __restrict__ part, T* __re
     acc += pp[c * (D + 2) + 2 + d] * f;
   }
   out[head * D + d] = rnd<T>(acc / sum);
+}
+
+// ------------------------------------------------------------------ attention on tensor cores
+// f16/bf16 caches: the same (token, kv head, key split) CTAs, but each of the 4
+// warps takes 16-key tiles (tiles w, w+4, ... of the split) and computes
+//   S = Q K^T  (mma.m16n8k16: rows = the n_rep query heads of the group, padded
+//               to 16; 8 k-steps over the head dim; two 8-key n-tiles)
+//   O += P V   (P from the score fragments, split into hi + lo parts of the
+//               operand type so that P keeps 16+ significant bits; 16 n-tiles
+//               of 8 dims)
+// with the online softmax in f32 on the score fragments (row max / sum over
+// the 4 lanes of a quad).  K/V tiles stream through a 2-deep per-warp ring of
+// cp.async copies into XOR-swizzled shared memory (16-byte chunk c of key row
+// r at chunk (c & 8) | ((c ^ r) & 7)), read back with ldmatrix (.trans for V).
+// The warps merge in shared memory; splits leave (max, sum, O) partials for the
+// combine step.
+constexpr int kTcWarps = 4;
+constexpr int kTcTile = 16;                         // keys per tile
+constexpr int kTcTileBytes = kTcTile * 128 * 2;     // one K or V tile (4 KB)
+constexpr int kTcWarpBytes = 2 * 2 * kTcTileBytes;  // 2 stages x (K, V)
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t tc_swz(int r, int c) {
+  return (uint32_t)(r * 256 + (((c & 8) | ((c ^ r) & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <typename T>
+__device__ __forceinline__ void mma_tc(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                       uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (sizeof(T) == 2 && std::is_same<T, __half>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+// (a, b) -> operand pair, and the pair of what rounding left behind
+template <typename T>
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const T ha = Act<T>::from_f32(a), hb = Act<T>::from_f32(b);
+  const T la = Act<T>::from_f32(a - Act<T>::to_f32(ha)), lb = Act<T>::from_f32(b - Act<T>::to_f32(hb));
+  hi = (uint32_t)(*reinterpret_cast<const uint16_t*>(&ha)) |
+       ((uint32_t)(*reinterpret_cast<const uint16_t*>(&hb)) << 16);
+  lo = (uint32_t)(*reinterpret_cast<const uint16_t*>(&la)) |
+       ((uint32_t)(*reinterpret_cast<const uint16_t*>(&lb)) << 16);
+}
+
+template <typename T, int REP>
+__global__ void __launch_bounds__(kTcWarps * 32)
+    attention_tc_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
+                        const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
+                        T* __restrict__ out, float* __restrict__ part, int hq, int hkv,
+                        int64_t max_seq, int nsplit, float qscale) {
+  pdl_begin();
+  constexpr int D = 128;
+  extern __shared__ __align__(1024) uint8_t tc_smem[];
+  __shared__ float sm_m[kTcWarps][REP], sm_l[kTcWarps][REP];
+  __shared__ float sm_o[kTcWarps][REP][D];
+  const int64_t t = blockIdx.x;
+  const int g = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gr = lane >> 2, qd = lane & 3;  // fragment row (query head) and quad index
+  const int len = pos[t] + 1;
+  const int per = (len + nsplit - 1) / nsplit;
+  const int k0 = split * per, k1 = min(len, k0 + per);
+  const int64_t s = slot[t];
+  const T* kbase = kc + ((s * hkv + g) * max_seq) * D;
+  const T* vbase = vc + ((s * hkv + g) * max_seq) * D;
+  const uint32_t wbuf = smem_addr(tc_smem) + (uint32_t)(warp * kTcWarpBytes);
+
+  // Q fragments: row gr = query head g*REP + gr (zero above REP), k-step ks
+  uint32_t qa[8][2];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    qa[ks][0] = qa[ks][1] = 0u;
+    if (gr < REP) {
+      const uint32_t* qr = reinterpret_cast<const uint32_t*>(q + (t * hq + g * REP + gr) * D);
+      qa[ks][0] = qr[(16 * ks + 2 * qd) >> 1];
+      qa[ks][1] = qr[(16 * ks + 8 + 2 * qd) >> 1];
+    }
+  }
+
+  const int ntile = k1 > k0 ? (k1 - k0 + kTcTile - 1) / kTcTile : 0;
+  // issue the copies of tile i (keys k0 + 16 i ..) into stage st of this warp
+  auto fetch = [&](int i, int st) {
+    const int kb = k0 + i * kTcTile;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int ch = lane + 32 * u, r = ch >> 4, c = ch & 15;
+      const int key = min(kb + r, k1 - 1);  // rows past the split repeat its last key (masked)
+      const uint32_t off = tc_swz(r, c);
+      cp_async16(wbuf + (uint32_t)(st * 2 * kTcTileBytes) + off, kbase + (int64_t)key * D + c * 8);
+      cp_async16(wbuf + (uint32_t)(st * 2 * kTcTileBytes + kTcTileBytes) + off,
+                 vbase + (int64_t)key * D + c * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  float m = -FLT_MAX, l = 0.f;  // row gr (only gr < REP is a real head)
+  float o[16][4];
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+
+  int st = 0;
+  if (warp < ntile) fetch(warp, 0);
+  for (int i = warp; i < ntile; i += kTcWarps) {
+    const bool more = i + kTcWarps < ntile;
+    if (more) fetch(i + kTcWarps, st ^ 1);
+    if (more) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+    const uint32_t kt = wbuf + (uint32_t)(st * 2 * kTcTileBytes), vt = kt + kTcTileBytes;
+    // ---- S = Q K^T for keys kb .. kb+15
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const int mi = lane >> 3, ri = lane & 7;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kt + tc_swz((mi >> 1) * 8 + ri, 2 * ks + (mi & 1)), b0, b1, b2, b3);
+      mma_tc<T>(sc[0], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+      mma_tc<T>(sc[1], qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+    }
+    // ---- online softmax on row gr: this lane holds keys 2qd, 2qd+1, 8+2qd, 9+2qd
+    const int kb = k0 + i * kTcTile;
+    float p[4] = {sc[0][0] * qscale, sc[0][1] * qscale, sc[1][0] * qscale, sc[1][1] * qscale};
+    const int kk[4] = {2 * qd, 2 * qd + 1, 8 + 2 * qd, 9 + 2 * qd};
+    float mx = -FLT_MAX;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (kb + kk[j] >= k1) p[j] = -FLT_MAX;
+      mx = fmaxf(mx, p[j]);
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m, mx);
+    const float corr = exp2f(m - mn);
+    m = mn;
+    float ps = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      p[j] = exp2f(p[j] - mn);
+      ps += p[j];
+    }
+    l = l * corr + ps;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      o[nt][0] *= corr;
+      o[nt][1] *= corr;
+    }
+    uint32_t ph0, pl0, ph1, pl1;
+    split_pair<T>(p[0], p[1], ph0, pl0);
+    split_pair<T>(p[2], p[3], ph1, pl1);
+    // ---- O += P V over 16 dim n-tiles
+#pragma unroll
+    for (int nt = 0; nt < 16; nt += 2) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vt + tc_swz((mi & 1) * 8 + ri, nt + (mi >> 1)), b0, b1, b2, b3);
+      mma_tc<T>(o[nt], ph0, 0u, ph1, 0u, b0, b1);
+      mma_tc<T>(o[nt], pl0, 0u, pl1, 0u, b0, b1);
+      mma_tc<T>(o[nt + 1], ph0, 0u, ph1, 0u, b2, b3);
+      mma_tc<T>(o[nt + 1], pl0, 0u, pl1, 0u, b2, b3);
+    }
+    __syncwarp();  // every lane is done with this stage before it is refilled
+    st ^= 1;
+  }
+  // row sums over the quad
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+
+  // ---- merge the warps (a warp without tiles keeps m = -FLT_MAX, l = 0)
+  if (gr < REP) {
+    if (qd == 0) {
+      sm_m[warp][gr] = m;
+      sm_l[warp][gr] = l;
+    }
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      sm_o[warp][gr][8 * nt + 2 * qd] = o[nt][0];
+      sm_o[warp][gr][8 * nt + 2 * qd + 1] = o[nt][1];
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < REP * D; idx += kTcWarps * 32) {
+    const int r = idx / D, d = idx % D;
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, sm_m[w][r]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kTcWarps; ++w) {
+      if (sm_l[w][r] == 0.f) continue;  // warp saw no key
+      const float f = exp2f(sm_m[w][r] - M);
+      L += sm_l[w][r] * f;
+      O += sm_o[w][r][d] * f;
+    }
+    const int64_t head = t * hq + g * REP + r;
+    if (nsplit == 1) {
+      out[head * D + d] = Act<T>::from_f32(O / L);
+    } else {
+      float* pp = part + (head * nsplit + split) * (D + 2);
+      if (d == 0) {
+        pp[0] = L > 0.f ? M : -FLT_MAX;  // -FLT_MAX for an empty split
+        pp[1] = L;
+      }
+      pp[2 + d] = O;
+    }
+  }
 }
 
 // ------------------------------------------------------------------ SwiGLU
@@ -442,10 +566,11 @@ dial_status launch_qk_rope_kv(const void* qkv, const void* qn, const void* kn, c
   return s;
 }
 
-// Key splits per (token, kv head): enough CTAs for ~2 per SM, at least 64 keys each.
+// Key splits per (token, kv head): enough CTAs for ~2 per SM, at least 128 keys
+// each (8 tiles of 16 keys, two per warp of the tensor-core kernel).
 static int attention_splits(int64_t tokens, int hkv, int64_t max_len) {
   const int64_t want = (2 * (int64_t)sm_count() + tokens * hkv - 1) / (tokens * hkv);
-  const int64_t cap = (max_len + 63) / 64;
+  const int64_t cap = (max_len + 127) / 128;
   return (int)std::max<int64_t>(1, std::min(want, cap));
 }
 
@@ -453,6 +578,25 @@ size_t attention_workspace_bytes(int64_t tokens, int hq, int64_t max_len) {
   // hkv is not known here: size for the largest split count any hkv >= 1 gives
   const int64_t nch = attention_splits(tokens, 1, max_len);
   return nch > 1 ? (size_t)(tokens * hq * nch * (128 + 2)) * sizeof(float) : 0;
+}
+
+// One (dtype, n_rep) instance of the tensor-core attention.
+template <typename T, int REP>
+dial_status launch_attention_rep(dim3 grid, const void* q, const void* kc, const void* vc,
+                                 const int32_t* pos, const int32_t* slot, void* out, void* ws,
+                                 int hq, int hkv, int64_t max_seq, int nch, float qscale,
+                                 cudaStream_t st) {
+  if constexpr (sizeof(T) != 2) {
+    return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "attention: f16/bf16 caches only");
+  } else {
+    constexpr int smem = kTcWarps * kTcWarpBytes;
+    const cudaError_t e = ensure_smem<attention_tc_kernel<T, REP>>(smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention_tc_kernel)");
+    return launch_pdl("attention_tc_kernel", attention_tc_kernel<T, REP>, grid, dim3(kTcWarps * 32),
+                      smem, st, static_cast<const T*>(q), static_cast<const T*>(kc),
+                      static_cast<const T*>(vc), pos, slot, static_cast<T*>(out),
+                      static_cast<float*>(ws), hq, hkv, max_seq, nch, qscale);
+  }
 }
 
 dial_status launch_attention(const void* q, const void* kc, const void* vc, const int32_t* pos,
@@ -464,21 +608,15 @@ dial_status launch_attention(const void* q, const void* kc, const void* vc, cons
   dim3 grid((unsigned)tokens, (unsigned)hkv, (unsigned)nch);
   const int rep = hq / hkv;
   dial_status s = DIAL_OK;
-#define ATT(REP_)                                                                                \
-  s = launch_pdl("attention_kernel", attention_kernel<T, REP_>, grid, dim3(kAttnWarps * 32), 0, st, \
-                 static_cast<const T*>(q), static_cast<const T*>(kc), static_cast<const T*>(vc),  \
-                 pos, slot, static_cast<T*>(out), static_cast<float*>(ws), hq, hkv, max_seq, nch, \
-                 qscale)
   DISPATCH_T(dt, {
-    switch (rep) {
-      case 1: ATT(1); break;
-      case 2: ATT(2); break;
-      case 4: ATT(4); break;
-      case 8: ATT(8); break;
-      default: return fail(DIAL_ERR_SHAPE, "attention supports Hq/Hkv in {1,2,4,8}");
-    }
+    auto fn = rep == 1   ? launch_attention_rep<T, 1>
+              : rep == 2 ? launch_attention_rep<T, 2>
+              : rep == 4 ? launch_attention_rep<T, 4>
+              : rep == 8 ? launch_attention_rep<T, 8>
+                         : nullptr;
+    if (!fn) return fail(DIAL_ERR_SHAPE, "attention supports Hq/Hkv in {1,2,4,8}");
+    s = fn(grid, q, kc, vc, pos, slot, out, ws, hq, hkv, max_seq, nch, qscale, st);
   });
-#undef ATT
   if (s != DIAL_OK || nch == 1) return s;
   DISPATCH_T(dt, {
     s = launch_pdl("attention_combine_kernel", attention_combine_kernel<T>,

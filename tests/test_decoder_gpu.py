@@ -133,34 +133,59 @@ def _attn_ref(q, kc, vc, pos, slot, Hkv):
     return out.reshape(T, Hq * Dh)
 
 
-@pytest.mark.parametrize("mode", ["decode", "prefill", "long"])
-def test_attention(D, torch, mode):
-    rng = np.random.default_rng({"decode": 1, "prefill": 2, "long": 3}[mode])
-    Hq, Hkv, Dh, slots = 32, 8, 128, 4
-    S = 1300 if mode == "long" else 256
+def _cast(x, dt):
+    """float32 array -> (array the kernel reads, float64 values it holds)."""
+    if dt == "f16":
+        h = x.astype(np.float16)
+        return h, h.astype(np.float64)
+    if dt == "bf16":
+        b = O.f32_to_bf16(x)
+        return b.view(np.int16), O.bf16_to_f32(b).astype(np.float64)
+    return x.astype(np.float32), x.astype(np.float64)
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("mode,Hq", [("decode", 32), ("prefill", 32), ("long", 32), ("decode", 8),
+                                     ("decode", 16), ("decode", 64), ("batched", 32)])
+def test_attention(D, torch, mode, Hq, dt):
+    """Decode (one token per sequence), prefill (causal run of one sequence),
+    long contexts (several key splits + combine), n_rep 1/2/4/8, and the batched
+    decode of 32 sequences with ~2k-token caches; f16/bf16 caches run on the
+    tensor-core kernel."""
+    rng = np.random.default_rng({"decode": 1, "prefill": 2, "long": 3, "batched": 4}[mode] + Hq)
+    Hkv, Dh, slots = 8, 128, 4
+    S = {"long": 1300, "batched": 2100}.get(mode, 256)
     if mode == "decode":
         pos = np.array([0, 5, 200, 255], np.int32)
         slot = np.array([0, 1, 2, 3], np.int32)
     elif mode == "prefill":
         pos = np.arange(40, dtype=np.int32)
         slot = np.full(40, 2, np.int32)
-    else:  # several 512-key chunks, combine step
+    elif mode == "long":  # several key splits, combine step
         pos = np.array([1299, 700, 511, 512], np.int32)
         slot = np.array([0, 1, 2, 3], np.int32)
+    else:
+        slots = 32
+        pos = rng.integers(2000, 2100, 32).astype(np.int32)
+        slot = rng.permutation(32).astype(np.int32)
     T = len(pos)
-    q = rng.normal(0, 1, (T, Hq, Dh)).astype(np.float16)
-    kc = rng.normal(0, 1, (slots, Hkv, S, Dh)).astype(np.float16)
-    vc = rng.normal(0, 1, (slots, Hkv, S, Dh)).astype(np.float16)
-    out = torch.empty((T, Hq * Dh), dtype=torch.float16, device="cuda")
+    q, q64 = _cast(rng.normal(0, 1, (T, Hq, Dh)).astype(np.float32), dt)
+    kc, k64 = _cast(rng.normal(0, 1, (slots, Hkv, S, Dh)).astype(np.float32), dt)
+    vc, v64 = _cast(rng.normal(0, 1, (slots, Hkv, S, Dh)).astype(np.float32), dt)
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dt]
+    out = torch.empty((T, Hq * Dh), dtype=tdt, device="cuda")
     max_len = int(pos.max()) + 1
     need = D.lib().dial_attention_workspace_bytes(T, Hq, max_len)
     ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
     t_in = [dev(torch, a) for a in (q, kc, vc, pos, slot)]
+    code = {"f16": D.F16, "bf16": D.BF16, "f32": D.F32}[dt]
     D.check(D.lib().dial_attention(*[t.data_ptr() for t in t_in], out.data_ptr(),
-                                   ws.data_ptr() if need else None, need, D.F16, T, Hq, Hkv, Dh, S,
+                                   ws.data_ptr() if need else None, need, code, T, Hq, Hkv, Dh, S,
                                    max_len, D.stream_ptr()), "attention")
-    ref = _attn_ref(q, kc, vc, pos, slot, Hkv)
-    assert rel(out.cpu().numpy(), ref) <= 3e-3
+    ref = _attn_ref(q64, k64, v64, pos, slot, Hkv)
+    got = out.float().cpu().numpy()
+    # output rounding of the type (f16 2^-11, bf16 2^-8) plus f32 accumulation
+    assert rel(got, ref) <= {"f16": 3e-3, "bf16": 1e-2}[dt]
 
 
 def test_swiglu_embedding_argmax(D, torch):

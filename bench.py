@@ -230,15 +230,39 @@ class W8A16Gemv:
     def bytes(cls):
         return cls.N * cls.K + 2 * cls.N + 2 * cls.M * cls.K + 2 * cls.M * cls.N
 
+    chain = 16  # GEMVs per chained graph (steps per replay)
+
     def run_copy(self, li):
         self.lins[li].forward(self.x, out=self.y)
 
     def build_graphs(self):
+        """Per-copy graphs, plus one graph of `chain` consecutive GEMVs cycling
+        through the copies, so that a Python-side replay per 25 us GEMV does not
+        starve the GPU: a step is still one GEMV over a weight copy not in L2."""
         build_copy_graphs(self)
+        torch = self.torch
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.run_copy(0)  # the stream's linear workspace
+        torch.cuda.synchronize()
+        self.chain_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.chain_graph, stream=side):
+            for k in range(self.chain):
+                self.run_copy(k % self.copies)
+        torch.cuda.synchronize()
+        self.config["launch"] = f"CUDA graph of {self.chain} consecutive GEMVs (PDL between them)"
 
     def step(self):
         self.graphs[self.i % self.copies].replay()
         self.i += 1
+
+    def run_steps(self, n):
+        """n steps: whole chains, then single GEMVs for the remainder."""
+        for _ in range(n // self.chain):
+            self.chain_graph.replay()
+        for _ in range(n % self.chain):
+            self.step()
 
     def step_e2e(self):
         """Through the public API with host buffers: H2D x, linear, D2H y."""
@@ -731,6 +755,8 @@ def run_ours(args, rank, local, world):
         wl.build_graphs()
     for _ in range(max(args.warmup, 3)):
         wl.step()
+    if hasattr(wl, "chain_graph"):
+        wl.chain_graph.replay()  # the chained graph's first replay uploads it
     torch.cuda.synchronize()
     assert D.lib().dial_device_error(1) == 0
 
@@ -743,10 +769,13 @@ def run_ours(args, rank, local, world):
         w0 = time.perf_counter()
         torch.cuda.nvtx.range_push("timed")  # lets a profiler select the timed steps
         t_begin.record(stream)
-        for i in range(args.steps):
-            starts[i].record(stream)
-            wl.step()
-            ends[i].record(stream)
+        if hasattr(wl, "run_steps"):  # chained launches: no per-step events
+            wl.run_steps(args.steps)
+        else:
+            for i in range(args.steps):
+                starts[i].record(stream)
+                wl.step()
+                ends[i].record(stream)
         t_end.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
@@ -755,7 +784,10 @@ def run_ours(args, rank, local, world):
     if hasattr(wl, "finish"):
         wl.finish()
     total_ms = max_over_ranks(t_begin.elapsed_time(t_end), world)
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    if hasattr(wl, "run_steps"):
+        step_ms = [t_begin.elapsed_time(t_end) / args.steps] * args.steps
+    else:
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     assert D.lib().dial_device_error(1) == 0
 
     e2e = None

@@ -110,6 +110,7 @@ __device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
   for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
 }
 
+
 // ------------------------------------------------------------------ W8A16 pieces
 // acc += W[row0:row0+16, groups g0..g1) . x^T (this lane's fragment)
 template <int NT, bool BF16>
@@ -596,16 +597,16 @@ __device__ __forceinline__ void tile_finish(const GemvPlan& pl, float* __restric
 // the f16 MMA biased: 1152 + q, built from the byte by one byte permute under
 // the f16 exponent of 1024 (plus one xor per 4 bytes), without the subtraction
 // of the exact conversion.  Per row, sum_k (1152 + q_k) x_k - 1152 sum_k x_k is
-// the wanted sum_k q_k x_k; the sums of x per 128-wide group are staged next
-// to x (fixed order, so results stay deterministic) and subtracted per segment.
-// Every (1152 + q) x product is exact in f32, as the plain products are; the
-// sums are rounded at a larger magnitude, a relative change of about 1e-5 of
-// the result, below the f16/bf16 rounding of the output.  bf16 inputs are
-// scaled per token by a power of two that puts max|x| in [2^13, 2^14) and
+// the wanted sum_k q_k x_k; the second term is one more MMA per k-step with
+// every weight -1152 (exact in f16), so no sums of x are staged.  Every
+// (1152 + q) x and 1152 x product is exact in f32, as the plain products are;
+// the accumulation runs at a larger magnitude, a relative change of about
+// 1e-5 of the result, below the f16/bf16 rounding of the output.  bf16 inputs
+// are scaled per token by a power of two that puts max|x| in [2^13, 2^14) and
 // rounded to f16 (exact for every value within 2^27 of the max); the output
-// is scaled back by the same power of two.
+// is scaled back by the same power of two.  f16 inputs are staged unscaled.
 constexpr int kXsBytes = 32 * 1024;
-constexpr float kQBias = 1152.0f;
+constexpr uint32_t kNegBiasF16x2 = 0xE480E480u;  // (-1152, -1152) in f16
 
 // Barrier 1 over the first `threads` threads of the CTA (the warps with work).
 __device__ __forceinline__ void active_warps_sync(int threads) {
@@ -650,49 +651,65 @@ __device__ __forceinline__ uint4 pack8(const uint32_t (&o)[8]) {
   return make_uint4(o[0] | (o[1] << 16), o[2] | (o[3] << 16), o[4] | (o[5] << 16), o[6] | (o[7] << 16));
 }
 
-// Shared-memory scratch of the staging, after x: group sums [ng][M] (<= 160
-// floats), per-token multipliers [M], per-token 1/rms [M], per-chunk sums
-// [M*K/8] (<= 2048 floats).
-constexpr int kAuxGs = 0, kAuxTm = 1024, kAuxInv = 1152, kAuxCs = 1280;
+// Shared-memory scratch of the staging, after x: per-token max |input| [M],
+// per-token 1/rms [M], per-token output multipliers [M], per-chunk sums of
+// squares [M*K/8] (<= 2048 floats).
+constexpr int kAuxTm = 0, kAuxInv = 128, kAuxMul = 256, kAuxCs = 384;
 constexpr int kXsAux = kAuxCs + 2048 * 4;
 constexpr int kXsSmem = kTmaSmem + kXsBytes + kXsAux;
 
 // Stages the linear's input for rows [0, M) as f16 into xsm (see the section
-// comment), with the per-group sums and per-token multipliers for the kernel.
-// The input is p.mode's function of x: x itself; rmsnorm(x + res) * w (the
-// sum h = x + res, rounded to the activation dtype, also written to h_out by
-// CTA 0); or swiglu of gate_up = x [M, 2K].  Rounding follows the standalone
-// kernels (rmsnorm_kernel, swiglu_kernel): every tensor those produce is
-// rounded to the activation dtype here too.  The sums of squares of a row are
-// added in a fixed order (per chunk, then per warp lane, then a shuffle tree),
-// so the staged values do not depend on timing.  Run by the CTA's first
-// `active` threads; ends with a barrier.
+// comment), with the per-token multipliers for the kernel.  The input is
+// p.mode's function of x: x itself; rmsnorm(x + res) * w (the sum h = x + res,
+// rounded to the activation dtype, also written to h_out by CTA 0); or swiglu
+// of gate_up = x [M, 2K].  Rounding follows the standalone kernels
+// (rmsnorm_kernel, swiglu_kernel): every tensor those produce is rounded to the
+// activation dtype here too.  The sums of squares of a row are added in a
+// fixed order (per chunk, then per warp lane, then a shuffle tree), so the
+// staged values do not depend on timing.  bf16 needs max|input| per token for
+// its scale: for the normalised input that is estimated as max|h w| / rms (it
+// only picks a power of two).  Run by the CTA's first `active` threads; ends
+// with a barrier.
 template <bool BF16>
 __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* __restrict__ x, int M,
-                                          int K, int ng, uint32_t xsm, uint32_t aux, int active) {
-  const uint32_t gs = aux + kAuxGs, tm = aux + kAuxTm, tinv = aux + kAuxInv, cs = aux + kAuxCs;
+                                          int K, uint32_t xsm, uint32_t aux, int active) {
+  const uint32_t tm = aux + kAuxTm, tinv = aux + kAuxInv, tmul = aux + kAuxMul, cs = aux + kAuxCs;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarp = active >> 5;
   const int per_tok = K / 8, n16 = M * per_tok;
+  // per-token output multiplier 2^e (bf16) or 1, once the token's max is final
+  auto put_mul = [&]() {
+    if (tid < M) sts32f(tmul + 4u * tid, BF16 ? ldexpf(1.0f, tok_exp(lds32f(tm + 4u * tid))) : 1.0f);
+  };
   const uint4 z = make_uint4(0, 0, 0, 0);
-  if (tid < M) sts32f(tm + 4u * tid, 0.0f);  // running max |input| per token (bits compare as ints)
+  unsigned int* tmax = reinterpret_cast<unsigned int*>(__cvta_shared_to_generic(tm));
+  if (BF16) {  // running max |input| per token (non-negative floats compare as ints)
+    if (tid < M) sts32f(tm + 4u * tid, 0.0f);
+    active_warps_sync(active);
+  }
+  auto amax = [&](int m, float v) {
+    if (BF16) atomicMax(tmax + m, __float_as_uint(v));
+  };
   if (p.mode == kProRms) {
     for (int c = tid; c < n16; c += active) {
-      const int m = c / per_tok;
-      const size_t off = (size_t)m * K + (size_t)(c - m * per_tok) * 8;
+      const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
+      const size_t off = (size_t)m * K + (size_t)k8;
       const uint4 xv = ld_ro16(x + off), rv = p.res ? ld_ro16(p.res + off) : z;
+      const uint4 wv = ld_ro16(p.w + k8);
       uint32_t o[8];
-      float ss = 0.0f;
+      float ss = 0.0f, mx = 0.0f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         float h = act_f32<BF16>(h16(xv, i));
         if (p.res) h = act_f32<BF16>(act_rnd<BF16>(h + act_f32<BF16>(h16(rv, i))));
         o[i] = act_rnd<BF16>(h);
         ss += h * h;
+        mx = fmaxf(mx, fabsf(h * act_f32<BF16>(h16(wv, i))));
       }
       const uint4 hv = pack8(o);
       if (blockIdx.x == 0 && p.h_out) *reinterpret_cast<uint4*>(p.h_out + off) = hv;
       sts16(xsm + 16u * (uint32_t)c, hv);
       sts32f(cs + 4u * (uint32_t)c, ss);
+      amax(m, mx);
     }
     active_warps_sync(active);
     for (int m = warp; m < M; m += nwarp) {
@@ -700,79 +717,82 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
       for (int c = lane; c < per_tok; c += 32) s += lds32f(cs + 4u * (uint32_t)(m * per_tok + c));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) sts32f(tinv + 4u * m, rsqrtf(s / (float)K + p.eps));
+      if (lane == 0) {
+        const float inv = rsqrtf(s / (float)K + p.eps);
+        sts32f(tinv + 4u * m, inv);
+        if (BF16) sts32f(tm + 4u * m, lds32f(tm + 4u * m) * inv);
+      }
     }
-  } else if (p.mode == kProSwiglu) {
-    for (int c = tid; c < n16; c += active) {
+    active_warps_sync(active);
+    put_mul();
+    for (int c = tid; c < n16; c += active) {  // normalise in place, scaled to f16
       const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
-      const uint16_t* gu = x + (size_t)m * 2 * K;
-      const uint4 gv = ld_ro16(gu + k8), uv = ld_ro16(gu + K + k8);
+      const uint4 hv = lds16(xsm + 16u * (uint32_t)c), wv = ld_ro16(p.w + k8);
+      const float inv = lds32f(tinv + 4u * m);
+      const int e = BF16 ? tok_exp(lds32f(tm + 4u * m)) : 0;
       uint32_t o[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float gg = act_f32<BF16>(h16(gv, i));
-        const float s = act_f32<BF16>(act_rnd<BF16>(gg / (1.0f + expf(-gg))));
-        o[i] = act_rnd<BF16>(s * act_f32<BF16>(h16(uv, i)));
+        const float v =
+            act_f32<BF16>(act_rnd<BF16>(act_f32<BF16>(h16(hv, i)) * inv * act_f32<BF16>(h16(wv, i))));
+        o[i] = __half_as_ushort(__float2half_rn(BF16 ? ldexpf(v, -e) : v));
       }
       sts16(xsm + 16u * (uint32_t)c, pack8(o));
     }
-  }
-  active_warps_sync(active);
-  // the input values of chunk c, as floats (exact in the activation dtype)
-  auto input8 = [&](int c, float (&v)[8]) {
-    const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
-    if (p.mode == kProX) {
-      const uint4 xv = ld_ro16(x + (size_t)m * K + k8);
+  } else {
+    // x itself or swiglu(gate, up), rounded to the activation dtype.  f16: one
+    // pass writes the staged values.  bf16: pass 1 takes the max (and keeps
+    // swiglu's values in xsm, computed once), pass 2 writes the scaled f16.
+    auto input8 = [&](int c, float (&v)[8]) {
+      const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
+      if (p.mode == kProX) {
+        const uint4 xv = ld_ro16(x + (size_t)m * K + k8);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(xv, i));
-    } else if (p.mode == kProRms) {
-      const uint4 hv = lds16(xsm + 16u * (uint32_t)c), wv = ld_ro16(p.w + k8);
-      const float inv = lds32f(tinv + 4u * m);
+        for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(xv, i));
+      } else {
+        const uint16_t* gu = x + (size_t)m * 2 * K;
+        const uint4 gv = ld_ro16(gu + k8), uv = ld_ro16(gu + K + k8);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        v[i] = act_f32<BF16>(act_rnd<BF16>(act_f32<BF16>(h16(hv, i)) * inv * act_f32<BF16>(h16(wv, i))));
-    } else {
-      const uint4 yv = lds16(xsm + 16u * (uint32_t)c);
+        for (int i = 0; i < 8; ++i) {
+          const float gg = act_f32<BF16>(h16(gv, i));
+          const float sl = act_f32<BF16>(act_rnd<BF16>(gg / (1.0f + expf(-gg))));
+          v[i] = act_f32<BF16>(act_rnd<BF16>(sl * act_f32<BF16>(h16(uv, i))));
+        }
+      }
+    };
+    if (BF16) {
+      for (int c = tid; c < n16; c += active) {
+        float v[8];
+        input8(c, v);
+        float mx = 0.0f;
+        uint32_t o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(yv, i));
+        for (int i = 0; i < 8; ++i) {
+          mx = fmaxf(mx, fabsf(v[i]));
+          o[i] = act_rnd<BF16>(v[i]);
+        }
+        if (p.mode != kProX) sts16(xsm + 16u * (uint32_t)c, pack8(o));
+        amax(c / per_tok, mx);
+      }
+      active_warps_sync(active);
     }
-  };
-  for (int c = tid; c < n16; c += active) {
-    float v[8];
-    input8(c, v);
-    float mx = 0.0f;
+    put_mul();
+    for (int c = tid; c < n16; c += active) {
+      float v[8];
+      if (BF16 && p.mode != kProX) {
+        const uint4 yv = lds16(xsm + 16u * (uint32_t)c);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[i]));
-    atomicMax(reinterpret_cast<unsigned int*>(__cvta_shared_to_generic(tm + 4u * (c / per_tok))),
-              __float_as_uint(mx));
-  }
-  active_warps_sync(active);
-  for (int c = tid; c < n16; c += active) {
-    float v[8];
-    input8(c, v);
-    const int e = tok_exp(__uint_as_float(
-        reinterpret_cast<const unsigned int*>(__cvta_shared_to_generic(tm))[c / per_tok]));
-    uint32_t o[8];
-    float s = 0.0f;
+        for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(yv, i));
+      } else {
+        input8(c, v);
+      }
+      const int e = BF16 ? tok_exp(__uint_as_float(tmax[c / per_tok])) : 0;
+      uint32_t o[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const __half h = __float2half_rn(ldexpf(v[i], -e));
-      o[i] = __half_as_ushort(h);
-      s += __half2float(h);
+      for (int i = 0; i < 8; ++i) o[i] = __half_as_ushort(__float2half_rn(BF16 ? ldexpf(v[i], -e) : v[i]));
+      sts16(xsm + 16u * (uint32_t)c, pack8(o));
     }
-    sts16(xsm + 16u * (uint32_t)c, pack8(o));
-    sts32f(cs + 4u * (uint32_t)c, s);
   }
-  active_warps_sync(active);
-  // group sums: thread (g, m) adds the chunk sums of its group in k order
-  for (int idx = tid; idx < ng * M; idx += active) {
-    const int gi = idx / M, m = idx - gi * M;
-    const int c0 = m * per_tok + gi * 16, c1 = m * per_tok + min(per_tok, gi * 16 + 16);
-    float s = 0.0f;
-    for (int c = c0; c < c1; ++c) s += lds32f(cs + 4u * (uint32_t)c);
-    sts32f(gs + 4u * (uint32_t)idx, s);
-  }
-  if (tid < M) sts32f(tm + 4u * tid, ldexpf(1.0f, tok_exp(lds32f(tm + 4u * tid))));
   active_warps_sync(active);
 }
 
@@ -790,7 +810,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
   constexpr bool kF16Mma = XS || !BF16;  // staged activations are f16
   extern __shared__ uint8_t smem_raw[];
   const Ring ring = warp_ring(smem_raw);
-  const uint32_t xsm = ring_end(smem_raw), gs = xsm + kXsBytes + kAuxGs, tm = xsm + kXsBytes + kAuxTm;
+  const uint32_t xsm = ring_end(smem_raw), tm = xsm + kXsBytes + kAuxMul;
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int wpc = blockDim.x >> 5;
   const int w = blockIdx.x * wpc + (threadIdx.x >> 5);
@@ -809,7 +829,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
   if (lane == 0)  // the weights are constant: prefetch before the previous kernel ends
     while (pr.issued < kStages && !pr.ended) pr.refill(ring, load);
   pdl_wait();  // x, y and the workspace belong to the stream's earlier kernels
-  if (XS) stage_act<BF16>(pro, x, M, K, pl.ng, xsm, xsm + kXsBytes, min(wpc, pl.NW - (int)blockIdx.x * wpc) * 32);
+  if (XS) stage_act<BF16>(pro, x, M, K, xsm, xsm + kXsBytes, min(wpc, pl.NW - (int)blockIdx.x * wpc) * 32);
   auto store = [&](int tile, const float (&a)[NT][4]) {
     if (XS) {  // undo the per-token power-of-two scale of the staged activations
       float b[NT][4];
@@ -825,9 +845,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     }
   };
   const uint16_t* xr[NT];
-  uint32_t xo[NT];     // XS: byte offset of this lane's token row in shared memory
-  uint32_t so[NT][2];  // XS: group-sum offsets of the lane's two output tokens
-  bool sv[NT][2];      //     and whether those tokens exist
+  uint32_t xo[NT];  // XS: byte offset of this lane's token row in shared memory
   bool tv[NT];
 #pragma unroll
   for (int j = 0; j < NT; ++j) {
@@ -835,29 +853,9 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     tv[j] = tok < M;
     xr[j] = x + (size_t)(tv[j] ? tok : 0) * K + 32 * t;
     xo[j] = xsm + (uint32_t)(((tv[j] ? tok : 0) * K + 32 * t) * 2);
-    const int t0 = j * 8 + 2 * t;
-    sv[j][0] = t0 < M, sv[j][1] = t0 + 1 < M;
-    so[j][0] = gs + 4u * (uint32_t)t0, so[j][1] = so[j][0] + 4u;
   }
-  float acc[NT][4], corr[NT][2];
+  float acc[NT][4];
   zero_acc(acc);
-  auto zero_corr = [&]() {
-#pragma unroll
-    for (int j = 0; j < NT; ++j) corr[j][0] = corr[j][1] = 0.0f;
-  };
-  auto apply_corr = [&]() {  // subtract the weight bias times the segment's x sums
-    if (XS) {
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        acc[j][0] = fmaf(-kQBias, corr[j][0], acc[j][0]);
-        acc[j][1] = fmaf(-kQBias, corr[j][1], acc[j][1]);
-        acc[j][2] = fmaf(-kQBias, corr[j][0], acc[j][2]);
-        acc[j][3] = fmaf(-kQBias, corr[j][1], acc[j][3]);
-      }
-      zero_corr();
-    }
-  };
-  zero_corr();
   const int first_tile = (int)div_u((uint64_t)ubegin(pl, w), (uint64_t)pl.ng);
   int cur = -1, units = 0;
   const uint4 z = make_uint4(0, 0, 0, 0);
@@ -871,10 +869,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     const int tile = (int)info.x, gi = (int)info.y;
     if (tile < 0) break;
     if (tile != cur) {
-      if (cur >= 0) {
-        apply_corr();
-        tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
-      }
+      if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
       zero_acc(acc);
       cur = tile;
       units = 0;
@@ -891,9 +886,6 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
         xv[j][1] = (tv[j] && v0) ? lds16(a + 16) : z;
         xv[j][2] = (tv[j] && v1) ? lds16(a + 32) : z;
         xv[j][3] = (tv[j] && v1) ? lds16(a + 48) : z;
-        const uint32_t go = 4u * (uint32_t)(gi * M);
-        if (sv[j][0]) corr[j][0] += lds32f(so[j][0] + go);
-        if (sv[j][1]) corr[j][1] += lds32f(so[j][1] + go);
       } else {
         xv[j][0] = (tv[j] && v0) ? ld_ro16(xr[j] + kb) : z;
         xv[j][1] = (tv[j] && v0) ? ld_ro16(xr[j] + kb + 8) : z;
@@ -928,14 +920,13 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
           const uint32_t b0 = word(xs, 2 * (st & 1)), b1 = word(xs, 2 * (st & 1) + 1);
           if (kF16Mma) mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
           else mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
+          if (XS)  // minus 1152 x: the weights' bias
+            mma_f16(acc[j], kNegBiasF16x2, kNegBiasF16x2, kNegBiasF16x2, kNegBiasF16x2, b0, b1);
         }
       }
     }
   }
-  if (cur >= 0) {
-    apply_corr();
-    tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
-  }
+  if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
 }
 
 template <int NT, int TYPE, typename YT>

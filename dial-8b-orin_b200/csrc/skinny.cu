@@ -380,7 +380,12 @@ struct GemvPlan {
   int ng;     // 128-wide K groups
   int NW;     // warps
   int64_t W;  // units, tiles * ng
+  int mode;   // kStreamK, or kTileCta: CTA c takes tiles c, c + C, ...; its warp j
+              // the groups [ng j / 8, ng (j + 1) / 8) of each; partials meet in
+              // shared memory (no global fixup)
+  int C;      // CTAs (kTileCta)
 };
+constexpr int kStreamK = 0, kTileCta = 1;
 
 // a / b with a 32-bit division whenever both fit (a 64-bit one is a long routine)
 __device__ __forceinline__ int64_t div_u(uint64_t a, uint64_t b) {
@@ -481,7 +486,9 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 }
 
 // Lane 0's side of a warp: which unit goes into the next stage -- the next
-// unit of its static range, then the end marker.
+// unit of its static range, then the end marker.  kTile: the kernel may run a
+// kTileCta plan.
+template <bool kTile>
 struct Producer {
   GemvPlan pl;
   int64_t su, su1;  // next unit, end
@@ -489,7 +496,17 @@ struct Producer {
   int issued;
   bool ended;
 
+  // kTileCta: su, su1 hold this warp's groups [su, su1) of every tile
+
   __device__ Producer(const GemvPlan& p, int w) : pl(p), issued(0), ended(false) {
+    if (kTile && pl.mode == kTileCta) {
+      const int j = w % kTmaWarps;
+      su = pl.ng * j / kTmaWarps;
+      su1 = pl.ng * (j + 1) / kTmaWarps;
+      st = w / kTmaWarps;
+      sg = (int)su;
+      return;
+    }
     su = ubegin(pl, w);
     su1 = ubegin(pl, w + 1);
     st = (int)div_u((uint64_t)su, (uint64_t)pl.ng);
@@ -501,7 +518,8 @@ struct Producer {
     if (ended) return;
     const int s = issued & (kStages - 1);
     ++issued;
-    if (su >= su1) {
+    const bool done = (kTile && pl.mode == kTileCta) ? st >= pl.tiles : su >= su1;
+    if (done) {
       sts8(ring.info + 8u * (uint32_t)s, -1, 0);
       mbar_arrive(ring.bar + 8u * (uint32_t)s);
       ended = true;
@@ -509,6 +527,13 @@ struct Producer {
     }
     sts8(ring.info + 8u * (uint32_t)s, st, sg);
     load(s, ring.bar + 8u * (uint32_t)s, st, sg);
+    if (kTile && pl.mode == kTileCta) {
+      if (++sg == (int)su1) {
+        sg = (int)su;
+        st += pl.C;
+      }
+      return;
+    }
     if (++sg == pl.ng) {
       sg = 0;
       ++st;
@@ -621,6 +646,79 @@ __device__ __forceinline__ void sts32f(uint32_t a, float v) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
 
+// kTileCta: rounds of partial tiles kept in shared memory (the staging's
+// chunk-sum area, 8 KB: 512 B per warp and token group), and their counters:
+// cnt[r] arrivals, done[r] the last tile round reduced in slot r.
+template <int NT>
+__host__ __device__ constexpr int cta_rounds() { return NT == 1 ? 2 : 1; }
+
+__device__ __forceinline__ int atom_add_acq_rel_cta(uint32_t a, int v) {
+  int old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], %2;" : "=r"(old) : "r"(a), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ int ld_acquire_cta(uint32_t a) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.s32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_cta(uint32_t a, int v) {
+  asm volatile("st.release.cta.shared::cta.s32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+
+// Ends this warp's part of tile `tile`, the CTA's tile round `lt`: the
+// partial goes to slot (lt mod R, warp); the CTA's last warp to arrive adds
+// the 8 partials in warp order and stores the tile.  A warp R rounds ahead of
+// the slot's reduction waits for it (bounded; the flag reports an expiry).
+template <int NT, typename StoreFn>
+__device__ __forceinline__ void cta_tile_finish(uint32_t part, uint32_t ctr, int lt, int tile,
+                                                float (&acc)[NT][4], StoreFn& store, int* err) {
+  constexpr int R = cta_rounds<NT>();
+  const int lane = threadIdx.x & 31, j = (threadIdx.x >> 5) & (kTmaWarps - 1);
+  const int r = lt % R;
+  const uint32_t cnt = ctr + 8u * (uint32_t)r, done = cnt + 4u;
+  if (lt >= R) {  // slot r must hold no unreduced round
+    bool ok = true;
+    if (lane == 0) {
+      const unsigned long long t0 = tma::global_ns();
+      while (ld_acquire_cta(done) != lt - R) {
+        if (tma::global_ns() - t0 > tma::kWaitNs) {
+          atomicCAS(err, 0, (int)DIAL_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
+  }
+  const uint32_t slot = part + (uint32_t)((r * kTmaWarps + j) * NT * 512);
+#pragma unroll
+  for (int jj = 0; jj < NT; ++jj)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sts32f(slot + 4u * (uint32_t)((jj * 4 + e) * 32 + lane), acc[jj][e]);
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) old = atom_add_acq_rel_cta(cnt, 1);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old != kTmaWarps - 1) return;
+  __syncwarp();
+  float sum[NT][4];
+  zero_acc(sum);
+  for (int k = 0; k < kTmaWarps; ++k) {
+    const uint32_t sk = part + (uint32_t)((r * kTmaWarps + k) * NT * 512);
+#pragma unroll
+    for (int jj = 0; jj < NT; ++jj)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sum[jj][e] += lds32f(sk + 4u * (uint32_t)((jj * 4 + e) * 32 + lane));
+  }
+  __syncwarp();
+  if (lane == 0) {
+    asm volatile("st.shared.s32 [%0], %1;" ::"r"(cnt), "r"(0) : "memory");
+    st_release_cta(done, lt);
+  }
+  store(tile, sum);
+}
+
 // Four int8 -> two f16x2 holding 1152 + q (exact).
 __device__ __forceinline__ void i8x4_to_f16x2_biased(uint32_t w, uint32_t& lo, uint32_t& hi) {
   const uint32_t u = w ^ 0x80808080u;
@@ -652,9 +750,10 @@ __device__ __forceinline__ uint4 pack8(const uint32_t (&o)[8]) {
 }
 
 // Shared-memory scratch of the staging, after x: per-token max |input| [M],
-// per-token 1/rms [M], per-token output multipliers [M], per-chunk sums of
-// squares [M*K/8] (<= 2048 floats).
-constexpr int kAuxTm = 0, kAuxInv = 128, kAuxMul = 256, kAuxCs = 384;
+// per-token 1/rms [M], per-token output multipliers [M], the kTileCta round
+// counters, per-chunk sums of squares [M*K/8] (<= 2048 floats; after the
+// staging, the kTileCta partial tiles).
+constexpr int kAuxTm = 0, kAuxInv = 128, kAuxMul = 256, kAuxCnt = 384, kAuxCs = 448;
 constexpr int kXsAux = kAuxCs + 2048 * 4;
 constexpr int kXsSmem = kTmaSmem + kXsBytes + kXsAux;
 
@@ -682,6 +781,11 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
   };
   const uint4 z = make_uint4(0, 0, 0, 0);
   unsigned int* tmax = reinterpret_cast<unsigned int*>(__cvta_shared_to_generic(tm));
+  if (tid < 8) {  // kTileCta round counters: cnt[r] = 0, done[r] = r - 2 (no round yet)
+    asm volatile("st.shared.s32 [%0], %1;" ::"r"(aux + kAuxCnt + 4u * (uint32_t)tid),
+                 "r"((tid & 1) ? (tid >> 1) - 2 : 0)
+                 : "memory");
+  }
   if (BF16) {  // running max |input| per token (non-negative floats compare as ints)
     if (tid < M) sts32f(tm + 4u * tid, 0.0f);
     active_warps_sync(active);
@@ -821,7 +925,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
   }
   if (lane == 0) tma::prefetch_map(&wmap);
   ring_init(ring);
-  Producer pr(pl, w);
+  Producer<XS && NT <= 2> pr(pl, w);
   auto load = [&](int s, uint32_t bar, int tile, int gi) {
     tma::mbar_expect_tx(bar, kUnitBytes);
     tma::load_2d(ring.w + (uint32_t)(s * kUnitBytes), &wmap, bar, gi * 128, tile * 16);
@@ -857,8 +961,13 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
   float acc[NT][4];
   zero_acc(acc);
   const int first_tile = (int)div_u((uint64_t)ubegin(pl, w), (uint64_t)pl.ng);
-  int cur = -1, units = 0;
+  int cur = -1, units = 0, lt = 0;
   const uint4 z = make_uint4(0, 0, 0, 0);
+  const uint32_t part = xsm + kXsBytes + kAuxCs, ctr = xsm + kXsBytes + kAuxCnt;
+  auto finish = [&](int tile) {  // the end of this warp's part of `tile`
+    if (XS && NT <= 2 && pl.mode == kTileCta) cta_tile_finish<NT>(part, ctr, lt++, tile, acc, store, err);
+    else tile_finish<NT>(pl, slots, cnt, w, first_tile, tile, units, acc, store);
+  };
   for (int i = 0;; ++i) {
     if (!ring_wait(ring, i, err)) {
       if (lane == 0) drain_ring(ring, i, pr.issued);
@@ -869,7 +978,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     const int tile = (int)info.x, gi = (int)info.y;
     if (tile < 0) break;
     if (tile != cur) {
-      if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+      if (cur >= 0) finish(cur);
       zero_acc(acc);
       cur = tile;
       units = 0;
@@ -926,7 +1035,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
       }
     }
   }
-  if (cur >= 0) tile_finish<NT>(pl, slots, cnt, w, first_tile, cur, units, acc, store);
+  if (cur >= 0) finish(cur);
 }
 
 template <int NT, int TYPE, typename YT>
@@ -948,7 +1057,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
   }
   if (lane == 0) tma::prefetch_map(&qmap);
   ring_init(ring);
-  Producer pr(pl, w);
+  Producer<false> pr(pl, w);
   auto load = [&](int s, uint32_t bar, int tile, int gi) {
     tma::mbar_expect_tx(bar, BOX + kDBytes);
     tma::load_2d(ring.w + (uint32_t)(s * kUnitBytes), &qmap, bar, gi * GB, tile * 16);
@@ -1142,12 +1251,23 @@ int pick_split(int64_t tiles, int64_t groups) {
 }
 
 // Stream-K grid: at most kCtasPerSM x kTmaWarps warps per SM, at least kMinUnits units per warp.
-GemvPlan plan_gemv(int64_t tiles, int64_t ng) {
-  const int64_t resident = (int64_t)sm_count() * kCtasPerSM * kTmaWarps;
+// tile_ok: the kernel can reduce tiles in shared memory (staged activations,
+// at most 2 token groups).  With at least one tile per SM and one K group per
+// warp the CTAs take whole tiles (no global fixup); otherwise stream-K.
+GemvPlan plan_gemv(int64_t tiles, int64_t ng, bool tile_ok) {
+  const int64_t ctas = (int64_t)sm_count() * kCtasPerSM, resident = ctas * kTmaWarps;
   GemvPlan p;
   p.tiles = (int)tiles;
   p.ng = (int)ng;
   p.W = tiles * ng;
+  if (tile_ok && tiles >= sm_count() && ng >= kTmaWarps) {
+    p.mode = kTileCta;
+    p.C = (int)std::min<int64_t>(tiles, ctas);
+    p.NW = p.C * kTmaWarps;
+    return p;
+  }
+  p.mode = kStreamK;
+  p.C = 0;
   p.NW = (int)std::min<int64_t>(resident, std::max<int64_t>(1, p.W / kMinUnits));
   return p;
 }
@@ -1204,14 +1324,14 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
     CUtensorMap map;
     s = tma::make_byte_map(&map, q, N, K, 128, 16, 128);
     if (s != DIAL_OK) return s;
-    const GemvPlan pl = plan_gemv(tiles, ng);
+    const bool xs = M * K * 2 <= kXsBytes && aligned16(x);
+    const GemvPlan pl = plan_gemv(tiles, ng, xs && nt <= 2);
     float* slots = static_cast<float*>(sk_ws);
     int* cnt = reinterpret_cast<int*>(static_cast<uint8_t*>(sk_ws) + slot_bytes());
     int* err = device_error_ptr();
     if (!err) return fail(DIAL_ERR_CUDA, "device error flag is unavailable");
-    const int wpc = tma_warps_per_cta(pl.NW);
+    const int wpc = pl.mode == kTileCta ? kTmaWarps : tma_warps_per_cta(pl.NW);
     const dim3 grid((unsigned)((pl.NW + wpc - 1) / wpc)), block((unsigned)(wpc * 32));
-    const bool xs = M * K * 2 <= kXsBytes && aligned16(x);
     const size_t smem = (size_t)ring_bytes(wpc) + 1024 + (xs ? kXsBytes + kXsAux : 0);
     cudaError_t ae = cudaSuccess;
 #define SKX(NT_, BF, ST, XS)                                                                   \
@@ -1299,7 +1419,7 @@ dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, co
     CUtensorMap map;
     s = tma::make_byte_map(&map, qs, N, G * GB, GB, 16, type != DIAL_GGML_Q4_0 ? 128 : 0);
     if (s != DIAL_OK) return s;
-    const GemvPlan pl = plan_gemv(tiles, G);
+    const GemvPlan pl = plan_gemv(tiles, G, false);
     float* slots = static_cast<float*>(sk_ws);
     int* cnt = reinterpret_cast<int*>(static_cast<uint8_t*>(sk_ws) + slot_bytes());
     int* err = device_error_ptr();

@@ -118,6 +118,32 @@ def test_w8a16_linear_streamk_shapes(D, torch, M, N, K):
     assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
 
 
+@pytest.mark.parametrize("M,N,K,xdt", [(1, 12288, 1024, "f16"), (2, 40000, 1024, "bf16"),
+                                        (9, 4096, 1536, "f16"), (16, 2400, 1024, "bf16")])
+def test_w8a16_linear_tile_cta_shapes(D, torch, M, N, K, xdt):
+    """Many 16-row tiles with staged activations: whole tiles per CTA, the K
+    range split over its 8 warps and reduced in shared memory -- several tile
+    rounds per CTA (up to 8 for N = 40000), one or two token groups (one or two
+    shared-memory rounds).  Repeated calls must give bit-identical outputs."""
+    rng = np.random.default_rng(M * 11 + N + K)
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    x = rng.normal(0, 1, (M, K)).astype(np.float32)
+    lin = D.W8A16Linear.from_linear("t", _to_dev(torch, w))
+    if xdt == "f16":
+        xin = x.astype(np.float16)
+        xt = _to_dev(torch, xin)
+    else:
+        xin = O.f32_to_bf16(x)
+        xt = _to_dev(torch, xin.view(np.int16)).view(torch.bfloat16)
+    y1 = lin.forward(xt).float().cpu().numpy()
+    y2 = lin.forward(xt).float().cpu().numpy()
+    assert D.lib().dial_device_error(1) == 0
+    y_ref, _ = O.w8a16_linear(xin, lin.qweight.cpu().numpy(), lin.scales.cpu().numpy(),
+                              x_is_bf16=(xdt == "bf16"))
+    assert rel_err(y1, y_ref) <= (2e-3 if xdt == "f16" else 8e-3)
+    assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
+
+
 @pytest.mark.parametrize("amax", [3e4, 1e6, 2.0**-20])
 def test_w8a16_bf16_activation_range(D, torch, amax):
     """bf16 activations far outside the f16 range (and tiny ones) on the decode

@@ -958,13 +958,24 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     xr[j] = x + (size_t)(tv[j] ? tok : 0) * K + 32 * t;
     xo[j] = xsm + (uint32_t)(((tv[j] ? tok : 0) * K + 32 * t) * 2);
   }
-  float acc[NT][4];
+  // acc: the weight MMAs; accb: the bias MMAs (XS), a second dependency chain
+  // that interleaves with the first (added to acc when a tile part ends)
+  constexpr bool kBiasChain = XS && NT <= 2;
+  float acc[NT][4], accb[kBiasChain ? NT : 1][4];
   zero_acc(acc);
+  zero_acc(accb);
   const int first_tile = (int)div_u((uint64_t)ubegin(pl, w), (uint64_t)pl.ng);
   int cur = -1, units = 0, lt = 0;
   const uint4 z = make_uint4(0, 0, 0, 0);
   const uint32_t part = xsm + kXsBytes + kAuxCs, ctr = xsm + kXsBytes + kAuxCnt;
   auto finish = [&](int tile) {  // the end of this warp's part of `tile`
+    if (kBiasChain) {
+#pragma unroll
+      for (int j = 0; j < (kBiasChain ? NT : 1); ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[j][e] += accb[j][e];
+      zero_acc(accb);
+    }
     if (XS && NT <= 2 && pl.mode == kTileCta) cta_tile_finish<NT>(part, ctr, lt++, tile, acc, store, err);
     else tile_finish<NT>(pl, slots, cnt, w, first_tile, tile, units, acc, store);
   };
@@ -1030,7 +1041,8 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
           if (kF16Mma) mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
           else mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
           if (XS)  // minus 1152 x: the weights' bias
-            mma_f16(acc[j], kNegBiasF16x2, kNegBiasF16x2, kNegBiasF16x2, kNegBiasF16x2, b0, b1);
+            mma_f16(kBiasChain ? accb[kBiasChain ? j : 0] : acc[j], kNegBiasF16x2, kNegBiasF16x2,
+                    kNegBiasF16x2, kNegBiasF16x2, b0, b1);
         }
       }
     }

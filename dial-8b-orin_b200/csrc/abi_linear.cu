@@ -175,7 +175,7 @@ dial_status dial_gguf_linear(const void* x, dial_dtype xdt, const void* qs, cons
   cudaStream_t st = as_stream(stream);
   void* sk = workspace;
   void* act = static_cast<uint8_t*>(workspace) + gemv_workspace_bytes(N);
-  if (M > kSkinnyMaxM && gemm_sm100_supported(M, K, N))
+  if (gemm_sm100_supported(M, K, N))
     return launch_gguf_gemm_sm100(x, xdt, qs, d, type, y, M, K, N, act, st);
   const size_t xsz = xdt == DIAL_F32 ? 4 : 2;
   for (int64_t m0 = 0; m0 < M; m0 += kSkinnyMaxM) {

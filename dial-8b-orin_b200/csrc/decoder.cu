@@ -95,7 +95,7 @@ dial_status linear(const dial_decoder_dims& d, int fmt, dial_linear_ref W, const
     return DIAL_OK;
   }
   const uint16_t* dd = static_cast<const uint16_t*>(W.s);
-  if (T > kSkinnyMaxM && gemm_sm100_supported(T, K, N))
+  if (gemm_sm100_supported(T, K, N))
     return launch_gguf_gemm_sm100(x, xdt, W.w, dd, fmt, y, T, K, N, lin_ws, st);
   const size_t e = xdt == DIAL_F32 ? 4 : 2;
   for (int64_t m0 = 0; m0 < T; m0 += kSkinnyMaxM) {

@@ -55,22 +55,18 @@ __device__ int g_device_error = 0;
 namespace {
 
 constexpr int BW = 256;   // weight rows per CTA (two UMMA M = 128 halves)
-constexpr int BT = 128;   // activation rows (tokens) per CTA (UMMA N)
+// BT: activation rows (tokens) per CTA (UMMA N), a template parameter: 128,
+// or 32 for at most 32 rows (batched decode), where wider tiles would spend
+// most MMA cycles on padding
 constexpr int BK = 64;    // K per stage (one 128-byte swizzle atom of f16/bf16)
 constexpr int B_STAGES = 4;  // token tiles in shared memory
 constexpr int A_STAGES = 4;  // dequantised weight stages in TMEM
 constexpr int W_STAGES = 4;  // packed weight groups (128 K) in shared memory
-constexpr int B_BYTES = BT * BK * 2;  // 16 KB token tile per stage
-constexpr int ACC_COLS = 2 * BT;      // two f32 accumulators of BT columns
 constexpr int A_HALF_COLS = BK / 2;   // TMEM columns of one weight half per stage
 constexpr int A_COLS = 2 * A_HALF_COLS;
 constexpr int TMEM_COLS = 512;
-static_assert(ACC_COLS + A_STAGES * A_COLS <= TMEM_COLS, "TMEM budget");
 constexpr int DQ_WARPS = 16;  // 4 per TMEM lane quarter: weight half x K half of a stage
 constexpr int THREADS = 64 + DQ_WARPS * 32 + 32;  // + the weight producer warp
-// split-K receive buffer of the owning CTA: [S senders][BW rows][BT / S + 4] f32
-// (the +4 pad keeps the 8 rows of a quarter warp's float4 accesses in distinct banks)
-constexpr int RED_BYTES = BW * 4 * (BT + 4 * 8);
 constexpr int kMaxSplit = 8;
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
 
@@ -79,8 +75,16 @@ enum Fmt { kW8F32 = 0, kW8F16 = 1, kQ4 = 2, kQ8 = 3 };
 // Shared memory of one CTA: [token ring | packed weight ring | GGUF d ring],
 // every stage 1024-byte aligned (the swizzle atoms); the split-K partial tile
 // reuses it after the main loop.
-template <int FMT>
+template <int FMT, int BT>
 struct Smem {
+  static constexpr int B_BYTES = BT * BK * 2;  // token tile per stage
+  static constexpr int ACC_COLS = 2 * BT;      // two f32 accumulators of BT columns
+  static_assert(ACC_COLS + A_STAGES * A_COLS <= TMEM_COLS, "TMEM budget");
+  // split-K: at most BT / 4 CTAs (each owns whole float4 column groups); the
+  // owner's receive buffer is [S senders][BW rows][BT / S + 4] f32 (the +4 pad
+  // keeps the 8 rows of a quarter warp's float4 accesses in distinct banks)
+  static constexpr int MAX_SPLIT = BT / 4 < kMaxSplit ? BT / 4 : kMaxSplit;
+  static constexpr int RED_BYTES = BW * 4 * (BT + 4 * MAX_SPLIT);
   static constexpr bool GGUF = FMT == kQ4 || FMT == kQ8;
   static constexpr int GB = FMT == kQ4 ? 64 : 128;  // packed bytes of a row per 128-K group
   static constexpr int W_BYTES = BW * GB;
@@ -422,12 +426,13 @@ __device__ __forceinline__ void store4(const Params& p, int t0, int n, float sc,
     if (t0 + i < p.M) y[(size_t)(t0 + i) * p.N + n] = Act<YT>::from_f32(a[i] * sc);
 }
 
-template <int FMT, bool BF16, typename YT>
+template <int FMT, bool BF16, typename YT, int BT>
 __global__ void __launch_bounds__(THREADS, 1)
     dequant_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_d, const Params p) {
-  using L = Smem<FMT>;
+  using L = Smem<FMT, BT>;
+  constexpr int B_BYTES = L::B_BYTES, ACC_COLS = L::ACC_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -628,11 +633,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = kh * (BT / 2); c < (kh + 1) * (BT / 2); c += 16) {
         float v[16];
         tmem_ld16(acc + (uint32_t)c, v);
-        const int z = c / W, cc = c - z * W;  // W >= 16: the 16 columns have one owner
-        const uint32_t dst = cluster_map(
-            smem_base + (uint32_t)(((split * BW + row) * RS + cc) * 4), (uint32_t)z);
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) st_cluster_v4(dst + 4u * i, v[i], v[i + 1], v[i + 2], v[i + 3]);
+        for (int i = 0; i < 16; i += 4) {  // W is a multiple of 4: a float4 has one owner
+          const int z = (c + i) / W, cc = c + i - z * W;
+          const uint32_t dst = cluster_map(
+              smem_base + (uint32_t)(((split * BW + row) * RS + cc) * 4), (uint32_t)z);
+          st_cluster_v4(dst, v[i], v[i + 1], v[i + 2], v[i + 3]);
+        }
       }
     }
     __syncwarp();
@@ -640,7 +647,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (dq && ok && n < p.N) {
       const float sc = row_scale<FMT>(p, n);
       const int tb = t0 + split * W;
-      for (int cc = kh * (W / 2); cc < (kh + 1) * (W / 2) && tb + cc < p.M; cc += 4) {
+      // the slice's float4 groups, halved between the two K-half warps of the row
+      const int hw = ((W / 4 + 1) / 2) * 4, ca = kh ? hw : 0, cb = kh ? W : hw;
+      for (int cc = ca; cc < cb && tb + cc < p.M; cc += 4) {
         float4 a = *reinterpret_cast<const float4*>(red + (row * RS + cc));
         for (int r = 1; r < S; ++r) {
           const float4 v = *reinterpret_cast<const float4*>(red + ((r * BW + row) * RS + cc));
@@ -702,12 +711,12 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-dial_status make_x_map(CUtensorMap* map, const void* x, bool bf16, int64_t M, int64_t K) {
+dial_status make_x_map(CUtensorMap* map, const void* x, bool bf16, int64_t M, int64_t K, int rows) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(DIAL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {BK, BT};
+  const cuuint32_t box[2] = {BK, (cuuint32_t)rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                    2, const_cast<void*>(x), dims, strides, box, estr,
@@ -722,13 +731,13 @@ dial_status make_x_map(CUtensorMap* map, const void* x, bool bf16, int64_t M, in
 // (pipeline fill and epilogue, about 4 groups) and one group for the
 // cross-CTA reduction.  Cluster capacity comes from the occupancy API.
 template <auto KERN>
-int choose_split(int64_t tiles, int ngr, int smem_bytes) {
+int choose_split(int64_t tiles, int ngr, int smem_bytes, int max_split) {
   static int cap[64][kMaxSplit + 1];  // active CTAs per device and split (0: not queried)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
   int best = 1;
   double best_cost = 1e30;
-  for (int S = 1; S <= kMaxSplit && S <= ngr; S *= 2) {
+  for (int S = 1; S <= max_split && S <= ngr; S *= 2) {
     if (S > 1 && ngr / S < 2) break;
     if (cap[dev][S] == 0) {
       int clusters = 0;
@@ -764,7 +773,7 @@ int choose_split(int64_t tiles, int ngr, int smem_bytes) {
 // for GGUF, the tile-major d array as [N / 16 tiles, G * 128 bytes].
 template <int FMT>
 dial_status make_w_maps(const Params& p, CUtensorMap* wmap, CUtensorMap* dmap) {
-  using L = Smem<FMT>;
+  using L = Smem<FMT, 128>;
   if (!L::GGUF) {
     dial_status s = tma::make_byte_map(wmap, p.w, p.N, p.K, 128, BW, 128);
     *dmap = *wmap;  // unused
@@ -775,17 +784,20 @@ dial_status make_w_maps(const Params& p, CUtensorMap* wmap, CUtensorMap* dmap) {
   return tma::make_byte_map(dmap, p.gd, (p.N + 15) / 16, (int64_t)p.G * 128, 128, BW / 16, 0);
 }
 
-template <int FMT, bool BF16, typename YT>
-dial_status launch_one(const CUtensorMap& map, const Params& p, cudaStream_t st) {
-  constexpr auto kern = dequant_gemm_kernel<FMT, BF16, YT>;
-  constexpr int smem = Smem<FMT>::BYTES;
+template <int FMT, bool BF16, typename YT, int BT>
+dial_status launch_bt(const void* x, const Params& p, cudaStream_t st) {
+  constexpr auto kern = dequant_gemm_kernel<FMT, BF16, YT, BT>;
+  constexpr int smem = Smem<FMT, BT>::BYTES;
+  CUtensorMap map;
+  dial_status xs = make_x_map(&map, x, BF16, p.M, p.K, BT);
+  if (xs != DIAL_OK) return xs;
   CUtensorMap wmap, dmap;
   dial_status ds = make_w_maps<FMT>(p, &wmap, &dmap);
   if (ds != DIAL_OK) return ds;
   cudaError_t e = ensure_smem<kern>(smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dequant_gemm)");
   const int64_t wt = (p.N + BW - 1) / BW, tt = (p.M + BT - 1) / BT;
-  const int S = choose_split<kern>(wt * tt, (p.nk + 1) / 2, smem);
+  const int S = choose_split<kern>(wt * tt, (p.nk + 1) / 2, smem, Smem<FMT, BT>::MAX_SPLIT);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)wt, (unsigned)tt, (unsigned)S);
   cfg.blockDim = dim3(THREADS);
@@ -803,6 +815,13 @@ dial_status launch_one(const CUtensorMap& map, const Params& p, cudaStream_t st)
   e = cudaLaunchKernelEx(&cfg, kern, map, wmap, dmap, p);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(dequant_gemm_kernel)");
   return check_launch("dequant_gemm_kernel");
+}
+
+// 32-row token tiles for batched decode (M <= 32), 128-row ones above.
+template <int FMT, bool BF16, typename YT>
+dial_status launch_one(const void* x, const Params& p, cudaStream_t st) {
+  if (p.M <= 32) return launch_bt<FMT, BF16, YT, 32>(x, p, st);
+  return launch_bt<FMT, BF16, YT, 128>(x, p, st);
 }
 
 }  // namespace
@@ -831,34 +850,30 @@ dial_status make_byte_map(CUtensorMap* map, const void* base, int64_t rows, int6
 
 bool gemm_sm100_supported(int64_t M, int64_t K, int64_t N) {
   (void)N;
-  return M > 32 && K % 64 == 0 && K >= 64;
+  return M >= kGemmMinRows && K % 64 == 0 && K >= 64;
 }
 
 size_t gemm_sm100_gguf_workspace_bytes(int64_t M, int64_t K) {
-  return M > 32 ? (size_t)((M * K * 2 + 255) / 256 * 256) : 0;
+  return M >= kGemmMinRows ? (size_t)((M * K * 2 + 255) / 256 * 256) : 0;
 }
 
 dial_status launch_w8a16_gemm_sm100(const void* x, dial_dtype xdt, const int8_t* q,
                                     const void* scale, dial_dtype sdt, void* y, int64_t M,
                                     int64_t K, int64_t N, cudaStream_t st) {
-  CUtensorMap map;
   const bool bf = xdt == DIAL_BF16;
-  dial_status s = make_x_map(&map, x, bf, M, K);
-  if (s != DIAL_OK) return s;
   Params p{reinterpret_cast<const uint8_t*>(q), scale, nullptr, y, (int)M, (int)N, (int)K, 0,
            (int)(K / BK)};
   if (sdt == DIAL_F32)
-    return bf ? launch_one<kW8F32, true, __nv_bfloat16>(map, p, st)
-              : launch_one<kW8F32, false, __half>(map, p, st);
-  return bf ? launch_one<kW8F16, true, __nv_bfloat16>(map, p, st)
-            : launch_one<kW8F16, false, __half>(map, p, st);
+    return bf ? launch_one<kW8F32, true, __nv_bfloat16>(x, p, st)
+              : launch_one<kW8F32, false, __half>(x, p, st);
+  return bf ? launch_one<kW8F16, true, __nv_bfloat16>(x, p, st)
+            : launch_one<kW8F16, false, __half>(x, p, st);
 }
 
 dial_status launch_gguf_gemm_sm100(const void* x, dial_dtype xdt, const void* qs,
                                    const uint16_t* d, int type, void* y, int64_t M, int64_t K,
                                    int64_t N, void* ws, cudaStream_t st) {
   const void* xin = x;
-  const bool bf = xdt == DIAL_BF16;
   if (xdt == DIAL_F32) {  // the tensor cores take f16 operands: convert once
     __half* xh = static_cast<__half*>(ws);
     const int64_t n8 = M * K / 8;
@@ -868,20 +883,17 @@ dial_status launch_gguf_gemm_sm100(const void* x, dial_dtype xdt, const void* qs
     if (s != DIAL_OK) return s;
     xin = xh;
   }
-  CUtensorMap map;
-  dial_status s = make_x_map(&map, xin, bf, M, K);
-  if (s != DIAL_OK) return s;
   const int64_t G = gguf_groups(K);
   Params p{static_cast<const uint8_t*>(qs), nullptr, reinterpret_cast<const __half*>(d), y, (int)M,
            (int)N, (int)K, (int)G, (int)(K / BK)};
   if (type == DIAL_GGML_Q4_0) {
-    if (xdt == DIAL_F32) return launch_one<kQ4, false, float>(map, p, st);
-    if (xdt == DIAL_F16) return launch_one<kQ4, false, __half>(map, p, st);
-    return launch_one<kQ4, true, __nv_bfloat16>(map, p, st);
+    if (xdt == DIAL_F32) return launch_one<kQ4, false, float>(xin, p, st);
+    if (xdt == DIAL_F16) return launch_one<kQ4, false, __half>(xin, p, st);
+    return launch_one<kQ4, true, __nv_bfloat16>(xin, p, st);
   }
-  if (xdt == DIAL_F32) return launch_one<kQ8, false, float>(map, p, st);
-  if (xdt == DIAL_F16) return launch_one<kQ8, false, __half>(map, p, st);
-  return launch_one<kQ8, true, __nv_bfloat16>(map, p, st);
+  if (xdt == DIAL_F32) return launch_one<kQ8, false, float>(xin, p, st);
+  if (xdt == DIAL_F16) return launch_one<kQ8, false, __half>(xin, p, st);
+  return launch_one<kQ8, true, __nv_bfloat16>(xin, p, st);
 }
 
 int* device_error_ptr() {

@@ -5,6 +5,11 @@
 
 namespace dial {
 
+// Fewest activation rows for the tcgen05 GEMM.  GGUF linears take it from 17
+// rows (32-row token tiles: the integer GEMV re-reads its quantised
+// activations per 16-row unit, which dominates at 32 rows); W8A16 linears
+// from kSkinnyMaxM + 1.
+constexpr int64_t kGemmMinRows = 17;
 // True when the tcgen05 GEMM takes this shape (else the caller uses the skinny kernel).
 bool gemm_sm100_supported(int64_t M, int64_t K, int64_t N);
 size_t gemm_sm100_gguf_workspace_bytes(int64_t M, int64_t K);

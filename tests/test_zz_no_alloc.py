@@ -42,9 +42,10 @@ def test_noalloc_matches_workspace_entry_point(cuda, qt):
         out = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
         need = L.dial_gguf_linear_workspace_bytes(M, K, N)
         ws = torch.zeros(need, dtype=torch.uint8, device="cuda")  # zero-filled before first use
-        # the workspace-taking entry point on the same integer path, one pass per 32 rows
-        for m0 in range(0, M, 32):
-            mc = min(32, M - m0)
+        # the workspace-taking entry point on the same integer path (at most 16 rows
+        # per call: from 17 rows it takes the tensor-core GEMM)
+        for m0 in range(0, M, 16):
+            mc = min(16, M - m0)
             st = L.dial_gguf_linear(x[m0:].data_ptr(), D.F32, lin.qs.data_ptr(), lin.d.data_ptr(),
                                     qt, ref[m0:].data_ptr(), mc, K, N, ws.data_ptr(), need, stream)
             assert st == 0, L.dial_last_error()

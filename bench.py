@@ -202,7 +202,7 @@ class W8A16Gemv:
     graph = True
     # ncu DRAM read + write bytes of one launch of this shape
     # (profiles/w8a16_tma_kernel_gemv_12288x4096.md)
-    traffic = 50_435_328 + 15_104
+    traffic = 50_430_976 + 4_608
 
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
         self.torch = torch
@@ -364,7 +364,7 @@ class QwenDecode:
     scaling = "strong"
     # ncu DRAM bytes of the 145 GEMV launches of one token on one GPU
     # (profiles/qwen3_decode_step_launches.md); per token, like `achieved`
-    traffic = 7_655_829_760
+    traffic = 7_596_160_192
     n_seqs, mb_size, prompt_len, decode_cap = 8, 1, 1024, 448
     head_layers = 3.2  # the output head's cost in layers (weights read per token)
     copies_per_step = 8  # one graph per micro-batch

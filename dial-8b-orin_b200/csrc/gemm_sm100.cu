@@ -54,32 +54,37 @@ __device__ int g_device_error = 0;
 
 namespace {
 
-constexpr int BW = 256;   // weight rows per CTA (two UMMA M = 128 halves)
-// BT: activation rows (tokens) per CTA (UMMA N), a template parameter: 128,
-// or 32 for at most 32 rows (batched decode), where wider tiles would spend
-// most MMA cycles on padding
 constexpr int BK = 64;    // K per stage (one 128-byte swizzle atom of f16/bf16)
-constexpr int B_STAGES = 4;  // token tiles in shared memory
-constexpr int A_STAGES = 4;  // dequantised weight stages in TMEM
-constexpr int W_STAGES = 4;  // packed weight groups (128 K) in shared memory
-constexpr int A_HALF_COLS = BK / 2;   // TMEM columns of one weight half per stage
-constexpr int A_COLS = 2 * A_HALF_COLS;
-constexpr int TMEM_COLS = 512;
-constexpr int DQ_WARPS = 16;  // 4 per TMEM lane quarter: weight half x K half of a stage
-constexpr int THREADS = 64 + DQ_WARPS * 32 + 32;  // + the weight producer warp
+constexpr int A_HALF_COLS = BK / 2;  // TMEM columns of one 128-row weight half per stage
 constexpr int kMaxSplit = 8;
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
 
 enum Fmt { kW8F32 = 0, kW8F16 = 1, kQ4 = 2, kQ8 = 3 };
 
-// Shared memory of one CTA: [token ring | packed weight ring | GGUF d ring],
-// every stage 1024-byte aligned (the swizzle atoms); the split-K partial tile
-// reuses it after the main loop.
-template <int FMT, int BT>
-struct Smem {
-  static constexpr int B_BYTES = BT * BK * 2;  // token tile per stage
-  static constexpr int ACC_COLS = 2 * BT;      // two f32 accumulators of BT columns
+// One CTA's tile and resources.  BT: activation rows (tokens) per CTA (UMMA N):
+// 128, or 32 for at most 32 rows (batched decode), where wider tiles would spend
+// most MMA cycles on padding.  NH: 128-row weight halves per CTA (UMMA M = 128
+// each).  NH = 2: 16 dequantising warps (lane quarter x weight half x K half of
+// a stage), all 512 TMEM columns, one CTA per SM.  NH = 1: 8 dequantising warps,
+// 256 TMEM columns and at most 113 KB of shared memory, so that two CTAs share
+// an SM and one's prologue and epilogue overlap the other's main loop.
+// Shared memory: [token ring | packed weight ring | GGUF d ring], every stage
+// 1024-byte aligned (the swizzle atoms); the split-K partial tile reuses it
+// after the main loop.
+template <int FMT, int BT, int NH>
+struct Cfg {
+  static constexpr int BW = 128 * NH;           // weight rows per CTA
+  static constexpr int DQ_WARPS = 8 * NH;
+  static constexpr int THREADS = 64 + DQ_WARPS * 32 + 32;  // + the weight producer warp
+  static constexpr int CTAS_PER_SM = NH == 1 ? 2 : 1;
+  static constexpr int TMEM_COLS = NH == 1 ? 256 : 512;
+  static constexpr int ACC_COLS = NH * BT;      // NH f32 accumulators of BT columns
+  static constexpr int A_COLS = NH * A_HALF_COLS;  // TMEM columns of a dequantised stage
+  static constexpr int A_STAGES = 4;
   static_assert(ACC_COLS + A_STAGES * A_COLS <= TMEM_COLS, "TMEM budget");
+  static constexpr int B_STAGES = NH == 1 ? 3 : 4;  // token tiles in shared memory
+  static constexpr int W_STAGES = NH == 1 ? 3 : 4;  // packed weight groups (128 K)
+  static constexpr int B_BYTES = BT * BK * 2;   // token tile per stage
   // split-K: at most BT / 4 CTAs (each owns whole float4 column groups); the
   // owner's receive buffer is [S senders][BW rows][BT / S + 4] f32 (the +4 pad
   // keeps the 8 rows of a quarter warp's float4 accesses in distinct banks)
@@ -94,7 +99,7 @@ struct Smem {
   static constexpr int RING = D_OFF + W_STAGES * D_BYTES;
   static constexpr int DATA = RING > RED_BYTES ? RING : RED_BYTES;
   static constexpr int BYTES = DATA + 1024 /*align*/ + 256 /*barriers*/;
-  static_assert(BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(BYTES <= (NH == 1 ? 113 : 227) * 1024, "shared memory budget");
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -426,13 +431,15 @@ __device__ __forceinline__ void store4(const Params& p, int t0, int n, float sc,
     if (t0 + i < p.M) y[(size_t)(t0 + i) * p.N + n] = Act<YT>::from_f32(a[i] * sc);
 }
 
-template <int FMT, bool BF16, typename YT, int BT>
-__global__ void __launch_bounds__(THREADS, 1)
+template <int FMT, bool BF16, typename YT, int BT, int NH>
+__global__ void __launch_bounds__(Cfg<FMT, BT, NH>::THREADS, Cfg<FMT, BT, NH>::CTAS_PER_SM)
     dequant_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_d, const Params p) {
-  using L = Smem<FMT, BT>;
-  constexpr int B_BYTES = L::B_BYTES, ACC_COLS = L::ACC_COLS;
+  using L = Cfg<FMT, BT, NH>;
+  constexpr int B_BYTES = L::B_BYTES, ACC_COLS = L::ACC_COLS, A_COLS = L::A_COLS;
+  constexpr int B_STAGES = L::B_STAGES, A_STAGES = L::A_STAGES, W_STAGES = L::W_STAGES;
+  constexpr int BW = L::BW, DQ_WARPS = L::DQ_WARPS, TMEM_COLS = L::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -518,7 +525,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t bd = sw128_desc(smem_base + (uint32_t)(sb * B_BYTES));
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < NH; ++h)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma_ts(tmem + (uint32_t)(h * BT),
@@ -550,8 +557,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   // ------------------------------------------------ dequantisers, then the epilogue
   const bool dq = warp >= 2 && warp < 2 + DQ_WARPS;
   const int quarter = warp & 3;             // TMEM lanes this warp may access
-  const int half = ((warp - 2) >> 2) & 1;   // weight half
-  const int kh = (warp - 2) >> 3;           // K half of each stage (and token half of the epilogue)
+  const int half = NH == 2 ? ((warp - 2) >> 2) & 1 : 0;  // weight half
+  const int kh = (warp - 2) >> (NH == 2 ? 3 : 2);  // K half of each stage (token half of the epilogue)
   const int row = half * 128 + quarter * 32 + lane;  // weight row within the tile
   const int n = n0 + row;
   const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
@@ -731,7 +738,7 @@ dial_status make_x_map(CUtensorMap* map, const void* x, bool bf16, int64_t M, in
 // (pipeline fill and epilogue, about 4 groups) and one group for the
 // cross-CTA reduction.  Cluster capacity comes from the occupancy API.
 template <auto KERN>
-int choose_split(int64_t tiles, int ngr, int smem_bytes, int max_split) {
+int choose_split(int64_t tiles, int ngr, int smem_bytes, int max_split, int threads) {
   static int cap[64][kMaxSplit + 1];  // active CTAs per device and split (0: not queried)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
@@ -743,7 +750,7 @@ int choose_split(int64_t tiles, int ngr, int smem_bytes, int max_split) {
       int clusters = 0;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(1, 1, (unsigned)S);
-      cfg.blockDim = dim3(THREADS);
+      cfg.blockDim = dim3((unsigned)threads);
       cfg.dynamicSmemBytes = smem_bytes;
       cudaLaunchAttribute at[1];
       at[0].id = cudaLaunchAttributeClusterDimension;
@@ -771,36 +778,38 @@ int choose_split(int64_t tiles, int ngr, int smem_bytes, int max_split) {
 
 // Tensor maps of the packed weights: rows of 128-K groups (GB bytes each) and,
 // for GGUF, the tile-major d array as [N / 16 tiles, G * 128 bytes].
-template <int FMT>
+template <int FMT, int BW>
 dial_status make_w_maps(const Params& p, CUtensorMap* wmap, CUtensorMap* dmap) {
-  using L = Smem<FMT, 128>;
-  if (!L::GGUF) {
+  constexpr bool gguf = FMT == kQ4 || FMT == kQ8;
+  constexpr int GB = FMT == kQ4 ? 64 : 128;
+  if (!gguf) {
     dial_status s = tma::make_byte_map(wmap, p.w, p.N, p.K, 128, BW, 128);
     *dmap = *wmap;  // unused
     return s;
   }
-  dial_status s = tma::make_byte_map(wmap, p.w, p.N, (int64_t)p.G * L::GB, L::GB, BW, L::GB);
+  dial_status s = tma::make_byte_map(wmap, p.w, p.N, (int64_t)p.G * GB, GB, BW, GB);
   if (s != DIAL_OK) return s;
   return tma::make_byte_map(dmap, p.gd, (p.N + 15) / 16, (int64_t)p.G * 128, 128, BW / 16, 0);
 }
 
-template <int FMT, bool BF16, typename YT, int BT>
+template <int FMT, bool BF16, typename YT, int BT, int NH>
 dial_status launch_bt(const void* x, const Params& p, cudaStream_t st) {
-  constexpr auto kern = dequant_gemm_kernel<FMT, BF16, YT, BT>;
-  constexpr int smem = Smem<FMT, BT>::BYTES;
+  using L = Cfg<FMT, BT, NH>;
+  constexpr auto kern = dequant_gemm_kernel<FMT, BF16, YT, BT, NH>;
+  constexpr int smem = L::BYTES, BW = L::BW;
   CUtensorMap map;
   dial_status xs = make_x_map(&map, x, BF16, p.M, p.K, BT);
   if (xs != DIAL_OK) return xs;
   CUtensorMap wmap, dmap;
-  dial_status ds = make_w_maps<FMT>(p, &wmap, &dmap);
+  dial_status ds = make_w_maps<FMT, BW>(p, &wmap, &dmap);
   if (ds != DIAL_OK) return ds;
   cudaError_t e = ensure_smem<kern>(smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dequant_gemm)");
   const int64_t wt = (p.N + BW - 1) / BW, tt = (p.M + BT - 1) / BT;
-  const int S = choose_split<kern>(wt * tt, (p.nk + 1) / 2, smem, Smem<FMT, BT>::MAX_SPLIT);
+  const int S = choose_split<kern>(wt * tt, (p.nk + 1) / 2, smem, L::MAX_SPLIT, L::THREADS);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)wt, (unsigned)tt, (unsigned)S);
-  cfg.blockDim = dim3(THREADS);
+  cfg.blockDim = dim3(L::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute at[2];
@@ -817,11 +826,13 @@ dial_status launch_bt(const void* x, const Params& p, cudaStream_t st) {
   return check_launch("dequant_gemm_kernel");
 }
 
-// 32-row token tiles for batched decode (M <= 32), 128-row ones above.
+// 32-row token tiles for batched decode (M <= 32), 128-row ones above; the
+// narrow CTA (128 weight rows, two per SM) or the wide one (256, one per SM).
+constexpr bool kNarrowDecode = true, kNarrowPrefill = true;
 template <int FMT, bool BF16, typename YT>
 dial_status launch_one(const void* x, const Params& p, cudaStream_t st) {
-  if (p.M <= 32) return launch_bt<FMT, BF16, YT, 32>(x, p, st);
-  return launch_bt<FMT, BF16, YT, 128>(x, p, st);
+  if (p.M <= 32) return launch_bt<FMT, BF16, YT, 32, kNarrowDecode ? 1 : 2>(x, p, st);
+  return launch_bt<FMT, BF16, YT, 128, kNarrowPrefill ? 1 : 2>(x, p, st);
 }
 
 }  // namespace

@@ -351,6 +351,62 @@ class GgufPrefill(GgufSweep):
         return sum(2 * m * N * K for m in cls.ms for _ in GGUF_BLOCK_BYTES for _, N, K in LAYER_SHAPES)
 
 
+class AttentionDecode:
+    """Batched decode attention of one layer: 32 sequences, each one query token
+    over its 2049-row f16 KV cache (Llama-3-8B heads: 32 query / 8 KV, head_dim
+    128), through dial_attention.  Metric: KV bytes read per second."""
+    metric, unit, bound, dtype = "decode attention KV GB/s", "GB/s", "hbm", "f16"
+    kernel = "attention_tc_kernel<f16, 4> + attention_combine_kernel"
+    T, HQ, HKV, D, CTX = 32, 32, 8, 128, 2049
+    graph = True
+    traffic = None
+
+    def __init__(self, torch, D_, rank: int = 0, world: int = 1):
+        self.torch, self.Dl = torch, D_
+        g = torch.Generator(device="cuda").manual_seed(SEED)
+        self.S = self.CTX + 15  # cache rows per slot
+        per = 2 * self.T * self.HKV * self.S * self.D * 2
+        self.copies = max(2, -(-3 * L2_BYTES // per))  # layer caches rotated past the L2
+        self.kc, self.vc = [], []
+        for _ in range(self.copies):
+            self.kc.append(torch.randn((self.T, self.HKV, self.S, self.D), generator=g, device="cuda",
+                                       dtype=torch.float16))
+            self.vc.append(torch.randn((self.T, self.HKV, self.S, self.D), generator=g, device="cuda",
+                                       dtype=torch.float16))
+        self.q = torch.randn((self.T, self.HQ, self.D), generator=g, device="cuda", dtype=torch.float16)
+        self.out = torch.empty((self.T, self.HQ * self.D), device="cuda", dtype=torch.float16)
+        self.pos = torch.full((self.T,), self.CTX - 1, dtype=torch.int32, device="cuda")
+        self.slot = torch.arange(self.T, dtype=torch.int32, device="cuda")
+        need = D_.lib().dial_attention_workspace_bytes(self.T, self.HQ, self.CTX)
+        self.ws = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
+        self.need = need
+        self.i = 0
+        self.work_per_step = self.bytes()
+        self.config = {"workload": "attention_batched", "sequences": self.T, "context": self.CTX,
+                       "heads": f"{self.HQ}/{self.HKV}", "head_dim": self.D, "kv_cache": "f16",
+                       "l2": f"{self.copies} rotating layer caches "
+                             f"({self.copies * per / 1e6:.0f} MB > 126 MB L2)"}
+
+    @classmethod
+    def bytes(cls):
+        return 2 * cls.T * cls.HKV * cls.CTX * cls.D * 2 + 2 * 2 * cls.T * cls.HQ * cls.D
+
+    def run_copy(self, li):
+        L = self.Dl.lib()
+        self.Dl.check(L.dial_attention(self.q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
+                                       self.pos.data_ptr(), self.slot.data_ptr(), self.out.data_ptr(),
+                                       self.ws.data_ptr() if self.need else None, self.need,
+                                       self.Dl.F16, self.T, self.HQ, self.HKV, self.D, self.S, self.CTX,
+                                       self.Dl.stream_ptr()), "dial_attention")
+
+    def build_graphs(self):
+        build_copy_graphs(self)
+
+    def step(self):
+        self.graphs[self.i % self.copies].replay()
+        self.i += 1
+
+
 class QwenDecode:
     """Qwen3-8B-shaped W8A16 decoder (36 layers, hidden 4096,
     MLP 12288, 32/8 heads, vocab 151936, random init N(0, 0.02)), 8 sequences,
@@ -533,7 +589,8 @@ class LlamaGgufDecode(QwenDecode):
 
 
 WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep, "gguf_prefill": GgufPrefill,
-             "qwen3_decode": QwenDecode, "llama_gguf_decode": LlamaGgufDecode}
+             "qwen3_decode": QwenDecode, "llama_gguf_decode": LlamaGgufDecode,
+             "attention_batched": AttentionDecode}
 
 
 # ------------------------------------------------------------------ workloads (CPU oracle)
@@ -674,7 +731,40 @@ def cpu_gguf_decode_measure(budget_s):
     return 1.0 / t_tok, t_tok, O.num_threads(), sample
 
 
+def cpu_attention_measure(budget_s):
+    """The same attention in numpy (f32 math on f16 caches, all host threads
+    numpy uses) over 4 of the 32 sequences per pass, scaled to KV bytes/s."""
+    import numpy as np
+    wl = AttentionDecode
+    rng = np.random.default_rng(SEED)
+    n = 4
+    k = rng.standard_normal((n, wl.HKV, wl.CTX, wl.D)).astype(np.float16)
+    v = rng.standard_normal((n, wl.HKV, wl.CTX, wl.D)).astype(np.float16)
+    q = rng.standard_normal((n, wl.HQ, wl.D)).astype(np.float16)
+    rep = wl.HQ // wl.HKV
+
+    def one():
+        for s in range(n):
+            kf, vf = k[s].astype(np.float32), v[s].astype(np.float32)
+            qs = q[s].astype(np.float32).reshape(wl.HKV, rep, wl.D)
+            sc = np.einsum("grd,gkd->grk", qs, kf) / np.sqrt(wl.D)
+            p = np.exp(sc - sc.max(axis=-1, keepdims=True))
+            np.einsum("grk,gkd->grd", p / p.sum(axis=-1, keepdims=True), vf)
+
+    one()
+    t0, passes = time.perf_counter(), 0
+    while time.perf_counter() - t0 < budget_s or passes == 0:
+        one()
+        passes += 1
+    dt = time.perf_counter() - t0
+    per_pass = 2 * n * wl.HKV * wl.CTX * wl.D * 2
+    return per_pass * passes / dt, dt / passes, os.cpu_count() or 1, \
+        f"{passes} passes over {n} of the {wl.T} sequences (numpy) in {dt:.1f}s"
+
+
 def cpu_measure(name, budget_s):
+    if name == "attention_batched":
+        return cpu_attention_measure(budget_s)
     if name == "qwen3_decode":
         return cpu_decode_measure(budget_s)
     if name == "llama_gguf_decode":

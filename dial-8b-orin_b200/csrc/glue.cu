@@ -566,17 +566,31 @@ dial_status launch_qk_rope_kv(const void* qkv, const void* qn, const void* kn, c
   return s;
 }
 
-// Key splits per (token, kv head): enough CTAs for ~2 per SM, at least 128 keys
-// each (8 tiles of 16 keys, two per warp of the tensor-core kernel).
+// Key splits per (token, kv head), at least 128 keys each (8 tiles of 16 keys,
+// two per warp): the count whose waves of CTAs (three resident per SM: 168
+// registers x 128 threads, 72 KB of shared memory) waste least of the last
+// wave, with a small charge per split for its partials and the combine.
 static int attention_splits(int64_t tokens, int hkv, int64_t max_len) {
-  const int64_t want = (2 * (int64_t)sm_count() + tokens * hkv - 1) / (tokens * hkv);
-  const int64_t cap = (max_len + 127) / 128;
-  return (int)std::max<int64_t>(1, std::min(want, cap));
+  const int64_t pairs = tokens * hkv, slots = 3 * (int64_t)sm_count();
+  const int64_t cap = std::min<int64_t>(32, std::max<int64_t>(1, (max_len + 127) / 128));
+  int best = 1;
+  double best_t = 1e30;
+  for (int n = 1; n <= cap; ++n) {
+    const double waves = (double)((pairs * n + slots - 1) / slots);
+    const double t = waves / n + 0.02 * n;
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = n;
+    }
+  }
+  return best;
 }
 
 size_t attention_workspace_bytes(int64_t tokens, int hq, int64_t max_len) {
-  // hkv is not known here: size for the largest split count any hkv >= 1 gives
-  const int64_t nch = attention_splits(tokens, 1, max_len);
+  // hkv is not known here: size for the largest split count any divisor of hq gives
+  int64_t nch = 1;
+  for (int hkv = 1; hkv <= hq; ++hkv)
+    if (hq % hkv == 0) nch = std::max<int64_t>(nch, attention_splits(tokens, hkv, max_len));
   return nch > 1 ? (size_t)(tokens * hq * nch * (128 + 2)) * sizeof(float) : 0;
 }
 

@@ -406,7 +406,9 @@ __global__ void __launch_bounds__(kTcWarps * 32)
 }
 
 // ------------------------------------------------------------------ SwiGLU
-// out[t, i] = round(round(silu(g)) * u), g = gate_up[t, i], u = gate_up[t, I + i]
+// out[t, i] = round(round(silu(g)) * u), g = gate_up[t, i], u = gate_up[t, I + i];
+// silu with the fast exp and divide (a few ulp in f32, then rounded to the
+// activation dtype)
 template <typename T>
 __global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t tokens,
                               int64_t inter) {
@@ -417,7 +419,7 @@ __global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int
     const int64_t t = i / inter, c = i % inter;
     const float g = ld(gu, t * 2 * inter + c);
     const float u = ld(gu, t * 2 * inter + inter + c);
-    const float s = Act<T>::to_f32(rnd<T>(g / (1.0f + expf(-g))));
+    const float s = Act<T>::to_f32(rnd<T>(__fdividef(g, 1.0f + __expf(-g))));
     out[i] = rnd<T>(s * u);
   }
 }

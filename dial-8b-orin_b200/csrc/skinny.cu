@@ -859,7 +859,7 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float gg = act_f32<BF16>(h16(gv, i));
-          const float sl = act_f32<BF16>(act_rnd<BF16>(gg / (1.0f + expf(-gg))));
+          const float sl = act_f32<BF16>(act_rnd<BF16>(__fdividef(gg, 1.0f + __expf(-gg))));
           v[i] = act_f32<BF16>(act_rnd<BF16>(sl * act_f32<BF16>(h16(uv, i))));
         }
       }

@@ -574,6 +574,7 @@ dial_status launch_qk_rope_kv(const void* qkv, const void* qn, const void* kn, c
 // wave, with a small charge per split for its partials and the combine.
 static int attention_splits(int64_t tokens, int hkv, int64_t max_len) {
   const int64_t pairs = tokens * hkv, slots = 3 * (int64_t)sm_count();
+  if (pairs >= slots) return 1;  // the unsplit grid already fills the GPU
   const int64_t cap = std::min<int64_t>(32, std::max<int64_t>(1, (max_len + 127) / 128));
   int best = 1;
   double best_t = 1e30;

@@ -559,8 +559,9 @@ class LlamaGgufDecode(QwenDecode):
     """Llama-3-8B-shaped GGUF decoder (32 layers, hidden 4096,
     MLP 14336, 32/8 heads, vocab 128256, theta 5e5, no QK-norm), layers Q4_0 and
     head Q8_0 from N(0, 0.02) weights, 32 sequences with 2048-token prompts
-    (prefilled before timing), batched decode as 8 micro-batches of 4 sequences
-    through the pipeline.  A step advances every sequence by one token."""
+    (prefilled before timing), batched decode as P micro-batches of 32/P
+    sequences through a pipeline of P stages (one micro-batch of 32 on one GPU).
+    A step advances every sequence by one token."""
     metric, unit, bound, dtype = "8B GGUF Q4_0 batched decode tok/s", "tok/s", "hbm", "q4_0 x f16"
     kernel = "gguf_tma_kernel (M = one micro-batch; the stage's linears from one graph, events)"
     traffic = None

@@ -205,11 +205,42 @@ class Pipeline:
         self.pending = [None] * n_mb  # last send of each micro-batch's output buffer
         self.t = 0  # decode steps since the last prefill
         self.host_io = None  # (host_in, host_out): pinned int32 token copies for host_io steps
+        self._connected = False  # decode-sized transfers made on every link (_connect)
 
     def _wait_send(self, b):
         if self.pending[b] is not None:
             self.pending[b].wait()
             self.pending[b] = None
+
+    def _connect(self, fwd, ring) -> None:
+        """One matched transfer per link, in link order (0 -> 1, ..., P-2 -> P-1,
+        then P-1 -> 0), of tensors shaped like that link's traffic.
+
+        NCCL sets up a peer connection on the host at the first transfer between
+        two ranks, and that call returns only once the peer makes its matching
+        call.  Without this exchange the ring's first send (the last stage's
+        first prefill tokens) blocks the last stage's host until stage 0 reaches
+        its first receive on the ring, after its whole prefill loop; stage 0's
+        host meanwhile blocks in a kernel launch once its stream, held up by
+        a forward send that the last stage has not received yet, has a full
+        launch queue.  Here every rank meets its links in one order, so the
+        set-ups form a chain and cannot wait in a cycle."""
+        r, P, ch = self.rank, self.world, self.ch
+        for s in range(P - 1):
+            if r == s:
+                ch.isend(fwd, s + 1).wait()
+            elif r == s + 1:
+                ch.irecv(fwd, s).wait()
+        if r == P - 1:
+            ch.isend(ring, 0).wait()
+        elif r == 0:
+            ch.irecv(ring, P - 1).wait()
+
+    def _connect_steps(self) -> None:
+        if self.world > 1 and not self._connected:
+            c = self.c
+            self._connect(c.hidden_buffer(0).clone(), c.token_buffer(0).clone())
+            self._connected = True
 
     def steps(self, n_steps: int, host_io: bool = False) -> None:
         """n_steps decode steps: every micro-batch advances one token per step.
@@ -221,6 +252,7 @@ class Pipeline:
         step's tokens to the host and synchronises at the end of the step."""
         torch = _torch() if host_io else None
         r, P, B, c, ch = self.rank, self.world, self.n_mb, self.c, self.ch
+        self._connect_steps()
         if host_io and self.host_io is None:
             n = [c.token_buffer(b).numel() for b in range(B)]  # one token per row
             self.host_io = ([torch.zeros(n[b], dtype=torch.int32).pin_memory() for b in range(B)],
@@ -280,6 +312,9 @@ class Pipeline:
         R = getattr(c, "mb_size", 1)
         T = len(prompts[0]) if prompts is not None else prompt_len
         buf = c.prefill_buffer(T)
+        if P > 1:
+            self._connect(buf, c.token_buffer(0).clone())
+            self._connect_steps()
         for b in range(B):
             for i in range(R):
                 if r > 0:

@@ -70,6 +70,32 @@ class FakeCompute:
             self.tokens[b].copy_(self.sample(self.pbuf[-1]))
 
 
+class FakeComputeRows(FakeCompute):
+    """The same stages with micro-batches of R sequences (rows): each row its own
+    sequence, prefilled one sequence at a time (prefill_run's third argument)."""
+
+    def __init__(self, r, world, n_mb, R):
+        super().__init__(r, world, n_mb)
+        self.mb_size = R
+        self.hidden = [torch.zeros(R, H) for _ in range(n_mb)]
+        self.tokens = [torch.zeros(R, dtype=torch.int32) for _ in range(n_mb)]
+
+    def run(self, b):
+        for i in range(self.mb_size):
+            if self.first:
+                self.hidden[b][i].copy_(self.embed(self.tokens[b][i]))
+            self.hidden[b][i].copy_(self.layers(self.hidden[b][i], self.pos[b]))
+            if self.last:
+                self.tokens[b][i] = self.sample(self.hidden[b][i])[0]
+
+    def prefill_run(self, b, ids=None, i=0):
+        if self.first:
+            self.pbuf.copy_(torch.stack([self.embed(torch.tensor(k)) for k in ids]))
+        self.pbuf.copy_(self.layers(self.pbuf, -1))
+        if self.last:
+            self.tokens[b][i] = self.sample(self.pbuf[-1])[0]
+
+
 def reference(world, n_mb, prompts, steps):
     """The same chain, every stage in one process."""
     stages = [FakeCompute(r, world, n_mb) for r in range(world)]
@@ -90,23 +116,24 @@ def reference(world, n_mb, prompts, steps):
     return out
 
 
-def _worker(rank, world, port, n_mb, prompts, steps, result_dir):
+def _worker(rank, world, port, n_mb, prompts, steps, result_dir, R=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
                                     "dial-8b-orin_b200"))
     from dial_cuda.pipeline import Pipeline, TorchChannel, init_distributed
     init_distributed("gloo", timeout_s=30)
-    c = FakeCompute(rank, world, n_mb)
+    c = FakeCompute(rank, world, n_mb) if R == 1 else FakeComputeRows(rank, world, n_mb, R)
     p = Pipeline(rank, world, c, TorchChannel(), n_mb)
     p.prefill(prompts if rank == 0 else None, prompt_len=len(prompts[0]))
-    firsts = [int(t) for t in c.tokens]
+    firsts = [int(v) for t in c.tokens for v in t.reshape(-1)]
     # two calls of one run, as the benchmark does (warm-up, then timed steps)
     p.steps(2)
     p.steps(steps - 2)
-    last = [int(t) for t in c.tokens]
+    last = [int(v) for t in c.tokens for v in t.reshape(-1)]
     p.finish()
-    torch.save({"firsts": firsts, "last": last, "after_finish": [int(t) for t in c.tokens]},
+    torch.save({"firsts": firsts, "last": last,
+                "after_finish": [int(v) for t in c.tokens for v in t.reshape(-1)]},
                os.path.join(result_dir, f"r{rank}.pt"))
     import torch.distributed as dist
     dist.barrier()
@@ -125,6 +152,116 @@ def test_pipeline_matches_single_process_chain(world, tmp_path):
     assert r0["firsts"] == [seq[0] for seq in ref]          # prefill tokens reached stage 0
     assert rl["last"] == [seq[-1] for seq in ref]           # last step's tokens on the last stage
     assert r0["after_finish"] == [seq[-1] for seq in ref]   # finish() hands them to stage 0
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_pipeline_micro_batches_of_several_sequences(world, tmp_path):
+    """Micro-batches of R = 2 sequences: prefill walks every sequence of a micro-batch
+    before the last stage hands that micro-batch's tokens back to stage 0."""
+    n_mb, R, steps = 3, 2, 5
+    prompts = [[(5 * s + 3 * i + 1) % V for i in range(4)] for s in range(n_mb * R)]
+    mp.start_processes(_worker, args=(world, _free_port(), n_mb, prompts, steps, str(tmp_path), R),
+                       nprocs=world, join=True, start_method="spawn")
+    ref = reference(world, n_mb * R, prompts, steps)
+    r0 = torch.load(tmp_path / "r0.pt")
+    rl = torch.load(tmp_path / f"r{world - 1}.pt")
+    assert r0["firsts"] == [seq[0] for seq in ref]
+    assert rl["last"] == [seq[-1] for seq in ref]
+    assert r0["after_finish"] == [seq[-1] for seq in ref]
+
+
+class RendezvousChannel:
+    """TorchChannel with two traits of NCCL on GPUs that gloo lacks.  (1) The
+    first transfer on a link returns only once the peer has made its own first
+    call on that link (NCCL sets up peer connections on the host that way).
+    (2) A sender's host blocks while `depth` of its sends on a link are not yet
+    received (a stream held up by an unreceived send fills the launch queue)."""
+
+    def __init__(self, store, rank, world, depth=2, timeout_s=8.0):
+        from dial_cuda.pipeline import TorchChannel
+        self.inner = TorchChannel(world)
+        self.store, self.rank, self.depth, self.timeout_s = store, rank, depth, timeout_s
+        self.seen, self.sent, self.got = set(), {}, {}
+
+    def _wait_until(self, cond, what):
+        import time
+        t0 = time.time()
+        while not cond():
+            if time.time() - t0 > self.timeout_s:
+                raise TimeoutError(what)
+            time.sleep(0.002)
+
+    def _first(self, a, b):
+        if (a, b) in self.seen:
+            return
+        self.seen.add((a, b))
+        self.store.add(f"link{a}-{b}", 1)
+        self._wait_until(lambda: self.store.add(f"link{a}-{b}", 0) >= 2, f"set-up of link {a}->{b}")
+
+    def isend(self, t, dst):
+        link = (self.rank, dst)
+        self._first(*link)
+        n = self.sent.get(link, 0)
+        key = f"recv{link[0]}-{link[1]}"
+        self._wait_until(lambda: self.store.add(key, 0) > n - self.depth, f"send queue of {link}")
+        self.sent[link] = n + 1
+        return self.inner.isend(t, dst)
+
+    def irecv(self, t, src):
+        link = (src, self.rank)
+        self._first(*link)
+        inner, store = self.inner.irecv(t, src), self.store
+
+        class Done:
+            def wait(self_):
+                inner.wait()
+                store.add(f"recv{link[0]}-{link[1]}", 1)
+        return Done()
+
+
+def _rendezvous_worker(rank, world, port, n_mb, R, prompts, steps, result_dir, skip_connect):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "dial-8b-orin_b200"))
+    import torch.distributed as dist
+    from dial_cuda.pipeline import Pipeline, init_distributed
+    init_distributed("gloo", timeout_s=30)
+    store = dist.distributed_c10d._get_default_store()
+    c = FakeComputeRows(rank, world, n_mb, R)
+    p = Pipeline(rank, world, c, RendezvousChannel(store, rank, world), n_mb)
+    if skip_connect:  # the schedule without its link set-up exchange
+        p._connect = lambda fwd, ring: None
+        p._connected = True
+    try:
+        p.prefill(prompts if rank == 0 else None, prompt_len=len(prompts[0]))
+        p.steps(steps)
+        p.finish()
+        out = {"ok": True, "tokens": [int(v) for t in c.tokens for v in t.reshape(-1)]}
+    except (TimeoutError, RuntimeError) as e:  # gave up, or the peer that gave up left
+        out = {"ok": False, "where": str(e)}
+    torch.save(out, os.path.join(result_dir, f"rv{rank}.pt"))
+    os._exit(0)  # a stuck peer's transfers may still be posted
+
+
+@pytest.mark.parametrize("skip_connect", [False, True])
+def test_pipeline_link_set_up_cannot_deadlock(skip_connect, tmp_path):
+    """Two stages, micro-batches of 2 sequences, a channel with NCCL's blocking
+    link set-up and bounded send queue: the pipeline finishes and matches the
+    single-process chain; without the set-up exchange it deadlocks in prefill
+    (the last stage waits on the ring's set-up, stage 0 on its full queue)."""
+    world, n_mb, R, steps = 2, 3, 2, 4
+    prompts = [[(11 * s + 5 * i + 2) % V for i in range(3)] for s in range(n_mb * R)]
+    mp.start_processes(_rendezvous_worker,
+                       args=(world, _free_port(), n_mb, R, prompts, steps, str(tmp_path), skip_connect),
+                       nprocs=world, join=True, start_method="spawn")
+    outs = [torch.load(tmp_path / f"rv{r}.pt") for r in range(world)]
+    if skip_connect:
+        assert not outs[1]["ok"] and "set-up of link 1->0" in outs[1]["where"], outs
+        return
+    assert all(o["ok"] for o in outs), outs
+    ref = reference(world, n_mb * R, prompts, steps)
+    assert outs[0]["tokens"] == [seq[-1] for seq in ref]
 
 
 def test_pipeline_rejects_too_few_micro_batches():

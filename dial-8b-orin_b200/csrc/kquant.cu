@@ -1,0 +1,291 @@
+// GGUF K-quant weights (Q4_K, Q6_K) in their native GGML super-block layout:
+// bit-exact dequantisation and a decode linear that dequantises on the fly.
+//
+// The reference loads these formats through candle's QMatMul
+// (worker_gguf.rs:462-522 load_worker_gguf_linear, forward at :574-611; the
+// deployed files are Q4_K_M, docs/worker_gguf.md:1-6; its GGUF tests all use
+// Q4_K, worker_gguf.rs:641-785).  The block arithmetic lives in candle-core
+// 0.11.0 (not vendored); it follows the public GGML definitions:
+//
+//   Q4_K, 144 bytes per 256 weights: {f16 d; f16 dmin; u8 scales[12]; u8 qs[128]}
+//     weight e = 64c + 32s + j (chunk c < 4, half s < 2, j < 32) is nibble s of
+//     qs[32c + j]; sub-block b = e / 32 has a 6-bit scale sc_b and min m_b packed
+//     in scales[] (b < 4: sc = scales[b] & 63, m = scales[b+4] & 63; b >= 4:
+//     sc = (scales[b+4] & 15) | (scales[b-4] >> 6) << 4,
+//     m = (scales[b+4] >> 4) | (scales[b] >> 6) << 4);
+//     value = (d*sc_b) * q - (dmin*m_b), each product and the difference
+//     rounded to f32 on its own.
+//   Q6_K, 210 bytes per 256 weights: {u8 ql[128]; u8 qh[64]; i8 scales[16]; f16 d}
+//     weight e = 128h + 32g + l (h < 2, g < 4, l < 32): low 4 bits are nibble
+//     g >> 1 of ql[64h + l + 32(g & 1)], high 2 bits are bits 2g..2g+1 of
+//     qh[32h + l]; q = that 6-bit value - 32; value = (d*scales[e/16]) * q.
+//
+// The kernels use the explicitly rounded intrinsics (__fmul_rn, __fsub_rn), so
+// no multiply-add is contracted and the values equal the GGML reference
+// dequantisers bit for bit.  A Q4_K row is 144*K/256 bytes (16-byte aligned for
+// an aligned base); a Q6_K block starts on an even byte only, so its bytes are
+// read as 16-bit words.
+#include "common.cuh"
+
+namespace dial {
+
+namespace {
+
+constexpr int kQKK = 256;  // weights per super-block
+
+__host__ __device__ constexpr int kq_block_bytes(int type) {
+  return type == DIAL_GGML_Q4_K ? 144 : type == DIAL_GGML_Q6_K ? 210 : 0;
+}
+
+__device__ __forceinline__ float f16_at(const uint8_t* p) {  // p: 2-byte aligned
+  return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p)));
+}
+
+// The 6-bit scale and min of Q4_K sub-block b (GGML get_scale_min_k4).
+__device__ __forceinline__ void q4k_scale_min(const uint8_t* sc, int b, int& s, int& m) {
+  if (b < 4) {
+    s = sc[b] & 63;
+    m = sc[b + 4] & 63;
+  } else {
+    s = (sc[b + 4] & 15) | ((sc[b - 4] >> 6) << 4);
+    m = (sc[b + 4] >> 4) | ((sc[b] >> 6) << 4);
+  }
+}
+
+// Lane `lane` of a warp owns 8 weights of one super-block:
+//   Q4_K: elements 64c + j0 + i (low nibbles) and 64c + 32 + j0 + i (high
+//         nibbles), i < 4, with c = lane / 8 and j0 = 4 (lane % 8): one 4-byte
+//         word of qs per lane, the warp reads all 128 bytes at once;
+//   Q6_K: elements 128h + 32g + l0 + i, g < 4, i < 2, with h = lane / 16 and
+//         l0 = 2 (lane % 16).
+// w[k] is the weight at kq_elem<TYPE>(lane, k).
+template <int TYPE>
+__device__ __forceinline__ int kq_elem(int lane, int k) {
+  if (TYPE == DIAL_GGML_Q4_K) {
+    const int c = lane >> 3, j0 = (lane & 7) * 4;
+    return 64 * c + (k < 4 ? 0 : 32) + j0 + (k & 3);
+  } else {
+    const int h = lane >> 4, l0 = (lane & 15) * 2;
+    return 128 * h + 32 * (k >> 1) + l0 + (k & 1);
+  }
+}
+
+template <int TYPE>
+__device__ __forceinline__ void kq_dequant8(const uint8_t* blk, int lane, float (&w)[8]) {
+  if (TYPE == DIAL_GGML_Q4_K) {
+    const float d = f16_at(blk), dmin = f16_at(blk + 2);
+    const uint8_t* sc = blk + 4;
+    const int c = lane >> 3, j0 = (lane & 7) * 4;
+    const uint32_t q = *reinterpret_cast<const uint32_t*>(blk + 16 + 32 * c + j0);
+    int s0, m0, s1, m1;
+    q4k_scale_min(sc, 2 * c, s0, m0);
+    q4k_scale_min(sc, 2 * c + 1, s1, m1);
+    const float d0 = __fmul_rn(d, (float)s0), mm0 = __fmul_rn(dmin, (float)m0);
+    const float d1 = __fmul_rn(d, (float)s1), mm1 = __fmul_rn(dmin, (float)m1);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t byte = (q >> (8 * i)) & 0xFFu;
+      w[i] = __fsub_rn(__fmul_rn(d0, (float)(byte & 15u)), mm0);
+      w[4 + i] = __fsub_rn(__fmul_rn(d1, (float)(byte >> 4)), mm1);
+    }
+  } else {
+    const float d = f16_at(blk + 208);
+    const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+    const int h = lane >> 4, l0 = (lane & 15) * 2;
+    const uint32_t lo = *reinterpret_cast<const unsigned short*>(blk + 64 * h + l0);       // ql[l0..+1]
+    const uint32_t hi = *reinterpret_cast<const unsigned short*>(blk + 64 * h + 32 + l0);  // ql[l0+32..]
+    const uint32_t qh = *reinterpret_cast<const unsigned short*>(blk + 128 + 32 * h + l0);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const float dg = __fmul_rn(d, (float)sc[8 * h + 2 * g + (l0 >> 4)]);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint32_t ql = ((g & 1) ? hi : lo) >> (8 * i);
+        const uint32_t low = (g >> 1) ? ((ql >> 4) & 15u) : (ql & 15u);
+        const uint32_t high = (qh >> (8 * i + 2 * g)) & 3u;
+        w[2 * g + i] = __fmul_rn(dg, (float)((int)(low | (high << 4)) - 32));
+      }
+    }
+  }
+}
+
+// w[n, k] in wdt.  One warp per (row, super-block).
+template <int TYPE, typename T>
+__global__ void __launch_bounds__(256) kq_dequantize_kernel(const uint8_t* __restrict__ blocks,
+                                                            int64_t N, int64_t nb, T* __restrict__ w) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * 8;
+  constexpr int BB = kq_block_bytes(TYPE);
+  for (int64_t u = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); u < N * nb; u += warps) {
+    float v[8];
+    kq_dequant8<TYPE>(blocks + u * BB, lane, v);
+    T* out = w + u * kQKK;  // row n, block b: (n * nb + b) * 256 = u * 256
+#pragma unroll
+    for (int k = 0; k < 8; ++k) out[kq_elem<TYPE>(lane, k)] = Act<T>::from_f32(v[k]);
+  }
+}
+
+// Activations at elements e, e+1 (Q6_K) or e..e+3 (Q4_K) of one row, as f32.
+template <typename T>
+__device__ __forceinline__ void ld_act2(const T* p, float& a, float& b) {
+  if constexpr (sizeof(T) == 4) {
+    const float2 v = *reinterpret_cast<const float2*>(p);
+    a = v.x;
+    b = v.y;
+  } else {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+    T lo, hi;
+    const unsigned short l16 = (unsigned short)(u & 0xFFFFu), h16 = (unsigned short)(u >> 16);
+    memcpy(&lo, &l16, 2);
+    memcpy(&hi, &h16, 2);
+    a = Act<T>::to_f32(lo);
+    b = Act<T>::to_f32(hi);
+  }
+}
+
+// y[m, n] = sum_k x[m, k] * deq(W)[n, k] in f32, rounded once to the activation
+// dtype.  One warp per output row n at a time; every lane dequantises its 8
+// weights of each super-block once and multiplies them into all MT activation
+// rows (rows m >= M are skipped).  The warp's 32 partial sums are added with a
+// butterfly of shuffles, so the summation order is fixed for a given K.
+template <int TYPE, typename T, int MT>
+__global__ void __launch_bounds__(256) kq_linear_kernel(const T* __restrict__ x,
+                                                        const uint8_t* __restrict__ blocks,
+                                                        T* __restrict__ y, int M, int64_t K, int64_t N) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nb = K / kQKK;
+  constexpr int BB = kq_block_bytes(TYPE);
+  for (int64_t n = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); n < N; n += (int64_t)gridDim.x * 8) {
+    const uint8_t* row = blocks + n * nb * BB;
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+#pragma unroll 2
+    for (int64_t b = 0; b < nb; ++b) {
+      float w[8];
+      kq_dequant8<TYPE>(row + b * BB, lane, w);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        if (m < M) {
+          const T* xr = x + (int64_t)m * K + b * kQKK;
+          float a[8];
+#pragma unroll
+          for (int k = 0; k < 8; k += 2) ld_act2(xr + kq_elem<TYPE>(lane, k), a[k], a[k + 1]);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[m] = fmaf(w[k], a[k], acc[m]);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+      if (lane == 0 && m < M) y[(int64_t)m * N + n] = Act<T>::from_f32(acc[m]);
+    }
+  }
+}
+
+template <int TYPE, typename T>
+dial_status launch_kq_dequant_t(const void* blocks, int64_t N, int64_t K, void* w, cudaStream_t st) {
+  const int64_t units = N * (K / kQKK);
+  const int64_t want = (units + 7) / 8, cap = (int64_t)sm_count() * 8;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  kq_dequantize_kernel<TYPE, T><<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(blocks), N, K / kQKK,
+                                                      static_cast<T*>(w));
+  return check_launch("kq_dequantize_kernel");
+}
+
+template <int TYPE>
+dial_status launch_kq_dequant(const void* blocks, int64_t N, int64_t K, void* w, dial_dtype wdt,
+                              cudaStream_t st) {
+  if (wdt == DIAL_F32) return launch_kq_dequant_t<TYPE, float>(blocks, N, K, w, st);
+  if (wdt == DIAL_F16) return launch_kq_dequant_t<TYPE, __half>(blocks, N, K, w, st);
+  return launch_kq_dequant_t<TYPE, __nv_bfloat16>(blocks, N, K, w, st);
+}
+
+constexpr int kKqRows = 8;  // activation rows per pass
+
+template <int TYPE, typename T>
+dial_status launch_kq_linear_t(const void* x, const void* blocks, void* y, int64_t M, int64_t K,
+                               int64_t N, cudaStream_t st) {
+  const int64_t want = (N + 7) / 8, cap = (int64_t)sm_count() * 8;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  const uint8_t* wb = static_cast<const uint8_t*>(blocks);
+  for (int64_t m0 = 0; m0 < M; m0 += kKqRows) {
+    const int mc = (int)(M - m0 < kKqRows ? M - m0 : kKqRows);
+    const T* xp = static_cast<const T*>(x) + m0 * K;
+    T* yp = static_cast<T*>(y) + m0 * N;
+    if (mc == 1)
+      kq_linear_kernel<TYPE, T, 1><<<grid, 256, 0, st>>>(xp, wb, yp, mc, K, N);
+    else if (mc == 2)
+      kq_linear_kernel<TYPE, T, 2><<<grid, 256, 0, st>>>(xp, wb, yp, mc, K, N);
+    else if (mc <= 4)
+      kq_linear_kernel<TYPE, T, 4><<<grid, 256, 0, st>>>(xp, wb, yp, mc, K, N);
+    else
+      kq_linear_kernel<TYPE, T, 8><<<grid, 256, 0, st>>>(xp, wb, yp, mc, K, N);
+    const dial_status s = check_launch("kq_linear_kernel");
+    if (s != DIAL_OK) return s;
+  }
+  return DIAL_OK;
+}
+
+template <int TYPE>
+dial_status launch_kq_linear(const void* x, dial_dtype xdt, const void* blocks, void* y, int64_t M,
+                             int64_t K, int64_t N, cudaStream_t st) {
+  if (xdt == DIAL_F32) return launch_kq_linear_t<TYPE, float>(x, blocks, y, M, K, N, st);
+  if (xdt == DIAL_F16) return launch_kq_linear_t<TYPE, __half>(x, blocks, y, M, K, N, st);
+  return launch_kq_linear_t<TYPE, __nv_bfloat16>(x, blocks, y, M, K, N, st);
+}
+
+dial_status check_kq(const void* blocks, dial_ggml_type type, int64_t N, int64_t K) {
+  if (!blocks) return fail(DIAL_ERR_INVALID_ARG, "null pointer");
+  if (type != DIAL_GGML_Q4_K && type != DIAL_GGML_Q6_K)
+    return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "ggml type %d is not Q4_K (12) or Q6_K (14)", (int)type);
+  if (N <= 0 || K <= 0) return fail(DIAL_ERR_INVALID_ARG, "sizes must be positive");
+  if (N > (1ll << 31) - 1) return fail(DIAL_ERR_SHAPE, "N exceeds 2^31-1");
+  if (K % kQKK) return fail(DIAL_ERR_SHAPE, "K-quants need K %% 256 == 0 (K=%lld)", (long long)K);
+  // Q4_K words are read 4 bytes at a time; Q6_K blocks 2 bytes at a time
+  if (reinterpret_cast<uintptr_t>(blocks) & (type == DIAL_GGML_Q4_K ? 15u : 1u))
+    return fail(DIAL_ERR_MISALIGNED, "Q4_K blocks must be 16-byte aligned, Q6_K blocks 2-byte aligned");
+  return DIAL_OK;
+}
+
+bool is_act_dtype(dial_dtype t) { return t == DIAL_F32 || t == DIAL_F16 || t == DIAL_BF16; }
+
+}  // namespace
+
+}  // namespace dial
+
+using namespace dial;
+
+extern "C" size_t dial_gguf_k_row_bytes(dial_ggml_type type, int64_t K) {
+  const int bb = kq_block_bytes((int)type);
+  if (!bb || K <= 0 || K % kQKK) return 0;
+  return (size_t)(K / kQKK) * (size_t)bb;
+}
+
+extern "C" dial_status dial_gguf_k_dequantize(const void* blocks, dial_ggml_type type, int64_t N,
+                                              int64_t K, void* w, dial_dtype wdt, dial_stream stream) {
+  clear_error();
+  dial_status s = check_kq(blocks, type, N, K);
+  if (s != DIAL_OK) return s;
+  if (!w) return fail(DIAL_ERR_INVALID_ARG, "null pointer");
+  if (!is_act_dtype(wdt)) return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "bad output dtype");
+  if (type == DIAL_GGML_Q4_K) return launch_kq_dequant<DIAL_GGML_Q4_K>(blocks, N, K, w, wdt, as_stream(stream));
+  return launch_kq_dequant<DIAL_GGML_Q6_K>(blocks, N, K, w, wdt, as_stream(stream));
+}
+
+extern "C" dial_status dial_gguf_k_linear(const void* x, dial_dtype xdt, const void* blocks,
+                                          dial_ggml_type type, void* y, int64_t M, int64_t K, int64_t N,
+                                          dial_stream stream) {
+  clear_error();
+  dial_status s = check_kq(blocks, type, N, K);
+  if (s != DIAL_OK) return s;
+  if (!x || !y) return fail(DIAL_ERR_INVALID_ARG, "null pointer");
+  if (M <= 0) return fail(DIAL_ERR_INVALID_ARG, "sizes must be positive");
+  if (!is_act_dtype(xdt)) return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "activation dtype must be f32/f16/bf16");
+  if (!aligned16(x)) return fail(DIAL_ERR_MISALIGNED, "x must be 16-byte aligned");
+  if (type == DIAL_GGML_Q4_K)
+    return launch_kq_linear<DIAL_GGML_Q4_K>(x, xdt, blocks, y, M, K, N, as_stream(stream));
+  return launch_kq_linear<DIAL_GGML_Q6_K>(x, xdt, blocks, y, M, K, N, as_stream(stream));
+}

@@ -28,7 +28,7 @@ PKG_ROOT = os.path.dirname(_HERE)
 LIB_PATH = os.environ.get("DIAL_CUDA_LIB") or os.path.join(PKG_ROOT, "_build", "libdial_cuda.so")
 
 F32, F16, BF16 = 0, 1, 2
-Q4_0, Q8_0 = 2, 8
+Q4_0, Q8_0, Q4_K, Q6_K = 2, 8, 12, 14
 
 STATUS = {
     0: "ok", 1: "invalid argument", 2: "unsupported dtype", 3: "misaligned", 4: "shape",
@@ -65,6 +65,9 @@ SIGNATURES = {
     "dial_gguf_linear_workspace_bytes": ([_i64, _i64, _i64], _sz),
     "dial_gguf_linear": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp, _sz, _vp], _i32),
     "dial_gguf_linear_noalloc": ([_vp, _i32, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _vp], _i32),
+    "dial_gguf_k_row_bytes": ([_i32, _i64], _sz),
+    "dial_gguf_k_dequantize": ([_vp, _i32, _i64, _i64, _vp, _i32, _vp], _i32),
+    "dial_gguf_k_linear": ([_vp, _i32, _vp, _i32, _vp, _i64, _i64, _i64, _vp], _i32),
     "dial_rmsnorm": ([_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, ctypes.c_float, _vp], _i32),
     "dial_rope_tables": ([_vp, _vp, _i32, _i64, _i32, ctypes.c_float, _vp], _i32),
     "dial_qk_norm_rope_kv_append": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64,
@@ -303,6 +306,57 @@ class GgufLinear:
         return self.qs.numel() + self.d.numel() * 2
 
 
+class GgufKLinear:
+    """Q4_K / Q6_K weight kept in the file's native super-block layout (the
+    reference's Q4_K_M files through candle's QMatMul, worker_gguf.rs:462-611)."""
+
+    def __init__(self, blocks, qtype: int, in_dim: int, out_dim: int, name: str = ""):
+        self.blocks, self.qtype = blocks, qtype
+        self.in_dim, self.out_dim, self.name = in_dim, out_dim, name
+
+    @classmethod
+    def from_blocks(cls, blocks, qtype: int, in_dim: int, out_dim: int, name: str = "") -> "GgufKLinear":
+        """blocks: CUDA uint8 tensor with the [out_dim, in_dim] tensor's blocks as
+        the file holds them (kept as they are; no device repack)."""
+        _require_cuda(blocks)
+        row = lib().dial_gguf_k_row_bytes(qtype, in_dim)
+        if row == 0:
+            raise ValueError(f"GGUF K-quant: bad type {qtype} or in_dim {in_dim} (needs a multiple of 256)")
+        if blocks.numel() != row * out_dim:
+            raise ValueError(f"GGUF K-quant: expected {row * out_dim} block bytes, got {blocks.numel()}")
+        return cls(blocks.contiguous(), qtype, in_dim, out_dim, name)
+
+    def dequantize(self, dtype=None):
+        torch = _torch()
+        dtype = dtype or torch.float32
+        w = torch.empty((self.out_dim, self.in_dim), dtype=dtype, device=self.blocks.device)
+        check(lib().dial_gguf_k_dequantize(self.blocks.data_ptr(), self.qtype, self.out_dim, self.in_dim,
+                                           w.data_ptr(), dtype_code(dtype), stream_ptr()),
+              "dial_gguf_k_dequantize")
+        return w
+
+    def forward(self, x, out=None):
+        """x [..., in_dim] f32/f16/bf16 -> [..., out_dim] in x's dtype."""
+        torch = _torch()
+        _require_cuda(x)
+        if x.shape[-1] != self.in_dim:
+            raise ValueError(f"GGUF input mismatch: expected last dim {self.in_dim}, got {tuple(x.shape)}")
+        x = x.contiguous()
+        rows = x.numel() // self.in_dim
+        if out is None:
+            out = torch.empty((*x.shape[:-1], self.out_dim), dtype=x.dtype, device=x.device)
+        check(lib().dial_gguf_k_linear(x.data_ptr(), dtype_code(x.dtype), self.blocks.data_ptr(), self.qtype,
+                                       out.data_ptr(), rows, self.in_dim, self.out_dim, stream_ptr()),
+              "dial_gguf_k_linear")
+        return out
+
+    __call__ = forward
+
+    @property
+    def weight_bytes(self) -> int:
+        return self.blocks.numel()
+
+
 class TextLinear:
     """Dispatch wrapper with the reference's constructor names (worker_w8a16.rs:65-121)."""
 
@@ -315,6 +369,8 @@ class TextLinear:
 
     @classmethod
     def from_gguf(cls, name: str, blocks, qtype: int, in_dim: int, out_dim: int) -> "TextLinear":
+        if qtype in (Q4_K, Q6_K):
+            return cls(GgufKLinear.from_blocks(blocks, qtype, in_dim, out_dim, name))
         return cls(GgufLinear.from_blocks(blocks, qtype, in_dim, out_dim, name))
 
     def forward(self, x, out=None):

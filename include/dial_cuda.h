@@ -55,7 +55,12 @@ enum {
 typedef enum { DIAL_F32 = 0, DIAL_F16 = 1, DIAL_BF16 = 2 } dial_dtype;
 
 /* GGML type codes, as in the GGUF file format. */
-typedef enum { DIAL_GGML_Q4_0 = 2, DIAL_GGML_Q8_0 = 8 } dial_ggml_type;
+typedef enum {
+  DIAL_GGML_Q4_0 = 2,
+  DIAL_GGML_Q8_0 = 8,
+  DIAL_GGML_Q4_K = 12, /* dial_gguf_k_* only */
+  DIAL_GGML_Q6_K = 14  /* dial_gguf_k_* only */
+} dial_ggml_type;
 
 typedef void* dial_stream; /* cudaStream_t */
 
@@ -170,6 +175,37 @@ DIAL_API dial_status dial_gguf_linear(const void* x, dial_dtype xdt, const void*
 DIAL_API dial_status dial_gguf_linear_noalloc(const void* x, dial_dtype xdt, const void* qs,
                                               const uint16_t* d, dial_ggml_type type, void* y,
                                               int64_t M, int64_t K, int64_t N, dial_stream stream);
+
+/* ------------------------------------------------------------------ GGUF K-quants
+ * Q4_K and Q6_K super-blocks of 256 weights in their native GGML layout, as a
+ * GGUF file holds them and candle's QMatMul loads them (load_worker_gguf_linear,
+ * worker_gguf.rs:462-522; the reference's deployed files are Q4_K_M):
+ *   Q4_K: 144 bytes {f16 d; f16 dmin; u8 scales[12] (6-bit scale and min of each
+ *         32-weight sub-block); u8 qs[128] (4-bit)};  value = d*sc*q - dmin*m
+ *   Q6_K: 210 bytes {u8 ql[128]; u8 qh[64]; i8 scales[16]; f16 d};
+ *         value = d*scale*(q - 32), q 6-bit
+ * Blocks are row-major over [N, K/256]; K must be a multiple of 256.  Q4_K
+ * blocks must be 16-byte aligned, Q6_K blocks 2-byte aligned.  Unlike Q4_0 and
+ * Q8_0 there is no repacked device layout: the kernels read the file's blocks.
+ */
+/* Bytes of one row of K weights (0 for a bad type or K). */
+DIAL_API size_t dial_gguf_k_row_bytes(dial_ggml_type type, int64_t K);
+
+/* w[n, k] in wdt: the GGML reference dequantisers' f32 values bit for bit
+ * (each product and the Q4_K difference rounded on its own), then to wdt. */
+DIAL_API dial_status dial_gguf_k_dequantize(const void* blocks, dial_ggml_type type, int64_t N,
+                                            int64_t K, void* w, dial_dtype wdt, dial_stream stream);
+
+/* y = x . deq(W)^T for decode-sized M: x [M, K] f32/f16/bf16 (16-byte aligned),
+ * y [M, N] in the same dtype (forward_worker_gguf keeps the activation dtype,
+ * worker_gguf.rs:589-605), f32 accumulation of f32 activations times the
+ * dequantised f32 weights, one rounding to the output dtype.  Rows are handled
+ * 8 per pass; for prefill the reference dequantises once to f16 and runs a
+ * dense GEMM (worker_gguf.rs:399-460), which dial_gguf_k_dequantize serves.
+ * Needs no workspace. */
+DIAL_API dial_status dial_gguf_k_linear(const void* x, dial_dtype xdt, const void* blocks,
+                                        dial_ggml_type type, void* y, int64_t M, int64_t K, int64_t N,
+                                        dial_stream stream);
 
 /* ------------------------------------------------------------------ decoder glue
  * Activations are row-major [tokens, ...] in `dt` (f16 as the reference's

@@ -60,6 +60,9 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_gguf_linear_exact": ([vp, i32, vp, i32, i64, i64, i64, vp], i32),
         "orc_gguf_linear_candle": ([vp, i32, vp, i32, i64, i64, i64, vp], i32),
         "orc_q8_0_quantize_rows": ([vp, i32, i64, i64, vp, vp], i32),
+        "orc_gguf_k_block_bytes": ([i32], i64),
+        "orc_gguf_k_dequantize": ([vp, i32, i64, i64, vp], i32),
+        "orc_gguf_k_linear_exact": ([vp, i32, vp, i32, i64, i64, i64, vp], i32),
     }
     f32 = ctypes.c_float
     sig.update({
@@ -251,6 +254,47 @@ def gguf_linear_candle(x: np.ndarray, blocks: np.ndarray, qtype: int, N: int,
     y = np.empty((M, N), np.float32)
     rc = lib().orc_gguf_linear_candle(_p(x), _dt(x, x_is_bf16), _p(np.ascontiguousarray(blocks)),
                                       qtype, M, K, N, _p(y))
+    assert rc == 0
+    return y
+
+
+# ---------------------------------------------------------------- GGUF K-quants
+Q4_K, Q6_K = 12, 14
+K_BLOCK_BYTES = {Q4_K: 144, Q6_K: 210}
+
+
+def gguf_k_random_blocks(rng, qtype: int, N: int, K: int, scale: float = 1e-4) -> np.ndarray:
+    """Seeded K-quant blocks [N, K/256*bytes]: random quant, scale and min bytes
+    with finite f16 super-block scales ~ N(0, scale) (GGUF weights as a file
+    holds them; a quantiser is not needed to exercise the arithmetic)."""
+    nb = K // 256
+    bb = K_BLOCK_BYTES[qtype]
+    raw = rng.integers(0, 256, (N, nb, bb), dtype=np.uint8)
+    d = rng.normal(0.0, scale, (N, nb)).astype(np.float16)
+    if qtype == Q4_K:
+        raw[:, :, 0:2] = d.view(np.uint8).reshape(N, nb, 2)
+        dmin = np.abs(rng.normal(0.0, scale, (N, nb))).astype(np.float16)
+        raw[:, :, 2:4] = dmin.view(np.uint8).reshape(N, nb, 2)
+    else:
+        raw[:, :, 208:210] = d.view(np.uint8).reshape(N, nb, 2)
+    return raw.reshape(N, nb * bb)
+
+
+def gguf_k_dequantize(blocks: np.ndarray, qtype: int, N: int, K: int) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty((N, K), np.float32)
+    rc = lib().orc_gguf_k_dequantize(_p(blocks), qtype, N, K, _p(out))
+    assert rc == 0
+    return out
+
+
+def gguf_k_linear_exact(x: np.ndarray, blocks: np.ndarray, qtype: int, N: int,
+                        x_is_bf16: bool = False) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    M, K = x.shape
+    y = np.empty((M, N), np.float64)
+    rc = lib().orc_gguf_k_linear_exact(_p(x), _dt(x, x_is_bf16), _p(np.ascontiguousarray(blocks)),
+                                       qtype, M, K, N, _p(y))
     assert rc == 0
     return y
 

@@ -375,6 +375,111 @@ ORC_API int orc_gguf_linear_candle(const void* x, int xdt, const uint8_t* blocks
   return 0;
 }
 
+/* ------------------------------------------------------------------------ */
+/* GGUF K-quants, native GGML super-blocks of 256 weights (the reference's     */
+/* deployed Q4_K_M files: docs/worker_gguf.md:1-6; loaded by                  */
+/* load_worker_gguf_linear worker_gguf.rs:462-522, arithmetic in candle-core   */
+/* 0.11.0, not vendored).  Restated from the public GGML definitions           */
+/* (block_q4_K / block_q6_K, dequantize_row_q4_K / dequantize_row_q6_K) and    */
+/* pinned against the independent gguf 0.19.0 Python dequantisers through      */
+/* tests/golden/gguf_q4_k_q6_k.npz (script: tests/golden/make_golden_k.py).   */
+/*   Q4_K 144 B: f16 d, f16 dmin, u8 scales[12], u8 qs[128]                    */
+/*   Q6_K 210 B: u8 ql[128], u8 qh[64], i8 scales[16], f16 d                   */
+/* ------------------------------------------------------------------------ */
+#define ORC_Q4_K 12
+#define ORC_Q6_K 14
+#define QKK 256
+
+ORC_API int64_t orc_gguf_k_block_bytes(int type) {
+  return type == ORC_Q4_K ? 144 : type == ORC_Q6_K ? 210 : -1;
+}
+
+/* 6-bit scale and min of Q4_K sub-block j (GGML get_scale_min_k4) */
+static void q4_k_scale_min(const uint8_t* q, int j, int* sc, int* m) {
+  if (j < 4) {
+    *sc = q[j] & 63;
+    *m = q[j + 4] & 63;
+  } else {
+    *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+    *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+/* One super-block to 256 f32 values, every product / difference rounded on
+ * its own (the file is built with -ffp-contract=off). */
+static void k_block_dequant(const uint8_t* blk, int type, float* y) {
+  if (type == ORC_Q4_K) {
+    const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+    const float dmin = h2f((uint16_t)(blk[2] | (blk[3] << 8)));
+    const uint8_t* scales = blk + 4;
+    const uint8_t* q = blk + 16;
+    for (int c = 0; c < 4; ++c) {  /* 64 weights: 32 low nibbles, then 32 high */
+      int sc, m;
+      q4_k_scale_min(scales, 2 * c, &sc, &m);
+      const float d1 = d * (float)sc, m1 = dmin * (float)m;
+      q4_k_scale_min(scales, 2 * c + 1, &sc, &m);
+      const float d2 = d * (float)sc, m2 = dmin * (float)m;
+      for (int l = 0; l < 32; ++l) y[64 * c + l] = d1 * (float)(q[32 * c + l] & 0xF) - m1;
+      for (int l = 0; l < 32; ++l) y[64 * c + 32 + l] = d2 * (float)(q[32 * c + l] >> 4) - m2;
+    }
+  } else {
+    const uint8_t* ql = blk;
+    const uint8_t* qh = blk + 128;
+    const int8_t* sc = (const int8_t*)(blk + 192);
+    const float d = h2f((uint16_t)(blk[208] | (blk[209] << 8)));
+    for (int h = 0; h < 2; ++h) {  /* 128 weights from 64 ql bytes, 32 qh bytes, 8 scales */
+      const uint8_t* L = ql + 64 * h;
+      const uint8_t* H = qh + 32 * h;
+      const int8_t* S = sc + 8 * h;
+      for (int l = 0; l < 32; ++l) {
+        const int is = l / 16;
+        const int q1 = (int)((L[l] & 0xF) | (((H[l] >> 0) & 3) << 4)) - 32;
+        const int q2 = (int)((L[l + 32] & 0xF) | (((H[l] >> 2) & 3) << 4)) - 32;
+        const int q3 = (int)((L[l] >> 4) | (((H[l] >> 4) & 3) << 4)) - 32;
+        const int q4 = (int)((L[l + 32] >> 4) | (((H[l] >> 6) & 3) << 4)) - 32;
+        float* o = y + 128 * h;
+        o[l] = d * (float)S[is] * (float)q1;
+        o[l + 32] = d * (float)S[is + 2] * (float)q2;
+        o[l + 64] = d * (float)S[is + 4] * (float)q3;
+        o[l + 96] = d * (float)S[is + 6] * (float)q4;
+      }
+    }
+  }
+}
+
+/* blocks [N, K/256] native -> w [N, K] f32 */
+ORC_API int orc_gguf_k_dequantize(const uint8_t* blocks, int type, int64_t N, int64_t K, float* w) {
+  const int64_t bb = orc_gguf_k_block_bytes(type);
+  if (bb < 0 || K % QKK) return -1;
+  const int64_t nb = K / QKK;
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n)
+    for (int64_t b = 0; b < nb; ++b) k_block_dequant(blocks + (n * nb + b) * bb, type, w + n * K + b * QKK);
+  return 0;
+}
+
+/* y = x . deq(W)^T, double accumulation over the f32 dequantised weights */
+ORC_API int orc_gguf_k_linear_exact(const void* x, int xdt, const uint8_t* blocks, int type,
+                                    int64_t M, int64_t K, int64_t N, double* y) {
+  const int64_t bb = orc_gguf_k_block_bytes(type);
+  if (bb < 0 || K % QKK) return -1;
+  const int64_t nb = K / QKK;
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n) {
+    float wrow[QKK];
+    for (int64_t m = 0; m < M; ++m) y[m * N + n] = 0.0;
+    for (int64_t b = 0; b < nb; ++b) {
+      k_block_dequant(blocks + (n * nb + b) * bb, type, wrow);
+      for (int64_t m = 0; m < M; ++m) {
+        double s = 0.0;
+        for (int j = 0; j < QKK; ++j) s += (double)wrow[j] * (double)load_act(x, xdt, m * K + b * QKK + j);
+        y[m * N + n] += s;
+      }
+    }
+  }
+  return 0;
+}
+
 /* Activation Q8_0 quantisation exposed on its own (the GPU kernels quantise
  * activations the same way before the integer block dots). */
 ORC_API int orc_q8_0_quantize_rows(const void* x, int xdt, int64_t M, int64_t K,

@@ -71,6 +71,26 @@ def test_validation_without_gpu():
     assert b"workspace" in L.dial_last_error()
 
 
+def test_gguf_k_validation_without_gpu():
+    L = D.lib()
+    fake = ctypes.c_void_p(0x1000)
+    # Q4_K / Q6_K only take K % 256 == 0, and only the K-quant entry points take them
+    assert L.dial_gguf_k_linear(fake, D.F32, fake, D.Q4_K, fake, 1, 4000, 64, None) == 4
+    assert L.dial_gguf_k_linear(fake, D.F32, fake, D.Q4_0, fake, 1, 4096, 64, None) == 2
+    assert L.dial_gguf_k_linear(None, D.F32, fake, D.Q6_K, fake, 1, 4096, 64, None) == 1
+    assert L.dial_gguf_k_linear(fake, D.F32, fake, D.Q6_K, fake, 0, 4096, 64, None) == 1
+    # Q4_K blocks are read as 16-byte words, Q6_K blocks as 2-byte words
+    assert L.dial_gguf_k_linear(fake, D.F32, ctypes.c_void_p(0x1002), D.Q4_K, fake, 1, 4096, 64, None) == 3
+    assert L.dial_gguf_k_linear(fake, D.F32, ctypes.c_void_p(0x1001), D.Q6_K, fake, 1, 4096, 64, None) == 3
+    assert L.dial_gguf_k_linear(ctypes.c_void_p(0x1008), D.F32, fake, D.Q6_K, fake, 1, 4096, 64, None) == 3
+    assert L.dial_gguf_k_dequantize(fake, D.Q4_K, 4, 4096, fake, 7, None) == 2
+    assert L.dial_gguf_linear(fake, D.F32, fake, fake, D.Q4_K, fake, 1, 4096, 64, None, 0, None) == 2
+    assert L.dial_gguf_k_row_bytes(D.Q4_K, 4096) == 16 * 144
+    assert L.dial_gguf_k_row_bytes(D.Q6_K, 14336) == 56 * 210
+    assert L.dial_gguf_k_row_bytes(D.Q6_K, 4000) == 0
+    assert L.dial_gguf_k_row_bytes(D.Q8_0, 4096) == 0
+
+
 def test_gguf_size_helpers():
     L = D.lib()
     # K=4096 -> 32 groups of 4 blocks; Q4_0 64 B / group, Q8_0 128 B / group

@@ -125,3 +125,36 @@ def test_half_conversions_match_numpy():
     # bf16 round-to-nearest-even: the error is at most half an ulp of bf16
     ulp = np.abs(back).view(np.uint32) & 0x7F800000
     assert np.all(np.abs(back - v) <= np.maximum(ulp.view(np.float32) * 2.0 ** -8, 1e-38))
+
+
+# ---------------------------------------------------------------- GGUF K-quants
+GOLDEN_K = os.path.join(os.path.dirname(__file__), "golden", "gguf_q4_k_q6_k.npz")
+
+
+@pytest.mark.parametrize("name,qt", [("q4_k", O.Q4_K), ("q6_k", O.Q6_K)])
+def test_gguf_k_dequantize_bit_exact(name, qt):
+    """The oracle's Q4_K / Q6_K dequantisers equal gguf-py's bit for bit on seeded
+    blocks and edge blocks (all-ones bytes, zero, subnormal and large scales)."""
+    g = np.load(GOLDEN_K)
+    blocks = g[f"{name}_blocks"]
+    N, K = g[f"{name}_dequant"].shape
+    w = O.gguf_k_dequantize(blocks, qt, N, K)
+    assert np.array_equal(w.view(np.uint32), g[f"{name}_dequant"].view(np.uint32))
+
+
+@pytest.mark.parametrize("name,qt", [("q4_k", O.Q4_K), ("q6_k", O.Q6_K)])
+def test_gguf_k_linear_exact_matches_fixture(name, qt):
+    g = np.load(GOLDEN_K)
+    N = g[f"{name}_dequant"].shape[0]
+    y = O.gguf_k_linear_exact(g["x"], g[f"{name}_blocks"], qt, N)
+    ref = g[f"{name}_linear_f64"]
+    assert np.abs(y - ref).max() <= 1e-12 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("qt", [O.Q4_K, O.Q6_K])
+def test_gguf_k_random_blocks_are_finite(qt):
+    rng = np.random.default_rng(3)
+    b = O.gguf_k_random_blocks(rng, qt, 16, 1024)
+    assert b.shape == (16, 4 * O.K_BLOCK_BYTES[qt])
+    w = O.gguf_k_dequantize(b, qt, 16, 1024)
+    assert np.isfinite(w).all() and np.abs(w).max() < 10.0

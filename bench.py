@@ -16,6 +16,12 @@ benchmark configurations; no dataset is involved):
                 activations.  Metric: dequant-GEMV HBM GB/s over the sweep.
   gguf_prefill  The same sweep at M = 512 (the prefill point of the GGUF
                 sweep).  Metric: dequant-GEMM TFLOP/s (tensor roofline).
+  gguf_k_sweep  The 7 linears of a Llama-3-8B layer in Q4_K and Q6_K (the
+                types of a Q4_K_M file) at M = 1, f16 activations.  Metric:
+                dequant-GEMV HBM GB/s over the sweep.
+  qwen3_decode / llama_gguf_decode / attention_batched: whole-model decode
+                (the default, qwen3_decode) and the batched decode attention;
+                their docstrings give the shapes.
 A step is one pass of the workload.  Multi-linear steps are captured once in
 a CUDA graph and replayed.  Inputs: rotating copies of the weights whose total
 exceeds the 126 MB L2, so every step reads its weights from HBM.
@@ -334,6 +340,78 @@ class GgufSweep:
         self.i += 1
 
 
+LLAMA_SHAPES = [  # (name, out N, in K) of one Llama-3-8B decoder layer
+    ("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+    ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336),
+]
+K_BLOCK_BYTES = {"Q4_K": 144, "Q6_K": 210}
+
+
+class GgufKSweep:
+    """GGUF K-quant decode sweep: the 7 linears of a Llama-3-8B layer in Q4_K and
+    in Q6_K (the two types of a Q4_K_M file) at M = 1, f16 activations, the
+    file's native super-blocks read by the decode linear."""
+    metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "q4_k/q6_k x f16"
+    kernel = "kq_linear_kernel (whole sweep)"
+    ms = (1,)
+    graph = True
+
+    def __init__(self, torch, D, rank: int = 0, world: int = 1):
+        import numpy as np
+
+        import oracle as O  # seeded block bytes only (no oracle arithmetic on this path)
+        self.torch, self.D = torch, D
+        rng = np.random.default_rng(SEED)
+        layer, per_layer = [], 0
+        for qt in (D.Q4_K, D.Q6_K):
+            for name, N, K in LLAMA_SHAPES:
+                b = torch.from_numpy(O.gguf_k_random_blocks(rng, qt, N, K).reshape(-1)).cuda()
+                lin = D.GgufKLinear.from_blocks(b, qt, K, N, name)
+                layer.append(lin)
+                per_layer += lin.weight_bytes
+        self.copies = max(2, -(-3 * L2_BYTES // per_layer))
+        self.layers = [layer] + [[D.GgufKLinear(l.blocks.clone(), l.qtype, l.in_dim, l.out_dim, l.name)
+                                  for l in layer] for _ in range(self.copies - 1)]
+        g = torch.Generator(device="cuda").manual_seed(SEED)
+        self.calls = []
+        for li, lay in enumerate(self.layers):
+            for m in self.ms:
+                for lin in lay:
+                    x = torch.randn((m, lin.in_dim), generator=g, device="cuda").half()
+                    y = torch.empty((m, lin.out_dim), device="cuda", dtype=torch.float16)
+                    self.calls.append((li, lin, x, y))
+        self.i = 0
+        self.work_per_step = self.bytes()
+        self.kernel_work = None
+        self.config = {"workload": "gguf_k_sweep", "M": list(self.ms), "types": ["Q4_K", "Q6_K"],
+                       "shapes": [f"{n}:{k}->{N}" for n, N, k in LLAMA_SHAPES], "activation": "f16",
+                       "weights": "seeded random super-blocks (finite f16 scales)",
+                       "l2": f"{self.copies} rotating layer copies "
+                             f"({self.copies * per_layer / 1e6:.0f} MB > 126 MB L2)",
+                       "launch": "CUDA graph per layer copy"}
+
+    @classmethod
+    def bytes(cls):
+        b = 0
+        for m in cls.ms:
+            for bb in K_BLOCK_BYTES.values():
+                for _, N, K in LLAMA_SHAPES:
+                    b += N * (K // 256) * bb + 2 * m * K + 2 * m * N
+        return b
+
+    def run_copy(self, li):
+        for lj, lin, x, y in self.calls:
+            if lj == li:
+                lin.forward(x, out=y)
+
+    def build_graphs(self):
+        build_copy_graphs(self)
+
+    def step(self):
+        self.graphs[self.i % self.copies].replay()
+        self.i += 1
+
+
 class GgufPrefill(GgufSweep):
     """GGUF prefill sweep: the same sweep at M = 512 (tensor-bound)."""
     metric, unit, bound, dtype = "dequant-GEMM TFLOP/s", "TFLOP/s", "tensor", "q4_0/q8_0 x f32 -> f16 MMA"
@@ -590,6 +668,7 @@ class LlamaGgufDecode(QwenDecode):
 
 
 WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep, "gguf_prefill": GgufPrefill,
+             "gguf_k_sweep": GgufKSweep,
              "qwen3_decode": QwenDecode, "llama_gguf_decode": LlamaGgufDecode,
              "attention_batched": AttentionDecode}
 
@@ -610,6 +689,11 @@ class CpuWorkload:
             self.q, self.s32, _ = O.w8a16_quantize(w)
             self.x = rng.normal(0, 1, (1, wl.K)).astype(np.float16)
             self.work = wl.bytes()
+        elif name == "gguf_k_sweep":
+            self.klins = [(O.gguf_k_random_blocks(rng, qt, N, K), qt, N, K)
+                          for qt in (O.Q4_K, O.Q6_K) for _, N, K in LLAMA_SHAPES]
+            self.xk = {K: rng.normal(0, 1, (1, K)).astype(np.float16) for _, _, K in LLAMA_SHAPES}
+            self.work = wl.bytes()
         else:
             self.lins = []
             for qt in (O.Q4_0, O.Q8_0):
@@ -625,6 +709,10 @@ class CpuWorkload:
         O = self.O
         if self.name == "w8a16_gemv":
             O.w8a16_linear_f32(self.x, self.q, self.s32)
+            return 1.0
+        if self.name == "gguf_k_sweep":
+            for blocks, qt, N, K in self.klins:
+                O.gguf_k_linear_exact(self.xk[K], blocks, qt, N)
             return 1.0
         done = 0.0
         for m in self.ms:

@@ -37,21 +37,6 @@ __host__ __device__ constexpr int kq_block_bytes(int type) {
   return type == DIAL_GGML_Q4_K ? 144 : type == DIAL_GGML_Q6_K ? 210 : 0;
 }
 
-__device__ __forceinline__ float f16_at(const uint8_t* p) {  // p: 2-byte aligned
-  return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p)));
-}
-
-// The 6-bit scale and min of Q4_K sub-block b (GGML get_scale_min_k4).
-__device__ __forceinline__ void q4k_scale_min(const uint8_t* sc, int b, int& s, int& m) {
-  if (b < 4) {
-    s = sc[b] & 63;
-    m = sc[b + 4] & 63;
-  } else {
-    s = (sc[b + 4] & 15) | ((sc[b - 4] >> 6) << 4);
-    m = (sc[b + 4] >> 4) | ((sc[b] >> 6) << 4);
-  }
-}
-
 // Lane `lane` of a warp owns 8 weights of one super-block:
 //   Q4_K: elements 64c + j0 + i (low nibbles) and 64c + 32 + j0 + i (high
 //         nibbles), i < 4, with c = lane / 8 and j0 = 4 (lane % 8): one 4-byte
@@ -70,43 +55,97 @@ __device__ __forceinline__ int kq_elem(int lane, int k) {
   }
 }
 
+// The bytes lane `lane` needs from one super-block, loaded first (so that a
+// warp can have several blocks' loads in flight) and unpacked afterwards.
+//   Q4_K: the 16-byte header {d, dmin, scales[12]} (one broadcast vector load)
+//         and one 4-byte word of qs;
+//   Q6_K: 16-bit words of ql (two), qh, the four scales (each in its own
+//         16-bit word: byte 8h + 2g + (l0 >> 4) for g < 4) and d.
 template <int TYPE>
-__device__ __forceinline__ void kq_dequant8(const uint8_t* blk, int lane, float (&w)[8]) {
-  if (TYPE == DIAL_GGML_Q4_K) {
-    const float d = f16_at(blk), dmin = f16_at(blk + 2);
-    const uint8_t* sc = blk + 4;
-    const int c = lane >> 3, j0 = (lane & 7) * 4;
-    const uint32_t q = *reinterpret_cast<const uint32_t*>(blk + 16 + 32 * c + j0);
-    int s0, m0, s1, m1;
-    q4k_scale_min(sc, 2 * c, s0, m0);
-    q4k_scale_min(sc, 2 * c + 1, s1, m1);
-    const float d0 = __fmul_rn(d, (float)s0), mm0 = __fmul_rn(dmin, (float)m0);
-    const float d1 = __fmul_rn(d, (float)s1), mm1 = __fmul_rn(dmin, (float)m1);
+struct KqRaw;
+template <>
+struct KqRaw<DIAL_GGML_Q4_K> {
+  uint4 hdr;
+  uint32_t q;
+};
+template <>
+struct KqRaw<DIAL_GGML_Q6_K> {
+  uint32_t lo, hi, qh, sc[4], d;
+};
+
+__device__ __forceinline__ uint32_t u16_at(const uint8_t* p) {
+  return *reinterpret_cast<const unsigned short*>(p);
+}
+
+template <int TYPE>
+__device__ __forceinline__ void kq_load(const uint8_t* blk, int lane, KqRaw<TYPE>& r) {
+  if constexpr (TYPE == DIAL_GGML_Q4_K) {
+    r.hdr = *reinterpret_cast<const uint4*>(blk);
+    r.q = *reinterpret_cast<const uint32_t*>(blk + 16 + 32 * (lane >> 3) + (lane & 7) * 4);
+  } else {
+    const int h = lane >> 4, l0 = (lane & 15) * 2;
+    r.lo = u16_at(blk + 64 * h + l0);       // ql[64h + l0 ..]
+    r.hi = u16_at(blk + 64 * h + 32 + l0);  // ql[64h + 32 + l0 ..]
+    r.qh = u16_at(blk + 128 + 32 * h + l0);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) r.sc[g] = u16_at(blk + 192 + 8 * h + 2 * g);  // bytes 8h+2g, 8h+2g+1
+    r.d = u16_at(blk + 208);
+  }
+}
+
+__device__ __forceinline__ uint32_t byte_of(const uint4& v, int i) {
+  return (word(v, i >> 2) >> (8 * (i & 3))) & 0xFFu;
+}
+
+template <int TYPE>
+__device__ __forceinline__ void kq_unpack(const KqRaw<TYPE>& r, int lane, float (&w)[8]) {
+  if constexpr (TYPE == DIAL_GGML_Q4_K) {
+    const float d = __half2float(__ushort_as_half((unsigned short)(r.hdr.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(r.hdr.x >> 16)));
+    const int c = lane >> 3;
+    // scales[j] is header byte 4 + j (GGML get_scale_min_k4 on sub-blocks 2c, 2c+1)
+    int s[2], m[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int j = 2 * c + t;
+      if (j < 4) {
+        s[t] = (int)(byte_of(r.hdr, 4 + j) & 63u);
+        m[t] = (int)(byte_of(r.hdr, 8 + j) & 63u);
+      } else {
+        s[t] = (int)((byte_of(r.hdr, 8 + j) & 15u) | ((byte_of(r.hdr, j) >> 6) << 4));
+        m[t] = (int)((byte_of(r.hdr, 8 + j) >> 4) | ((byte_of(r.hdr, 4 + j) >> 6) << 4));
+      }
+    }
+    const float d0 = __fmul_rn(d, (float)s[0]), mm0 = __fmul_rn(dmin, (float)m[0]);
+    const float d1 = __fmul_rn(d, (float)s[1]), mm1 = __fmul_rn(dmin, (float)m[1]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t byte = (q >> (8 * i)) & 0xFFu;
+      const uint32_t byte = (r.q >> (8 * i)) & 0xFFu;
       w[i] = __fsub_rn(__fmul_rn(d0, (float)(byte & 15u)), mm0);
       w[4 + i] = __fsub_rn(__fmul_rn(d1, (float)(byte >> 4)), mm1);
     }
   } else {
-    const float d = f16_at(blk + 208);
-    const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
-    const int h = lane >> 4, l0 = (lane & 15) * 2;
-    const uint32_t lo = *reinterpret_cast<const unsigned short*>(blk + 64 * h + l0);       // ql[l0..+1]
-    const uint32_t hi = *reinterpret_cast<const unsigned short*>(blk + 64 * h + 32 + l0);  // ql[l0+32..]
-    const uint32_t qh = *reinterpret_cast<const unsigned short*>(blk + 128 + 32 * h + l0);
+    const float d = __half2float(__ushort_as_half((unsigned short)r.d));
+    const int sh = ((lane & 15) * 2) >> 4 ? 8 : 0;  // l0 >> 4 picks the high byte
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const float dg = __fmul_rn(d, (float)sc[8 * h + 2 * g + (l0 >> 4)]);
+      const float dg = __fmul_rn(d, (float)(int8_t)((r.sc[g] >> sh) & 0xFFu));
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        const uint32_t ql = ((g & 1) ? hi : lo) >> (8 * i);
+        const uint32_t ql = ((g & 1) ? r.hi : r.lo) >> (8 * i);
         const uint32_t low = (g >> 1) ? ((ql >> 4) & 15u) : (ql & 15u);
-        const uint32_t high = (qh >> (8 * i + 2 * g)) & 3u;
+        const uint32_t high = (r.qh >> (8 * i + 2 * g)) & 3u;
         w[2 * g + i] = __fmul_rn(dg, (float)((int)(low | (high << 4)) - 32));
       }
     }
   }
+}
+
+template <int TYPE>
+__device__ __forceinline__ void kq_dequant8(const uint8_t* blk, int lane, float (&w)[8]) {
+  KqRaw<TYPE> r;
+  kq_load<TYPE>(blk, lane, r);
+  kq_unpack<TYPE>(r, lane, w);
 }
 
 // w[n, k] in wdt.  One warp per (row, super-block).
@@ -144,43 +183,86 @@ __device__ __forceinline__ void ld_act2(const T* p, float& a, float& b) {
 }
 
 // y[m, n] = sum_k x[m, k] * deq(W)[n, k] in f32, rounded once to the activation
-// dtype.  One warp per output row n at a time; every lane dequantises its 8
-// weights of each super-block once and multiplies them into all MT activation
-// rows (rows m >= M are skipped).  The warp's 32 partial sums are added with a
-// butterfly of shuffles, so the summation order is fixed for a given K.
-template <int TYPE, typename T, int MT>
+// dtype.  KS warps share an output row (8 / KS rows per CTA pass): warp part p
+// takes super-blocks p, p + KS, p + 2 KS, ..., loading the bytes of four of
+// them before unpacking any, so that each warp keeps four blocks' loads in
+// flight.  Every lane dequantises its 8 weights of a block once and multiplies
+// them into all MT activation rows (rows m >= M are skipped).  A warp's 32
+// partial sums are added by a butterfly of shuffles and the KS parts of a row
+// in part order through shared memory, so the summation order is fixed for a
+// given K and KS.
+template <int TYPE, typename T, int MT, int KS>
 __global__ void __launch_bounds__(256) kq_linear_kernel(const T* __restrict__ x,
                                                         const uint8_t* __restrict__ blocks,
                                                         T* __restrict__ y, int M, int64_t K, int64_t N) {
-  const int lane = threadIdx.x & 31;
-  const int64_t nb = K / kQKK;
+  constexpr int RPC = 8 / KS;  // rows per CTA pass
   constexpr int BB = kq_block_bytes(TYPE);
-  for (int64_t n = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); n < N; n += (int64_t)gridDim.x * 8) {
-    const uint8_t* row = blocks + n * nb * BB;
+  constexpr int U = 4;         // blocks in flight per warp
+  __shared__ float part[KS > 1 ? 8 : 1][MT];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r = warp / KS, p = warp % KS;
+  const int64_t nb = K / kQKK;
+  for (int64_t n0 = (int64_t)blockIdx.x * RPC; n0 < N; n0 += (int64_t)gridDim.x * RPC) {
+    const int64_t n = n0 + r;
     float acc[MT];
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
-#pragma unroll 2
-    for (int64_t b = 0; b < nb; ++b) {
-      float w[8];
-      kq_dequant8<TYPE>(row + b * BB, lane, w);
+    if (n < N) {
+      const uint8_t* row = blocks + n * nb * BB;
+      for (int64_t b0 = p; b0 < nb; b0 += (int64_t)U * KS) {
+        KqRaw<TYPE> raw[U];
 #pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        if (m < M) {
-          const T* xr = x + (int64_t)m * K + b * kQKK;
-          float a[8];
+        for (int u = 0; u < U; ++u) {
+          const int64_t b = b0 + (int64_t)u * KS;
+          if (b < nb) kq_load<TYPE>(row + b * BB, lane, raw[u]);
+        }
 #pragma unroll
-          for (int k = 0; k < 8; k += 2) ld_act2(xr + kq_elem<TYPE>(lane, k), a[k], a[k + 1]);
+        for (int u = 0; u < U; ++u) {
+          const int64_t b = b0 + (int64_t)u * KS;
+          if (b < nb) {
+            float w[8];
+            kq_unpack<TYPE>(raw[u], lane, w);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) acc[m] = fmaf(w[k], a[k], acc[m]);
+            for (int m = 0; m < MT; ++m) {
+              if (m < M) {
+                const T* xr = x + (int64_t)m * K + b * kQKK;
+                float a[8];
+#pragma unroll
+                for (int k = 0; k < 8; k += 2) ld_act2(xr + kq_elem<TYPE>(lane, k), a[k], a[k + 1]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) acc[m] = fmaf(w[k], a[k], acc[m]);
+              }
+            }
+          }
         }
       }
     }
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
+    for (int m = 0; m < MT; ++m)
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-      if (lane == 0 && m < M) y[(int64_t)m * N + n] = Act<T>::from_f32(acc[m]);
+    if constexpr (KS == 1) {
+      if (lane == 0 && n < N)
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+          if (m < M) y[(int64_t)m * N + n] = Act<T>::from_f32(acc[m]);
+    } else {
+      if (lane == 0)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) part[warp][m] = acc[m];
+      __syncthreads();
+      if (p == 0 && lane == 0 && n < N) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          if (m < M) {
+            float v = part[warp][m];
+#pragma unroll
+            for (int q = 1; q < KS; ++q) v += part[warp + q][m];
+            y[(int64_t)m * N + n] = Act<T>::from_f32(v);
+          }
+        }
+      }
+      __syncthreads();  // part[] is rewritten by the next pass
     }
   }
 }
@@ -205,24 +287,54 @@ dial_status launch_kq_dequant(const void* blocks, int64_t N, int64_t K, void* w,
 
 constexpr int kKqRows = 8;  // activation rows per pass
 
+// Warps per output row: the fewest (1, 2, 4 or 8) that give the GPU about
+// 32 warps per SM (four resident 256-thread CTAs at 64 registers a thread),
+// keeping at least four super-blocks per warp where the row has them.
+int kq_warps_per_row(int64_t N, int64_t nb) {
+  const int64_t want = (int64_t)sm_count() * 32;
+  int ks = 1;
+  while (ks < 8 && N * ks < want && nb >= 4 * ks) ks *= 2;
+  return ks;
+}
+
+template <int TYPE, typename T, int MT, int KS>
+void launch_kq_linear_ks(const T* x, const uint8_t* w, T* y, int mc, int64_t K, int64_t N, cudaStream_t st) {
+  constexpr int RPC = 8 / KS;
+  static int occ = 0;  // resident CTAs per SM (the same on every B200)
+  if (occ == 0) {
+    int o = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kq_linear_kernel<TYPE, T, MT, KS>, 256, 0) !=
+            cudaSuccess || o < 1)
+      o = 1;
+    occ = o;
+  }
+  const int64_t want = (N + RPC - 1) / RPC, cap = (int64_t)sm_count() * occ;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  kq_linear_kernel<TYPE, T, MT, KS><<<grid, 256, 0, st>>>(x, w, y, mc, K, N);
+}
+
+template <int TYPE, typename T, int MT>
+void launch_kq_linear_mt(const T* x, const uint8_t* w, T* y, int mc, int64_t K, int64_t N, int ks,
+                         cudaStream_t st) {
+  if (ks == 1) launch_kq_linear_ks<TYPE, T, MT, 1>(x, w, y, mc, K, N, st);
+  else if (ks == 2) launch_kq_linear_ks<TYPE, T, MT, 2>(x, w, y, mc, K, N, st);
+  else if (ks == 4) launch_kq_linear_ks<TYPE, T, MT, 4>(x, w, y, mc, K, N, st);
+  else launch_kq_linear_ks<TYPE, T, MT, 8>(x, w, y, mc, K, N, st);
+}
+
 template <int TYPE, typename T>
 dial_status launch_kq_linear_t(const void* x, const void* blocks, void* y, int64_t M, int64_t K,
                                int64_t N, cudaStream_t st) {
-  const int64_t want = (N + 7) / 8, cap = (int64_t)sm_count() * 8;
-  const unsigned grid = (unsigned)(want < cap ? want : cap);
   const uint8_t* wb = static_cast<const uint8_t*>(blocks);
+  const int ks = kq_warps_per_row(N, K / kQKK);
   for (int64_t m0 = 0; m0 < M; m0 += kKqRows) {
     const int mc = (int)(M - m0 < kKqRows ? M - m0 : kKqRows);
     const T* xp = static_cast<const T*>(x) + m0 * K;
     T* yp = static_cast<T*>(y) + m0 * N;
-    if (mc == 1)
-      kq_linear_kernel<TYPE, T, 1><<<grid, 256, 0, st>>>(xp, wb, yp, mc, K, N);
-    else if (mc == 2)
-      kq_linear_kernel<TYPE, T, 2><<<grid, 256, 0, st>>>(xp, wb, yp, mc, K, N);
-    else if (mc <= 4)
-      kq_linear_kernel<TYPE, T, 4><<<grid, 256, 0, st>>>(xp, wb, yp, mc, K, N);
-    else
-      kq_linear_kernel<TYPE, T, 8><<<grid, 256, 0, st>>>(xp, wb, yp, mc, K, N);
+    if (mc == 1) launch_kq_linear_mt<TYPE, T, 1>(xp, wb, yp, mc, K, N, ks, st);
+    else if (mc == 2) launch_kq_linear_mt<TYPE, T, 2>(xp, wb, yp, mc, K, N, ks, st);
+    else if (mc <= 4) launch_kq_linear_mt<TYPE, T, 4>(xp, wb, yp, mc, K, N, ks, st);
+    else launch_kq_linear_mt<TYPE, T, 8>(xp, wb, yp, mc, K, N, ks, st);
     const dial_status s = check_launch("kq_linear_kernel");
     if (s != DIAL_OK) return s;
   }

@@ -93,8 +93,10 @@ __device__ __forceinline__ void kq_load(const uint8_t* blk, int lane, KqRaw<TYPE
   }
 }
 
-__device__ __forceinline__ uint32_t byte_of(const uint4& v, int i) {
-  return (word(v, i >> 2) >> (8 * (i & 3))) & 0xFFu;
+// Exact float of a small unsigned integer v < 2^23 without an I2F (a slow
+// pipe): 2^23 + v has v as its mantissa, and the subtraction is exact.
+__device__ __forceinline__ float small_u2f(uint32_t v, float bias = 8388608.0f) {
+  return __uint_as_float(0x4B000000u | v) - bias;
 }
 
 template <int TYPE>
@@ -102,40 +104,37 @@ __device__ __forceinline__ void kq_unpack(const KqRaw<TYPE>& r, int lane, float 
   if constexpr (TYPE == DIAL_GGML_Q4_K) {
     const float d = __half2float(__ushort_as_half((unsigned short)(r.hdr.x & 0xFFFFu)));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(r.hdr.x >> 16)));
-    const int c = lane >> 3;
-    // scales[j] is header byte 4 + j (GGML get_scale_min_k4 on sub-blocks 2c, 2c+1)
-    int s[2], m[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const int j = 2 * c + t;
-      if (j < 4) {
-        s[t] = (int)(byte_of(r.hdr, 4 + j) & 63u);
-        m[t] = (int)(byte_of(r.hdr, 8 + j) & 63u);
-      } else {
-        s[t] = (int)((byte_of(r.hdr, 8 + j) & 15u) | ((byte_of(r.hdr, j) >> 6) << 4));
-        m[t] = (int)((byte_of(r.hdr, 8 + j) >> 4) | ((byte_of(r.hdr, 4 + j) >> 6) << 4));
-      }
-    }
-    const float d0 = __fmul_rn(d, (float)s[0]), mm0 = __fmul_rn(dmin, (float)m[0]);
-    const float d1 = __fmul_rn(d, (float)s[1]), mm1 = __fmul_rn(dmin, (float)m[1]);
+    // sub-blocks j = 2c, 2c + 1 (c = lane / 8); scales[] is header bytes 4..15,
+    // i.e. words y (bytes 4-7), z (8-11), w (12-15).  With jj = j mod 4 (here
+    // 2 (c mod 2) and the next byte), GGML get_scale_min_k4 reads
+    //   j < 4:  sc = y[jj] & 63,                   m = z[jj] & 63
+    //   j >= 4: sc = (w[jj] & 15) | (y[jj] >> 6) << 4, m = (w[jj] >> 4) | (z[jj] >> 6) << 4
+    // done here on both sub-blocks at once (two bytes of each word).
+    const int c = lane >> 3, sh = 16 * (c & 1);
+    const uint32_t a = (r.hdr.y >> sh) & 0xFFFFu, b = (r.hdr.z >> sh) & 0xFFFFu, e = (r.hdr.w >> sh) & 0xFFFFu;
+    const bool hi = c >= 2;
+    const uint32_t s2 = hi ? ((e & 0x0F0Fu) | ((a >> 2) & 0x3030u)) : (a & 0x3F3Fu);
+    const uint32_t m2 = hi ? (((e >> 4) & 0x0F0Fu) | ((b >> 2) & 0x3030u)) : (b & 0x3F3Fu);
+    const float d0 = __fmul_rn(d, small_u2f(s2 & 0xFFu)), mm0 = __fmul_rn(dmin, small_u2f(m2 & 0xFFu));
+    const float d1 = __fmul_rn(d, small_u2f(s2 >> 8)), mm1 = __fmul_rn(dmin, small_u2f(m2 >> 8));
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t byte = (r.q >> (8 * i)) & 0xFFu;
-      w[i] = __fsub_rn(__fmul_rn(d0, (float)(byte & 15u)), mm0);
-      w[4 + i] = __fsub_rn(__fmul_rn(d1, (float)(byte >> 4)), mm1);
+      w[i] = __fsub_rn(__fmul_rn(d0, small_u2f((r.q >> (8 * i)) & 15u)), mm0);
+      w[4 + i] = __fsub_rn(__fmul_rn(d1, small_u2f((r.q >> (8 * i + 4)) & 15u)), mm1);
     }
   } else {
     const float d = __half2float(__ushort_as_half((unsigned short)r.d));
     const int sh = ((lane & 15) * 2) >> 4 ? 8 : 0;  // l0 >> 4 picks the high byte
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const float dg = __fmul_rn(d, (float)(int8_t)((r.sc[g] >> sh) & 0xFFu));
+      // int8 scale: (u ^ 0x80) - 128
+      const float dg = __fmul_rn(d, small_u2f(((r.sc[g] >> sh) & 0xFFu) ^ 0x80u, 8388736.0f));
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const uint32_t ql = ((g & 1) ? r.hi : r.lo) >> (8 * i);
         const uint32_t low = (g >> 1) ? ((ql >> 4) & 15u) : (ql & 15u);
         const uint32_t high = (r.qh >> (8 * i + 2 * g)) & 3u;
-        w[2 * g + i] = __fmul_rn(dg, (float)((int)(low | (high << 4)) - 32));
+        w[2 * g + i] = __fmul_rn(dg, small_u2f(low | (high << 4), 8388640.0f));  // q - 32
       }
     }
   }

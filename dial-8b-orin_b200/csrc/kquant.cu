@@ -163,16 +163,6 @@ __global__ void __launch_bounds__(256) kq_dequantize_kernel(const uint8_t* __res
   }
 }
 
-// Asks L2 for the 16-byte-aligned part of [p, p + bytes) (a hint: no data is
-// returned and nothing waits for it).  The range is shrunk, never widened, to
-// 16-byte boundaries, so it stays inside the buffer that holds [p, p + bytes).
-__device__ __forceinline__ void prefetch_l2(const uint8_t* p, int64_t bytes) {
-  const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 15u) & ~uintptr_t(15);
-  const uintptr_t b = (reinterpret_cast<uintptr_t>(p) + (uintptr_t)bytes) & ~uintptr_t(15);
-  if (b > a)
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((uint32_t)(b - a)) : "memory");
-}
-
 // Activations at elements e, e+1 (Q6_K) or e..e+3 (Q4_K) of one row, as f32.
 template <typename T>
 __device__ __forceinline__ void ld_act2(const T* p, float& a, float& b) {
@@ -211,15 +201,8 @@ __global__ void __launch_bounds__(256) kq_linear_kernel(const T* __restrict__ x,
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r = warp / KS, p = warp % KS;
   const int64_t nb = K / kQKK;
-  const int64_t stride = (int64_t)gridDim.x * RPC;
-  for (int64_t n0 = (int64_t)blockIdx.x * RPC; n0 < N; n0 += stride) {
+  for (int64_t n0 = (int64_t)blockIdx.x * RPC; n0 < N; n0 += (int64_t)gridDim.x * RPC) {
     const int64_t n = n0 + r;
-    // The row's bytes go to L2 ahead of the loads (the whole row at once, and
-    // the row this warp takes next), so the loads below wait on L2, not DRAM.
-    if (p == 0 && lane == 0) {
-      if (n0 == (int64_t)blockIdx.x * RPC && n < N) prefetch_l2(blocks + n * nb * BB, nb * BB);
-      if (n + stride < N) prefetch_l2(blocks + (n + stride) * nb * BB, nb * BB);
-    }
     float acc[MT];
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[m] = 0.0f;

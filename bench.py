@@ -51,6 +51,7 @@ for _p in (ROOT, PKG):
         sys.path.insert(0, _p)
 
 SEED = 299792458
+DATA = "synthetic (seeded N(0,0.02) weights, N(0,1) activations)"
 L2_BYTES = 126 * 2**20
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -353,6 +354,7 @@ class GgufKSweep:
     file's native super-blocks read by the decode linear."""
     metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "q4_k/q6_k x f16"
     kernel = "kq_linear_kernel (whole sweep)"
+    data = "synthetic (seeded random Q4_K/Q6_K super-blocks with N(0,1e-4) f16 scales, N(0,1) activations)"
     ms = (1,)
     graph = True
 
@@ -899,7 +901,7 @@ def run_reference(args, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(work / (value * unit_scale(wl.unit)) * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
-        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+        "data": getattr(wl, "data", DATA),
         "config": {"workload": args.workload},
         "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads, "kind": "port",
                          "sample": f"per step: {sample}"},
@@ -1007,7 +1009,7 @@ def run_ours(args, rank, local, world):
         "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
         "higher_is_better": True, "scaling": "strong" if pipelined else "weak", "vs_baseline": None,
-        "dtype": wl.dtype, "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+        "dtype": wl.dtype, "data": getattr(wl, "data", DATA),
         "config": dict(wl.config, parallelism=(f"pipeline x{world}" if pipelined else f"replicas x{world}")),
         "roofline": {"bound": wl.bound, "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s" if wl.bound == "hbm" else "TFLOP/s",

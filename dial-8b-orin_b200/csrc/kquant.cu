@@ -299,13 +299,17 @@ int kq_warps_per_row(int64_t N, int64_t nb) {
 template <int TYPE, typename T, int MT, int KS>
 void launch_kq_linear_ks(const T* x, const uint8_t* w, T* y, int mc, int64_t K, int64_t N, cudaStream_t st) {
   constexpr int RPC = 8 / KS;
-  static int occ = 0;  // resident CTAs per SM (the same on every B200)
+  // resident CTAs per SM (the same on every B200); worker threads may race to
+  // set it, all with the same value
+  static std::atomic<int> occ_cache{0};
+  int occ = occ_cache.load(std::memory_order_relaxed);
   if (occ == 0) {
-    int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kq_linear_kernel<TYPE, T, MT, KS>, 256, 0) !=
-            cudaSuccess || o < 1)
-      o = 1;
-    occ = o;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kq_linear_kernel<TYPE, T, MT, KS>, 256, 0) !=
+            cudaSuccess || occ < 1) {
+      (void)cudaGetLastError();
+      occ = 1;
+    }
+    occ_cache.store(occ, std::memory_order_relaxed);
   }
   const int64_t want = (N + RPC - 1) / RPC, cap = (int64_t)sm_count() * occ;
   const unsigned grid = (unsigned)(want < cap ? want : cap);

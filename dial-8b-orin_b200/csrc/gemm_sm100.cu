@@ -739,14 +739,17 @@ dial_status make_x_map(CUtensorMap* map, const void* x, bool bf16, int64_t M, in
 // cross-CTA reduction.  Cluster capacity comes from the occupancy API.
 template <auto KERN>
 int choose_split(int64_t tiles, int ngr, int smem_bytes, int max_split, int threads) {
-  static int cap[64][kMaxSplit + 1];  // active CTAs per device and split (0: not queried)
+  // active CTAs per device and split (0: not queried); worker threads may race
+  // to fill an entry, all with the same value
+  static std::atomic<int> cap[64][kMaxSplit + 1];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
   int best = 1;
   double best_cost = 1e30;
   for (int S = 1; S <= max_split && S <= ngr; S *= 2) {
     if (S > 1 && ngr / S < 2) break;
-    if (cap[dev][S] == 0) {
+    int c = cap[dev][S].load(std::memory_order_relaxed);
+    if (c == 0) {
       int clusters = 0;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(1, 1, (unsigned)S);
@@ -763,10 +766,11 @@ int choose_split(int64_t tiles, int ngr, int smem_bytes, int max_split, int thre
         cudaGetLastError();
         clusters = S == 1 ? sm_count() : 0;
       }
-      cap[dev][S] = clusters > 0 ? clusters * S : -1;
+      c = clusters > 0 ? clusters * S : -1;
+      cap[dev][S].store(c, std::memory_order_relaxed);
     }
-    if (cap[dev][S] < 0) continue;
-    const double waves = (double)((tiles * S + cap[dev][S] - 1) / cap[dev][S]);
+    if (c < 0) continue;
+    const double waves = (double)((tiles * S + c - 1) / c);
     const double cost = waves * ((ngr + S - 1) / S + 4 + (S > 1 ? 1 : 0));
     if (cost < best_cost) {
       best_cost = cost;

@@ -712,9 +712,9 @@ class CpuWorkload:
         if self.name == "w8a16_gemv":
             O.w8a16_linear_f32(self.x, self.q, self.s32)
             return 1.0
-        if self.name == "gguf_k_sweep":
+        if self.name == "gguf_k_sweep":  # the CPU QMatMul arithmetic (Q8_K activations)
             for blocks, qt, N, K in self.klins:
-                O.gguf_k_linear_exact(self.xk[K], blocks, qt, N)
+                O.gguf_k_linear_candle(self.xk[K], blocks, qt, N)
             return 1.0
         done = 0.0
         for m in self.ms:

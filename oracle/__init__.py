@@ -63,6 +63,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_gguf_k_block_bytes": ([i32], i64),
         "orc_gguf_k_dequantize": ([vp, i32, i64, i64, vp], i32),
         "orc_gguf_k_linear_exact": ([vp, i32, vp, i32, i64, i64, i64, vp], i32),
+        "orc_gguf_k_linear_candle": ([vp, i32, vp, i32, i64, i64, i64, vp], i32),
     }
     f32 = ctypes.c_float
     sig.update({
@@ -295,6 +296,18 @@ def gguf_k_linear_exact(x: np.ndarray, blocks: np.ndarray, qtype: int, N: int,
     y = np.empty((M, N), np.float64)
     rc = lib().orc_gguf_k_linear_exact(_p(x), _dt(x, x_is_bf16), _p(np.ascontiguousarray(blocks)),
                                        qtype, M, K, N, _p(y))
+    assert rc == 0
+    return y
+
+
+def gguf_k_linear_candle(x: np.ndarray, blocks: np.ndarray, qtype: int, N: int,
+                         x_is_bf16: bool = False) -> np.ndarray:
+    """GGML / candle CPU arithmetic for Q4_K / Q6_K (Q8_K activations, integer dots)."""
+    x = np.ascontiguousarray(x)
+    M, K = x.shape
+    y = np.empty((M, N), np.float32)
+    rc = lib().orc_gguf_k_linear_candle(_p(x), _dt(x, x_is_bf16), _p(np.ascontiguousarray(blocks)),
+                                        qtype, M, K, N, _p(y))
     assert rc == 0
     return y
 

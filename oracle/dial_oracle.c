@@ -22,6 +22,10 @@
  *    independent `gguf` 0.19.0 Python implementation through the fixtures in
  *    tests/golden/ (script: tests/golden/make_golden.py).  candle equality
  *    itself cannot be checked here (no Rust toolchain, candle not vendored).
+ *  - GGUF Q4_K / Q6_K (the reference's Q4_K_M files, docs/worker_gguf.md:1-6):
+ *    dequantisers restated from the public GGML definitions, pinned bit-for-bit
+ *    to gguf 0.19.0 (tests/golden/make_golden_k.py); an exact linear and the
+ *    GGML/candle CPU arithmetic (Q8_K activations), the latter unpinned.
  *  - Decoder glue: text.rs:1478-1596 (attention order), text.rs:1636-1688
  *    (residuals), text.rs:816-820 (SwiGLU), llama3/cache.rs:24-64 (RoPE
  *    tables), cache.rs:149-217 (KV append), qwen3_vl.rs:130-143 (argmax).
@@ -477,6 +481,120 @@ ORC_API int orc_gguf_k_linear_exact(const void* x, int xdt, const uint8_t* block
       }
     }
   }
+  return 0;
+}
+
+/*
+ * The CPU arithmetic of GGML / candle k_quants for Q4_K and Q6_K (the scalar
+ * vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K): each activation row is quantised per
+ * 256 to Q8_K blocks (f32 d, int8 qs[256], int16 sums of every 16), with
+ * iscale = -128/max (max = the element of largest magnitude, sign kept),
+ * q = min(127, round-half-even(iscale * x)), d = 1/iscale; then per weight
+ * block an exact integer dot per sub-block times its 6-bit (Q4_K) or int8
+ * (Q6_K) scale, scaled in f32:
+ *   Q4_K: sumf += (d_w*d_x) * sum_j sc_j * dot_j  -  (dmin_w*d_x) * sum_j m_j * bsum_j
+ *   Q6_K: sumf += (d_w*d_x) * sum_j sc_j * dot_j          (q6 - 32 in the dots)
+ * The published algorithm, restated; candle-core 0.11.0 is not vendored, so
+ * equality with its code (Q8_K scale and rounding rule, float order) is
+ * unverified.  Used as the CPU baseline of the K-quant decode and as a second,
+ * looser oracle.  y is f32.
+ */
+static void q8_k_block(const float* x, float* d, int8_t* qs, int16_t* bsums) {
+  float amax = 0.0f, mx = 0.0f;
+  for (int j = 0; j < QKK; ++j) {
+    const float ax = fabsf(x[j]);
+    if (ax > amax) {
+      amax = ax;
+      mx = x[j];
+    }
+  }
+  if (amax == 0.0f) {
+    *d = 0.0f;
+    memset(qs, 0, QKK);
+    memset(bsums, 0, 16 * sizeof(int16_t));
+    return;
+  }
+  const float iscale = -128.0f / mx;
+  for (int j = 0; j < QKK; ++j) {
+    const long v = lrintf(iscale * x[j]);
+    qs[j] = (int8_t)(v > 127 ? 127 : v);
+  }
+  for (int g = 0; g < 16; ++g) {
+    int s = 0;
+    for (int j = 0; j < 16; ++j) s += qs[16 * g + j];
+    bsums[g] = (int16_t)s;
+  }
+  *d = 1.0f / iscale;
+}
+
+ORC_API int orc_gguf_k_linear_candle(const void* x, int xdt, const uint8_t* blocks, int type,
+                                     int64_t M, int64_t K, int64_t N, float* y) {
+  const int64_t bb = orc_gguf_k_block_bytes(type);
+  if (bb < 0 || K % QKK) return -1;
+  const int64_t nb = K / QKK;
+  float* xd = (float*)malloc(sizeof(float) * (size_t)(M * nb));
+  int8_t* xq = (int8_t*)malloc((size_t)(M * K));
+  int16_t* xs = (int16_t*)malloc(sizeof(int16_t) * (size_t)(M * nb * 16));
+  float buf[QKK];
+  for (int64_t m = 0; m < M; ++m)
+    for (int64_t b = 0; b < nb; ++b) {
+      for (int j = 0; j < QKK; ++j) buf[j] = load_act(x, xdt, m * K + b * QKK + j);
+      q8_k_block(buf, xd + m * nb + b, xq + m * K + b * QKK, xs + (m * nb + b) * 16);
+    }
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      float sumf = 0.0f;
+      for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* wb = blocks + (n * nb + b) * bb;
+        const int8_t* q8 = xq + m * K + b * QKK;
+        const float dx = xd[m * nb + b];
+        if (type == ORC_Q4_K) {
+          const uint8_t* q4 = wb + 16;
+          int isum = 0, msum = 0;
+          for (int c = 0; c < 4; ++c) {
+            int sc0, m0, sc1, m1, dot0 = 0, dot1 = 0;
+            q4_k_scale_min(wb + 4, 2 * c, &sc0, &m0);
+            q4_k_scale_min(wb + 4, 2 * c + 1, &sc1, &m1);
+            for (int l = 0; l < 32; ++l) {
+              dot0 += (q4[32 * c + l] & 0xF) * q8[64 * c + l];
+              dot1 += (q4[32 * c + l] >> 4) * q8[64 * c + 32 + l];
+            }
+            isum += sc0 * dot0 + sc1 * dot1;
+            const int16_t* bs = xs + (m * nb + b) * 16 + 4 * c;
+            msum += m0 * (bs[0] + bs[1]) + m1 * (bs[2] + bs[3]);
+          }
+          const float d = h2f((uint16_t)(wb[0] | (wb[1] << 8))) * dx;
+          const float dmin = h2f((uint16_t)(wb[2] | (wb[3] << 8))) * dx;
+          sumf += d * (float)isum;
+          sumf -= dmin * (float)msum;
+        } else {
+          const int8_t* sc = (const int8_t*)(wb + 192);
+          int isum = 0;
+          for (int h = 0; h < 2; ++h) {
+            const uint8_t* L = wb + 64 * h;
+            const uint8_t* H = wb + 128 + 32 * h;
+            for (int g = 0; g < 4; ++g)
+              for (int half = 0; half < 2; ++half) {
+                int dot = 0;
+                for (int ll = 0; ll < 16; ++ll) {
+                  const int l = 16 * half + ll;
+                  const int lo = (g & 1) ? L[l + 32] : L[l];
+                  const int q = (int)(((g >> 1) ? (lo >> 4) : (lo & 0xF)) | (((H[l] >> (2 * g)) & 3) << 4)) - 32;
+                  dot += q * q8[128 * h + 32 * g + l];
+                }
+                isum += sc[8 * h + 2 * g + half] * dot;
+              }
+          }
+          sumf += h2f((uint16_t)(wb[208] | (wb[209] << 8))) * dx * (float)isum;
+        }
+      }
+      y[m * N + n] = sumf;
+    }
+  }
+  free(xd);
+  free(xq);
+  free(xs);
   return 0;
 }
 

@@ -158,3 +158,23 @@ def test_gguf_k_random_blocks_are_finite(qt):
     assert b.shape == (16, 4 * O.K_BLOCK_BYTES[qt])
     w = O.gguf_k_dequantize(b, qt, 16, 1024)
     assert np.isfinite(w).all() and np.abs(w).max() < 10.0
+
+
+@pytest.mark.parametrize("name,qt", [("q4_k", O.Q4_K), ("q6_k", O.Q6_K)])
+def test_gguf_k_candle_style_linear_near_exact(name, qt):
+    """The CPU QMatMul arithmetic (activations quantised to Q8_K, integer
+    sub-block dots) stays within its activation-rounding error of the exact
+    product: 1e-2 on seeded blocks, 2.5e-2 on the golden edge rows."""
+    g = np.load(GOLDEN_K)
+    N = g[f"{name}_dequant"].shape[0]
+    y = O.gguf_k_linear_candle(g["x"], g[f"{name}_blocks"], qt, N)
+    ref = g[f"{name}_linear_f64"]
+    assert np.abs(y - ref).max() <= 2.5e-2 * np.abs(ref).max()
+    rng = np.random.default_rng(17)
+    blocks = O.gguf_k_random_blocks(rng, qt, 300, 4096)
+    x = rng.normal(0.0, 1.0, (3, 4096)).astype(np.float32)
+    x[1] = 0.0  # an all-zero activation row quantises to d = 0
+    yc = O.gguf_k_linear_candle(x, blocks, qt, 300)
+    ye = O.gguf_k_linear_exact(x, blocks, qt, 300)
+    assert np.abs(yc - ye).max() <= 1e-2 * np.abs(ye).max()
+    assert np.all(yc[1] == 0.0)

@@ -1,7 +1,8 @@
-"""Pipeline schedule on the CPU: world-size 2 and 3 gloo ranks, a stand-in for
-the stage compute, checked against the same chain run in one process.  Also
-the failure path: a rank that never joins makes its peers fail within the
-process-group timeout instead of hanging."""
+"""Pipeline schedule on the CPU: world-size 2, 3 and 4 gloo ranks, a stand-in for
+the stage compute, checked against the same chain run in one process, with
+micro-batches of one and of several sequences, and over a channel that models
+NCCL's blocking link set-up.  Also the failure path: a rank that never joins
+makes its peers fail within the process-group timeout instead of hanging."""
 import os
 import socket
 import sys
@@ -244,13 +245,14 @@ def _rendezvous_worker(rank, world, port, n_mb, R, prompts, steps, result_dir, s
     os._exit(0)  # a stuck peer's transfers may still be posted
 
 
-@pytest.mark.parametrize("skip_connect", [False, True])
-def test_pipeline_link_set_up_cannot_deadlock(skip_connect, tmp_path):
-    """Two stages, micro-batches of 2 sequences, a channel with NCCL's blocking
-    link set-up and bounded send queue: the pipeline finishes and matches the
-    single-process chain; without the set-up exchange it deadlocks in prefill
-    (the last stage waits on the ring's set-up, stage 0 on its full queue)."""
-    world, n_mb, R, steps = 2, 3, 2, 4
+@pytest.mark.parametrize("world,skip_connect", [(2, False), (2, True), (4, False)])
+def test_pipeline_link_set_up_cannot_deadlock(world, skip_connect, tmp_path):
+    """Two (or four) stages, micro-batches of 2 sequences, a channel with NCCL's
+    blocking link set-up and bounded send queue: the pipeline finishes and
+    matches the single-process chain; without the set-up exchange two stages
+    deadlock in prefill (the last stage waits on the ring's set-up, stage 0 on
+    its full queue)."""
+    n_mb, R, steps = max(3, world), 2, 4
     prompts = [[(11 * s + 5 * i + 2) % V for i in range(3)] for s in range(n_mb * R)]
     mp.start_processes(_rendezvous_worker,
                        args=(world, _free_port(), n_mb, R, prompts, steps, str(tmp_path), skip_connect),

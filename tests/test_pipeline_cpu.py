@@ -175,8 +175,12 @@ class RendezvousChannel:
     """TorchChannel with two traits of NCCL on GPUs that gloo lacks.  (1) The
     first transfer on a link returns only once the peer has made its own first
     call on that link (NCCL sets up peer connections on the host that way).
-    (2) A sender's host blocks while `depth` of its sends on a link are not yet
-    received (a stream held up by an unreceived send fills the launch queue)."""
+    (2) On a forward link, a sender's host blocks while `depth` of its sends
+    are not yet received: the prefill makes the compute stream wait on each
+    forward send, so an unreceived send holds the stream and the host's later
+    launches fill its queue.  The ring's token sends are never waited on by the
+    compute stream during prefill (and small NCCL sends finish into the peer's
+    buffer), so they do not block the host."""
 
     def __init__(self, store, rank, world, depth=2, timeout_s=8.0):
         from dial_cuda.pipeline import TorchChannel
@@ -202,10 +206,11 @@ class RendezvousChannel:
     def isend(self, t, dst):
         link = (self.rank, dst)
         self._first(*link)
-        n = self.sent.get(link, 0)
-        key = f"recv{link[0]}-{link[1]}"
-        self._wait_until(lambda: self.store.add(key, 0) > n - self.depth, f"send queue of {link}")
-        self.sent[link] = n + 1
+        if dst == self.rank + 1:
+            n = self.sent.get(link, 0)
+            key = f"recv{link[0]}-{link[1]}"
+            self._wait_until(lambda: self.store.add(key, 0) > n - self.depth, f"send queue of {link}")
+            self.sent[link] = n + 1
         return self.inner.isend(t, dst)
 
     def irecv(self, t, src):
@@ -245,9 +250,9 @@ def _rendezvous_worker(rank, world, port, n_mb, R, prompts, steps, result_dir, s
     os._exit(0)  # a stuck peer's transfers may still be posted
 
 
-@pytest.mark.parametrize("world,skip_connect", [(2, False), (2, True), (4, False)])
+@pytest.mark.parametrize("world,skip_connect", [(2, False), (2, True), (4, False), (8, False)])
 def test_pipeline_link_set_up_cannot_deadlock(world, skip_connect, tmp_path):
-    """Two (or four) stages, micro-batches of 2 sequences, a channel with NCCL's
+    """Two to eight stages, micro-batches of 2 sequences, a channel with NCCL's
     blocking link set-up and bounded send queue: the pipeline finishes and
     matches the single-process chain; without the set-up exchange two stages
     deadlock in prefill (the last stage waits on the ring's set-up, stage 0 on

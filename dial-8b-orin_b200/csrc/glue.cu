@@ -125,16 +125,20 @@ __global__ void qk_rope_kv_kernel(const T* __restrict__ qkv, const T* __restrict
     for (int i = 0; i < 4; ++i)
       v[i] = Act<T>::to_f32(rnd<T>(v[i] * inv * ld(nw, lane + 32 * i)));  // normed tensor in T
   }
-  // rotate_half: out[i] = x[i] c_i - x[i+64] s_i ; out[i+64] = x[i+64] c_i + x[i] s_i
+  // rotate_half: out[i] = x[i] c_i - x[i+64] s_i ; out[i+64] = x[i] s_i + x[i+64] c_i,
+  // every product and the sum in T as candle's rope evaluates them over T
+  // tensors (a product of two T values is exact in f32, so rounding it to T is
+  // the T multiplication)
   const T* cr = cos_t + (int64_t)p * (D / 2);
   const T* sr = sin_t + (int64_t)p * (D / 2);
+  auto r = [](float a) { return Act<T>::to_f32(rnd<T>(a)); };
   float o[4];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int e = lane + 32 * i;  // 0..63
     const float c = ld(cr, e), sn = ld(sr, e);
-    o[i] = v[i] * c - v[i + 2] * sn;
-    o[i + 2] = v[i + 2] * c + v[i] * sn;
+    o[i] = r(v[i] * c) - r(v[i + 2] * sn);
+    o[i + 2] = r(v[i] * sn) + r(v[i + 2] * c);
   }
   T* dst = is_q ? q_out + (t * hq + h) * D : kc + ((s * hkv + (h - hq)) * max_seq + p) * D;
 #pragma unroll
@@ -145,9 +149,11 @@ __global__ void qk_rope_kv_kernel(const T* __restrict__ qkv, const T* __restrict
 // Query token t attends cache rows 0..pos[t] of slot[t] (decode: one token per
 // sequence; prefill: a run of tokens of one sequence, causal through pos).
 // CTA = (token, kv head, key split); the n_rep query heads of the group share
-// every K/V row.  Scores are in the log2 domain (log2(e)/sqrt(D) applied to the
-// f32 dot products), softmax and accumulation in f32; splits are merged by the
-// combine step.
+// every K/V row.  Scores follow the reference's T tensors (text.rs:1278-1279):
+// s = T(T(q.k) * T(1/sqrt(D))) -- the matmul's output in T, then the affine
+// `/ sqrt(D)` with its multiplier in T -- and enter the softmax in the log2
+// domain (times log2(e) in f32); softmax and accumulation in f32; splits are
+// merged by the combine step.
 template <typename T>
 __global__ void attention_combine_kernel(const float* __restrict__ part, T* __restrict__ out,
                                          int nchunks) {
@@ -243,6 +249,18 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
        ((uint32_t)(*reinterpret_cast<const uint16_t*>(&lb)) << 16);
 }
 
+// (a, b) -> three operand pairs: hi, what hi left behind, and what that left
+// (bf16: 8 + 8 + 8 significant bits, the f32 value in the normal range)
+template <typename T>
+__device__ __forceinline__ void split_pair3(float a, float b, uint32_t& hi, uint32_t& mid,
+                                            uint32_t& lo) {
+  const T ha = Act<T>::from_f32(a), hb = Act<T>::from_f32(b);
+  const float ra = a - Act<T>::to_f32(ha), rb = b - Act<T>::to_f32(hb);
+  split_pair<T>(ra, rb, mid, lo);
+  hi = (uint32_t)(*reinterpret_cast<const uint16_t*>(&ha)) |
+       ((uint32_t)(*reinterpret_cast<const uint16_t*>(&hb)) << 16);
+}
+
 template <typename T, int REP>
 __global__ void __launch_bounds__(kTcWarps * 32)
     attention_tc_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
@@ -320,7 +338,11 @@ __global__ void __launch_bounds__(kTcWarps * 32)
     }
     // ---- online softmax on row gr: this lane holds keys 2qd, 2qd+1, 8+2qd, 9+2qd
     const int kb = k0 + i * kTcTile;
-    float p[4] = {sc[0][0] * qscale, sc[0][1] * qscale, sc[1][0] * qscale, sc[1][1] * qscale};
+    auto score = [&](float a) {  // T(T(a) * T(1/sqrt(D))) * log2(e)
+      return Act<T>::to_f32(Act<T>::from_f32(Act<T>::to_f32(Act<T>::from_f32(a)) * qscale)) *
+             1.4426950408889634f;
+    };
+    float p[4] = {score(sc[0][0]), score(sc[0][1]), score(sc[1][0]), score(sc[1][1])};
     const int kk[4] = {2 * qd, 2 * qd + 1, 8 + 2 * qd, 9 + 2 * qd};
     float mx = -FLT_MAX;
 #pragma unroll
@@ -345,9 +367,18 @@ __global__ void __launch_bounds__(kTcWarps * 32)
       o[nt][0] *= corr;
       o[nt][1] *= corr;
     }
-    uint32_t ph0, pl0, ph1, pl1;
-    split_pair<T>(p[0], p[1], ph0, pl0);
-    split_pair<T>(p[2], p[3], ph1, pl1);
+    // P as operand parts: f16 hi + lo keeps 22 significant bits; bf16 takes a
+    // third part (24 bits), as two bf16 parts (16 bits) would round P far more
+    // coarsely than the f32 accumulation does
+    constexpr bool kThree = !std::is_same<T, __half>::value;
+    uint32_t ph0, pl0, ph1, pl1, pm0 = 0u, pm1 = 0u;
+    if constexpr (kThree) {
+      split_pair3<T>(p[0], p[1], ph0, pm0, pl0);
+      split_pair3<T>(p[2], p[3], ph1, pm1, pl1);
+    } else {
+      split_pair<T>(p[0], p[1], ph0, pl0);
+      split_pair<T>(p[2], p[3], ph1, pl1);
+    }
     // ---- O += P V over 16 dim n-tiles
 #pragma unroll
     for (int nt = 0; nt < 16; nt += 2) {
@@ -355,8 +386,10 @@ __global__ void __launch_bounds__(kTcWarps * 32)
       ldsm_x4_t(vt + tc_swz((mi & 1) * 8 + ri, nt + (mi >> 1)), b0, b1, b2, b3);
       mma_tc<T>(o[nt], ph0, 0u, ph1, 0u, b0, b1);
       mma_tc<T>(o[nt], pl0, 0u, pl1, 0u, b0, b1);
+      if constexpr (kThree) mma_tc<T>(o[nt], pm0, 0u, pm1, 0u, b0, b1);
       mma_tc<T>(o[nt + 1], ph0, 0u, ph1, 0u, b2, b3);
       mma_tc<T>(o[nt + 1], pl0, 0u, pl1, 0u, b2, b3);
+      if constexpr (kThree) mma_tc<T>(o[nt + 1], pm0, 0u, pm1, 0u, b2, b3);
     }
     __syncwarp();  // every lane is done with this stage before it is refilled
     st ^= 1;
@@ -621,7 +654,8 @@ dial_status launch_attention(const void* q, const void* kc, const void* vc, cons
                              int64_t tokens, int hq, int hkv, int64_t max_seq, int64_t max_len,
                              cudaStream_t st) {
   const int nch = attention_splits(tokens, hkv, max_len);
-  const float qscale = 1.4426950408889634f / sqrtf(128.0f);  // log2(e) / sqrt(D)
+  // T(1/sqrt(128)): 0x1.6a0p-4 = 0.08837890625 in both f16 and bf16
+  const float qscale = 0.08837890625f;
   dim3 grid((unsigned)tokens, (unsigned)hkv, (unsigned)nch);
   const int rep = hq / hkv;
   dial_status s = DIAL_OK;

@@ -13,18 +13,27 @@
 //  * K <= kNoAllocMaxK (16384); larger K is rejected with DIAL_ERR_SHAPE.  Any
 //    M is accepted and processed 32 activation rows per pass, always on the
 //    integer (Q8_0-activation) path, passes running one after another on the
-//    caller's stream.
+//    caller's stream.  The GEMV is the in-CTA K-split kernel
+//    (gguf_skinny_kernel: plain 16-byte loads, the K groups of a tile split
+//    over a CTA's warps and reduced in shared memory), not the TMA-fed
+//    stream-K kernel dial_gguf_linear runs: that one needs a workspace for its
+//    split-tile partials.  Same arithmetic, so the outputs agree within the
+//    integer path's tolerance; its speed is not tuned.
 //  * The array (640 KiB) lives on every GPU that loads the library until the
 //    process exits.
 //  * The first call on a device looks up the array's device address with
-//    cudaGetSymbolAddress (with that device current) and caches it; make that
-//    first call before any stream capture on that device.
+//    cudaGetSymbolAddress (with that device current) and caches it with the
+//    device's current context; make that first call before any stream capture
+//    on that device.  After cudaDeviceReset the context differs, and the next
+//    call looks the address up again (again outside a capture).
 //  * Every call shares the one array.  Calls whose kernels overlap on the GPU
 //    (different streams, or different host threads, without ordering between
 //    them) race on it and give wrong results; order them on one stream.
 //  * The array keeps the last call's contents.  Nothing in it has to start at
 //    zero: each pass writes every quantised activation and block scale it later
 //    reads.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -44,19 +53,42 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
 std::mutex g_mu;
 void* g_scratch_ptr[64] = {nullptr};
+CUcontext g_scratch_ctx[64] = {nullptr};  // the context each cached address belongs to
 
-// Device address of g_noalloc_scratch for the current device (set-up on first use).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry point (no -lcuda).
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
+
+// Device address of g_noalloc_scratch for the current device (set-up on the
+// first use in the device's current context).
 dial_status scratch_for_current_device(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(DIAL_ERR_INVALID_ARG, "device ordinal %d out of range", dev);
+  CtxGetCurrentFn get = ctx_get_current();
+  if (!get) return fail(DIAL_ERR_CUDA, "cuCtxGetCurrent is unavailable");
+  CUcontext ctx = nullptr;  // null until the runtime has made a context current on this thread
+  if (get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_scratch_ptr[dev]) {
+  if (!g_scratch_ptr[dev] || !ctx || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // sets up the primary context if needed
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    if (get(&ctx) != CUDA_SUCCESS || !ctx) return fail(DIAL_ERR_CUDA, "no current CUDA context");
     g_scratch_ptr[dev] = p;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_ptr[dev];
   return DIAL_OK;

@@ -472,13 +472,19 @@ __device__ __forceinline__ void ring_init(const Ring& ring) {
 }
 
 // Orders lane 0's next TMA write into a stage after every lane's shared-memory
-// reads of it: each lane first consumes `dep`, a value computed from its own
-// loaded registers (so its loads have returned), then the warp synchronises.
-// Lane 0's registers alone would not do: the warp's lanes need not execute the
-// loads together.
+// reads of it: each lane first consumes `dep`, a value folded from every word
+// it loaded from the stage (so all of its loads have returned), the warp
+// synchronises, and a proxy fence orders those generic-proxy reads before the
+// async-proxy (TMA) write that follows.  Lane 0's registers alone would not
+// do: the warp's lanes need not execute the loads together.  Without the full
+// fold and the fence, a refill overwrote a stage that some lane had not
+// finished reading (wrong partial sums in about one tile per call at M = 8).
+__device__ __forceinline__ uint32_t fold(const uint4& v) { return v.x ^ v.y ^ v.z ^ v.w; }
+__device__ __forceinline__ uint32_t fold(const uint2& v) { return v.x ^ v.y; }
 __device__ __forceinline__ void stage_reads_done(uint32_t dep) {
   asm volatile("" ::"r"(dep) : "memory");
   __syncwarp();
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -619,19 +625,15 @@ __device__ __forceinline__ void tile_finish(const GemvPlan& pl, float* __restric
 // lane then reads its fragments from there instead of from L1/L2 on each unit.
 //
 // Staged activations are f16 whatever the input dtype, and the weights enter
-// the f16 MMA biased: 1152 + q, built from the byte by one byte permute under
-// the f16 exponent of 1024 (plus one xor per 4 bytes), without the subtraction
-// of the exact conversion.  Per row, sum_k (1152 + q_k) x_k - 1152 sum_k x_k is
-// the wanted sum_k q_k x_k; the second term is one more MMA per k-step with
-// every weight -1152 (exact in f16), so no sums of x are staged.  Every
-// (1152 + q) x and 1152 x product is exact in f32, as the plain products are;
-// the accumulation runs at a larger magnitude, a relative change of about
-// 1e-5 of the result, below the f16/bf16 rounding of the output.  bf16 inputs
-// are scaled per token by a power of two that puts max|x| in [2^13, 2^14) and
-// rounded to f16 (exact for every value within 2^27 of the max); the output
-// is scaled back by the same power of two.  f16 inputs are staged unscaled.
+// the f16 MMA exactly converted (i8x4_to_f16x2).  bf16 inputs are scaled per
+// token by a power of two that puts max|x| in [2^13, 2^14) and rounded to f16
+// (exact for every value within 2^27 of the max); the output is scaled back by
+// the same power of two.  f16 inputs are staged unscaled.  (Feeding the MMA
+// biased weights 1152 + q and subtracting 1152 sum x with a second MMA saves
+// the two subtractions per 4 weights, but the tensor cores accumulate the
+// 40x larger biased sums inexactly: 10-15% of f16 outputs came out one ulp
+// off, against 0.2% with exact weights.)
 constexpr int kXsBytes = 32 * 1024;
-constexpr uint32_t kNegBiasF16x2 = 0xE480E480u;  // (-1152, -1152) in f16
 
 // Barrier 1 over the first `threads` threads of the CTA (the warps with work).
 __device__ __forceinline__ void active_warps_sync(int threads) {
@@ -719,12 +721,6 @@ __device__ __forceinline__ void cta_tile_finish(uint32_t part, uint32_t ctr, int
   store(tile, sum);
 }
 
-// Four int8 -> two f16x2 holding 1152 + q (exact).
-__device__ __forceinline__ void i8x4_to_f16x2_biased(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  lo = prmt(u, 0x64646464u, 0x4140u);
-  hi = prmt(u, 0x64646464u, 0x4342u);
-}
 
 // Power-of-two exponent e with 2^13 <= max|x| * 2^-e < 2^14 (0 for a zero or
 // non-finite max): every bf16 value within 2^27 of the row's max is then an f16
@@ -958,24 +954,13 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     xr[j] = x + (size_t)(tv[j] ? tok : 0) * K + 32 * t;
     xo[j] = xsm + (uint32_t)(((tv[j] ? tok : 0) * K + 32 * t) * 2);
   }
-  // acc: the weight MMAs; accb: the bias MMAs (XS), a second dependency chain
-  // that interleaves with the first (added to acc when a tile part ends)
-  constexpr bool kBiasChain = XS && NT <= 2;
-  float acc[NT][4], accb[kBiasChain ? NT : 1][4];
+  float acc[NT][4];
   zero_acc(acc);
-  zero_acc(accb);
   const int first_tile = (int)div_u((uint64_t)ubegin(pl, w), (uint64_t)pl.ng);
   int cur = -1, units = 0, lt = 0;
   const uint4 z = make_uint4(0, 0, 0, 0);
   const uint32_t part = xsm + kXsBytes + kAuxCs, ctr = xsm + kXsBytes + kAuxCnt;
   auto finish = [&](int tile) {  // the end of this warp's part of `tile`
-    if (kBiasChain) {
-#pragma unroll
-      for (int j = 0; j < (kBiasChain ? NT : 1); ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][e] += accb[j][e];
-      zero_acc(accb);
-    }
     if (XS && NT <= 2 && pl.mode == kTileCta) cta_tile_finish<NT>(part, ctr, lt++, tile, acc, store, err);
     else tile_finish<NT>(pl, slots, cnt, w, first_tile, tile, units, acc, store);
   };
@@ -1016,7 +1001,7 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     const uint32_t buf = ring.w + (uint32_t)(s * kUnitBytes);
     const uint4 al0 = lds16(sw128(buf, g, 2 * t)), al1 = lds16(sw128(buf, g, 2 * t + 1));
     const uint4 ah0 = lds16(sw128(buf, g + 8, 2 * t)), ah1 = lds16(sw128(buf, g + 8, 2 * t + 1));
-    stage_reads_done(al0.x ^ al1.x ^ ah0.x ^ ah1.x ^ info.x);
+    stage_reads_done(fold(al0) ^ fold(al1) ^ fold(ah0) ^ fold(ah1) ^ fold(info));
     if (lane == 0) pr.refill(ring, load);  // the stage's bytes are in registers: refill it
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -1025,8 +1010,8 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
         const uint32_t wl = word(h ? al1 : al0, st), wh = word(h ? ah1 : ah0, st);
         uint32_t a0, a1, a2, a3;
         if (XS) {
-          i8x4_to_f16x2_biased(wl, a0, a2);
-          i8x4_to_f16x2_biased(wh, a1, a3);
+          i8x4_to_f16x2(wl, a0, a2);
+          i8x4_to_f16x2(wh, a1, a3);
         } else if (BF16) {
           i8x4_to_bf16x2(wl, a0, a2);
           i8x4_to_bf16x2(wh, a1, a3);
@@ -1040,9 +1025,6 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
           const uint32_t b0 = word(xs, 2 * (st & 1)), b1 = word(xs, 2 * (st & 1) + 1);
           if (kF16Mma) mma_f16(acc[j], a0, a1, a2, a3, b0, b1);
           else mma_bf16(acc[j], a0, a1, a2, a3, b0, b1);
-          if (XS)  // minus 1152 x: the weights' bias
-            mma_f16(kBiasChain ? accb[kBiasChain ? j : 0] : acc[j], kNegBiasF16x2, kNegBiasF16x2,
-                    kNegBiasF16x2, kNegBiasF16x2, b0, b1);
         }
       }
     }
@@ -1129,7 +1111,8 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     }
     const uint32_t dbuf = ring.d + (uint32_t)(s * kDBytes);
     const uint2 dl = lds8(dbuf + (uint32_t)(g * 8)), dh = lds8(dbuf + (uint32_t)((g + 8) * 8));
-    stage_reads_done(wl[0].x ^ wl[1].x ^ wh[0].x ^ wh[1].x ^ dl.x ^ dh.x ^ info.x);
+    stage_reads_done(fold(wl[0]) ^ fold(wl[1]) ^ fold(wh[0]) ^ fold(wh[1]) ^ fold(dl) ^ fold(dh) ^
+                     fold(info));
     if (lane == 0) pr.refill(ring, load);  // the stage's bytes are in registers: refill it
     const float dlv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dl.x)),
                           __high2float(*reinterpret_cast<const __half2*>(&dl.x)),

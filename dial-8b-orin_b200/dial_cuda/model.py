@@ -138,6 +138,8 @@ class Stage:
         self._keep = []
         self.layers = []
         self.linears = []
+        self.layer_linears = []  # per layer: {"qkv", "o", "gate_up", "down"} -> _Linear
+        self.layer_norms = []    # per layer: {"input_norm", "post_norm", "q_norm", "k_norm"}
         gen = torch.Generator(device=self.device)
 
         def rand(shape, *key, std=None):
@@ -173,6 +175,8 @@ class Stage:
             self.v_caches.append(vc)
             self._keep += [lin, norms]
             self.linears += list(lin.values())
+            self.layer_linears.append(lin)
+            self.layer_norms.append(norms)
             arr[i] = LayerWeights(lin["qkv"].ref, lin["o"].ref, lin["gate_up"].ref, lin["down"].ref,
                                   norms["input_norm"].data_ptr(), norms["post_norm"].data_ptr(),
                                   norms["q_norm"].data_ptr(), norms["k_norm"].data_ptr(),

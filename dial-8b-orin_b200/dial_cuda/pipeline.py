@@ -206,6 +206,7 @@ class Pipeline:
         self.t = 0  # decode steps since the last prefill
         self.host_io = None  # (host_in, host_out): pinned int32 token copies for host_io steps
         self._connected = False  # decode-sized transfers made on every link (_connect)
+        self._prefill_connected = set()  # prompt lengths whose hand-off sizes were exchanged
 
     def _wait_send(self, b):
         if self.pending[b] is not None:
@@ -312,9 +313,12 @@ class Pipeline:
         R = getattr(c, "mb_size", 1)
         T = len(prompts[0]) if prompts is not None else prompt_len
         buf = c.prefill_buffer(T)
-        if P > 1:
+        if P > 1 and T not in self._prefill_connected:
+            # once per hand-off size: NCCL may open further connections for a
+            # larger message the first time one crosses a link
             self._connect(buf, c.token_buffer(0).clone())
             self._connect_steps()
+            self._prefill_connected.add(T)
         for b in range(B):
             for i in range(R):
                 if r > 0:

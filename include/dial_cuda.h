@@ -168,10 +168,12 @@ DIAL_API dial_status dial_gguf_linear(const void* x, dial_dtype xdt, const void*
  * with no device allocator.  No counterpart in the reference: its scratch
  * lives in a fixed 640 KiB __device__ array inside this library instead of a
  * caller workspace, so the call allocates nothing.  K <= 16384 (larger K
- * returns DIAL_ERR_SHAPE); any M, 32 rows per pass.  The first call on a
- * device looks up the array's address (make it before any stream capture).
- * All calls share the array: calls that overlap on the GPU race on it, so
- * order them on one stream. */
+ * returns DIAL_ERR_SHAPE); any M, 32 rows per pass, on the in-CTA K-split GEMV
+ * (plain loads; not the TMA stream-K kernel of dial_gguf_linear, which needs
+ * the workspace; speed not tuned).  The first call on a device looks up the
+ * array's address (make it before any stream capture); after cudaDeviceReset
+ * the next call looks it up again.  All calls share the array: calls that
+ * overlap on the GPU race on it, so order them on one stream. */
 DIAL_API dial_status dial_gguf_linear_noalloc(const void* x, dial_dtype xdt, const void* qs,
                                               const uint16_t* d, dial_ggml_type type, void* y,
                                               int64_t M, int64_t K, int64_t N, dial_stream stream);

@@ -71,6 +71,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_rope_tables": ([vp, vp, i64, i32, f32], None),
         "orc_decoder_generate": ([ctypes.POINTER(OrcDecoder), ctypes.POINTER(ctypes.c_void_p), vp, vp,
                                   vp, vp, vp, i32, i32, vp, vp], i32),
+        "orc_decoder_run": ([ctypes.POINTER(OrcDecoder), ctypes.POINTER(ctypes.c_void_p), vp, vp,
+                             vp, vp, vp, i32, i32, vp, vp, vp, vp, vp], i32),
     })
     for name, (argtypes, restype) in sig.items():
         fn = getattr(L, name)
@@ -82,7 +84,8 @@ class OrcDecoder(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int32), ("hidden", ctypes.c_int32), ("inter", ctypes.c_int32),
                 ("n_heads", ctypes.c_int32), ("n_kv", ctypes.c_int32), ("head_dim", ctypes.c_int32),
                 ("vocab", ctypes.c_int32), ("qk_norm", ctypes.c_int32), ("eps", ctypes.c_float),
-                ("theta", ctypes.c_float)]
+                ("theta", ctypes.c_float), ("act_dtype", ctypes.c_int32),
+                ("weight_format", ctypes.c_int32), ("head_format", ctypes.c_int32)]
 
 
 def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float, res: np.ndarray | None = None):
@@ -105,33 +108,57 @@ def rope_tables(max_pos: int, head_dim: int, theta: float):
 
 
 def decoder_generate(cfg: dict, layers: list, embed: np.ndarray, final_norm: np.ndarray,
-                     head_q: np.ndarray, head_s: np.ndarray, prompt, n_new: int):
-    """Greedy generation on the oracle decoder (W8A16 weights, f16 activations).
+                     head_q: np.ndarray, head_s, prompt, n_new: int, act_dtype: int = F16,
+                     weight_format: int = 0, head_format: int = 0, forced=None,
+                     return_logits: bool = False, return_hidden: bool = False):
+    """Greedy generation on the oracle decoder.
 
-    layers: list of dicts with int8 `qkv_q, o_q, gu_q, down_q`, f32 `*_s` and f16
-    `input_norm, post_norm, q_norm, k_norm`.  Returns (tokens, top1-top2 margins)."""
+    act_dtype F16 or BF16: `embed`, the norms and every activation are 16-bit
+    patterns of that type (numpy float16, or uint16 holding bf16 bits).
+    weight_format / head_format: 0 W8A16 with f32 scales, 1 W8A16 with f16
+    scales, Q4_0 or Q8_0 (native GGML blocks [N, K/32 * block bytes], `*_s`
+    None).  layers: list of dicts with `qkv_q, o_q, gu_q, down_q` (int8 or
+    blocks), `*_s` (scales or None) and `input_norm, post_norm, q_norm, k_norm`
+    (the QK norms may be None when cfg["qk_norm"] is false).
+    forced: optional [n_new] tokens fed back instead of the argmax (teacher forcing).
+    Returns (tokens, top1-top2 margins of the rounded logits), plus the
+    [n_new, vocab] f32 logits with return_logits and the [n_new, hidden] bits of
+    the last position's residual stream before the final norm with
+    return_hidden."""
     keys = ["qkv_q", "qkv_s", "o_q", "o_s", "gu_q", "gu_s", "down_q", "down_s", "input_norm",
             "post_norm", "q_norm", "k_norm"]
     keep = []
     ptrs = (ctypes.c_void_p * (len(layers) * len(keys)))()
     for i, L in enumerate(layers):
         for j, k in enumerate(keys):
+            if L.get(k) is None:
+                ptrs[i * len(keys) + j] = None
+                continue
             a = np.ascontiguousarray(L[k])
             keep.append(a)
             ptrs[i * len(keys) + j] = a.ctypes.data
     d = OrcDecoder(cfg["n_layers"], cfg["hidden"], cfg["inter"], cfg["n_heads"], cfg["n_kv"],
-                   cfg["head_dim"], cfg["vocab"], int(cfg["qk_norm"]), cfg["eps"], cfg["theta"])
+                   cfg["head_dim"], cfg["vocab"], int(cfg["qk_norm"]), cfg["eps"], cfg["theta"],
+                   act_dtype, weight_format, head_format)
     prompt = np.ascontiguousarray(prompt, np.int32)
     toks = np.empty(n_new, np.int32)
     margins = np.empty(n_new, np.float32)
-    embed = np.ascontiguousarray(embed, np.float16)
-    rc = lib().orc_decoder_generate(ctypes.byref(d), ptrs, _p(embed),
-                                    _p(np.ascontiguousarray(final_norm, np.float16)),
-                                    _p(np.ascontiguousarray(head_q, np.int8)),
-                                    _p(np.ascontiguousarray(head_s, np.float32)), _p(prompt),
-                                    len(prompt), n_new, _p(toks), _p(margins))
-    assert rc == 0
-    return toks, margins
+    bits = lambda a: np.ascontiguousarray(a).view(np.uint16)
+    head_q = np.ascontiguousarray(head_q)
+    head_s = None if head_s is None else np.ascontiguousarray(head_s)
+    fz = None if forced is None else np.ascontiguousarray(forced, np.int32)
+    logits = np.empty((n_new, cfg["vocab"]), np.float32) if return_logits else None
+    hidden = np.empty((n_new, cfg["hidden"]), np.uint16) if return_hidden else None
+    rc = lib().orc_decoder_run(ctypes.byref(d), ptrs, _p(bits(embed)), _p(bits(final_norm)),
+                               _p(head_q), _p(head_s), _p(prompt), len(prompt), n_new, _p(fz),
+                               _p(toks), _p(margins), _p(logits), _p(hidden))
+    assert rc == 0, "orc_decoder_run rejected its configuration"
+    out = (toks, margins)
+    if return_logits:
+        out += (logits,)
+    if return_hidden:
+        out += (hidden,)
+    return out
 
 
 def _p(a: np.ndarray | None):

@@ -617,129 +617,232 @@ ORC_API int orc_q8_0_quantize_rows(const void* x, int xdt, int64_t M, int64_t K,
 }
 
 /* ------------------------------------------------------------------------ */
-/* Decoder glue and a whole decoder (greedy), W8A16 weights, f16 activations */
-/* Order and rounding points follow the reference's f16 tensors:            */
-/*   text.rs:1636-1688 (Transformer::forward: rms_1, attn + residual, rms_2, */
-/*   mlp + residual), text.rs:1478-1596 (QKV -> QK RMSNorm -> RoPE -> KV ->   */
-/*   GQA attention -> O), text.rs:816-820 (silu(gate) * up),                  */
-/*   llama3/cache.rs:24-64 (RoPE tables in f32, stored as f16),              */
-/*   qwen3_vl.rs:2420-2451 (ln_f -> last position -> lm_head), :130-143       */
-/*   (argmax).  Accumulations are done in double.                            */
+/* Decoder glue and a whole greedy decoder (f16 or bf16 activations; W8A16   */
+/* or GGUF Q4_0 / Q8_0 layers; W8A16 or Q8_0 output head).                    */
+/*                                                                          */
+/* Order (text.rs:1636-1688 Transformer::forward: rms_1, attention +        */
+/* residual, rms_2, MLP + residual; text.rs:1478-1596 QwenAttention: QKV ->  */
+/* QK RMSNorm -> RoPE -> KV -> GQA attention -> O; llama3/attention.rs:41-157 */
+/* the same without QK-norm; text.rs:816-820 and llama3/mlp.rs:15-21         */
+/* silu(gate) * up; qwen3_vl.rs:2420-2451 ln_f -> last position -> lm_head;  */
+/* qwen3_vl.rs:130-143 argmax, first index of the maximum).                  */
+/*                                                                          */
+/* Rounding points.  Every tensor a candle op produces is in the model dtype */
+/* T (f16; bf16 as an extension), so each op's result is rounded to T once,  */
+/* with the op's inner arithmetic in f32 (sums in double here):              */
+/*   RMSNorm     T(h * 1/sqrt(mean(h^2) + eps) * w)                           */
+/*   residual    T(a + b)                                                   */
+/*   RoPE        candle rotary_emb::rope evaluates x1*c - x2*s and          */
+/*               x1*s + x2*c in T (text.rs:1143-1153 with T tables,          */
+/*               llama3/cache.rs:49-50): each product and the sum rounded    */
+/*   attention   q.k^T is a T matmul, `/ sqrt(D)` an affine op whose          */
+/*               multiplier is T(1/sqrt(D)) (text.rs:1278, :1305,            */
+/*               llama3/attention.rs:125):  s = T(T(q.k) * T(1/sqrt(D)));    */
+/*               softmax over the causal keys; o = T(sum_j p_j v_j)          */
+/*               (text.rs:1279-1280).  The reference's probability tensor is */
+/*               T as well; here p stays unrounded, like the CUDA kernel's   */
+/*               single-pass softmax that never holds normalised             */
+/*               probabilities (2^-11 relative per probability in f16).      */
+/*   SwiGLU      T(T(silu(g)) * u)                                          */
+/* Linears:                                                                  */
+/*   W8A16       T(f32(sum q x) * scale)         (worker_w8a16.rs:158-181)  */
+/*   GGUF        the worker's hybrid route (worker_gguf_prefill_for_dims     */
+/*               worker_gguf.rs:399-421): a run of more than one position    */
+/*               multiplies by the dequantised copy T(d q)                   */
+/*               (build_worker_gguf_fp16_prefill_linear :423-449); a single  */
+/*               position runs QMatMul (forward_worker_gguf :574-611), whose */
+/*               CPU arithmetic is orc_gguf_linear_candle's (activations     */
+/*               quantised to Q8_0, integer block dots, f32 block scaling).  */
+/*               The output head sees one position: QMatMul.                 */
 /* ------------------------------------------------------------------------ */
 
-static inline float hr(float v) { return h2f(f2h(v)); } /* round through f16 */
+static inline float rnd_dt(float v, int dt) { return dt == ORC_BF16 ? bf2f(f2bf(v)) : h2f(f2h(v)); }
+static inline uint16_t enc_dt(float v, int dt) { return dt == ORC_BF16 ? f2bf(v) : f2h(v); }
+static inline float dec_dt(uint16_t b, int dt) { return dt == ORC_BF16 ? bf2f(b) : h2f(b); }
 
-/* y = f16(h * (1/sqrt(mean(h^2)+eps)) * w), h = f16(x + res) when res != NULL */
-ORC_API void orc_rmsnorm(const uint16_t* x, const uint16_t* res, uint16_t* h_out,
-                         const uint16_t* w, uint16_t* y, int64_t rows, int64_t dim, float eps) {
+/* weight formats: the codes of include/dial_cuda.h (dial_weight_format) */
+enum { ORC_WFMT_W8A16 = 0, ORC_WFMT_W8A16_F16S = 1 };
+
+/* y = T(h * (1/sqrt(mean(h^2)+eps)) * w), h = T(x + res) when res != NULL */
+static void rmsnorm_dt(const uint16_t* x, const uint16_t* res, uint16_t* h_out, const uint16_t* w,
+                       uint16_t* y, int64_t rows, int64_t dim, float eps, int dt) {
   float* h = (float*)malloc(sizeof(float) * (size_t)dim);
   for (int64_t r = 0; r < rows; ++r) {
     double ss = 0.0;
     for (int64_t i = 0; i < dim; ++i) {
-      float v = h2f(x[r * dim + i]);
-      if (res) v = hr(v + h2f(res[r * dim + i]));
+      float v = dec_dt(x[r * dim + i], dt);
+      if (res) v = rnd_dt(v + dec_dt(res[r * dim + i], dt), dt);
       h[i] = v;
       ss += (double)v * v;
     }
     const float inv = (float)(1.0 / sqrt(ss / (double)dim + (double)eps));
     for (int64_t i = 0; i < dim; ++i) {
-      if (h_out) h_out[r * dim + i] = f2h(h[i]);
-      y[r * dim + i] = f2h(h[i] * inv * h2f(w[i]));
+      if (h_out) h_out[r * dim + i] = enc_dt(h[i], dt);
+      y[r * dim + i] = enc_dt(h[i] * inv * dec_dt(w[i], dt), dt);
     }
   }
   free(h);
 }
 
-/* cos/sin [max_pos, D/2] as f16: inv_freq = 1/theta^(2i/D) (f32), angle = p*inv_freq */
-ORC_API void orc_rope_tables(uint16_t* cos_t, uint16_t* sin_t, int64_t max_pos, int D,
-                             float theta) {
+ORC_API void orc_rmsnorm(const uint16_t* x, const uint16_t* res, uint16_t* h_out,
+                         const uint16_t* w, uint16_t* y, int64_t rows, int64_t dim, float eps) {
+  rmsnorm_dt(x, res, h_out, w, y, rows, dim, eps, ORC_F16);
+}
+
+/* cos/sin [max_pos, D/2] in T: inv_freq = 1/theta^(2i/D) (f32), angle = p*inv_freq
+ * (llama3/cache.rs:31-50) */
+static void rope_tables_dt(uint16_t* cos_t, uint16_t* sin_t, int64_t max_pos, int D, float theta,
+                           int dt) {
   for (int64_t p = 0; p < max_pos; ++p)
     for (int i = 0; i < D / 2; ++i) {
       const float inv = 1.0f / powf(theta, (float)(2 * i) / (float)D);
       const float a = (float)p * inv;
-      cos_t[p * (D / 2) + i] = f2h(cosf(a));
-      sin_t[p * (D / 2) + i] = f2h(sinf(a));
+      cos_t[p * (D / 2) + i] = enc_dt(cosf(a), dt);
+      sin_t[p * (D / 2) + i] = enc_dt(sinf(a), dt);
     }
 }
 
-/* one head (D values, f16 bits in/out): optional RMSNorm then RoPE at position p */
+ORC_API void orc_rope_tables(uint16_t* cos_t, uint16_t* sin_t, int64_t max_pos, int D,
+                             float theta) {
+  rope_tables_dt(cos_t, sin_t, max_pos, D, theta, ORC_F16);
+}
+
+/* One head of D values: optional RMSNorm over the head, then RoPE at position p
+ * with every product and sum rounded to T (candle rotary_emb::rope). */
 static void head_norm_rope(const uint16_t* src, const uint16_t* nw, int qk_norm, float eps,
-                           const uint16_t* cos_t, const uint16_t* sin_t, int p, int D,
+                           const uint16_t* cos_t, const uint16_t* sin_t, int p, int D, int dt,
                            uint16_t* dst) {
   float v[256];
   double ss = 0.0;
-  for (int i = 0; i < D; ++i) { v[i] = h2f(src[i]); ss += (double)v[i] * v[i]; }
+  for (int i = 0; i < D; ++i) { v[i] = dec_dt(src[i], dt); ss += (double)v[i] * v[i]; }
   if (qk_norm) {
     const float inv = (float)(1.0 / sqrt(ss / (double)D + (double)eps));
-    for (int i = 0; i < D; ++i) v[i] = hr(v[i] * inv * h2f(nw[i]));
+    for (int i = 0; i < D; ++i) v[i] = rnd_dt(v[i] * inv * dec_dt(nw[i], dt), dt);
   }
   const int half = D / 2;
   for (int i = 0; i < half; ++i) {
-    const float c = h2f(cos_t[(int64_t)p * half + i]), s = h2f(sin_t[(int64_t)p * half + i]);
-    dst[i] = f2h(v[i] * c - v[i + half] * s);
-    dst[i + half] = f2h(v[i + half] * c + v[i] * s);
+    const float c = dec_dt(cos_t[(int64_t)p * half + i], dt), s = dec_dt(sin_t[(int64_t)p * half + i], dt);
+    const float x1 = v[i], x2 = v[i + half];
+    dst[i] = enc_dt(rnd_dt(x1 * c, dt) - rnd_dt(x2 * s, dt), dt);
+    dst[i + half] = enc_dt(rnd_dt(x1 * s, dt) + rnd_dt(x2 * c, dt), dt);
   }
 }
 
-/* attention of one query head over cache rows 0..len-1 (f16 K/V [max_seq][D]) */
-static void attend(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int len, int D,
+/* Attention of one query head over cache rows 0..len-1 (T K/V [max_seq][D]). */
+static void attend(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int len, int D, int dt,
                    uint16_t* out) {
   double* sc = (double*)malloc(sizeof(double) * (size_t)len);
-  const double scale = 1.0 / sqrt((double)D);
+  const float mul = rnd_dt((float)(1.0 / sqrt((double)D)), dt);
   double mx = -1e300;
   for (int j = 0; j < len; ++j) {
     double s = 0.0;
-    for (int d = 0; d < D; ++d) s += (double)h2f(q[d]) * h2f(kc[(int64_t)j * D + d]);
-    sc[j] = s * scale;
+    for (int d = 0; d < D; ++d) s += (double)dec_dt(q[d], dt) * dec_dt(kc[(int64_t)j * D + d], dt);
+    sc[j] = (double)rnd_dt(rnd_dt((float)s, dt) * mul, dt);
     if (sc[j] > mx) mx = sc[j];
   }
   double sum = 0.0;
   for (int j = 0; j < len; ++j) { sc[j] = exp(sc[j] - mx); sum += sc[j]; }
   for (int d = 0; d < D; ++d) {
     double acc = 0.0;
-    for (int j = 0; j < len; ++j) acc += sc[j] * h2f(vc[(int64_t)j * D + d]);
-    out[d] = f2h((float)(acc / sum));
+    for (int j = 0; j < len; ++j) acc += sc[j] * dec_dt(vc[(int64_t)j * D + d], dt);
+    out[d] = enc_dt((float)(acc / sum), dt);
   }
   free(sc);
 }
 
-/* y[t, n] = f16((sum_k q[n,k] x[t,k]) * s[n]) */
-static void lin16(const uint16_t* x, const int8_t* q, const float* s, int64_t T, int64_t K,
-                  int64_t N, uint16_t* y) {
-#pragma omp parallel for collapse(2) schedule(static)
-  for (int64_t t = 0; t < T; ++t)
+/* One linear y[T, N] = x[T, K] W^T in format fmt (see the section comment). */
+static void lin_dt(const uint16_t* x, int dt, int fmt, const void* W, const void* S, int64_t T,
+                   int64_t K, int64_t N, uint16_t* y) {
+  double* xd = (double*)malloc(sizeof(double) * (size_t)(T * K));
+  for (int64_t i = 0; i < T * K; ++i) xd[i] = dec_dt(x[i], dt);
+  if (fmt == ORC_WFMT_W8A16 || fmt == ORC_WFMT_W8A16_F16S) {
+    const int8_t* q = (const int8_t*)W;
+#pragma omp parallel for schedule(static)
     for (int64_t n = 0; n < N; ++n) {
-      double acc = 0.0;
+      const float s = fmt == ORC_WFMT_W8A16 ? ((const float*)S)[n] : h2f(((const uint16_t*)S)[n]);
       const int8_t* row = q + n * K;
-      for (int64_t k = 0; k < K; ++k) acc += (double)row[k] * h2f(x[t * K + k]);
-      y[t * N + n] = f2h((float)acc * s[n]);
+      for (int64_t t = 0; t < T; ++t) {
+        double acc = 0.0;
+        const double* xr = xd + t * K;
+        for (int64_t k = 0; k < K; ++k) acc += (double)row[k] * xr[k];
+        y[t * N + n] = enc_dt((float)acc * s, dt);
+      }
     }
+  } else if (T > 1) { /* the dequantised copy: T(d q) weights, dense product */
+    const int64_t bb = orc_gguf_block_bytes(fmt), nb = K / QK;
+#pragma omp parallel
+    {
+      double* wr = (double*)malloc(sizeof(double) * (size_t)K);
+#pragma omp for schedule(static)
+      for (int64_t n = 0; n < N; ++n) {
+        for (int64_t b = 0; b < nb; ++b) {
+          const uint8_t* blk = (const uint8_t*)W + (n * nb + b) * bb;
+          const float d = block_d(blk);
+          for (int j = 0; j < QK; ++j) wr[b * QK + j] = rnd_dt(d * (float)block_q(blk, fmt, j), dt);
+        }
+        for (int64_t t = 0; t < T; ++t) {
+          double acc = 0.0;
+          const double* xr = xd + t * K;
+          for (int64_t k = 0; k < K; ++k) acc += wr[k] * xr[k];
+          y[t * N + n] = enc_dt((float)acc, dt);
+        }
+      }
+      free(wr);
+    }
+  } else { /* QMatMul: activations to Q8_0, integer block dots, f32 block scaling */
+    float* yf = (float*)malloc(sizeof(float) * (size_t)(T * N));
+    float* xf = (float*)malloc(sizeof(float) * (size_t)(T * K));
+    for (int64_t i = 0; i < T * K; ++i) xf[i] = (float)xd[i];
+    orc_gguf_linear_candle(xf, ORC_F32, (const uint8_t*)W, fmt, T, K, N, yf);
+    for (int64_t i = 0; i < T * N; ++i) y[i] = enc_dt(yf[i], dt);
+    free(xf);
+    free(yf);
+  }
+  free(xd);
 }
 
 typedef struct orc_decoder {
   int32_t n_layers, hidden, inter, n_heads, n_kv, head_dim, vocab, qk_norm;
   float eps, theta;
+  int32_t act_dtype;     /* ORC_F16 or ORC_BF16 */
+  int32_t weight_format; /* layer linears: 0 W8A16 (f32 scale), 1 W8A16 (f16 scale), 2 Q4_0, 8 Q8_0 */
+  int32_t head_format;   /* output head, same codes */
 } orc_decoder;
 
-/* Per-layer pointer table (12 entries): qkv_q, qkv_s, o_q, o_s, gu_q, gu_s,
- * down_q, down_s, input_norm, post_norm, q_norm, k_norm.  Norms are f16 bits. */
+/* Per-layer pointer table (12 entries): qkv_w, qkv_s, o_w, o_s, gu_w, gu_s,
+ * down_w, down_s (W8A16: int8 [N, K] and scales [N]; GGUF: native blocks
+ * [N, K/32] and NULL), input_norm, post_norm, q_norm, k_norm (T bits; the QK
+ * norms may be NULL without qk_norm). */
 enum { L_QKV_Q, L_QKV_S, L_O_Q, L_O_S, L_GU_Q, L_GU_S, L_DN_Q, L_DN_S, L_IN, L_POST, L_QN, L_KN, L_N };
 
+static int fmt_ok(int f) {
+  return f == ORC_WFMT_W8A16 || f == ORC_WFMT_W8A16_F16S || f == ORC_Q4_0 || f == ORC_Q8_0;
+}
+
 /* Greedy generation for one sequence: prefill `prompt`, then n_new tokens.
- * out_tokens[n_new]; margins[n_new] = top1 - top2 logit of each step. */
-ORC_API int orc_decoder_generate(const orc_decoder* c, const void* const* layer_ptrs,
-                                 const uint16_t* embed, const uint16_t* final_norm,
-                                 const int8_t* head_q, const float* head_s, const int32_t* prompt,
-                                 int n_prompt, int n_new, int32_t* out_tokens, float* margins) {
+ * out_tokens[n_new]; margins[n_new] = top1 - top2 of each step's T logits;
+ * logits_out (optional) [n_new, vocab]: each step's T logits as f32.
+ * forced (optional) [n_new]: the token fed back after each step instead of the
+ * argmax (teacher forcing; out_tokens still receive the argmax).
+ * embed: [vocab, hidden] T bits. */
+ORC_API int orc_decoder_run(const orc_decoder* c, const void* const* layer_ptrs,
+                            const uint16_t* embed, const uint16_t* final_norm, const void* head_w,
+                            const void* head_s, const int32_t* prompt, int n_prompt, int n_new,
+                            const int32_t* forced, int32_t* out_tokens, float* margins,
+                            float* logits_out, uint16_t* hidden_out) {
+  const int dt = c->act_dtype;
+  if ((dt != ORC_F16 && dt != ORC_BF16) || !fmt_ok(c->weight_format) || !fmt_ok(c->head_format) ||
+      c->head_dim > 256 || c->n_kv <= 0 || c->n_heads % c->n_kv || n_prompt <= 0)
+    return -1;
   const int64_t H = c->hidden, I = c->inter, D = c->head_dim, Hq = c->n_heads, Hkv = c->n_kv;
   const int64_t QKV = (Hq + 2 * Hkv) * D, QD = Hq * D, V = c->vocab;
   const int64_t max_seq = n_prompt + n_new + 1;
-  const int rep = (int)(Hq / Hkv);
+  const int rep = (int)(Hq / Hkv), wf = c->weight_format;
   uint16_t* kc = (uint16_t*)calloc((size_t)(c->n_layers * Hkv * max_seq * D), 2);
   uint16_t* vc = (uint16_t*)calloc((size_t)(c->n_layers * Hkv * max_seq * D), 2);
   uint16_t* cos_t = (uint16_t*)malloc((size_t)(max_seq * D / 2) * 2);
   uint16_t* sin_t = (uint16_t*)malloc((size_t)(max_seq * D / 2) * 2);
-  orc_rope_tables(cos_t, sin_t, max_seq, (int)D, c->theta);
+  rope_tables_dt(cos_t, sin_t, max_seq, (int)D, c->theta, dt);
   const int64_t Tmax = n_prompt;
   uint16_t* h = (uint16_t*)malloc((size_t)(Tmax * H) * 2);
   uint16_t* x1 = (uint16_t*)malloc((size_t)(Tmax * H) * 2);
@@ -757,56 +860,68 @@ ORC_API int orc_decoder_generate(const orc_decoder* c, const void* const* layer_
     for (int64_t t = 0; t < T; ++t) memcpy(h + t * H, embed + (int64_t)toks[p0 + t] * H, (size_t)H * 2);
     for (int l = 0; l < c->n_layers; ++l) {
       const void* const* P = layer_ptrs + (int64_t)l * L_N;
-      orc_rmsnorm(h, NULL, NULL, (const uint16_t*)P[L_IN], x1, T, H, c->eps);
-      lin16(x1, (const int8_t*)P[L_QKV_Q], (const float*)P[L_QKV_S], T, H, QKV, qkv);
+      rmsnorm_dt(h, NULL, NULL, (const uint16_t*)P[L_IN], x1, T, H, c->eps, dt);
+      lin_dt(x1, dt, wf, P[L_QKV_Q], P[L_QKV_S], T, H, QKV, qkv);
       uint16_t* kl = kc + (int64_t)l * Hkv * max_seq * D;
       uint16_t* vl = vc + (int64_t)l * Hkv * max_seq * D;
       for (int64_t t = 0; t < T; ++t) {
         const int pos = (int)(p0 + t);
         for (int64_t hh = 0; hh < Hq; ++hh)
           head_norm_rope(qkv + t * QKV + hh * D, (const uint16_t*)P[L_QN], c->qk_norm, c->eps,
-                         cos_t, sin_t, pos, (int)D, qr + t * QD + hh * D);
+                         cos_t, sin_t, pos, (int)D, dt, qr + t * QD + hh * D);
         for (int64_t g = 0; g < Hkv; ++g) {
           head_norm_rope(qkv + t * QKV + (Hq + g) * D, (const uint16_t*)P[L_KN], c->qk_norm, c->eps,
-                         cos_t, sin_t, pos, (int)D, kl + (g * max_seq + pos) * D);
+                         cos_t, sin_t, pos, (int)D, dt, kl + (g * max_seq + pos) * D);
           memcpy(vl + (g * max_seq + pos) * D, qkv + t * QKV + (Hq + Hkv + g) * D, (size_t)D * 2);
         }
       }
+#pragma omp parallel for collapse(2) schedule(static)
       for (int64_t t = 0; t < T; ++t)
         for (int64_t hh = 0; hh < Hq; ++hh) {
           const int64_t g = hh / rep;
           attend(qr + t * QD + hh * D, kl + g * max_seq * D, vl + g * max_seq * D,
-                 (int)(p0 + t + 1), (int)D, att + t * QD + hh * D);
+                 (int)(p0 + t + 1), (int)D, dt, att + t * QD + hh * D);
         }
-      lin16(att, (const int8_t*)P[L_O_Q], (const float*)P[L_O_S], T, QD, H, dl);
-      orc_rmsnorm(dl, h, h, (const uint16_t*)P[L_POST], x1, T, H, c->eps);
-      lin16(x1, (const int8_t*)P[L_GU_Q], (const float*)P[L_GU_S], T, H, 2 * I, gu);
+      lin_dt(att, dt, wf, P[L_O_Q], P[L_O_S], T, QD, H, dl);
+      rmsnorm_dt(dl, h, h, (const uint16_t*)P[L_POST], x1, T, H, c->eps, dt);
+      lin_dt(x1, dt, wf, P[L_GU_Q], P[L_GU_S], T, H, 2 * I, gu);
       for (int64_t t = 0; t < T; ++t)
         for (int64_t i = 0; i < I; ++i) {
-          const float g = h2f(gu[t * 2 * I + i]), u = h2f(gu[t * 2 * I + I + i]);
-          const float s = hr(g / (1.0f + expf(-g)));
-          mid[t * I + i] = f2h(s * u);
+          const float g = dec_dt(gu[t * 2 * I + i], dt), u = dec_dt(gu[t * 2 * I + I + i], dt);
+          const float s = rnd_dt(g / (1.0f + expf(-g)), dt);
+          mid[t * I + i] = enc_dt(s * u, dt);
         }
-      lin16(mid, (const int8_t*)P[L_DN_Q], (const float*)P[L_DN_S], T, I, H, dl);
-      for (int64_t i = 0; i < T * H; ++i) h[i] = f2h(h2f(h[i]) + h2f(dl[i]));
+      lin_dt(mid, dt, wf, P[L_DN_Q], P[L_DN_S], T, I, H, dl);
+      for (int64_t i = 0; i < T * H; ++i) h[i] = enc_dt(dec_dt(h[i], dt) + dec_dt(dl[i], dt), dt);
     }
     /* head on the last position */
-    orc_rmsnorm(h + (T - 1) * H, NULL, NULL, final_norm, x1, 1, H, c->eps);
-    lin16(x1, head_q, head_s, 1, H, V, logits);
+    if (hidden_out) memcpy(hidden_out + (int64_t)step * H, h + (T - 1) * H, (size_t)H * 2);
+    rmsnorm_dt(h + (T - 1) * H, NULL, NULL, final_norm, x1, 1, H, c->eps, dt);
+    lin_dt(x1, dt, c->head_format, head_w, head_s, 1, H, V, logits);
     float best = -INFINITY, second = -INFINITY;
     int32_t bi = 0;
     for (int64_t v = 0; v < V; ++v) {
-      const float lv = h2f(logits[v]);
+      const float lv = dec_dt(logits[v], dt);
       if (lv > best) { second = best; best = lv; bi = (int32_t)v; }
       else if (lv > second) second = lv;
     }
     out_tokens[step] = bi;
     if (margins) margins[step] = best - second;
-    toks[p0 + T] = bi;
+    if (logits_out)
+      for (int64_t v = 0; v < V; ++v) logits_out[(int64_t)step * V + v] = dec_dt(logits[v], dt);
+    toks[p0 + T] = forced ? forced[step] : bi;
     p0 += T;
     T = 1;
   }
   free(kc); free(vc); free(cos_t); free(sin_t); free(h); free(x1); free(qkv); free(qr);
   free(att); free(dl); free(gu); free(mid); free(logits); free(toks);
   return 0;
+}
+
+ORC_API int orc_decoder_generate(const orc_decoder* c, const void* const* layer_ptrs,
+                                 const uint16_t* embed, const uint16_t* final_norm,
+                                 const void* head_w, const void* head_s, const int32_t* prompt,
+                                 int n_prompt, int n_new, int32_t* out_tokens, float* margins) {
+  return orc_decoder_run(c, layer_ptrs, embed, final_norm, head_w, head_s, prompt, n_prompt, n_new,
+                         NULL, out_tokens, margins, NULL, NULL);
 }

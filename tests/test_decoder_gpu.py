@@ -76,11 +76,13 @@ def test_rope_tables(D, torch):
 
 
 def _rope_ref(v, cos_t, sin_t, p):
+    """candle's rope over f16 tensors: every product and sum rounded to f16."""
     half = v.shape[-1] // 2
     c = cos_t[p].astype(np.float32)
     s = sin_t[p].astype(np.float32)
-    a, b = v[..., :half], v[..., half:]
-    return np.concatenate([a * c - b * s, b * c + a * s], -1)
+    a, b = np.asarray(v[..., :half], np.float32), np.asarray(v[..., half:], np.float32)
+    r = lambda x: x.astype(np.float16).astype(np.float32)
+    return np.concatenate([r(a * c) - r(b * s), r(a * s) + r(b * c)], -1).astype(np.float16)
 
 
 @pytest.mark.parametrize("qk_norm", [1, 0])
@@ -114,20 +116,37 @@ def test_qk_norm_rope_kv_append(D, torch, qk_norm):
                 heads[h] = (x / np.sqrt((x.astype(np.float64) ** 2).mean() + 1e-6) * w).astype(np.float16)
         rq = _rope_ref(heads[:Hq], cos_t, sin_t, pos[t])
         rk = _rope_ref(heads[Hq:Hq + Hkv], cos_t, sin_t, pos[t])
-        assert rel(qo[t], rq) <= 3e-3
-        assert rel(kco[slot[t], :, pos[t]], rk) <= 3e-3
+        if qk_norm:
+            assert rel(qo[t], rq) <= 3e-3
+            assert rel(kco[slot[t], :, pos[t]], rk) <= 3e-3
+        else:  # RoPE alone: the same f16 operations, bit-exact
+            assert np.array_equal(qo[t].view(np.uint16), rq.view(np.uint16))
+            assert np.array_equal(kco[slot[t], :, pos[t]].view(np.uint16), rk.view(np.uint16))
         assert np.array_equal(vco[slot[t], :, pos[t]], qkv[t].reshape(-1, Dh)[Hq + Hkv:])
 
 
-def _attn_ref(q, kc, vc, pos, slot, Hkv):
+def _round_dt(x, dt):
+    """Round to the activation type (float64 values out)."""
+    x = np.asarray(x, np.float32)
+    if dt == "f16":
+        return x.astype(np.float16).astype(np.float64)
+    if dt == "bf16":
+        return O.bf16_to_f32(O.f32_to_bf16(x)).astype(np.float64)
+    return x.astype(np.float64)
+
+
+def _attn_ref(q, kc, vc, pos, slot, Hkv, dt):
+    """The reference's attention (text.rs:1278-1280): s = T(T(q.k) * T(1/sqrt(D))),
+    softmax, o = p.V (probabilities unrounded, see the kernel's note)."""
     T, Hq, Dh = q.shape
     rep = Hq // Hkv
+    mul = _round_dt(1.0 / np.sqrt(Dh), dt)
     out = np.zeros((T, Hq, Dh))
     for t in range(T):
         for h in range(Hq):
             K = kc[slot[t], h // rep, :pos[t] + 1].astype(np.float64)
             V = vc[slot[t], h // rep, :pos[t] + 1].astype(np.float64)
-            s = K @ q[t, h].astype(np.float64) / np.sqrt(Dh)
+            s = _round_dt(_round_dt(K @ q[t, h].astype(np.float64), dt) * mul, dt)
             p = np.exp(s - s.max())
             out[t, h] = p @ V / p.sum()
     return out.reshape(T, Hq * Dh)
@@ -186,7 +205,7 @@ def test_attention(D, torch, mode, Hq, dt):
                                        S, max_len, D.stream_ptr()), "attention")
         outs.append(out.float().cpu().numpy())
     assert np.array_equal(outs[0], outs[1])
-    ref = _attn_ref(q64, k64, v64, pos, slot, Hkv)
+    ref = _attn_ref(q64, k64, v64, pos, slot, Hkv, dt)
     got = outs[0]
     # output rounding of the type (f16 2^-11, bf16 2^-8) plus f32 accumulation
     assert rel(got, ref) <= {"f16": 3e-3, "bf16": 1e-2}[dt]

@@ -118,6 +118,27 @@ def test_w8a16_linear_streamk_shapes(D, torch, M, N, K):
     assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
 
 
+@pytest.mark.parametrize("M,N,K", [(8, 4096, 12288), (8, 24576, 4096), (7, 4096, 12288)])
+def test_w8a16_linear_ring_reuse_is_race_free(D, torch, M, N, K):
+    """Stream-K GEMV shapes where every warp refills its shared-memory ring many
+    times: a refill must not overwrite a stage before every lane has read it.
+    A missing ordering showed as about one wrong 16-row tile per call; twelve
+    calls must all match the oracle and each other bit for bit."""
+    rng = np.random.default_rng(M * 17 + N + K)
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    x = rng.normal(0, 1, (M, K)).astype(np.float16)
+    lin = D.W8A16Linear.from_linear("t", _to_dev(torch, w))
+    xt = _to_dev(torch, x)
+    y_ref, _ = O.w8a16_linear(x, lin.qweight.cpu().numpy(), lin.scales.cpu().numpy())
+    first = None
+    for _ in range(12):
+        y = lin.forward(xt).float().cpu().numpy()
+        assert rel_err(y, y_ref) <= 2e-3
+        if first is None:
+            first = y
+        assert np.array_equal(first.view(np.uint32), y.view(np.uint32))
+
+
 @pytest.mark.parametrize("M,N,K,xdt", [(1, 12288, 1024, "f16"), (2, 40000, 1024, "bf16"),
                                         (9, 4096, 1536, "f16"), (16, 2400, 1024, "bf16")])
 def test_w8a16_linear_tile_cta_shapes(D, torch, M, N, K, xdt):

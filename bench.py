@@ -14,14 +14,21 @@ benchmark configurations; no dataset is involved):
   gguf_sweep    GGUF QMatMul over the 7 linears of an 8B decoder layer (q, k,
                 v, o, gate, up, down) for Q4_0 and Q8_0 at M in {1, 8}, f32
                 activations.  Metric: dequant-GEMV HBM GB/s over the sweep.
+  gguf_sweep_m32  The same sweep at M = 32 (between decode and prefill; still
+                HBM-bound).  Metric: HBM GB/s over the sweep.
   gguf_prefill  The same sweep at M = 512 (the prefill point of the GGUF
                 sweep).  Metric: dequant-GEMM TFLOP/s (tensor roofline).
+  w8a16_prefill The 4 fused linears of a Qwen3-8B layer (QKV 6144x4096, O
+                4096x4096, gate_up 24576x4096, down 4096x12288) at M = 512
+                (a 512-token prompt), f16.  Metric: dequant-GEMM TFLOP/s.
   gguf_k_sweep  The 7 linears of a Llama-3-8B layer in Q4_K and Q6_K (the
                 types of a Q4_K_M file) at M = 1, f16 activations.  Metric:
                 dequant-GEMV HBM GB/s over the sweep.
-  qwen3_decode / llama_gguf_decode / attention_batched: whole-model decode
-                (the default, qwen3_decode) and the batched decode attention;
-                their docstrings give the shapes.
+  qwen3_decode / qwen3_decode_bf16 / qwen3_generate / llama_gguf_decode /
+  attention_batched: whole-model decode (the default, qwen3_decode: f16, the
+                reference's W8A16 dtype) and the batched decode attention;
+                their docstrings give the shapes.  --split even|planner picks
+                the layer split of the pipeline workloads.
 A step is one pass of the workload.  Multi-linear steps are captured once in
 a CUDA graph and replayed.  Inputs: rotating copies of the weights whose total
 exceeds the 126 MB L2, so every step reads its weights from HBM.
@@ -207,8 +214,7 @@ class W8A16Gemv:
     kernel = "w8a16_tma_kernel<NT=1>"
     M, N, K = 1, 12288, 4096
     graph = True
-    # ncu DRAM read + write bytes of one launch of this shape
-    # (profiles/w8a16_tma_kernel_gemv_12288x4096.md)
+    # DRAM read + write bytes of one launch of this shape, from an ncu capture
     traffic = 50_430_976 + 4_608
 
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
@@ -228,10 +234,16 @@ class W8A16Gemv:
         self.kernel_work = self.work_per_step
         self.h_x = self.x.cpu().pin_memory()
         self.h_y = torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
-        self.config = {"workload": "w8a16_gemv", "M": 1, "N": self.N, "K": self.K,
-                       "weight": "int8 per-row, f16 scale", "activation": "f16",
-                       "l2": f"{self.copies} rotating weight copies "
-                             f"({self.copies * per / 1e6:.0f} MB > 126 MB L2)"}
+        self.config = self.describe()
+
+    @classmethod
+    def describe(cls, world: int = 1):
+        per = cls.N * cls.K + 2 * cls.N
+        copies = max(2, -(-3 * L2_BYTES // per))
+        return {"workload": "w8a16_gemv", "M": 1, "N": cls.N, "K": cls.K,
+                "weight": "int8 per-row, f16 scale", "activation": "f16",
+                "l2": f"{copies} rotating weight copies ({copies * per / 1e6:.0f} MB > 126 MB L2)",
+                "launch": f"CUDA graph of {cls.chain} consecutive GEMVs (PDL between them)"}
 
     @classmethod
     def bytes(cls):
@@ -258,7 +270,6 @@ class W8A16Gemv:
             for k in range(self.chain):
                 self.run_copy(k % self.copies)
         torch.cuda.synchronize()
-        self.config["launch"] = f"CUDA graph of {self.chain} consecutive GEMVs (PDL between them)"
 
     def step(self):
         self.graphs[self.i % self.copies].replay()
@@ -313,11 +324,18 @@ class GgufSweep:
         self.i = 0
         self.work_per_step = self.bytes()
         self.kernel_work = None
-        self.config = {"workload": "gguf_sweep", "M": list(self.ms), "types": ["Q4_0", "Q8_0"],
-                       "shapes": [f"{n}:{k}->{N}" for n, N, k in LAYER_SHAPES], "activation": "f32",
-                       "l2": f"{self.copies} rotating layer copies "
-                             f"({self.copies * per_layer / 1e6:.0f} MB > 126 MB L2)",
-                       "launch": "CUDA graph per layer copy"}
+        self.config = self.describe()
+
+    name = "gguf_sweep"
+
+    @classmethod
+    def describe(cls, world: int = 1):
+        per_layer = sum(N * (K // 32) * bb for bb in GGUF_BLOCK_BYTES.values() for _, N, K in LAYER_SHAPES)
+        copies = max(2, -(-3 * L2_BYTES // per_layer))
+        return {"workload": cls.name, "M": list(cls.ms), "types": ["Q4_0", "Q8_0"],
+                "shapes": [f"{n}:{k}->{N}" for n, N, k in LAYER_SHAPES], "activation": "f32",
+                "l2": f"{copies} rotating layer copies ({copies * per_layer / 1e6:.0f} MB > 126 MB L2)",
+                "launch": "CUDA graph per layer copy"}
 
     @classmethod
     def bytes(cls):
@@ -358,16 +376,30 @@ class GgufKSweep:
     ms = (1,)
     graph = True
 
+    @staticmethod
+    def random_blocks(rng, qt: int, N: int, K: int, scale: float = 1e-4):
+        """Seeded K-quant super-blocks [N, K/256*bytes]: random quant, scale and
+        min bytes with finite f16 super-block scales ~ N(0, scale)."""
+        import numpy as np
+        nb, bb = K // 256, (144 if qt == 12 else 210)
+        raw = rng.integers(0, 256, (N, nb, bb), dtype=np.uint8)
+        d = rng.normal(0.0, scale, (N, nb)).astype(np.float16)
+        if qt == 12:  # Q4_K: f16 d, f16 dmin at bytes 0..3
+            raw[:, :, 0:2] = d.view(np.uint8).reshape(N, nb, 2)
+            dmin = np.abs(rng.normal(0.0, scale, (N, nb))).astype(np.float16)
+            raw[:, :, 2:4] = dmin.view(np.uint8).reshape(N, nb, 2)
+        else:  # Q6_K: f16 d at bytes 208..209
+            raw[:, :, 208:210] = d.view(np.uint8).reshape(N, nb, 2)
+        return raw.reshape(N, nb * bb)
+
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
         import numpy as np
-
-        import oracle as O  # seeded block bytes only (no oracle arithmetic on this path)
         self.torch, self.D = torch, D
         rng = np.random.default_rng(SEED)
         layer, per_layer = [], 0
         for qt in (D.Q4_K, D.Q6_K):
             for name, N, K in LLAMA_SHAPES:
-                b = torch.from_numpy(O.gguf_k_random_blocks(rng, qt, N, K).reshape(-1)).cuda()
+                b = torch.from_numpy(self.random_blocks(rng, qt, N, K).reshape(-1)).cuda()
                 lin = D.GgufKLinear.from_blocks(b, qt, K, N, name)
                 layer.append(lin)
                 per_layer += lin.weight_bytes
@@ -385,12 +417,17 @@ class GgufKSweep:
         self.i = 0
         self.work_per_step = self.bytes()
         self.kernel_work = None
-        self.config = {"workload": "gguf_k_sweep", "M": list(self.ms), "types": ["Q4_K", "Q6_K"],
-                       "shapes": [f"{n}:{k}->{N}" for n, N, k in LLAMA_SHAPES], "activation": "f16",
-                       "weights": "seeded random super-blocks (finite f16 scales)",
-                       "l2": f"{self.copies} rotating layer copies "
-                             f"({self.copies * per_layer / 1e6:.0f} MB > 126 MB L2)",
-                       "launch": "CUDA graph per layer copy"}
+        self.config = self.describe()
+
+    @classmethod
+    def describe(cls, world: int = 1):
+        per_layer = sum(N * (K // 256) * bb for bb in K_BLOCK_BYTES.values() for _, N, K in LLAMA_SHAPES)
+        copies = max(2, -(-3 * L2_BYTES // per_layer))
+        return {"workload": "gguf_k_sweep", "M": list(cls.ms), "types": ["Q4_K", "Q6_K"],
+                "shapes": [f"{n}:{k}->{N}" for n, N, k in LLAMA_SHAPES], "activation": "f16",
+                "weights": "seeded random super-blocks (finite f16 scales)",
+                "l2": f"{copies} rotating layer copies ({copies * per_layer / 1e6:.0f} MB > 126 MB L2)",
+                "launch": "CUDA graph per layer copy"}
 
     @classmethod
     def bytes(cls):
@@ -414,21 +451,88 @@ class GgufKSweep:
         self.i += 1
 
 
+class GgufSweepM32(GgufSweep):
+    """GGUF sweep at M = 32 (the batched-decode row count of the Llama GGUF
+    decoder; Q4_0 at 32 rows is still HBM-bound: ~104 flop per byte)."""
+    kernel = "dequant_gemm_kernel, 32-token tiles (whole sweep)"
+    ms = (32,)
+    name = "gguf_sweep_m32"
+
+
 class GgufPrefill(GgufSweep):
     """GGUF prefill sweep: the same sweep at M = 512 (tensor-bound)."""
     metric, unit, bound, dtype = "dequant-GEMM TFLOP/s", "TFLOP/s", "tensor", "q4_0/q8_0 x f32 -> f16 MMA"
     kernel = "dequant_gemm_kernel (whole sweep)"
     ms = (512,)
+    name = "gguf_prefill"
 
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
         super().__init__(torch, D)
         self.work_per_step = self.flops()
-        self.config["workload"] = "gguf_prefill"
-        self.config["M"] = list(self.ms)
 
     @classmethod
     def flops(cls):
         return sum(2 * m * N * K for m in cls.ms for _ in GGUF_BLOCK_BYTES for _, N, K in LAYER_SHAPES)
+
+
+QWEN_LAYER_LINEARS = [  # (name, out N, in K): the fused linears of one Qwen3-8B layer
+    ("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 24576, 4096), ("down", 4096, 12288),
+]
+
+
+class W8A16Prefill:
+    """W8A16 prefill: the 4 fused linears of a Qwen3-8B layer at M = 512 (a
+    512-token prompt), f16 activations, f32 row scales, through
+    dial_w8a16_linear (the tcgen05 dequant GEMM).  Metric: TFLOP/s."""
+    metric, unit, bound, dtype = "dequant-GEMM TFLOP/s", "TFLOP/s", "tensor", "int8 x f16 -> f16 MMA"
+    kernel = "dequant_gemm_kernel (the layer's 4 linears)"
+    M = 512
+    graph = True
+
+    def __init__(self, torch, D, rank: int = 0, world: int = 1):
+        self.torch, self.D = torch, D
+        g = torch.Generator(device="cuda").manual_seed(SEED)
+        layer = []
+        for name, N, K in QWEN_LAYER_LINEARS:
+            w = torch.randn((N, K), generator=g, device="cuda", dtype=torch.float32) * 0.02
+            layer.append(D.W8A16Linear.from_linear(name, w))
+            del w
+        per_layer = sum(l.weight_bytes for l in layer)
+        self.copies = max(2, -(-3 * L2_BYTES // per_layer))
+        self.layers = [layer] + [[D.W8A16Linear(l.qweight.clone(), l.scales.clone(), l.in_dim, l.out_dim,
+                                                l.name) for l in layer] for _ in range(self.copies - 1)]
+        self.xs = {K: torch.randn((self.M, K), generator=g, device="cuda").half()
+                   for _, _, K in QWEN_LAYER_LINEARS}
+        self.ys = [torch.empty((self.M, N), device="cuda", dtype=torch.float16)
+                   for _, N, _ in QWEN_LAYER_LINEARS]
+        self.i = 0
+        self.work_per_step = self.flops()
+        self.config = self.describe()
+
+    @classmethod
+    def describe(cls, world: int = 1):
+        per_layer = sum(N * K + 4 * N for _, N, K in QWEN_LAYER_LINEARS)
+        copies = max(2, -(-3 * L2_BYTES // per_layer))
+        return {"workload": "w8a16_prefill", "M": cls.M,
+                "shapes": [f"{n}:{k}->{N}" for n, N, k in QWEN_LAYER_LINEARS], "activation": "f16",
+                "weight": "int8 per-row, f32 scale",
+                "l2": f"{copies} rotating layer copies ({copies * per_layer / 1e6:.0f} MB > 126 MB L2)",
+                "launch": "CUDA graph per layer copy"}
+
+    @classmethod
+    def flops(cls):
+        return sum(2 * cls.M * N * K for _, N, K in QWEN_LAYER_LINEARS)
+
+    def run_copy(self, li):
+        for lin, y in zip(self.layers[li], self.ys):
+            lin.forward(self.xs[lin.in_dim], out=y)
+
+    def build_graphs(self):
+        build_copy_graphs(self)
+
+    def step(self):
+        self.graphs[self.i % self.copies].replay()
+        self.i += 1
 
 
 class AttentionDecode:
@@ -462,10 +566,15 @@ class AttentionDecode:
         self.need = need
         self.i = 0
         self.work_per_step = self.bytes()
-        self.config = {"workload": "attention_batched", "sequences": self.T, "context": self.CTX,
-                       "heads": f"{self.HQ}/{self.HKV}", "head_dim": self.D, "kv_cache": "f16",
-                       "l2": f"{self.copies} rotating layer caches "
-                             f"({self.copies * per / 1e6:.0f} MB > 126 MB L2)"}
+        self.config = self.describe()
+
+    @classmethod
+    def describe(cls, world: int = 1):
+        per = 2 * cls.T * cls.HKV * (cls.CTX + 15) * cls.D * 2
+        copies = max(2, -(-3 * L2_BYTES // per))
+        return {"workload": "attention_batched", "sequences": cls.T, "context": cls.CTX,
+                "heads": f"{cls.HQ}/{cls.HKV}", "head_dim": cls.D, "kv_cache": "f16",
+                "l2": f"{copies} rotating layer caches ({copies * per / 1e6:.0f} MB > 126 MB L2)"}
 
     @classmethod
     def bytes(cls):
@@ -494,39 +603,58 @@ class QwenDecode:
     through a pipeline of one stage per rank (layers split by the stage
     planner, the output head counted as 3.2 layers).  A step advances every
     sequence by one greedy token.  Metric: decode tok/s of the whole job."""
-    metric, unit, bound, dtype = "8B W8A16 decode tok/s", "tok/s", "hbm", "int8 x bf16"
+    metric, unit, bound, dtype = "8B W8A16 decode tok/s", "tok/s", "hbm", "int8 x f16"
     kernel = "w8a16_tma_kernel<NT=1> (the stage's linears from one graph, events)"
     graph = True
     scaling = "strong"
-    # ncu DRAM bytes of the 145 GEMV launches of one token on one GPU
-    # (profiles/qwen3_decode_step_launches.md); per token, like `achieved`
+    # DRAM bytes per token of the stage's linears on one GPU: ncu DRAM bytes per
+    # 2 KB weight unit of one captured GEMV launch, times the token's units
     traffic = 7_596_160_192
     n_seqs, mb_size, prompt_len, decode_cap = 8, 1, 1024, 448
     head_layers = 3.2  # the output head's cost in layers (weights read per token)
     copies_per_step = 8  # one graph per micro-batch
-    act = "bf16"
+    act = "f16"
+    split = "planner"  # layer split over the stages: "planner" or "even"
+    name = "qwen3_decode"
 
-    def model_config(self):
+    @classmethod
+    def model_config(cls):
         from dial_cuda.model import ModelConfig
-        return ModelConfig(act_dtype=self.act)
+        return ModelConfig(act_dtype=cls.act)
 
-    def micro_batch(self, world):
-        return self.mb_size
+    @classmethod
+    def micro_batch(cls, world):
+        return cls.mb_size
 
-    def describe(self):
+    @classmethod
+    def ranges_for(cls, world):
+        from dial_cuda.pipeline import stage_layers
+        return stage_layers(cls.model_config().n_layers, world, head_layers=cls.head_layers,
+                            method=cls.split)
+
+    @classmethod
+    def model_desc(cls):
         return {"workload": "qwen3_8b_w8a16_decode", "model": "Qwen3-8B-shaped, random init",
                 "layers": 36, "hidden": 4096, "intermediate": 12288, "heads": "32/8",
                 "vocab": 151936, "weights": "int8 per row, f32 scale (layers and head)",
                 "l2": "7.6 GB of weights per token >> 126 MB L2"}
 
+    @classmethod
+    def describe(cls, world: int = 1):
+        return dict(cls.model_desc(), sequences=cls.n_seqs, micro_batch=cls.micro_batch(world),
+                    prompt_len=cls.prompt_len, activation=cls.act, kv_cache=cls.act,
+                    split=cls.split if world > 1 else "one stage",
+                    stages=[[r.start, r.stop] for r in cls.ranges_for(world)],
+                    launch="one CUDA graph per micro-batch and stage; NCCL p2p hand-off")
+
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
         from dial_cuda.model import Stage
-        from dial_cuda.pipeline import ModelStageCompute, Pipeline, TorchChannel, stage_layers
+        from dial_cuda.pipeline import ModelStageCompute, Pipeline, TorchChannel
         self.torch, self.D, self.rank, self.world = torch, D, rank, world
         self.cfg = self.model_config()
         self.mb_size = self.micro_batch(world)
         n_mb = self.n_seqs // self.mb_size
-        self.ranges = stage_layers(self.cfg.n_layers, world, head_layers=self.head_layers)
+        self.ranges = self.ranges_for(world)
         rr = self.ranges[rank]
         self.max_seq = self.prompt_len + self.decode_cap + 16
         self.stage = Stage(self.cfg, rr.start, rr.stop, n_slots=self.n_seqs, max_seq=self.max_seq)
@@ -550,12 +678,9 @@ class QwenDecode:
         self.weight_bytes = st.weight_bytes
         self.steps_done = 0
         self.copies_per_step = n_mb
-        self.config = dict(self.describe(), sequences=self.n_seqs, micro_batch=self.mb_size,
-                           prompt_len=self.prompt_len, activation=self.act, kv_cache=self.act,
-                           stages=[[r.start, r.stop] for r in self.ranges],
-                           stage_weights_GB=round(self.weight_bytes / 1e9, 3),
-                           prefill_ms_per_seq=round(self.prefill_ms, 2),
-                           launch="one CUDA graph per micro-batch and stage; NCCL p2p hand-off")
+        self.config = self.describe(world)
+        self.details = {"stage_weights_GB": round(self.weight_bytes / 1e9, 3),
+                        "prefill_ms_per_seq": round(self.prefill_ms, 2)}
 
     def run_copy(self, _):
         """One eager micro-batch for the launch count (its state is restored)."""
@@ -649,29 +774,58 @@ class LlamaGgufDecode(QwenDecode):
     head_layers = 1.4  # Q8_0 head 558 MB vs a Q4_0 layer's 123 MB + 268 MB of KV per step
     act = "f16"
 
-    def model_config(self):
+    name = "llama_gguf_decode"
+
+    @classmethod
+    def model_config(cls):
         from dial_cuda.model import ModelConfig
         c = ModelConfig.llama3_8b_q4_0()
-        c.act_dtype = self.act
+        c.act_dtype = cls.act
         return c
 
-    def micro_batch(self, world):
+    @classmethod
+    def micro_batch(cls, world):
         """As many micro-batches as stages (one on a single GPU): each stage reads
         its weights once per micro-batch, and with fewer micro-batches than
         stages some stage would idle."""
-        assert self.n_seqs % world == 0, "sequences must split evenly over the stages"
-        return self.n_seqs // world
+        assert cls.n_seqs % world == 0, "sequences must split evenly over the stages"
+        return cls.n_seqs // world
 
-    def describe(self):
+    @classmethod
+    def model_desc(cls):
         return {"workload": "llama3_8b_gguf_q4_0_batched_decode", "model": "Llama-3-8B-shaped, random init",
                 "layers": 32, "hidden": 4096, "intermediate": 14336, "heads": "32/8", "vocab": 128256,
                 "weights": "Q4_0 layers, Q8_0 head",
                 "l2": "3.9 GB of weights + 9 GB of KV per step >> 126 MB L2"}
 
 
-WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep, "gguf_prefill": GgufPrefill,
+class QwenDecodeBf16(QwenDecode):
+    """qwen3_decode with bf16 activations and KV cache."""
+    dtype = "int8 x bf16"
+    act = "bf16"
+    name = "qwen3_decode_bf16"
+
+
+class QwenGenerate(QwenDecode):
+    """Qwen3-8B-shaped W8A16 decoder, batch 1: a 512-token prompt prefilled
+    (untimed; its time is reported), then greedy decode steps of one token,
+    f16 activations and KV cache, positions wrapping after 256 steps.  A step
+    is one token.  Metric: decode tok/s."""
+    metric = "8B W8A16 decode tok/s (batch 1)"
+    n_seqs, mb_size, prompt_len, decode_cap = 1, 1, 512, 256
+    copies_per_step = 1
+    name = "qwen3_generate"
+
+    @classmethod
+    def model_desc(cls):
+        return dict(super().model_desc(), workload="qwen3_8b_w8a16_generate")
+
+
+WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep, "gguf_sweep_m32": GgufSweepM32,
+             "gguf_prefill": GgufPrefill, "w8a16_prefill": W8A16Prefill,
              "gguf_k_sweep": GgufKSweep,
-             "qwen3_decode": QwenDecode, "llama_gguf_decode": LlamaGgufDecode,
+             "qwen3_decode": QwenDecode, "qwen3_decode_bf16": QwenDecodeBf16,
+             "qwen3_generate": QwenGenerate, "llama_gguf_decode": LlamaGgufDecode,
              "attention_batched": AttentionDecode}
 
 
@@ -696,6 +850,14 @@ class CpuWorkload:
                           for qt in (O.Q4_K, O.Q6_K) for _, N, K in LLAMA_SHAPES]
             self.xk = {K: rng.normal(0, 1, (1, K)).astype(np.float16) for _, _, K in LLAMA_SHAPES}
             self.work = wl.bytes()
+        elif name == "w8a16_prefill":
+            self.wlins = []
+            for _, N, K in QWEN_LAYER_LINEARS:
+                q, s32, _ = O.w8a16_quantize(rng.normal(0, 0.02, (N, K)).astype(np.float32))
+                self.wlins.append((q, s32, K))
+            self.xw = {K: rng.normal(0, 1, (wl.M, K)).astype(np.float16) for _, _, K in QWEN_LAYER_LINEARS}
+            self.work = wl.flops()
+            self.M = wl.M
         else:
             self.lins = []
             for qt in (O.Q4_0, O.Q8_0):
@@ -716,6 +878,11 @@ class CpuWorkload:
             for blocks, qt, N, K in self.klins:
                 O.gguf_k_linear_candle(self.xk[K], blocks, qt, N)
             return 1.0
+        if self.name == "w8a16_prefill":
+            mm = max(1, int(round(self.M * frac)))
+            for q, s32, K in self.wlins:
+                O.w8a16_linear_f32(self.xw[K][:mm], q, s32)
+            return mm / self.M
         done = 0.0
         for m in self.ms:
             mm = max(1, int(round(m * frac)))
@@ -725,57 +892,69 @@ class CpuWorkload:
         return done
 
 
-def cpu_decode_measure(budget_s):
-    """Qwen3-8B decode on the C oracle (the CPU restatement of the reference's
-    layer + head path): 1- and 2-layer models with the full dims time the cost of
-    a layer and of embed + head; a 36-layer token is extrapolated from them."""
+_CPU_QWEN = {}
+
+
+def _cpu_qwen_model(act):
+    """A 36-layer Qwen3-8B-dim oracle model whose layers share one layer's int8
+    weights (the CPU cost depends on the shapes only; 193 MB per layer already
+    streams from DRAM), built once per process."""
     import numpy as np
 
     import oracle as O
+    if act in _CPU_QWEN:
+        return _CPU_QWEN[act]
     rng = np.random.default_rng(SEED)
     H, I, V, Dh, Hq, Hkv = 4096, 12288, 151936, 128, 32, 8
     QKV = (Hq + 2 * Hkv) * Dh
 
-    # the cost depends on the shapes only: int8 weights and scales are drawn directly
     def q8(shape):
         return (rng.integers(-127, 128, shape, dtype=np.int8),
                 np.full(shape[0], 0.02 * 3.5 / 127, np.float32))
 
-    def layer():
-        L = {}
-        for key, shape in (("qkv", (QKV, H)), ("o", (H, Hq * Dh)), ("gu", (2 * I, H)),
-                           ("down", (H, I))):
-            L[f"{key}_q"], L[f"{key}_s"] = q8(shape)
-        for n, dim in (("input_norm", H), ("post_norm", H), ("q_norm", Dh), ("k_norm", Dh)):
-            L[n] = np.ones(dim, np.float16)
-        return L
-
-    layers = [layer(), layer()]
-    embed = (rng.random((V, H), dtype=np.float32) * 0.04 - 0.02).astype(np.float16)
-    hq, hs = q8((V, H))
-    norm = np.ones(H, np.float16)
-    cfg = dict(n_layers=1, hidden=H, inter=I, n_heads=Hq, n_kv=Hkv, head_dim=Dh, vocab=V,
+    one = np.float16(1.0).view(np.uint16) if act == O.F16 else np.uint16(0x3F80)
+    L = {}
+    for key, shape in (("qkv", (QKV, H)), ("o", (H, Hq * Dh)), ("gu", (2 * I, H)), ("down", (H, I))):
+        L[f"{key}_q"], L[f"{key}_s"] = q8(shape)
+    for n, dim in (("input_norm", H), ("post_norm", H), ("q_norm", Dh), ("k_norm", Dh)):
+        L[n] = np.full(dim, one, np.uint16)
+    block = (rng.standard_normal((4096, H), dtype=np.float32) * 0.02)
+    block = block.astype(np.float16).view(np.uint16) if act == O.F16 else O.f32_to_bf16(block)
+    embed = np.tile(block, (-(-V // 4096), 1))[:V]
+    hq = np.tile(rng.integers(-127, 128, (4096, H), dtype=np.int8), (-(-V // 4096), 1))[:V]
+    hs = np.full(V, 0.02 * 3.5 / 127, np.float32)
+    cfg = dict(n_layers=36, hidden=H, inter=I, n_heads=Hq, n_kv=Hkv, head_dim=Dh, vocab=V,
                qk_norm=True, eps=1e-6, theta=1e6)
-    prompt = np.array([1], np.int32)
+    _CPU_QWEN[act] = (cfg, [L] * 36, embed, np.full(H, one, np.uint16), hq, hs)
+    return _CPU_QWEN[act]
 
-    def per_token(nl, n_new):
-        c = dict(cfg, n_layers=nl)
+
+def cpu_decode_measure(budget_s, act_name="f16"):
+    """Qwen3-8B decode on the C oracle (the CPU restatement of the reference's
+    layer + head path): the whole 36-layer model generating 2 greedy tokens
+    from a 1-token prompt per pass (each token: 36 layers + final norm + head)."""
+    import numpy as np
+
+    import oracle as O
+    act = O.F16 if act_name == "f16" else O.BF16
+    cfg, layers, embed, norm, hq, hs = _cpu_qwen_model(act)
+    prompt = np.array([1], np.int32)
+    n_new = 2
+
+    def per_token():
         t0 = time.perf_counter()
-        O.decoder_generate(c, layers[:nl], embed, norm, hq, hs, prompt, n_new)
+        O.decoder_generate(cfg, layers, embed, norm, hq, hs, prompt, n_new, act_dtype=act)
         return (time.perf_counter() - t0) / n_new
 
-    per_token(1, 1)  # warm-up
-    n_new, t1, t2 = 2, [], []
+    ts = []
     t0 = time.perf_counter()
-    while time.perf_counter() - t0 < budget_s or not t1:
-        t1.append(per_token(1, n_new))
-        t2.append(per_token(2, n_new))
-    a, b = statistics.median(t1), statistics.median(t2)
-    t_layer = max(b - a, 1e-9)
-    t_tok = (a - t_layer) + 36 * t_layer
-    sample = (f"{len(t1)} x ({n_new} tokens on 1-layer and 2-layer Qwen3-8B-dim oracle models, "
-              f"f16 activations); token = embed/head {1e3 * (a - t_layer):.1f} ms + 36 x layer "
-              f"{1e3 * t_layer:.1f} ms")
+    while time.perf_counter() - t0 < budget_s or not ts:
+        ts.append(per_token())
+    t_tok = statistics.median(ts)
+    sample = (f"{len(ts)} passes of 2 greedy tokens from a 1-token prompt on the 36-layer "
+              f"Qwen3-8B-dim oracle model ({act_name}; the layers share one layer's int8 weights); "
+              f"attention at context <= 2, so the GPU's 1024-token attention (about 4% of a token's "
+              f"multiply-adds) is not in the CPU time")
     return 1.0 / t_tok, t_tok, O.num_threads(), sample
 
 
@@ -853,15 +1032,20 @@ def cpu_attention_measure(budget_s):
         f"{passes} passes over {n} of the {wl.T} sequences (numpy) in {dt:.1f}s"
 
 
+_CPU_WORKLOADS = {}
+
+
 def cpu_measure(name, budget_s):
     if name == "attention_batched":
         return cpu_attention_measure(budget_s)
-    if name == "qwen3_decode":
-        return cpu_decode_measure(budget_s)
+    if name in ("qwen3_decode", "qwen3_generate"):
+        return cpu_decode_measure(budget_s, "f16")
+    if name == "qwen3_decode_bf16":
+        return cpu_decode_measure(budget_s, "bf16")
     if name == "llama_gguf_decode":
         return cpu_gguf_decode_measure(budget_s)
-    cw = CpuWorkload(name)
-    frac = 1.0 if name != "gguf_prefill" else 16 / 512  # 16 of the 512 rows per sample
+    cw = _CPU_WORKLOADS.get(name) or _CPU_WORKLOADS.setdefault(name, CpuWorkload(name))
+    frac = 1.0 if name not in ("gguf_prefill", "w8a16_prefill") else 16 / 512  # 16 of 512 rows
     cw.step(frac)  # warm-up
     t0 = time.perf_counter()
     n, work = 0, 0.0
@@ -878,6 +1062,11 @@ def cpu_measure(name, budget_s):
 
 def unit_scale(unit):
     return {"GB/s": 1e9, "TFLOP/s": 1e12}.get(unit, 1.0)
+
+
+def parallelism(wl, world):
+    pipelined = getattr(wl, "scaling", "weak") == "strong"
+    return f"pipeline x{world}" if pipelined else f"replicas x{world}"
 
 
 def run_reference(args, rank, world):
@@ -902,7 +1091,7 @@ def run_reference(args, rank, world):
         "ms_per_step": round(work / (value * unit_scale(wl.unit)) * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
         "data": getattr(wl, "data", DATA),
-        "config": {"workload": args.workload},
+        "config": dict(wl.describe(world), parallelism=parallelism(wl, world)),
         "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads, "kind": "port",
                          "sample": f"per step: {sample}"},
         "e2e": {"value": round(value, 4), "unit": wl.unit, "h2d_bytes_per_step": 0,
@@ -997,7 +1186,7 @@ def run_ours(args, rank, local, world):
     # (for the whole-model decode: the linears' bytes over their per-launch times)
     if hasattr(wl, "kernel_roofline"):
         achieved = wl.kernel_roofline()
-        wl.config["step_weight_GBps"] = round(
+        wl.details["step_weight_GBps"] = round(
             wl.weight_bytes * wl.copies_per_step / (statistics.mean(step_ms) / 1e3) / 1e9, 1)
     else:
         achieved = wl.work_per_step / (statistics.mean(step_ms) / 1e3) / unit_scale(wl.unit)
@@ -1010,7 +1199,7 @@ def run_ours(args, rank, local, world):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
         "higher_is_better": True, "scaling": "strong" if pipelined else "weak", "vs_baseline": None,
         "dtype": wl.dtype, "data": getattr(wl, "data", DATA),
-        "config": dict(wl.config, parallelism=(f"pipeline x{world}" if pipelined else f"replicas x{world}")),
+        "config": dict(wl.config, parallelism=parallelism(wl, world)),
         "roofline": {"bound": wl.bound, "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s" if wl.bound == "hbm" else "TFLOP/s",
                      "frac": round(achieved / peak, 4),
@@ -1020,6 +1209,8 @@ def run_ours(args, rank, local, world):
         "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(w0, w1),
     }
+    if getattr(wl, "details", None):
+        line["details"] = wl.details
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, _, threads, sample = cpu_measure(args.workload, args.cpu_budget)
         line["cpu_baseline"] = {"value": round(rate / unit_scale(wl.unit), 4), "unit": wl.unit,
@@ -1037,7 +1228,11 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen3_decode")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--split", choices=["planner", "even"], default=None,
+                    help="layer split of the pipeline workloads (default: the workload's)")
     args = ap.parse_args()
+    if args.split is not None and hasattr(WORKLOADS[args.workload], "split"):
+        WORKLOADS[args.workload].split = args.split
     rank, local, world = dist_setup()
     try:
         if args.impl == "reference":

@@ -765,9 +765,20 @@ constexpr int kXsSmem = kTmaSmem + kXsBytes + kXsAux;
 // its scale: for the normalised input that is estimated as max|h w| / rms (it
 // only picks a power of two).  Run by the CTA's first `active` threads; ends
 // with a barrier.
+// Staged chunk c (16 bytes, 8 activations) lives at slot xslot(c): within each
+// 128-wide K group the 16 chunks are stored transposed (chunk 4t + i at slot
+// 4i + t), so that the 4 lanes t of a fragment read load i at 4 consecutive
+// 16-byte slots -- 4 different bank groups -- instead of 64 bytes apart (a
+// two-way bank conflict).  Used when K % 128 == 0 (groups never straddle rows).
+__device__ __forceinline__ uint32_t xslot(uint32_t c) {
+  return (c & ~15u) | ((c & 3u) << 2) | ((c >> 2) & 3u);
+}
+
 template <bool BF16>
 __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* __restrict__ x, int M,
-                                          int K, uint32_t xsm, uint32_t aux, int active) {
+                                          int K, uint32_t xsm_base, uint32_t aux, int active) {
+  const bool perm = (K & 127) == 0;
+  auto xa = [&](int c) { return xsm_base + 16u * (perm ? xslot((uint32_t)c) : (uint32_t)c); };
   const uint32_t tm = aux + kAuxTm, tinv = aux + kAuxInv, tmul = aux + kAuxMul, cs = aux + kAuxCs;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarp = active >> 5;
   const int per_tok = K / 8, n16 = M * per_tok;
@@ -807,7 +818,7 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
       }
       const uint4 hv = pack8(o);
       if (blockIdx.x == 0 && p.h_out) *reinterpret_cast<uint4*>(p.h_out + off) = hv;
-      sts16(xsm + 16u * (uint32_t)c, hv);
+      sts16(xa(c), hv);
       sts32f(cs + 4u * (uint32_t)c, ss);
       amax(m, mx);
     }
@@ -827,7 +838,7 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
     put_mul();
     for (int c = tid; c < n16; c += active) {  // normalise in place, scaled to f16
       const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
-      const uint4 hv = lds16(xsm + 16u * (uint32_t)c), wv = ld_ro16(p.w + k8);
+      const uint4 hv = lds16(xa(c)), wv = ld_ro16(p.w + k8);
       const float inv = lds32f(tinv + 4u * m);
       const int e = BF16 ? tok_exp(lds32f(tm + 4u * m)) : 0;
       uint32_t o[8];
@@ -837,7 +848,7 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
             act_f32<BF16>(act_rnd<BF16>(act_f32<BF16>(h16(hv, i)) * inv * act_f32<BF16>(h16(wv, i))));
         o[i] = __half_as_ushort(__float2half_rn(BF16 ? ldexpf(v, -e) : v));
       }
-      sts16(xsm + 16u * (uint32_t)c, pack8(o));
+      sts16(xa(c), pack8(o));
     }
   } else {
     // x itself or swiglu(gate, up), rounded to the activation dtype.  f16: one
@@ -871,7 +882,7 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
           mx = fmaxf(mx, fabsf(v[i]));
           o[i] = act_rnd<BF16>(v[i]);
         }
-        if (p.mode != kProX) sts16(xsm + 16u * (uint32_t)c, pack8(o));
+        if (p.mode != kProX) sts16(xa(c), pack8(o));
         amax(c / per_tok, mx);
       }
       active_warps_sync(active);
@@ -880,7 +891,7 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
     for (int c = tid; c < n16; c += active) {
       float v[8];
       if (BF16 && p.mode != kProX) {
-        const uint4 yv = lds16(xsm + 16u * (uint32_t)c);
+        const uint4 yv = lds16(xa(c));
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(yv, i));
       } else {
@@ -890,7 +901,7 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
       uint32_t o[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = __half_as_ushort(__float2half_rn(BF16 ? ldexpf(v[i], -e) : v[i]));
-      sts16(xsm + 16u * (uint32_t)c, pack8(o));
+      sts16(xa(c), pack8(o));
     }
   }
   active_warps_sync(active);
@@ -985,12 +996,13 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     uint4 xv[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
-      if (XS) {
+      if (XS) {  // staged layout: see xslot (transposed chunks when K % 128 == 0)
         const uint32_t a = xo[j] + (uint32_t)(kb * 2);
-        xv[j][0] = (tv[j] && v0) ? lds16(a) : z;
-        xv[j][1] = (tv[j] && v0) ? lds16(a + 16) : z;
-        xv[j][2] = (tv[j] && v1) ? lds16(a + 32) : z;
-        xv[j][3] = (tv[j] && v1) ? lds16(a + 48) : z;
+        const uint32_t ci = (K & 127) == 0 ? 64u : 16u, c0 = (K & 127) == 0 ? (uint32_t)(16 * t) - (uint32_t)(64 * t) : 0u;
+        xv[j][0] = (tv[j] && v0) ? lds16(a + c0) : z;
+        xv[j][1] = (tv[j] && v0) ? lds16(a + c0 + ci) : z;
+        xv[j][2] = (tv[j] && v1) ? lds16(a + c0 + 2 * ci) : z;
+        xv[j][3] = (tv[j] && v1) ? lds16(a + c0 + 3 * ci) : z;
       } else {
         xv[j][0] = (tv[j] && v0) ? ld_ro16(xr[j] + kb) : z;
         xv[j][1] = (tv[j] && v0) ? ld_ro16(xr[j] + kb + 8) : z;
@@ -1030,6 +1042,153 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     }
   }
   if (cur >= 0) finish(cur);
+}
+
+// ------------------------------------------------------------------ decode GEMV, whole tiles per CTA
+// The decode linears (M <= 16 tokens, staged activations, K % 128 == 0, at
+// least one 16-row tile per CTA and one 128-wide K group per warp).  CTA c
+// takes the tiles c, c + C, ...; its warp j owns the K groups
+// [ng j / 8, ng (j + 1) / 8) of every tile and streams them through its own
+// 4-stage TMA ring, lane 0 issuing.  The warp's unit sequence (tile-major over
+// its groups) is plain arithmetic, so producer and consumer walk it with
+// counters and no per-stage bookkeeping.  Per 2 KB unit a lane loads its 64
+// weight bytes and converts them to f16 pairs before the warp releases the
+// stage (the conversions consume every loaded word), then issues its MMAs into
+// 4 independent accumulator chains.  Activation fragments are read for token
+// min(g, M - 1), so every MMA column holds a real (possibly repeated) token
+// and no load is predicated; the staged rows use the transposed chunk layout
+// (xslot), so those reads are free of bank conflicts.  The 8 partial tiles
+// meet in shared memory (cta_tile_finish).  (Splitting tiles between CTAs
+// balances the last wave but costs a GPU-scope fixup at each CTA's tail,
+// which measured slower for every decode shape.)
+template <int NT, bool BF16, typename ST>
+__global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
+    w8a16_gemv_kernel(const __grid_constant__ CUtensorMap wmap, const ST* __restrict__ scale,
+                      const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int N, int K,
+                      int tiles, int ng, int* err, ActPrologue pro) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (tma::smem_u32(smem_raw) + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const uint32_t ring = base + (uint32_t)(warp * kStages * kUnitBytes);
+  const uint32_t bars = base + (uint32_t)(kTmaWarps * kStages * kUnitBytes + warp * kStages * 8);
+  const uint32_t xsm = base + (uint32_t)(kTmaWarps * kStages * kUnitBytes + kTmaWarps * kStages * 8);
+  const uint32_t aux = xsm + kXsBytes, tm = aux + kAuxMul;
+  pdl_trigger();
+  const int C = gridDim.x;
+  const int g0 = ng * warp / kTmaWarps, g1 = ng * (warp + 1) / kTmaWarps, ngw = g1 - g0;
+  const int ntile = (tiles - (int)blockIdx.x + C - 1) / C;
+  const int U = ntile * ngw;  // this warp's units
+  // producer (lane 0): the next unit to issue and its (tile, group)
+  int pu = 0, ptile = blockIdx.x, pg = g0;
+  auto issue = [&](int st) {
+    const uint32_t bar = bars + 8u * (uint32_t)st;
+    tma::mbar_expect_tx(bar, kUnitBytes);
+    tma::load_2d(ring + (uint32_t)(st * kUnitBytes), &wmap, bar, pg * 128, ptile * 16);
+    ++pu;
+    if (++pg == g1) pg = g0, ptile += C;
+  };
+  if (lane == 0) {
+    tma::prefetch_map(&wmap);
+    for (int st = 0; st < kStages; ++st) tma::mbar_init(bars + 8u * st, 1);
+    tma::fence_barrier_init();
+    tma::fence_proxy_async();
+    // the weights are constant: start streaming before the previous kernel ends
+    for (int st = 0; st < kStages && pu < U; ++st) issue(st);
+  }
+  __syncwarp();
+  pdl_wait();  // x, y and h_out belong to the stream's earlier kernels
+  stage_act<BF16>(pro, x, M, K, xsm, aux, kTmaWarps * 32);
+  // this lane's activation fragment rows (token min(j * 8 + g, M - 1)); load i of
+  // lane t in group gi sits at slot 16 gi + 4 i + t of the token's row (xslot)
+  uint32_t xo[NT];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) xo[j] = xsm + (uint32_t)(min(j * 8 + g, M - 1) * K * 2 + 16 * t);
+  // this lane's weight chunks in a stage: rows g and g + 8, 16-byte chunks 2t and 2t+1 (SWIZZLE_128B)
+  const uint32_t w_lo0 = (uint32_t)(g * 128 + (((2 * t) ^ g) << 4));
+  const uint32_t w_lo1 = (uint32_t)(g * 128 + (((2 * t + 1) ^ g) << 4));
+  const uint32_t w_hi0 = w_lo0 + 8 * 128, w_hi1 = w_lo1 + 8 * 128;
+  auto store = [&](int tile, const float (&a)[NT][4]) {
+    float b[NT][4];  // undo the per-token power-of-two scale of the staged activations
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int t0 = j * 8 + 2 * t;
+      const float m0 = t0 < M ? lds32f(tm + 4u * t0) : 1.0f, m1 = t0 + 1 < M ? lds32f(tm + 4u * (t0 + 1)) : 1.0f;
+      b[j][0] = a[j][0] * m0, b[j][1] = a[j][1] * m1, b[j][2] = a[j][2] * m0, b[j][3] = a[j][3] * m1;
+    }
+    w8a16_store<NT, BF16, ST>(b, scale, y, M, N, tile * 16);
+  };
+  const uint32_t part = aux + kAuxCs, ctr = aux + kAuxCnt;
+  // kChains independent accumulator chains (MMA m of a unit feeds chain m %
+  // kChains): one chain would serialise a tile's MMAs on the tensor pipe's latency
+  constexpr int kChains = 4;
+  float acc[kChains][NT][4];
+#pragma unroll
+  for (int q = 0; q < kChains; ++q) zero_acc(acc[q]);
+  int ctile = blockIdx.x, cg = g0, lt = 0;
+  for (int u0 = 0; u0 < U; u0 += kStages) {
+    const uint32_t par = (uint32_t)((u0 / kStages) & 1);
+#pragma unroll
+    for (int st = 0; st < kStages; ++st) {
+      if (u0 + st >= U) break;
+      if (!__all_sync(0xffffffffu, tma::mbar_wait(bars + 8u * st, par, err))) {
+        if (lane == 0) {  // wait (bounded) for this warp's copies still in flight
+          const unsigned long long deadline = tma::global_ns() + tma::kWaitNs;
+          for (int v = u0 + st; v < pu; ++v)
+            if (!tma::mbar_drain(bars + 8u * (uint32_t)(v & (kStages - 1)), (uint32_t)((v / kStages) & 1),
+                                 deadline))
+              break;
+        }
+        return;
+      }
+      const uint32_t sb = ring + (uint32_t)(st * kUnitBytes);
+      const uint4 al0 = lds16(sb + w_lo0), al1 = lds16(sb + w_lo1);
+      const uint4 ah0 = lds16(sb + w_hi0), ah1 = lds16(sb + w_hi1);
+      uint4 xv[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const uint32_t a = xo[j] + (uint32_t)(cg * 256);
+        xv[j][0] = lds16(a);
+        xv[j][1] = lds16(a + 64);
+        xv[j][2] = lds16(a + 128);
+        xv[j][3] = lds16(a + 192);
+      }
+      // exact f16 weight pairs (this consumes every word loaded from the stage)
+      uint32_t fa[2][4][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          i8x4_to_f16x2(word(h ? al1 : al0, k), fa[h][k][0], fa[h][k][2]);
+          i8x4_to_f16x2(word(h ? ah1 : ah0, k), fa[h][k][1], fa[h][k][3]);
+        }
+      __syncwarp();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (lane == 0 && pu < U) issue(st);  // the stage is free: refill it with unit u + 4
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const uint4& xs = xv[j][2 * h + (k >> 1)];
+            mma_f16(acc[(h * 4 + k) % kChains][j], fa[h][k][0], fa[h][k][1], fa[h][k][2], fa[h][k][3],
+                    word(xs, 2 * (k & 1)), word(xs, 2 * (k & 1) + 1));
+          }
+      if (++cg == g1) {  // the end of this warp's part of the tile
+#pragma unroll
+        for (int q = 1; q < kChains; ++q)
+#pragma unroll
+          for (int jj = 0; jj < NT; ++jj)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[0][jj][e] += acc[q][jj][e];
+        cta_tile_finish<NT>(part, ctr, lt++, ctile, acc[0], store, err);
+#pragma unroll
+        for (int q = 0; q < kChains; ++q) zero_acc(acc[q]);
+        cg = g0;
+        ctile += C;
+      }
+    }
+  }
 }
 
 template <int NT, int TYPE, typename YT>
@@ -1321,6 +1480,36 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
     if (s != DIAL_OK) return s;
     const bool xs = M * K * 2 <= kXsBytes && aligned16(x);
     const GemvPlan pl = plan_gemv(tiles, ng, xs && nt <= 2);
+    int* err0 = device_error_ptr();
+    if (!err0) return fail(DIAL_ERR_CUDA, "device error flag is unavailable");
+    // the decode GEMV: whole tiles per CTA (K a multiple of 128: its activation
+    // fragments are read unpredicated from the staged rows)
+    if (pl.mode == kTileCta && K % 128 == 0) {
+      const int C = (int)std::min<int64_t>(tiles, (int64_t)sm_count() * kCtasPerSM);
+      const size_t smem = (size_t)kTmaSmem + kXsBytes + kXsAux;
+      cudaError_t ae = cudaSuccess;
+#define GV(NT_, BF, ST)                                                                            \
+  ae = ensure_smem<w8a16_gemv_kernel<NT_, BF, ST>>((int)smem);                                     \
+  if (ae == cudaSuccess)                                                                           \
+    s = launch_pdl("w8a16_gemv_kernel", w8a16_gemv_kernel<NT_, BF, ST>, dim3((unsigned)C),         \
+                   dim3(kTmaWarps * 32), smem, st, map, static_cast<const ST*>(scale), xp, yp,     \
+                   (int)M, (int)N, (int)K, (int)tiles, (int)ng, err0, pro)
+#define GV_NT(BF, ST)     \
+  if (nt == 1) {          \
+    GV(1, BF, ST);        \
+  } else {                \
+    GV(2, BF, ST);        \
+  }
+      if (sdt == DIAL_F32) {
+        if (bf) { GV_NT(true, float) } else { GV_NT(false, float) }
+      } else {
+        if (bf) { GV_NT(true, __half) } else { GV_NT(false, __half) }
+      }
+#undef GV_NT
+#undef GV
+      if (ae != cudaSuccess) return cuda_fail(ae, "cudaFuncSetAttribute(w8a16_gemv_kernel)");
+      return s;
+    }
     float* slots = static_cast<float*>(sk_ws);
     int* cnt = reinterpret_cast<int*>(static_cast<uint8_t*>(sk_ws) + slot_bytes());
     int* err = device_error_ptr();

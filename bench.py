@@ -607,9 +607,10 @@ class QwenDecode:
     kernel = "w8a16_tma_kernel<NT=1> (the stage's linears from one graph, events)"
     graph = True
     scaling = "strong"
-    # DRAM bytes per token of the stage's linears on one GPU: ncu DRAM bytes per
-    # 2 KB weight unit of one captured GEMV launch, times the token's units
-    traffic = 7_596_160_192
+    # DRAM bytes per token of the stage's linears on one GPU: the DRAM read + write
+    # bytes of one captured 12288 x 4096 decode GEMV launch (50,425,088 B over its
+    # 24,576 weight units of 2 KB) times the token's 3,695,360 units
+    traffic = 7_582_147_346
     n_seqs, mb_size, prompt_len, decode_cap = 8, 1, 1024, 448
     head_layers = 3.2  # the output head's cost in layers (weights read per token)
     copies_per_step = 8  # one graph per micro-batch
@@ -649,7 +650,7 @@ class QwenDecode:
 
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
         from dial_cuda.model import Stage
-        from dial_cuda.pipeline import ModelStageCompute, Pipeline, TorchChannel
+        from dial_cuda.pipeline import ModelStageCompute, NcclChannel, Pipeline
         self.torch, self.D, self.rank, self.world = torch, D, rank, world
         self.cfg = self.model_config()
         self.mb_size = self.micro_batch(world)
@@ -660,7 +661,8 @@ class QwenDecode:
         self.stage = Stage(self.cfg, rr.start, rr.stop, n_slots=self.n_seqs, max_seq=self.max_seq)
         st = self.stage
         self.comp = ModelStageCompute(st, n_mb, self.prompt_len, mb_size=self.mb_size)
-        self.pipe = Pipeline(rank, world, self.comp, TorchChannel() if world > 1 else None, n_mb)
+        self.channel = NcclChannel(rank, world) if world > 1 else None  # C-ABI stage communicators
+        self.pipe = Pipeline(rank, world, self.comp, self.channel, n_mb)
         prompts = None
         if rank == 0:
             g = torch.Generator(device="cuda").manual_seed(SEED)
@@ -718,6 +720,10 @@ class QwenDecode:
 
     def finish(self):
         self.pipe.finish()
+
+    def close(self):
+        if self.channel is not None:
+            self.channel.close()
 
     def kernel_roofline(self, reps: int = 5):
         """HBM GB/s of the dominant kernel: this stage's linears (M = one
@@ -1211,6 +1217,8 @@ def run_ours(args, rank, local, world):
     }
     if getattr(wl, "details", None):
         line["details"] = wl.details
+    if hasattr(wl, "close"):
+        wl.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, _, threads, sample = cpu_measure(args.workload, args.cpu_budget)
         line["cpu_baseline"] = {"value": round(rate / unit_scale(wl.unit), 4), "unit": wl.unit,

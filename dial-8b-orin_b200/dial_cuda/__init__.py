@@ -46,6 +46,8 @@ _lib: Optional[ctypes.CDLL] = None
 
 # name -> (argtypes, restype); kept in the order of include/dial_cuda.h
 _vp, _i64, _i32, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+ID_BYTES = 128  # DIAL_STAGE_COMM_ID_BYTES
+
 SIGNATURES = {
     "dial_status_string": ([_i32], ctypes.c_char_p),
     "dial_last_error": ([], ctypes.c_char_p),
@@ -78,6 +80,12 @@ SIGNATURES = {
     "dial_swiglu": ([_vp, _vp, _i32, _i64, _i64, _vp], _i32),
     "dial_embedding": ([_vp, _vp, _vp, _i32, _i64, _i64, _i64, _vp], _i32),
     "dial_argmax": ([_vp, _vp, _i32, _i64, _i64, _vp], _i32),
+    "dial_stage_comm_unique_id": ([_vp], _i32),
+    "dial_stage_comm_init": ([_vp, _i32, _i32, _i32, ctypes.c_double, ctypes.POINTER(_vp)], _i32),
+    "dial_stage_comm_send": ([_vp, _vp, _sz, _i32, _vp], _i32),
+    "dial_stage_comm_recv": ([_vp, _vp, _sz, _i32, _vp], _i32),
+    "dial_stage_comm_wait": ([_vp, _vp], _i32),
+    "dial_stage_comm_destroy": ([_vp], _i32),
 }
 
 

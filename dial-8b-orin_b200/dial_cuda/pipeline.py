@@ -19,9 +19,10 @@ asynchronous (a send buffer is reused only after its previous send finished)
 and each stage pair has its own channel, so the token ring back to stage 0
 cannot block the forward chain.
 
-The communication is a `Channel` object: TorchChannel (torch.distributed
-point-to-point; NCCL over NVLink on GPUs, gloo for the CPU tests).  The compute
-of a stage is a `StageCompute` object; ModelStageCompute runs a model.Stage.
+The communication is a `Channel` object: NcclChannel (the C ABI's NCCL stage
+communicators, dial_stage_comm_*, over NVLink between GPUs) or TorchChannel
+(torch.distributed point-to-point; gloo for the CPU tests).  The compute of a
+stage is a `StageCompute` object; ModelStageCompute runs a model.Stage.
 """
 from __future__ import annotations
 
@@ -64,6 +65,89 @@ class TorchChannel:
 
     def irecv(self, t, src: int):
         return self.dist.irecv(t, src, group=self._group(src, self.rank))
+
+
+class _Done:
+    """A transfer enqueued on a link's stream: wait() orders the caller's
+    current stream after it (the host does not block)."""
+
+    def __init__(self, event):
+        self.event = event
+
+    def wait(self):
+        _torch().cuda.current_stream().wait_event(self.event)
+
+
+class NcclChannel:
+    """The pipeline's links over the C ABI's NCCL stage communicators
+    (dial_stage_comm_*): link s carries stage s -> s+1, the last link the token
+    ring from stage P-1 to stage 0.  Each link is a two-rank communicator (link
+    rank 0 = its sender) with its own CUDA stream, so a transfer waiting on one
+    link never holds up another.  Each link's sender makes the clique id; the
+    ids are shared with one all_gather_object on the default torch.distributed
+    group (bootstrap only: no tensor crosses it).  Every rank initialises its
+    links in the global link order, so no two ranks wait on each other's
+    initialisation in a cycle; every host wait is bounded by `timeout_s`."""
+
+    def __init__(self, rank: int, world: int, timeout_s: float = 60.0):
+        import ctypes  # noqa: PLC0415
+
+        import torch.distributed as dist  # noqa: PLC0415
+
+        from . import ID_BYTES, check, lib  # noqa: PLC0415
+        torch = _torch()
+        self.rank, self.P, self.L = rank, world, lib()
+        self.links = [(s, s + 1) for s in range(world - 1)] + ([(world - 1, 0)] if world > 1 else [])
+        mine = {}
+        for i, (a, _) in enumerate(self.links):
+            if a == rank:
+                buf = (ctypes.c_uint8 * ID_BYTES)()
+                check(self.L.dial_stage_comm_unique_id(buf), "dial_stage_comm_unique_id")
+                mine[i] = bytes(buf)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, mine)
+        ids = {}
+        for d in gathered:
+            ids.update(d)
+        dev = torch.cuda.current_device()
+        self.comms = {}  # link index -> (communicator, stream, my rank in the link)
+        for i, (a, b) in enumerate(self.links):
+            if rank not in (a, b):
+                continue
+            lr = 0 if rank == a else 1
+            comm = ctypes.c_void_p()
+            idbuf = (ctypes.c_uint8 * ID_BYTES).from_buffer_copy(ids[i])
+            check(self.L.dial_stage_comm_init(idbuf, lr, 2, dev, timeout_s, ctypes.byref(comm)),
+                  f"dial_stage_comm_init(link {a}->{b})")
+            self.comms[i] = (comm, torch.cuda.Stream(device=dev), lr)
+
+    def _link(self, a: int, b: int) -> int:
+        return self.links.index((a, b))
+
+    def _op(self, fn, t, link: int, where: str):
+        from . import check  # noqa: PLC0415
+        torch = _torch()
+        comm, stream, lr = self.comms[link]
+        stream.wait_stream(torch.cuda.current_stream())  # the buffer's producers (or readers)
+        check(fn(comm, t.data_ptr(), t.numel() * t.element_size(), 1 - lr, stream.cuda_stream), where)
+        t.record_stream(stream)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        return _Done(ev)
+
+    def isend(self, t, dst: int):
+        return self._op(self.L.dial_stage_comm_send, t, self._link(self.rank, dst), "dial_stage_comm_send")
+
+    def irecv(self, t, src: int):
+        return self._op(self.L.dial_stage_comm_recv, t, self._link(src, self.rank), "dial_stage_comm_recv")
+
+    def close(self) -> None:
+        """Waits (bounded) for each link's transfers, then frees its communicator."""
+        from . import check  # noqa: PLC0415
+        for comm, stream, _ in self.comms.values():
+            check(self.L.dial_stage_comm_wait(comm, stream.cuda_stream), "dial_stage_comm_wait")
+            check(self.L.dial_stage_comm_destroy(comm), "dial_stage_comm_destroy")
+        self.comms = {}
 
 
 def init_distributed(backend: str = "nccl", timeout_s: float = 120.0):

@@ -406,6 +406,45 @@ DIAL_API dial_status dial_plan_stages(const dial_plan_model* model, const dial_p
                                       const dial_plan_device* devices, int n_devices, int algorithm,
                                       dial_plan_result* out);
 
+/* ------------------------------------------------------------------ stage hand-off
+ * The pipeline's links over NCCL, replacing the reference's serialised TCP
+ * hand-off between master and workers: RawTensor::{from_tensor, to_tensor}
+ * (dial-core/src/spm/proto/message.rs:147-165) and its framing (:366-408),
+ * Client::forward_batch / request (spm/client.rs:389-452, :281-329) and the
+ * worker loop (spm/worker.rs:645-765).  One communicator per link (stage s ->
+ * s + 1, and the token ring from the last stage to stage 0), two ranks each;
+ * transfers are device to device and enqueued on the caller's stream.
+ *
+ * NCCL is loaded at run time (libnccl.so.2, reusing a copy the process has
+ * already loaded); without it these calls return DIAL_ERR_NCCL.  A process
+ * that also loads its own NCCL (PyTorch bundles one) should load that first:
+ * two libraries with the soname libnccl.so.2 cannot coexist.
+ * Communicators are non-blocking: initialisation, a link's first transfer
+ * (NCCL connects a link there, which needs the peer's matching call) and
+ * teardown are polled against `timeout_s` of host time and return
+ * DIAL_ERR_TIMEOUT (the communicator is then aborted) instead of hanging.
+ * After a failure the communicator only accepts dial_stage_comm_destroy. */
+#define DIAL_STAGE_COMM_ID_BYTES 128
+typedef struct dial_stage_comm dial_stage_comm;
+
+/* A new clique id (DIAL_STAGE_COMM_ID_BYTES bytes, host memory), made by one
+ * rank of a link and handed to the other out of band. */
+DIAL_API dial_status dial_stage_comm_unique_id(uint8_t* id_out);
+/* Joins the clique as `rank` of `nranks` on CUDA device `device` (made
+ * current); returns once every rank has joined, or DIAL_ERR_TIMEOUT. */
+DIAL_API dial_status dial_stage_comm_init(const uint8_t* unique_id, int rank, int nranks, int device,
+                                          double timeout_s, dial_stage_comm** out);
+/* `bytes` from device memory `buf` to rank `peer`, enqueued on `stream`. */
+DIAL_API dial_status dial_stage_comm_send(dial_stage_comm* comm, const void* buf, size_t bytes,
+                                          int peer, dial_stream stream);
+/* `bytes` from rank `peer` into device memory `buf`, enqueued on `stream`. */
+DIAL_API dial_status dial_stage_comm_recv(dial_stage_comm* comm, void* buf, size_t bytes, int peer,
+                                          dial_stream stream);
+/* Host wait (bounded by the communicator's timeout) until `stream` is idle. */
+DIAL_API dial_status dial_stage_comm_wait(dial_stage_comm* comm, dial_stream stream);
+/* Finalises (bounded) and frees the communicator; NULL is a no-op. */
+DIAL_API dial_status dial_stage_comm_destroy(dial_stage_comm* comm);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -3,8 +3,10 @@
 - One stage (world 1): the pipeline's schedule and CUDA graphs give the same
   greedy tokens as Decoder.prefill/decode_step.
 - Two stages over NCCL (needs 2 GPUs; skipped otherwise): each rank holds half
-  the layers, and the tokens equal the single-GPU ones (the weights of a layer
-  do not depend on the split, and the arithmetic of a layer is the same).
+  the layers, the hand-off runs through the C ABI's stage communicators
+  (dial_stage_comm_*), and the tokens equal the single-GPU ones (the weights of
+  a layer do not depend on the split, and the arithmetic of a layer is the
+  same).
 """
 import json
 import os
@@ -112,14 +114,15 @@ def _two_stage_worker():
     import torch
 
     from dial_cuda.model import Stage
-    from dial_cuda.pipeline import ModelStageCompute, Pipeline, TorchChannel, init_distributed
+    from dial_cuda.pipeline import ModelStageCompute, NcclChannel, Pipeline, init_distributed
     rank, local, world = init_distributed("nccl", timeout_s=60)
     cfg = _cfg()
     half = cfg.n_layers // 2
     a, b = (0, half) if rank == 0 else (half, cfg.n_layers)
     st = Stage(cfg, a, b, n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
     comp = ModelStageCompute(st, N_MB, PROMPT)
-    pipe = Pipeline(rank, world, comp, TorchChannel(), N_MB)
+    ch = NcclChannel(rank, world, timeout_s=60.0)  # the C ABI's stage communicators
+    pipe = Pipeline(rank, world, comp, ch, N_MB)
     pipe.prefill(_prompts(torch) if rank == 0 else None, prompt_len=PROMPT)
     firsts = [int(t.item()) for t in comp.tokens]
     saved = [t.clone() for t in comp.tokens]
@@ -130,6 +133,7 @@ def _two_stage_worker():
     torch.cuda.synchronize()
     last = [int(t.item()) for t in comp.tokens]
     pipe.finish()
+    ch.close()
     import torch.distributed as dist
     dist.barrier()
     with open(os.path.join(os.environ["DIAL_TEST_OUT"], f"rank{rank}.json"), "w") as f:

@@ -85,6 +85,39 @@ dial_status dial_attention(const void* q, const void* k_cache, const void* v_cac
                           n_heads, n_kv_heads, max_seq, max_len, as_stream(stream));
 }
 
+size_t dial_decode_attention_workspace_bytes(int n_heads, int64_t max_len) {
+  if (n_heads <= 0 || max_len <= 0) return 0;
+  return attention_decode_workspace_bytes(n_heads, max_len);
+}
+
+dial_status dial_decode_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                                  const void* cos_t, const void* sin_t, const int32_t* positions,
+                                  const int32_t* slots, void* k_cache, void* v_cache, void* out,
+                                  void* workspace, size_t workspace_bytes, dial_dtype dt,
+                                  int n_heads, int n_kv_heads, int head_dim, int64_t max_seq,
+                                  int64_t max_len, float eps, int qk_norm, dial_stream stream) {
+  clear_error();
+  if (!qkv || !cos_t || !sin_t || !positions || !slots || !k_cache || !v_cache || !out || !workspace)
+    return fail(DIAL_ERR_INVALID_ARG, "null pointer");
+  if (qk_norm && (!q_norm_w || !k_norm_w)) return fail(DIAL_ERR_INVALID_ARG, "null norm weight");
+  if (max_seq <= 0 || max_len <= 0 || max_len > max_seq)
+    return fail(DIAL_ERR_INVALID_ARG, "bad sizes (need 0 < max_len <= max_seq)");
+  if (dt != DIAL_F16 && dt != DIAL_BF16) return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "f16/bf16 only");
+  dial_status s = check_heads(n_heads, n_kv_heads, head_dim);
+  if (s != DIAL_OK) return s;
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(DIAL_ERR_MISALIGNED, "caches must be 16-byte aligned");
+  const size_t need = attention_decode_workspace_bytes(n_heads, max_len);
+  if (workspace_bytes < need)
+    return fail(DIAL_ERR_INVALID_ARG, "decode attention workspace must hold %zu bytes", need);
+  if (!aligned16(workspace)) return fail(DIAL_ERR_MISALIGNED, "workspace must be 16-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* ctr = reinterpret_cast<int*>(ws + need - (size_t)n_heads * sizeof(int));
+  return launch_attention_decode(qkv, q_norm_w, k_norm_w, cos_t, sin_t, positions, slots, k_cache,
+                                 v_cache, out, ws, ctr, dt, 1, n_heads, n_kv_heads, max_seq,
+                                 max_len, eps, qk_norm, as_stream(stream));
+}
+
 dial_status dial_swiglu(const void* gate_up, void* out, dial_dtype dt, int64_t tokens,
                         int64_t intermediate, dial_stream stream) {
   clear_error();

@@ -26,6 +26,7 @@ size_t al256(size_t b) { return (b + 255) / 256 * 256; }
 
 struct Ws {
   uint8_t* sk;      // stream-K scratch shared by every linear (zero counters between calls)
+  int* actr;        // decode attention split counters (zero between calls)
   uint8_t* x1;      // [T, H]
   uint8_t* qkv;     // [T, (Hq+2Hkv)D]
   uint8_t* q;       // [T, Hq D]
@@ -53,6 +54,7 @@ Ws layout(const dial_decoder_dims& d, int64_t T, int64_t max_len, uint8_t* base)
   };
   const int64_t nmax = std::max<int64_t>(std::max<int64_t>(QKV, 2 * I), std::max<int64_t>(H, d.vocab));
   w.sk = take(gemv_workspace_bytes(nmax));  // first, so its place does not depend on T
+  w.actr = reinterpret_cast<int*>(take((size_t)d.n_heads * sizeof(int)));  // as fixed
   w.x1 = take(T * H * e);
   w.qkv = take(T * QKV * e);
   w.q = take(T * QD * e);
@@ -187,13 +189,21 @@ dial_status dial_decoder_layers(const dial_decoder_dims* dims, const dial_layer_
                       st, &rms1)) != DIAL_OK)
         return s;
       if (li) h_cur = h_next, h_next = h_cur == h_buf[0] ? h_buf[1] : h_buf[0];
-      if ((s = launch_qk_rope_kv(w.qkv, L.q_norm, L.k_norm, cos_t, sin_t, positions, slots, w.q,
-                                 L.k_cache, L.v_cache, dt, T, d.n_heads, d.n_kv_heads, d.max_seq,
-                                 d.rms_eps, d.qk_norm, st)) != DIAL_OK)
-        return s;
-      if ((s = launch_attention(w.q, L.k_cache, L.v_cache, positions, slots, w.attn, w.attn_ws, dt, T,
-                                d.n_heads, d.n_kv_heads, d.max_seq, max_len, st)) != DIAL_OK)
-        return s;
+      if (T == 1) {  // one sequence's next token: QK-norm, RoPE, append and attention in one launch
+        if ((s = launch_attention_decode(w.qkv, L.q_norm, L.k_norm, cos_t, sin_t, positions, slots,
+                                         L.k_cache, L.v_cache, w.attn, w.attn_ws, w.actr, dt, T,
+                                         d.n_heads, d.n_kv_heads, d.max_seq, max_len, d.rms_eps,
+                                         d.qk_norm, st)) != DIAL_OK)
+          return s;
+      } else {
+        if ((s = launch_qk_rope_kv(w.qkv, L.q_norm, L.k_norm, cos_t, sin_t, positions, slots, w.q,
+                                   L.k_cache, L.v_cache, dt, T, d.n_heads, d.n_kv_heads, d.max_seq,
+                                   d.rms_eps, d.qk_norm, st)) != DIAL_OK)
+          return s;
+        if ((s = launch_attention(w.q, L.k_cache, L.v_cache, positions, slots, w.attn, w.attn_ws, dt,
+                                  T, d.n_heads, d.n_kv_heads, d.max_seq, max_len, st)) != DIAL_OK)
+          return s;
+      }
       if ((s = linear(d, d.weight_format, L.o, w.attn, w.delta, T, QD, H, w.lin_ws, w.sk, st)) != DIAL_OK)
         return s;
       const ActPrologue rms2{kProRms, static_cast<const uint16_t*>(h_cur), static_cast<uint16_t*>(h_next),

@@ -86,6 +86,38 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_kernel(const T* x,  // x/res 
 }
 
 // ------------------------------------------------------------------ QK-norm + RoPE + KV append
+// One head of 128 values by one warp: lane l owns elements {l, l+32, l+64,
+// l+96}, so both RoPE pairs (i, i+64) stay in the lane.  Optional RMSNorm over
+// the head (rounded to T), then RoPE at the position whose table rows are
+// cr / sr, with every product and the sum in T as candle's rope evaluates them
+// over T tensors (a product of two T values is exact in f32, so rounding it to
+// T is the T multiplication).  o[i] = the T-rounded result of element lane + 32 i.
+template <typename T>
+__device__ __forceinline__ void head_norm_rope_warp(const T* __restrict__ src, const T* __restrict__ nw,
+                                                    int qk_norm, float eps, const T* __restrict__ cr,
+                                                    const T* __restrict__ sr, float (&o)[4]) {
+  constexpr int D = 128;
+  const int lane = threadIdx.x & 31;
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = ld(src, lane + 32 * i);
+  if (qk_norm) {
+    const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+    const float inv = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      v[i] = Act<T>::to_f32(rnd<T>(v[i] * inv * ld(nw, lane + 32 * i)));  // normed tensor in T
+  }
+  auto r = [](float a) { return Act<T>::to_f32(rnd<T>(a)); };
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int e = lane + 32 * i;  // 0..63
+    const float c = ld(cr, e), sn = ld(sr, e);
+    o[i] = r(r(v[i] * c) - r(v[i + 2] * sn));
+    o[i + 2] = r(r(v[i] * sn) + r(v[i + 2] * c));
+  }
+}
+
 // One warp per (token, head) over Hq + 2*Hkv heads; lane l owns elements
 // {l, l+32, l+64, l+96} of the 128-wide head, so both RoPE pairs (i, i+64)
 // stay in the lane.  head_dim is fixed to 128 (Qwen3-8B / Llama-3-8B).
@@ -117,29 +149,10 @@ __global__ void qk_rope_kv_kernel(const T* __restrict__ qkv, const T* __restrict
     return;
   }
   const bool is_q = h < hq;
-  if (qk_norm) {
-    const T* nw = is_q ? qn : kn;
-    const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
-    const float inv = rsqrtf(ss / (float)D + eps);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      v[i] = Act<T>::to_f32(rnd<T>(v[i] * inv * ld(nw, lane + 32 * i)));  // normed tensor in T
-  }
-  // rotate_half: out[i] = x[i] c_i - x[i+64] s_i ; out[i+64] = x[i] s_i + x[i+64] c_i,
-  // every product and the sum in T as candle's rope evaluates them over T
-  // tensors (a product of two T values is exact in f32, so rounding it to T is
-  // the T multiplication)
-  const T* cr = cos_t + (int64_t)p * (D / 2);
-  const T* sr = sin_t + (int64_t)p * (D / 2);
-  auto r = [](float a) { return Act<T>::to_f32(rnd<T>(a)); };
+  // rotate_half: out[i] = x[i] c_i - x[i+64] s_i ; out[i+64] = x[i] s_i + x[i+64] c_i
   float o[4];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int e = lane + 32 * i;  // 0..63
-    const float c = ld(cr, e), sn = ld(sr, e);
-    o[i] = r(v[i] * c) - r(v[i + 2] * sn);
-    o[i + 2] = r(v[i] * sn) + r(v[i + 2] * c);
-  }
+  head_norm_rope_warp<T>(src, is_q ? qn : kn, qk_norm, eps, cos_t + (int64_t)p * (D / 2),
+                         sin_t + (int64_t)p * (D / 2), o);
   T* dst = is_q ? q_out + (t * hq + h) * D : kc + ((s * hkv + (h - hq)) * max_seq + p) * D;
 #pragma unroll
   for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = rnd<T>(o[i]);
@@ -261,17 +274,42 @@ __device__ __forceinline__ void split_pair3(float a, float b, uint32_t& hi, uint
        ((uint32_t)(*reinterpret_cast<const uint16_t*>(&hb)) << 16);
 }
 
-template <typename T, int REP>
+// Inputs of the decode form (FUSE): the raw qkv rows, the QK-norm gains, the
+// RoPE tables, and the caches to append the new key / value rows to.
+template <typename T>
+struct QkvIn {
+  const T* qkv;
+  const T* qn;
+  const T* kn;
+  const T* cos_t;
+  const T* sin_t;
+  T* kc;
+  T* vc;
+  int* ctr;  // [tokens * hkv] split arrival counters, zero between launches
+  float eps;
+  int qk_norm;
+};
+
+// FUSE (decode, one token per sequence): the CTA computes its REP query heads'
+// QK-norm + RoPE from the raw qkv row itself (head_norm_rope_warp, the same
+// arithmetic as qk_rope_kv_kernel), the split that holds the new position
+// appends the token's key (normed, rotated) and value rows to the caches before
+// reading its tiles, and the last of the (token, kv head)'s splits to finish
+// (an arrival counter, no waiting) merges the splits' partials exactly as
+// attention_combine_kernel does -- no qk_rope and no combine launch.
+template <typename T, int REP, bool FUSE>
 __global__ void __launch_bounds__(kTcWarps * 32)
     attention_tc_kernel(const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
                         const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
                         T* __restrict__ out, float* __restrict__ part, int hq, int hkv,
-                        int64_t max_seq, int nsplit, float qscale) {
+                        int64_t max_seq, int nsplit, float qscale, QkvIn<T> in) {
   pdl_begin();
   constexpr int D = 128;
   extern __shared__ __align__(1024) uint8_t tc_smem[];
   __shared__ float sm_m[kTcWarps][REP], sm_l[kTcWarps][REP];
   __shared__ float sm_o[kTcWarps][REP][D];
+  __shared__ __align__(16) T sm_q[FUSE ? REP : 1][D];
+  __shared__ int sm_last;
   const int64_t t = blockIdx.x;
   const int g = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -284,13 +322,43 @@ __global__ void __launch_bounds__(kTcWarps * 32)
   const T* vbase = vc + ((s * hkv + g) * max_seq) * D;
   const uint32_t wbuf = smem_addr(tc_smem) + (uint32_t)(warp * kTcWarpBytes);
 
+  if constexpr (FUSE) {
+    const int p = len - 1;
+    const T* src = in.qkv + t * (int64_t)(hq + 2 * hkv) * D;
+    const T* cr = in.cos_t + (int64_t)p * (D / 2);
+    const T* sr = in.sin_t + (int64_t)p * (D / 2);
+    for (int h = warp; h < REP; h += kTcWarps) {  // this group's query heads
+      float o[4];
+      head_norm_rope_warp<T>(src + (int64_t)(g * REP + h) * D, in.qn, in.qk_norm, in.eps, cr, sr, o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sm_q[h][lane + 32 * i] = rnd<T>(o[i]);
+    }
+    if (p >= k0 && p < k1) {  // the split holding the new position appends its key and value rows
+      if (warp == kTcWarps - 1) {
+        float o[4];
+        head_norm_rope_warp<T>(src + (int64_t)(hq + g) * D, in.kn, in.qk_norm, in.eps, cr, sr, o);
+        T* dst = in.kc + ((s * hkv + g) * max_seq + p) * D;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = rnd<T>(o[i]);
+      } else if (warp == kTcWarps - 2) {
+        const T* vs = src + (int64_t)(hq + hkv + g) * D;
+        T* dst = in.vc + ((s * hkv + g) * max_seq + p) * D;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = vs[lane + 32 * i];
+      }
+      __threadfence();  // the rows are read back below through cp.async (L2)
+    }
+    __syncthreads();
+  }
+
   // Q fragments: row gr = query head g*REP + gr (zero above REP), k-step ks
   uint32_t qa[8][2];
 #pragma unroll
   for (int ks = 0; ks < 8; ++ks) {
     qa[ks][0] = qa[ks][1] = 0u;
     if (gr < REP) {
-      const uint32_t* qr = reinterpret_cast<const uint32_t*>(q + (t * hq + g * REP + gr) * D);
+      const uint32_t* qr = FUSE ? reinterpret_cast<const uint32_t*>(&sm_q[FUSE ? gr : 0][0])
+                                : reinterpret_cast<const uint32_t*>(q + (t * hq + g * REP + gr) * D);
       qa[ks][0] = qr[(16 * ks + 2 * qd) >> 1];
       qa[ks][1] = qr[(16 * ks + 8 + 2 * qd) >> 1];
     }
@@ -435,6 +503,58 @@ __global__ void __launch_bounds__(kTcWarps * 32)
       }
       pp[2 + d] = O;
     }
+  }
+  if constexpr (FUSE) {
+    if (nsplit == 1) return;
+    // the last split of this (token, kv head) to arrive merges the partials
+    __threadfence();
+    __syncthreads();
+    int* ctr = in.ctr + t * hkv + g;
+    if (threadIdx.x == 0) sm_last = atomicAdd(ctr, 1) == nsplit - 1;
+    __syncthreads();
+    if (!sm_last) return;
+    __threadfence();
+    // the arithmetic of attention_combine_kernel in its order, with the loads
+    // of all splits issued together: per head, a warp finds the maximum, the
+    // split weights f_c = 2^(m_c - m) and the sum; then every output element
+    // accumulates its splits' O in split order
+    __shared__ float sm_f[REP][32];
+    __shared__ float sm_sum[REP];
+    __shared__ unsigned sm_valid[REP];
+    for (int r = warp; r < REP; r += kTcWarps) {
+      const float* pp = part + (t * hq + g * REP + r) * nsplit * (D + 2);
+      const float cm = lane < nsplit ? __ldcg(pp + lane * (D + 2)) : -FLT_MAX;
+      const float cl = lane < nsplit ? __ldcg(pp + lane * (D + 2) + 1) : 0.f;
+      float m = cm;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const bool ok = lane < nsplit && cm != -FLT_MAX;
+      const float f = ok ? exp2f(cm - m) : 0.f;  // partial maxima are in the log2 domain
+      const unsigned valid = __ballot_sync(0xffffffffu, ok);
+      float sum = 0.f;
+      for (int c = 0; c < nsplit; ++c) {
+        const float lc = __shfl_sync(0xffffffffu, cl, c), fc = __shfl_sync(0xffffffffu, f, c);
+        if ((valid >> c) & 1u) sum += lc * fc;
+      }
+      sm_f[r][lane] = f;
+      if (lane == 0) sm_sum[r] = sum, sm_valid[r] = valid;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < REP * D; idx += kTcWarps * 32) {
+      const int r = idx / D, d = idx % D;
+      const int64_t head = t * hq + g * REP + r;
+      const float* pp = part + head * nsplit * (D + 2) + 2 + d;
+      float ov[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) ov[c] = c < nsplit ? __ldcg(pp + c * (D + 2)) : 0.f;
+      const unsigned valid = sm_valid[r];
+      float acc = 0.f;
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        if (c < nsplit && ((valid >> c) & 1u)) acc += ov[c] * sm_f[r][c];
+      out[head * D + d] = rnd<T>(acc / sm_sum[r]);
+    }
+    if (threadIdx.x == 0) *ctr = 0;  // ready for the next launch
   }
 }
 
@@ -640,13 +760,29 @@ dial_status launch_attention_rep(dim3 grid, const void* q, const void* kc, const
     return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "attention: f16/bf16 caches only");
   } else {
     constexpr int smem = kTcWarps * kTcWarpBytes;
-    const cudaError_t e = ensure_smem<attention_tc_kernel<T, REP>>(smem);
+    const cudaError_t e = ensure_smem<attention_tc_kernel<T, REP, false>>(smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention_tc_kernel)");
-    return launch_pdl("attention_tc_kernel", attention_tc_kernel<T, REP>, grid, dim3(kTcWarps * 32),
-                      smem, st, static_cast<const T*>(q), static_cast<const T*>(kc),
-                      static_cast<const T*>(vc), pos, slot, static_cast<T*>(out),
-                      static_cast<float*>(ws), hq, hkv, max_seq, nch, qscale);
+    return launch_pdl("attention_tc_kernel", attention_tc_kernel<T, REP, false>, grid,
+                      dim3(kTcWarps * 32), smem, st, static_cast<const T*>(q),
+                      static_cast<const T*>(kc), static_cast<const T*>(vc), pos, slot,
+                      static_cast<T*>(out), static_cast<float*>(ws), hq, hkv, max_seq, nch, qscale,
+                      QkvIn<T>{});
   }
+}
+
+// The decode form: grid (tokens, hkv, nch).
+template <typename T, int REP>
+dial_status launch_attention_fused_rep(dim3 grid, const QkvIn<T>& in, const int32_t* pos,
+                                       const int32_t* slot, void* out, void* part, int hq, int hkv,
+                                       int64_t max_seq, int nch, float qscale, cudaStream_t st) {
+  constexpr int smem = kTcWarps * kTcWarpBytes;
+  const cudaError_t e = ensure_smem<attention_tc_kernel<T, REP, true>>(smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention_tc_kernel)");
+  return launch_pdl("attention_tc_kernel", attention_tc_kernel<T, REP, true>, grid,
+                    dim3(kTcWarps * 32), smem, st, static_cast<const T*>(nullptr),
+                    static_cast<const T*>(in.kc), static_cast<const T*>(in.vc), pos, slot,
+                    static_cast<T*>(out), static_cast<float*>(part), hq, hkv, max_seq, nch, qscale,
+                    in);
 }
 
 dial_status launch_attention(const void* q, const void* kc, const void* vc, const int32_t* pos,
@@ -674,6 +810,41 @@ dial_status launch_attention(const void* q, const void* kc, const void* vc, cons
                    dim3((unsigned)(tokens * hq)), dim3(128), 0, st, static_cast<const float*>(ws),
                    static_cast<T*>(out), nch);
   });
+  return s;
+}
+
+size_t attention_decode_workspace_bytes(int hq, int64_t max_len) {
+  // partials, then the counters at a 256-byte boundary
+  return (attention_workspace_bytes(1, hq, max_len) + 255) / 256 * 256 + (size_t)hq * sizeof(int);
+}
+
+dial_status launch_attention_decode(const void* qkv, const void* qn, const void* kn,
+                                    const void* cos_t, const void* sin_t, const int32_t* pos,
+                                    const int32_t* slot, void* kc, void* vc, void* out, void* ws,
+                                    int* ctr, dial_dtype dt, int64_t tokens, int hq, int hkv,
+                                    int64_t max_seq, int64_t max_len, float eps, int qk_norm,
+                                    cudaStream_t st) {
+  if (tokens != 1) return fail(DIAL_ERR_SHAPE, "the fused decode attention takes one token");
+  const int nch = attention_splits(tokens, hkv, max_len);  // as launch_attention
+  const float qscale = 0.08837890625f;
+  dim3 grid((unsigned)tokens, (unsigned)hkv, (unsigned)nch);
+  const int rep = hq / hkv;
+  dial_status s = DIAL_OK;
+  if (dt != DIAL_F16 && dt != DIAL_BF16) return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "attention: f16/bf16");
+  auto run = [&](auto tag) {
+    using T = decltype(tag);
+    const QkvIn<T> in{static_cast<const T*>(qkv), static_cast<const T*>(qn), static_cast<const T*>(kn),
+                      static_cast<const T*>(cos_t), static_cast<const T*>(sin_t), static_cast<T*>(kc),
+                      static_cast<T*>(vc), ctr, eps, qk_norm};
+    auto fn = rep == 1   ? launch_attention_fused_rep<T, 1>
+              : rep == 2 ? launch_attention_fused_rep<T, 2>
+              : rep == 4 ? launch_attention_fused_rep<T, 4>
+              : rep == 8 ? launch_attention_fused_rep<T, 8>
+                         : nullptr;
+    if (!fn) return fail(DIAL_ERR_SHAPE, "attention supports Hq/Hkv in {1,2,4,8}");
+    return fn(grid, in, pos, slot, out, ws, hq, hkv, max_seq, nch, qscale, st);
+  };
+  s = dt == DIAL_F16 ? run(__half{}) : run(__nv_bfloat16{});
   return s;
 }
 

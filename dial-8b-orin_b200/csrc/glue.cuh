@@ -21,6 +21,18 @@ dial_status launch_attention(const void* q, const void* kc, const void* vc, cons
                              const int32_t* slot, void* out, void* ws, dial_dtype dt,
                              int64_t tokens, int hq, int hkv, int64_t max_seq, int64_t max_len,
                              cudaStream_t st);
+// Decode attention for one token (tokens == 1): QK-norm + RoPE of the raw
+// qkv row, the K/V cache append and the attention in one launch (the
+// arithmetic of launch_qk_rope_kv followed by launch_attention).  `ws` holds
+// the split partials (attention_workspace_bytes(1, hq, max_len)); `ctr` hkv
+// ints, zero before the launch and zero again after it.
+size_t attention_decode_workspace_bytes(int hq, int64_t max_len);
+dial_status launch_attention_decode(const void* qkv, const void* qn, const void* kn,
+                                    const void* cos_t, const void* sin_t, const int32_t* pos,
+                                    const int32_t* slot, void* kc, void* vc, void* out, void* ws,
+                                    int* ctr, dial_dtype dt, int64_t tokens, int hq, int hkv,
+                                    int64_t max_seq, int64_t max_len, float eps, int qk_norm,
+                                    cudaStream_t st);
 dial_status launch_swiglu(const void* gu, void* out, dial_dtype dt, int64_t tokens, int64_t inter,
                           cudaStream_t st);
 dial_status launch_gather_rows(const void* src, const int32_t* idx, void* dst, dial_dtype dt,

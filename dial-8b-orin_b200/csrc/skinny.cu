@@ -1324,18 +1324,21 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
 // ------------------------------------------------------------------ GGUF decode GEMV, whole tiles per CTA
 // The W8A16 decode GEMV's structure (w8a16_gemv_kernel) for Q4_0 / Q8_0: CTA c
 // takes 16-row tiles c, c + C, ...; warp j streams the groups [G j / 8,
-// G (j + 1) / 8) of each tile (the packed bytes by a 2D TMA box, the tile's
-// 128 bytes of block scales by a bulk copy on the same barrier) and the 8
-// partial tiles meet in shared memory.  FUSED (one activation row): each CTA
-// first quantises the row to Q8_0 blocks in shared memory, with the
-// arithmetic of q8_0_act_quantize_kernel (GGML quantize_row_q8_0_ref: d =
-// max|x|/127, q = round(x * (1/d)), the f16-rounded d used in the dot), so a
-// linear is one launch and the quantised row never goes to global memory;
-// every lane then reads token 0's values (the MMA's 8 columns repeat it).
-// Otherwise the activations come from q8_0_act_quantize_kernel's global
-// buffers.  Per 32-block: one m16n8k32 s8 MMA (exact integer dot), Q4_0's -8
-// folded in as -8 * sum(q_x), scaled in f32 by d_w * d_x.
-constexpr int kGvDRing = kTmaWarps * kStages * kDBytes;  // d stages of all warps
+// G (j + 1) / 8) of each tile, GPS groups per ring stage (2 for Q4_0, so a
+// stage carries 2 KB of packed weights like Q8_0's 1; the 2D TMA box brings
+// the bytes and a bulk copy on the same barrier the tile's GPS x 128 bytes of
+// block scales), and the 8 partial tiles meet in shared memory.  FUSED (one
+// activation row): each warp first quantises its own K range of the row to
+// Q8_0 blocks in shared memory, with the arithmetic of
+// q8_0_act_quantize_kernel (GGML quantize_row_q8_0_ref: d = max|x|/127, q =
+// round(x * (1/d)), the f16-rounded d used in the dot), so a linear is one
+// launch and the quantised row never goes to global memory; every lane then
+// reads token 0's values (the MMA's 8 columns repeat it).  Otherwise the
+// activations come from q8_0_act_quantize_kernel's global buffers.  Per
+// 32-block: one m16n8k32 s8 MMA (exact integer dot), Q4_0's -8 folded in as
+// -8 * sum(q_x), scaled in f32 by d_w * d_x.
+constexpr int kGvDMax = 2 * kDBytes;                     // block scales of one stage (at most 2 groups)
+constexpr int kGvDRing = kTmaWarps * kStages * kGvDMax;  // d stages of all warps
 constexpr int kGgufFusedMaxK = 32768;  // the fused row staging: K bytes + K/32 * 8 bytes of smem
 constexpr int kGgufGemvSmemMax = 1024 + kTmaWarps * kStages * kUnitBytes + kGvDRing + kTmaWarps * kStages * 8 +
                                  kXsAux + kGgufFusedMaxK + kGgufFusedMaxK / 32 * 8;
@@ -1346,31 +1349,37 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
                      const XT* __restrict__ x, const int8_t* __restrict__ xq_g,
                      const float2* __restrict__ xs_g, YT* __restrict__ y, int M, int Mp, int N, int K,
                      int G, int tiles, int* err) {
-  constexpr int GB = TYPE == DIAL_GGML_Q4_0 ? 64 : 128;
-  constexpr uint32_t BOX = GB * 16;
+  constexpr int GB = TYPE == DIAL_GGML_Q4_0 ? 64 : 128;  // bytes of a group row
+  // groups per stage: 2 for the fused Q4_0 row (a 2 KB stage, like Q8_0's 1
+  // group); with global activations the per-stage loads are longer and more,
+  // shorter tiles let the warps queue on the shared-memory reduction rounds
+  constexpr int GPS = TYPE == DIAL_GGML_Q4_0 && FUSED ? 2 : 1;
+  constexpr bool kSw = GB * GPS == 128;  // 128-byte box rows, SWIZZLE_128B
+  constexpr uint32_t BOX = GB * GPS * 16;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = (tma::smem_u32(smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const uint32_t ring = base + (uint32_t)(warp * kStages * kUnitBytes);
-  const uint32_t dring = base + (uint32_t)(kTmaWarps * kStages * kUnitBytes + warp * kStages * kDBytes);
+  const uint32_t dring = base + (uint32_t)(kTmaWarps * kStages * kUnitBytes + warp * kStages * kGvDMax);
   const uint32_t bars = base + (uint32_t)(kTmaWarps * kStages * kUnitBytes + kGvDRing + warp * kStages * 8);
   const uint32_t aux = base + (uint32_t)(kTmaWarps * kStages * kUnitBytes + kGvDRing + kTmaWarps * kStages * 8);
   const uint32_t xqs = aux + kXsAux;                 // FUSED: [G * 128] int8, Q8_0 group order
   const uint32_t xss = xqs + (uint32_t)(G * 128);    // FUSED: [G * 4] {d, sum q}
   pdl_trigger();
   const int C = gridDim.x;
-  const int g0 = G * warp / kTmaWarps, g1 = G * (warp + 1) / kTmaWarps, ngw = g1 - g0;
+  const int g0 = G * warp / kTmaWarps, g1 = G * (warp + 1) / kTmaWarps;
+  const int nsw = (g1 - g0) / GPS;  // stages per tile (the launcher makes G / 8 a multiple of GPS)
   const int ntile = (tiles - (int)blockIdx.x + C - 1) / C;
-  const int U = ntile * ngw;
+  const int U = ntile * nsw;
   int pu = 0, ptile = blockIdx.x, pg = g0;
   auto issue = [&](int st) {
     const uint32_t bar = bars + 8u * (uint32_t)st;
-    tma::mbar_expect_tx(bar, BOX + kDBytes);
+    tma::mbar_expect_tx(bar, BOX + GPS * kDBytes);
     tma::load_2d(ring + (uint32_t)(st * kUnitBytes), &qmap, bar, pg * GB, ptile * 16);
-    // d of rows [16 tile, 16 tile + 16) x blocks [4 pg, 4 pg + 4): 128 contiguous bytes
-    tma::load_1d(dring + (uint32_t)(st * kDBytes), dw + ((int64_t)ptile * G + pg) * 64, kDBytes, bar);
+    // d of rows [16 tile, 16 tile + 16) x groups [pg, pg + GPS): GPS x 128 contiguous bytes
+    tma::load_1d(dring + (uint32_t)(st * kGvDMax), dw + ((int64_t)ptile * G + pg) * 64, GPS * kDBytes, bar);
     ++pu;
-    if (++pg == g1) pg = g0, ptile += C;
+    if ((pg += GPS) == g1) pg = g0, ptile += C;
   };
   if (lane == 0) {
     tma::prefetch_map(&qmap);
@@ -1379,18 +1388,19 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     tma::fence_proxy_async();
     for (int st = 0; st < kStages && pu < U; ++st) issue(st);  // constant weights: before the wait
   }
-  __syncwarp();
-  pdl_wait();  // activations, y and the quantised buffers belong to earlier kernels
   if (threadIdx.x < 8)  // cta_tile_finish round counters: cnt[r] = 0, done[r] = r - 2
     asm volatile("st.shared.s32 [%0], %1;" ::"r"(aux + kAuxCnt + 4u * threadIdx.x),
                  "r"((threadIdx.x & 1) ? (int)(threadIdx.x >> 1) - 2 : 0)
                  : "memory");
-  if (FUSED) {  // the row's Q8_0 blocks (padding blocks of the last group: zero)
+  active_warps_sync(kTmaWarps * 32);
+  pdl_wait();  // activations, y and the quantised buffers belong to earlier kernels
+  if (FUSED) {  // this warp's Q8_0 blocks of the row (padding blocks of the last group: zero)
     const int nb = K / kQK;
-    for (int b = threadIdx.x; b < G * kBlocksPerGroup; b += kTmaWarps * 32) {
-      const int gi = b >> 2, j = b & 3;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(__cvta_shared_to_generic(xqs)) + gi * 128;
-      float2* ds = reinterpret_cast<float2*>(__cvta_shared_to_generic(xss));
+    uint8_t* xq8 = reinterpret_cast<uint8_t*>(__cvta_shared_to_generic(xqs));
+    float2* ds = reinterpret_cast<float2*>(__cvta_shared_to_generic(xss));
+    for (int b = g0 * kBlocksPerGroup + lane; b < g1 * kBlocksPerGroup; b += 32) {
+      uint8_t* dst = xq8 + (b >> 2) * 128;
+      const int j = b & 3;
       if (b >= nb) {
         for (int p = 0; p < kQK; ++p) dst[q8_0_offset(j, p)] = 0;
         ds[b] = make_float2(0.0f, 0.0f);
@@ -1415,16 +1425,20 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
       }
       ds[b] = make_float2(__half2float(__float2half_rn(dd)), (float)sum);
     }
+    __syncwarp();
   }
-  active_warps_sync(kTmaWarps * 32);
   auto store = [&](int tile, const float (&a)[NT][4]) { gguf_store<NT, YT>(a, y, M, N, tile * 16); };
   const uint32_t part = aux + kAuxCs, ctr = aux + kAuxCnt;
-  // this lane's weight bytes in a stage (Q4_0: 64-byte rows, no swizzle; Q8_0:
-  // 128-byte rows, SWIZZLE_128B, chunks 2t and 2t+1)
-  const uint32_t w_lo0 = TYPE == DIAL_GGML_Q4_0 ? (uint32_t)(g * 64 + 16 * t) : (uint32_t)(g * 128 + (((2 * t) ^ g) << 4));
-  const uint32_t w_lo1 = (uint32_t)(g * 128 + (((2 * t + 1) ^ g) << 4));
-  const uint32_t w_hi0 = TYPE == DIAL_GGML_Q4_0 ? w_lo0 + 8 * 64 : w_lo0 + 8 * 128;
-  const uint32_t w_hi1 = w_lo1 + 8 * 128;
+  // this lane's weight bytes of group h of a stage (Q4_0: 128-byte rows of 2
+  // groups, 64 bytes each, SWIZZLE_128B, chunk 4h + t; Q8_0: 128-byte rows,
+  // SWIZZLE_128B, chunks 2t and 2t+1)
+  uint32_t w_lo[2], w_hi[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int c = TYPE == DIAL_GGML_Q4_0 ? 4 * h + t : 2 * t + h;
+    w_lo[h] = kSw ? (uint32_t)(g * 128 + ((c ^ g) << 4)) : (uint32_t)(g * 64 + 16 * c);
+    w_hi[h] = kSw ? (uint32_t)((g + 8) * 128 + ((c ^ g) << 4)) : (uint32_t)((g + 8) * 64 + 16 * c);
+  }
   float acc[NT][4];
   zero_acc(acc);
   int ctile = blockIdx.x, cg = g0, lt = 0;
@@ -1443,92 +1457,108 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
         }
         return;
       }
-      // activations of group cg, and their block scales
-      uint4 xv[NT][2];
-      float4 sc[NT][4];
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        if (FUSED) {
-          const uint32_t a = xqs + (uint32_t)(cg * 128 + 32 * t);
-          xv[j][0] = lds16(a);
-          xv[j][1] = lds16(a + 16);
-#pragma unroll
-          for (int jb = 0; jb < 4; ++jb) {
-            const uint2 v2 = lds8(xss + 8u * (uint32_t)(cg * 4 + jb));
-            sc[j][jb] = make_float4(__uint_as_float(v2.x), __uint_as_float(v2.y), __uint_as_float(v2.x),
-                                    __uint_as_float(v2.y));
-          }
-        } else {
-          const int8_t* xr = xq_g + (size_t)(j * 8 + g) * G * 128 + (size_t)cg * 128 + 32 * t;
-          xv[j][0] = ld_ro16(xr);
-          xv[j][1] = ld_ro16(xr + 16);
-#pragma unroll
-          for (int jb = 0; jb < 4; ++jb)
-            sc[j][jb] = __ldg(reinterpret_cast<const float4*>(xs_g + (size_t)(cg * 4 + jb) * Mp + j * 8 + 2 * t));
-        }
-      }
-      const uint32_t sb = ring + (uint32_t)(st * kUnitBytes);
+      const uint32_t sb = ring + (uint32_t)(st * kUnitBytes), db = dring + (uint32_t)(st * kGvDMax);
       uint4 wl[2], wh[2];
-      wl[0] = lds16(sb + w_lo0);
-      wh[0] = lds16(sb + w_hi0);
-      if (TYPE == DIAL_GGML_Q4_0) {
-        wl[1] = wh[1] = make_uint4(0, 0, 0, 0);
-      } else {
-        wl[1] = lds16(sb + w_lo1);
-        wh[1] = lds16(sb + w_hi1);
-      }
-      const uint32_t db = dring + (uint32_t)(st * kDBytes);
-      const uint2 dl = lds8(db + (uint32_t)(g * 8)), dh = lds8(db + (uint32_t)((g + 8) * 8));
-      // A fragments and block scales in registers (this consumes every word loaded from the stage)
-      uint32_t fa[4][4];
+      uint2 dl[GPS], dh[GPS];
 #pragma unroll
-      for (int jb = 0; jb < 4; ++jb) {
-        if (TYPE == DIAL_GGML_Q4_0) {
-          const uint32_t l = word(wl[0], jb), h = word(wh[0], jb);
-          fa[jb][0] = l & 0x0F0F0F0Fu;
-          fa[jb][2] = (l >> 4) & 0x0F0F0F0Fu;
-          fa[jb][1] = h & 0x0F0F0F0Fu;
-          fa[jb][3] = (h >> 4) & 0x0F0F0F0Fu;
+      for (int h = 0; h < 2; ++h) {
+        if (TYPE == DIAL_GGML_Q4_0 && GPS == 1 && h == 1) {
+          wl[1] = wh[1] = make_uint4(0, 0, 0, 0);
         } else {
-          fa[jb][0] = word(wl[jb >> 1], 2 * (jb & 1));
-          fa[jb][2] = word(wl[jb >> 1], 2 * (jb & 1) + 1);
-          fa[jb][1] = word(wh[jb >> 1], 2 * (jb & 1));
-          fa[jb][3] = word(wh[jb >> 1], 2 * (jb & 1) + 1);
+          wl[h] = lds16(sb + w_lo[h]);
+          wh[h] = lds16(sb + w_hi[h]);
         }
       }
-      const float dlv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dl.x)),
-                            __high2float(*reinterpret_cast<const __half2*>(&dl.x)),
-                            __low2float(*reinterpret_cast<const __half2*>(&dl.y)),
-                            __high2float(*reinterpret_cast<const __half2*>(&dl.y))};
-      const float dhv[4] = {__low2float(*reinterpret_cast<const __half2*>(&dh.x)),
-                            __high2float(*reinterpret_cast<const __half2*>(&dh.x)),
-                            __low2float(*reinterpret_cast<const __half2*>(&dh.y)),
-                            __high2float(*reinterpret_cast<const __half2*>(&dh.y))};
+#pragma unroll
+      for (int q = 0; q < GPS; ++q) {
+        dl[q] = lds8(db + (uint32_t)(q * kDBytes + g * 8));
+        dh[q] = lds8(db + (uint32_t)(q * kDBytes + (g + 8) * 8));
+      }
+      // A fragments of the stage's GPS x 4 blocks (this consumes every word loaded from it)
+      uint32_t fa[GPS][4][4];
+#pragma unroll
+      for (int q = 0; q < GPS; ++q)
+#pragma unroll
+        for (int jb = 0; jb < 4; ++jb) {
+          if (TYPE == DIAL_GGML_Q4_0) {
+            const uint32_t l = word(wl[q], jb), h = word(wh[q], jb);
+            fa[q][jb][0] = l & 0x0F0F0F0Fu;
+            fa[q][jb][2] = (l >> 4) & 0x0F0F0F0Fu;
+            fa[q][jb][1] = h & 0x0F0F0F0Fu;
+            fa[q][jb][3] = (h >> 4) & 0x0F0F0F0Fu;
+          } else {
+            fa[q][jb][0] = word(wl[jb >> 1], 2 * (jb & 1));
+            fa[q][jb][2] = word(wl[jb >> 1], 2 * (jb & 1) + 1);
+            fa[q][jb][1] = word(wh[jb >> 1], 2 * (jb & 1));
+            fa[q][jb][3] = word(wh[jb >> 1], 2 * (jb & 1) + 1);
+          }
+        }
+      float dlv[GPS][4], dhv[GPS][4];
+#pragma unroll
+      for (int q = 0; q < GPS; ++q) {
+        dlv[q][0] = __low2float(*reinterpret_cast<const __half2*>(&dl[q].x));
+        dlv[q][1] = __high2float(*reinterpret_cast<const __half2*>(&dl[q].x));
+        dlv[q][2] = __low2float(*reinterpret_cast<const __half2*>(&dl[q].y));
+        dlv[q][3] = __high2float(*reinterpret_cast<const __half2*>(&dl[q].y));
+        dhv[q][0] = __low2float(*reinterpret_cast<const __half2*>(&dh[q].x));
+        dhv[q][1] = __high2float(*reinterpret_cast<const __half2*>(&dh[q].x));
+        dhv[q][2] = __low2float(*reinterpret_cast<const __half2*>(&dh[q].y));
+        dhv[q][3] = __high2float(*reinterpret_cast<const __half2*>(&dh[q].y));
+      }
       __syncwarp();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       if (lane == 0 && pu < U) issue(st);  // the stage is free: refill it
 #pragma unroll
-      for (int jb = 0; jb < 4; ++jb)
+      for (int q = 0; q < GPS; ++q) {
+        const int gq = cg + q;
+        // activations of group gq and their block scales
+        uint4 xv[NT][2];
+        float4 sc[NT][4];
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
-          const uint4& xw = xv[j][jb >> 1];
-          int cc[4] = {0, 0, 0, 0};
-          mma_s8(cc, fa[jb][0], fa[jb][1], fa[jb][2], fa[jb][3], word(xw, 2 * (jb & 1)),
-                 word(xw, 2 * (jb & 1) + 1));
-          const float4 scv = sc[j][jb];
-          float v0 = (float)cc[0], v1 = (float)cc[1], v2 = (float)cc[2], v3 = (float)cc[3];
-          if (TYPE == DIAL_GGML_Q4_0) {
-            v0 = fmaf(-8.0f, scv.y, v0);
-            v1 = fmaf(-8.0f, scv.w, v1);
-            v2 = fmaf(-8.0f, scv.y, v2);
-            v3 = fmaf(-8.0f, scv.w, v3);
+          if (FUSED) {
+            const uint32_t a = xqs + (uint32_t)(gq * 128 + 32 * t);
+            xv[j][0] = lds16(a);
+            xv[j][1] = lds16(a + 16);
+#pragma unroll
+            for (int jb = 0; jb < 4; ++jb) {
+              const uint2 v2 = lds8(xss + 8u * (uint32_t)(gq * 4 + jb));
+              sc[j][jb] = make_float4(__uint_as_float(v2.x), __uint_as_float(v2.y), __uint_as_float(v2.x),
+                                      __uint_as_float(v2.y));
+            }
+          } else {
+            const int8_t* xr = xq_g + (size_t)(j * 8 + g) * G * 128 + (size_t)gq * 128 + 32 * t;
+            xv[j][0] = ld_ro16(xr);
+            xv[j][1] = ld_ro16(xr + 16);
+#pragma unroll
+            for (int jb = 0; jb < 4; ++jb)
+              sc[j][jb] =
+                  __ldg(reinterpret_cast<const float4*>(xs_g + (size_t)(gq * 4 + jb) * Mp + j * 8 + 2 * t));
           }
-          acc[j][0] = fmaf(dlv[jb] * scv.x, v0, acc[j][0]);
-          acc[j][1] = fmaf(dlv[jb] * scv.z, v1, acc[j][1]);
-          acc[j][2] = fmaf(dhv[jb] * scv.x, v2, acc[j][2]);
-          acc[j][3] = fmaf(dhv[jb] * scv.z, v3, acc[j][3]);
         }
-      if (++cg == g1) {
+#pragma unroll
+        for (int jb = 0; jb < 4; ++jb)
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const uint4& xw = xv[j][jb >> 1];
+            int cc[4] = {0, 0, 0, 0};
+            mma_s8(cc, fa[q][jb][0], fa[q][jb][1], fa[q][jb][2], fa[q][jb][3], word(xw, 2 * (jb & 1)),
+                   word(xw, 2 * (jb & 1) + 1));
+            const float4 scv = sc[j][jb];
+            float v0 = (float)cc[0], v1 = (float)cc[1], v2 = (float)cc[2], v3 = (float)cc[3];
+            if (TYPE == DIAL_GGML_Q4_0) {
+              v0 = fmaf(-8.0f, scv.y, v0);
+              v1 = fmaf(-8.0f, scv.w, v1);
+              v2 = fmaf(-8.0f, scv.y, v2);
+              v3 = fmaf(-8.0f, scv.w, v3);
+            }
+            acc[j][0] = fmaf(dlv[q][jb] * scv.x, v0, acc[j][0]);
+            acc[j][1] = fmaf(dlv[q][jb] * scv.z, v1, acc[j][1]);
+            acc[j][2] = fmaf(dhv[q][jb] * scv.x, v2, acc[j][2]);
+            acc[j][3] = fmaf(dhv[q][jb] * scv.z, v3, acc[j][3]);
+          }
+      }
+      if ((cg += GPS) == g1) {
         cta_tile_finish<NT>(part, ctr, lt++, ctile, acc, store, err);
         zero_acc(acc);
         cg = g0;
@@ -1800,13 +1830,18 @@ dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, co
   const int nt = (int)(Mp / 8);
   const uint8_t* qp = static_cast<const uint8_t*>(qs);
   const __half* dp = reinterpret_cast<const __half*>(d);
+  // whole tiles per CTA from 32 tiles on (fewer CTAs than SMs still beat the
+  // stream-K path's global fixups); the fused Q4_0 row takes 2 groups per
+  // stage, so its groups per warp must be even
   const bool tile_mode = sk_ws && aligned16(qs) && aligned16(d) && nt <= 2 && G >= kTmaWarps &&
-                         tiles >= sm_count();
-  const bool fused = tile_mode && M == 1 && K <= kGgufFusedMaxK;
+                         G % kTmaWarps == 0 && tiles >= 32;
+  const bool fused = tile_mode && M == 1 && K <= kGgufFusedMaxK &&
+                     (type != DIAL_GGML_Q4_0 || G % (2 * kTmaWarps) == 0);
+  const int gps = type == DIAL_GGML_Q4_0 && fused ? 2 : 1;
   if (tile_mode) {  // the decode GEMV: whole tiles per CTA (+ the row's Q8_0 staging when fused)
     const int GB = type == DIAL_GGML_Q4_0 ? 64 : 128;
     CUtensorMap map;
-    s = tma::make_byte_map(&map, qs, N, G * GB, GB, 16, type != DIAL_GGML_Q4_0 ? 128 : 0);
+    s = tma::make_byte_map(&map, qs, N, G * GB, GB * gps, 16, GB * gps == 128 ? 128 : 0);
     if (s != DIAL_OK) return s;
     int* err = device_error_ptr();
     if (!err) return fail(DIAL_ERR_CUDA, "device error flag is unavailable");

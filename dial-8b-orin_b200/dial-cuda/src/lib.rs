@@ -258,6 +258,14 @@ extern "C" {
                           workspace_bytes: usize, dt: dial_dtype, tokens: i64, n_heads: c_int,
                           n_kv_heads: c_int, head_dim: c_int, max_seq: i64, max_len: i64,
                           stream: dial_stream) -> dial_status;
+    pub fn dial_decode_attention_workspace_bytes(n_heads: c_int, max_len: i64) -> usize;
+    pub fn dial_decode_attention(qkv: *const c_void, q_norm_w: *const c_void, k_norm_w: *const c_void,
+                                 cos_t: *const c_void, sin_t: *const c_void, positions: *const i32,
+                                 slots: *const i32, k_cache: *mut c_void, v_cache: *mut c_void,
+                                 out: *mut c_void, workspace: *mut c_void, workspace_bytes: usize,
+                                 dt: dial_dtype, n_heads: c_int, n_kv_heads: c_int, head_dim: c_int,
+                                 max_seq: i64, max_len: i64, eps: f32, qk_norm: c_int,
+                                 stream: dial_stream) -> dial_status;
     pub fn dial_swiglu(gate_up: *const c_void, out: *mut c_void, dt: dial_dtype, tokens: i64,
                        intermediate: i64, stream: dial_stream) -> dial_status;
     pub fn dial_embedding(table: *const c_void, ids: *const i32, out: *mut c_void, dt: dial_dtype, tokens: i64,

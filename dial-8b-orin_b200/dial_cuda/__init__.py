@@ -4,6 +4,8 @@ This mirrors the reference's linear-module interface so a caller that used
 DIAL's `TextLinear` finds the same shape of API:
 
   reference (lisa301/DIAL-8B-orin)                          here
+  configure_worker_w8a16_from_args  worker_w8a16.rs:15-44  configure_worker_w8a16_from_args
+  worker_w8a16_enabled / _summary   worker_w8a16.rs:46-63  worker_w8a16_enabled / _summary
   TextLinear::from_dense        worker_w8a16.rs:78-101      TextLinear.from_dense
   TextLinear::forward           worker_w8a16.rs:103-121     TextLinear.forward
   CudaW8A16Linear::from_linear  worker_w8a16.rs:301-366     W8A16Linear.from_linear
@@ -77,6 +79,9 @@ SIGNATURES = {
     "dial_attention_workspace_bytes": ([_i64, _i32, _i64], _sz),
     "dial_attention": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i32, _i64, _i32, _i32, _i32, _i64,
                         _i64, _vp], _i32),
+    "dial_decode_attention_workspace_bytes": ([_i32, _i64], _sz),
+    "dial_decode_attention": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i32, _i32,
+                               _i32, _i32, _i64, _i64, ctypes.c_float, _i32, _vp], _i32),
     "dial_swiglu": ([_vp, _vp, _i32, _i64, _i64, _vp], _i32),
     "dial_embedding": ([_vp, _vp, _vp, _i32, _i64, _i64, _i64, _vp], _i32),
     "dial_argmax": ([_vp, _vp, _i32, _i64, _i64, _vp], _i32),
@@ -365,6 +370,51 @@ class GgufKLinear:
         return self.blocks.numel()
 
 
+# ------------------------------------------------------------------ worker selection
+# worker_w8a16.rs:9-13: process-wide switch and the converted linears' totals
+_WORKER_W8A16 = {"enabled": False, "linears": 0, "weight_bytes": 0}
+
+
+def _is_f16(dtype) -> bool:
+    return dtype in ("f16", "float16", F16) or str(dtype) == "torch.float16"
+
+
+def configure_worker_w8a16_from_args(requested: bool, worker_mode: bool, device, dtype,
+                                     gguf_enabled: bool = False) -> str:
+    """worker_w8a16.rs:15-44.  W8A16 linears are enabled iff they were requested,
+    no GGUF source is loaded (GGUF takes precedence), the process is a worker,
+    the device is CUDA and the model dtype is f16 (the reference op accepts F16
+    activations only).  Sets the switch that TextLinear.from_dense reads and
+    returns the message the reference logs for the same case ("" when silent)."""
+    cuda = str(device).startswith("cuda")
+    enabled = bool(requested and not gguf_enabled and worker_mode and cuda and _is_f16(dtype))
+    _WORKER_W8A16["enabled"] = enabled
+    if requested and gguf_enabled:
+        return ("both worker W8A16 and GGUF were requested; GGUF takes precedence and W8A16 is "
+                "disabled")
+    if requested and not worker_mode:
+        return "worker W8A16 ignored in master mode; master weights remain unchanged"
+    if requested and not cuda:
+        return "worker W8A16 requested on a non-CUDA device; falling back to dense weights"
+    if requested and not _is_f16(dtype):
+        return f"worker W8A16 requires --dtype f16 (got {dtype}); falling back to dense weights"
+    if enabled:
+        return ("worker W8A16 enabled: CUDA linear weights use row-wise int8, activations/outputs "
+                "remain F16")
+    return ""
+
+
+def worker_w8a16_enabled() -> bool:
+    return _WORKER_W8A16["enabled"]
+
+
+def worker_w8a16_summary():
+    """(linears converted, their int8 weight + f32 scale bytes) while enabled, else None."""
+    if not _WORKER_W8A16["enabled"]:
+        return None
+    return _WORKER_W8A16["linears"], _WORKER_W8A16["weight_bytes"]
+
+
 class TextLinear:
     """Dispatch wrapper with the reference's constructor names (worker_w8a16.rs:65-121)."""
 
@@ -372,8 +422,20 @@ class TextLinear:
         self.inner = inner
 
     @classmethod
-    def from_dense(cls, name: str, weight, scale_dtype=None) -> "TextLinear":
-        return cls(W8A16Linear.from_linear(name, weight, scale_dtype))
+    def from_dense(cls, name: str, weight, scale_dtype=None, dense=None) -> "TextLinear":
+        """worker_w8a16.rs:78-101: a W8A16 linear when the worker switch is on;
+        otherwise the caller's own dense module `dense` is wrapped unchanged (the
+        reference's TextLinear::Dense -- that path is the caller's, not this
+        library's).  With the switch off and no `dense` given this raises."""
+        if not worker_w8a16_enabled():
+            if dense is None:
+                raise RuntimeError(f"{name}: worker W8A16 is not enabled (configure_worker_w8a16_from_args)"
+                                   " and no dense module was given")
+            return cls(dense)
+        lin = W8A16Linear.from_linear(name, weight, scale_dtype)
+        _WORKER_W8A16["linears"] += 1
+        _WORKER_W8A16["weight_bytes"] += lin.out_dim * lin.in_dim + lin.out_dim * 4  # :351
+        return cls(lin)
 
     @classmethod
     def from_gguf(cls, name: str, blocks, qtype: int, in_dim: int, out_dim: int) -> "TextLinear":

@@ -252,6 +252,24 @@ DIAL_API dial_status dial_attention(const void* q, const void* k_cache, const vo
                                     int64_t tokens, int n_heads, int n_kv_heads, int head_dim,
                                     int64_t max_seq, int64_t max_len, dial_stream stream);
 
+/* One decode token (text.rs:1485-1531 then 1258-1327 for a single query row):
+ * dial_qk_norm_rope_kv_append followed by dial_attention with tokens = 1, as
+ * one launch -- the split of the key range holding positions[0] appends the
+ * normed, rotated key and the value to the caches, every split computes the
+ * query heads of its kv group from the raw qkv row, and the last split of a kv
+ * group to finish merges the group's partials.  Same results, bit for bit, as
+ * the two-call form.  `workspace` (16-byte aligned) holds
+ * dial_decode_attention_workspace_bytes(n_heads, max_len) bytes, zero-filled
+ * once by the caller; every call leaves it zeroed again.  Calls sharing a
+ * workspace must not overlap on the GPU. */
+DIAL_API size_t dial_decode_attention_workspace_bytes(int n_heads, int64_t max_len);
+DIAL_API dial_status dial_decode_attention(
+    const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos_t,
+    const void* sin_t, const int32_t* positions, const int32_t* slots, void* k_cache,
+    void* v_cache, void* out, void* workspace, size_t workspace_bytes, dial_dtype dt,
+    int n_heads, int n_kv_heads, int head_dim, int64_t max_seq, int64_t max_len, float eps,
+    int qk_norm, dial_stream stream);
+
 /* SwiGLU of Mlp (text.rs:816-820): out[t, i] = silu(g) * u over the halves of
  * gate_up [T, 2I] (silu result rounded to dt first, as two tensor ops). */
 DIAL_API dial_status dial_swiglu(const void* gate_up, void* out, dial_dtype dt, int64_t tokens,
@@ -317,7 +335,8 @@ typedef struct dial_layer_weights {
 } dial_layer_weights;
 
 /* Workspace for dial_decoder_layers / dial_decoder_head on `tokens` rows whose
- * positions are < max_len. */
+ * positions are < max_len.  Zero-fill it once (it holds counters that every
+ * call leaves at zero); one workspace sized for the largest call serves all. */
 DIAL_API size_t dial_decoder_workspace_bytes(const dial_decoder_dims* dims, int64_t tokens,
                                              int64_t max_len);
 

@@ -211,6 +211,63 @@ def test_attention(D, torch, mode, Hq, dt):
     assert rel(got, ref) <= {"f16": 3e-3, "bf16": 1e-2}[dt]
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("Hq,Hkv,qk_norm", [(32, 8, 1), (32, 8, 0), (8, 8, 1), (16, 8, 1), (64, 8, 1),
+                                            (16, 2, 1)])
+def test_decode_attention_fused_matches_two_call_form(D, torch, dt, Hq, Hkv, qk_norm):
+    """dial_decode_attention (one launch: QK-norm, RoPE, cache append, the key
+    splits and their merge by the last split to finish) against
+    dial_qk_norm_rope_kv_append + dial_attention on the same inputs: output and
+    both caches bit-identical, for contexts from one key to many splits; one
+    zero-filled workspace serves every call (its counters return to zero)."""
+    rng = np.random.default_rng(Hq + Hkv + qk_norm + (dt == "bf16"))
+    Dh, S, slots = 128, 4200, 3
+    cos_t, sin_t = O.rope_tables(S, Dh, 1e6)
+    if dt == "bf16":
+        cos_t, sin_t = (O.f32_to_bf16(x.astype(np.float32)).view(np.int16) for x in (cos_t, sin_t))
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    code = {"f16": D.F16, "bf16": D.BF16}[dt]
+    kc0, _ = _cast(rng.normal(0, 1, (slots, Hkv, S, Dh)).astype(np.float32), dt)
+    vc0, _ = _cast(rng.normal(0, 1, (slots, Hkv, S, Dh)).astype(np.float32), dt)
+    qn, _ = _cast((1 + 0.1 * rng.normal(0, 1, Dh)).astype(np.float32), dt)
+    kn, _ = _cast((1 + 0.1 * rng.normal(0, 1, Dh)).astype(np.float32), dt)
+    tabs = [dev(torch, a) for a in (qn, kn, cos_t, sin_t)]
+    wsb = D.lib().dial_decode_attention_workspace_bytes(Hq, S)
+    dws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    for p, sl in [(0, 1), (5, 0), (130, 2), (700, 1), (1299, 2), (4100, 0)]:
+        qkv, _ = _cast(rng.normal(0, 1, (1, (Hq + 2 * Hkv) * Dh)).astype(np.float32), dt)
+        qkv_t, pos_t, slot_t = dev(torch, qkv), dev(torch, np.array([p], np.int32)), \
+            dev(torch, np.array([sl], np.int32))
+        max_len = p + 1
+        # two-call form
+        kc_a, vc_a = dev(torch, kc0), dev(torch, vc0)
+        q = torch.empty((1, Hq, Dh), dtype=tdt, device="cuda")
+        out_a = torch.empty((1, Hq * Dh), dtype=tdt, device="cuda")
+        D.check(D.lib().dial_qk_norm_rope_kv_append(
+            qkv_t.data_ptr(), *[t.data_ptr() for t in tabs], pos_t.data_ptr(), slot_t.data_ptr(),
+            q.data_ptr(), kc_a.data_ptr(), vc_a.data_ptr(), code, 1, Hq, Hkv, Dh, S, 1e-6, qk_norm,
+            D.stream_ptr()), "qk_rope")
+        need = D.lib().dial_attention_workspace_bytes(1, Hq, max_len)
+        ws = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
+        D.check(D.lib().dial_attention(q.data_ptr(), kc_a.data_ptr(), vc_a.data_ptr(), pos_t.data_ptr(),
+                                       slot_t.data_ptr(), out_a.data_ptr(), ws.data_ptr() if need else None,
+                                       need, code, 1, Hq, Hkv, Dh, S, max_len, D.stream_ptr()), "attention")
+        # one launch
+        kc_b, vc_b = dev(torch, kc0), dev(torch, vc0)
+        out_b = torch.empty_like(out_a)
+        for _ in range(2):  # the second call finds the counters back at zero
+            D.check(D.lib().dial_decode_attention(
+                qkv_t.data_ptr(), *[t.data_ptr() for t in tabs], pos_t.data_ptr(), slot_t.data_ptr(),
+                kc_b.data_ptr(), vc_b.data_ptr(), out_b.data_ptr(), dws.data_ptr(), wsb, code, Hq, Hkv,
+                Dh, S, max_len, 1e-6, qk_norm, D.stream_ptr()), "decode_attention")
+            torch.cuda.synchronize()
+            assert torch.equal(kc_a.view(torch.int16), kc_b.view(torch.int16)), p
+            assert torch.equal(vc_a.view(torch.int16), vc_b.view(torch.int16)), p
+            assert torch.equal(out_a.view(torch.int16), out_b.view(torch.int16)), p
+    assert int(dws[wsb - 4 * Hq:].count_nonzero()) == 0
+    assert D.lib().dial_device_error(1) == 0
+
+
 def test_swiglu_embedding_argmax(D, torch):
     rng = np.random.default_rng(5)
     T, I = 3, 1000

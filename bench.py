@@ -28,7 +28,10 @@ benchmark configurations; no dataset is involved):
   attention_batched: whole-model decode (the default, qwen3_decode: f16, the
                 reference's W8A16 dtype) and the batched decode attention;
                 their docstrings give the shapes.  --split even|planner picks
-                the layer split of the pipeline workloads.
+                the layer split of the pipeline workloads; --head vocab
+                splits their output head over the stages by vocabulary rows
+                (each stage a share that evens out the stages' weight bytes)
+                instead of running it on the last stage.
 A step is one pass of the workload.  Multi-linear steps are captured once in
 a CUDA graph and replayed.  Inputs: rotating copies of the weights whose total
 exceeds the 126 MB L2, so every step reads its weights from HBM.
@@ -604,7 +607,7 @@ class QwenDecode:
     planner, the output head counted as 3.2 layers).  A step advances every
     sequence by one greedy token.  Metric: decode tok/s of the whole job."""
     metric, unit, bound, dtype = "8B W8A16 decode tok/s", "tok/s", "hbm", "int8 x f16"
-    kernel = "w8a16_tma_kernel<NT=1> (the stage's linears from one graph, events)"
+    kernel = "w8a16_gemv_kernel<NT=1> (the stage's linears from one graph, events)"
     graph = True
     scaling = "strong"
     # DRAM bytes per token of the stage's linears on one GPU: the DRAM read + write
@@ -616,6 +619,7 @@ class QwenDecode:
     copies_per_step = 8  # one graph per micro-batch
     act = "f16"
     split = "planner"  # layer split over the stages: "planner" or "even"
+    head = "last"  # output head: on the last stage, or "vocab" (vocabulary-parallel)
     name = "qwen3_decode"
 
     @classmethod
@@ -628,10 +632,24 @@ class QwenDecode:
         return cls.mb_size
 
     @classmethod
+    def vocab_head(cls, world):
+        return cls.head == "vocab" and world > 1
+
+    @classmethod
     def ranges_for(cls, world):
         from dial_cuda.pipeline import stage_layers
-        return stage_layers(cls.model_config().n_layers, world, head_layers=cls.head_layers,
-                            method=cls.split)
+        # a vocabulary-parallel head is spread over the stages after the split
+        hl = 0.0 if cls.vocab_head(world) else cls.head_layers
+        return stage_layers(cls.model_config().n_layers, world, head_layers=hl, method=cls.split)
+
+    @classmethod
+    def head_spans(cls, world):
+        """Vocabulary rows per stage: shares that bring every stage's weight up
+        to the mean (layers + the head's cost in layers) / stages."""
+        from dial_cuda.model import vocab_shards
+        n = [len(r) for r in cls.ranges_for(world)]
+        target = (sum(n) + cls.head_layers) / world
+        return vocab_shards(cls.model_config().vocab, [max(0.0, target - k) for k in n])
 
     @classmethod
     def model_desc(cls):
@@ -646,6 +664,8 @@ class QwenDecode:
                     prompt_len=cls.prompt_len, activation=cls.act, kv_cache=cls.act,
                     split=cls.split if world > 1 else "one stage",
                     stages=[[r.start, r.stop] for r in cls.ranges_for(world)],
+                    head=("vocabulary-parallel rows " + str([list(v) for v in cls.head_spans(world)]))
+                    if cls.vocab_head(world) else "last stage",
                     launch="one CUDA graph per micro-batch and stage; NCCL p2p hand-off")
 
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
@@ -658,11 +678,25 @@ class QwenDecode:
         self.ranges = self.ranges_for(world)
         rr = self.ranges[rank]
         self.max_seq = self.prompt_len + self.decode_cap + 16
-        self.stage = Stage(self.cfg, rr.start, rr.stop, n_slots=self.n_seqs, max_seq=self.max_seq)
+        self.head_channel = None
+        if self.vocab_head(world):
+            from dial_cuda.pipeline import head_links
+            spans = self.head_spans(world)
+            rows = [v1 - v0 for v0, v1 in spans]
+            self.stage = Stage(self.cfg, rr.start, rr.stop, n_slots=self.n_seqs, max_seq=self.max_seq,
+                               with_head=False, head_rows=spans[rank])
+            self.comp = ModelStageCompute(self.stage, n_mb, self.prompt_len, mb_size=self.mb_size,
+                                          vocab_head_stages=world)
+            self.channel = NcclChannel(rank, world)
+            self.head_channel = NcclChannel(rank, world, links=head_links(world, rows))
+            self.pipe = Pipeline(rank, world, self.comp, self.channel, n_mb,
+                                 head_channel=self.head_channel, head_rows=rows)
+        else:
+            self.stage = Stage(self.cfg, rr.start, rr.stop, n_slots=self.n_seqs, max_seq=self.max_seq)
+            self.comp = ModelStageCompute(self.stage, n_mb, self.prompt_len, mb_size=self.mb_size)
+            self.channel = NcclChannel(rank, world) if world > 1 else None  # C-ABI stage communicators
+            self.pipe = Pipeline(rank, world, self.comp, self.channel, n_mb)
         st = self.stage
-        self.comp = ModelStageCompute(st, n_mb, self.prompt_len, mb_size=self.mb_size)
-        self.channel = NcclChannel(rank, world) if world > 1 else None  # C-ABI stage communicators
-        self.pipe = Pipeline(rank, world, self.comp, self.channel, n_mb)
         prompts = None
         if rank == 0:
             g = torch.Generator(device="cuda").manual_seed(SEED)
@@ -724,13 +758,15 @@ class QwenDecode:
     def close(self):
         if self.channel is not None:
             self.channel.close()
+        if self.head_channel is not None:
+            self.head_channel.close()
 
     def kernel_roofline(self, reps: int = 5):
         """HBM GB/s of the dominant kernel: this stage's linears (M = one
         micro-batch) launched back to back in model order from one CUDA graph,
         algorithmic bytes over the replay's event time."""
         torch, st = self.torch, self.stage
-        lins = st.linears + ([st.head] if st.head is not None else [])
+        lins = st.linears + [h for h in (st.head, st.head_shard) if h is not None]
         R = self.mb_size
         xs, ys = {}, []
         for lin in lins:
@@ -1238,9 +1274,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split", choices=["planner", "even"], default=None,
                     help="layer split of the pipeline workloads (default: the workload's)")
+    ap.add_argument("--head", choices=["last", "vocab"], default=None,
+                    help="output head of the pipeline workloads: on the last stage, or "
+                         "vocabulary-parallel over the stages (default: the workload's)")
     args = ap.parse_args()
     if args.split is not None and hasattr(WORKLOADS[args.workload], "split"):
         WORKLOADS[args.workload].split = args.split
+    if args.head is not None and hasattr(WORKLOADS[args.workload], "head"):
+        WORKLOADS[args.workload].head = args.head
     rank, local, world = dist_setup()
     try:
         if args.impl == "reference":

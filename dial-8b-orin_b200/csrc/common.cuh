@@ -128,6 +128,16 @@ __device__ __forceinline__ uint4 ld_ro16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
+// Greedy-sampling key of a logit: the order of the keys is the order of
+// (value, -index), so the largest key is the first index of the maximum, as
+// argmax_kernel picks it (NaN never wins: it maps to the smallest key; -0 and
+// +0 compare equal, as floats do).
+__device__ __forceinline__ unsigned long long argmax_key(float v, long long idx) {
+  uint32_t b = v == 0.0f ? 0u : __float_as_uint(v);
+  const uint32_t ord = v != v ? 0u : (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));

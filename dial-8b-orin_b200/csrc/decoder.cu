@@ -38,6 +38,7 @@ struct Ws {
   uint8_t* attn_ws; // attention partials
   uint8_t* lin_ws;  // GGUF activation scratch
   uint8_t* logits;  // [T, V] for the head
+  unsigned long long* keys;  // [T, ceil(V / 16)] per-tile greedy keys of the head
   size_t total;
 };
 
@@ -68,6 +69,7 @@ Ws layout(const dial_decoder_dims& d, int64_t T, int64_t max_len, uint8_t* base)
   w.lin_ws = take(std::max(gguf_skinny_workspace_bytes(std::min<int64_t>(T, kSkinnyMaxM), kmax),
                            gemm_sm100_gguf_workspace_bytes(T, kmax)));
   w.logits = take(T * (int64_t)d.vocab * e);
+  w.keys = reinterpret_cast<unsigned long long*>(take(T * ((d.vocab + 15) / 16) * 8));
   w.total = off;
   return w;
 }
@@ -244,6 +246,46 @@ dial_status dial_decoder_layers(const dial_decoder_dims* dims, const dial_layer_
   return launch_add(hidden, hidden, w.delta, dt, T * H, st);  // h = h + d of the last layer
 }
 
+namespace {
+
+// The head over vocabulary rows [v0, v0 + n) (the full head: v0 = 0, n = vocab):
+// y = head(rmsnorm(hidden[rows])) into lg, and per row either the index of
+// its maximum (ids) or its greedy key (keys, indices from v0).  The W8A16
+// decode GEMV writes each tile's key in its epilogue (one small reduction
+// follows); other paths take argmax over the logits.
+dial_status head_rows(const dial_decoder_dims& d, const void* final_norm, dial_linear_ref head,
+                      int64_t v0, int64_t n, const void* hidden, const int32_t* row_index,
+                      int64_t rows, int32_t* ids, unsigned long long* keys, void* logits,
+                      const Ws& w, cudaStream_t st) {
+  dial_status s;
+  const dial_dtype dt = (dial_dtype)d.act_dtype;
+  const int64_t H = d.hidden, tiles = (n + 15) / 16;
+  void* lg = logits ? logits : w.logits;
+  const bool w8head = d.head_format == DIAL_WFMT_W8A16 || d.head_format == DIAL_WFMT_W8A16_F16S;
+  if (!row_index && w8head && d.act_dtype != DIAL_F32 && rows <= kSkinnyMaxM && w8a16_prologue_ok(rows, H)) {
+    const ActPrologue fin{kProRms, nullptr, nullptr, static_cast<const uint16_t*>(final_norm), d.rms_eps};
+    const dial_dtype sdt = d.head_format == DIAL_WFMT_W8A16 ? DIAL_F32 : DIAL_F16;
+    bool keyed = false;
+    if ((s = launch_w8a16_skinny(hidden, dt, static_cast<const int8_t*>(head.w), head.s, sdt, lg, rows,
+                                 H, n, st, w.sk, &fin, w.keys, v0, &keyed)) != DIAL_OK)
+      return s;
+    if (keyed) return launch_key_reduce(w.keys, tiles, 1, tiles, rows, keys, ids, st);
+  } else {
+    const void* src = hidden;
+    if (row_index) {
+      if ((s = launch_gather_rows(hidden, row_index, w.delta, dt, rows, H, st)) != DIAL_OK) return s;
+      src = w.delta;
+    }
+    if ((s = launch_rmsnorm(src, nullptr, nullptr, final_norm, w.x1, dt, rows, H, d.rms_eps, st)) != DIAL_OK)
+      return s;
+    if ((s = linear(d, d.head_format, head, w.x1, lg, rows, H, n, w.lin_ws, w.sk, st)) != DIAL_OK) return s;
+  }
+  if (keys) return launch_argmax_keys(lg, keys, dt, rows, n, v0, st);
+  return launch_argmax(lg, ids, dt, rows, n, st);
+}
+
+}  // namespace
+
 dial_status dial_decoder_head(const dial_decoder_dims* dims, const void* final_norm,
                               dial_linear_ref head, const void* hidden, const int32_t* row_index,
                               int64_t rows, int32_t* out_ids, void* logits, void* workspace,
@@ -258,26 +300,39 @@ dial_status dial_decoder_head(const dial_decoder_dims* dims, const void* final_n
   Ws w = layout(d, rows, 1, static_cast<uint8_t*>(workspace));
   if (workspace_bytes < w.total)
     return fail(DIAL_ERR_INVALID_ARG, "head workspace must hold %zu bytes", w.total);
-  cudaStream_t st = as_stream(stream);
-  const dial_dtype dt = (dial_dtype)d.act_dtype;
-  const int64_t H = d.hidden, V = d.vocab;
-  void* lg = logits ? logits : w.logits;
-  const bool w8head = d.head_format == DIAL_WFMT_W8A16 || d.head_format == DIAL_WFMT_W8A16_F16S;
-  if (!row_index && w8head && d.act_dtype != DIAL_F32 && rows <= kSkinnyMaxM && w8a16_prologue_ok(rows, H)) {
-    const ActPrologue fin{kProRms, nullptr, nullptr, static_cast<const uint16_t*>(final_norm), d.rms_eps};
-    if ((s = linear(d, d.head_format, head, hidden, lg, rows, H, V, w.lin_ws, w.sk, st, &fin)) != DIAL_OK)
-      return s;
-    return launch_argmax(lg, out_ids, dt, rows, V, st);
-  }
-  const void* src = hidden;
-  if (row_index) {
-    if ((s = launch_gather_rows(hidden, row_index, w.delta, dt, rows, H, st)) != DIAL_OK) return s;
-    src = w.delta;
-  }
-  if ((s = launch_rmsnorm(src, nullptr, nullptr, final_norm, w.x1, dt, rows, H, d.rms_eps, st)) != DIAL_OK)
-    return s;
-  if ((s = linear(d, d.head_format, head, w.x1, lg, rows, H, V, w.lin_ws, w.sk, st)) != DIAL_OK) return s;
-  return launch_argmax(lg, out_ids, dt, rows, V, st);
+  return head_rows(d, final_norm, head, 0, d.vocab, hidden, row_index, rows, out_ids, nullptr, logits,
+                   w, as_stream(stream));
+}
+
+dial_status dial_decoder_head_shard(const dial_decoder_dims* dims, const void* final_norm,
+                                    dial_linear_ref head_shard, int64_t vocab_offset,
+                                    int64_t shard_rows, const void* hidden, const int32_t* row_index,
+                                    int64_t rows, uint64_t* out_keys, void* logits, void* workspace,
+                                    size_t workspace_bytes, dial_stream stream) {
+  clear_error();
+  dial_status s = check_dims(dims);
+  if (s != DIAL_OK) return s;
+  const dial_decoder_dims& d = *dims;
+  if (!final_norm || !head_shard.w || !head_shard.s || !hidden || !out_keys || !workspace)
+    return fail(DIAL_ERR_INVALID_ARG, "null pointer");
+  if (rows <= 0) return fail(DIAL_ERR_INVALID_ARG, "rows must be positive");
+  if (vocab_offset < 0 || shard_rows <= 0 || vocab_offset + shard_rows > d.vocab)
+    return fail(DIAL_ERR_INVALID_ARG, "shard rows [%lld, %lld) outside the vocabulary of %lld",
+                (long long)vocab_offset, (long long)(vocab_offset + shard_rows), (long long)d.vocab);
+  Ws w = layout(d, rows, 1, static_cast<uint8_t*>(workspace));
+  if (workspace_bytes < w.total)
+    return fail(DIAL_ERR_INVALID_ARG, "head workspace must hold %zu bytes", w.total);
+  return head_rows(d, final_norm, head_shard, vocab_offset, shard_rows, hidden, row_index, rows, nullptr,
+                   reinterpret_cast<unsigned long long*>(out_keys), logits, w, as_stream(stream));
+}
+
+dial_status dial_head_merge(const uint64_t* keys, int n_shards, int64_t rows, int32_t* out_ids,
+                            dial_stream stream) {
+  clear_error();
+  if (!keys || !out_ids) return fail(DIAL_ERR_INVALID_ARG, "null pointer");
+  if (n_shards <= 0 || rows <= 0) return fail(DIAL_ERR_INVALID_ARG, "n_shards and rows must be positive");
+  return launch_key_reduce(reinterpret_cast<const unsigned long long*>(keys), n_shards, rows, 1, rows,
+                           nullptr, out_ids, as_stream(stream));
 }
 
 }  // extern "C"

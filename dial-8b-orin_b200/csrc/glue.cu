@@ -648,6 +648,71 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x,
   }
 }
 
+// Per row, the greedy key (argmax_key, indices from `offset`) of the row's
+// largest value: argmax_kernel's choice, as a key that merges across shards.
+template <typename T>
+__global__ void __launch_bounds__(1024) argmax_key_kernel(const T* __restrict__ x,
+                                                          unsigned long long* __restrict__ keys,
+                                                          int64_t n, int64_t offset) {
+  pdl_begin();
+  __shared__ unsigned long long bk[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * n;
+  unsigned long long best = 0ull;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long k = argmax_key(ld(xr, i), offset + i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
+    best = ok > best ? ok : best;
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) bk[w] = best;
+  __syncthreads();
+  if (w == 0) {
+    best = threadIdx.x < (blockDim.x >> 5) ? bk[threadIdx.x] : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
+      best = ok > best ? ok : best;
+    }
+    if (threadIdx.x == 0) keys[row] = best;
+  }
+}
+
+// keys_out[r] / ids[r] from the n keys keys[r * n .. r * n + n) (or, with
+// stride, keys[c * stride + r] for c < n): the largest key, and its index (0
+// when every value of the row was NaN, as argmax_kernel).
+__global__ void __launch_bounds__(256) key_reduce_kernel(const unsigned long long* __restrict__ keys,
+                                                         int64_t n, int64_t elem_stride,
+                                                         int64_t row_stride,
+                                                         unsigned long long* __restrict__ keys_out,
+                                                         int32_t* __restrict__ ids) {
+  pdl_begin();
+  __shared__ unsigned long long bk[8];
+  const int64_t row = blockIdx.x;
+  unsigned long long best = 0ull;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long k = keys[row * row_stride + i * elem_stride];
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
+    best = ok > best ? ok : best;
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) bk[w] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) best = bk[k] > best ? bk[k] : best;
+    if (keys_out) keys_out[row] = best;
+    if (ids) ids[row] = (best >> 32) ? (int32_t)(0xFFFFFFFFu - (uint32_t)best) : 0;
+  }
+}
+
 // cos/sin tables: angle = pos * (1 / theta^(i/ (D/2) ... )) computed in f32 as
 // llama3/cache.rs:31-50 (inv_freq from powf in f32, the product in f32).
 template <typename T>
@@ -898,6 +963,23 @@ dial_status launch_argmax(const void* x, int32_t* out, dial_dtype dt, int64_t ro
                    static_cast<const T*>(x), out, n);
   });
   return s;
+}
+
+dial_status launch_argmax_keys(const void* x, unsigned long long* keys, dial_dtype dt, int64_t rows,
+                               int64_t n, int64_t offset, cudaStream_t st) {
+  dial_status s = DIAL_OK;
+  DISPATCH_T(dt, {
+    s = launch_pdl("argmax_key_kernel", argmax_key_kernel<T>, dim3((unsigned)rows), dim3(1024), 0, st,
+                   static_cast<const T*>(x), keys, n, offset);
+  });
+  return s;
+}
+
+dial_status launch_key_reduce(const unsigned long long* keys, int64_t n, int64_t elem_stride,
+                              int64_t row_stride, int64_t rows, unsigned long long* keys_out,
+                              int32_t* ids, cudaStream_t st) {
+  return launch_pdl("key_reduce_kernel", key_reduce_kernel, dim3((unsigned)rows), dim3(256), 0, st,
+                    keys, n, elem_stride, row_stride, keys_out, ids);
 }
 
 dial_status launch_rope_tables(void* cos_t, void* sin_t, dial_dtype dt, int64_t max_pos,

@@ -44,6 +44,14 @@ dial_status launch_embedding(const void* table, const int32_t* ids, void* out, d
                              int64_t tokens, int64_t vocab, int64_t dim, cudaStream_t st);
 dial_status launch_argmax(const void* x, int32_t* out, dial_dtype dt, int64_t rows, int64_t n,
                           cudaStream_t st);
+// keys[r] = the greedy key (argmax_key) of row r of x [rows, n], indices from offset.
+dial_status launch_argmax_keys(const void* x, unsigned long long* keys, dial_dtype dt, int64_t rows,
+                               int64_t n, int64_t offset, cudaStream_t st);
+// Per row r: the largest of keys[r * row_stride + i * elem_stride], i < n, into
+// keys_out[r] and/or its index into ids[r] (either may be NULL).
+dial_status launch_key_reduce(const unsigned long long* keys, int64_t n, int64_t elem_stride,
+                              int64_t row_stride, int64_t rows, unsigned long long* keys_out,
+                              int32_t* ids, cudaStream_t st);
 dial_status launch_rope_tables(void* cos_t, void* sin_t, dial_dtype dt, int64_t max_pos,
                                int head_dim, float theta, cudaStream_t st);
 

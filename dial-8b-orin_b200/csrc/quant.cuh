@@ -42,9 +42,15 @@ struct ActPrologue {
 };
 bool w8a16_prologue_ok(int64_t M, int64_t K);
 
+// keys (optional): the whole-tile decode GEMV then also writes each tile's
+// greedy key per token (argmax_key of the rounded outputs, rows numbered from
+// key_off) to keys[token * ceil(N / 16) + tile], and *keyed reports whether it
+// did (other paths leave that to the caller); y may then be NULL.
 dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
                                 dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
-                                cudaStream_t st, void* sk_ws, const ActPrologue* pro = nullptr);
+                                cudaStream_t st, void* sk_ws, const ActPrologue* pro = nullptr,
+                                unsigned long long* keys = nullptr, int64_t key_off = 0,
+                                bool* keyed = nullptr);
 // GGUF integer path: activations quantised to Q8_0 in `ws` first.
 size_t gguf_skinny_workspace_bytes(int64_t M, int64_t K);
 dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,

@@ -202,6 +202,64 @@ __device__ __forceinline__ void w8a16_store(const float (&acc)[NT][4], const ST*
   }
 }
 
+// w8a16_store, plus the tile's greedy key per token (the largest argmax_key of
+// its 16 rows' rounded outputs, rows numbered from key_off) in
+// keys[token * tiles + tile]; y == nullptr stores no outputs.  The whole warp
+// calls it.
+template <int NT, bool BF16, typename ST>
+__device__ __forceinline__ void w8a16_store_keys(const float (&acc)[NT][4], const ST* __restrict__ scale,
+                                                 uint16_t* __restrict__ y, int M, int N, int tile,
+                                                 unsigned long long* __restrict__ keys, int tiles,
+                                                 long long key_off) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int row0 = tile * 16;
+  const int r[2] = {row0 + g, row0 + g + 8};
+  unsigned long long best[NT][2];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) best[j][0] = best[j][1] = 0ull;
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    if (r[hr] >= N) continue;
+    const float sc = Act<ST>::to_f32(scale[r[hr]]);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int tok = j * 8 + 2 * t + c;
+        if (tok >= M) continue;
+        const float v = acc[j][2 * hr + c] * sc;
+        uint16_t bits;
+        float rv;
+        if (BF16) {
+          const __nv_bfloat16 h = __float2bfloat16_rn(v);
+          bits = __bfloat16_as_ushort(h);
+          rv = __bfloat162float(h);
+        } else {
+          const __half h = __float2half_rn(v);
+          bits = __half_as_ushort(h);
+          rv = __half2float(h);
+        }
+        if (y) y[(size_t)tok * N + r[hr]] = bits;
+        const unsigned long long k = argmax_key(rv, key_off + r[hr]);
+        best[j][c] = k > best[j][c] ? k : best[j][c];
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      unsigned long long k = best[j][c];
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {  // over the 8 row groups g (same t)
+        const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+        k = ok > k ? ok : k;
+      }
+      const int tok = j * 8 + 2 * t + c;
+      if (g == 0 && tok < M) keys[(size_t)tok * tiles + tile] = k;
+    }
+}
+
 // ------------------------------------------------------------------ GGUF pieces
 template <int NT, int TYPE>
 __device__ __forceinline__ void gguf_segment(const uint8_t* __restrict__ qs,
@@ -1065,7 +1123,8 @@ template <int NT, bool BF16, typename ST>
 __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     w8a16_gemv_kernel(const __grid_constant__ CUtensorMap wmap, const ST* __restrict__ scale,
                       const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M, int N, int K,
-                      int tiles, int ng, int* err, ActPrologue pro) {
+                      int tiles, int ng, int* err, ActPrologue pro, unsigned long long* keys,
+                      long long key_off) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = (tma::smem_u32(smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -1115,7 +1174,8 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
       const float m0 = t0 < M ? lds32f(tm + 4u * t0) : 1.0f, m1 = t0 + 1 < M ? lds32f(tm + 4u * (t0 + 1)) : 1.0f;
       b[j][0] = a[j][0] * m0, b[j][1] = a[j][1] * m1, b[j][2] = a[j][2] * m0, b[j][3] = a[j][3] * m1;
     }
-    w8a16_store<NT, BF16, ST>(b, scale, y, M, N, tile * 16);
+    if (keys) w8a16_store_keys<NT, BF16, ST>(b, scale, y, M, N, tile, keys, tiles, key_off);
+    else w8a16_store<NT, BF16, ST>(b, scale, y, M, N, tile * 16);
   };
   const uint32_t part = aux + kAuxCs, ctr = aux + kAuxCnt;
   // kChains independent accumulator chains (MMA m of a unit feeds chain m %
@@ -1710,7 +1770,9 @@ bool w8a16_prologue_ok(int64_t M, int64_t K) { return K >= 128 && K % 16 == 0 &&
 
 dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, const void* scale,
                                 dial_dtype sdt, void* y, int64_t M, int64_t K, int64_t N,
-                                cudaStream_t st, void* sk_ws, const ActPrologue* pro_in) {
+                                cudaStream_t st, void* sk_ws, const ActPrologue* pro_in,
+                                unsigned long long* keys, int64_t key_off, bool* keyed) {
+  if (keyed) *keyed = false;
   const ActPrologue pro = pro_in ? *pro_in : ActPrologue{kProX, nullptr, nullptr, nullptr, 0.0f};
   if (pro.mode != kProX && !(sk_ws && aligned16(q) && aligned16(x) && w8a16_prologue_ok(M, K)))
     return fail(DIAL_ERR_SHAPE, "the fused prologue needs the staged decode path");
@@ -1740,7 +1802,7 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
   if (ae == cudaSuccess)                                                                           \
     s = launch_pdl("w8a16_gemv_kernel", w8a16_gemv_kernel<NT_, BF, ST>, dim3((unsigned)C),         \
                    dim3(kTmaWarps * 32), smem, st, map, static_cast<const ST*>(scale), xp, yp,     \
-                   (int)M, (int)N, (int)K, (int)tiles, (int)ng, err0, pro)
+                   (int)M, (int)N, (int)K, (int)tiles, (int)ng, err0, pro, keys, (long long)key_off)
 #define GV_NT(BF, ST)     \
   if (nt == 1) {          \
     GV(1, BF, ST);        \
@@ -1755,8 +1817,10 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
 #undef GV_NT
 #undef GV
       if (ae != cudaSuccess) return cuda_fail(ae, "cudaFuncSetAttribute(w8a16_gemv_kernel)");
+      if (keyed && keys && s == DIAL_OK) *keyed = true;
       return s;
     }
+    if (!yp) return fail(DIAL_ERR_INVALID_ARG, "null output");
     float* slots = static_cast<float*>(sk_ws);
     int* cnt = reinterpret_cast<int*>(static_cast<uint8_t*>(sk_ws) + slot_bytes());
     int* err = device_error_ptr();

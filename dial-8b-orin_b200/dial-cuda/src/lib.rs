@@ -284,6 +284,13 @@ extern "C" {
                              hidden: *const c_void, row_index: *const i32, rows: i64, out_ids: *mut i32,
                              logits: *mut c_void, workspace: *mut c_void, workspace_bytes: usize,
                              stream: dial_stream) -> dial_status;
+    pub fn dial_decoder_head_shard(dims: *const dial_decoder_dims, final_norm: *const c_void,
+                                   head_shard: dial_linear_ref, vocab_offset: i64, shard_rows: i64,
+                                   hidden: *const c_void, row_index: *const i32, rows: i64,
+                                   out_keys: *mut u64, logits: *mut c_void, workspace: *mut c_void,
+                                   workspace_bytes: usize, stream: dial_stream) -> dial_status;
+    pub fn dial_head_merge(keys: *const u64, n_shards: c_int, rows: i64, out_ids: *mut i32,
+                           stream: dial_stream) -> dial_status;
 
     // stage planner (AutoPlanner::plan_with_algorithm, spm/planner.rs:378-522)
     pub fn dial_plan_stages(model: *const dial_plan_model, objective: *const dial_plan_objective,

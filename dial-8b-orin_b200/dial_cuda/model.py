@@ -56,6 +56,10 @@ _SIGS = {
     "dial_decoder_head": ([ctypes.POINTER(DecoderDims), ctypes.c_void_p, LinearRef, ctypes.c_void_p,
                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
                            ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
+    "dial_decoder_head_shard": ([ctypes.POINTER(DecoderDims), ctypes.c_void_p, LinearRef, ctypes.c_int64,
+                                 ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                 ctypes.c_void_p], ctypes.c_int),
 }
 
 
@@ -122,7 +126,8 @@ class Stage:
 
     def __init__(self, cfg: ModelConfig, first: int, last: int, n_slots: int, max_seq: int,
                  seed: int = 299792458, device=None, with_embed: Optional[bool] = None,
-                 with_head: Optional[bool] = None, weights: Optional[dict] = None):
+                 with_head: Optional[bool] = None, weights: Optional[dict] = None,
+                 head_rows: Optional[tuple] = None):
         torch = _torch()
         self.L = _bind()
         self.cfg, self.first, self.last = cfg, first, last
@@ -188,10 +193,18 @@ class Stage:
             self.embed = e.to(self.dt)
             del e
         self.head = None
-        if self.with_head:
+        # head_rows = (v0, v1): this stage's share of a vocabulary-parallel head
+        # (rows v0..v1 of the same seeded head), used by head_shard_forward
+        self.head_rows = tuple(head_rows) if head_rows is not None else None
+        self.head_shard = None
+        if self.with_head or (self.head_rows is not None and self.head_rows[1] > self.head_rows[0]):
             self.final_norm = ones(H, "final_norm")
             w = rand((c.vocab, H), "lm_head")
-            self.head = _Linear(c.head_format, w)
+            if self.head_rows is not None:
+                v0, v1 = self.head_rows
+                self.head_shard = _Linear(c.head_format, w[v0:v1].contiguous())
+            if self.with_head:
+                self.head = _Linear(c.head_format, w)
             del w
         # RoPE tables (llama3/cache.rs:24-64) in the activation dtype
         self.cos = torch.empty((max_seq, D // 2), device=self.device, dtype=self.dt)
@@ -207,6 +220,8 @@ class Stage:
         b = sum(l.weight_bytes for l in self.linears)
         if self.head is not None:
             b += self.head.weight_bytes
+        if self.head_shard is not None:
+            b += self.head_shard.weight_bytes
         return b
 
     def workspace(self, tokens: int, max_len: int):
@@ -247,6 +262,48 @@ class Stage:
                                        logits.data_ptr() if logits is not None else None,
                                        ws.data_ptr(), need, stream_ptr()), "dial_decoder_head")
         return out_ids
+
+
+    def head_shard_forward(self, hidden, keys_out, row_index=None, logits=None):
+        """This stage's share of a vocabulary-parallel head: keys_out (int64
+        [rows], the unsigned greedy keys' bits) of head rows head_rows over
+        rmsnorm(hidden) (dial_decoder_head_shard); logits [rows, v1 - v0]."""
+        rows = keys_out.numel()
+        v0, v1 = self.head_rows
+        ws, need = self.workspace(max(rows, hidden.shape[0]), 1)
+        check(self.L.dial_decoder_head_shard(ctypes.byref(self.dims), self.final_norm.data_ptr(),
+                                             self.head_shard.ref, v0, v1 - v0, hidden.data_ptr(),
+                                             row_index.data_ptr() if row_index is not None else None,
+                                             rows, keys_out.data_ptr(),
+                                             logits.data_ptr() if logits is not None else None,
+                                             ws.data_ptr(), need, stream_ptr()), "dial_decoder_head_shard")
+        return keys_out
+
+
+def head_merge(keys, out_ids):
+    """keys int64 [n_shards, rows] (the shards' greedy keys) -> out_ids int32 [rows]."""
+    n, rows = keys.shape
+    check(lib().dial_head_merge(keys.data_ptr(), n, rows, out_ids.data_ptr(), stream_ptr()),
+          "dial_head_merge")
+    return out_ids
+
+
+def vocab_shards(vocab: int, weights) -> list:
+    """Splits the head's rows over stages in proportion to `weights` (a stage
+    with weight 0 holds none), each share a multiple of 16 rows (one GEMV tile)
+    except the last non-empty one; returns [(v0, v1)] per stage."""
+    tot = float(sum(weights))
+    if tot <= 0:
+        raise ValueError("no stage takes a share of the head")
+    out, v0, acc = [], 0, 0.0
+    last = max(i for i, w in enumerate(weights) if w > 0)
+    for i, w in enumerate(weights):
+        acc += w
+        v1 = vocab if i >= last else min(vocab, int(round(vocab * acc / tot / 16)) * 16)
+        v1 = max(v0, v1)
+        out.append((v0, v1))
+        v0 = v1
+    return out
 
 
 class Decoder:

@@ -19,6 +19,16 @@ asynchronous (a send buffer is reused only after its previous send finished)
 and each stage pair has its own channel, so the token ring back to stage 0
 cannot block the forward chain.
 
+Vocabulary-parallel head (Pipeline(..., head_channel=, head_rows=)): every
+stage holds a share of the output head's rows; the last stage sends each
+micro-batch's final hidden state to the stages with rows (on a side stream,
+so the forward chain does not wait for it), each computes the greedy keys of
+its rows (final norm + GEMV + argmax, dial_decoder_head_shard) and sends them
+to stage 0, which merges them into the token (dial_head_merge) -- no stage
+reads the whole head, and the token ring carries 8-byte keys instead of the
+token.  This is the reference's output head split by vocabulary rows (its
+head runs on the last worker, worker_gguf.rs:342-386, qwen3_vl.rs:2420-2451).
+
 The communication is a `Channel` object: NcclChannel (the C ABI's NCCL stage
 communicators, dial_stage_comm_*, over NVLink between GPUs) or TorchChannel
 (torch.distributed point-to-point; gloo for the CPU tests).  The compute of a
@@ -37,6 +47,23 @@ def _torch():
 
 
 # ------------------------------------------------------------------ channels
+def pipeline_links(P: int) -> List[tuple]:
+    """The hand-off links: stage s -> s+1, and the token ring P-1 -> 0."""
+    return [(s, s + 1) for s in range(P - 1)] + ([(P - 1, 0)] if P > 1 else [])
+
+
+def head_links(P: int, rows: Sequence) -> List[tuple]:
+    """The vocabulary-parallel head's links, in their global set-up order: the
+    last stage's final hidden state to every other stage with head rows, then
+    each stage's greedy keys to stage 0 (the last stage's keys reuse its link
+    to stage 0)."""
+    out = [(P - 1, s) for s in range(P - 1) if rows[s]]
+    out += [(s, 0) for s in range(1, P - 1) if rows[s]]
+    if rows[P - 1] and (P - 1, 0) not in out:
+        out.append((P - 1, 0))
+    return out
+
+
 class TorchChannel:
     """Point-to-point sends over torch.distributed, one process group per link:
     fwd[s] carries stage s -> s+1, `ring` carries the last stage -> stage 0.
@@ -44,20 +71,18 @@ class TorchChannel:
     a blocked send on one link never holds up another link's operations.
     Every rank creates every group, in the same order (a torch requirement)."""
 
-    def __init__(self, world: Optional[int] = None):
+    def __init__(self, world: Optional[int] = None, links: Optional[List[tuple]] = None):
         import torch.distributed as dist  # noqa: PLC0415
         self.dist = dist
         self.rank = dist.get_rank()
         P = world if world is not None else dist.get_world_size()
         self.P = P
-        self.fwd = [dist.new_group([s, s + 1]) for s in range(P - 1)]
-        self.ring = dist.new_group([P - 1, 0]) if P > 1 else None
+        self.links = list(links) if links is not None else pipeline_links(P)
+        self.groups = [dist.new_group(sorted({a, b})) for a, b in self.links]
 
     def _group(self, a: int, b: int):  # link a -> b
-        if b == a + 1:
-            return self.fwd[a]
-        if a == self.P - 1 and b == 0:
-            return self.ring
+        if (a, b) in self.links:
+            return self.groups[self.links.index((a, b))]
         raise ValueError(f"no pipeline link {a} -> {b}")
 
     def isend(self, t, dst: int):
@@ -89,7 +114,8 @@ class NcclChannel:
     links in the global link order, so no two ranks wait on each other's
     initialisation in a cycle; every host wait is bounded by `timeout_s`."""
 
-    def __init__(self, rank: int, world: int, timeout_s: float = 60.0):
+    def __init__(self, rank: int, world: int, timeout_s: float = 60.0,
+                 links: Optional[List[tuple]] = None):
         import ctypes  # noqa: PLC0415
 
         import torch.distributed as dist  # noqa: PLC0415
@@ -97,7 +123,7 @@ class NcclChannel:
         from . import ID_BYTES, check, lib  # noqa: PLC0415
         torch = _torch()
         self.rank, self.P, self.L = rank, world, lib()
-        self.links = [(s, s + 1) for s in range(world - 1)] + ([(world - 1, 0)] if world > 1 else [])
+        self.links = list(links) if links is not None else pipeline_links(world)
         mine = {}
         for i, (a, _) in enumerate(self.links):
             if a == rank:
@@ -197,7 +223,10 @@ class ModelStageCompute(StageCompute):
     (micro-batch b holds KV slots b*mb_size .. b*mb_size + mb_size - 1), each
     step captured once as a CUDA graph per micro-batch."""
 
-    def __init__(self, stage, n_mb: int, prompt_len: int, use_graphs: bool = True, mb_size: int = 1):
+    def __init__(self, stage, n_mb: int, prompt_len: int, use_graphs: bool = True, mb_size: int = 1,
+                 vocab_head_stages: int = 0):
+        """vocab_head_stages = P: the head is vocabulary-parallel over P stages
+        (the stage holds rows stage.head_rows; the last stage runs no head)."""
         torch = _torch()
         self.st = stage
         self.first, self.last = stage.first == 0, stage.last == stage.cfg.n_layers
@@ -205,6 +234,13 @@ class ModelStageCompute(StageCompute):
         dev, dt, H, R = stage.device, stage.dt, stage.cfg.hidden, mb_size
         self.hidden = [torch.zeros((R, H), device=dev, dtype=dt) for _ in range(n_mb)]
         self.tokens = [torch.zeros(R, device=dev, dtype=torch.int32) for _ in range(n_mb)]
+        self.vocab_head = vocab_head_stages > 0
+        if self.vocab_head:
+            P = vocab_head_stages
+            self.head_in = [torch.zeros((R, H), device=dev, dtype=dt) for _ in range(n_mb)]
+            # stage 0 gathers every stage's keys ([P, R], its own in row 0)
+            self.keys = [torch.zeros((P if self.first else 1, R), device=dev, dtype=torch.int64)
+                         for _ in range(n_mb)]
         self.pos = [torch.full((R,), prompt_len, device=dev, dtype=torch.int32) for _ in range(n_mb)]
         self.slot = [torch.arange(b * R, (b + 1) * R, device=dev, dtype=torch.int32) for b in range(n_mb)]
         self.use_graphs = use_graphs
@@ -221,8 +257,25 @@ class ModelStageCompute(StageCompute):
         if self.first:
             st.embed_tokens(self.tokens[b], self.hidden[b])
         st.layers_forward(self.hidden[b], self.pos[b], self.slot[b], st.max_seq)
-        if self.last:
+        if self.last and not self.vocab_head:
             st.head_forward(self.hidden[b], self.tokens[b])
+
+    # vocabulary-parallel head
+    def head_input(self, b):  # where the last stage's final hidden state arrives
+        return self.hidden[b] if self.last else self.head_in[b]
+
+    def head_keys(self, b):  # this stage's keys [R]
+        return self.keys[b][0]
+
+    def gathered_keys(self, b, s):  # stage 0: the row of stage s's keys
+        return self.keys[b][s]
+
+    def run_head_shard(self, b):
+        self.st.head_shard_forward(self.head_input(b), self.head_keys(b))
+
+    def merge(self, b):
+        from .model import head_merge  # noqa: PLC0415
+        head_merge(self.keys[b], self.tokens[b])
 
     def capture(self) -> None:
         """Captures one graph per micro-batch (its positions advance in place)."""
@@ -274,7 +327,9 @@ class ModelStageCompute(StageCompute):
         if self.first:
             st.embed_tokens(ids, h)
         st.layers_forward(h, self._ppos, torch.full((T,), seq, device=st.device, dtype=torch.int32), T)
-        if self.last:
+        if self.last and self.vocab_head:  # the head runs on every stage (Pipeline._head_exchange)
+            self.hidden[b][i].copy_(h[T - 1])
+        elif self.last:
             st.head_forward(h, self.tokens[b][i:i + 1], row_index=self._plast)
 
 
@@ -282,10 +337,21 @@ class ModelStageCompute(StageCompute):
 class Pipeline:
     """Stage `rank` of a `world`-stage pipeline over n_mb micro-batches."""
 
-    def __init__(self, rank: int, world: int, compute: StageCompute, channel, n_mb: int):
+    def __init__(self, rank: int, world: int, compute: StageCompute, channel, n_mb: int,
+                 head_channel=None, head_rows: Optional[Sequence] = None):
+        """head_rows (per stage, the number of head rows it holds) with
+        head_channel (links head_links(world, head_rows)): the head is
+        vocabulary-parallel; otherwise it runs on the last stage."""
         if world > 1 and n_mb < world:
             raise ValueError(f"{n_mb} micro-batches cannot keep {world} stages busy")
         self.rank, self.world, self.c, self.ch, self.n_mb = rank, world, compute, channel, n_mb
+        self.vocab = head_rows is not None and world > 1
+        self.hch, self.rows = head_channel, list(head_rows) if head_rows is not None else None
+        if self.vocab and (head_channel is None or not getattr(compute, "vocab_head", False)):
+            raise ValueError("a vocabulary-parallel head needs head_channel and a vocab-head compute")
+        self.head_pending = [[] for _ in range(n_mb)]  # head sends that read this micro-batch's buffers
+        self.merged = [None] * n_mb  # stage 0: event of each micro-batch's merged token
+        self._hs = None  # the head's side stream
         self.pending = [None] * n_mb  # last send of each micro-batch's output buffer
         self.t = 0  # decode steps since the last prefill
         self.host_io = None  # (host_in, host_out): pinned int32 token copies for host_io steps
@@ -321,11 +387,73 @@ class Pipeline:
         elif r == 0:
             ch.irecv(ring, P - 1).wait()
 
+    def _connect_head(self) -> None:
+        """One matched transfer per head link and message kind, in head_links
+        order (as _connect): the final hidden state on the last stage's links,
+        keys on the links into stage 0."""
+        r, P, c = self.rank, self.world, self.c
+        h, k = c.hidden_buffer(0).clone(), c.head_keys(0).clone()
+        for a, b in head_links(P, self.rows):
+            kinds = ([h] if a == P - 1 and self.rows[b] else []) + ([k] if b == 0 and self.rows[a] else [])
+            for t in kinds:
+                if r == a:
+                    self.hch.isend(t, b).wait()
+                elif r == b:
+                    self.hch.irecv(t, a).wait()
+
     def _connect_steps(self) -> None:
         if self.world > 1 and not self._connected:
             c = self.c
             self._connect(c.hidden_buffer(0).clone(), c.token_buffer(0).clone())
+            if self.vocab:
+                self._connect_head()
             self._connected = True
+
+    def _wait_merged(self, b) -> None:  # stage 0: b's tokens are merged
+        if self.merged[b] is not None:
+            _torch().cuda.current_stream().wait_event(self.merged[b])
+
+    def _wait_head(self, b) -> None:
+        for d in self.head_pending[b]:
+            d.wait()
+        self.head_pending[b] = []
+
+    def _head_exchange(self, b) -> None:
+        """The vocabulary-parallel head for micro-batch b (every stage, after
+        its compute of b): on the side stream, the last stage sends the final
+        hidden state to the stages with rows, each computes its keys and sends
+        them to stage 0, and stage 0 merges them into b's tokens."""
+        import contextlib  # noqa: PLC0415
+        torch = _torch()
+        r, P, c, hch = self.rank, self.world, self.c, self.hch
+        cuda = torch.cuda.is_available()  # (the CPU tests run it synchronously over gloo)
+        if cuda and self._hs is None:
+            self._hs = torch.cuda.Stream()
+        hs = self._hs
+        if cuda:
+            hs.wait_stream(torch.cuda.current_stream())  # b's compute on this stage
+        with torch.cuda.stream(hs) if cuda else contextlib.nullcontext():
+            self._wait_head(b)  # the buffers of b's previous exchange are free again
+            sends = []
+            if r == P - 1:
+                sends += [hch.isend(c.hidden_buffer(b), s) for s in range(P - 1) if self.rows[s]]
+            elif self.rows[r]:
+                hch.irecv(c.head_input(b), P - 1).wait()
+            if self.rows[r]:
+                c.run_head_shard(b)
+                if r != 0:
+                    sends.append(hch.isend(c.head_keys(b), 0))
+            self.head_pending[b] = sends
+            if r == 0:
+                for s in range(1, P):
+                    if self.rows[s]:
+                        hch.irecv(c.gathered_keys(b, s), s).wait()
+                c.merge(b)
+                ev = None
+                if cuda:
+                    ev = torch.cuda.Event()
+                    ev.record(hs)
+                self.merged[b] = ev
 
     def steps(self, n_steps: int, host_io: bool = False) -> None:
         """n_steps decode steps: every micro-batch advances one token per step.
@@ -347,8 +475,12 @@ class Pipeline:
                 tok = c.token_buffer(b)
                 if P > 1:
                     self._wait_send(b)  # the buffer is an input of this micro-batch again
+                    if self.vocab:
+                        self._wait_head(b)
                     if r == 0:
-                        if self.t > 0:
+                        if self.vocab:
+                            self._wait_merged(b)
+                        elif self.t > 0:
                             ch.irecv(tok, P - 1).wait()
                     else:
                         ch.irecv(c.hidden_buffer(b), r - 1).wait()
@@ -359,14 +491,16 @@ class Pipeline:
                     tok.copy_(hin, non_blocking=True)
                 c.run(b)
                 c.advance(b)
-                if host_io and r == P - 1:
+                if host_io and r == P - 1 and not self.vocab:
                     self.host_io[1][b].copy_(tok, non_blocking=True)
                 if P > 1:
                     if r < P - 1:
                         self.pending[b] = ch.isend(c.hidden_buffer(b), r + 1)
-                    else:
+                    elif not self.vocab:
                         self.pending[b] = ch.isend(tok, 0)
-            if host_io and r == P - 1:
+                    if self.vocab:
+                        self._head_exchange(b)
+            if host_io and r == P - 1 and not self.vocab:
                 torch.cuda.current_stream().synchronize()
             self.t += 1
 
@@ -376,7 +510,10 @@ class Pipeline:
         its sends."""
         if self.world > 1 and self.rank == 0 and self.t > 0:
             for b in range(self.n_mb):
-                self.ch.irecv(self.c.token_buffer(b), self.world - 1).wait()
+                if self.vocab:
+                    self._wait_merged(b)
+                else:
+                    self.ch.irecv(self.c.token_buffer(b), self.world - 1).wait()
         self.drain()
         self.t = 0
 
@@ -387,6 +524,7 @@ class Pipeline:
     def drain(self) -> None:
         for b in range(self.n_mb):
             self._wait_send(b)
+            self._wait_head(b)
 
     def prefill(self, prompts: Optional[Sequence] = None, prompt_len: int = 0) -> None:
         """Prefills every sequence (stage 0 holds the prompts, one per sequence,
@@ -413,11 +551,16 @@ class Pipeline:
                     c.prefill_run(b, prompts[b * R + i] if r == 0 else None, i)
                 if r < P - 1:
                     ch.isend(buf, r + 1).wait()
-            if r == P - 1 and P > 1:
+            if self.vocab:
+                self._head_exchange(b)
+            elif r == P - 1 and P > 1:
                 self.pending[b] = ch.isend(c.token_buffer(b), 0)
         if P > 1 and r == 0:
             for b in range(B):
-                ch.irecv(c.token_buffer(b), P - 1).wait()
+                if self.vocab:
+                    self._wait_merged(b)
+                else:
+                    ch.irecv(c.token_buffer(b), P - 1).wait()
         self.drain()
         self.t = 0
 

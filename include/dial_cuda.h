@@ -360,6 +360,32 @@ DIAL_API dial_status dial_decoder_head(const dial_decoder_dims* dims, const void
                                        void* logits, void* workspace, size_t workspace_bytes,
                                        dial_stream stream);
 
+/* Vocabulary-parallel head (a stage's share of the output head): rows
+ * [vocab_offset, vocab_offset + shard_rows) of the head, given as their own
+ * [shard_rows, hidden] linear; the final norm and the GEMV as
+ * dial_decoder_head, then per hidden row the greedy key of the shard's
+ * largest logit: out_keys[r] = (order-preserving 32 bits of the rounded logit
+ * << 32) | (0xFFFFFFFF - vocabulary index), so the largest key over all
+ * shards is the first index of the maximum -- dial_decoder_head's argmax
+ * (NaN never wins).  logits (optional, [rows, shard_rows]) receives the
+ * shard's logits: the logits hand-back of the reference's output head
+ * (worker_gguf.rs:342-386, RemoteOutputKind::Logits qwen3_vl.rs:258-279),
+ * gathered by the caller.  The workspace is
+ * dial_decoder_workspace_bytes(dims, rows, 1). */
+DIAL_API dial_status dial_decoder_head_shard(
+    const dial_decoder_dims* dims, const void* final_norm, dial_linear_ref head_shard,
+    int64_t vocab_offset, int64_t shard_rows, const void* hidden, const int32_t* row_index,
+    int64_t rows, uint64_t* out_keys, void* logits, void* workspace, size_t workspace_bytes,
+    dial_stream stream);
+
+/* Greedy token from the shards' keys: keys [n_shards, rows] (shard-major, as
+ * gathered), out_ids[r] = the vocabulary index of the largest keys[., r] (0 if
+ * every logit was NaN) -- the sampled-token hand-back with greedy sampling
+ * (sample_remote_logits at temperature <= 0, qwen3_vl.rs:282-323; the
+ * SampledToken kind, qwen3_vl.rs:262-264). */
+DIAL_API dial_status dial_head_merge(const uint64_t* keys, int n_shards, int64_t rows,
+                                     int32_t* out_ids, dial_stream stream);
+
 /* ------------------------------------------------------------------ stage planner
  * Host-only (no GPU needed).  Restates AutoPlanner::plan_with_algorithm
  * (dial-core/src/spm/planner.rs:378-522, segment_cost :743-836): contiguous

@@ -299,3 +299,112 @@ def test_missing_peer_fails_within_the_timeout(tmp_path):
     mp.start_processes(_lonely, args=(2, _free_port(), str(tmp_path)), nprocs=1, join=True,
                        start_method="spawn")
     assert (tmp_path / "lonely0.txt").read_text() != "joined"
+
+
+# ------------------------------------------------------------------ vocabulary-parallel head
+class FakeVocabCompute(FakeComputeRows):
+    """The same stages with the head split by vocabulary rows: stage s holds
+    rows [v0, v1) of a stand-in head whose logit for id v peaks at
+    FakeCompute.sample(h) (so the merged token must equal the single-process
+    chain's), and produces greedy keys as dial_decoder_head_shard does
+    (value << 32 | 0xFFFFFFFF - id; the largest key is the first maximum)."""
+
+    def __init__(self, r, world, n_mb, R, span):
+        super().__init__(r, world, n_mb, R)
+        self.vocab_head = True
+        self.v0, self.v1 = span
+        self.head_in = [torch.zeros(R, H) for _ in range(n_mb)]
+        self.keys = [torch.zeros((world if r == 0 else 1, R), dtype=torch.int64) for _ in range(n_mb)]
+
+    def run(self, b):
+        for i in range(self.mb_size):
+            if self.first:
+                self.hidden[b][i].copy_(self.embed(self.tokens[b][i]))
+            self.hidden[b][i].copy_(self.layers(self.hidden[b][i], self.pos[b]))
+
+    def prefill_run(self, b, ids=None, i=0):
+        if self.first:
+            self.pbuf.copy_(torch.stack([self.embed(torch.tensor(k)) for k in ids]))
+        self.pbuf.copy_(self.layers(self.pbuf, -1))
+        if self.last:
+            self.hidden[b][i].copy_(self.pbuf[-1])
+
+    def head_input(self, b):
+        return self.hidden[b] if self.last else self.head_in[b]
+
+    def head_keys(self, b):
+        return self.keys[b][0]
+
+    def gathered_keys(self, b, s):
+        return self.keys[b][s]
+
+    def run_head_shard(self, b):
+        for i in range(self.mb_size):
+            target = int(self.sample(self.head_input(b)[i])[0])
+            best = 0
+            for v in range(self.v0, self.v1):
+                key = ((V - abs(v - target)) << 32) | (0xFFFFFFFF - v)
+                best = max(best, key)
+            self.keys[b][0][i] = best
+
+    def merge(self, b):
+        for i in range(self.mb_size):
+            k = int(self.keys[b][:, i].max())
+            self.tokens[b][i] = 0xFFFFFFFF - (k & 0xFFFFFFFF)
+
+
+def _vocab_worker(rank, world, port, n_mb, R, prompts, steps, result_dir, shares):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "dial-8b-orin_b200"))
+    from dial_cuda.model import vocab_shards
+    from dial_cuda.pipeline import Pipeline, TorchChannel, head_links, init_distributed
+    init_distributed("gloo", timeout_s=30)
+    spans = vocab_shards(V, shares)
+    rows = [v1 - v0 for v0, v1 in spans]
+    c = FakeVocabCompute(rank, world, n_mb, R, spans[rank])
+    hch = TorchChannel(world, links=head_links(world, rows))
+    p = Pipeline(rank, world, c, TorchChannel(world), n_mb, head_channel=hch, head_rows=rows)
+    p.prefill(prompts if rank == 0 else None, prompt_len=len(prompts[0]))
+    firsts = [int(v) for t in c.tokens for v in t.reshape(-1)]
+    p.steps(2)
+    p.steps(steps - 2)
+    p.finish()
+    torch.save({"firsts": firsts, "after_finish": [int(v) for t in c.tokens for v in t.reshape(-1)]},
+               os.path.join(result_dir, f"v{rank}.pt"))
+    import torch.distributed as dist
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,shares", [(2, [1, 1]), (3, [1, 2, 1]), (4, [0, 1, 0, 3]),
+                                          (4, [1, 1, 1, 0])])
+def test_vocab_parallel_head_matches_single_process_chain(world, shares, tmp_path):
+    """The head split over the stages by vocabulary rows (uneven shares, stages
+    with none, the last stage with none): the tokens merged on stage 0 after
+    prefill and after the decode steps equal the single-process chain's."""
+    n_mb, R, steps = max(3, world), 2, 5
+    prompts = [[(3 * s + 7 * i + 1) % V for i in range(4)] for s in range(n_mb * R)]
+    mp.start_processes(_vocab_worker,
+                       args=(world, _free_port(), n_mb, R, prompts, steps, str(tmp_path), shares),
+                       nprocs=world, join=True, start_method="spawn")
+    ref = reference(world, n_mb * R, prompts, steps)
+    r0 = torch.load(tmp_path / "v0.pt")
+    assert r0["firsts"] == [seq[0] for seq in ref]
+    assert r0["after_finish"] == [seq[-1] for seq in ref]
+
+
+def test_vocab_shards_and_head_links():
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "dial-8b-orin_b200"))
+    from dial_cuda.model import vocab_shards
+    from dial_cuda.pipeline import head_links
+    spans = vocab_shards(151936, [1] * 8)
+    assert spans[0][0] == 0 and spans[-1][1] == 151936
+    assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    assert all((v1 - v0) % 16 == 0 for v0, v1 in spans[:-1])
+    assert vocab_shards(100, [0, 1, 0]) == [(0, 0), (0, 100), (100, 100)]
+    assert head_links(4, [1, 1, 1, 1]) == [(3, 0), (3, 1), (3, 2), (1, 0), (2, 0)]
+    assert head_links(4, [0, 1, 0, 3]) == [(3, 1), (1, 0), (3, 0)]
+    assert head_links(3, [5, 5, 0]) == [(2, 0), (2, 1), (1, 0)]

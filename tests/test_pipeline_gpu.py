@@ -6,7 +6,9 @@
   the layers, the hand-off runs through the C ABI's stage communicators
   (dial_stage_comm_*), and the tokens equal the single-GPU ones (the weights of
   a layer do not depend on the split, and the arithmetic of a layer is the
-  same).
+  same).  Also with the vocabulary-parallel head: each rank holds half of the
+  head's rows (both halves above the whole-tile GEMV's size, so each row's
+  logit is computed exactly as on one GPU) and stage 0 merges the keys.
 """
 import json
 import os
@@ -26,12 +28,12 @@ SMALL = dict(n_layers=4, hidden=1024, intermediate=2048, n_heads=8, n_kv_heads=2
 N_MB, PROMPT, STEPS = 4, 24, 6
 
 
-def _cfg(gguf: bool = False):
+def _cfg(gguf: bool = False, vocab: int = SMALL["vocab"]):
     from dial_cuda.model import WFMT_Q4_0, WFMT_Q8_0, ModelConfig
     if gguf:  # the Llama-style GGUF decoder: Q4_0 layers, Q8_0 head, f16, no QK-norm
         return ModelConfig(**dict(SMALL, act_dtype="f16", qk_norm=False, rope_theta=5e5,
-                                  weight_format=WFMT_Q4_0, head_format=WFMT_Q8_0))
-    return ModelConfig(**SMALL)
+                                  weight_format=WFMT_Q4_0, head_format=WFMT_Q8_0, vocab=vocab))
+    return ModelConfig(**dict(SMALL, vocab=vocab))
 
 
 def _prompts(torch):
@@ -40,10 +42,10 @@ def _prompts(torch):
             for _ in range(N_MB)]
 
 
-def reference_tokens(torch, gguf: bool = False):
+def reference_tokens(torch, gguf: bool = False, vocab: int = SMALL["vocab"]):
     """Greedy tokens of every sequence from the single-stage Decoder."""
     from dial_cuda.model import Decoder
-    dec = Decoder(_cfg(gguf), n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
+    dec = Decoder(_cfg(gguf, vocab), n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
     out = []
     for b, p in enumerate(_prompts(torch)):
         tok = dec.prefill(p, slot=b)
@@ -113,16 +115,28 @@ def _two_stage_worker():
     """Body of one rank (run by torchrun): writes this rank's tokens to DIAL_TEST_OUT."""
     import torch
 
-    from dial_cuda.model import Stage
-    from dial_cuda.pipeline import ModelStageCompute, NcclChannel, Pipeline, init_distributed
+    from dial_cuda.model import Stage, vocab_shards
+    from dial_cuda.pipeline import ModelStageCompute, NcclChannel, Pipeline, head_links, init_distributed
     rank, local, world = init_distributed("nccl", timeout_s=60)
-    cfg = _cfg()
+    vocab_head = os.environ.get("DIAL_TEST_VOCAB_HEAD") == "1"
+    cfg = _cfg(vocab=VOCAB_PARALLEL if vocab_head else SMALL["vocab"])
     half = cfg.n_layers // 2
     a, b = (0, half) if rank == 0 else (half, cfg.n_layers)
-    st = Stage(cfg, a, b, n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
-    comp = ModelStageCompute(st, N_MB, PROMPT)
-    ch = NcclChannel(rank, world, timeout_s=60.0)  # the C ABI's stage communicators
-    pipe = Pipeline(rank, world, comp, ch, N_MB)
+    hch = None
+    if vocab_head:
+        spans = vocab_shards(cfg.vocab, [1, 1])
+        st = Stage(cfg, a, b, n_slots=N_MB, max_seq=PROMPT + STEPS + 8, with_head=False,
+                   head_rows=spans[rank])
+        comp = ModelStageCompute(st, N_MB, PROMPT, vocab_head_stages=world)
+        rows = [v1 - v0 for v0, v1 in spans]
+        hch = NcclChannel(rank, world, timeout_s=60.0, links=head_links(world, rows))
+        ch = NcclChannel(rank, world, timeout_s=60.0)
+        pipe = Pipeline(rank, world, comp, ch, N_MB, head_channel=hch, head_rows=rows)
+    else:
+        st = Stage(cfg, a, b, n_slots=N_MB, max_seq=PROMPT + STEPS + 8)
+        comp = ModelStageCompute(st, N_MB, PROMPT)
+        ch = NcclChannel(rank, world, timeout_s=60.0)  # the C ABI's stage communicators
+        pipe = Pipeline(rank, world, comp, ch, N_MB)
     pipe.prefill(_prompts(torch) if rank == 0 else None, prompt_len=PROMPT)
     firsts = [int(t.item()) for t in comp.tokens]
     saved = [t.clone() for t in comp.tokens]
@@ -133,11 +147,15 @@ def _two_stage_worker():
     torch.cuda.synchronize()
     last = [int(t.item()) for t in comp.tokens]
     pipe.finish()
+    torch.cuda.synchronize()
+    after = [int(t.item()) for t in comp.tokens]
     ch.close()
+    if hch is not None:
+        hch.close()
     import torch.distributed as dist
     dist.barrier()
     with open(os.path.join(os.environ["DIAL_TEST_OUT"], f"rank{rank}.json"), "w") as f:
-        json.dump({"rank": rank, "firsts": firsts, "last": last}, f)
+        json.dump({"rank": rank, "firsts": firsts, "last": last, "after_finish": after}, f)
     dist.destroy_process_group()
 
 
@@ -147,12 +165,17 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_two_stage_pipeline_matches_single_gpu(cuda, tmp_path):
+VOCAB_PARALLEL = 8192  # two halves of 256 GEMV tiles each
+
+
+@pytest.mark.parametrize("vocab_head", [False, True], ids=["head-last", "head-vocab-parallel"])
+def test_two_stage_pipeline_matches_single_gpu(cuda, tmp_path, vocab_head):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    ref = reference_tokens(torch)
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", DIAL_TEST_OUT=str(tmp_path))
+    ref = reference_tokens(torch, vocab=VOCAB_PARALLEL if vocab_head else SMALL["vocab"])
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", DIAL_TEST_OUT=str(tmp_path),
+               DIAL_TEST_VOCAB_HEAD="1" if vocab_head else "0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.abspath(__file__)]
@@ -160,7 +183,9 @@ def test_two_stage_pipeline_matches_single_gpu(cuda, tmp_path):
     assert out.returncode == 0, out.stderr[-3000:]
     res = {r: json.loads((tmp_path / f"rank{r}.json").read_text()) for r in (0, 1)}
     assert res[0]["firsts"] == [s[0] for s in ref]   # prefill tokens came back to stage 0
-    assert res[1]["last"] == [s[-1] for s in ref]    # last step's tokens on the last stage
+    if not vocab_head:
+        assert res[1]["last"] == [s[-1] for s in ref]    # last step's tokens on the last stage
+    assert res[0]["after_finish"] == [s[-1] for s in ref]  # and, after finish(), on stage 0
 
 
 if __name__ == "__main__":  # a rank of the two-stage test

@@ -201,6 +201,7 @@ extern "C" {
     pub fn dial_abi_version() -> c_int;
     pub fn dial_launch_count() -> u64;
     pub fn dial_device_error(clear: c_int) -> dial_status;
+    pub fn dial_check_bounded_wait(src: *const c_void, result: *mut i32, stream: dial_stream) -> dial_status;
 
     // W8A16 (CudaW8A16Linear, worker_w8a16.rs:291-476)
     pub fn dial_w8a16_quantize(w: *const c_void, wdt: dial_dtype, n: i64, k: i64, q: *mut i8,

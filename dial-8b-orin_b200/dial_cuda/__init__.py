@@ -83,6 +83,7 @@ SIGNATURES = {
     "dial_decode_attention": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i32, _i32,
                                _i32, _i32, _i64, _i64, ctypes.c_float, _i32, _vp], _i32),
     "dial_head_merge": ([_vp, _i32, _i64, _vp, _vp], _i32),
+    "dial_check_bounded_wait": ([_vp, _vp, _vp], _i32),
     "dial_swiglu": ([_vp, _vp, _i32, _i64, _i64, _vp], _i32),
     "dial_embedding": ([_vp, _vp, _vp, _i32, _i64, _i64, _i64, _vp], _i32),
     "dial_argmax": ([_vp, _vp, _i32, _i64, _i64, _vp], _i32),

@@ -75,6 +75,15 @@ DIAL_API uint64_t dial_launch_count(void);
  * waits set when a wait expires (DIAL_ERR_TIMEOUT); `clear` resets it. */
 DIAL_API dial_status dial_device_error(int clear);
 
+/* Self-test of the bounded-wait error path (no reference counterpart): one
+ * CTA starts a 256-byte bulk copy from `src` (device, 16-byte aligned) into
+ * shared memory, waits on an mbarrier that nothing signals until the wait
+ * limit (1 s) expires -- which records DIAL_ERR_TIMEOUT in the device error
+ * flag -- then drains the copy and writes result[0..2] (device int[3]):
+ * {wait succeeded (0 expected), copy drained (1), word 12 of src as read}.
+ * Clear the flag with dial_device_error(1) before and after. */
+DIAL_API dial_status dial_check_bounded_wait(const void* src, int* result, dial_stream stream);
+
 /* ------------------------------------------------------------------ W8A16
  * Layout: q int8 [N, K] row-major (K contiguous), scale [N] (f32 as in the
  * reference, or f16).  K must be a multiple of 16 and q 16-byte aligned.

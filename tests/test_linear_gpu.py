@@ -252,6 +252,33 @@ def test_gguf_linear_parity(D, torch, qt, M, xdt):
         assert rel_err(y, cand) <= 1e-4 + out_tol
 
 
+# BASELINE config 2's sweep: the 7 linears of an 8B decoder layer (q, k, v, o,
+# gate, up: K = 4096; down: K = 12288), N(0, 0.02) weights, f32 N(0, 1)
+# activations, M in {1, 8, 32, 512}.  Rows are independent, so at M = 512 the
+# oracle checks 8 of them (first, last and seeded others) of the full launch.
+CONFIG2_LINEARS = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+                   ("gate", 12288, 4096), ("up", 12288, 4096), ("down", 4096, 12288)]
+
+
+@pytest.mark.parametrize("qt", [O.Q4_0, O.Q8_0])
+@pytest.mark.parametrize("M", [1, 8, 32, 512])
+def test_gguf_config2_sweep_as_a_set(D, torch, qt, M):
+    rng = np.random.default_rng(1000 + M + qt)
+    rows = np.arange(M) if M <= 32 else np.unique(np.r_[0, M - 1, rng.choice(M, 6, replace=False)])
+    for name, N, K in CONFIG2_LINEARS:
+        w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+        x = rng.normal(0, 1, (M, K)).astype(np.float32)
+        blocks = O.gguf_quantize(w, qt)
+        lin = D.GgufLinear.from_blocks(_to_dev(torch, blocks), qt, K, N)
+        y = lin.forward(_to_dev(torch, x)).float().cpu().numpy()[rows]
+        exact = O.gguf_linear_exact(x[rows], blocks, qt, N)
+        assert rel_err(y, exact) <= 1e-2, (name, M)
+        if M <= 16:  # the integer path reproduces candle's arithmetic
+            cand = O.gguf_linear_candle(x[rows], blocks, qt, N)
+            assert rel_err(y, cand) <= 1e-4, (name, M)
+    assert D.lib().dial_device_error(1) == 0
+
+
 def test_gguf_rejects_missing_workspace(D, torch):
     w = torch.zeros((64, 64), dtype=torch.float32, device="cuda")
     lin = D.GgufLinear.quantize(w, O.Q4_0)

@@ -89,3 +89,29 @@ def test_missing_peer_times_out(D, cuda):
     assert L.dial_stage_comm_destroy(ok) == 0
     x = torch.ones(4, device="cuda")
     assert float(x.sum()) == 4.0
+
+
+@pytest.mark.gpu
+def test_device_wait_expires_with_a_status(cuda):
+    """A device-side bounded wait that nothing signals (dial_check_bounded_wait):
+    it gives up after its 1 s limit, the host reads DIAL_ERR_TIMEOUT from the
+    device error flag, the copy the kernel started was drained, and the context
+    still runs work afterwards."""
+    import time
+
+    import torch
+
+    import dial_cuda as D
+    D.lib().dial_device_error(1)  # start clean
+    src = torch.arange(64, dtype=torch.int32, device="cuda")
+    res = torch.full((3,), -7, dtype=torch.int32, device="cuda")
+    t0 = time.time()
+    D.check(D.lib().dial_check_bounded_wait(src.data_ptr(), res.data_ptr(), D.stream_ptr()),
+            "dial_check_bounded_wait")
+    torch.cuda.synchronize()
+    took = time.time() - t0
+    assert res.tolist() == [0, 1, 12]
+    assert D.lib().dial_device_error(1) == 7  # DIAL_ERR_TIMEOUT
+    assert D.lib().dial_device_error(0) == 0  # cleared
+    assert 0.9 < took < 30
+    assert int((src * 2).sum().item()) == 2 * sum(range(64))  # the context is usable

@@ -297,7 +297,7 @@ class W8A16Gemv:
 class GgufSweep:
     """GGUF decode sweep: 7 shapes x {Q4_0, Q8_0} x M in {1, 8}."""
     metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "q4_0/q8_0 x f32"
-    kernel = "gguf_tma_kernel + q8_0_act_quantize_kernel (whole sweep)"
+    kernel = "gguf_gemv_kernel (whole tiles; Q8_0 staging fused at M = 1) (whole sweep)"
     ms = (1, 8)
     graph = True
 

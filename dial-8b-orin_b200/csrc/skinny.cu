@@ -1458,30 +1458,56 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
     const int nb = K / kQK;
     uint8_t* xq8 = reinterpret_cast<uint8_t*>(__cvta_shared_to_generic(xqs));
     float2* ds = reinterpret_cast<float2*>(__cvta_shared_to_generic(xss));
+    // a lane per block: 16-byte loads of the block's 32 activations, and the
+    // quantised bytes stored as 8 words (4 consecutive elements of a block are
+    // 4 consecutive bytes of the group order, q8_0_offset)
     for (int b = g0 * kBlocksPerGroup + lane; b < g1 * kBlocksPerGroup; b += 32) {
-      uint8_t* dst = xq8 + (b >> 2) * 128;
+      uint32_t* dst = reinterpret_cast<uint32_t*>(xq8 + (b >> 2) * 128);
       const int j = b & 3;
       if (b >= nb) {
-        for (int p = 0; p < kQK; ++p) dst[q8_0_offset(j, p)] = 0;
+#pragma unroll
+        for (int w = 0; w < kQK / 4; ++w) dst[q8_0_offset(j, 4 * w) >> 2] = 0u;
         ds[b] = make_float2(0.0f, 0.0f);
         continue;
       }
-      const XT* src = x + (size_t)b * kQK;
+      const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)b * kQK);
       float v[kQK];
+      if constexpr (sizeof(XT) == 4) {
+#pragma unroll
+        for (int i = 0; i < kQK / 4; ++i) {
+          const uint4 u = src[i];
+          v[4 * i] = __uint_as_float(u.x), v[4 * i + 1] = __uint_as_float(u.y);
+          v[4 * i + 2] = __uint_as_float(u.z), v[4 * i + 3] = __uint_as_float(u.w);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kQK / 8; ++i) {
+          const uint4 u = src[i];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const unsigned short bits = (unsigned short)(word(u, k >> 1) >> (16 * (k & 1)));
+            XT h;
+            memcpy(&h, &bits, sizeof(bits));
+            v[8 * i + k] = Act<XT>::to_f32(h);
+          }
+        }
+      }
       float amax = 0.0f;
 #pragma unroll
-      for (int p = 0; p < kQK; ++p) {
-        v[p] = Act<XT>::to_f32(src[p]);
-        amax = fmaxf(amax, fabsf(v[p]));
-      }
+      for (int p = 0; p < kQK; ++p) amax = fmaxf(amax, fabsf(v[p]));
       const float dd = __fdiv_rn(amax, 127.0f);
       const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
       int sum = 0;
 #pragma unroll
-      for (int p = 0; p < kQK; ++p) {
-        const int qv = (int)roundf(__fmul_rn(v[p], id));
-        sum += qv;
-        dst[q8_0_offset(j, p)] = (uint8_t)(int8_t)qv;
+      for (int w = 0; w < kQK / 4; ++w) {
+        uint32_t packed = 0u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int qv = (int)roundf(__fmul_rn(v[4 * w + k], id));
+          sum += qv;
+          packed |= (uint32_t)(uint8_t)(int8_t)qv << (8 * k);
+        }
+        dst[q8_0_offset(j, 4 * w) >> 2] = packed;
       }
       ds[b] = make_float2(__half2float(__float2half_rn(dd)), (float)sum);
     }
@@ -1899,7 +1925,7 @@ dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, co
   // stage, so its groups per warp must be even
   const bool tile_mode = sk_ws && aligned16(qs) && aligned16(d) && nt <= 2 && G >= kTmaWarps &&
                          G % kTmaWarps == 0 && tiles >= 32;
-  const bool fused = tile_mode && M == 1 && K <= kGgufFusedMaxK &&
+  const bool fused = tile_mode && M == 1 && K <= kGgufFusedMaxK && aligned16(x) &&
                      (type != DIAL_GGML_Q4_0 || G % (2 * kTmaWarps) == 0);
   const int gps = type == DIAL_GGML_Q4_0 && fused ? 2 : 1;
   if (tile_mode) {  // the decode GEMV: whole tiles per CTA (+ the row's Q8_0 staging when fused)

@@ -214,11 +214,12 @@ def build_copy_graphs(wl):
 class W8A16Gemv:
     """One W8A16 decode linear per step (the Qwen3-8B up-proj shape)."""
     metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "int8 x f16"
-    kernel = "w8a16_tma_kernel<NT=1>"
+    kernel = "w8a16_gemv_kernel<NT=1>"
     M, N, K = 1, 12288, 4096
     graph = True
-    # DRAM read + write bytes of one launch of this shape, from an ncu capture
-    traffic = 50_430_976 + 4_608
+    # DRAM read + write bytes of one w8a16_gemv_kernel launch of this shape, from
+    # an ncu capture of this workload
+    traffic = 50_430_464 + 256
 
     def __init__(self, torch, D, rank: int = 0, world: int = 1):
         self.torch = torch
@@ -611,9 +612,9 @@ class QwenDecode:
     graph = True
     scaling = "strong"
     # DRAM bytes per token of the stage's linears on one GPU: the DRAM read + write
-    # bytes of one captured 12288 x 4096 decode GEMV launch (50,425,088 B over its
-    # 24,576 weight units of 2 KB) times the token's 3,695,360 units
-    traffic = 7_582_147_346
+    # bytes of one captured 12288 x 4096 w8a16_gemv_kernel launch (50,430,720 B
+    # over its 24,576 weight units of 2 KB) times the token's 3,695,360 units
+    traffic = 7_582_994_200
     n_seqs, mb_size, prompt_len, decode_cap = 8, 1, 1024, 448
     head_layers = 3.2  # the output head's cost in layers (weights read per token)
     copies_per_step = 8  # one graph per micro-batch

@@ -86,6 +86,8 @@ struct Planner {
       dec += m.head_decode_ms, tdec += m.head_decode_ms;
     }
     if (mem > D.usable_memory_mb) return false;
+    // stage to stage: the master takes the prompt and the tokens, so it holds layer 0
+    if (m.link_topology == DIAL_PLAN_LINKS_CHAIN && !first && D.role == DIAL_PLAN_MASTER) return false;
     s.dev = d, s.start = a, s.end = b, s.mem = mem;
     s.compute = pre + dec * o.output_tokens;
     Cost& c = s.c;
@@ -93,7 +95,29 @@ struct Planner {
     c.energy = msum(D.prefill_energy_mj, a, b) + msum(D.decode_energy_mj, a, b) * o.output_tokens;
     s.network = 0;
     const bool worker = D.role == DIAL_PLAN_WORKER;
-    if (worker) {
+    if (m.link_topology == DIAL_PLAN_LINKS_CHAIN) {
+      // stage-to-stage hand-off: one hidden state per token into every segment
+      // but the first (over the receiving device's link), and the token id back
+      // from the last segment to the first
+      const double in_pre = first ? 0.0 : (double)o.prompt_tokens * m.hidden_size * o.dtype_bytes;
+      const double in_dec = first ? 0.0 : (double)m.hidden_size * o.dtype_bytes;
+      const double out_tok = last && !first ? 4.0 : 0.0;
+      if (worker && (in_dec > 0 || out_tok > 0)) {
+        const double bw = D.bandwidth_mbps;
+        const double tbw = D.bandwidth_p05_mbps >= 0 ? D.bandwidth_p05_mbps : bw;
+        const double lat = D.rtt_ms + D.protocol_ms;
+        const double tlat = (D.rtt_p95_ms >= 0 ? D.rtt_p95_ms : D.rtt_ms) +
+                            (D.protocol_p95_ms >= 0 ? D.protocol_p95_ms : D.protocol_ms);
+        const int hops = (in_dec > 0) + (out_tok > 0);
+        const double pre_net = hops * lat + (in_pre + out_tok) * 8.0 / (bw * 1000.0);
+        const double dec_net = hops * lat + (in_dec + out_tok) * 8.0 / (bw * 1000.0);
+        const double tpre_net = hops * tlat + (in_pre + out_tok) * 8.0 / (tbw * 1000.0);
+        const double tdec_net = hops * tlat + (in_dec + out_tok) * 8.0 / (tbw * 1000.0);
+        s.network = pre_net + dec_net * o.output_tokens;
+        c.ttft += pre_net + dec_net, c.tpot += dec_net;
+        c.tail_ttft += tpre_net + tdec_net, c.tail_tpot += tdec_net;
+      }
+    } else if (worker) {
       const double bw = D.bandwidth_mbps;
       const double tbw = D.bandwidth_p05_mbps >= 0 ? D.bandwidth_p05_mbps : bw;
       const double trtt = D.rtt_p95_ms >= 0 ? D.rtt_p95_ms : D.rtt_ms;
@@ -138,6 +162,9 @@ struct Planner {
 dial_status validate(const dial_plan_model& m, const dial_plan_objective& o,
                      const dial_plan_device* devices, int n, Planner& p) {
   if (m.num_layers <= 0) return fail(DIAL_ERR_INVALID_ARG, "model must have layers");
+  if (m.link_topology != DIAL_PLAN_LINKS_STAR && m.link_topology != DIAL_PLAN_LINKS_CHAIN)
+    return fail(DIAL_ERR_INVALID_ARG, "link_topology must be %d (star) or %d (chain)", DIAL_PLAN_LINKS_STAR,
+                DIAL_PLAN_LINKS_CHAIN);
   if (o.prompt_tokens <= 0) return fail(DIAL_ERR_INVALID_ARG, "objective.prompt_tokens must be greater than zero");
   if (o.output_tokens <= 0) return fail(DIAL_ERR_INVALID_ARG, "objective.output_tokens must be greater than zero");
   if (o.dtype_bytes <= 0) return fail(DIAL_ERR_INVALID_ARG, "objective.dtype_bytes must be greater than zero");

@@ -157,6 +157,7 @@ pub struct dial_plan_model {
     pub embed_memory_mb: f64,
     pub embed_prefill_ms: f64,
     pub embed_decode_ms: f64,
+    pub link_topology: c_int,
 }
 
 #[repr(C)]

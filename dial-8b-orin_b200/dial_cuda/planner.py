@@ -21,6 +21,7 @@ from typing import List, Optional, Sequence, Union
 from . import DialError, lib
 
 DIAL, EDGESHARD_LATENCY, EDGESHARD_THROUGHPUT = 0, 1, 2
+LINKS_STAR, LINKS_CHAIN = 0, 1  # dial_plan_model.link_topology
 MASTER, WORKER = 0, 1
 MAX_DEVICES = 12
 SCORE_DEFINITION = {
@@ -63,7 +64,8 @@ class _Model(ctypes.Structure):
                 ("max_seq_len", ctypes.c_int),
                 ("head_memory_mb", ctypes.c_double), ("head_prefill_ms", ctypes.c_double),
                 ("head_decode_ms", ctypes.c_double), ("embed_memory_mb", ctypes.c_double),
-                ("embed_prefill_ms", ctypes.c_double), ("embed_decode_ms", ctypes.c_double)]
+                ("embed_prefill_ms", ctypes.c_double), ("embed_decode_ms", ctypes.c_double),
+                ("link_topology", ctypes.c_int)]
 
 
 class _Segment(ctypes.Structure):
@@ -138,6 +140,7 @@ class PlannerModel:
     embed_memory_mb: float = 0.0
     embed_prefill_ms: float = 0.0
     embed_decode_ms: float = 0.0
+    link_topology: int = 0  # LINKS_STAR (the reference's) or LINKS_CHAIN (stage to stage)
 
 
 def _metric(v: Metric, keep: list) -> _Metric:
@@ -181,7 +184,7 @@ def plan_stages(model: PlannerModel, objective: PlannerObjective, devices: List[
     m = model
     mod = _Model(m.num_layers, m.hidden_size, m.num_attention_heads, m.num_key_value_heads,
                  m.max_seq_len, m.head_memory_mb, m.head_prefill_ms, m.head_decode_ms,
-                 m.embed_memory_mb, m.embed_prefill_ms, m.embed_decode_ms)
+                 m.embed_memory_mb, m.embed_prefill_ms, m.embed_decode_ms, m.link_topology)
     res = _Result()
     st = fn(ctypes.byref(mod), ctypes.byref(obj), arr, len(devices), algorithm, ctypes.byref(res))
     if st != 0:
@@ -209,19 +212,23 @@ def plan_stages(model: PlannerModel, objective: PlannerObjective, devices: List[
             "rejected_for_memory": res.rejected_for_memory}
 
 
-def local_gpu_plan(n_layers: int, n_gpus: int, *, layer_decode_ms: float = 1.0,
+def local_gpu_plan(n_layers: int, n_gpus: int, *, layer_decode_ms: float = 0.071,
                    head_layers: float = 0.0, embed_layers: float = 0.0,
                    layer_memory_mb: float = 193.0, usable_memory_mb: float = 170_000.0,
                    hidden_size: int = 4096, heads: int = 32, kv_heads: int = 8,
-                   max_seq_len: int = 4096, link_latency_ms: float = 0.01,
-                   link_mbps: float = 900e3 * 8, stages: Optional[int] = None,
+                   max_seq_len: int = 4096, link_latency_ms: float = 0.015,
+                   link_mbps: float = 770e3 * 8, stages: Optional[int] = None,
                    algorithm: int = EDGESHARD_THROUGHPUT) -> List[range]:
     """Layer ranges of a pipeline over `n_gpus` local GPUs (stage s on GPU s).
 
-    Every GPU is a device with the same per-layer cost; the output head and the
-    embedding are charged as `head_layers` / `embed_layers` layer-equivalents to
-    the last / first stage.  `stages` forces the stage count (min = max devices);
-    the default objective is the pipeline bottleneck (EdgeShardThroughput)."""
+    Every GPU is a device with the same per-layer cost (default: a Qwen3-8B
+    W8A16 layer's decode time on a B200); the output head and the embedding
+    are charged as `head_layers` / `embed_layers` layer-equivalents to the last
+    / first stage.  Hand-offs follow the stage-to-stage chain (LINKS_CHAIN):
+    each stage after the first receives one hidden state per token over NVLink
+    (`link_latency_ms`, `link_mbps`: 770 GB/s per direction, the measured peer
+    copy rate).  `stages` forces the stage count (min = max devices); the
+    default objective is the pipeline bottleneck (EdgeShardThroughput)."""
     devs = [PlannerDevice(name=f"cuda:{i}", role=MASTER if i == 0 else WORKER,
                           usable_memory_mb=usable_memory_mb, layer_memory_mb=layer_memory_mb,
                           prefill_ms=layer_decode_ms, decode_ms=layer_decode_ms,
@@ -231,6 +238,7 @@ def local_gpu_plan(n_layers: int, n_gpus: int, *, layer_decode_ms: float = 1.0,
     k = stages if stages is not None else n_gpus
     obj = PlannerObjective(prompt_tokens=1, output_tokens=1, min_devices=k, max_devices=k)
     model = PlannerModel(n_layers, hidden_size, heads, kv_heads, max_seq_len,
+                         link_topology=LINKS_CHAIN,
                          head_memory_mb=head_layers * layer_memory_mb,
                          head_prefill_ms=head_layers * layer_decode_ms,
                          head_decode_ms=head_layers * layer_decode_ms,

@@ -439,7 +439,18 @@ typedef struct dial_plan_model {
   int num_layers, hidden_size, num_attention_heads, num_key_value_heads, max_seq_len;
   double head_memory_mb, head_prefill_ms, head_decode_ms;    /* segment ending at the last layer */
   double embed_memory_mb, embed_prefill_ms, embed_decode_ms; /* segment starting at layer 0 */
+  /* DIAL_PLAN_LINKS_STAR (0, the reference's model, planner.rs:787-805): every
+   * worker segment gets its input from the master and returns its output, two
+   * hidden states per token over its own link.  DIAL_PLAN_LINKS_CHAIN: the
+   * stages of a local GPU pipeline hand off stage to stage -- a segment that
+   * does not start at layer 0 receives one hidden state per token over its
+   * device's link (rtt + protocol + bytes / bandwidth), the last segment
+   * returns a 4-byte token id to the first, and the master holds layer 0 (it
+   * takes the prompt and the tokens). */
+  int link_topology;
 } dial_plan_model;
+#define DIAL_PLAN_LINKS_STAR 0
+#define DIAL_PLAN_LINKS_CHAIN 1
 
 typedef struct dial_plan_segment {
   int device; /* index into the devices array */

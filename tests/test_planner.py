@@ -147,3 +147,64 @@ def test_local_gpu_plan_minimises_the_bottleneck(layers, gpus, head):
 def test_local_gpu_plan_even_without_head_weight():
     assert [len(r) for r in P.local_gpu_plan(36, 4, link_latency_ms=0.0)] == [9, 9, 9, 9]
     assert sorted(len(r) for r in P.local_gpu_plan(36, 8, link_latency_ms=0.0)) == [4, 4, 4, 4, 5, 5, 5, 5]
+
+
+# ---------------------------------------------------------------- stage-to-stage links
+def _chain_devices(n, rtt, proto=0.0, mbps=8000.0):
+    return [P.PlannerDevice(name=f"gpu{i}", role=P.MASTER if i == 0 else P.WORKER,
+                            usable_memory_mb=250.0 if n > 1 else 5000.0, fixed_memory_mb=0.0,
+                            layer_memory_mb=100.0, prefill_ms=1.0, decode_ms=1.0,
+                            rtt_ms=rtt if i else 0.0, protocol_ms=proto if i else 0.0,
+                            bandwidth_mbps=mbps if i else None)
+            for i in range(n)]
+
+
+def test_chain_links_charge_one_hidden_state_into_each_later_stage():
+    """Four 2-layer stages (memory forces the split): stage s > 0 pays one
+    incoming hand-off per token (rtt + protocol + H * dtype bytes over its
+    link), the last stage also the 4-byte token back; stage 0 (the master,
+    which holds layer 0 under the chain model) pays nothing."""
+    m = config(8)
+    m.link_topology = P.LINKS_CHAIN
+    rtt, proto, mbps = 0.5, 0.25, 8000.0
+    r = P.plan_stages(m, objective(min_devices=4, max_devices=4), _chain_devices(4, rtt, proto, mbps))
+    segs = sorted(r["segments"], key=lambda s: s["start_layer"])
+    assert [s["num_layers"] for s in segs] == [2, 2, 2, 2]
+    hop = rtt + proto
+    hidden = 4096 * 2 * 8.0 / (mbps * 1000.0)
+    tok = 4 * 8.0 / (mbps * 1000.0)
+    want = [2.0, 2.0 + hop + hidden, 2.0 + hop + hidden, 2.0 + 2 * hop + hidden + tok]
+    assert [s["estimated_tpot_ms"] for s in segs] == pytest.approx(want, rel=1e-12)
+    assert segs[0]["device"] == "gpu0"
+
+
+def test_star_links_keep_the_reference_cost():
+    """The default (star): a worker segment pays 2 hidden states per token plus
+    one rtt + protocol per direction-pair, as planner.rs:787-805."""
+    m = config(8)
+    rtt, proto, mbps = 0.5, 0.25, 8000.0
+    r = P.plan_stages(m, objective(min_devices=4, max_devices=4), _chain_devices(4, rtt, proto, mbps))
+    segs = sorted(r["segments"], key=lambda s: s["start_layer"])
+    star = 2.0 + rtt + proto + 2 * 4096 * 2 * 8.0 / (mbps * 1000.0)
+    by_dev = {s["device"]: s["estimated_tpot_ms"] for s in segs}
+    assert by_dev.pop("gpu0") == pytest.approx(2.0)  # the master pays no link
+    assert sorted(by_dev.values()) == pytest.approx([star] * 3, rel=1e-12)
+
+
+def test_slow_chain_links_favour_fewer_stages():
+    """With 3 ms per hop the planner keeps all 8 layers on one GPU when it can
+    (4 stages would add 3 hops + the token's return per token)."""
+    m = config(8)
+    m.link_topology = P.LINKS_CHAIN
+    devs = _chain_devices(4, 3.0)
+    for d in devs:
+        d.usable_memory_mb = 5000.0
+    r = P.plan_stages(m, objective(), devs)
+    assert r["selected_device_count"] == 1
+
+
+def test_rejects_an_unknown_link_topology():
+    m = config(8)
+    m.link_topology = 7
+    with pytest.raises(DialError, match="link_topology"):
+        P.plan_stages(m, objective(), _chain_devices(2, 0.1))

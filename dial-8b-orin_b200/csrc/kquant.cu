@@ -26,6 +26,7 @@
 // an aligned base); a Q6_K block starts on an even byte only, so its bytes are
 // read as 16-bit words.
 #include "common.cuh"
+#include "quant.cuh"
 
 namespace dial {
 
@@ -400,7 +401,11 @@ extern "C" dial_status dial_gguf_k_linear(const void* x, dial_dtype xdt, const v
   if (M <= 0) return fail(DIAL_ERR_INVALID_ARG, "sizes must be positive");
   if (!is_act_dtype(xdt)) return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "activation dtype must be f32/f16/bf16");
   if (!aligned16(x)) return fail(DIAL_ERR_MISALIGNED, "x must be 16-byte aligned");
+  if (type == DIAL_GGML_Q4_K && kq4_gemv_ok(M, K, N, xdt, x, blocks))
+    return launch_kq4_gemv(x, xdt, blocks, y, M, K, N, as_stream(stream));
   if (type == DIAL_GGML_Q4_K)
     return launch_kq_linear<DIAL_GGML_Q4_K>(x, xdt, blocks, y, M, K, N, as_stream(stream));
+  if (kq6_gemv_ok(M, K, N, xdt, x, blocks))
+    return launch_kq6_gemv(x, xdt, blocks, y, M, K, N, as_stream(stream));
   return launch_kq_linear<DIAL_GGML_Q6_K>(x, xdt, blocks, y, M, K, N, as_stream(stream));
 }

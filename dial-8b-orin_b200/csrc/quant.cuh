@@ -51,6 +51,16 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
                                 cudaStream_t st, void* sk_ws, const ActPrologue* pro = nullptr,
                                 unsigned long long* keys = nullptr, int64_t key_off = 0,
                                 bool* keyed = nullptr);
+// Q4_K decode GEMV on tensor cores (M <= 8 tokens, f16/bf16 activations, K a
+// multiple of 256 with at least 8 super-blocks, 16-byte aligned x and blocks).
+bool kq4_gemv_ok(int64_t M, int64_t K, int64_t N, dial_dtype xdt, const void* x, const void* blocks);
+dial_status launch_kq4_gemv(const void* x, dial_dtype xdt, const void* blocks, void* y, int64_t M,
+                            int64_t K, int64_t N, cudaStream_t st);
+// Q6_K decode GEMV on tensor cores (as the Q4_K one; K a multiple of 2048, so
+// that a row of 210-byte super-blocks is a 16-byte multiple).
+bool kq6_gemv_ok(int64_t M, int64_t K, int64_t N, dial_dtype xdt, const void* x, const void* blocks);
+dial_status launch_kq6_gemv(const void* x, dial_dtype xdt, const void* blocks, void* y, int64_t M,
+                            int64_t K, int64_t N, cudaStream_t st);
 // GGUF integer path: activations quantised to Q8_0 in `ws` first.
 size_t gguf_skinny_workspace_bytes(int64_t M, int64_t K);
 dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, const uint16_t* d,

@@ -1741,6 +1741,372 @@ int pick_split(int64_t tiles, int64_t groups) {
 // tile_ok: the kernel can reduce tiles in shared memory (staged activations,
 // at most 2 token groups).  With at least one tile per SM and one K group per
 // warp the CTAs take whole tiles (no global fixup); otherwise stream-K.
+// ------------------------------------------------------------------ Q4_K decode GEMV on tensor cores
+// The Q4_K linear at M <= 8 tokens with f16/bf16 activations
+// (dial_gguf_k_linear; the reference's QMatMul on Q4_K tensors,
+// worker_gguf.rs:574-611).  Units of 16 rows x one super-block (16 rows x 144
+// bytes: {f16 d, f16 dmin, 12 scale bytes, 128 nibble bytes}) stream through a
+// per-warp 4-stage TMA ring (no swizzle; the 144-byte rows are 16-byte
+// aligned), whole 16-row tiles per CTA, warp j taking super-blocks
+// [nb j / 8, nb (j + 1) / 8) of every tile, as w8a16_gemv_kernel does.
+//
+// A super-block's weights are w = d sc_j q - dmin m_j for sub-block j (32
+// weights; q a 4-bit code), so its dot product with x is
+//     sum_j [ d sc_j (sum q x) - dmin m_j (sum x) ].
+// Per 32-byte chunk c of the nibbles (sub-block 2c in the low nibbles, 2c + 1
+// in the high ones) and k-step s, lane (g, t) takes bytes 8t + 4s .. 8t + 4s + 3
+// of rows g and g + 8: the 16 k positions of a step are bytes {0-3, 8-11,
+// 16-19, 24-27} (+ 4 s) of the chunk, and the activation fragment follows the
+// same order (4 consecutive activations per lane).  The codes enter the MMA
+// as f16 (bf16) values bias + q, exact (bias 1024 = 0x6400 in f16, 128 =
+// 0x4300 in bf16, q in the mantissa), and an MMA with an all-ones A gives
+// sum x of the step for every token column; per sub-block
+//     acc += d sc_j * C - (bias d sc_j + dmin m_j) * S,
+// C and S the sub-block's two steps of those MMAs.  f32 accumulation; the
+// rows' 8 partial sums meet in shared memory (cta_tile_finish) and are
+// rounded once to the activation dtype.
+constexpr int kKq4Row = 144;                 // bytes of a Q4_K super-block
+constexpr int kKq4Unit = 16 * kKq4Row;       // one TMA box: 16 rows x 144 bytes
+constexpr int kKq4Smem = 1024 + kTmaWarps * kStages * kKq4Unit + kTmaWarps * kStages * 8 + kXsAux;
+
+template <bool BF16>
+__global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
+    kq4_gemv_kernel(const __grid_constant__ CUtensorMap wmap, const uint16_t* __restrict__ x,
+                    uint16_t* __restrict__ y, int M, int N, int K, int tiles, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (tma::smem_u32(smem_raw) + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const uint32_t ring = base + (uint32_t)(warp * kStages * kKq4Unit);
+  const uint32_t bars = base + (uint32_t)(kTmaWarps * kStages * kKq4Unit + warp * kStages * 8);
+  const uint32_t aux = base + (uint32_t)(kTmaWarps * kStages * kKq4Unit + kTmaWarps * kStages * 8);
+  pdl_trigger();
+  const int C = gridDim.x, nb = K / 256;
+  const int s0 = nb * warp / kTmaWarps, s1 = nb * (warp + 1) / kTmaWarps;
+  const int ntile = (tiles - (int)blockIdx.x + C - 1) / C;
+  const int U = ntile * (s1 - s0);
+  int pu = 0, ptile = blockIdx.x, psb = s0;
+  auto issue = [&](int st) {
+    const uint32_t bar = bars + 8u * (uint32_t)st;
+    tma::mbar_expect_tx(bar, kKq4Unit);
+    tma::load_2d(ring + (uint32_t)(st * kKq4Unit), &wmap, bar, psb * kKq4Row, ptile * 16);
+    ++pu;
+    if (++psb == s1) psb = s0, ptile += C;
+  };
+  if (lane == 0) {
+    tma::prefetch_map(&wmap);
+    for (int st = 0; st < kStages; ++st) tma::mbar_init(bars + 8u * st, 1);
+    tma::fence_barrier_init();
+    tma::fence_proxy_async();
+    for (int st = 0; st < kStages && pu < U; ++st) issue(st);  // constant weights: before the wait
+  }
+  if (threadIdx.x < 8)  // cta_tile_finish round counters: cnt[r] = 0, done[r] = r - 2
+    asm volatile("st.shared.s32 [%0], %1;" ::"r"(aux + kAuxCnt + 4u * threadIdx.x),
+                 "r"((threadIdx.x & 1) ? (int)(threadIdx.x >> 1) - 2 : 0)
+                 : "memory");
+  active_warps_sync(kTmaWarps * 32);
+  pdl_wait();  // x and y belong to the stream's earlier kernels
+  constexpr uint32_t kMagic = BF16 ? 0x43004300u : 0x64006400u;  // bias + 0 in both halves
+  constexpr float kBias = BF16 ? 128.0f : 1024.0f;
+  constexpr uint32_t kOnes = BF16 ? 0x3F803F80u : 0x3C003C00u;
+  const uint16_t* xr = x + (size_t)min(g, M - 1) * K + 8 * t;  // this lane's token row
+  auto store = [&](int tile, const float (&a)[1][4]) {
+    const int r0 = tile * 16 + g;
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = r0 + 8 * hr;
+      if (r >= N) continue;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int tok = 2 * t + c;
+        if (tok >= M) continue;
+        const float v = a[0][2 * hr + c];
+        y[(size_t)tok * N + r] = BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                      : __half_as_ushort(__float2half_rn(v));
+      }
+    }
+  };
+  const uint32_t part = aux + kAuxCs, ctr = aux + kAuxCnt;
+  float acc[1][4];
+  zero_acc(acc);
+  int ctile = blockIdx.x, csb = s0, lt = 0;
+  for (int u = 0; u < U; ++u) {
+    const int st = u & (kStages - 1);
+    if (!__all_sync(0xffffffffu, tma::mbar_wait(bars + 8u * (uint32_t)st, (uint32_t)((u / kStages) & 1), err))) {
+      if (lane == 0) {  // wait (bounded) for this warp's copies still in flight
+        const unsigned long long deadline = tma::global_ns() + tma::kWaitNs;
+        for (int v = u; v < pu; ++v)
+          if (!tma::mbar_drain(bars + 8u * (uint32_t)(v & (kStages - 1)), (uint32_t)((v / kStages) & 1),
+                               deadline))
+            break;
+      }
+      return;
+    }
+    const uint32_t ub = ring + (uint32_t)(st * kKq4Unit);
+    const uint32_t rl = ub + (uint32_t)(g * kKq4Row), rh = ub + (uint32_t)((g + 8) * kKq4Row);
+    const uint4 hl = lds16(rl), hh = lds16(rh);  // {d, dmin}, scales[0..11]
+    uint2 ql[4], qh[4];                          // chunk c: bytes 8t .. 8t + 7
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      ql[c] = lds8(rl + (uint32_t)(16 + 32 * c + 8 * t));
+      qh[c] = lds8(rh + (uint32_t)(16 + 32 * c + 8 * t));
+    }
+    stage_reads_done(fold(hl) ^ fold(hh) ^ fold(ql[0]) ^ fold(ql[1]) ^ fold(ql[2]) ^ fold(ql[3]) ^
+                     fold(qh[0]) ^ fold(qh[1]) ^ fold(qh[2]) ^ fold(qh[3]));
+    if (lane == 0 && pu < U) issue(st);  // the stage is free: refill it
+    const uint16_t* xs = xr + (size_t)csb * 256;
+    const float dl = __half2float(__ushort_as_half((unsigned short)(hl.x & 0xFFFFu)));
+    const float ml = __half2float(__ushort_as_half((unsigned short)(hl.x >> 16)));
+    const float dh = __half2float(__ushort_as_half((unsigned short)(hh.x & 0xFFFFu)));
+    const float mh = __half2float(__ushort_as_half((unsigned short)(hh.x >> 16)));
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      // scales and mins of sub-blocks 2c (byte 0) and 2c + 1 (byte 1), GGML's
+      // get_scale_min_k4 on two bytes at once
+      const int sh = 16 * (c & 1);
+      uint32_t s2[2], m2[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint4& hd = r ? hh : hl;
+        const uint32_t a = (hd.y >> sh) & 0xFFFFu, b = (hd.z >> sh) & 0xFFFFu, e = (hd.w >> sh) & 0xFFFFu;
+        s2[r] = c >= 2 ? ((e & 0x0F0Fu) | ((a >> 2) & 0x3030u)) : (a & 0x3F3Fu);
+        m2[r] = c >= 2 ? (((e >> 4) & 0x0F0Fu) | ((b >> 2) & 0x3030u)) : (b & 0x3F3Fu);
+      }
+      const uint4 xlo = ld_ro16(xs + 64 * c), xhi = ld_ro16(xs + 64 * c + 32);
+      float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
+      float sl[4] = {0.f, 0.f, 0.f, 0.f}, shh[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        const uint32_t wl = s ? ql[c].y : ql[c].x, wh = s ? qh[c].y : qh[c].x;
+        const uint32_t l01 = prmt(wl, 0u, 0x4140u), l23 = prmt(wl, 0u, 0x4342u);
+        const uint32_t h01 = prmt(wh, 0u, 0x4140u), h23 = prmt(wh, 0u, 0x4342u);
+        const uint32_t b0l = s ? xlo.z : xlo.x, b1l = s ? xlo.w : xlo.y;
+        const uint32_t b0h = s ? xhi.z : xhi.x, b1h = s ? xhi.w : xhi.y;
+        // low nibbles: sub-block 2c
+        const uint32_t a0 = (l01 & 0x000F000Fu) | kMagic, a2 = (l23 & 0x000F000Fu) | kMagic;
+        const uint32_t a1 = (h01 & 0x000F000Fu) | kMagic, a3 = (h23 & 0x000F000Fu) | kMagic;
+        // high nibbles: sub-block 2c + 1
+        const uint32_t e0 = ((l01 >> 4) & 0x000F000Fu) | kMagic, e2 = ((l23 >> 4) & 0x000F000Fu) | kMagic;
+        const uint32_t e1 = ((h01 >> 4) & 0x000F000Fu) | kMagic, e3 = ((h23 >> 4) & 0x000F000Fu) | kMagic;
+        if (BF16) {
+          mma_bf16(cl, a0, a1, a2, a3, b0l, b1l);
+          mma_bf16(ch, e0, e1, e2, e3, b0h, b1h);
+          mma_bf16(sl, kOnes, kOnes, kOnes, kOnes, b0l, b1l);
+          mma_bf16(shh, kOnes, kOnes, kOnes, kOnes, b0h, b1h);
+        } else {
+          mma_f16(cl, a0, a1, a2, a3, b0l, b1l);
+          mma_f16(ch, e0, e1, e2, e3, b0h, b1h);
+          mma_f16(sl, kOnes, kOnes, kOnes, kOnes, b0l, b1l);
+          mma_f16(shh, kOnes, kOnes, kOnes, kOnes, b0h, b1h);
+        }
+      }
+      // rows g (acc 0, 1) and g + 8 (acc 2, 3)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float d = r ? dh : dl, dm = r ? mh : ml;
+        const float aL = d * (float)(s2[r] & 0xFFu), bL = fmaf(kBias, aL, dm * (float)(m2[r] & 0xFFu));
+        const float aH = d * (float)(s2[r] >> 8), bH = fmaf(kBias, aH, dm * (float)(m2[r] >> 8));
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float v = acc[0][2 * r + q];
+          v = fmaf(aL, cl[2 * r + q], v);
+          v = fmaf(-bL, sl[2 * r + q], v);
+          v = fmaf(aH, ch[2 * r + q], v);
+          v = fmaf(-bH, shh[2 * r + q], v);
+          acc[0][2 * r + q] = v;
+        }
+      }
+    }
+    if (++csb == s1) {  // the end of this warp's part of the tile
+      cta_tile_finish<1>(part, ctr, lt++, ctile, acc, store, err);
+      zero_acc(acc);
+      csb = s0;
+      ctile += C;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ Q6_K decode GEMV on tensor cores
+// The Q6_K linear, same plan as kq4_gemv_kernel.  A Q6_K super-block (210
+// bytes: ql[128] low nibbles, qh[64] high 2-bit pairs, int8 scales[16], f16 d)
+// starts 2 bytes past a 16-byte boundary for odd positions, so each unit is a
+// 224-byte TMA box from the boundary below it (the box x coordinate stays
+// 16-byte aligned; the block sits at offset o = 210 sb mod 16 inside, past the
+// end of a row the box reads the fill value), 3 stages per warp.  Element
+// 128 n + 32 p + l (half n, quarter p, l < 32) has code
+//     q = ((ql[64 n + 32 (p & 1) + l] >> 4 (p >> 1)) & 15) | ((qh[32 n + l] >> 2 p) & 3) << 4
+// and weight d sc[8 n + 2 p + l / 16] (q - 32): each 16-element k-step is one
+// scale sub-block.  Lane t takes bytes 4t .. 4t + 3 of the step's 16 ql / qh
+// bytes (read as two aligned words and a funnel shift when o mod 4 = 2); the
+// codes enter the MMA as bias + q (exact), an all-ones MMA gives the step's
+// sum x, and acc += d sc (C - (bias + 32) S).
+constexpr int kKq6Block = 210;
+constexpr int kKq6Box = 224;                 // 16-byte multiple >= 210 + 14
+constexpr int kKq6Unit = 16 * kKq6Box;
+constexpr int kKq6Stages = 3;
+constexpr int kKq6Smem = 1024 + kTmaWarps * kKq6Stages * kKq6Unit + kTmaWarps * kKq6Stages * 8 + kXsAux;
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+// 4 bytes at a 2-byte aligned shared address
+__device__ __forceinline__ uint32_t lds32_a2(uint32_t a) {
+  if ((a & 3u) == 0) return lds32(a);
+  const uint32_t lo = lds32(a - 2), hi = lds32(a + 2);
+  return __funnelshift_r(lo, hi, 16);
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
+    kq6_gemv_kernel(const __grid_constant__ CUtensorMap wmap, const uint16_t* __restrict__ x,
+                    uint16_t* __restrict__ y, int M, int N, int K, int tiles, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (tma::smem_u32(smem_raw) + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const uint32_t ring = base + (uint32_t)(warp * kKq6Stages * kKq6Unit);
+  const uint32_t bars = base + (uint32_t)(kTmaWarps * kKq6Stages * kKq6Unit + warp * kKq6Stages * 8);
+  const uint32_t aux = base + (uint32_t)(kTmaWarps * kKq6Stages * kKq6Unit + kTmaWarps * kKq6Stages * 8);
+  pdl_trigger();
+  const int C = gridDim.x, nb = K / 256;
+  const int s0 = nb * warp / kTmaWarps, s1 = nb * (warp + 1) / kTmaWarps;
+  const int ntile = (tiles - (int)blockIdx.x + C - 1) / C;
+  const int U = ntile * (s1 - s0);
+  int pu = 0, ptile = blockIdx.x, psb = s0;
+  auto issue = [&](int st) {
+    const uint32_t bar = bars + 8u * (uint32_t)st;
+    tma::mbar_expect_tx(bar, kKq6Unit);
+    tma::load_2d(ring + (uint32_t)(st * kKq6Unit), &wmap, bar, (psb * kKq6Block) & ~15, ptile * 16);
+    ++pu;
+    if (++psb == s1) psb = s0, ptile += C;
+  };
+  if (lane == 0) {
+    tma::prefetch_map(&wmap);
+    for (int st = 0; st < kKq6Stages; ++st) tma::mbar_init(bars + 8u * st, 1);
+    tma::fence_barrier_init();
+    tma::fence_proxy_async();
+    for (int st = 0; st < kKq6Stages && pu < U; ++st) issue(st);  // constant weights: before the wait
+  }
+  if (threadIdx.x < 8)  // cta_tile_finish round counters: cnt[r] = 0, done[r] = r - 2
+    asm volatile("st.shared.s32 [%0], %1;" ::"r"(aux + kAuxCnt + 4u * threadIdx.x),
+                 "r"((threadIdx.x & 1) ? (int)(threadIdx.x >> 1) - 2 : 0)
+                 : "memory");
+  active_warps_sync(kTmaWarps * 32);
+  pdl_wait();  // x and y belong to the stream's earlier kernels
+  constexpr uint32_t kMagic = BF16 ? 0x43004300u : 0x64006400u;
+  constexpr float kBias = BF16 ? 160.0f : 1056.0f;  // bias + 32
+  constexpr uint32_t kOnes = BF16 ? 0x3F803F80u : 0x3C003C00u;
+  const uint16_t* xr = x + (size_t)min(g, M - 1) * K + 4 * t;
+  auto store = [&](int tile, const float (&a)[1][4]) {
+    const int r0 = tile * 16 + g;
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = r0 + 8 * hr;
+      if (r >= N) continue;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int tok = 2 * t + c;
+        if (tok >= M) continue;
+        const float v = a[0][2 * hr + c];
+        y[(size_t)tok * N + r] = BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                      : __half_as_ushort(__float2half_rn(v));
+      }
+    }
+  };
+  const uint32_t part = aux + kAuxCs, ctr = aux + kAuxCnt;
+  float acc[1][4];
+  zero_acc(acc);
+  int ctile = blockIdx.x, csb = s0, lt = 0;
+  for (int u = 0; u < U; ++u) {
+    const int st = u % kKq6Stages;
+    const uint32_t par = (uint32_t)((u / kKq6Stages) & 1);
+    if (!__all_sync(0xffffffffu, tma::mbar_wait(bars + 8u * (uint32_t)st, par, err))) {
+      if (lane == 0) {  // wait (bounded) for this warp's copies still in flight
+        const unsigned long long deadline = tma::global_ns() + tma::kWaitNs;
+        for (int v = u; v < pu; ++v)
+          if (!tma::mbar_drain(bars + 8u * (uint32_t)(v % kKq6Stages), (uint32_t)((v / kKq6Stages) & 1),
+                               deadline))
+            break;
+      }
+      return;
+    }
+    const uint32_t o = (uint32_t)((csb * kKq6Block) & 15);
+    const uint32_t ub = ring + (uint32_t)(st * kKq6Unit) + o;
+    uint32_t qa[2][4], qb[2][4], qhw[2][4], scw[2][4], dw[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const uint32_t rb = ub + (uint32_t)((g + 8 * r) * kKq6Box);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {  // i = 2 n + lh
+        const int n = i >> 1, lh = i & 1;
+        qa[r][i] = lds32_a2(rb + (uint32_t)(64 * n + 16 * lh + 4 * t));
+        qb[r][i] = lds32_a2(rb + (uint32_t)(64 * n + 32 + 16 * lh + 4 * t));
+        qhw[r][i] = lds32_a2(rb + (uint32_t)(128 + 32 * n + 16 * lh + 4 * t));
+        scw[r][i] = lds32_a2(rb + (uint32_t)(192 + 4 * i));
+      }
+      dw[r] = lds32_a2(rb + 208u);  // d in the low half
+    }
+    uint32_t dep = dw[0] ^ dw[1];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dep ^= qa[r][i] ^ qb[r][i] ^ qhw[r][i] ^ scw[r][i];
+    stage_reads_done(dep);
+    if (lane == 0 && pu < U) issue(st);  // the stage is free: refill it
+    const float d[2] = {__half2float(__ushort_as_half((unsigned short)(dw[0] & 0xFFFFu))),
+                        __half2float(__ushort_as_half((unsigned short)(dw[1] & 0xFFFFu)))};
+    const uint16_t* xs = xr + (size_t)csb * 256;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int n = i >> 1, lh = i & 1;
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        // this step's x: elements 128 n + 32 p + 16 lh + 4t .. + 3
+        const uint2 xv = *reinterpret_cast<const uint2*>(xs + 128 * n + 32 * p + 16 * lh);
+        uint32_t a[2][2];  // [row][pair: bytes 0-1 | bytes 2-3]
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const uint32_t ql = (p & 1) ? qb[r][i] : qa[r][i];
+          const uint32_t qh = qhw[r][i];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t l2 = prmt(ql, 0u, h ? 0x4342u : 0x4140u);  // bytes -> 16-bit lanes
+            const uint32_t h2 = prmt(qh, 0u, h ? 0x4342u : 0x4140u);
+            const uint32_t nib = (l2 >> (4 * (p >> 1))) & 0x000F000Fu;
+            const uint32_t hi = ((h2 >> (2 * p)) & 0x00030003u) << 4;
+            a[r][h] = nib | hi | kMagic;
+          }
+        }
+        float cq[4] = {0.f, 0.f, 0.f, 0.f}, sx[4] = {0.f, 0.f, 0.f, 0.f};
+        if (BF16) {
+          mma_bf16(cq, a[0][0], a[1][0], a[0][1], a[1][1], xv.x, xv.y);
+          mma_bf16(sx, kOnes, kOnes, kOnes, kOnes, xv.x, xv.y);
+        } else {
+          mma_f16(cq, a[0][0], a[1][0], a[0][1], a[1][1], xv.x, xv.y);
+          mma_f16(sx, kOnes, kOnes, kOnes, kOnes, xv.x, xv.y);
+        }
+        const int sub = 8 * n + 2 * p + lh;  // scale index, byte sub % 4 of word sub / 4
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int sc = (int)(int8_t)((scw[r][sub >> 2] >> (8 * (sub & 3))) & 0xFFu);
+          const float ds = d[r] * (float)sc;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            float v = fmaf(ds, cq[2 * r + q], acc[0][2 * r + q]);
+            acc[0][2 * r + q] = fmaf(-kBias * ds, sx[2 * r + q], v);
+          }
+        }
+      }
+    }
+    if (++csb == s1) {  // the end of this warp's part of the tile
+      cta_tile_finish<1>(part, ctr, lt++, ctile, acc, store, err);
+      zero_acc(acc);
+      csb = s0;
+      ctile += C;
+    }
+  }
+}
+
 GemvPlan plan_gemv(int64_t tiles, int64_t ng, bool tile_ok) {
   const int64_t ctas = (int64_t)sm_count() * kCtasPerSM, resident = ctas * kTmaWarps;
   GemvPlan p;
@@ -2053,6 +2419,74 @@ dial_status launch_gguf_skinny(const void* x, dial_dtype xdt, const void* qs, co
 #undef GG_Y
 #undef GG_NT
 #undef GG
+  return s;
+}
+
+// ------------------------------------------------------------------ Q4_K decode GEMV launcher
+bool kq4_gemv_ok(int64_t M, int64_t K, int64_t N, dial_dtype xdt, const void* x, const void* blocks) {
+  return M >= 1 && M <= 8 && (xdt == DIAL_F16 || xdt == DIAL_BF16) && K % 256 == 0 &&
+         K / 256 >= kTmaWarps && N >= 1 && N < (1ll << 31) && K < (1ll << 31) && aligned16(x) &&
+         aligned16(blocks);
+}
+
+bool kq6_gemv_ok(int64_t M, int64_t K, int64_t N, dial_dtype xdt, const void* x, const void* blocks) {
+  return M >= 1 && M <= 8 && (xdt == DIAL_F16 || xdt == DIAL_BF16) && K % 2048 == 0 && N >= 1 &&
+         N < (1ll << 31) && K < (1ll << 31) && aligned16(x) && aligned16(blocks);
+}
+
+dial_status launch_kq6_gemv(const void* x, dial_dtype xdt, const void* blocks, void* y, int64_t M,
+                            int64_t K, int64_t N, cudaStream_t st) {
+  if (!kq6_gemv_ok(M, K, N, xdt, x, blocks)) return fail(DIAL_ERR_SHAPE, "Q6_K GEMV: unsupported shape");
+  CUtensorMap map;  // rows of K / 256 blocks of 210 bytes: a 16-byte multiple for K % 2048 == 0
+  dial_status s = tma::make_byte_map(&map, blocks, N, (K / 256) * kKq6Block, kKq6Box, 16, 0);
+  if (s != DIAL_OK) return s;
+  int* err = device_error_ptr();
+  if (!err) return fail(DIAL_ERR_CUDA, "device error flag is unavailable");
+  const int64_t tiles = (N + 15) / 16;
+  const int C = (int)std::min<int64_t>(tiles, (int64_t)sm_count() * kCtasPerSM);
+  cudaError_t ae;
+  if (xdt == DIAL_BF16) {
+    ae = ensure_smem<kq6_gemv_kernel<true>>(kKq6Smem);
+    if (ae == cudaSuccess)
+      s = launch_pdl("kq6_gemv_kernel", kq6_gemv_kernel<true>, dim3((unsigned)C), dim3(kTmaWarps * 32),
+                     kKq6Smem, st, map, static_cast<const uint16_t*>(x), static_cast<uint16_t*>(y), (int)M,
+                     (int)N, (int)K, (int)tiles, err);
+  } else {
+    ae = ensure_smem<kq6_gemv_kernel<false>>(kKq6Smem);
+    if (ae == cudaSuccess)
+      s = launch_pdl("kq6_gemv_kernel", kq6_gemv_kernel<false>, dim3((unsigned)C), dim3(kTmaWarps * 32),
+                     kKq6Smem, st, map, static_cast<const uint16_t*>(x), static_cast<uint16_t*>(y), (int)M,
+                     (int)N, (int)K, (int)tiles, err);
+  }
+  if (ae != cudaSuccess) return cuda_fail(ae, "cudaFuncSetAttribute(kq6_gemv_kernel)");
+  return s;
+}
+
+dial_status launch_kq4_gemv(const void* x, dial_dtype xdt, const void* blocks, void* y, int64_t M,
+                            int64_t K, int64_t N, cudaStream_t st) {
+  if (!kq4_gemv_ok(M, K, N, xdt, x, blocks)) return fail(DIAL_ERR_SHAPE, "Q4_K GEMV: unsupported shape");
+  CUtensorMap map;
+  dial_status s = tma::make_byte_map(&map, blocks, N, (K / 256) * kKq4Row, kKq4Row, 16, 0);
+  if (s != DIAL_OK) return s;
+  int* err = device_error_ptr();
+  if (!err) return fail(DIAL_ERR_CUDA, "device error flag is unavailable");
+  const int64_t tiles = (N + 15) / 16;
+  const int C = (int)std::min<int64_t>(tiles, (int64_t)sm_count() * kCtasPerSM);
+  cudaError_t ae;
+  if (xdt == DIAL_BF16) {
+    ae = ensure_smem<kq4_gemv_kernel<true>>(kKq4Smem);
+    if (ae == cudaSuccess)
+      s = launch_pdl("kq4_gemv_kernel", kq4_gemv_kernel<true>, dim3((unsigned)C), dim3(kTmaWarps * 32),
+                     kKq4Smem, st, map, static_cast<const uint16_t*>(x), static_cast<uint16_t*>(y), (int)M,
+                     (int)N, (int)K, (int)tiles, err);
+  } else {
+    ae = ensure_smem<kq4_gemv_kernel<false>>(kKq4Smem);
+    if (ae == cudaSuccess)
+      s = launch_pdl("kq4_gemv_kernel", kq4_gemv_kernel<false>, dim3((unsigned)C), dim3(kTmaWarps * 32),
+                     kKq4Smem, st, map, static_cast<const uint16_t*>(x), static_cast<uint16_t*>(y), (int)M,
+                     (int)N, (int)K, (int)tiles, err);
+  }
+  if (ae != cudaSuccess) return cuda_fail(ae, "cudaFuncSetAttribute(kq4_gemv_kernel)");
   return s;
 }
 

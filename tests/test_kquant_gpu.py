@@ -120,3 +120,27 @@ def test_text_linear_dispatches_k_quants(D, torch):
     x = rng.normal(0.0, 1.0, (2, 512)).astype(np.float32)
     y = t(_dev(torch, x)).cpu().numpy()
     assert rel_err(y, O.gguf_k_linear_exact(x, blocks, O.Q4_K, 64)) < 1e-4
+
+
+@pytest.mark.parametrize("qt,N,K,M", [(O.Q4_K, 1030, 2304, 5), (O.Q4_K, 4096, 4096, 8),
+                                      (O.Q4_K, 100, 2048, 7), (O.Q4_K, 16, 14336, 1),
+                                      (O.Q6_K, 1030, 6144, 5), (O.Q6_K, 4096, 4096, 8),
+                                      (O.Q6_K, 100, 2048, 7), (O.Q6_K, 16, 14336, 1)])
+@pytest.mark.parametrize("xdt", ["f16", "bf16"])
+def test_k_quant_tensor_core_gemv_shapes(D, torch, qt, N, K, M, xdt):
+    """The Q4_K / Q6_K tensor-core GEMVs (M <= 8, f16/bf16): uneven super-block
+    counts per warp (Q4_K K = 2304: 9 super-blocks over 8 warps), every 2-byte
+    offset of a Q6_K block inside its 16-byte-aligned box (K = 6144: 24 blocks
+    per row), a 6-row tile tail, the smallest K each takes, one tile, and
+    repeated calls give identical bytes."""
+    rng = np.random.default_rng(N + K + M + qt)
+    blocks = O.gguf_k_random_blocks(rng, qt, N, K)
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16}[xdt]
+    xt = _dev(torch, rng.normal(0.0, 1.0, (M, K)).astype(np.float32)).to(tdt)
+    lin = _lin(D, torch, blocks, qt, N, K)
+    y1 = lin.forward(xt)
+    y2 = lin.forward(xt)
+    assert torch.equal(y1, y2)
+    ref = O.gguf_k_linear_exact(xt.float().cpu().numpy(), blocks, qt, N)
+    assert rel_err(y1.float().cpu().numpy(), ref) < 1e-2
+    assert D.lib().dial_device_error(1) == 0

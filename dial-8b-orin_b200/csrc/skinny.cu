@@ -1903,12 +1903,8 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const float d = r ? dh : dl, dm = r ? mh : ml;
-        // 6-bit scales and mins as floats without a conversion instruction: 2^23 + v has
-        // v as its mantissa, and the subtraction of 2^23 is exact
-        const float aL = d * (__uint_as_float(0x4B000000u | (s2[r] & 0xFFu)) - 8388608.0f);
-        const float bL = fmaf(kBias, aL, dm * (__uint_as_float(0x4B000000u | (m2[r] & 0xFFu)) - 8388608.0f));
-        const float aH = d * (__uint_as_float(0x4B000000u | (s2[r] >> 8)) - 8388608.0f);
-        const float bH = fmaf(kBias, aH, dm * (__uint_as_float(0x4B000000u | (m2[r] >> 8)) - 8388608.0f));
+        const float aL = d * (float)(s2[r] & 0xFFu), bL = fmaf(kBias, aL, dm * (float)(m2[r] & 0xFFu));
+        const float aH = d * (float)(s2[r] >> 8), bH = fmaf(kBias, aH, dm * (float)(m2[r] >> 8));
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           float v = acc[0][2 * r + q];
@@ -2092,9 +2088,8 @@ __global__ void __launch_bounds__(kTmaWarps * 32, kCtasPerSM)
         const int sub = 8 * n + 2 * p + lh;  // scale index, byte sub % 4 of word sub / 4
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-          // int8 scale as a float: 2^23 + (u ^ 0x80) less 2^23 + 128, both exact
-          const uint32_t u8 = ((scw[r][sub >> 2] >> (8 * (sub & 3))) & 0xFFu) ^ 0x80u;
-          const float ds = d[r] * (__uint_as_float(0x4B000000u | u8) - 8388736.0f);
+          const int sc = (int)(int8_t)((scw[r][sub >> 2] >> (8 * (sub & 3))) & 0xFFu);
+          const float ds = d[r] * (float)sc;
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             float v = fmaf(ds, cq[2 * r + q], acc[0][2 * r + q]);

@@ -375,7 +375,7 @@ class GgufKSweep:
     in Q6_K (the two types of a Q4_K_M file) at M = 1, f16 activations, the
     file's native super-blocks read by the decode linear."""
     metric, unit, bound, dtype = "dequant-GEMV HBM GB/s", "GB/s", "hbm", "q4_k/q6_k x f16"
-    kernel = "kq_linear_kernel (whole sweep)"
+    kernel = "kq4_gemv_kernel + kq6_gemv_kernel (whole sweep)"
     data = "synthetic (seeded random Q4_K/Q6_K super-blocks with N(0,1e-4) f16 scales, N(0,1) activations)"
     ms = (1,)
     graph = True

@@ -21,6 +21,8 @@ benchmark configurations; no dataset is involved):
   w8a16_prefill The 4 fused linears of a Qwen3-8B layer (QKV 6144x4096, O
                 4096x4096, gate_up 24576x4096, down 4096x12288) at M = 512
                 (a 512-token prompt), f16.  Metric: dequant-GEMM TFLOP/s.
+  gguf_k_prefill  The same layer's 7 linears in Q4_K at M = 512 (a prompt),
+                f16.  Metric: dequant-GEMM TFLOP/s.
   gguf_k_sweep  The 7 linears of a Llama-3-8B layer in Q4_K and Q6_K (the
                 types of a Q4_K_M file) at M = 1, f16 activations.  Metric:
                 dequant-GEMV HBM GB/s over the sweep.
@@ -378,6 +380,8 @@ class GgufKSweep:
     kernel = "kq4_gemv_kernel + kq6_gemv_kernel (whole sweep)"
     data = "synthetic (seeded random Q4_K/Q6_K super-blocks with N(0,1e-4) f16 scales, N(0,1) activations)"
     ms = (1,)
+    types = ("Q4_K", "Q6_K")
+    name = "gguf_k_sweep"
     graph = True
 
     @staticmethod
@@ -401,7 +405,7 @@ class GgufKSweep:
         self.torch, self.D = torch, D
         rng = np.random.default_rng(SEED)
         layer, per_layer = [], 0
-        for qt in (D.Q4_K, D.Q6_K):
+        for qt in [{"Q4_K": D.Q4_K, "Q6_K": D.Q6_K}[t] for t in self.types]:
             for name, N, K in LLAMA_SHAPES:
                 b = torch.from_numpy(self.random_blocks(rng, qt, N, K).reshape(-1)).cuda()
                 lin = D.GgufKLinear.from_blocks(b, qt, K, N, name)
@@ -425,9 +429,9 @@ class GgufKSweep:
 
     @classmethod
     def describe(cls, world: int = 1):
-        per_layer = sum(N * (K // 256) * bb for bb in K_BLOCK_BYTES.values() for _, N, K in LLAMA_SHAPES)
+        per_layer = sum(N * (K // 256) * K_BLOCK_BYTES[t] for t in cls.types for _, N, K in LLAMA_SHAPES)
         copies = max(2, -(-3 * L2_BYTES // per_layer))
-        return {"workload": "gguf_k_sweep", "M": list(cls.ms), "types": ["Q4_K", "Q6_K"],
+        return {"workload": cls.name, "M": list(cls.ms), "types": list(cls.types),
                 "shapes": [f"{n}:{k}->{N}" for n, N, k in LLAMA_SHAPES], "activation": "f16",
                 "weights": "seeded random super-blocks (finite f16 scales)",
                 "l2": f"{copies} rotating layer copies ({copies * per_layer / 1e6:.0f} MB > 126 MB L2)",
@@ -437,9 +441,9 @@ class GgufKSweep:
     def bytes(cls):
         b = 0
         for m in cls.ms:
-            for bb in K_BLOCK_BYTES.values():
+            for t in cls.types:
                 for _, N, K in LLAMA_SHAPES:
-                    b += N * (K // 256) * bb + 2 * m * K + 2 * m * N
+                    b += N * (K // 256) * K_BLOCK_BYTES[t] + 2 * m * K + 2 * m * N
         return b
 
     def run_copy(self, li):
@@ -453,6 +457,25 @@ class GgufKSweep:
     def step(self):
         self.graphs[self.i % self.copies].replay()
         self.i += 1
+
+
+class GgufKPrefill(GgufKSweep):
+    """Q4_K prefill: the 7 linears of a Llama-3-8B layer as the file's Q4_K
+    super-blocks at M = 512 (a 512-token prompt), f16: the tcgen05 GEMM
+    dequantises each super-block once per token tile."""
+    metric, unit, bound, dtype = "dequant-GEMM TFLOP/s", "TFLOP/s", "tensor", "q4_k x f16 -> f16 MMA"
+    kernel = "dequant_gemm_kernel<Q4_K> (whole sweep)"
+    ms = (512,)
+    types = ("Q4_K",)
+    name = "gguf_k_prefill"
+
+    def __init__(self, torch, D, rank: int = 0, world: int = 1):
+        super().__init__(torch, D)
+        self.work_per_step = self.flops()
+
+    @classmethod
+    def flops(cls):
+        return sum(2 * m * N * K for m in cls.ms for _ in cls.types for _, N, K in LLAMA_SHAPES)
 
 
 class GgufSweepM32(GgufSweep):
@@ -866,7 +889,7 @@ class QwenGenerate(QwenDecode):
 
 WORKLOADS = {"w8a16_gemv": W8A16Gemv, "gguf_sweep": GgufSweep, "gguf_sweep_m32": GgufSweepM32,
              "gguf_prefill": GgufPrefill, "w8a16_prefill": W8A16Prefill,
-             "gguf_k_sweep": GgufKSweep,
+             "gguf_k_sweep": GgufKSweep, "gguf_k_prefill": GgufKPrefill,
              "qwen3_decode": QwenDecode, "qwen3_decode_bf16": QwenDecodeBf16,
              "qwen3_generate": QwenGenerate, "llama_gguf_decode": LlamaGgufDecode,
              "attention_batched": AttentionDecode}
@@ -888,11 +911,13 @@ class CpuWorkload:
             self.q, self.s32, _ = O.w8a16_quantize(w)
             self.x = rng.normal(0, 1, (1, wl.K)).astype(np.float16)
             self.work = wl.bytes()
-        elif name == "gguf_k_sweep":
+        elif name in ("gguf_k_sweep", "gguf_k_prefill"):
+            qts = [{"Q4_K": O.Q4_K, "Q6_K": O.Q6_K}[t] for t in wl.types]
             self.klins = [(O.gguf_k_random_blocks(rng, qt, N, K), qt, N, K)
-                          for qt in (O.Q4_K, O.Q6_K) for _, N, K in LLAMA_SHAPES]
-            self.xk = {K: rng.normal(0, 1, (1, K)).astype(np.float16) for _, _, K in LLAMA_SHAPES}
-            self.work = wl.bytes()
+                          for qt in qts for _, N, K in LLAMA_SHAPES]
+            self.M = wl.ms[0]
+            self.xk = {K: rng.normal(0, 1, (self.M, K)).astype(np.float16) for _, _, K in LLAMA_SHAPES}
+            self.work = wl.flops() if name == "gguf_k_prefill" else wl.bytes()
         elif name == "w8a16_prefill":
             self.wlins = []
             for _, N, K in QWEN_LAYER_LINEARS:
@@ -917,10 +942,11 @@ class CpuWorkload:
         if self.name == "w8a16_gemv":
             O.w8a16_linear_f32(self.x, self.q, self.s32)
             return 1.0
-        if self.name == "gguf_k_sweep":  # the CPU QMatMul arithmetic (Q8_K activations)
+        if self.name in ("gguf_k_sweep", "gguf_k_prefill"):  # the CPU QMatMul arithmetic (Q8_K activations)
+            mm = max(1, int(round(self.M * frac)))
             for blocks, qt, N, K in self.klins:
-                O.gguf_k_linear_candle(self.xk[K], blocks, qt, N)
-            return 1.0
+                O.gguf_k_linear_candle(self.xk[K][:mm], blocks, qt, N)
+            return mm / self.M
         if self.name == "w8a16_prefill":
             mm = max(1, int(round(self.M * frac)))
             for q, s32, K in self.wlins:
@@ -1088,7 +1114,7 @@ def cpu_measure(name, budget_s):
     if name == "llama_gguf_decode":
         return cpu_gguf_decode_measure(budget_s)
     cw = _CPU_WORKLOADS.get(name) or _CPU_WORKLOADS.setdefault(name, CpuWorkload(name))
-    frac = 1.0 if name not in ("gguf_prefill", "w8a16_prefill") else 16 / 512  # 16 of 512 rows
+    frac = 1.0 if name not in ("gguf_prefill", "w8a16_prefill", "gguf_k_prefill") else 16 / 512  # 16 of 512 rows
     cw.step(frac)  # warm-up
     t0 = time.perf_counter()
     n, work = 0, 0.0

@@ -59,7 +59,7 @@ constexpr int A_HALF_COLS = BK / 2;  // TMEM columns of one 128-row weight half 
 constexpr int kMaxSplit = 8;
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
 
-enum Fmt { kW8F32 = 0, kW8F16 = 1, kQ4 = 2, kQ8 = 3 };
+enum Fmt { kW8F32 = 0, kW8F16 = 1, kQ4 = 2, kQ8 = 3, kQ4K = 4 };
 
 // One CTA's tile and resources.  BT: activation rows (tokens) per CTA (UMMA N):
 // 128, or 32 for at most 32 rows (batched decode), where wider tiles would spend
@@ -91,7 +91,10 @@ struct Cfg {
   static constexpr int MAX_SPLIT = BT / 4 < kMaxSplit ? BT / 4 : kMaxSplit;
   static constexpr int RED_BYTES = BW * 4 * (BT + 4 * MAX_SPLIT);
   static constexpr bool GGUF = FMT == kQ4 || FMT == kQ8;
-  static constexpr int GB = FMT == kQ4 ? 64 : 128;  // packed bytes of a row per 128-K group
+  // packed bytes of a row per weight group: 128 K (2 stages), or for Q4_K one
+  // 256-K super-block of 144 bytes (4 stages)
+  static constexpr int GB = FMT == kQ4 ? 64 : (FMT == kQ4K ? 144 : 128);
+  static constexpr int SPG = FMT == kQ4K ? 4 : 2;  // K stages per weight group
   static constexpr int W_BYTES = BW * GB;
   static constexpr int D_BYTES = GGUF ? (BW / 16) * 128 : 0;  // 16-row tiles x 4 blocks x 16 rows
   static constexpr int W_OFF = B_STAGES * B_BYTES;
@@ -332,7 +335,13 @@ __device__ __forceinline__ uint2 ld_shared8(uint32_t addr) {
 // group g holds [16 rows][4 blocks] f16, row r's 4 scales at (r & 15) * 8.
 template <int FMT>
 __device__ __forceinline__ void read_group(uint32_t wbase, uint32_t dbase, int r, uint4 (&raw)[8],
-                                           float (&dv)[4]) {
+                                           float (&dv)[4], uint4& hdr) {
+  if (FMT == kQ4K) {  // 144-byte rows, no swizzle: the 16-byte header, then the 128 nibble bytes
+    hdr = ld_shared16(wbase + r * 144);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) raw[c] = ld_shared16(wbase + r * 144 + 16 + 16 * c);
+    return;
+  }
   if (FMT == kQ4) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) raw[c] = ld_shared16(wbase + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
@@ -403,6 +412,40 @@ __device__ __forceinline__ void dequant_part(int h, int kh, const uint4 (&raw)[8
   }
 }
 
+// Q4_K stage h of a super-block, K half kh: sub-block j = 2h + kh, the low
+// (kh = 0) or high nibbles of qs bytes 32h .. 32h + 31, as 16 operand pairs
+// (word w: elements 2w, 2w + 1).  Values as GGML's dequantiser computes them
+// (d sc q - dmin m in f32, no contraction), rounded once to the operand type:
+// the reference's f16 prefill copy (worker_gguf.rs:399-460) holds the same.
+template <bool BF16>
+__device__ __forceinline__ void dequant_q4k(int h, int kh, const uint4& hdr, const uint4 (&raw)[8],
+                                            uint32_t (&wv)[16]) {
+  const int j = 2 * h + kh;
+  auto sbyte = [&](int i) {  // scales[i], i < 12: bytes 4 .. 15 of the header
+    const uint32_t w = i < 4 ? hdr.y : (i < 8 ? hdr.z : hdr.w);
+    return (w >> (8 * (i & 3))) & 0xFFu;
+  };
+  uint32_t sc, m;
+  if (j < 4) {
+    sc = sbyte(j) & 63u;
+    m = sbyte(j + 4) & 63u;
+  } else {
+    sc = (sbyte(j + 4) & 15u) | ((sbyte(j - 4) >> 6) << 4);
+    m = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
+  }
+  const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
+  const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+  const float d0 = __fmul_rn(d, (float)sc), mm0 = __fmul_rn(dmin, (float)m);
+  const int sh = 4 * kh;
+#pragma unroll
+  for (int w = 0; w < 16; ++w) {
+    const uint32_t src = word(raw[2 * h + (w >> 3)], (w & 7) >> 1) >> (16 * (w & 1));
+    const float q0 = (float)((src >> sh) & 15u), q1 = (float)((src >> (8 + sh)) & 15u);
+    const float v0 = __fsub_rn(__fmul_rn(d0, q0), mm0), v1 = __fsub_rn(__fmul_rn(d0, q1), mm0);
+    wv[w] = BF16 ? pack_bf16(v0, v1) : h2_bits(__floats2half2_rn(v0, v1));
+  }
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
@@ -466,10 +509,10 @@ __global__ void __launch_bounds__(Cfg<FMT, BT, NH>::THREADS, Cfg<FMT, BT, NH>::C
   const int t0 = blockIdx.y * BT;  // tokens
   const int S = (int)gridDim.z;
   const int split = S > 1 ? (int)cluster_rank() : 0;
-  // this CTA's K range, in whole 128-wide groups (2 stages)
-  const int ngr = (p.nk + 1) >> 1;
+  // this CTA's K range, in whole weight groups (SPG stages each)
+  const int ngr = (p.nk + L::SPG - 1) / L::SPG;
   const int g0 = (int)((int64_t)ngr * split / S), g1 = (int)((int64_t)ngr * (split + 1) / S);
-  const int kt0 = 2 * g0, kt1 = min(2 * g1, p.nk);
+  const int kt0 = L::SPG * g0, kt1 = min(L::SPG * g1, p.nk);
   const int nst = kt1 - kt0;
 
   if (threadIdx.x == 0) {
@@ -581,17 +624,18 @@ __global__ void __launch_bounds__(Cfg<FMT, BT, NH>::THREADS, Cfg<FMT, BT, NH>::C
         ok = false;
         break;
       }
-      uint4 raw[8];
+      uint4 raw[8], hdr;
       float dv[4];
       read_group<FMT>(smem_base + (uint32_t)(L::W_OFF + ws * L::W_BYTES),
-                      smem_base + (uint32_t)(L::D_OFF + ws * L::D_BYTES), row, raw, dv);
+                      smem_base + (uint32_t)(L::D_OFF + ws * L::D_BYTES), row, raw, dv, hdr);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int kt = 2 * g + h;
+      for (int h = 0; h < L::SPG; ++h) {
+        const int kt = L::SPG * g + h;
         if (kt >= kt1) break;
         const int i = kt - kt0, sa = i % A_STAGES;
         uint32_t wv[16];
-        dequant_part<FMT, BF16>(h, kh, raw, dv, wv);
+        if constexpr (FMT == kQ4K) dequant_q4k<BF16>(h, kh, hdr, raw, wv);
+        else dequant_part<FMT, BF16>(h, kh, raw, dv, wv);
         if (pend >= 0) publish();
         const bool free = mbar_wait(EMPTY_A(sa), ((uint32_t)(i / A_STAGES) & 1u) ^ 1u);
         if (!__all_sync(0xffffffffu, free)) {
@@ -784,6 +828,11 @@ int choose_split(int64_t tiles, int ngr, int smem_bytes, int max_split, int thre
 // for GGUF, the tile-major d array as [N / 16 tiles, G * 128 bytes].
 template <int FMT, int BW>
 dial_status make_w_maps(const Params& p, CUtensorMap* wmap, CUtensorMap* dmap) {
+  if (FMT == kQ4K) {  // the file's rows of 144-byte super-blocks, one per box column
+    dial_status s = tma::make_byte_map(wmap, p.w, p.N, (int64_t)(p.K / 256) * 144, 144, BW, 0);
+    *dmap = *wmap;  // unused
+    return s;
+  }
   constexpr bool gguf = FMT == kQ4 || FMT == kQ8;
   constexpr int GB = FMT == kQ4 ? 64 : 128;
   if (!gguf) {
@@ -810,7 +859,7 @@ dial_status launch_bt(const void* x, const Params& p, cudaStream_t st) {
   cudaError_t e = ensure_smem<kern>(smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dequant_gemm)");
   const int64_t wt = (p.N + BW - 1) / BW, tt = (p.M + BT - 1) / BT;
-  const int S = choose_split<kern>(wt * tt, (p.nk + 1) / 2, smem, L::MAX_SPLIT, L::THREADS);
+  const int S = choose_split<kern>(wt * tt, (p.nk + L::SPG - 1) / L::SPG, smem, L::MAX_SPLIT, L::THREADS);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)wt, (unsigned)tt, (unsigned)S);
   cfg.blockDim = dim3(L::THREADS);
@@ -909,6 +958,15 @@ dial_status launch_gguf_gemm_sm100(const void* x, dial_dtype xdt, const void* qs
   if (xdt == DIAL_F32) return launch_one<kQ8, false, float>(xin, p, st);
   if (xdt == DIAL_F16) return launch_one<kQ8, false, __half>(xin, p, st);
   return launch_one<kQ8, true, __nv_bfloat16>(xin, p, st);
+}
+
+dial_status launch_q4k_gemm_sm100(const void* x, dial_dtype xdt, const void* blocks, void* y,
+                                  int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+  if (xdt != DIAL_F16 && xdt != DIAL_BF16) return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "Q4_K GEMM: f16/bf16 x");
+  Params p{static_cast<const uint8_t*>(blocks), nullptr, nullptr, y, (int)M, (int)N, (int)K, 0,
+           (int)(K / BK)};
+  if (xdt == DIAL_F16) return launch_one<kQ4K, false, __half>(x, p, st);
+  return launch_one<kQ4K, true, __nv_bfloat16>(x, p, st);
 }
 
 int* device_error_ptr() {

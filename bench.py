@@ -21,8 +21,8 @@ benchmark configurations; no dataset is involved):
   w8a16_prefill The 4 fused linears of a Qwen3-8B layer (QKV 6144x4096, O
                 4096x4096, gate_up 24576x4096, down 4096x12288) at M = 512
                 (a 512-token prompt), f16.  Metric: dequant-GEMM TFLOP/s.
-  gguf_k_prefill  The same layer's 7 linears in Q4_K at M = 512 (a prompt),
-                f16.  Metric: dequant-GEMM TFLOP/s.
+  gguf_k_prefill  The same layer's 7 linears in Q4_K and Q6_K at M = 512 (a
+                prompt), f16.  Metric: dequant-GEMM TFLOP/s.
   gguf_k_sweep  The 7 linears of a Llama-3-8B layer in Q4_K and Q6_K (the
                 types of a Q4_K_M file) at M = 1, f16 activations.  Metric:
                 dequant-GEMV HBM GB/s over the sweep.
@@ -460,13 +460,13 @@ class GgufKSweep:
 
 
 class GgufKPrefill(GgufKSweep):
-    """Q4_K prefill: the 7 linears of a Llama-3-8B layer as the file's Q4_K
-    super-blocks at M = 512 (a 512-token prompt), f16: the tcgen05 GEMM
-    dequantises each super-block once per token tile."""
-    metric, unit, bound, dtype = "dequant-GEMM TFLOP/s", "TFLOP/s", "tensor", "q4_k x f16 -> f16 MMA"
-    kernel = "dequant_gemm_kernel<Q4_K> (whole sweep)"
+    """K-quant prefill: the 7 linears of a Llama-3-8B layer as the file's Q4_K
+    and Q6_K super-blocks at M = 512 (a 512-token prompt), f16: the tcgen05
+    GEMM dequantises each super-block once per token tile."""
+    metric, unit, bound, dtype = "dequant-GEMM TFLOP/s", "TFLOP/s", "tensor", "q4_k/q6_k x f16 -> f16 MMA"
+    kernel = "dequant_gemm_kernel<Q4_K, Q6_K> (whole sweep)"
     ms = (512,)
-    types = ("Q4_K",)
+    types = ("Q4_K", "Q6_K")
     name = "gguf_k_prefill"
 
     def __init__(self, torch, D, rank: int = 0, world: int = 1):

@@ -59,7 +59,7 @@ constexpr int A_HALF_COLS = BK / 2;  // TMEM columns of one 128-row weight half 
 constexpr int kMaxSplit = 8;
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
 
-enum Fmt { kW8F32 = 0, kW8F16 = 1, kQ4 = 2, kQ8 = 3, kQ4K = 4 };
+enum Fmt { kW8F32 = 0, kW8F16 = 1, kQ4 = 2, kQ8 = 3, kQ4K = 4, kQ6K = 5 };
 
 // One CTA's tile and resources.  BT: activation rows (tokens) per CTA (UMMA N):
 // 128, or 32 for at most 32 rows (batched decode), where wider tiles would spend
@@ -83,7 +83,7 @@ struct Cfg {
   static constexpr int A_STAGES = 4;
   static_assert(ACC_COLS + A_STAGES * A_COLS <= TMEM_COLS, "TMEM budget");
   static constexpr int B_STAGES = NH == 1 ? 3 : 4;  // token tiles in shared memory
-  static constexpr int W_STAGES = NH == 1 ? 3 : 4;  // packed weight groups (128 K)
+  static constexpr int W_STAGES = FMT == kQ6K ? 2 : (NH == 1 ? 3 : 4);  // packed weight groups
   static constexpr int B_BYTES = BT * BK * 2;   // token tile per stage
   // split-K: at most BT / 4 CTAs (each owns whole float4 column groups); the
   // owner's receive buffer is [S senders][BW rows][BT / S + 4] f32 (the +4 pad
@@ -93,8 +93,10 @@ struct Cfg {
   static constexpr bool GGUF = FMT == kQ4 || FMT == kQ8;
   // packed bytes of a row per weight group: 128 K (2 stages), or for Q4_K one
   // 256-K super-block of 144 bytes (4 stages)
-  static constexpr int GB = FMT == kQ4 ? 64 : (FMT == kQ4K ? 144 : 128);
-  static constexpr int SPG = FMT == kQ4K ? 4 : 2;  // K stages per weight group
+  // (Q6_K: a 224-byte box from the 16-byte boundary at or below the 210-byte
+  // super-block, which starts o = 210 g mod 16 bytes into it)
+  static constexpr int GB = FMT == kQ4 ? 64 : (FMT == kQ4K ? 144 : (FMT == kQ6K ? 224 : 128));
+  static constexpr int SPG = FMT == kQ4K || FMT == kQ6K ? 4 : 2;  // K stages per weight group
   static constexpr int W_BYTES = BW * GB;
   static constexpr int D_BYTES = GGUF ? (BW / 16) * 128 : 0;  // 16-row tiles x 4 blocks x 16 rows
   static constexpr int W_OFF = B_STAGES * B_BYTES;
@@ -336,6 +338,7 @@ __device__ __forceinline__ uint2 ld_shared8(uint32_t addr) {
 template <int FMT>
 __device__ __forceinline__ void read_group(uint32_t wbase, uint32_t dbase, int r, uint4 (&raw)[8],
                                            float (&dv)[4], uint4& hdr) {
+  if (FMT == kQ6K) return;  // read per stage by dequant_q6k
   if (FMT == kQ4K) {  // 144-byte rows, no swizzle: the 16-byte header, then the 128 nibble bytes
     hdr = ld_shared16(wbase + r * 144);
 #pragma unroll
@@ -443,6 +446,45 @@ __device__ __forceinline__ void dequant_q4k(int h, int kh, const uint4& hdr, con
     const float q0 = (float)((src >> sh) & 15u), q1 = (float)((src >> (8 + sh)) & 15u);
     const float v0 = __fsub_rn(__fmul_rn(d0, q0), mm0), v1 = __fsub_rn(__fmul_rn(d0, q1), mm0);
     wv[w] = BF16 ? pack_bf16(v0, v1) : h2_bits(__floats2half2_rn(v0, v1));
+  }
+}
+
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+// 4 bytes at a 2-byte aligned shared address
+__device__ __forceinline__ uint32_t ld_shared_u32_a2(uint32_t addr) {
+  if ((addr & 3u) == 0) return ld_shared_u32(addr);
+  return __funnelshift_r(ld_shared_u32(addr - 2), ld_shared_u32(addr + 2), 16);
+}
+
+// Q6_K stage h of a super-block (at shared address `blk`, 2-byte aligned), K
+// half kh: elements 64h + 32kh + l, l < 32, are half n = h / 2, quarter
+// p = 2 (h % 2) + kh of GGML's layout: code ((ql[64n + 32(p & 1) + l] >> 4(p >> 1))
+// & 15) | ((qh[32n + l] >> 2p) & 3) << 4, weight d sc[8n + 2p + l / 16] (code - 32),
+// computed as GGML does in f32 and rounded once to the operand type.
+template <bool BF16>
+__device__ __forceinline__ void dequant_q6k(int h, int kh, uint32_t blk, uint32_t (&wv)[16]) {
+  const int n = h >> 1, p = 2 * (h & 1) + kh;
+  const uint32_t qla = blk + (uint32_t)(64 * n + 32 * (p & 1)), qha = blk + (uint32_t)(128 + 32 * n);
+  const uint32_t scw = ld_shared_u32_a2(blk + (uint32_t)(192 + 8 * n + 2 * p));  // scales 8n+2p, +1
+  const float d = __half2float(__ushort_as_half((unsigned short)(ld_shared_u32_a2(blk + 208u) & 0xFFFFu)));
+  const float d0 = __fmul_rn(d, (float)(int)(int8_t)(scw & 0xFFu));
+  const float d1 = __fmul_rn(d, (float)(int)(int8_t)((scw >> 8) & 0xFFu));
+  const int ns = 4 * (p >> 1), hs = 2 * p;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {  // bytes 4q .. 4q + 3 of the 32 -> words 2q, 2q + 1
+    const uint32_t l = ld_shared_u32_a2(qla + 4u * q), hh = ld_shared_u32_a2(qha + 4u * q);
+    float v[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int code = (int)(((l >> (8 * b + ns)) & 15u) | (((hh >> (8 * b + hs)) & 3u) << 4));
+      v[b] = __fmul_rn(q < 4 ? d0 : d1, (float)(code - 32));
+    }
+    wv[2 * q] = BF16 ? pack_bf16(v[0], v[1]) : h2_bits(__floats2half2_rn(v[0], v[1]));
+    wv[2 * q + 1] = BF16 ? pack_bf16(v[2], v[3]) : h2_bits(__floats2half2_rn(v[2], v[3]));
   }
 }
 
@@ -589,7 +631,7 @@ __global__ void __launch_bounds__(Cfg<FMT, BT, NH>::THREADS, Cfg<FMT, BT, NH>::C
         if (!mbar_wait(EMPTY_W(s), ((uint32_t)(i / W_STAGES) & 1u) ^ 1u)) break;
         mbar_expect_tx(FULL_W(s), tx);
         tma_load_2d(smem_base + (uint32_t)(L::W_OFF + s * L::W_BYTES), &tmap_w, FULL_W(s),
-                    g * L::GB, n0);
+                    FMT == kQ6K ? (g * 210) & ~15 : g * L::GB, n0);
         if (L::GGUF)
           tma_load_2d(smem_base + (uint32_t)(L::D_OFF + s * L::D_BYTES), &tmap_d, FULL_W(s),
                       g * 128, n0 / 16);
@@ -635,6 +677,10 @@ __global__ void __launch_bounds__(Cfg<FMT, BT, NH>::THREADS, Cfg<FMT, BT, NH>::C
         const int i = kt - kt0, sa = i % A_STAGES;
         uint32_t wv[16];
         if constexpr (FMT == kQ4K) dequant_q4k<BF16>(h, kh, hdr, raw, wv);
+        else if constexpr (FMT == kQ6K)
+          dequant_q6k<BF16>(h, kh,
+                            smem_base + (uint32_t)(L::W_OFF + ws * L::W_BYTES + row * 224 + ((g * 210) & 15)),
+                            wv);
         else dequant_part<FMT, BF16>(h, kh, raw, dv, wv);
         if (pend >= 0) publish();
         const bool free = mbar_wait(EMPTY_A(sa), ((uint32_t)(i / A_STAGES) & 1u) ^ 1u);
@@ -828,8 +874,10 @@ int choose_split(int64_t tiles, int ngr, int smem_bytes, int max_split, int thre
 // for GGUF, the tile-major d array as [N / 16 tiles, G * 128 bytes].
 template <int FMT, int BW>
 dial_status make_w_maps(const Params& p, CUtensorMap* wmap, CUtensorMap* dmap) {
-  if (FMT == kQ4K) {  // the file's rows of 144-byte super-blocks, one per box column
-    dial_status s = tma::make_byte_map(wmap, p.w, p.N, (int64_t)(p.K / 256) * 144, 144, BW, 0);
+  if (FMT == kQ4K || FMT == kQ6K) {  // the file's rows of super-blocks (144 / 210 bytes each)
+    const int bb = FMT == kQ4K ? 144 : 210;
+    dial_status s = tma::make_byte_map(wmap, p.w, p.N, (int64_t)(p.K / 256) * bb, FMT == kQ4K ? 144 : 224,
+                                       BW, 0);
     *dmap = *wmap;  // unused
     return s;
   }
@@ -960,13 +1008,18 @@ dial_status launch_gguf_gemm_sm100(const void* x, dial_dtype xdt, const void* qs
   return launch_one<kQ8, true, __nv_bfloat16>(xin, p, st);
 }
 
-dial_status launch_q4k_gemm_sm100(const void* x, dial_dtype xdt, const void* blocks, void* y,
-                                  int64_t M, int64_t K, int64_t N, cudaStream_t st) {
-  if (xdt != DIAL_F16 && xdt != DIAL_BF16) return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "Q4_K GEMM: f16/bf16 x");
+dial_status launch_kquant_gemm_sm100(const void* x, dial_dtype xdt, const void* blocks, int type,
+                                     void* y, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+  if (xdt != DIAL_F16 && xdt != DIAL_BF16) return fail(DIAL_ERR_UNSUPPORTED_DTYPE, "K-quant GEMM: f16/bf16 x");
   Params p{static_cast<const uint8_t*>(blocks), nullptr, nullptr, y, (int)M, (int)N, (int)K, 0,
            (int)(K / BK)};
-  if (xdt == DIAL_F16) return launch_one<kQ4K, false, __half>(x, p, st);
-  return launch_one<kQ4K, true, __nv_bfloat16>(x, p, st);
+  if (type == DIAL_GGML_Q4_K) {
+    if (xdt == DIAL_F16) return launch_one<kQ4K, false, __half>(x, p, st);
+    return launch_one<kQ4K, true, __nv_bfloat16>(x, p, st);
+  }
+  if (K % 2048) return fail(DIAL_ERR_SHAPE, "Q6_K GEMM: K %% 2048 != 0");
+  if (xdt == DIAL_F16) return launch_one<kQ6K, false, __half>(x, p, st);
+  return launch_one<kQ6K, true, __nv_bfloat16>(x, p, st);
 }
 
 int* device_error_ptr() {

@@ -20,10 +20,11 @@ dial_status launch_gguf_gemm_sm100(const void* x, dial_dtype xdt, const void* qs
                                    const uint16_t* d, int type, void* y, int64_t M, int64_t K,
                                    int64_t N, void* ws, cudaStream_t st);
 
-// Q4_K super-blocks as the file holds them ([N, K / 256] x 144 bytes, 16-byte
-// aligned), f16/bf16 activations, K % 256 == 0: each weight group is one
+// Q4_K / Q6_K super-blocks as the file holds them ([N, K / 256] x 144 / 210
+// bytes, 16-byte aligned), f16/bf16 activations, K % 256 == 0 (Q6_K: K % 2048
+// == 0, so that a row is a 16-byte multiple): each weight group is one
 // super-block, dequantised as GGML does and rounded to the activation dtype.
-dial_status launch_q4k_gemm_sm100(const void* x, dial_dtype xdt, const void* blocks, void* y,
-                                  int64_t M, int64_t K, int64_t N, cudaStream_t st);
+dial_status launch_kquant_gemm_sm100(const void* x, dial_dtype xdt, const void* blocks, int type,
+                                     void* y, int64_t M, int64_t K, int64_t N, cudaStream_t st);
 
 }  // namespace dial

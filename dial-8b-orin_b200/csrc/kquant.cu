@@ -404,11 +404,11 @@ extern "C" dial_status dial_gguf_k_linear(const void* x, dial_dtype xdt, const v
   if (!aligned16(x)) return fail(DIAL_ERR_MISALIGNED, "x must be 16-byte aligned");
   if (type == DIAL_GGML_Q4_K && kq4_gemv_ok(M, K, N, xdt, x, blocks))
     return launch_kq4_gemv(x, xdt, blocks, y, M, K, N, as_stream(stream));
-  // prefill-sized Q4_K: the tcgen05 GEMM dequantises each super-block once per
+  // prefill-sized: the tcgen05 GEMM dequantises each super-block once per
   // token tile (the values of the reference's f16 prefill copy)
-  if (type == DIAL_GGML_Q4_K && M > 8 && (xdt == DIAL_F16 || xdt == DIAL_BF16) && aligned16(blocks) &&
-      N < (1ll << 31) && K < (1ll << 31) && M < (1ll << 31))
-    return launch_q4k_gemm_sm100(x, xdt, blocks, y, M, K, N, as_stream(stream));
+  if (M > 8 && (xdt == DIAL_F16 || xdt == DIAL_BF16) && aligned16(blocks) && N < (1ll << 31) &&
+      K < (1ll << 31) && M < (1ll << 31) && (type == DIAL_GGML_Q4_K || K % 2048 == 0))
+    return launch_kquant_gemm_sm100(x, xdt, blocks, (int)type, y, M, K, N, as_stream(stream));
   if (type == DIAL_GGML_Q4_K)
     return launch_kq_linear<DIAL_GGML_Q4_K>(x, xdt, blocks, y, M, K, N, as_stream(stream));
   if (kq6_gemv_ok(M, K, N, xdt, x, blocks))

@@ -149,20 +149,22 @@ def test_k_quant_tensor_core_gemv_shapes(D, torch, qt, N, K, M, xdt):
 @pytest.mark.parametrize("M,N,K", [(9, 1030, 4096), (32, 2048, 4096), (33, 1030, 4096),
                                    (128, 512, 2048), (512, 1030, 4096), (64, 4096, 14336)])
 @pytest.mark.parametrize("xdt", ["f16", "bf16"])
-def test_q4_k_prefill_gemm(D, torch, M, N, K, xdt):
-    """Prefill-sized Q4_K linears run on the tcgen05 GEMM, each super-block
-    dequantised once per token tile (GGML's values rounded to the activation
-    dtype): against the exact oracle, and against the dequantised copy times x
-    (the reference's f16 prefill route) in f32."""
-    rng = np.random.default_rng(M + N + K)
-    blocks = O.gguf_k_random_blocks(rng, O.Q4_K, N, K)
+@pytest.mark.parametrize("name,qt", TYPES)
+def test_k_quant_prefill_gemm(D, torch, name, qt, M, N, K, xdt):
+    """Prefill-sized Q4_K / Q6_K linears run on the tcgen05 GEMM, each
+    super-block dequantised once per token tile (GGML's values rounded to the
+    activation dtype; Q6_K blocks at every 2-byte offset of their boxes):
+    against the exact oracle, and against the dequantised copy times x (the
+    reference's f16 prefill route) in f32."""
+    rng = np.random.default_rng(M + N + K + qt)
+    blocks = O.gguf_k_random_blocks(rng, qt, N, K)
     tdt = {"f16": torch.float16, "bf16": torch.bfloat16}[xdt]
     xt = _dev(torch, rng.normal(0.0, 1.0, (M, K)).astype(np.float32)).to(tdt)
-    lin = _lin(D, torch, blocks, O.Q4_K, N, K)
+    lin = _lin(D, torch, blocks, qt, N, K)
     y = lin.forward(xt)
     assert D.lib().dial_device_error(1) == 0
     yf = y.float().cpu().numpy()
-    ref = O.gguf_k_linear_exact(xt.float().cpu().numpy(), blocks, O.Q4_K, N)
+    ref = O.gguf_k_linear_exact(xt.float().cpu().numpy(), blocks, qt, N)
     assert rel_err(yf, ref) < 1e-2
     wcopy = lin.dequantize(tdt).float()  # the values the GEMM multiplies
     dense = (xt.float() @ wcopy.t()).cpu().numpy()

@@ -62,8 +62,10 @@ constexpr unsigned long long kTimeoutNs = 1000000000ull;
 enum Fmt { kW8F32 = 0, kW8F16 = 1, kQ4 = 2, kQ8 = 3, kQ4K = 4, kQ6K = 5 };
 
 // One CTA's tile and resources.  BT: activation rows (tokens) per CTA (UMMA N):
-// 128, or 32 for at most 32 rows (batched decode), where wider tiles would spend
-// most MMA cycles on padding.  NH: 128-row weight halves per CTA (UMMA M = 128
+// 256 from 256 rows on (each dequantised weight stage then feeds twice the
+// MMAs; one CTA per SM with all 512 TMEM columns), 128 below, or 32 for at
+// most 32 rows (batched decode), where wider tiles would spend most MMA cycles
+// on padding.  NH: 128-row weight halves per CTA (UMMA M = 128
 // each).  NH = 2: 16 dequantising warps (lane quarter x weight half x K half of
 // a stage), all 512 TMEM columns, one CTA per SM.  NH = 1: 8 dequantising warps,
 // 256 TMEM columns and at most 113 KB of shared memory, so that two CTAs share
@@ -76,8 +78,10 @@ struct Cfg {
   static constexpr int BW = 128 * NH;           // weight rows per CTA
   static constexpr int DQ_WARPS = 8 * NH;
   static constexpr int THREADS = 64 + DQ_WARPS * 32 + 32;  // + the weight producer warp
-  static constexpr int CTAS_PER_SM = NH == 1 ? 2 : 1;
-  static constexpr int TMEM_COLS = NH == 1 ? 256 : 512;
+  // two CTAs per SM for the narrow CTA up to 128 tokens; a 256-token tile
+  // needs all 512 TMEM columns (one CTA per SM)
+  static constexpr int CTAS_PER_SM = NH == 1 && BT <= 128 ? 2 : 1;
+  static constexpr int TMEM_COLS = NH == 1 && BT <= 128 ? 256 : 512;
   static constexpr int ACC_COLS = NH * BT;      // NH f32 accumulators of BT columns
   static constexpr int A_COLS = NH * A_HALF_COLS;  // TMEM columns of a dequantised stage
   static constexpr int A_STAGES = 4;
@@ -104,7 +108,7 @@ struct Cfg {
   static constexpr int RING = D_OFF + W_STAGES * D_BYTES;
   static constexpr int DATA = RING > RED_BYTES ? RING : RED_BYTES;
   static constexpr int BYTES = DATA + 1024 /*align*/ + 256 /*barriers*/;
-  static_assert(BYTES <= (NH == 1 ? 113 : 227) * 1024, "shared memory budget");
+  static_assert(BYTES <= (CTAS_PER_SM == 2 ? 113 : 227) * 1024, "shared memory budget");
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -933,6 +937,7 @@ constexpr bool kNarrowDecode = true, kNarrowPrefill = true;
 template <int FMT, bool BF16, typename YT>
 dial_status launch_one(const void* x, const Params& p, cudaStream_t st) {
   if (p.M <= 32) return launch_bt<FMT, BF16, YT, 32, kNarrowDecode ? 1 : 2>(x, p, st);
+  if (p.M >= 256) return launch_bt<FMT, BF16, YT, 256, 1>(x, p, st);
   return launch_bt<FMT, BF16, YT, 128, kNarrowPrefill ? 1 : 2>(x, p, st);
 }
 

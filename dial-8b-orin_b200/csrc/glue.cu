@@ -786,19 +786,20 @@ dial_status launch_qk_rope_kv(const void* qkv, const void* qn, const void* kn, c
   return s;
 }
 
-// Key splits per (token, kv head), at least 128 keys each (8 tiles of 16 keys,
-// two per warp): the count whose waves of CTAs (three resident per SM: 168
+// Key splits per (token, kv head), at least 64 keys each (4 tiles of 16 keys,
+// one per warp): the count whose waves of CTAs (three resident per SM: 168
 // registers x 128 threads, 72 KB of shared memory) waste least of the last
-// wave, with a small charge per split for its partials and the combine.
+// wave, with a small charge per split for its partials and the merge (a
+// one-token decode is latency bound: more, shorter splits measured faster).
 static int attention_splits(int64_t tokens, int hkv, int64_t max_len) {
   const int64_t pairs = tokens * hkv, slots = 3 * (int64_t)sm_count();
   if (pairs >= slots) return 1;  // the unsplit grid already fills the GPU
-  const int64_t cap = std::min<int64_t>(32, std::max<int64_t>(1, (max_len + 127) / 128));
+  const int64_t cap = std::min<int64_t>(32, std::max<int64_t>(1, (max_len + 63) / 64));
   int best = 1;
   double best_t = 1e30;
   for (int n = 1; n <= cap; ++n) {
     const double waves = (double)((pairs * n + slots - 1) / slots);
-    const double t = waves / n + 0.02 * n;
+    const double t = waves / n + 0.005 * n;
     if (t < best_t - 1e-9) {
       best_t = t;
       best = n;

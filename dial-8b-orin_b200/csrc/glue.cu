@@ -303,7 +303,27 @@ __global__ void __launch_bounds__(kTcWarps * 32)
                         const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
                         T* __restrict__ out, float* __restrict__ part, int hq, int hkv,
                         int64_t max_seq, int nsplit, float qscale, QkvIn<T> in) {
-  pdl_begin();
+  pdl_trigger();
+  if constexpr (FUSE) {
+    // The split's cache rows before the new position were written by kernels
+    // that ended long before this one (earlier steps, or the prompt): pull them
+    // into L2 while the previous kernel finishes.  Only a hint -- the position
+    // read here may still be the previous step's, so it is clamped into the
+    // cache and nothing below uses it.
+    if (threadIdx.x < 2) {
+      int64_t lp = (int64_t)pos[blockIdx.x] + 1;
+      lp = lp < 1 ? 1 : (lp > max_seq ? max_seq : lp);
+      const int64_t per = (lp + nsplit - 1) / nsplit, k0 = (int64_t)blockIdx.z * per;
+      const int64_t k1 = lp < k0 + per ? lp : k0 + per;
+      if (k1 > k0) {
+        const T* base = (threadIdx.x ? vc : kc) + (((int64_t)slot[blockIdx.x] * hkv + (int64_t)blockIdx.y) * max_seq + k0) * 128;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base),
+                     "r"((uint32_t)(k1 - k0) * 256u)
+                     : "memory");
+      }
+    }
+  }
+  pdl_wait();
   constexpr int D = 128;
   extern __shared__ __align__(1024) uint8_t tc_smem[];
   __shared__ float sm_m[kTcWarps][REP], sm_l[kTcWarps][REP];

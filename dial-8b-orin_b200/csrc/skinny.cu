@@ -832,6 +832,13 @@ __device__ __forceinline__ uint32_t xslot(uint32_t c) {
   return (c & ~15u) | ((c & 3u) << 2) | ((c >> 2) & 3u);
 }
 
+// Chunks per thread whose global loads are issued together: the staging runs
+// on the critical path between two linears, while the next linear's weight
+// prefetch keeps the memory system busy, so every dependent L2 round trip
+// costs about a microsecond.  Each pass loads a batch of its chunks' inputs
+// (and the norm gains) before it uses any of them.
+constexpr int kStageBatch = 4;
+
 template <bool BF16>
 __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* __restrict__ x, int M,
                                           int K, uint32_t xsm_base, uint32_t aux, int active) {
@@ -840,6 +847,7 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
   const uint32_t tm = aux + kAuxTm, tinv = aux + kAuxInv, tmul = aux + kAuxMul, cs = aux + kAuxCs;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarp = active >> 5;
   const int per_tok = K / 8, n16 = M * per_tok;
+  constexpr int B = kStageBatch;
   // per-token output multiplier 2^e (bf16) or 1, once the token's max is final
   auto put_mul = [&]() {
     if (tid < M) sts32f(tmul + 4u * tid, BF16 ? ldexpf(1.0f, tok_exp(lds32f(tm + 4u * tid))) : 1.0f);
@@ -858,27 +866,45 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
   auto amax = [&](int m, float v) {
     if (BF16) atomicMax(tmax + m, __float_as_uint(v));
   };
+  // chunk b of this thread's batch starting at c0 (chunks tid, tid + active, ...)
+  auto chunk = [&](int c0, int b) { return c0 + b * active; };
   if (p.mode == kProRms) {
-    for (int c = tid; c < n16; c += active) {
-      const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
-      const size_t off = (size_t)m * K + (size_t)k8;
-      const uint4 xv = ld_ro16(x + off), rv = p.res ? ld_ro16(p.res + off) : z;
-      const uint4 wv = ld_ro16(p.w + k8);
-      uint32_t o[8];
-      float ss = 0.0f, mx = 0.0f;
+    for (int c0 = tid; c0 < n16; c0 += B * active) {
+      uint4 xv[B], rv[B], wv[B];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float h = act_f32<BF16>(h16(xv, i));
-        if (p.res) h = act_f32<BF16>(act_rnd<BF16>(h + act_f32<BF16>(h16(rv, i))));
-        o[i] = act_rnd<BF16>(h);
-        ss += h * h;
-        mx = fmaxf(mx, fabsf(h * act_f32<BF16>(h16(wv, i))));
+      for (int b = 0; b < B; ++b) {
+        const int c = chunk(c0, b);
+        xv[b] = rv[b] = wv[b] = z;
+        if (c < n16) {
+          const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
+          const size_t off = (size_t)m * K + (size_t)k8;
+          xv[b] = ld_ro16(x + off);
+          if (p.res) rv[b] = ld_ro16(p.res + off);
+          wv[b] = ld_ro16(p.w + k8);
+        }
       }
-      const uint4 hv = pack8(o);
-      if (blockIdx.x == 0 && p.h_out) *reinterpret_cast<uint4*>(p.h_out + off) = hv;
-      sts16(xa(c), hv);
-      sts32f(cs + 4u * (uint32_t)c, ss);
-      amax(m, mx);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int c = chunk(c0, b);
+        if (c >= n16) break;
+        const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
+        const size_t off = (size_t)m * K + (size_t)k8;
+        uint32_t o[8];
+        float ss = 0.0f, mx = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float h = act_f32<BF16>(h16(xv[b], i));
+          if (p.res) h = act_f32<BF16>(act_rnd<BF16>(h + act_f32<BF16>(h16(rv[b], i))));
+          o[i] = act_rnd<BF16>(h);
+          ss += h * h;
+          mx = fmaxf(mx, fabsf(h * act_f32<BF16>(h16(wv[b], i))));
+        }
+        const uint4 hv = pack8(o);
+        if (blockIdx.x == 0 && p.h_out) *reinterpret_cast<uint4*>(p.h_out + off) = hv;
+        sts16(xa(c), hv);
+        sts32f(cs + 4u * (uint32_t)c, ss);
+        amax(m, mx);
+      }
     }
     active_warps_sync(active);
     for (int m = warp; m < M; m += nwarp) {
@@ -894,33 +920,54 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
     }
     active_warps_sync(active);
     put_mul();
-    for (int c = tid; c < n16; c += active) {  // normalise in place, scaled to f16
-      const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
-      const uint4 hv = lds16(xa(c)), wv = ld_ro16(p.w + k8);
-      const float inv = lds32f(tinv + 4u * m);
-      const int e = BF16 ? tok_exp(lds32f(tm + 4u * m)) : 0;
-      uint32_t o[8];
+    for (int c0 = tid; c0 < n16; c0 += B * active) {  // normalise in place, scaled to f16
+      uint4 hv[B], wv[B];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float v =
-            act_f32<BF16>(act_rnd<BF16>(act_f32<BF16>(h16(hv, i)) * inv * act_f32<BF16>(h16(wv, i))));
-        o[i] = __half_as_ushort(__float2half_rn(BF16 ? ldexpf(v, -e) : v));
+      for (int b = 0; b < B; ++b) {
+        const int c = chunk(c0, b);
+        hv[b] = wv[b] = z;
+        if (c < n16) {
+          const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
+          hv[b] = lds16(xa(c));
+          wv[b] = ld_ro16(p.w + k8);
+        }
       }
-      sts16(xa(c), pack8(o));
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int c = chunk(c0, b);
+        if (c >= n16) break;
+        const int m = c / per_tok;
+        const float inv = lds32f(tinv + 4u * m);
+        const int e = BF16 ? tok_exp(lds32f(tm + 4u * m)) : 0;
+        uint32_t o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float v = act_f32<BF16>(
+              act_rnd<BF16>(act_f32<BF16>(h16(hv[b], i)) * inv * act_f32<BF16>(h16(wv[b], i))));
+          o[i] = __half_as_ushort(__float2half_rn(BF16 ? ldexpf(v, -e) : v));
+        }
+        sts16(xa(c), pack8(o));
+      }
     }
   } else {
     // x itself or swiglu(gate, up), rounded to the activation dtype.  f16: one
     // pass writes the staged values.  bf16: pass 1 takes the max (and keeps
     // swiglu's values in xsm, computed once), pass 2 writes the scaled f16.
-    auto input8 = [&](int c, float (&v)[8]) {
+    auto load8 = [&](int c, uint4& gv, uint4& uv) {
       const int m = c / per_tok, k8 = (c - m * per_tok) * 8;
       if (p.mode == kProX) {
-        const uint4 xv = ld_ro16(x + (size_t)m * K + k8);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(xv, i));
+        gv = ld_ro16(x + (size_t)m * K + k8);
       } else {
         const uint16_t* gu = x + (size_t)m * 2 * K;
-        const uint4 gv = ld_ro16(gu + k8), uv = ld_ro16(gu + K + k8);
+        gv = ld_ro16(gu + k8);
+        uv = ld_ro16(gu + K + k8);
+      }
+    };
+    auto input8 = [&](const uint4& gv, const uint4& uv, float (&v)[8]) {
+      if (p.mode == kProX) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(gv, i));
+      } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float gg = act_f32<BF16>(h16(gv, i));
@@ -930,36 +977,61 @@ __device__ __forceinline__ void stage_act(const ActPrologue& p, const uint16_t* 
       }
     };
     if (BF16) {
-      for (int c = tid; c < n16; c += active) {
-        float v[8];
-        input8(c, v);
-        float mx = 0.0f;
-        uint32_t o[8];
+      for (int c0 = tid; c0 < n16; c0 += B * active) {
+        uint4 gv[B], uv[B];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          mx = fmaxf(mx, fabsf(v[i]));
-          o[i] = act_rnd<BF16>(v[i]);
+        for (int b = 0; b < B; ++b) {
+          gv[b] = uv[b] = z;
+          if (chunk(c0, b) < n16) load8(chunk(c0, b), gv[b], uv[b]);
         }
-        if (p.mode != kProX) sts16(xa(c), pack8(o));
-        amax(c / per_tok, mx);
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const int c = chunk(c0, b);
+          if (c >= n16) break;
+          float v[8];
+          input8(gv[b], uv[b], v);
+          float mx = 0.0f;
+          uint32_t o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            mx = fmaxf(mx, fabsf(v[i]));
+            o[i] = act_rnd<BF16>(v[i]);
+          }
+          if (p.mode != kProX) sts16(xa(c), pack8(o));
+          amax(c / per_tok, mx);
+        }
       }
       active_warps_sync(active);
     }
     put_mul();
-    for (int c = tid; c < n16; c += active) {
-      float v[8];
-      if (BF16 && p.mode != kProX) {
-        const uint4 yv = lds16(xa(c));
+    for (int c0 = tid; c0 < n16; c0 += B * active) {
+      uint4 gv[B], uv[B];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(yv, i));
-      } else {
-        input8(c, v);
+      for (int b = 0; b < B; ++b) {
+        const int c = chunk(c0, b);
+        gv[b] = uv[b] = z;
+        if (c < n16) {
+          if (BF16 && p.mode != kProX) gv[b] = lds16(xa(c));
+          else load8(c, gv[b], uv[b]);
+        }
       }
-      const int e = BF16 ? tok_exp(__uint_as_float(tmax[c / per_tok])) : 0;
-      uint32_t o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = __half_as_ushort(__float2half_rn(BF16 ? ldexpf(v[i], -e) : v[i]));
-      sts16(xa(c), pack8(o));
+      for (int b = 0; b < B; ++b) {
+        const int c = chunk(c0, b);
+        if (c >= n16) break;
+        float v[8];
+        if (BF16 && p.mode != kProX) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = act_f32<BF16>(h16(gv[b], i));
+        } else {
+          input8(gv[b], uv[b], v);
+        }
+        const int e = BF16 ? tok_exp(__uint_as_float(tmax[c / per_tok])) : 0;
+        uint32_t o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = __half_as_ushort(__float2half_rn(BF16 ? ldexpf(v[i], -e) : v[i]));
+        sts16(xa(c), pack8(o));
+      }
     }
   }
   active_warps_sync(active);

@@ -1,0 +1,212 @@
+"""The reference's TCP framing and message kinds (spm/proto/message.rs) and the
+pipeline over TCP links: framing limits, every message kind through the body
+codec, the transfer limiter's environment and pacing, and 2- and 3-stage
+pipelines over TcpChannel checked against the single-process chain."""
+import os
+import socket
+import struct
+import sys
+
+import pytest
+
+import torch
+import torch.multiprocessing as mp
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "dial-8b-orin_b200"))
+from dial_cuda import wire as W  # noqa: E402
+
+from test_pipeline_cpu import FakeCompute, _free_port, reference  # noqa: E402
+
+
+def _pair():
+    a, b = socket.socketpair()
+    return a, b
+
+
+def _roundtrip(m):
+    a, b = _pair()
+    try:
+        n = W.write_message(a, m, limiter=None)
+        size, got = W.read_message(b)
+        assert n == 8 + size
+        return got
+    finally:
+        a.close()
+        b.close()
+
+
+def test_header_is_big_endian_magic_and_length():
+    a, b = _pair()
+    W.write_message(a, W.Message.hello(), limiter=None)
+    head = b.recv(8)
+    assert struct.unpack(">II", head) == (0x104F4C7, 1)  # Hello: one variant byte
+    assert head[:4] == bytes([0x01, 0x04, 0xF4, 0xC7])
+    a.close()
+    b.close()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32, torch.float64,
+                                   torch.uint8, torch.int64])
+def test_tensor_message_round_trip(dtype):
+    x = (torch.arange(24, dtype=torch.float64) * 0.37 - 3.0).to(dtype).view(2, 3, 4)
+    got = _roundtrip(W.Message.from_tensor(x, compute_us=1234))
+    assert got.kind == "Tensor" and got.compute_us == 1234
+    assert got.x.shape == (2, 3, 4)
+    y = got.x.to_tensor()
+    assert y.dtype == dtype and torch.equal(y.view(torch.uint8), x.view(torch.uint8))
+
+
+def test_token_ids_travel_as_u32():
+    ids = torch.tensor([0, 7, 151935], dtype=torch.int32)
+    got = _roundtrip(W.Message.from_tensor(ids))
+    assert got.x.dtype == "U32"
+    out = torch.zeros(3, dtype=torch.int32)
+    got.x.to_tensor(out=out)
+    assert out.tolist() == [0, 7, 151935]
+
+
+def test_every_message_kind_round_trips():
+    x = W.RawTensor.from_tensor(torch.ones(1, 4, dtype=torch.float16))
+    s = W.SamplingRequest(seed=299792458, sample_index=3, temperature=0.7, top_k=40, top_p=None,
+                          repeat_penalty=1.25, repeat_context=[1, 2, 3])  # f32 field: exact value
+    msgs = [
+        W.Message.hello(),
+        W.Message("WorkerInfo", info=W.WorkerInfo(version="0.3|w8a16|gguf", dtype="f16", os="linux",
+                                                  arch="x86_64", device="cuda", device_idx=1,
+                                                  latency=2 ** 70 + 5, cpu_usage_percent=12.5,
+                                                  system_model="B200")),
+        W.Message("SingleOp", layer_name="model.layers.3", x=x, index_pos=17, block_idx=3, sampling=s),
+        W.Message("Batch", x=x, batch=[("model.layers.0", 5, 0), ("model.layers.1", 5, 1)]),
+        W.Message("CompactBatch", x=x, batch=W.CompactBatch("model.layers.4", 9, 4, 12), sampling=s),
+        W.Message("CompactRangeBatch", x=x, batch=W.CompactRangeBatch(9, 18, 18)),
+        W.Message("Tensor", x=x, compute_us=77),
+    ]
+    for m in msgs:
+        assert _roundtrip(m) == m
+    info = msgs[1].info
+    assert info.supports("gguf") and info.supports("w8a16") and not info.supports("0.3")
+
+
+def test_reader_rejects_bad_magic_and_oversized_length():
+    for head, what in ((struct.pack(">II", 0xDEADBEEF, 1), "invalid magic value"),
+                       (struct.pack(">II", W.PROTO_MAGIC, W.MESSAGE_MAX_SIZE + 1), "MESSAGE_MAX_SIZE")):
+        a, b = _pair()
+        a.sendall(head)
+        with pytest.raises(W.WireError, match=what):
+            W.read_message(b)
+        a.close()
+        b.close()
+
+
+def test_writer_refuses_an_oversized_body():
+    with pytest.raises(W.WireError, match="MESSAGE_MAX_SIZE"):
+        W.frame_header(W.MESSAGE_MAX_SIZE + 1)
+    assert W.frame_header(W.MESSAGE_MAX_SIZE)[4:] == struct.pack(">I", W.MESSAGE_MAX_SIZE)
+
+
+def test_truncated_and_malformed_bodies_are_errors():
+    body = W.encode_body(W.Message.from_tensor(torch.ones(3)))
+    with pytest.raises(W.WireError, match="ends early"):
+        W.decode_body(body[:-3])
+    with pytest.raises(W.WireError, match="after the message"):
+        W.decode_body(body + b"\x00")
+    with pytest.raises(W.WireError, match="unknown message variant"):
+        W.decode_body(b"\x07")
+    a, b = _pair()
+    a.sendall(struct.pack(">II", W.PROTO_MAGIC, 100) + body[:10])
+    a.close()
+    with pytest.raises(W.WireError, match="connection closed"):
+        W.read_message(b)
+    b.close()
+
+
+def test_unsupported_dtype_and_mismatched_buffer():
+    with pytest.raises(W.WireError, match="unsupported tensor dtype"):
+        W.RawTensor.from_tensor(torch.ones(2, dtype=torch.complex64))
+    r = W.RawTensor.from_tensor(torch.ones(2, 4, dtype=torch.float16))
+    with pytest.raises(W.WireError, match="shape"):
+        r.to_tensor(out=torch.zeros(4, 2, dtype=torch.float16))
+    with pytest.raises(W.WireError, match="dtype"):
+        r.to_tensor(out=torch.zeros(2, 4, dtype=torch.bfloat16))
+
+
+def test_limiter_environment():
+    f = W.TransferLimiter.from_env
+    assert f({}) is None
+    lim = f({"SPM_TRANSFER_LIMIT_MBPS": "8"})
+    assert lim.bytes_per_sec == 1_000_000.0 and lim.chunk_bytes == 65536  # 100 KB clamped
+    lim = f({"SPM_TRANSFER_LIMIT_KBPS": "80"})
+    assert lim.bytes_per_sec == 10_000.0 and lim.chunk_bytes == 1024  # 1 KB floor
+    lim = f({"SPM_TRANSFER_LIMIT_BYTES_PER_SEC": "200000", "SPM_TRANSFER_LIMIT_CHUNK_BYTES": "300"})
+    assert lim.bytes_per_sec == 200_000.0 and lim.chunk_bytes == 300
+    # MBPS wins over the others; a bad number falls through; non-positive disables
+    assert f({"SPM_TRANSFER_LIMIT_MBPS": "1", "SPM_TRANSFER_LIMIT_KBPS": "5"}).bytes_per_sec == 125_000.0
+    assert f({"SPM_TRANSFER_LIMIT_MBPS": "x", "SPM_TRANSFER_LIMIT_KBPS": "8"}).bytes_per_sec == 1000.0
+    assert f({"SPM_TRANSFER_LIMIT_MBPS": "0"}) is None
+    assert f({"SPM_TRANSFER_LIMIT_MBPS": "-3"}) is None
+    assert f({"SPM_TRANSFER_LIMIT_BYTES_PER_SEC": "1000", "SPM_TRANSFER_LIMIT_CHUNK_BYTES": "0.5"}).chunk_bytes == 1024
+
+
+def test_limiter_paces_chunks():
+    now = [100.0]
+    slept = []
+
+    def sleep(d):
+        slept.append(round(d, 9))
+        now[0] += d
+    lim = W.TransferLimiter(1000.0, 250, clock=lambda: now[0], sleep=sleep)
+
+    class Sink:
+        def __init__(self):
+            self.writes = []
+
+        def sendall(self, b):
+            self.writes.append(len(b))
+    s = Sink()
+    W._write_all(s, b"x" * 1000, lim)
+    assert s.writes == [250, 250, 250, 250]
+    assert slept == [0.25, 0.25, 0.25]  # the first chunk goes at once, then one chunk per 0.25 s
+    now[0] += 5.0  # idle time is not banked: the next chunk waits for nothing
+    W._write_all(s, b"x" * 100, lim)
+    assert slept == [0.25, 0.25, 0.25]
+
+
+def _tcp_worker(rank, world, ports, n_mb, prompts, steps, result_dir):
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "dial-8b-orin_b200"))
+    from dial_cuda.pipeline import Pipeline
+    from dial_cuda.wire import TcpChannel
+    ch = TcpChannel(rank, world, [("127.0.0.1", p) for p in ports], timeout_s=30.0, limiter=None)
+    c = FakeCompute(rank, world, n_mb)
+    p = Pipeline(rank, world, c, ch, n_mb)
+    p.prefill(prompts if rank == 0 else None, prompt_len=len(prompts[0]))
+    firsts = [int(v) for t in c.tokens for v in t.reshape(-1)]
+    p.steps(2)
+    p.steps(steps - 2)
+    last = [int(v) for t in c.tokens for v in t.reshape(-1)]
+    p.finish()
+    ch.close()
+    torch.save({"firsts": firsts, "last": last,
+                "after_finish": [int(v) for t in c.tokens for v in t.reshape(-1)]},
+               os.path.join(result_dir, f"r{rank}.pt"))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_pipeline_over_tcp_matches_single_process_chain(world, tmp_path):
+    n_mb, steps = 3, 5
+    prompts = [[(7 * b + 3 * i) % 97 for i in range(4)] for b in range(n_mb)]
+    ports = [_free_port() for _ in range(world)]
+    mp.start_processes(_tcp_worker, args=(world, ports, n_mb, prompts, steps, str(tmp_path)),
+                       nprocs=world, join=True, start_method="spawn")
+    ref = reference(world, n_mb, prompts, steps)
+    r0 = torch.load(tmp_path / "r0.pt")
+    rl = torch.load(tmp_path / f"r{world - 1}.pt")
+    assert r0["firsts"] == [seq[0] for seq in ref]
+    assert rl["last"] == [seq[-1] for seq in ref]
+    assert r0["after_finish"] == [seq[-1] for seq in ref]
+
+
+def test_missing_tcp_peer_times_out():
+    port = _free_port()  # nothing listens there
+    with pytest.raises(TimeoutError, match="no listener"):
+        W.TcpChannel(0, 2, [("127.0.0.1", _free_port()), ("127.0.0.1", port)], timeout_s=0.5, limiter=None)

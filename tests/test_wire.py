@@ -210,3 +210,38 @@ def test_missing_tcp_peer_times_out():
     port = _free_port()  # nothing listens there
     with pytest.raises(TimeoutError, match="no listener"):
         W.TcpChannel(0, 2, [("127.0.0.1", _free_port()), ("127.0.0.1", port)], timeout_s=0.5, limiter=None)
+
+
+@pytest.mark.gpu
+def test_tcp_channel_carries_device_buffers():
+    """Two stages in two threads of one process on one GPU: a bf16 hidden state
+    forward and int32 token ids back, device -> pinned host -> TCP -> device,
+    bit-exact and in order over repeated transfers."""
+    import threading
+    addrs = [("127.0.0.1", _free_port()), ("127.0.0.1", _free_port())]
+    chans = [None, None]
+
+    def make(r):
+        chans[r] = W.TcpChannel(r, 2, addrs, timeout_s=20.0, limiter=None)
+    th = [threading.Thread(target=make, args=(r,)) for r in range(2)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    c0, c1 = chans
+    g = torch.Generator(device="cuda").manual_seed(299792458)
+    try:
+        for step in range(3):
+            h = torch.randn(4, 4096, device="cuda", generator=g).to(torch.bfloat16)
+            ids = torch.randint(0, 151936, (4,), device="cuda", generator=g, dtype=torch.int32)
+            got_h = torch.empty_like(h)
+            got_ids = torch.zeros_like(ids)
+            done = [c0.isend(h, 1), c1.irecv(got_h, 0), c1.isend(ids, 0), c0.irecv(got_ids, 1)]
+            for d in done:
+                d.wait()
+            torch.cuda.synchronize()
+            assert torch.equal(got_h.view(torch.int16), h.view(torch.int16)), step
+            assert torch.equal(got_ids, ids), step
+    finally:
+        c0.close()
+        c1.close()

@@ -534,45 +534,89 @@ __global__ void __launch_bounds__(kTcWarps * 32)
     __syncthreads();
     if (!sm_last) return;
     __threadfence();
-    // the arithmetic of attention_combine_kernel in its order, with the loads
-    // of all splits issued together: per head, a warp finds the maximum, the
-    // split weights f_c = 2^(m_c - m) and the sum; then every output element
-    // accumulates its splits' O in split order
-    __shared__ float sm_f[REP][32];
-    __shared__ float sm_sum[REP];
-    __shared__ unsigned sm_valid[REP];
-    for (int r = warp; r < REP; r += kTcWarps) {
-      const float* pp = part + (t * hq + g * REP + r) * nsplit * (D + 2);
-      const float cm = lane < nsplit ? __ldcg(pp + lane * (D + 2)) : -FLT_MAX;
-      const float cl = lane < nsplit ? __ldcg(pp + lane * (D + 2) + 1) : 0.f;
-      float m = cm;
+    // the arithmetic of attention_combine_kernel in its order: per head, a
+    // warp finds the maximum, the split weights f_c = 2^(m_c - m) and the sum;
+    // then every output element accumulates its splits' O in split order.
+    // Up to 16 splits, warp r owns head r and lane l dims 4l .. 4l+3, and every
+    // load (the splits' maxima and sums, and their O) is issued in one round.
+    if (nsplit <= 16) {
+      for (int r = warp; r < REP; r += kTcWarps) {
+        const int64_t head = t * hq + g * REP + r;
+        const float* pp = part + head * nsplit * (D + 2);
+        const float cm = lane < nsplit ? __ldcg(pp + lane * (D + 2)) : -FLT_MAX;
+        const float cl = lane < nsplit ? __ldcg(pp + lane * (D + 2) + 1) : 0.f;
+        float2 ov[16][2];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const bool ok = lane < nsplit && cm != -FLT_MAX;
-      const float f = ok ? exp2f(cm - m) : 0.f;  // partial maxima are in the log2 domain
-      const unsigned valid = __ballot_sync(0xffffffffu, ok);
-      float sum = 0.f;
-      for (int c = 0; c < nsplit; ++c) {
-        const float lc = __shfl_sync(0xffffffffu, cl, c), fc = __shfl_sync(0xffffffffu, f, c);
-        if ((valid >> c) & 1u) sum += lc * fc;
+        for (int c = 0; c < 16; ++c) {
+          ov[c][0] = ov[c][1] = make_float2(0.f, 0.f);
+          if (c < nsplit) {  // (D + 2) floats per split row: dims 4l.. start 8-byte aligned
+            const float2* src = reinterpret_cast<const float2*>(pp + c * (D + 2) + 2 + 4 * lane);
+            ov[c][0] = __ldcg(src);
+            ov[c][1] = __ldcg(src + 1);
+          }
+        }
+        float m = cm;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const bool ok = lane < nsplit && cm != -FLT_MAX;
+        const float f = ok ? exp2f(cm - m) : 0.f;  // partial maxima are in the log2 domain
+        const unsigned valid = __ballot_sync(0xffffffffu, ok);
+        float sum = 0.f;
+        for (int c = 0; c < nsplit; ++c) {
+          const float lc = __shfl_sync(0xffffffffu, cl, c), fc = __shfl_sync(0xffffffffu, f, c);
+          if ((valid >> c) & 1u) sum += lc * fc;
+        }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float fc = __shfl_sync(0xffffffffu, f, c);
+          if (c < nsplit && ((valid >> c) & 1u)) {
+            acc[0] += ov[c][0].x * fc;
+            acc[1] += ov[c][0].y * fc;
+            acc[2] += ov[c][1].x * fc;
+            acc[3] += ov[c][1].y * fc;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) out[head * D + 4 * lane + e] = rnd<T>(acc[e] / sum);
       }
-      sm_f[r][lane] = f;
-      if (lane == 0) sm_sum[r] = sum, sm_valid[r] = valid;
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < REP * D; idx += kTcWarps * 32) {
-      const int r = idx / D, d = idx % D;
-      const int64_t head = t * hq + g * REP + r;
-      const float* pp = part + head * nsplit * (D + 2) + 2 + d;
-      float ov[32];
+    } else {
+      __shared__ float sm_f[REP][32];
+      __shared__ float sm_sum[REP];
+      __shared__ unsigned sm_valid[REP];
+      for (int r = warp; r < REP; r += kTcWarps) {
+        const float* pp = part + (t * hq + g * REP + r) * nsplit * (D + 2);
+        const float cm = lane < nsplit ? __ldcg(pp + lane * (D + 2)) : -FLT_MAX;
+        const float cl = lane < nsplit ? __ldcg(pp + lane * (D + 2) + 1) : 0.f;
+        float m = cm;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) ov[c] = c < nsplit ? __ldcg(pp + c * (D + 2)) : 0.f;
-      const unsigned valid = sm_valid[r];
-      float acc = 0.f;
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const bool ok = lane < nsplit && cm != -FLT_MAX;
+        const float f = ok ? exp2f(cm - m) : 0.f;
+        const unsigned valid = __ballot_sync(0xffffffffu, ok);
+        float sum = 0.f;
+        for (int c = 0; c < nsplit; ++c) {
+          const float lc = __shfl_sync(0xffffffffu, cl, c), fc = __shfl_sync(0xffffffffu, f, c);
+          if ((valid >> c) & 1u) sum += lc * fc;
+        }
+        sm_f[r][lane] = f;
+        if (lane == 0) sm_sum[r] = sum, sm_valid[r] = valid;
+      }
+      __syncthreads();
+      for (int idx = threadIdx.x; idx < REP * D; idx += kTcWarps * 32) {
+        const int r = idx / D, d = idx % D;
+        const int64_t head = t * hq + g * REP + r;
+        const float* pp = part + head * nsplit * (D + 2) + 2 + d;
+        float ov[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if (c < nsplit && ((valid >> c) & 1u)) acc += ov[c] * sm_f[r][c];
-      out[head * D + d] = rnd<T>(acc / sm_sum[r]);
+        for (int c = 0; c < 32; ++c) ov[c] = c < nsplit ? __ldcg(pp + c * (D + 2)) : 0.f;
+        const unsigned valid = sm_valid[r];
+        float acc = 0.f;
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (c < nsplit && ((valid >> c) & 1u)) acc += ov[c] * sm_f[r][c];
+        out[head * D + d] = rnd<T>(acc / sm_sum[r]);
+      }
     }
     if (threadIdx.x == 0) *ctr = 0;  // ready for the next launch
   }

@@ -2258,7 +2258,11 @@ dial_status launch_w8a16_skinny(const void* x, dial_dtype xdt, const int8_t* q, 
     // the decode GEMV: whole tiles per CTA (K a multiple of 128: its activation
     // fragments are read unpredicated from the staged rows)
     if (pl.mode == kTileCta && K % 128 == 0) {
-      const int C = (int)std::min<int64_t>(tiles, (int64_t)sm_count() * kCtasPerSM);
+      // as many CTAs as give every CTA the same number of tiles (at most the
+      // resident CTAs): a last wave of a few CTAs would stream alone at a
+      // fraction of the bandwidth
+      const int64_t slots = (int64_t)sm_count() * kCtasPerSM, per = (tiles + slots - 1) / slots;
+      const int C = (int)((tiles + per - 1) / per);
       const size_t smem = (size_t)kTmaSmem + kXsBytes + kXsAux;
       cudaError_t ae = cudaSuccess;
 #define GV(NT_, BF, ST)                                                                            \

@@ -1158,8 +1158,8 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": wl.metric, "value": round(value, 4), "unit": wl.unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(work / (value * unit_scale(wl.unit)) * 1e3, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
-        "data": getattr(wl, "data", DATA),
+        "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None,
+        "dtype": wl.dtype, "data": getattr(wl, "data", DATA),
         "config": dict(wl.describe(world), parallelism=parallelism(wl, world)),
         "cpu_baseline": {"value": round(value, 4), "unit": wl.unit, "cores": threads, "kind": "port",
                          "sample": f"per step: {sample}"},

@@ -510,11 +510,14 @@ def read_message(sock) -> Tuple[int, Message]:
 
 # ---------------------------------------------------------------- pipeline links over TCP
 class _Sent:
-    def __init__(self, fut):
-        self.fut = fut
+    def __init__(self, fut, timeout_s, link):
+        self.fut, self.timeout_s, self.link = fut, timeout_s, link
 
     def wait(self):
-        err = self.fut.get()
+        try:
+            err = self.fut.get(timeout=self.timeout_s)
+        except queue.Empty:
+            raise TimeoutError(f"link {self.link}: frame not written within {self.timeout_s} s") from None
         self.fut.put(err)  # wait() may be called again
         if err is not None:
             raise err
@@ -645,7 +648,7 @@ class TcpChannel:
         m = Message.from_tensor(t, pinned=self.pinned if t.is_cuda else None)
         fut = queue.Queue()
         self.outbox[i].put((m, fut))
-        return _Sent(fut)
+        return _Sent(fut, self.timeout_s, self.links[i])
 
     def irecv(self, t, src: int):
         return _Received(self, self._link(src, self.rank), t)

@@ -206,6 +206,48 @@ def test_pipeline_over_tcp_matches_single_process_chain(world, tmp_path):
     assert r0["after_finish"] == [seq[-1] for seq in ref]
 
 
+def _tcp_vocab_worker(rank, world, ports, head_ports, n_mb, R, prompts, steps, result_dir, shares):
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "dial-8b-orin_b200"))
+    from test_pipeline_cpu import FakeVocabCompute, V
+    from dial_cuda.model import vocab_shards
+    from dial_cuda.pipeline import Pipeline, head_links
+    from dial_cuda.wire import TcpChannel
+    spans = vocab_shards(V, shares)
+    rows = [v1 - v0 for v0, v1 in spans]
+    ch = TcpChannel(rank, world, [("127.0.0.1", p) for p in ports], timeout_s=30.0, limiter=None)
+    hch = TcpChannel(rank, world, [("127.0.0.1", p) for p in head_ports],
+                     links=head_links(world, rows), timeout_s=30.0, limiter=None)
+    c = FakeVocabCompute(rank, world, n_mb, R, spans[rank])
+    p = Pipeline(rank, world, c, ch, n_mb, head_channel=hch, head_rows=rows)
+    p.prefill(prompts if rank == 0 else None, prompt_len=len(prompts[0]))
+    firsts = [int(v) for t in c.tokens for v in t.reshape(-1)]
+    p.steps(steps)
+    p.finish()
+    ch.close()
+    hch.close()
+    torch.save({"firsts": firsts, "after_finish": [int(v) for t in c.tokens for v in t.reshape(-1)]},
+               os.path.join(result_dir, f"v{rank}.pt"))
+
+
+@pytest.mark.parametrize("world,shares", [(2, [1, 1]), (3, [1, 2, 0])])
+def test_vocab_parallel_head_over_tcp(world, shares, tmp_path):
+    """The vocabulary-parallel head's exchange (hidden states to the shard
+    stages, greedy keys to stage 0) over a second set of TCP links."""
+    n_mb, R, steps = max(3, world), 2, 4
+    V = 97
+    prompts = [[(3 * s + 7 * i + 1) % V for i in range(4)] for s in range(n_mb * R)]
+    ports = [_free_port() for _ in range(world)]
+    head_ports = [_free_port() for _ in range(world)]
+    mp.start_processes(_tcp_vocab_worker,
+                       args=(world, ports, head_ports, n_mb, R, prompts, steps, str(tmp_path), shares),
+                       nprocs=world, join=True, start_method="spawn")
+    ref = reference(world, n_mb * R, prompts, steps)
+    r0 = torch.load(tmp_path / "v0.pt")
+    assert r0["firsts"] == [seq[0] for seq in ref]
+    assert r0["after_finish"] == [seq[-1] for seq in ref]
+
+
 def test_missing_tcp_peer_times_out():
     port = _free_port()  # nothing listens there
     with pytest.raises(TimeoutError, match="no listener"):

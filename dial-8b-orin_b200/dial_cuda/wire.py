@@ -52,6 +52,10 @@ class WireError(RuntimeError):
     """A malformed, oversized or unexpected message."""
 
 
+class ConnectionClosed(WireError):
+    """The peer closed the connection between two messages."""
+
+
 def _torch():
     import torch  # noqa: PLC0415
     return torch
@@ -486,12 +490,14 @@ def write_message(sock, m: Message, limiter=_LIMITER_UNSET) -> int:
     return 8 + len(body)
 
 
-def _read_exact(sock, n: int) -> bytes:
+def _read_exact(sock, n: int, at_boundary: bool = False) -> bytes:
     buf = bytearray(n)
     mv, got = memoryview(buf), 0
     while got < n:
         k = sock.recv_into(mv[got:], n - got)
         if k == 0:
+            if at_boundary and got == 0:
+                raise ConnectionClosed("connection closed")
             raise WireError("connection closed inside a message")
         got += k
     return bytes(buf)
@@ -499,7 +505,7 @@ def _read_exact(sock, n: int) -> bytes:
 
 def read_message(sock) -> Tuple[int, Message]:
     """Message::from_reader (message.rs:366-388): (body bytes, message)."""
-    magic, size = struct.unpack(">II", _read_exact(sock, 8))
+    magic, size = struct.unpack(">II", _read_exact(sock, 8, at_boundary=True))
     if magic != PROTO_MAGIC:
         raise WireError(f"invalid magic value: {magic}")
     if size > MESSAGE_MAX_SIZE:
@@ -668,3 +674,136 @@ class TcpChannel:
                 pass
             s.close()
         self.socks = {}
+
+
+# ---------------------------------------------------------------- the master/worker exchange
+WORKER_CAPABILITIES = ("compact_batch_v1", "compact_range_batch_v1")  # worker.rs:263-268
+
+
+def expand_compact_batch(first_layer_name: str, index_pos: int, first_block_idx: int,
+                         num_layers: int) -> List[Tuple[str, int, int]]:
+    """worker.rs:349-372: the layer names continue the first name's numeric
+    suffix, the block indices the first block index."""
+    i = len(first_layer_name)
+    while i > 0 and first_layer_name[i - 1].isdigit():
+        i -= 1
+    if i == len(first_layer_name):
+        raise WireError("compact batch layer name has no numeric suffix")
+    prefix, start = first_layer_name[:i], int(first_layer_name[i:])
+    return [(f"{prefix}{start + o}", index_pos, first_block_idx + o) for o in range(num_layers)]
+
+
+def request_ops(m: Message, names_by_idx) -> List[Tuple[str, int, int]]:
+    """The (layer name, index_pos, block index) list a request asks a worker to
+    run (worker.rs:661-690); names_by_idx maps the worker's block indices to
+    its layer names (for CompactRangeBatch, worker.rs:297-312)."""
+    if m.kind == "SingleOp":
+        return [(m.layer_name, m.index_pos, m.block_idx)]
+    if m.kind == "Batch":
+        return [(str(n), int(p), int(b)) for n, p, b in m.batch]
+    if m.kind == "CompactBatch":
+        b = m.batch
+        return expand_compact_batch(b.first_layer_name, b.index_pos, b.first_block_idx, b.num_layers)
+    if m.kind == "CompactRangeBatch":
+        b = m.batch
+        ops = []
+        for blk in range(b.first_block_idx, b.first_block_idx + b.num_layers):
+            if blk not in names_by_idx:
+                raise WireError(f"compact range references missing local block index {blk}")
+            ops.append((names_by_idx[blk], b.index_pos, blk))
+        return ops
+    raise WireError(f"unhandled message in loop: {m.kind}")
+
+
+class StageWorker:
+    """The worker side of the reference's exchange over one connection
+    (worker.rs:615-765): a Hello answered with WorkerInfo, then per request
+    the layers it names run on its hidden state, answered with a Tensor
+    message and the compute time in microseconds.
+
+    run(x, first_block, num_layers, index_pos) computes a contiguous run of
+    this worker's blocks at token positions index_pos.. on x (a host tensor in
+    the request's dtype and shape) and returns the result (any device).  The
+    blocks of one request must be local, contiguous and share one index_pos --
+    what the reference's master sends to a worker that holds whole stages."""
+
+    def __init__(self, run, names_by_idx, info: Optional[WorkerInfo] = None):
+        self.run, self.names = run, dict(names_by_idx)
+        self.info = info or WorkerInfo(version="dial-b200|" + "|".join(WORKER_CAPABILITIES), device="cuda")
+
+    def serve(self, sock, limiter=None) -> int:
+        """Serves one connection until the peer closes it; returns the requests served."""
+        t0 = time.monotonic()
+        _, hello = read_message(sock)
+        if hello.kind != "Hello":
+            raise WireError(f"unexpected message instead of hello: {hello.kind}")
+        self.info.latency = int((time.monotonic() - t0) * 1000)
+        write_message(sock, Message("WorkerInfo", info=self.info), limiter)
+        served = 0
+        while True:
+            try:
+                _, m = read_message(sock)
+            except ConnectionClosed:
+                return served
+            start = time.monotonic()
+            ops = request_ops(m, self.names)
+            if not ops:
+                raise WireError("request names no layers")
+            first, index_pos = ops[0][2], ops[0][1]
+            for o, (name, ip, blk) in enumerate(ops):
+                if self.names.get(blk) != name:
+                    raise WireError(f"could not find layer {name}")
+                if ip != index_pos or blk != first + o:
+                    raise WireError("a request must name contiguous blocks at one index_pos")
+            y = self.run(m.x.to_tensor(), first, len(ops), index_pos)
+            us = int((time.monotonic() - start) * 1e6)
+            write_message(sock, Message.from_tensor(y, compute_us=us), limiter)
+            served += 1
+
+
+class RemoteStage:
+    """The master side (Client::request / forward_batch, client.rs:281-329,
+    389-452): connects, sends Hello, reads the worker's WorkerInfo, and sends
+    each batch as the most compact message the worker supports -- a
+    CompactRangeBatch or CompactBatch when the blocks are contiguous at one
+    index_pos, a Batch otherwise."""
+
+    def __init__(self, addr: Tuple[str, int], timeout_s: float = 60.0, limiter=_LIMITER_UNSET):
+        self.limiter = transfer_limiter() if limiter is _LIMITER_UNSET else limiter
+        self.sock = socket.create_connection(tuple(addr), timeout=timeout_s)
+        self.sock.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
+        write_message(self.sock, Message.hello(), self.limiter)
+        _, m = read_message(self.sock)
+        if m.kind != "WorkerInfo":
+            raise WireError(f"expected WorkerInfo, got {m.kind}")
+        self.info = m.info
+        self.compact_batch = self.info.supports("compact_batch_v1")
+        self.compact_range_batch = self.info.supports("compact_range_batch_v1")
+        self.last_compute_us = 0
+        self.last_kind = None
+
+    def forward_batch(self, x, batch: Sequence[Tuple[str, int, int]], sampling=None, out=None):
+        batch = [(str(n), int(p), int(b)) for n, p, b in batch]
+        if not batch:
+            raise WireError("empty batch")
+        name0, ip0, b0 = batch[0]
+        compact = all(p == ip0 for _, p, _ in batch) and all(b == b0 + o for o, (_, _, b) in enumerate(batch))
+        rx = RawTensor.from_tensor(x)
+        if compact and self.compact_batch and self.compact_range_batch:
+            m = Message("CompactRangeBatch", x=rx, batch=CompactRangeBatch(ip0, b0, len(batch)),
+                        sampling=sampling)
+        elif compact and self.compact_batch:
+            m = Message("CompactBatch", x=rx, batch=CompactBatch(name0, ip0, b0, len(batch)), sampling=sampling)
+        else:
+            m = Message("Batch", x=rx, batch=batch, sampling=sampling)
+        self.last_kind = m.kind
+        write_message(self.sock, m, self.limiter)
+        _, r = read_message(self.sock)
+        if r.kind != "Tensor":
+            raise WireError(f"expected a Tensor response, got {r.kind}")
+        self.last_compute_us = r.compute_us
+        return r.x.to_tensor(out=out) if out is not None else r.x.to_tensor()
+
+    def close(self) -> None:
+        self.sock.close()
+

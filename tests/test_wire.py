@@ -287,3 +287,89 @@ def test_tcp_channel_carries_device_buffers():
     finally:
         c0.close()
         c1.close()
+
+
+# ---------------------------------------------------------------- master/worker exchange
+def _fake_run(x, first, n, index_pos):
+    y = x.clone().double()
+    for blk in range(first, first + n):
+        y = y * 0.75 + 0.125 * (blk + 1) + 0.01 * index_pos
+    return y.to(x.dtype)
+
+
+def _serve_once(worker):
+    """A listener on a free port; the worker serves its first connection in a thread."""
+    import threading
+    srv = socket.create_server(("127.0.0.1", 0))
+    box = {}
+
+    def go():
+        s, _ = srv.accept()
+        try:
+            box["served"] = worker.serve(s, limiter=None)
+        except Exception as e:  # noqa: BLE001 -- checked by the test
+            box["error"] = e
+        finally:
+            s.close()
+            srv.close()
+    th = threading.Thread(target=go, daemon=True)
+    th.start()
+    return srv.getsockname(), th, box
+
+
+NAMES = {b: f"model.layers.{b}" for b in range(8, 14)}
+
+
+def test_compact_batch_names_follow_the_first_name():
+    assert W.expand_compact_batch("model.layers.7", 5, 7, 3) == [
+        ("model.layers.7", 5, 7), ("model.layers.8", 5, 8), ("model.layers.9", 5, 9)]
+    with pytest.raises(W.WireError, match="numeric suffix"):
+        W.expand_compact_batch("model.layers.x", 0, 0, 1)
+    m = W.Message("CompactRangeBatch", batch=W.CompactRangeBatch(3, 12, 3))
+    with pytest.raises(W.WireError, match="missing local block index 14"):
+        W.request_ops(m, NAMES)
+
+
+@pytest.mark.parametrize("caps,kind", [(W.WORKER_CAPABILITIES, "CompactRangeBatch"),
+                                       (("compact_batch_v1",), "CompactBatch"), ((), "Batch")])
+def test_master_worker_exchange(caps, kind):
+    """The master's request kind follows the worker's advertised capabilities;
+    every kind runs the same blocks and returns the same hidden state."""
+    info = W.WorkerInfo(version="dial-b200|" + "|".join(caps))
+    addr, th, box = _serve_once(W.StageWorker(_fake_run, NAMES, info))
+    cl = W.RemoteStage(addr, timeout_s=10.0, limiter=None)
+    assert cl.info.version == info.version
+    x = torch.randn(1, 5, 64).to(torch.bfloat16)
+    for index_pos in (0, 5):  # a prompt, then the next position
+        batch = [(NAMES[b], index_pos, b) for b in range(9, 13)]
+        y = cl.forward_batch(x, batch)
+        assert cl.last_kind == kind
+        assert torch.equal(y.view(torch.int16), _fake_run(x, 9, 4, index_pos).view(torch.int16))
+    out = torch.empty_like(x)
+    cl.forward_batch(x, [(NAMES[8], 2, 8)], out=out)  # one block
+    assert torch.equal(out.view(torch.int16), _fake_run(x, 8, 1, 2).view(torch.int16))
+    cl.close()
+    th.join(timeout=10)
+    assert box.get("served") == 3, box
+
+
+def test_worker_rejects_foreign_and_scattered_blocks():
+    for batch, what in (([("model.layers.20", 0, 20)], "missing local block index 20"),
+                        ([("model.layers.8", 0, 8), ("model.layers.10", 0, 10)], "contiguous")):
+        addr, th, box = _serve_once(W.StageWorker(_fake_run, NAMES))
+        cl = W.RemoteStage(addr, timeout_s=10.0, limiter=None)
+        with pytest.raises(W.WireError):
+            cl.forward_batch(torch.ones(1, 1, 8), batch)  # the worker drops the connection
+        cl.close()
+        th.join(timeout=10)
+        assert what in str(box.get("error")), box
+
+
+def test_worker_wants_hello_first():
+    addr, th, box = _serve_once(W.StageWorker(_fake_run, NAMES))
+    s = socket.create_connection(addr)
+    W.write_message(s, W.Message.from_tensor(torch.ones(2)), limiter=None)
+    th.join(timeout=10)
+    s.close()
+    assert "instead of hello" in str(box.get("error")), box
+

@@ -373,3 +373,17 @@ def test_worker_wants_hello_first():
     s.close()
     assert "instead of hello" in str(box.get("error")), box
 
+
+
+def test_send_wait_is_bounded():
+    """A frame the writer thread never finishes (a peer that stops reading)
+    ends the sender's wait with a timeout instead of blocking it."""
+    import queue
+    d = W._Sent(queue.Queue(), 0.2, (0, 1))
+    with pytest.raises(TimeoutError, match="not written within"):
+        d.wait()
+    q = queue.Queue()
+    q.put(None)
+    done = W._Sent(q, 0.2, (0, 1))
+    done.wait()
+    done.wait()  # a finished send may be waited on again
